@@ -1,0 +1,319 @@
+// PyTorch bindings of the sm_100a kernels.  Every entry point checks device,
+// dtype, contiguity and shapes on the host before launching on the current
+// CUDA stream, so a bad call raises a Python exception instead of faulting.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "attention.h"
+#include "fused_ops.h"
+#include "gemm_tc.h"
+#include "sampler.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_DT(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has dtype ", (t).scalar_type(), ", expected ", dt)
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+template <typename T>
+T* ptr_or_null(const c10::optional<Tensor>& t) {
+  return t.has_value() ? static_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+// out = grouped GEMM of weight groups x activation rows (see gemm_tc.cu).
+void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor group_count,
+          c10::optional<Tensor> group_offset, Tensor out, int64_t bn, int64_t epi, int64_t m_tiles,
+          int64_t pair_row_offset, int64_t out_group_stride, c10::optional<Tensor> slot_of_row,
+          c10::optional<Tensor> slot_weight, Tensor status) {
+  CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(group_count); CHECK_CUDA(status);
+  CHECK_CONTIG(weight); CHECK_CONTIG(group_count);
+  TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [rows, K] with unit inner stride");
+  TORCH_CHECK(weight.dim() == 2 || weight.dim() == 3, "weight must be [N, K] or [groups, N, K]");
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(group_count, torch::kInt32);
+  CHECK_DT(status, torch::kInt32);
+  const bool fp8 = weight.scalar_type() == torch::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || weight.scalar_type() == torch::kBFloat16, "weight must be e4m3 or bf16");
+  const int64_t groups = weight.dim() == 3 ? weight.size(0) : 1;
+  const int64_t rows_per_group = weight.size(-2);
+  const int64_t K = weight.size(-1);
+  TORCH_CHECK(x.size(1) == K, "K mismatch: weight ", K, " vs x ", x.size(1));
+  TORCH_CHECK(group_count.numel() == groups, "group_count must have one entry per weight group");
+  if (fp8) {
+    TORCH_CHECK(weight_scale.has_value(), "fp8 weight needs weight_scale");
+    CHECK_DT((*weight_scale), torch::kFloat32);
+    CHECK_CONTIG((*weight_scale));
+    TORCH_CHECK(weight_scale->numel() == groups * (rows_per_group / 128) * (K / 128),
+                "weight_scale must be [groups, N/128, K/128]");
+  }
+  if (group_offset.has_value()) {
+    CHECK_DT((*group_offset), torch::kInt32);
+    TORCH_CHECK(group_offset->numel() >= groups, "group_offset too short");
+  }
+  const bool pair = epi == b200::kEpiSiluPair;
+  if (epi == b200::kEpiScatter) {
+    TORCH_CHECK(slot_of_row.has_value() && slot_weight.has_value(), "scatter epilogue needs slots");
+    CHECK_DT((*slot_of_row), torch::kInt32);
+    CHECK_DT((*slot_weight), torch::kFloat32);
+  }
+  if (epi == b200::kEpiF32) {
+    CHECK_DT(out, torch::kFloat32);
+  } else {
+    CHECK_DT(out, torch::kBFloat16);
+  }
+  TORCH_CHECK(m_tiles * 128 <= rows_per_group, "m_tiles exceeds weight rows");
+  if (pair) TORCH_CHECK(pair_row_offset + m_tiles * 128 <= rows_per_group, "pair rows out of range");
+  if (x.size(0) == 0) return;
+
+  c10::cuda::CUDAGuard guard(x.device());
+  b200::GemmLaunch L{};
+  L.args.a_scale = fp8 ? weight_scale->data_ptr<float>() : nullptr;
+  L.args.a_rows_per_group = (int)rows_per_group;
+  L.args.m_tiles = (int)m_tiles;
+  L.args.k_stages = (int)(K / 64);
+  L.args.scale_m_blocks = (int)(rows_per_group / 128);
+  L.args.scale_k_blocks = (int)(K / 128);
+  L.args.num_groups = (int)groups;
+  L.args.group_count = group_count.data_ptr<int>();
+  L.args.group_offset = group_offset.has_value() ? group_offset->data_ptr<int>() : nullptr;
+  L.args.pair_row_offset = (int)pair_row_offset;
+  L.args.out = out.data_ptr();
+  L.args.ld_out = (int)out.stride(0);
+  L.args.out_group_stride = (int)out_group_stride;
+  L.args.slot_of_row = ptr_or_null<int>(slot_of_row);
+  L.args.slot_weight = ptr_or_null<float>(slot_weight);
+  L.args.status = status.data_ptr<int>();
+  L.a = weight.data_ptr();
+  L.a_row_stride_bytes = K * weight.element_size();
+  L.b = x.data_ptr();
+  L.b_rows = x.size(0);
+  L.b_row_stride_bytes = x.stride(0) * 2;
+  L.K = (int)K;
+  L.bn = (int)bn;
+  L.a_fp8 = fp8;
+  L.pair = pair;
+  L.epi = (int)epi;
+  b200::gemm_tc_launch(L, stream());
+}
+
+void embed(Tensor ids, Tensor table, Tensor out, Tensor status) {
+  CHECK_CUDA(ids); CHECK_CUDA(table); CHECK_CUDA(out);
+  CHECK_DT(ids, torch::kInt32); CHECK_DT(table, torch::kBFloat16); CHECK_DT(out, torch::kBFloat16);
+  CHECK_CONTIG(table); CHECK_CONTIG(out); CHECK_CONTIG(ids);
+  TORCH_CHECK(out.size(0) == ids.numel() && out.size(1) == table.size(1), "embed shape mismatch");
+  b200::embed_gather(ids.data_ptr<int>(), table.data_ptr(), out.data_ptr(), (int)ids.numel(), (int)table.size(1),
+                     (int)table.size(0), status.data_ptr<int>(), stream());
+}
+
+void rmsnorm(Tensor x, c10::optional<Tensor> residual_in, Tensor weight, Tensor out,
+             c10::optional<Tensor> residual_out, double eps) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_CONTIG(out); CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(weight, torch::kBFloat16); CHECK_DT(out, torch::kBFloat16);
+  TORCH_CHECK(residual_in.has_value() == residual_out.has_value(), "residual in/out go together");
+  const int H = (int)x.size(-1);
+  const int T = (int)(x.numel() / H);
+  TORCH_CHECK(out.numel() == x.numel() && weight.numel() == H, "rmsnorm shape mismatch");
+  if (residual_in.has_value()) {
+    CHECK_CONTIG((*residual_in));
+    TORCH_CHECK(residual_in->numel() == x.numel(), "residual shape mismatch");
+  }
+  b200::rmsnorm(x.data_ptr(), residual_in.has_value() ? residual_in->data_ptr() : nullptr, weight.data_ptr(),
+                out.data_ptr(), residual_out.has_value() ? residual_out->data_ptr() : nullptr, T, H, (float)eps,
+                stream());
+}
+
+void moe_combine(Tensor slots, int64_t topk, Tensor residual, Tensor weight, Tensor out, double eps) {
+  CHECK_CUDA(slots); CHECK_CONTIG(slots); CHECK_CONTIG(residual); CHECK_CONTIG(out);
+  CHECK_DT(slots, torch::kBFloat16); CHECK_DT(residual, torch::kBFloat16);
+  const int H = (int)residual.size(-1);
+  const int T = (int)residual.size(0);
+  TORCH_CHECK(slots.numel() >= (int64_t)T * topk * H, "slots too small");
+  b200::moe_combine_add_rmsnorm(slots.data_ptr(), (int)topk, residual.data_ptr(), weight.data_ptr(),
+                                out.data_ptr(), T, H, (float)eps, stream());
+}
+
+void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tensor q_norm_w, Tensor k_norm_w,
+                         Tensor cos_sin, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
+                         c10::optional<Tensor> v_scale, Tensor q_out, int64_t num_q_heads, int64_t num_kv_heads,
+                         int64_t head_dim, int64_t block_size, int64_t block_stride, int64_t scale_block_stride,
+                         double eps) {
+  CHECK_CUDA(qkv); CHECK_DT(qkv, torch::kBFloat16); CHECK_DT(positions, torch::kInt32);
+  CHECK_DT(slot_mapping, torch::kInt32); CHECK_DT(cos_sin, torch::kFloat32); CHECK_CONTIG(q_out);
+  TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride must be 1");
+  const int T = (int)qkv.size(0);
+  TORCH_CHECK(positions.numel() >= T && slot_mapping.numel() >= T, "positions/slot_mapping too short");
+  TORCH_CHECK(qkv.size(1) == (num_q_heads + 2 * num_kv_heads) * head_dim, "qkv width mismatch");
+  b200::QkvArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.qkv_stride = (int)qkv.stride(0);
+  a.positions = positions.data_ptr<int>();
+  a.slot_mapping = slot_mapping.data_ptr<int>();
+  a.q_norm_w = q_norm_w.data_ptr();
+  a.k_norm_w = k_norm_w.data_ptr();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.kv_int8 = k_cache.scalar_type() == torch::kInt8;
+  a.k_scale = ptr_or_null<float>(k_scale);
+  a.v_scale = ptr_or_null<float>(v_scale);
+  if (a.kv_int8) TORCH_CHECK(a.k_scale && a.v_scale, "int8 KV needs scale pools");
+  a.block_size = (int)block_size;
+  a.block_stride = block_stride;
+  a.scale_block_stride = scale_block_stride;
+  a.q_out = q_out.data_ptr();
+  a.num_q_heads = (int)num_q_heads;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.head_dim = (int)head_dim;
+  a.eps = (float)eps;
+  b200::qknorm_rope_kvstore(a, T, stream());
+}
+
+void router_topk(Tensor logits, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
+                 c10::optional<Tensor> counts) {
+  CHECK_CUDA(logits); CHECK_DT(logits, torch::kFloat32);
+  TORCH_CHECK(logits.stride(1) == 1 && logits.size(1) >= num_experts, "router logits layout");
+  CHECK_DT(ids, torch::kInt32); CHECK_DT(weights, torch::kFloat32); CHECK_CONTIG(ids); CHECK_CONTIG(weights);
+  TORCH_CHECK(ids.numel() >= logits.size(0) * topk, "ids too small");
+  b200::router_topk(logits.data_ptr<float>(), (int)logits.stride(0), (int)logits.size(0), (int)num_experts,
+                    (int)topk, renorm, ids.data_ptr<int>(), weights.data_ptr<float>(), ptr_or_null<int>(counts),
+                    stream());
+}
+
+void moe_permute(Tensor x, Tensor ids, Tensor counts, Tensor cursor, Tensor x_perm, Tensor slot_of_row,
+                 c10::optional<Tensor> offsets_out) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_CONTIG(x_perm); CHECK_DT(ids, torch::kInt32); CHECK_CONTIG(ids);
+  CHECK_DT(counts, torch::kInt32); CHECK_DT(cursor, torch::kInt32); CHECK_DT(slot_of_row, torch::kInt32);
+  const int T = (int)x.size(0), H = (int)x.size(1), topk = (int)ids.size(1), E = (int)counts.numel();
+  TORCH_CHECK(ids.size(0) == T, "ids rows mismatch");
+  TORCH_CHECK(x_perm.size(0) >= (int64_t)T * topk && slot_of_row.numel() >= (int64_t)T * topk, "x_perm too small");
+  b200::moe_permute(x.data_ptr(), ids.data_ptr<int>(), T, topk, E, H, counts.data_ptr<int>(), cursor.data_ptr<int>(),
+                    x_perm.data_ptr(), slot_of_row.data_ptr<int>(), ptr_or_null<int>(offsets_out), stream());
+}
+
+void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
+                 c10::optional<Tensor> v_scale, Tensor block_tables, Tensor seq_lens, Tensor out, Tensor part_o,
+                 Tensor part_m, Tensor part_l, int64_t block_size, int64_t block_stride, int64_t num_kv_heads,
+                 double scale, int64_t num_splits, int64_t split_len) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_DT(q, torch::kBFloat16);
+  CHECK_DT(block_tables, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_CONTIG(block_tables);
+  const int B = (int)q.size(0);
+  const int nq = (int)q.size(1), D = (int)q.size(2);
+  TORCH_CHECK(nq % num_kv_heads == 0, "q heads must be a multiple of kv heads");
+  TORCH_CHECK(block_tables.size(0) >= B && seq_lens.numel() >= B, "metadata rows");
+  b200::DecodeArgs a{};
+  a.q = q.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.kv_int8 = k_cache.scalar_type() == torch::kInt8;
+  a.k_scale = ptr_or_null<float>(k_scale);
+  a.v_scale = ptr_or_null<float>(v_scale);
+  a.block_tables = block_tables.data_ptr<int>();
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.max_blocks = (int)block_tables.size(1);
+  a.block_size = (int)block_size;
+  a.block_stride = block_stride;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.group = nq / (int)num_kv_heads;
+  a.head_dim = D;
+  a.scale = (float)scale;
+  a.num_splits = (int)num_splits;
+  a.split_len = (int)split_len;
+  a.part_o = part_o.data_ptr<float>();
+  a.part_m = part_m.data_ptr<float>();
+  a.part_l = part_l.data_ptr<float>();
+  a.out = out.data_ptr();
+  if (num_splits > 1)
+    TORCH_CHECK(part_m.numel() >= (int64_t)B * nq * num_splits && part_o.numel() >= (int64_t)B * nq * num_splits * D,
+                "split workspace too small");
+  b200::paged_decode_attn(a, B, stream());
+}
+
+void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
+                  c10::optional<Tensor> v_scale, Tensor cu_seqlens_q, Tensor seq_lens, Tensor block_tables,
+                  Tensor out, int64_t max_q_len, int64_t block_size, int64_t block_stride, int64_t num_kv_heads,
+                  double scale) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_DT(q, torch::kBFloat16);
+  CHECK_DT(cu_seqlens_q, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_DT(block_tables, torch::kInt32);
+  CHECK_CONTIG(block_tables); CHECK_CONTIG(cu_seqlens_q);
+  const int B = (int)seq_lens.numel();
+  const int nq = (int)q.size(1), D = (int)q.size(2);
+  b200::PrefillArgs a{};
+  a.q = q.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.kv_int8 = k_cache.scalar_type() == torch::kInt8;
+  a.k_scale = ptr_or_null<float>(k_scale);
+  a.v_scale = ptr_or_null<float>(v_scale);
+  a.cu_seqlens_q = cu_seqlens_q.data_ptr<int>();
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.block_tables = block_tables.data_ptr<int>();
+  a.max_blocks = (int)block_tables.size(1);
+  a.block_size = (int)block_size;
+  a.block_stride = block_stride;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.group = nq / (int)num_kv_heads;
+  a.head_dim = D;
+  a.scale = (float)scale;
+  a.out = out.data_ptr();
+  b200::paged_prefill_attn(a, B, (int)max_q_len, stream());
+}
+
+void argmax(Tensor logits, Tensor out) {
+  CHECK_CUDA(logits); CHECK_DT(logits, torch::kFloat32); CHECK_DT(out, torch::kInt32);
+  TORCH_CHECK(logits.stride(1) == 1, "logits inner stride must be 1");
+  b200::argmax_rows(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1), logits.stride(0),
+                    out.data_ptr<int>(), stream());
+}
+
+void sample(Tensor logits, Tensor temperature, c10::optional<Tensor> top_k, c10::optional<Tensor> top_p,
+            c10::optional<Tensor> min_p, Tensor seeds, c10::optional<Tensor> offsets, Tensor out) {
+  CHECK_CUDA(logits); CHECK_DT(logits, torch::kFloat32); CHECK_DT(temperature, torch::kFloat32);
+  CHECK_DT(seeds, torch::kInt64); CHECK_DT(out, torch::kInt32);
+  TORCH_CHECK(logits.stride(1) == 1, "logits inner stride must be 1");
+  b200::SampleArgs a{};
+  a.temperature = temperature.data_ptr<float>();
+  a.top_k = ptr_or_null<int>(top_k);
+  a.top_p = ptr_or_null<float>(top_p);
+  a.min_p = ptr_or_null<float>(min_p);
+  a.seeds = seeds.data_ptr<int64_t>();
+  a.offsets = ptr_or_null<int64_t>(offsets);
+  b200::sample_rows(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1), logits.stride(0), a,
+                    out.data_ptr<int>(), stream());
+}
+
+void penalties(Tensor logits, Tensor rows, Tensor ids, Tensor gen_counts, Tensor presence, Tensor frequency,
+               Tensor repetition) {
+  CHECK_CUDA(logits); CHECK_DT(logits, torch::kFloat32);
+  CHECK_DT(rows, torch::kInt32); CHECK_DT(ids, torch::kInt32); CHECK_DT(gen_counts, torch::kInt32);
+  b200::apply_penalties(logits.data_ptr<float>(), logits.stride(0), rows.data_ptr<int>(), ids.data_ptr<int>(),
+                        gen_counts.data_ptr<int>(), presence.data_ptr<float>(), frequency.data_ptr<float>(),
+                        repetition.data_ptr<float>(), (int)rows.numel(), stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "b200moe sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("embed", &embed);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("moe_combine", &moe_combine);
+  m.def("qknorm_rope_kvstore", &qknorm_rope_kvstore);
+  m.def("router_topk", &router_topk);
+  m.def("moe_permute", &moe_permute);
+  m.def("decode_attn", &decode_attn);
+  m.def("prefill_attn", &prefill_attn);
+  m.def("argmax", &argmax);
+  m.def("sample", &sample);
+  m.def("penalties", &penalties);
+  m.attr("EPI_BF16") = (int)b200::kEpiBf16;
+  m.attr("EPI_F32") = (int)b200::kEpiF32;
+  m.attr("EPI_SILU_PAIR") = (int)b200::kEpiSiluPair;
+  m.attr("EPI_SCATTER") = (int)b200::kEpiScatter;
+}

@@ -1,0 +1,55 @@
+// Host interface of the paged attention kernels (kernels/attention.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace b200 {
+
+struct DecodeArgs {
+  const void* q;             // [B, q_heads, D] bf16
+  const void* k_cache;       // layer base of the pool, [blocks, kv_heads, block_size, D]
+  const void* v_cache;
+  const float* k_scale;      // int8 KV scales (unused for bf16)
+  const float* v_scale;
+  int kv_int8;
+  const int* block_tables;   // [B, max_blocks]
+  const int* seq_lens;       // [B] keys per sequence (including the current token)
+  int max_blocks;
+  int block_size;
+  int64_t block_stride;      // elements between consecutive blocks of one layer
+  int num_kv_heads;
+  int group;                 // q heads per kv head
+  int head_dim;
+  float scale;
+  int num_splits;
+  int split_len;             // keys per split (multiple of 64)
+  float* part_o;             // [B, q_heads, num_splits, D]
+  float* part_m;             // [B, q_heads, num_splits]
+  float* part_l;
+  void* out;                 // [B, q_heads, D] bf16
+};
+
+struct PrefillArgs {
+  const void* q;             // [T, q_heads, D] bf16 (rows of all prefill sequences)
+  const void* k_cache;
+  const void* v_cache;
+  const float* k_scale;
+  const float* v_scale;
+  int kv_int8;
+  const int* cu_seqlens_q;   // [B + 1]
+  const int* seq_lens;       // [B] total keys (cached + new)
+  const int* block_tables;   // [B, max_blocks]
+  int max_blocks;
+  int block_size;
+  int64_t block_stride;
+  int num_kv_heads;
+  int group;
+  int head_dim;
+  float scale;
+  void* out;                 // [T, q_heads, D] bf16
+};
+
+void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s);
+void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t s);
+
+}  // namespace b200

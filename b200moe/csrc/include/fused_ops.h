@@ -1,0 +1,45 @@
+// Host interface of the memory-bound fused ops (kernels/fused_ops.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace b200 {
+
+constexpr int kMaxExperts = 512;
+
+struct QkvArgs {
+  const void* qkv;          // [T, qkv_stride] bf16: q heads | k heads | v heads
+  int qkv_stride;           // elements
+  const int* positions;     // [T]
+  const int* slot_mapping;  // [T] flat KV slot (block * block_size + offset), -1 = no store
+  const void* q_norm_w;     // [D] bf16
+  const void* k_norm_w;     // [D] bf16
+  const float* cos_sin;     // [max_pos, D]: cos[0:D/2] | sin[0:D/2]
+  void* k_cache;            // layer base, [blocks, kv_heads, block_size, D] bf16 or int8
+  void* v_cache;
+  float* k_scale;           // int8 KV: layer base, [blocks, kv_heads, block_size]
+  float* v_scale;
+  int kv_int8;
+  int block_size;
+  int64_t block_stride;     // elements between consecutive blocks of the KV pool
+  int64_t scale_block_stride;
+  void* q_out;              // [T, q_heads, D] bf16
+  int num_q_heads;
+  int num_kv_heads;
+  int head_dim;
+  float eps;
+};
+
+void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,
+                  cudaStream_t s);
+void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,
+             float eps, cudaStream_t s);
+void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
+                             int H, float eps, cudaStream_t s);
+void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s);
+void router_topk(const float* logits, int ld, int T, int E, int topk, bool renorm, int* ids, float* weights,
+                 int* counts, cudaStream_t s);
+void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
+                 void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s);
+
+}  // namespace b200

@@ -1,0 +1,54 @@
+// Host/device interface of the tcgen05 grouped GEMM (kernels/gemm_tc.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace b200 {
+
+enum GemmEpilogue : int {
+  kEpiBf16 = 0,      // out[row, g*out_group_stride + m] = bf16(acc)
+  kEpiF32 = 1,       // same, fp32
+  kEpiSiluPair = 2,  // out[row, m] = bf16(silu(acc_gate) * acc_up)
+  kEpiScatter = 3,   // out[slot_of_row[row], m] = bf16(acc * slot_weight[slot])
+};
+
+// Kernel arguments (passed by value; device pointers only).
+struct GemmArgs {
+  const float* a_scale;        // fp8 mode: [groups, scale_m_blocks, scale_k_blocks]
+  int a_rows_per_group;        // weight rows per group (row stride between groups)
+  int m_tiles;                 // 128-row tiles computed per group (pair: gate tiles)
+  int k_stages;                // K / 64
+  int scale_m_blocks;
+  int scale_k_blocks;
+  int num_groups;
+  const int* group_count;      // [groups] activation rows per group (device)
+  const int* group_offset;     // [groups] first activation row, or null = prefix of counts
+  int pair_row_offset;         // pair mode: row offset of the "up" half inside a group
+  void* out;
+  int ld_out;                  // output row stride (elements)
+  int out_group_stride;        // column offset per group for kEpiBf16/kEpiF32
+  const int* slot_of_row;      // kEpiScatter
+  const float* slot_weight;    // kEpiScatter
+  int* status;                 // device status word (0 = ok)
+};
+
+struct GemmLaunch {
+  GemmArgs args;
+  const void* a;               // weight base
+  int64_t a_row_stride_bytes;
+  const void* b;               // activation base (bf16)
+  int64_t b_rows;              // rows addressable through the activation tensor map
+  int64_t b_row_stride_bytes;
+  int K;
+  int bn;                      // token tile: 16, 32, 64, 128 (256 when not pair)
+  bool a_fp8;
+  bool pair;
+  int epi;
+};
+
+void gemm_tc_launch(const GemmLaunch& launch, cudaStream_t stream);
+CUtensorMap make_tmap_2d(const void* base, bool is_bf16, int64_t rows, int64_t cols,
+                         int64_t row_stride_bytes, int box_cols, int box_rows, bool swizzle128);
+
+}  // namespace b200

@@ -1,0 +1,564 @@
+// Paged-KV attention for Qwen3 GQA (sm_100a).
+//
+// KV pool layout per layer: [num_blocks, kv_heads, block_size, D] so that one
+// (block, kv head) is a contiguous block_size x D slab; `block_stride` is the
+// element distance between consecutive blocks (the pool interleaves layers).
+//
+// paged_decode_attn   one query per sequence.  Split-KV (flash-decoding): CTA =
+//                     (split, kv head, sequence); the GQA group's G query heads
+//                     are the MMA rows, so every K/V byte is read once per
+//                     group.  64-key tiles are staged through shared memory with
+//                     cp.async double buffering; each warp owns 16 keys of a tile
+//                     and keeps its own online-softmax state; warps and splits
+//                     are merged at the end.  Decode attention is bound by HBM
+//                     (bytes of K/V per query head group), so the 16x8x16 bf16
+//                     warp MMA is enough compute.
+// paged_prefill_attn  varlen causal prefill / chunked prefill over the paged pool
+//                     (prefix-cache hits and earlier chunks included).  CTA =
+//                     (query block, kv head, sequence); the 64 MMA rows pack
+//                     64/G query positions x G heads of one group, so K/V tiles
+//                     are shared by the whole group.
+//
+// int8 KV: tiles are dequantised (per-token-head scale) while they are staged.
+//
+// Reference: Triton paged decode kernel nanovllm/kernels/paged_attention.py:74-190
+// (one program per (batch, q head), no GQA sharing) and the per-sequence SDPA
+// prefill loop nanovllm/layers/attention.py:179-213.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "sm100.cuh"
+#include "attention.h"
+
+namespace b200 {
+
+using bf16 = __nv_bfloat16;
+constexpr int kKT = 64;  // keys per tile
+
+// ------------------------------------------------------------- primitives
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Row-major [rows][D] bf16 tile with the 16-byte chunk index XOR-swizzled by row % 8.
+template <int D>
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+  return row * (D * 2) + ((chunk ^ (row & 7)) << 4);
+}
+
+// Load kKT keys [k0, k0+kKT) of kv head h into swizzled K and V tiles.  Keys at
+// or beyond k_end are zero-filled and never read out of bounds.
+template <int D, int NT>
+__device__ __forceinline__ void load_kv_tile(uint32_t sk, uint32_t sv, const void* kc_, const void* vc_,
+                                             const float* ks, const float* vs, bool int8, const int* btab,
+                                             int bs, int64_t block_stride, int64_t sblock_stride, int h,
+                                             int k0, int k_end, uint8_t* sk_gen, uint8_t* sv_gen) {
+  constexpr int CPR = D / 8;  // 16-byte chunks per bf16 row
+  if (!int8) {
+    const bf16* kc = static_cast<const bf16*>(kc_);
+    const bf16* vc = static_cast<const bf16*>(vc_);
+    for (int idx = threadIdx.x; idx < kKT * CPR; idx += NT) {
+      const int r = idx / CPR, c = idx % CPR;
+      const int key = k0 + r;
+      const bool valid = key < k_end;
+      int64_t off = 0;
+      if (valid) {
+        const int blk = btab[key / bs];
+        off = (int64_t)blk * block_stride + ((int64_t)h * bs + key % bs) * D + c * 8;
+      }
+      cp_async16(sk + tile_off<D>(r, c), kc + off, valid);
+      cp_async16(sv + tile_off<D>(r, c), vc + off, valid);
+    }
+    return;
+  }
+  // int8: 8 values per thread-iteration, dequantised into the bf16 tile
+  const int8_t* kc = static_cast<const int8_t*>(kc_);
+  const int8_t* vc = static_cast<const int8_t*>(vc_);
+  for (int idx = threadIdx.x; idx < kKT * CPR; idx += NT) {
+    const int r = idx / CPR, c = idx % CPR;
+    const int key = k0 + r;
+    uint4 ko = make_uint4(0, 0, 0, 0), vo = make_uint4(0, 0, 0, 0);
+    if (key < k_end) {
+      const int blk = btab[key / bs];
+      const int64_t tok = (int64_t)h * bs + key % bs;
+      const int64_t off = (int64_t)blk * block_stride + tok * D + c * 8;
+      const float skl = ks[(int64_t)blk * sblock_stride + tok];
+      const float svl = vs[(int64_t)blk * sblock_stride + tok];
+      const uint2 kq = *reinterpret_cast<const uint2*>(kc + off);
+      const uint2 vq = *reinterpret_cast<const uint2*>(vc + off);
+      const int8_t* kb = reinterpret_cast<const int8_t*>(&kq);
+      const int8_t* vb = reinterpret_cast<const int8_t*>(&vq);
+      uint32_t kw[4], vw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        kw[j] = pack_bf16(kb[2 * j] * skl, kb[2 * j + 1] * skl);
+        vw[j] = pack_bf16(vb[2 * j] * svl, vb[2 * j + 1] * svl);
+      }
+      ko = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+      vo = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+    }
+    *reinterpret_cast<uint4*>(sk_gen + tile_off<D>(r, c)) = ko;
+    *reinterpret_cast<uint4*>(sv_gen + tile_off<D>(r, c)) = vo;
+  }
+}
+
+// S[16 x 8*NB] = Q(frag) * K^T for keys [kbase, kbase + 8*NB) of the smem tile
+template <int D, int NB>
+__device__ __forceinline__ void qk_mma(float (&s)[NB][4], const uint32_t (&qf)[D / 16][4], uint32_t sk,
+                                       int kbase, int lane) {
+#pragma unroll
+  for (int n = 0; n < NB; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+    for (int n = 0; n < NB; n += 2) {
+      // x4: (keys n*8.., d lo), (same keys, d hi), (keys +8, d lo), (keys +8, d hi)
+      const int mi = lane >> 3, rr = lane & 7;
+      const int key = kbase + n * 8 + (mi >> 1) * 8 + rr;
+      const int chunk = ks * 2 + (mi & 1);
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(sk + tile_off<D>(key, chunk), b0, b1, b2, b3);
+      mma16816(s[n], qf[ks], b0, b1);
+      mma16816(s[n + 1], qf[ks], b2, b3);
+    }
+  }
+}
+
+// O[16 x D] += P(16 x 16 keys, bf16 A fragment) * V[keys kbase.., D]
+template <int D>
+__device__ __forceinline__ void pv_mma(float (&o)[D / 8][4], const uint32_t (&pf)[4], uint32_t sv, int kbase,
+                                       int lane) {
+#pragma unroll
+  for (int n = 0; n < D / 8; n += 2) {
+    // trans x4: (keys 0-7, d n*8), (keys 8-15, d n*8), (keys 0-7, d n*8+8), (keys 8-15, d n*8+8)
+    const int mi = lane >> 3, rr = lane & 7;
+    const int key = kbase + (mi & 1) * 8 + rr;
+    const int chunk = n + (mi >> 1);
+    uint32_t b0, b1, b2, b3;
+    ldmatrix_x4_t(sv + tile_off<D>(key, chunk), b0, b1, b2, b3);
+    mma16816(o[n], pf, b0, b1);
+    mma16816(o[n + 1], pf, b2, b3);
+  }
+}
+
+// online-softmax update of one 16-row fragment set; returns row correction factors
+template <int NB>
+__device__ __forceinline__ void softmax_update(float (&s)[NB][4], float (&m_r)[2], float (&l_r)[2],
+                                               float (&corr)[2]) {
+  float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+  for (int n = 0; n < NB; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) mx[e >> 1] = fmaxf(mx[e >> 1], s[n][e]);
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    corr[r] = mx[r] == -INFINITY ? 1.f : exp2f(m_r[r] - mx[r]);
+    m_r[r] = mx[r];
+  }
+  float rs[2] = {0.f, 0.f};
+#pragma unroll
+  for (int n = 0; n < NB; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float mm = m_r[e >> 1];
+      const float p = mm == -INFINITY ? 0.f : exp2f(s[n][e] - mm);
+      s[n][e] = p;
+      rs[e >> 1] += p;
+    }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) l_r[r] = l_r[r] * corr[r] + rs[r];
+}
+
+// ================================================================== decode
+// Q rows: r < G are heads h*G + r of the sequence's single query.
+template <int D>
+__global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
+  constexpr int NT = 128;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int b = blockIdx.z, h = blockIdx.y, split = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.group;
+  const int L = a.seq_lens[b];
+  const int k_begin = split * a.split_len;
+  const int k_end = min(L, k_begin + a.split_len);
+  const int nq = a.num_kv_heads * G;
+  const bool int8 = a.kv_int8 != 0;
+  const int64_t sbs = a.block_stride / a.head_dim;  // int8 scale pool block stride
+
+  uint8_t* sQ = smem;                                   // [16][D]
+  uint8_t* sK = sQ + 16 * D * 2;                        // 2 x [64][D]
+  uint8_t* sV = sK + 2 * kKT * D * 2;                   // 2 x [64][D]
+  float* sM = reinterpret_cast<float*>(sV + 2 * kKT * D * 2);  // [4][16]
+  float* sL = sM + 64;                                  // [4][16]
+  float* sO = sL + 64;                                  // [16][D]
+
+  const bf16* qsrc = static_cast<const bf16*>(a.q) + ((size_t)b * nq + (size_t)h * G) * D;
+  for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += NT) {
+    const int r = idx / (D / 8), c = idx % (D / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = *reinterpret_cast<const uint4*>(qsrc + (size_t)r * D + c * 8);
+    *reinterpret_cast<uint4*>(sQ + tile_off<D>(r, c)) = v;
+  }
+  const int* btab = a.block_tables + (size_t)b * a.max_blocks;
+  const uint32_t sk0 = smem_u32(sK), sv0 = smem_u32(sV);
+  const int ntiles = k_end > k_begin ? (k_end - k_begin + kKT - 1) / kKT : 0;
+  if (ntiles > 0)
+    load_kv_tile<D, NT>(sk0, sv0, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab, a.block_size,
+                        a.block_stride, sbs, h, k_begin, k_end, sK, sV);
+  cp_async_commit();
+  __syncthreads();
+
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const int mi = lane >> 3, rr = lane & 7;
+    // A x4: (rows 0-7, k lo), (rows 8-15, k lo), (rows 0-7, k hi), (rows 8-15, k hi)
+    const int row = (mi & 1) * 8 + rr, chunk = ks * 2 + (mi >> 1);
+    ldmatrix_x4(smem_u32(sQ) + tile_off<D>(row, chunk), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+  }
+
+  const float sl2 = a.scale * 1.4426950408889634f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      const int nb = buf ^ 1;
+      load_kv_tile<D, NT>(sk0 + nb * kKT * D * 2, sv0 + nb * kKT * D * 2, a.k_cache, a.v_cache, a.k_scale,
+                          a.v_scale, int8, btab, a.block_size, a.block_stride, sbs, h, k_begin + (t + 1) * kKT,
+                          k_end, sK + nb * kKT * D * 2, sV + nb * kKT * D * 2);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t sk = sk0 + buf * kKT * D * 2, sv = sv0 + buf * kKT * D * 2;
+    float s[2][4];
+    qk_mma<D, 2>(s, qf, sk, warp * 16, lane);
+    const int key0 = k_begin + t * kKT + warp * 16;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key0 + n * 8 + 2 * (lane & 3) + (e & 1);
+        s[n][e] = key < k_end ? s[n][e] * sl2 : -INFINITY;
+      }
+    float corr[2];
+    softmax_update<2>(s, m_r, l_r, corr);
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= corr[0]; o[n][1] *= corr[0];
+      o[n][2] *= corr[1]; o[n][3] *= corr[1];
+    }
+    uint32_t pf[4];
+    pf[0] = pack_bf16(s[0][0], s[0][1]);
+    pf[1] = pack_bf16(s[0][2], s[0][3]);
+    pf[2] = pack_bf16(s[1][0], s[1][1]);
+    pf[3] = pack_bf16(s[1][2], s[1][3]);
+    pv_mma<D>(o, pf, sv, warp * 16, lane);
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // ---- merge the 4 warps (each saw different keys)
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = l_r[r];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    l_r[r] = l;
+  }
+  const int r0 = lane >> 2;
+  if ((lane & 3) == 0) {
+    sM[warp * 16 + r0] = m_r[0];
+    sM[warp * 16 + r0 + 8] = m_r[1];
+    sL[warp * 16 + r0] = l_r[0];
+    sL[warp * 16 + r0 + 8] = l_r[1];
+  }
+  for (int i = threadIdx.x; i < 16 * D; i += NT) sO[i] = 0.f;
+  __syncthreads();
+  float wscale[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = r0 + 8 * r;
+    float m = -INFINITY;
+    for (int w = 0; w < 4; ++w) m = fmaxf(m, sM[w * 16 + row]);
+    wscale[r] = (m == -INFINITY || m_r[r] == -INFINITY) ? 0.f : exp2f(m_r[r] - m);
+  }
+  for (int w = 0; w < 4; ++w) {
+    if (w == warp) {
+#pragma unroll
+      for (int n = 0; n < D / 8; ++n) {
+        const int col = n * 8 + 2 * (lane & 3);
+        sO[r0 * D + col] += o[n][0] * wscale[0];
+        sO[r0 * D + col + 1] += o[n][1] * wscale[0];
+        sO[(r0 + 8) * D + col] += o[n][2] * wscale[1];
+        sO[(r0 + 8) * D + col + 1] += o[n][3] * wscale[1];
+      }
+    }
+    __syncthreads();
+  }
+  for (int idx = threadIdx.x; idx < G * D; idx += NT) {
+    const int row = idx / D, col = idx % D;
+    float m = -INFINITY;
+    for (int w = 0; w < 4; ++w) m = fmaxf(m, sM[w * 16 + row]);
+    float l = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sM[w * 16 + row];
+      if (mw != -INFINITY) l += sL[w * 16 + row] * exp2f(mw - m);
+    }
+    const int head = h * G + row;
+    if (a.num_splits == 1) {
+      bf16* out = static_cast<bf16*>(a.out) + ((size_t)b * nq + head) * D;
+      out[col] = __float2bfloat16(l > 0.f ? sO[row * D + col] / l : 0.f);
+    } else {
+      const size_t pidx = ((size_t)b * nq + head) * a.num_splits + split;
+      a.part_o[pidx * D + col] = sO[row * D + col];
+      if (col == 0) {
+        a.part_m[pidx] = m;
+        a.part_l[pidx] = l;
+      }
+    }
+  }
+}
+
+template <int D>
+__global__ void decode_combine_kernel(const DecodeArgs a) {
+  const int b = blockIdx.y, head = blockIdx.x;
+  const int nq = a.num_kv_heads * a.group;
+  const int L = a.seq_lens[b];
+  const int nsplit = min(a.num_splits, (L + a.split_len - 1) / a.split_len);
+  const size_t base = ((size_t)b * nq + head) * a.num_splits;
+  float m = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) m = fmaxf(m, a.part_m[base + s]);
+  float l = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float ms = a.part_m[base + s];
+    if (ms != -INFINITY) l += a.part_l[base + s] * exp2f(ms - m);
+  }
+  for (int col = threadIdx.x; col < D; col += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float ms = a.part_m[base + s];
+      if (ms != -INFINITY) acc += a.part_o[(base + s) * D + col] * exp2f(ms - m);
+    }
+    bf16* out = static_cast<bf16*>(a.out) + ((size_t)b * nq + head) * D;
+    out[col] = __float2bfloat16(l > 0.f ? acc / l : 0.f);
+  }
+}
+
+// ================================================================= prefill
+// Packed rows: r -> query position qb*QPB + r / G, head h*G + r % G.
+template <int D>
+__global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) {
+  constexpr int NT = 128;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int b = blockIdx.z, h = blockIdx.y, qb = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.group;
+  const int QPB = 64 / G;
+  const int q0 = a.cu_seqlens_q[b];
+  const int q_len = a.cu_seqlens_q[b + 1] - q0;
+  if (qb * QPB >= q_len) return;
+  const int kv_len = a.seq_lens[b];
+  const int pos0 = kv_len - q_len;  // position of query 0
+  const int nq = a.num_kv_heads * G;
+  const bool int8 = a.kv_int8 != 0;
+  const int64_t sbs = a.block_stride / a.head_dim;
+
+  uint8_t* sQ = smem;                     // [64][D]
+  uint8_t* sK = sQ + 64 * D * 2;          // 2 x [64][D]
+  uint8_t* sV = sK + 2 * kKT * D * 2;     // 2 x [64][D]
+
+  const bf16* q = static_cast<const bf16*>(a.q);
+  for (int idx = threadIdx.x; idx < 64 * (D / 8); idx += NT) {
+    const int r = idx / (D / 8), c = idx % (D / 8);
+    const int qi = qb * QPB + r / G, head = h * G + r % G;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (qi < q_len) v = *reinterpret_cast<const uint4*>(q + ((size_t)(q0 + qi) * nq + head) * D + c * 8);
+    *reinterpret_cast<uint4*>(sQ + tile_off<D>(r, c)) = v;
+  }
+  const int* btab = a.block_tables + (size_t)b * a.max_blocks;
+  const int last_q = min(q_len, (qb + 1) * QPB) - 1;
+  const int k_end = min(kv_len, pos0 + last_q + 1);  // causal bound of the block's last query
+  const int ntiles = (k_end + kKT - 1) / kKT;
+  const uint32_t sk0 = smem_u32(sK), sv0 = smem_u32(sV);
+  load_kv_tile<D, NT>(sk0, sv0, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab, a.block_size,
+                      a.block_stride, sbs, h, 0, k_end, sK, sV);
+  cp_async_commit();
+  __syncthreads();
+
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const int mi = lane >> 3, rr = lane & 7;
+    const int row = warp * 16 + (mi & 1) * 8 + rr, chunk = ks * 2 + (mi >> 1);
+    ldmatrix_x4(smem_u32(sQ) + tile_off<D>(row, chunk), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+  }
+  int qpos[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = warp * 16 + (lane >> 2) + 8 * r;
+    const int qi = qb * QPB + row / G;
+    qpos[r] = qi < q_len ? pos0 + qi : -1;
+  }
+  const float sl2 = a.scale * 1.4426950408889634f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      const int nb = buf ^ 1;
+      load_kv_tile<D, NT>(sk0 + nb * kKT * D * 2, sv0 + nb * kKT * D * 2, a.k_cache, a.v_cache, a.k_scale,
+                          a.v_scale, int8, btab, a.block_size, a.block_stride, sbs, h, (t + 1) * kKT, k_end,
+                          sK + nb * kKT * D * 2, sV + nb * kKT * D * 2);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t sk = sk0 + buf * kKT * D * 2, sv = sv0 + buf * kKT * D * 2;
+    float s[8][4];
+    qk_mma<D, 8>(s, qf, sk, 0, lane);
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = t * kKT + n * 8 + 2 * (lane & 3) + (e & 1);
+        s[n][e] = (key <= qpos[e >> 1]) ? s[n][e] * sl2 : -INFINITY;
+      }
+    float corr[2];
+    softmax_update<8>(s, m_r, l_r, corr);
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= corr[0]; o[n][1] *= corr[0];
+      o[n][2] *= corr[1]; o[n][3] *= corr[1];
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {  // 16-key chunks of the 64-key tile
+      uint32_t pf[4];
+      pf[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pf[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pf[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pf[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      pv_mma<D>(o, pf, sv, kk * 16, lane);
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = l_r[r];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    l_r[r] = l;
+  }
+  bf16* out = static_cast<bf16*>(a.out);
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = warp * 16 + (lane >> 2) + 8 * r;
+    const int qi = qb * QPB + row / G, head = h * G + row % G;
+    if (qi >= q_len) continue;
+    const float inv = l_r[r] > 0.f ? 1.f / l_r[r] : 0.f;
+    bf16* dst = out + ((size_t)(q0 + qi) * nq + head) * D;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      const int col = n * 8 + 2 * (lane & 3);
+      *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
+    }
+  }
+}
+
+// --------------------------------------------------------------- launchers
+static void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <int D>
+static int decode_smem() { return 16 * D * 2 + 4 * kKT * D * 2 + 2 * 64 * 4 + 16 * D * 4; }
+template <int D>
+static int prefill_smem() { return 64 * D * 2 + 4 * kKT * D * 2; }
+
+void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
+  if (B == 0) return;
+  if (a.group > 16 || 64 % a.group) throw std::runtime_error("decode attention: GQA group must divide 64 and be <= 16");
+  if (a.split_len % kKT) throw std::runtime_error("decode attention: split_len % 64");
+  if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("decode attention: int8 KV needs scales");
+  dim3 grid(a.num_splits, a.num_kv_heads, B);
+  if (a.head_dim == 128) {
+    static bool set = false;
+    if (!set) { cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<128>()); set = true; }
+    decode_attn_kernel<128><<<grid, 128, decode_smem<128>(), s>>>(a);
+    if (a.num_splits > 1) decode_combine_kernel<128><<<dim3(a.num_kv_heads * a.group, B), 128, 0, s>>>(a);
+  } else if (a.head_dim == 64) {
+    static bool set = false;
+    if (!set) { cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<64>()); set = true; }
+    decode_attn_kernel<64><<<grid, 128, decode_smem<64>(), s>>>(a);
+    if (a.num_splits > 1) decode_combine_kernel<64><<<dim3(a.num_kv_heads * a.group, B), 64, 0, s>>>(a);
+  } else {
+    throw std::runtime_error("decode attention: head_dim must be 64 or 128");
+  }
+  check_launch("paged_decode_attn");
+}
+
+void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t s) {
+  if (B == 0 || max_q_len == 0) return;
+  if (a.group > 16 || 64 % a.group) throw std::runtime_error("prefill attention: GQA group must divide 64");
+  if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("prefill attention: int8 KV needs scales");
+  const int QPB = 64 / a.group;
+  dim3 grid((max_q_len + QPB - 1) / QPB, a.num_kv_heads, B);
+  if (a.head_dim == 128) {
+    static bool set = false;
+    if (!set) { cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<128>()); set = true; }
+    prefill_attn_kernel<128><<<grid, 128, prefill_smem<128>(), s>>>(a);
+  } else if (a.head_dim == 64) {
+    static bool set = false;
+    if (!set) { cudaFuncSetAttribute(prefill_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<64>()); set = true; }
+    prefill_attn_kernel<64><<<grid, 128, prefill_smem<64>(), s>>>(a);
+  } else {
+    throw std::runtime_error("prefill attention: head_dim must be 64 or 128");
+  }
+  check_launch("paged_prefill_attn");
+}
+
+}  // namespace b200

@@ -1,0 +1,412 @@
+// Memory-bound fused ops of the Qwen3-MoE layer (sm_100a).
+//
+//   embed_gather             token-id row gather (reference: VocabParallelEmbedding,
+//                            nanovllm/layers/embed_head.py:34-42)
+//   rmsnorm / add_rmsnorm    reference numerics of nanovllm/layers/layernorm.py:18-38:
+//                            fp32 statistics, bf16 round, then bf16 weight multiply
+//   moe_combine_add_rmsnorm  fixed-order top-k slot sum (nanovllm/kernels/moe_fusion.py:31-50)
+//                            + residual add + the next RMSNorm, one pass over the row
+//   qknorm_rope_kvstore      per-head q/k RMSNorm, neox RoPE and the paged KV store in
+//                            one kernel (qwen3.py:82-86, rotary_embedding.py:7-16,
+//                            attention.py:9-30); int8 KV gets a per-(token, head) scale
+//   router_topk              fp32 softmax over experts, top-k, renormalise, bf16-round
+//                            the weights, per-expert counts (qwen3_moe.py:389-395)
+//   moe_permute              expert-sorted copy of the routed rows (qwen3_moe.py:219-245)
+//
+// Rows are processed with 16-byte vector accesses; one CTA (or warp) per token.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <algorithm>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "sm100.cuh"
+#include "fused_ops.h"
+
+namespace b200 {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(p[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  __syncthreads();
+  return s;
+}
+
+// ------------------------------------------------------------ embedding
+__global__ void embed_gather_kernel(const int* __restrict__ ids, const bf16* __restrict__ table,
+                                    bf16* __restrict__ out, int H, int V, int* status) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= V) {  // the host validates ids; never read out of bounds
+    record_status(status, kStatusBadShape);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// ------------------------------------------------------------- RMSNorm
+// H = NT * 8 * VPT; one CTA per token.
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* res_in,
+                                                     const bf16* __restrict__ w, bf16* __restrict__ out,
+                                                     bf16* res_out, int H, float eps) {
+  __shared__ float red[NT / 32];
+  const size_t base = (size_t)blockIdx.x * H;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int idx = (threadIdx.x + j * NT) * 8;
+    unpack8(*reinterpret_cast<const uint4*>(x + base + idx), v[j]);
+    if (res_in != nullptr) {
+      float r[8];
+      unpack8(*reinterpret_cast<const uint4*>(res_in + base + idx), r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] += r[e];
+      *reinterpret_cast<uint4*>(res_out + base + idx) = pack8(v[j]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+  }
+  const float inv = rsqrtf(block_sum<NT>(ss, red) / H + eps);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int idx = (threadIdx.x + j * NT) * 8;
+    float wf[8], o[8];
+    unpack8(*reinterpret_cast<const uint4*>(w + idx), wf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = bf16r(v[j][e] * inv) * wf[e];
+    *reinterpret_cast<uint4*>(out + base + idx) = pack8(o);
+  }
+}
+
+// Combine the top-k expert slots of each token in fixed order, add the
+// residual, and normalise with the next RMSNorm.
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) moe_combine_kernel(const bf16* __restrict__ slots, int topk,
+                                                         bf16* residual, const bf16* __restrict__ w,
+                                                         bf16* __restrict__ out, int H, float eps) {
+  __shared__ float red[NT / 32];
+  const int t = blockIdx.x;
+  const size_t base = (size_t)t * H;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int idx = (threadIdx.x + j * NT) * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < topk; ++k) {
+      float s[8];
+      unpack8(*reinterpret_cast<const uint4*>(slots + ((size_t)t * topk + k) * H + idx), s);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += s[e];
+    }
+    float r[8];
+    unpack8(*reinterpret_cast<const uint4*>(residual + base + idx), r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[j][e] = bf16r(acc[e]) + r[e];
+    *reinterpret_cast<uint4*>(residual + base + idx) = pack8(v[j]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+  }
+  const float inv = rsqrtf(block_sum<NT>(ss, red) / H + eps);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int idx = (threadIdx.x + j * NT) * 8;
+    float wf[8], o[8];
+    unpack8(*reinterpret_cast<const uint4*>(w + idx), wf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = bf16r(v[j][e] * inv) * wf[e];
+    *reinterpret_cast<uint4*>(out + base + idx) = pack8(o);
+  }
+}
+
+// ------------------------------------------------ q/k norm + RoPE + KV store
+// One CTA per token, one warp per head (q heads, then k heads, then v heads).
+// Lane l owns elements {l*E2 .. l*E2+E2-1} of each half (E2 = D/64).
+template <int D>
+__global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
+  constexpr int E2 = D / 64;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = a.num_q_heads, nkv = a.num_kv_heads;
+  const int pos = a.positions[t];
+  const int slot = a.slot_mapping[t];
+  const bf16* row = static_cast<const bf16*>(a.qkv) + (size_t)t * a.qkv_stride;
+  const float* cs = a.cos_sin + (size_t)pos * D;  // [cos(D/2) | sin(D/2)]
+  for (int h = warp; h < nq + 2 * nkv; h += blockDim.x >> 5) {
+    const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
+    const bf16* src = row + (size_t)h * D;
+    float x1[E2], x2[E2];
+#pragma unroll
+    for (int e = 0; e < E2; ++e) {
+      x1[e] = __bfloat162float(src[lane * E2 + e]);
+      x2[e] = __bfloat162float(src[D / 2 + lane * E2 + e]);
+    }
+    if (is_q || is_k) {
+      const bf16* nw = static_cast<const bf16*>(is_q ? a.q_norm_w : a.k_norm_w);
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < E2; ++e) ss += x1[e] * x1[e] + x2[e] * x2[e];
+      const float inv = rsqrtf(warp_sum(ss) / D + a.eps);
+#pragma unroll
+      for (int e = 0; e < E2; ++e) {
+        const int i1 = lane * E2 + e, i2 = D / 2 + i1;
+        // the norm output is bf16 (normalise, round, bf16 weight multiply, round)
+        x1[e] = bf16r(bf16r(x1[e] * inv) * __bfloat162float(nw[i1]));
+        x2[e] = bf16r(bf16r(x2[e] * inv) * __bfloat162float(nw[i2]));
+        const float c = cs[i1], s = cs[D / 2 + i1];
+        const float y1 = x1[e] * c - x2[e] * s;
+        const float y2 = x2[e] * c + x1[e] * s;
+        x1[e] = y1;
+        x2[e] = y2;
+      }
+    }
+    if (is_q) {
+      bf16* dst = static_cast<bf16*>(a.q_out) + ((size_t)t * nq + h) * D;
+#pragma unroll
+      for (int e = 0; e < E2; ++e) {
+        dst[lane * E2 + e] = __float2bfloat16(x1[e]);
+        dst[D / 2 + lane * E2 + e] = __float2bfloat16(x2[e]);
+      }
+    } else if (slot >= 0) {
+      const int kvh = is_k ? h - nq : h - nq - nkv;
+      const int blk = slot / a.block_size, bo = slot % a.block_size;
+      const int64_t off = (int64_t)blk * a.block_stride + ((int64_t)kvh * a.block_size + bo) * D;
+      const int64_t soff = (int64_t)blk * a.scale_block_stride + (int64_t)kvh * a.block_size + bo;
+      if (a.kv_int8) {
+        // per-(token, head) absmax scale, round-to-nearest into [-127, 127]
+        float m = 0.f;
+#pragma unroll
+        for (int e = 0; e < E2; ++e) m = fmaxf(m, fmaxf(fabsf(bf16r(x1[e])), fabsf(bf16r(x2[e]))));
+        m = warp_max(m);
+        const float scale = m > 0.f ? m / 127.f : 1.f;
+        int8_t* dst = reinterpret_cast<int8_t*>(is_k ? a.k_cache : a.v_cache) + off;
+#pragma unroll
+        for (int e = 0; e < E2; ++e) {
+          dst[lane * E2 + e] = (int8_t)max(-127, min(127, __float2int_rn(bf16r(x1[e]) / scale)));
+          dst[D / 2 + lane * E2 + e] = (int8_t)max(-127, min(127, __float2int_rn(bf16r(x2[e]) / scale)));
+        }
+        if (lane == 0) (is_k ? a.k_scale : a.v_scale)[soff] = scale;
+      } else {
+        bf16* dst = reinterpret_cast<bf16*>(is_k ? a.k_cache : a.v_cache) + off;
+#pragma unroll
+        for (int e = 0; e < E2; ++e) {
+          dst[lane * E2 + e] = __float2bfloat16(x1[e]);
+          dst[D / 2 + lane * E2 + e] = __float2bfloat16(x2[e]);
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------- router
+// One warp per token; E <= 32 * EPL.  Logits are rounded to bf16 first: the
+// reference's gate GEMM returns bf16 (qwen3_moe.py:390).
+template <int EPL>
+__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int topk, int renorm,
+                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* row = logits + (size_t)warp * ld;
+  float p[EPL];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = j * 32 + lane;
+    p[j] = e < E ? bf16r(row[e]) : -INFINITY;
+    mx = fmaxf(mx, p[j]);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = j * 32 + lane;
+    p[j] = e < E ? __expf(p[j] - mx) : 0.f;
+    sum += p[j];
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) p[j] = j * 32 + lane < E ? p[j] * inv : -1.f;
+  float sel_w[8];
+  int sel_e[8];
+  float wsum = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    // warp argmax, lowest expert id wins ties
+    float bv = -2.f;
+    int be = 1 << 30;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = j * 32 + lane;
+      if (p[j] > bv || (p[j] == bv && e < be)) { bv = p[j]; be = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+    }
+    sel_w[k] = bv;
+    sel_e[k] = be;
+    wsum += bv;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (j * 32 + lane == be) p[j] = -1.f;
+  }
+  if (lane < topk) {
+    float wv = 0.f;
+    int ev = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k == lane) { wv = sel_w[k]; ev = sel_e[k]; }
+    if (renorm) wv = wv / wsum;
+    ids[(size_t)warp * topk + lane] = ev;
+    weights[(size_t)warp * topk + lane] = bf16r(wv);  // the reference casts weights to bf16
+    if (counts != nullptr) atomicAdd(&counts[ev], 1);
+  }
+}
+
+// Each warp copies one routed (token, k) row to its expert-sorted position.
+__global__ void moe_permute_kernel(const bf16* __restrict__ x, const int* __restrict__ ids, int T, int topk,
+                                   int E, int H, const int* __restrict__ counts, int* __restrict__ cursor,
+                                   bf16* __restrict__ x_perm, int* __restrict__ slot_of_row,
+                                   int* __restrict__ offsets_out) {
+  __shared__ int offs[kMaxExperts + 1];
+  if (threadIdx.x < 32) {
+    const int per = (E + 31) / 32;
+    const int lane = threadIdx.x;
+    int e0 = lane * per, e1 = min(E, e0 + per), s = 0;
+    for (int e = e0; e < e1; ++e) s += counts[e];
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int pre = incl - s;
+    for (int e = e0; e < e1; ++e) { offs[e] = pre; pre += counts[e]; }
+    if (lane == 31) offs[E] = incl;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && offsets_out != nullptr)
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets_out[e] = offs[e];
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T * topk) return;
+  const int t = warp / topk;
+  const int e = ids[warp];
+  if (e < 0 || e >= E) return;
+  int pos = 0;
+  if (lane == 0) pos = offs[e] + atomicAdd(&cursor[e], 1);
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  if (lane == 0) slot_of_row[pos] = warp;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * H);
+  uint4* dst = reinterpret_cast<uint4*>(x_perm + (size_t)pos * H);
+  for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+}
+
+// --------------------------------------------------------------- launchers
+static void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,
+                  cudaStream_t s) {
+  if (T == 0) return;
+  if (H % 8) throw std::runtime_error("embed_gather: H % 8");
+  embed_gather_kernel<<<T, 256, 0, s>>>(ids, (const bf16*)table, (bf16*)out, H, V, status);
+  check_launch("embed_gather");
+}
+
+void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,
+             float eps, cudaStream_t s) {
+  if (T == 0) return;
+  const bf16 *X = (const bf16*)x, *R = (const bf16*)res_in, *W = (const bf16*)w;
+  bf16 *O = (bf16*)out, *RO = (bf16*)res_out;
+  if (H == 2048) rmsnorm_kernel<256, 1><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps);
+  else if (H == 4096) rmsnorm_kernel<256, 2><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps);
+  else if (H == 256) rmsnorm_kernel<32, 1><<<T, 32, 0, s>>>(X, R, W, O, RO, H, eps);
+  else if (H == 512) rmsnorm_kernel<64, 1><<<T, 64, 0, s>>>(X, R, W, O, RO, H, eps);
+  else if (H == 1024) rmsnorm_kernel<128, 1><<<T, 128, 0, s>>>(X, R, W, O, RO, H, eps);
+  else throw std::runtime_error("rmsnorm: unsupported hidden size " + std::to_string(H));
+  check_launch("rmsnorm");
+}
+
+void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
+                             int H, float eps, cudaStream_t s) {
+  if (T == 0) return;
+  const bf16 *S = (const bf16*)slots, *W = (const bf16*)w;
+  bf16 *R = (bf16*)residual, *O = (bf16*)out;
+  if (H == 2048) moe_combine_kernel<256, 1><<<T, 256, 0, s>>>(S, topk, R, W, O, H, eps);
+  else if (H == 4096) moe_combine_kernel<256, 2><<<T, 256, 0, s>>>(S, topk, R, W, O, H, eps);
+  else if (H == 256) moe_combine_kernel<32, 1><<<T, 32, 0, s>>>(S, topk, R, W, O, H, eps);
+  else if (H == 512) moe_combine_kernel<64, 1><<<T, 64, 0, s>>>(S, topk, R, W, O, H, eps);
+  else if (H == 1024) moe_combine_kernel<128, 1><<<T, 128, 0, s>>>(S, topk, R, W, O, H, eps);
+  else throw std::runtime_error("moe_combine: unsupported hidden size " + std::to_string(H));
+  check_launch("moe_combine_add_rmsnorm");
+}
+
+void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s) {
+  if (T == 0) return;
+  const int heads = a.num_q_heads + 2 * a.num_kv_heads;
+  const int threads = 32 * std::min(heads, 16);
+  if (a.head_dim == 128) qknorm_rope_kvstore_kernel<128><<<T, threads, 0, s>>>(a);
+  else if (a.head_dim == 64) qknorm_rope_kvstore_kernel<64><<<T, threads, 0, s>>>(a);
+  else throw std::runtime_error("qknorm_rope_kvstore: head_dim must be 64 or 128");
+  check_launch("qknorm_rope_kvstore");
+}
+
+void router_topk(const float* logits, int ld, int T, int E, int topk, bool renorm, int* ids, float* weights,
+                 int* counts, cudaStream_t s) {
+  if (T == 0) return;
+  if (topk > 8 || topk < 1) throw std::runtime_error("router_topk: topk must be in [1, 8]");
+  const int blocks = (T * 32 + 255) / 256;
+  if (E <= 32) router_topk_kernel<1><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else if (E <= 64) router_topk_kernel<2><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else if (E <= 128) router_topk_kernel<4><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else if (E <= 256) router_topk_kernel<8><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else throw std::runtime_error("router_topk: at most 256 experts");
+  check_launch("router_topk");
+}
+
+void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
+                 void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s) {
+  if (E > kMaxExperts) throw std::runtime_error("moe_permute: too many experts");
+  const int rows = T * topk;
+  const int blocks = std::max(1, (rows * 32 + 255) / 256);
+  moe_permute_kernel<<<blocks, 256, 0, s>>>((const bf16*)x, ids, T, topk, E, H, counts, cursor, (bf16*)x_perm,
+                                            slot_of_row, offsets_out);
+  check_launch("moe_permute");
+}
+
+}  // namespace b200

@@ -1,0 +1,474 @@
+// Grouped weight x activation GEMM on tcgen05 (sm_100a).
+//
+//   D_g^T[m, n] = sum_k  W_g[m, k] * X[row_off[g] + n, k]      for every group g
+//
+// W (the "A" operand, M = output features) is either a 128x128 block-scaled
+// e4m3 weight (the checkpoint format: w = q * scale_inv[m/128, k/128]) or a
+// plain bf16 weight.  X (the "B" operand, N = tokens) is bf16.  One CTA per SM
+// runs a persistent loop over (group, n-tile, m-tile) work items computed on
+// the device from per-group token counts, so the launch needs no host sync and
+// is CUDA-graph safe.  Roles (320 threads):
+//
+//   warp 0     TMA producer: fp8/bf16 weight tile + bf16 activation tile per stage
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-5  dequantisers: e4m3 * scale -> bf16 into the 128B-swizzled UMMA
+//              layout (exactly bf16(float(q) * scale), the reference's
+//              load-time dequant, done per tile in shared memory)
+//   warps 6-9  epilogue: tcgen05.ld of the double-buffered TMEM accumulator,
+//              fused op, global store
+//
+// Epilogues: bf16 store, fp32 store (router / LM-head logits), SiLU(gate)*up of
+// a gate/up tile pair (two MMAs into adjacent TMEM columns), and the MoE "down"
+// epilogue that scales by the routing weight and scatters each row to its
+// (token, k) slot so the combine is a fixed-order sum.
+//
+// Reference ops replaced: torch._grouped_mm / torch.bmm expert GEMMs and
+// F.linear (nanovllm/models/qwen3_moe.py:216-340, nanovllm/layers/linear.py:73),
+// fused_silu_and_mul (nanovllm/kernels/moe_fusion.py:19-28) and the weighted
+// slot scatter (qwen3_moe.py:270-279).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "sm100.cuh"
+#include "gemm_tc.h"
+
+namespace b200 {
+
+constexpr int kThreads = 320;
+constexpr int kMaxGroups = 512;
+constexpr int kBK = 64;            // K elements per pipeline stage (128 B of bf16)
+constexpr int kSmemBudget = 225 * 1024;
+
+template <int BN, bool PAIR, bool AFP8>
+struct GemmCfg {
+  static constexpr int NA = PAIR ? 2 : 1;
+  static constexpr int A16_BYTES = 128 * kBK * 2;     // 16 KB bf16 tile
+  static constexpr int A8_BYTES = AFP8 ? 128 * kBK : 0;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = NA * A16_BYTES + B_BYTES + NA * A8_BYTES;
+  static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4;
+  static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EXTRA + 1024;
+  static constexpr int ACC_COLS = NA * BN;
+  static constexpr int TMEM_COLS_RAW = 2 * ACC_COLS;
+  static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
+                                   : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
+  static_assert(STAGES >= 2, "not enough shared memory for two stages");
+  static_assert(TMEM_COLS_RAW <= 512, "accumulators exceed TMEM");
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16,256]");
+  static constexpr uint32_t TX_BYTES = NA * (AFP8 ? A8_BYTES : A16_BYTES) + B_BYTES;
+};
+
+struct TileCoord {
+  int g, j, i;
+};
+
+// tile_prefix[g] = first tile of group g (exclusive prefix, ngroups+1 entries);
+// the owner of tile t is the last g with tile_prefix[g] <= t.
+__device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, int ngroups, int m_tiles) {
+  int lo = 0, hi = ngroups;
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (tile_prefix[mid] <= t) lo = mid; else hi = mid;
+  }
+  int local = t - tile_prefix[lo];
+  TileCoord c;
+  c.g = lo;
+  c.j = local / m_tiles;
+  c.i = local % m_tiles;
+  return c;
+}
+
+template <int BN, bool PAIR, bool AFP8, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+               const GemmArgs args) {
+  using C = GemmCfg<BN, PAIR, AFP8>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  // ---- shared-memory carve-up
+  uint8_t* stage_base = smem;
+  uint8_t* extra = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);
+  uint64_t* conv_bar = full_bar + 8;
+  uint64_t* empty_bar = conv_bar + 8;
+  uint64_t* accf_bar = empty_bar + 8;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* conv_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  int* tile_prefix = reinterpret_cast<int*>(extra + 4096);
+  int* row_off = tile_prefix + (kMaxGroups + 1);
+
+  auto A16 = [&](int s, int a) { return stage_base + s * C::STAGE_BYTES + a * C::A16_BYTES; };
+  auto Bt = [&](int s) { return stage_base + s * C::STAGE_BYTES + C::NA * C::A16_BYTES; };
+  auto A8 = [&](int s, int a) {
+    return stage_base + s * C::STAGE_BYTES + C::NA * C::A16_BYTES + C::B_BYTES + a * C::A8_BYTES;
+  };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ngroups = args.num_groups;
+  const int m_tiles = args.m_tiles;
+
+  // ---- per-CTA schedule: prefix sums of tiles and rows over groups (one warp)
+  if (warp == 0) {
+    const int per = (ngroups + 31) / 32;
+    int g0 = lane * per, g1 = min(ngroups, g0 + per);
+    int tiles = 0, rows = 0;
+    for (int g = g0; g < g1; ++g) {
+      int c = args.group_count[g];
+      tiles += (c + BN - 1) / BN * m_tiles;
+      rows += c;
+    }
+    int tincl = tiles, rincl = rows;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int tv = __shfl_up_sync(0xffffffffu, tincl, o);
+      int rv = __shfl_up_sync(0xffffffffu, rincl, o);
+      if (lane >= o) { tincl += tv; rincl += rv; }
+    }
+    int tpre = tincl - tiles, rpre = rincl - rows;
+    for (int g = g0; g < g1; ++g) {
+      int c = args.group_count[g];
+      tile_prefix[g] = tpre;
+      row_off[g] = args.group_offset ? args.group_offset[g] : rpre;
+      tpre += (c + BN - 1) / BN * m_tiles;
+      rpre += c;
+    }
+    if (lane == 31) tile_prefix[ngroups] = tincl;
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&conv_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_tiles = tile_prefix[ngroups];
+  const int k_stages = args.k_stages;
+  int* status = args.status;
+
+  if (warp == 0) {
+    // ===================================================== TMA producer
+    if (elect_one()) {
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
+        const int a_row = tc.g * args.a_rows_per_group + tc.i * 128;
+        const int b_row = row_off[tc.g] + tc.j * BN;
+        for (int ks = 0; ks < k_stages; ++ks) {
+          if (!mbar_wait(&empty_bar[s], phase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[s], C::TX_BYTES);
+          const int x = ks * kBK;
+          if constexpr (AFP8) {
+            tma_load_2d(A8(s, 0), &tmap_a, &full_bar[s], x, a_row);
+            if constexpr (PAIR) tma_load_2d(A8(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
+          } else {
+            tma_load_2d(A16(s, 0), &tmap_a, &full_bar[s], x, a_row);
+            if constexpr (PAIR) tma_load_2d(A16(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
+          }
+          tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
+          if (++s == C::STAGES) { s = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // aborted: give loads already issued (valid global sources, so they
+        // finish in microseconds) 1 ms to land before the CTA can exit
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1) {
+    // ====================================================== MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+      int s = 0;
+      uint32_t phase = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
+        const int abuf = lt & 1;
+        const uint32_t aphase = (lt >> 1) & 1;
+        if (!mbar_wait(&acce_bar[abuf], aphase ^ 1, status, kStatusTimeoutAccEmpty, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_base = tmem_base + abuf * C::ACC_COLS;
+        for (int ks = 0; ks < k_stages; ++ks) {
+          if (!mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) { ok = false; break; }
+          if constexpr (AFP8) {
+            if (!mbar_wait(&conv_bar[s], phase, status, kStatusTimeoutConv, abort_flag)) { ok = false; break; }
+          }
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(Bt(s));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t bdesc = umma_sdesc_sw128(b_addr + k * 32);
+#pragma unroll
+            for (int a = 0; a < C::NA; ++a) {
+              const uint64_t adesc = umma_sdesc_sw128(smem_u32(A16(s, a)) + k * 32);
+              umma_f16_ss(d_base + a * BN, adesc, bdesc, idesc, (ks | k) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty_bar[s]);
+          if (++s == C::STAGES) { s = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&accf_bar[abuf]);
+      }
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ================================================= dequantisers
+    if constexpr (AFP8) {
+      const int c = threadIdx.x - 64;  // 0..127
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
+        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * args.scale_k_blocks;
+        for (int ks = 0; ks < k_stages; ++ks) {
+          // one thread waits, the verdict is broadcast so all 128 leave together
+          if (c == 0) *conv_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) ? 1 : 0;
+          named_barrier_sync(1, 128);
+          if (!*conv_ok) { ok = false; break; }
+          const int kb = (ks * kBK) / 128;
+#pragma unroll
+          for (int a = 0; a < C::NA; ++a) {
+            const int mb = tc.i + (a ? args.pair_row_offset / 128 : 0);
+            const float scale = __ldg(sc + mb * args.scale_k_blocks + kb);
+            const uint8_t* src = A8(s, a);
+            uint8_t* dst = A16(s, a);
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int chunk = c + 128 * it;
+              const int row = chunk >> 2, c16 = chunk & 3;
+              const uint4 q = *reinterpret_cast<const uint4*>(src + row * 64 + c16 * 16);
+              const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+              uint32_t o[8];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] & 0xFFFFu), __NV_E4M3);
+                __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] >> 16), __NV_E4M3);
+                float2 flo = __half22float2(*reinterpret_cast<__half2*>(&lo));
+                float2 fhi = __half22float2(*reinterpret_cast<__half2*>(&hi));
+                __nv_bfloat162 blo = __floats2bfloat162_rn(flo.x * scale, flo.y * scale);
+                __nv_bfloat162 bhi = __floats2bfloat162_rn(fhi.x * scale, fhi.y * scale);
+                o[2 * h] = *reinterpret_cast<uint32_t*>(&blo);
+                o[2 * h + 1] = *reinterpret_cast<uint32_t*>(&bhi);
+              }
+              const int sw = row & 7;
+              const int p0 = (2 * c16) ^ sw, p1 = (2 * c16 + 1) ^ sw;
+              *reinterpret_cast<uint4*>(dst + row * 128 + p0 * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4*>(dst + row * 128 + p1 * 16) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+          }
+          fence_proxy_async_smem();
+          named_barrier_sync(1, 128);
+          if (c == 0) mbar_arrive(&conv_bar[s]);
+          if (++s == C::STAGES) { s = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else {
+    // ====================================================== epilogue
+    const int q = warp & 3;              // TMEM lane quarter this warp may access
+    const int m_local = q * 32 + lane;
+    int lt = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
+      TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
+      const int abuf = lt & 1;
+      const uint32_t aphase = (lt >> 1) & 1;
+      if (!mbar_wait(&accf_bar[abuf], aphase, status, kStatusTimeoutAccFull, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const int count = args.group_count[tc.g];
+      const int ncols = min(BN, count - tc.j * BN);
+      const int row0 = row_off[tc.g] + tc.j * BN;
+      const uint32_t t_base = tmem_base + (uint32_t(q * 32) << 16) + abuf * C::ACC_COLS;
+      const int m_out = tc.i * 128 + m_local;
+#pragma unroll 1
+      for (int c16 = 0; c16 < BN / 16; ++c16) {
+        if (c16 * 16 >= ncols) break;
+        float v[16];
+        tmem_ld16(t_base + c16 * 16, v);
+        if constexpr (EPI == kEpiSiluPair) {
+          float u[16];
+          tmem_ld16(t_base + BN + c16 * 16, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int col = c16 * 16 + n;
+            if (col < ncols) {
+              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+              out[(size_t)(row0 + col) * args.ld_out + m_out] = __float2bfloat16(silu(v[n]) * u[n]);
+            }
+          }
+        } else {
+          tmem_ld_wait();
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int col = c16 * 16 + n;
+            if (col < ncols) {
+              const int row = row0 + col;
+              const int m_glob = tc.g * args.out_group_stride + m_out;
+              if constexpr (EPI == kEpiBf16) {
+                __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+                out[(size_t)row * args.ld_out + m_glob] = __float2bfloat16(v[n]);
+              } else if constexpr (EPI == kEpiF32) {
+                float* out = reinterpret_cast<float*>(args.out);
+                out[(size_t)row * args.ld_out + m_glob] = v[n];
+              } else {  // kEpiScatter
+                const int slot = args.slot_of_row[row];
+                const float w = args.slot_weight[slot];
+                __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+                out[(size_t)slot * args.ld_out + m_out] = __float2bfloat16(v[n] * w);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[abuf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult qres;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qres);
+    if (e != cudaSuccess || qres != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+CUtensorMap make_tmap_2d(const void* base, bool is_bf16, int64_t rows, int64_t cols,
+                         int64_t row_stride_bytes, int box_cols, int box_rows, bool swizzle128) {
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(
+      &map, is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return map;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool PAIR, bool AFP8, int EPI>
+static void launch_impl(const GemmLaunch& L, cudaStream_t stream) {
+  using C = GemmCfg<BN, PAIR, AFP8>;
+  auto kern = gemm_tc_kernel<BN, PAIR, AFP8, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr_set = true;
+  }
+  // A: [groups * rows_per_group, K] row-major; box 64 x 128 rows
+  CUtensorMap ta = make_tmap_2d(L.a, !AFP8, (int64_t)L.args.num_groups * L.args.a_rows_per_group,
+                                L.K, L.a_row_stride_bytes, kBK, 128, !AFP8);
+  CUtensorMap tb = make_tmap_2d(L.b, true, L.b_rows, L.K, L.b_row_stride_bytes, kBK, BN, true);
+  // upper bound of work items without reading device counts
+  int64_t max_tiles = ((int64_t)L.b_rows / BN + L.args.num_groups) * L.args.m_tiles;
+  int grid = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, max_tiles));
+  kern<<<grid, kThreads, C::SMEM, stream>>>(ta, tb, L.args);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_tc launch: ") + cudaGetErrorString(e));
+}
+
+template <bool PAIR, bool AFP8, int EPI>
+static void dispatch_bn(int bn, const GemmLaunch& L, cudaStream_t s) {
+  switch (bn) {
+    case 16: launch_impl<16, PAIR, AFP8, EPI>(L, s); return;
+    case 32: launch_impl<32, PAIR, AFP8, EPI>(L, s); return;
+    case 64: launch_impl<64, PAIR, AFP8, EPI>(L, s); return;
+    case 128: launch_impl<128, PAIR, AFP8, EPI>(L, s); return;
+    case 256:
+      if constexpr (!PAIR) { launch_impl<256, PAIR, AFP8, EPI>(L, s); return; }
+      break;
+    default: break;
+  }
+  throw std::runtime_error("unsupported BN " + std::to_string(bn));
+}
+
+void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
+  if (L.args.num_groups < 1 || L.args.num_groups > kMaxGroups) throw std::runtime_error("bad group count");
+  if (L.K % 128 != 0) throw std::runtime_error("K must be a multiple of 128");
+  if (L.args.a_rows_per_group % 128 != 0) throw std::runtime_error("weight rows must be a multiple of 128");
+  if ((reinterpret_cast<uintptr_t>(L.a) & 15) || (reinterpret_cast<uintptr_t>(L.b) & 15))
+    throw std::runtime_error("operands must be 16-byte aligned");
+  if (L.b_row_stride_bytes % 16 != 0) throw std::runtime_error("activation row stride must be a multiple of 16 bytes");
+  const int bn = L.bn;
+  if (L.pair) {
+    if (!L.a_fp8 || L.epi != kEpiSiluPair) throw std::runtime_error("pair mode is fp8 + silu only");
+    dispatch_bn<true, true, kEpiSiluPair>(bn, L, stream);
+    return;
+  }
+  if (L.a_fp8) {
+    if (L.epi == kEpiBf16) dispatch_bn<false, true, kEpiBf16>(bn, L, stream);
+    else if (L.epi == kEpiScatter) dispatch_bn<false, true, kEpiScatter>(bn, L, stream);
+    else throw std::runtime_error("unsupported fp8 epilogue");
+  } else {
+    if (L.epi == kEpiF32) dispatch_bn<false, false, kEpiF32>(bn, L, stream);
+    else if (L.epi == kEpiBf16) dispatch_bn<false, false, kEpiBf16>(bn, L, stream);
+    else throw std::runtime_error("unsupported bf16 epilogue");
+  }
+}
+
+}  // namespace b200

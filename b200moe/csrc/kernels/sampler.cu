@@ -1,0 +1,312 @@
+// Token sampler (sm_100a).  One CTA of 1024 threads per row of fp32 logits.
+//
+//   greedy rows          argmax, lowest token id on ties
+//   sampled rows         logits / temperature -> top-k -> top-p -> min-p ->
+//                        exponential race: argmax_i p_i / E_i with E_i ~ Exp(1)
+//                        (the reference's sampler, nanovllm/layers/sampler.py:112-169,
+//                        which sorts the whole vocabulary for top-k / top-p)
+//
+// No sort: the top-k and top-p thresholds come from an MSB-first radix select
+// over the order-preserving integer image of the scaled logits (4 passes of 8
+// bits; top-k counts tokens per bucket, top-p accumulates probability mass per
+// bucket).  Ties at the threshold are kept.  Random numbers come from the
+// Philox-4x32-10 counter-based generator (Salmon, Moraes, Dror, Shaw:
+// "Parallel random numbers: as easy as 1, 2, 3", SC 2011), keyed by the row's
+// seed and counted by (token id, step offset), so a row's draw does not depend
+// on the batch it runs in.
+//
+// Penalties (repetition on prompt+generated, presence / frequency on
+// generated ids) are applied in place by a separate kernel before sampling.
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "sm100.cuh"
+#include "sampler.h"
+
+namespace b200 {
+
+constexpr int kST = 1024;
+
+__device__ __forceinline__ uint32_t f2ord(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Philox 4x32, 10 rounds (multipliers and Weyl keys from the SC'11 paper).
+__device__ __forceinline__ uint4 philox4x32(uint4 ctr, uint2 key) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(M0, ctr.x), lo0 = M0 * ctr.x;
+    const uint32_t hi1 = __umulhi(M1, ctr.z), lo1 = M1 * ctr.z;
+    ctr = make_uint4(hi1 ^ ctr.y ^ key.x, lo1, hi0 ^ ctr.w ^ key.y, lo0);
+    key.x += W0;
+    key.y += W1;
+  }
+  return ctr;
+}
+
+// uniform in (0, 1]
+__device__ __forceinline__ float u01(uint32_t x) { return (float)((x >> 8) + 1) * (1.0f / 16777216.0f); }
+
+__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float s = l < kST / 32 ? red[l] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (l == 0) red[0] = s;
+  }
+  __syncthreads();
+  const float s = red[0];
+  __syncthreads();
+  return s;
+}
+
+__device__ __forceinline__ float block_reduce_max(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float s = l < kST / 32 ? red[l] : -INFINITY;
+    for (int o = 16; o > 0; o >>= 1) s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (l == 0) red[0] = s;
+  }
+  __syncthreads();
+  const float s = red[0];
+  __syncthreads();
+  return s;
+}
+
+// (value, index) argmax with lowest index on ties
+__device__ __forceinline__ void block_argmax(float& v, int& idx, float* redv, int* redi) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) { redv[w] = v; redi[w] = idx; }
+  __syncthreads();
+  if (w == 0) {
+    v = l < kST / 32 ? redv[l] : -INFINITY;
+    idx = l < kST / 32 ? redi[l] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+    }
+    if (l == 0) { redv[0] = v; redi[0] = idx; }
+  }
+  __syncthreads();
+  v = redv[0];
+  idx = redi[0];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kST) argmax_kernel(const float* __restrict__ logits, int V, int64_t ld,
+                                                     int* __restrict__ out) {
+  __shared__ float redv[32];
+  __shared__ int redi[32];
+  const float* row = logits + (size_t)blockIdx.x * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += kST) {
+    const float v = row[i];
+    if (v > bv) { bv = v; bi = i; }  // strided scan: first hit per thread is its lowest index
+  }
+  block_argmax(bv, bi, redv, redi);
+  if (threadIdx.x == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+}
+
+// Radix select over the ordered image of x/temp among tokens with image >= lo_bound.
+// mode 0: image of the k-th largest value (k counted from the top)
+// mode 1: largest image t such that the probability mass of tokens with image
+//         >= t reaches `target` (mass weight exp(x - M) * invZ)
+__device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t lo_bound, int mode, int k,
+                                 float target, float M, float invZ, uint32_t* hist_u, float* hist_f) {
+  uint32_t prefix = 0, mask = 0;
+  float above_mass = 0.f;
+  uint32_t above_cnt = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += kST) { hist_u[i] = 0; hist_f[i] = 0.f; }
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += kST) {
+      const float x = row[i] * inv_t;
+      const uint32_t o = f2ord(x);
+      if (o < lo_bound || (o & mask) != prefix) continue;
+      const uint32_t bin = (o >> shift) & 0xFFu;
+      if (mode == 0) atomicAdd(&hist_u[bin], 1u);
+      else atomicAdd(&hist_f[bin], __expf(x - M) * invZ);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int l = threadIdx.x;
+      // each lane owns 8 bins, lane 0 the highest
+      float m8[8];
+      uint32_t c8[8];
+      float ms = 0.f;
+      uint32_t cs = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int bin = 255 - (l * 8 + j);
+        m8[j] = hist_f[bin];
+        c8[j] = hist_u[bin];
+        ms += m8[j];
+        cs += c8[j];
+      }
+      float mi = ms;
+      uint32_t ci = cs;
+      for (int o = 1; o < 32; o <<= 1) {
+        const float mv = __shfl_up_sync(0xffffffffu, mi, o);
+        const uint32_t cv = __shfl_up_sync(0xffffffffu, ci, o);
+        if (l >= o) { mi += mv; ci += cv; }
+      }
+      float mpre = mi - ms;
+      uint32_t cpre = ci - cs;
+      int found = -1;
+      float m_before = 0.f;
+      uint32_t c_before = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool hit = mode == 0 ? (above_cnt + cpre + c8[j] >= (uint32_t)k)
+                                   : (above_mass + mpre + m8[j] >= target);
+        if (found < 0 && hit) { found = 255 - (l * 8 + j); m_before = mpre; c_before = cpre; }
+        mpre += m8[j];
+        cpre += c8[j];
+      }
+      const unsigned ball = __ballot_sync(0xffffffffu, found >= 0);
+      const int src = ball ? __ffs(ball) - 1 : 31;
+      const int fbin = __shfl_sync(0xffffffffu, found, src);
+      const float mb = __shfl_sync(0xffffffffu, m_before, src);
+      const uint32_t cb = __shfl_sync(0xffffffffu, c_before, src);
+      if (l == 0) {
+        hist_u[256] = ball ? (uint32_t)fbin : 0u;
+        hist_f[256] = ball ? mb : 0.f;
+        hist_u[257] = ball ? cb : 0u;
+      }
+    }
+    __syncthreads();
+    const uint32_t bin = hist_u[256];
+    above_mass += hist_f[256];
+    above_cnt += hist_u[257];
+    prefix |= bin << shift;
+    mask |= 0xFFu << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+__global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ logits, int V, int64_t ld,
+                                                     SampleArgs a, int* __restrict__ out) {
+  __shared__ float red[32];
+  __shared__ int redi[32];
+  __shared__ uint32_t hist_u[260];
+  __shared__ float hist_f[260];
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * ld;
+  const float temp = a.temperature[r];
+  if (temp < 1e-3f) {  // greedy row
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += kST) {
+      const float v = row[i];
+      if (v > bv) { bv = v; bi = i; }
+    }
+    block_argmax(bv, bi, red, redi);
+    if (threadIdx.x == 0) out[r] = bi == 0x7fffffff ? 0 : bi;
+    return;
+  }
+  const float inv_t = 1.f / temp;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += kST) mx = fmaxf(mx, row[i] * inv_t);
+  const float M = block_reduce_max(mx, red);
+  float z = 0.f;
+  for (int i = threadIdx.x; i < V; i += kST) z += __expf(row[i] * inv_t - M);
+  const float Z = block_reduce_sum(z, red);
+
+  uint32_t lo = 0;  // keep tokens with f2ord(x) >= lo
+  const int top_k = a.top_k ? a.top_k[r] : -1;
+  if (top_k > 0 && top_k < V) lo = radix_select(row, V, inv_t, 0, 0, top_k, 0.f, M, 1.f / Z, hist_u, hist_f);
+  const float top_p = a.top_p ? a.top_p[r] : 1.f;
+  if (top_p < 1.f) {
+    // nucleus mass is measured over the top-k survivors
+    float zk = 0.f;
+    for (int i = threadIdx.x; i < V; i += kST) {
+      const float x = row[i] * inv_t;
+      if (f2ord(x) >= lo) zk += __expf(x - M);
+    }
+    const float Zk = block_reduce_sum(zk, red);
+    const uint32_t tp = radix_select(row, V, inv_t, lo, 1, 0, top_p, M, 1.f / Zk, hist_u, hist_f);
+    lo = max(lo, tp);
+  }
+  const float min_p = a.min_p ? a.min_p[r] : 0.f;
+  if (min_p > 0.f) lo = max(lo, f2ord(M + __logf(min_p)));
+
+  const uint2 key = make_uint2((uint32_t)a.seeds[r], (uint32_t)((uint64_t)a.seeds[r] >> 32));
+  const uint32_t off = a.offsets ? (uint32_t)a.offsets[r] : 0u;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += kST) {
+    const float x = row[i] * inv_t;
+    if (f2ord(x) < lo) continue;
+    const uint4 rnd = philox4x32(make_uint4((uint32_t)i, off, 0x5A3Cu, 0u), key);
+    const float e = -__logf(u01(rnd.x));  // Exp(1)
+    const float score = (x - M) - __logf(fmaxf(e, 1e-20f));
+    if (score > bv) { bv = score; bi = i; }
+  }
+  block_argmax(bv, bi, red, redi);
+  if (threadIdx.x == 0) out[r] = bi == 0x7fffffff ? 0 : bi;
+}
+
+__global__ void penalty_kernel(float* __restrict__ logits, int64_t ld, const int* __restrict__ rows,
+                               const int* __restrict__ ids, const int* __restrict__ gen_counts,
+                               const float* __restrict__ presence, const float* __restrict__ frequency,
+                               const float* __restrict__ repetition, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int r = rows[i];
+  float* p = logits + (size_t)r * ld + ids[i];
+  float v = *p;
+  const float rp = repetition[r];
+  v = v < 0.f ? v * rp : v / rp;
+  const int c = gen_counts[i];
+  if (c > 0) v = v - presence[r] - frequency[r] * (float)c;
+  *p = v;
+}
+
+static void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void argmax_rows(const float* logits, int B, int V, int64_t ld, int* out, cudaStream_t s) {
+  if (B == 0) return;
+  argmax_kernel<<<B, kST, 0, s>>>(logits, V, ld, out);
+  check_launch("argmax_rows");
+}
+
+void sample_rows(const float* logits, int B, int V, int64_t ld, const SampleArgs& a, int* out, cudaStream_t s) {
+  if (B == 0) return;
+  sample_kernel<<<B, kST, 0, s>>>(logits, V, ld, a, out);
+  check_launch("sample_rows");
+}
+
+void apply_penalties(float* logits, int64_t ld, const int* rows, const int* ids, const int* gen_counts,
+                     const float* presence, const float* frequency, const float* repetition, int n,
+                     cudaStream_t s) {
+  if (n == 0) return;
+  penalty_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, ld, rows, ids, gen_counts, presence, frequency,
+                                                 repetition, n);
+  check_launch("apply_penalties");
+}
+
+}  // namespace b200
