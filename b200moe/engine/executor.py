@@ -1,0 +1,231 @@
+"""Runs engine steps on every rank.
+
+One process per GPU.  Rank 0 lives in the engine's process; ranks 1..N-1 are
+spawned workers, each owning its GPU and a :class:`ModelRunner`.  The control
+plane is one duplex pipe per worker carrying small step plans (numpy arrays)
+instead of pickled ``Sequence`` objects, with bounded waits on every reply:
+
+* a worker that dies is seen as EOF on its pipe and raises :class:`RankFailure`
+  on the driver at once;
+* a worker that stops answering raises :class:`RankFailure` after
+  ``rank_timeout_s``;
+* a worker whose driver disappears exits on its own (parent-pid check).
+
+Reference: the SharedMemory pickle channel + ``dist.barrier`` after every
+command (nanovllm/engine/model_runner.py:168-246) and the exit watchdog
+(llm_engine.py:134-177).
+"""
+from __future__ import annotations
+
+import os
+import socket
+import time
+import traceback
+
+import numpy as np
+
+from b200moe.config import Config
+from b200moe.engine.step_plan import StepPlan, build_plan, empty_plan
+
+
+class RankFailure(RuntimeError):
+    """A worker rank died, hung past the limit, or raised."""
+
+
+def free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker_main(config: Config, rank: int, conn, parent_pid: int):
+    try:
+        from b200moe.engine.model_runner import ModelRunner
+        runner = ModelRunner(config, rank)
+        conn.send(("ready", config.num_kvcache_blocks))
+    except BaseException:
+        try:
+            conn.send(("error", traceback.format_exc()))
+        finally:
+            return
+    while True:
+        if not conn.poll(1.0):
+            if os.getppid() != parent_pid:  # driver is gone: leave
+                os._exit(1)
+            continue
+        try:
+            cmd, args = conn.recv()
+        except EOFError:
+            os._exit(1)
+        if cmd == "exit":
+            try:
+                runner.exit()
+            finally:
+                conn.send(("ok", None))
+            return
+        try:
+            res = getattr(runner, cmd)(*args)
+            conn.send(("ok", res))
+        except BaseException:
+            conn.send(("error", traceback.format_exc()))
+
+
+class Executor:
+
+    def __init__(self, config: Config):
+        self.config = config
+        self.world = config.world_size
+        self.dp = config.dp_size
+        self.procs = []
+        self.conns = []
+        from b200moe.engine.model_runner import ModelRunner
+        if self.world > 1:
+            import multiprocessing as mp
+            if not config.distributed_init_method:
+                config.distributed_init_method = f"tcp://127.0.0.1:{free_port()}"
+            ctx = mp.get_context("spawn")
+            for r in range(1, self.world):
+                a, b = ctx.Pipe(duplex=True)
+                p = ctx.Process(target=_worker_main, args=(config, r, b, os.getpid()), daemon=True)
+                p.start()
+                self.procs.append(p)
+                self.conns.append(a)
+        self.runner = ModelRunner(config, 0, self.world)
+        for r, c in enumerate(self.conns, start=1):
+            status, payload = self._recv(r, c, timeout=max(600.0, config.rank_timeout_s))
+            if status != "ready":
+                raise RankFailure(f"rank {r} failed to start:\n{payload}")
+        self.max_blocks = self.runner.max_blocks
+        self._inflight = None
+
+    # ------------------------------------------------------------ plumbing
+    def _recv(self, rank: int, conn, timeout: float | None = None):
+        timeout = self.config.rank_timeout_s if timeout is None else timeout
+        deadline = time.monotonic() + timeout
+        while True:
+            remaining = deadline - time.monotonic()
+            if remaining <= 0:
+                raise RankFailure(f"rank {rank} did not answer within {timeout:.0f} s")
+            try:
+                if conn.poll(min(remaining, 1.0)):
+                    return conn.recv()
+            except (EOFError, OSError) as exc:
+                raise RankFailure(f"rank {rank} exited ({exc!r})") from exc
+            proc = self.procs[rank - 1]
+            if not proc.is_alive():
+                raise RankFailure(f"rank {rank} exited with code {proc.exitcode}")
+
+    def _send_all(self, cmd: str, per_rank_args: list[tuple]):
+        for r, c in enumerate(self.conns, start=1):
+            try:
+                c.send((cmd, per_rank_args[r]))
+            except (BrokenPipeError, OSError) as exc:
+                raise RankFailure(f"rank {r} is gone ({exc!r})") from exc
+
+    def _gather(self) -> list:
+        out = []
+        for r, c in enumerate(self.conns, start=1):
+            status, payload = self._recv(r, c)
+            if status != "ok":
+                raise RankFailure(f"rank {r} raised:\n{payload}")
+            out.append(payload)
+        return out
+
+    def call(self, method: str, *args):
+        """Run ``runner.method(*args)`` on every rank; returns rank 0's result."""
+        self._send_all(method, [args] * self.world)
+        res = getattr(self.runner, method)(*args)
+        self._gather()
+        return res
+
+    def call_rank(self, rank: int, method: str, *args):
+        """Run ``runner.method(*args)`` on one rank only (its private KV pool)."""
+        if rank == 0:
+            return getattr(self.runner, method)(*args)
+        c = self.conns[rank - 1]
+        try:
+            c.send((method, args))
+        except (BrokenPipeError, OSError) as exc:
+            raise RankFailure(f"rank {rank} is gone ({exc!r})") from exc
+        status, payload = self._recv(rank, c)
+        if status != "ok":
+            raise RankFailure(f"rank {rank} raised:\n{payload}")
+        return payload
+
+    def rank_caller(self, rank: int):
+        """Object with ``call(method, *args)`` bound to one rank (KV offload hooks)."""
+        ex = self
+
+        class _Caller:
+            def call(self, method, *args):
+                return ex.call_rank(rank, method, *args)
+        return _Caller()
+
+    # --------------------------------------------------------------- steps
+    def plans(self, batch, grammar_masks: dict | None = None) -> list[StepPlan]:
+        """One plan per rank: all rows on rank 0 (shared attention), or each
+        sequence's rows on its data-parallel rank."""
+        seqs, q, flags = batch.sequences, batch.query_lens, batch.prefill_flags
+        bs = self.config.kvcache_block_size
+        if self.dp == 1:
+            plans = [build_plan(seqs, q, flags, bs, self.max_blocks)] + \
+                    [empty_plan(self.max_blocks) for _ in range(self.world - 1)]
+        else:
+            parts: list[list[int]] = [[] for _ in range(self.world)]
+            for i, s in enumerate(seqs):
+                parts[max(s.dp_rank, 0)].append(i)
+            plans = [build_plan([seqs[i] for i in idx], [q[i] for i in idx], [flags[i] for i in idx], bs,
+                                self.max_blocks, rows=idx) if idx else empty_plan(self.max_blocks)
+                     for idx in parts]
+        if grammar_masks:
+            for p in plans:
+                g = [(r, grammar_masks[br]) for r, br in enumerate(p.rows.tolist()) if br in grammar_masks]
+                if g:
+                    p.grammar_rows = np.asarray([r for r, _ in g], np.int32)
+                    p.grammar_mask = np.stack([m for _, m in g]).astype(np.int32)
+        return plans
+
+    def launch(self, batch, grammar_masks: dict | None = None):
+        plans = self.plans(batch, grammar_masks)
+        self._send_all("run", [(p,) for p in plans])
+        self.runner.launch(plans[0])
+        self._inflight = (plans, len(batch.sequences))
+
+    def collect(self):
+        plans, n = self._inflight
+        self._inflight = None
+        results = [self.runner.collect()] + self._gather()
+        tokens = [0] * n
+        logprobs = None
+        for plan, (toks, lps) in zip(plans, results):
+            for r, t in zip(plan.rows.tolist(), toks):
+                tokens[r] = t
+            if lps is not None:
+                logprobs = logprobs or [None] * n
+                for r, lp in zip(plan.rows.tolist(), lps):
+                    logprobs[r] = lp
+        return tokens, logprobs
+
+    def execute(self, batch):
+        self.launch(batch)
+        return self.collect()
+
+    def exit(self):
+        for r, c in enumerate(self.conns, start=1):
+            try:
+                c.send(("exit", ()))
+            except Exception:
+                pass
+        for r, c in enumerate(self.conns, start=1):
+            try:
+                self._recv(r, c, timeout=30.0)
+            except Exception:
+                pass
+        for p in self.procs:
+            p.join(timeout=10)
+            if p.is_alive():
+                p.kill()
+        self.procs, self.conns = [], []
+        if getattr(self, "runner", None) is not None:
+            self.runner.exit()
+            self.runner = None

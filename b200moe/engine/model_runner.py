@@ -1,0 +1,378 @@
+"""Per-rank device runtime: model, KV pool, step upload, CUDA graphs, sampling.
+
+One ``ModelRunner`` lives in each rank's process and owns that rank's GPU.  A
+step arrives as a :class:`StepPlan`; the runner packs it into one pinned int32
+buffer, issues ONE host-to-device copy, runs the forward (a captured CUDA graph
+for pure-decode steps up to ``cuda_graph_max_bs`` rows, eager otherwise),
+samples on the device and returns the sampled ids with a single
+device-to-host read.
+
+Reference: nanovllm/engine/model_runner.py:95-1248 (pickled Sequence objects,
+per-tensor pinned copies, whole-graph capture per batch bucket).
+"""
+from __future__ import annotations
+
+import gc
+import math
+import os
+import time
+
+import numpy as np
+import torch
+
+from b200moe import ops
+from b200moe.config import Config
+from b200moe.engine.kv_cache import KVPool
+from b200moe.engine.step_plan import StepPlan, empty_plan, pack_plan
+from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM, StepInputs
+from b200moe.utils.profiler import DeviceProfiler
+from b200moe.utils.weights import load_checkpoint, random_init_
+
+GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512)
+
+
+def expert_placement(config: Config, rank: int, world: int, layer: int = 0) -> list[int]:
+    """Global expert ids owned by ``rank`` (reference: qwen3_moe.py:144-166)."""
+    E = config.hf_config.num_experts
+    per = E // world
+    if config.expert_placement == "linear":
+        return list(range(rank * per, (rank + 1) * per))
+    if config.expert_placement == "round_robin":
+        return list(range(rank, E, world))
+    import hashlib
+    import json
+    with open(config.expert_map_path) as f:
+        mapping = json.load(f)
+    want = mapping.get("model_config_sha256")
+    if want and os.path.isdir(config.model):
+        with open(os.path.join(config.model, "config.json"), "rb") as f:
+            got = hashlib.sha256(f.read()).hexdigest()
+        if got != want:
+            raise ValueError("profiled expert map was generated for a different model config")
+    layers = mapping.get("layers", mapping)
+    lm = layers.get(str(layer), layers.get(layer))
+    ids = lm.get(str(rank), lm.get(rank))
+    if len(ids) != per or len(set(ids)) != per:
+        raise ValueError("profiled expert map must give each rank E/world distinct experts")
+    return list(ids)
+
+
+class ModelRunner:
+
+    def __init__(self, config: Config, rank: int = 0, world_size: int | None = None, init_dist: bool = True):
+        self.config = config
+        self.rank = rank
+        self.world_size = world_size or config.world_size
+        self.block_size = config.kvcache_block_size
+        args = config.hf_config
+        self.args = args
+        if config.device == "cuda":
+            if not torch.cuda.is_available():
+                raise RuntimeError("device='cuda' but no CUDA device is visible")
+            local = int(os.environ.get("LOCAL_RANK", rank)) % torch.cuda.device_count()
+            torch.cuda.set_device(local)
+            self.device = torch.device("cuda", local)
+            ops.native()  # fail loudly when the extension is missing on a GPU box
+        else:
+            self.device = torch.device("cpu")
+        if self.world_size > 1 and init_dist:
+            self._init_dist()
+        self.profiler = DeviceProfiler(self.device, enabled=config.enable_profiling)
+        expert_ids = expert_placement(config, rank, self.world_size) if args.is_moe else []
+        t0 = time.perf_counter()
+        self.model = Qwen3MoeForCausalLM(args, self.device, ep_rank=rank, ep_size=self.world_size,
+                                         expert_ids=expert_ids)
+        self.model.moe_backend = "loop" if config.moe_backend == "loop" else "fused"
+        if self.world_size > 1:
+            from b200moe.parallel.ep import ExpertParallel
+            self.model.ep = ExpertParallel(self, config.moe_backend)
+        if config.random_init:
+            random_init_(self.model, seed=config.seed)
+        else:
+            load_checkpoint(self.model, config.model)
+        self.model.profiler = self.profiler if config.enable_profiling else None
+        self.load_s = time.perf_counter() - t0
+        self.max_blocks = -(-config.max_model_len // self.block_size)
+        self.max_rows = config.max_num_seqs
+        self.max_tokens = config.max_num_batched_tokens
+        self.max_splits = self.model.decode_splits(1, config.max_model_len)[1]
+        if self.device.type == "cuda":
+            self.model.reserve_workspace(self.max_tokens, self.max_rows, self.max_splits)
+        self.allocate_kv_cache()
+        # two pinned staging buffers: a step may be uploaded while the previous one's copy is in flight
+        words = 8 * self.max_tokens + 8 * self.max_rows + self.max_rows * self.max_blocks + 16
+        pin = self.device.type == "cuda"
+        self._pinned = [torch.empty(words, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._pinned_np = [p.numpy() for p in self._pinned]
+        self._dev_in = torch.empty(words, dtype=torch.int32, device=self.device)
+        self._pin_idx = 0
+        self._logits = None
+        self.graphs: dict[int, tuple] = {}
+        self.graph_pool = None
+        self.offloader = None
+        self._pending = None
+        self.steps = 0
+        if self.device.type == "cuda" and not config.enforce_eager:
+            self.capture_cudagraphs()
+
+    # ------------------------------------------------------------- setup
+    def _init_dist(self):
+        import torch.distributed as dist
+        from datetime import timedelta
+        if not dist.is_initialized():
+            backend = "nccl" if self.device.type == "cuda" else "gloo"
+            method = self.config.distributed_init_method or "env://"
+            dist.init_process_group(backend, init_method=method, world_size=self.world_size, rank=self.rank,
+                                    timeout=timedelta(seconds=self.config.rank_timeout_s),
+                                    device_id=self.device if self.device.type == "cuda" else None)
+
+    def allocate_kv_cache(self):
+        c, a = self.config, self.args
+        int8 = c.kv_cache_dtype == "int8"
+        nkv = a.num_key_value_heads
+        block_bytes = KVPool.bytes_per_block(a.num_hidden_layers, nkv, self.block_size, a.head_dim,
+                                             self.model.dtype, int8)
+        if c.num_kvcache_blocks <= 0:
+            if self.device.type == "cuda":
+                free, total = torch.cuda.mem_get_info(self.device)
+                reserve = 3 << 30  # graphs, logits, transient allocator growth
+                budget = free - (1.0 - c.gpu_memory_utilization) * total - reserve
+                c.num_kvcache_blocks = int(budget // block_bytes)
+            else:
+                c.num_kvcache_blocks = max(64, c.max_num_seqs * self.max_blocks // 4)
+        if self.world_size > 1:
+            import torch.distributed as dist
+            t = torch.tensor([c.num_kvcache_blocks], dtype=torch.int64, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            c.num_kvcache_blocks = int(t.item())
+        if c.num_kvcache_blocks <= 0:
+            raise RuntimeError(f"no memory left for the KV cache (block = {block_bytes / 2**20:.1f} MiB)")
+        self.kv = KVPool(c.num_kvcache_blocks + 1, a.num_hidden_layers, nkv, self.block_size, a.head_dim,
+                         self.model.dtype, self.device, int8=int8)
+        self.block_bytes = block_bytes
+        self.scratch_block = self.kv.scratch_block
+
+    # ------------------------------------------------------------ upload
+    def _upload(self, plan: StepPlan, dev: torch.Tensor | None = None) -> dict:
+        i = self._pin_idx
+        self._pin_idx ^= 1
+        buf, offs = pack_plan(plan, self._pinned_np[i])
+        n = buf.size
+        dev = self._dev_in if dev is None else dev
+        if n > dev.numel():
+            raise RuntimeError("step plan larger than the staging buffer")
+        dev[:n].copy_(self._pinned[i][:n], non_blocking=True)
+        views = {k: dev[o:o + s] for k, (o, s) in offs.items()}
+        views["block_tables"] = views["block_tables"].view(plan.num_rows, -1)
+        return views
+
+    def _inputs(self, plan: StepPlan, v: dict, max_seq_len: int | None = None) -> StepInputs:
+        nd = plan.num_decode
+        return StepInputs(
+            input_ids=v["input_ids"], positions=v["positions"], slot_mapping=v["slot_mapping"],
+            cu_seqlens_q=v["cu_seqlens_q"], seq_lens=v["seq_lens"], block_tables=v["block_tables"],
+            logits_indices=v["logits_indices"], num_decode=nd, max_q_len=plan.max_q_len,
+            max_seq_len=max_seq_len or plan.max_seq_len, num_rows=plan.num_rows,
+            prefill_cu=v["prefill_cu"] if plan.num_rows > nd else None)
+
+    def _pad_plan(self, plan: StepPlan, rows: int) -> StepPlan:
+        """A decode plan padded to ``rows`` rows; padding rows write the scratch block."""
+        B = plan.num_rows
+        p = rows - B
+        mb = self.max_blocks
+        tables = np.full((rows, mb), self.scratch_block, np.int32)
+        tables[:B, :plan.block_tables.shape[1]] = plan.block_tables
+        tables[:B, plan.block_tables.shape[1]:] = 0
+        pad_i = np.zeros(p, np.int32)
+        return StepPlan(
+            np.concatenate([plan.input_ids, pad_i]), np.concatenate([plan.positions, pad_i]),
+            np.concatenate([plan.slot_mapping, np.full(p, self.scratch_block * self.block_size, np.int32)]),
+            np.arange(rows + 1, dtype=np.int32), np.concatenate([plan.seq_lens, np.ones(p, np.int32)]),
+            tables, rows, 0, plan.max_seq_len, np.arange(rows, dtype=np.int32),
+            np.concatenate([plan.temperature, np.zeros(p, np.float32)]))
+
+    # ------------------------------------------------------------ graphs
+    def _bucket(self, rows: int) -> int | None:
+        for b in GRAPH_BUCKETS:
+            if b >= rows and b <= min(self.config.cuda_graph_max_bs, self.max_rows):
+                return b
+        return None
+
+    @torch.inference_mode()
+    def capture_cudagraphs(self):
+        """One graph per decode bucket: forward + LM head + greedy argmax into
+        static buffers.  Decode split sizing uses max_model_len so the graph
+        is valid for any context length."""
+        max_bs = min(self.config.cuda_graph_max_bs, self.max_rows)
+        buckets = [b for b in GRAPH_BUCKETS if b <= max_bs]
+        V = self.args.vocab_size
+        self._graph_logits = torch.empty(max(buckets), V, dtype=torch.float32, device=self.device)
+        self._graph_tokens = torch.empty(max(buckets), dtype=torch.int32, device=self.device)
+        words = self._dev_in.numel()
+        self.graph_pool = torch.cuda.graph_pool_handle()
+        stream = torch.cuda.Stream(self.device)
+        for b in reversed(buckets):
+            dummy = self._pad_plan(empty_plan(self.max_blocks), b)
+            dummy.max_seq_len = self.config.max_model_len
+            dev = torch.empty(words, dtype=torch.int32, device=self.device)
+            views = self._upload(dummy, dev)
+            inp = self._inputs(dummy, views, max_seq_len=self.config.max_model_len)
+            logits = self._graph_logits[:b]
+            tokens = self._graph_tokens[:b]
+            # warm-up run outside capture (first-use allocations, cached tensors)
+            h = self.model(inp, self.kv)
+            self.model.compute_logits(h, out=logits)
+            ops.argmax(logits, tokens)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.graph(g, pool=self.graph_pool, stream=stream):
+                h = self.model(inp, self.kv)
+                self.model.compute_logits(h, out=logits)
+                ops.argmax(logits, tokens)
+            torch.cuda.synchronize(self.device)
+            self.graphs[b] = (g, dev, logits, tokens)
+        ops.check_status(self.device)
+
+    # --------------------------------------------------------------- run
+    @torch.inference_mode()
+    def run(self, plan: StepPlan):
+        """Forward + sample; returns (token ids in plan-row order, logprobs|None)."""
+        self.launch(plan)
+        return self.collect()
+
+    @torch.inference_mode()
+    def launch(self, plan: StepPlan):
+        """Enqueue the step (no host sync); ``collect`` reads the result."""
+        self.steps += 1
+        B = plan.num_rows
+        if B == 0:
+            if self.model.ep is not None:  # expert-parallel peers still need this rank's collectives
+                self.model(self._inputs(plan, self._upload(plan)), self.kv)
+            self._pending = (plan, None, None)
+            return
+        bucket = self._bucket(B) if (plan.is_pure_decode and self.graphs) else None
+        if bucket is not None:
+            g, dev, logits, tokens = self.graphs[bucket]
+            self._upload(self._pad_plan(plan, bucket), dev)
+            g.replay()
+            logits, tokens = logits[:B], tokens[:B]
+        else:
+            views = self._upload(plan)
+            with self.profiler.range("forward"):
+                h = self.model(self._inputs(plan, views), self.kv)
+            logits = self.model.compute_logits(h)
+            tokens = None
+        if plan.needs_full_sampler or tokens is None:
+            tokens = self._sample(plan, logits)
+        lp = self._logprobs(plan, logits, tokens) if plan.logprobs_k else None
+        out = torch.empty(B, dtype=torch.int32, pin_memory=self.device.type == "cuda")
+        out.copy_(tokens, non_blocking=True)
+        if self.device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record()
+        else:
+            ev = None
+        self._pending = (plan, out, (ev, lp))
+
+    def collect(self):
+        plan, out, extra = self._pending
+        self._pending = None
+        if out is None:
+            return [], None
+        ev, lp = extra
+        if ev is not None:
+            ev.synchronize()
+        toks = out.tolist()
+        logprobs = None
+        if lp is not None:
+            topv, topi, chosen = (t.tolist() for t in lp)
+            logprobs = [{"top": list(zip(topi[r], topv[r])), "chosen": chosen[r]} for r in range(len(toks))]
+        return toks, logprobs
+
+    def _dev(self, arr, dtype):
+        t = torch.from_numpy(np.ascontiguousarray(arr))
+        if self.device.type == "cuda":
+            t = t.pin_memory().to(self.device, non_blocking=True)
+        return t.to(dtype)
+
+    def _sample(self, plan: StepPlan, logits: torch.Tensor) -> torch.Tensor:
+        if plan.pen_rows is not None:
+            ops.apply_penalties(logits, self._dev(plan.pen_rows, torch.int32), self._dev(plan.pen_ids, torch.int32),
+                                self._dev(plan.pen_counts, torch.int32), self._dev(plan.presence, torch.float32),
+                                self._dev(plan.frequency, torch.float32), self._dev(plan.repetition, torch.float32))
+        if plan.grammar_mask is not None:
+            rows = self._dev(plan.grammar_rows, torch.int64)
+            mask = self._dev(plan.grammar_mask, torch.int32)
+            V = logits.shape[1]
+            bits = torch.arange(V, device=logits.device)
+            allowed = ((mask[:, bits // 32] >> (bits % 32)) & 1).bool()
+            sub = logits.index_select(0, rows)
+            logits.index_copy_(0, rows, sub.masked_fill(~allowed, torch.finfo(torch.float32).min))
+        if plan.all_greedy:
+            return ops.argmax(logits)
+        n = plan.num_rows
+        return ops.sample(
+            logits, self._dev(plan.temperature, torch.float32),
+            None if plan.top_k is None else self._dev(plan.top_k, torch.int32),
+            None if plan.top_p is None else self._dev(plan.top_p, torch.float32),
+            None if plan.min_p is None else self._dev(plan.min_p, torch.float32),
+            self._dev(plan.seeds if plan.seeds is not None else np.zeros(n, np.int64), torch.int64),
+            None if plan.offsets is None else self._dev(plan.offsets, torch.int64))
+
+    @staticmethod
+    def _logprobs(plan: StepPlan, logits, tokens):
+        t = torch.from_numpy(plan.temperature).to(logits.device).clamp_min(1e-5).unsqueeze(1)
+        greedy = torch.from_numpy(plan.temperature < 1e-3).to(logits.device).unsqueeze(1)
+        scaled = torch.where(greedy, logits, logits / t)
+        lp = torch.log_softmax(scaled.float(), dim=-1)
+        chosen = lp.gather(1, tokens.long().unsqueeze(1)).squeeze(1)
+        topv, topi = lp.topk(min(plan.logprobs_k, lp.shape[1]), dim=-1)
+        return topv.cpu(), topi.cpu(), chosen.cpu()
+
+    # ----------------------------------------------------------- offload
+    def offload_put(self, block_id: int) -> int:
+        from b200moe.engine.kv_offload import HostBlockPool
+        if self.offloader is None:
+            self.offloader = HostBlockPool(self.config.kv_offload_host_blocks, self.kv, self.device)
+        return self.offloader.put(block_id)
+
+    def offload_get(self, slot: int, block_id: int):
+        self.offloader.get(slot, block_id)
+
+    def offload_release(self, slot: int):
+        self.offloader.release(slot)
+
+    # -------------------------------------------------------------- misc
+    def warmup(self):
+        """One max-size prefill through the eager path (allocator + kernel first use)."""
+        bs = self.block_size
+        seq_len = min(self.max_tokens, self.config.max_model_len)
+        nblk = -(-seq_len // bs)
+        if nblk > self.config.num_kvcache_blocks:
+            return
+        pos = np.arange(seq_len, dtype=np.int32)
+        tables = np.zeros((1, self.max_blocks), np.int32)
+        tables[0, :nblk] = np.arange(nblk)
+        plan = StepPlan(np.zeros(seq_len, np.int32), pos, pos.copy(), np.array([0, seq_len], np.int32),
+                        np.array([seq_len], np.int32), tables, 0, seq_len, seq_len, np.zeros(1, np.int32),
+                        np.zeros(1, np.float32))
+        self.run(plan)
+
+    def check_status(self):
+        if self.device.type == "cuda":
+            ops.check_status(self.device)
+
+    def exit(self):
+        self.graphs.clear()
+        self.graph_pool = None
+        for attr in ("model", "kv"):
+            if hasattr(self, attr):
+                delattr(self, attr)
+        gc.collect()
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+        if self.world_size > 1:
+            import torch.distributed as dist
+            if dist.is_initialized():
+                dist.destroy_process_group()

@@ -1,0 +1,185 @@
+"""Host-side step plan: the flat arrays one forward step needs.
+
+The driver turns a :class:`ScheduledBatch` into one plan per rank (with
+data-parallel attention every rank runs its own rows).  A plan is a handful of
+numpy arrays, cheap to ship to worker processes and packed into ONE pinned
+int32 buffer on the device side, so a step costs a single host-to-device copy
+(the reference builds ~8 tensors with separate pinned copies,
+nanovllm/engine/model_runner.py:595-699).
+
+Row order inside a plan: decode rows (one new token) first, then prefill
+rows; ``rows`` maps plan rows back to batch rows.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class StepPlan:
+    input_ids: np.ndarray        # int32 [T]
+    positions: np.ndarray        # int32 [T]
+    slot_mapping: np.ndarray     # int32 [T]
+    cu_seqlens_q: np.ndarray     # int32 [B + 1]
+    seq_lens: np.ndarray         # int32 [B]
+    block_tables: np.ndarray     # int32 [B, max_blocks]
+    num_decode: int
+    max_q_len: int
+    max_seq_len: int
+    rows: np.ndarray             # int32 [B]: batch row of each plan row
+    temperature: np.ndarray      # float32 [B]
+    top_k: np.ndarray | None = None
+    top_p: np.ndarray | None = None
+    min_p: np.ndarray | None = None
+    seeds: np.ndarray | None = None
+    offsets: np.ndarray | None = None
+    # penalties: flat (row, token, generated count) triples + per-row coefficients
+    pen_rows: np.ndarray | None = None
+    pen_ids: np.ndarray | None = None
+    pen_counts: np.ndarray | None = None
+    presence: np.ndarray | None = None
+    frequency: np.ndarray | None = None
+    repetition: np.ndarray | None = None
+    logprobs_k: int = 0
+    grammar_rows: np.ndarray | None = None
+    grammar_mask: np.ndarray | None = None   # int32 [n, words] allowed-token bitmask
+
+    @property
+    def num_rows(self) -> int:
+        return int(self.seq_lens.shape[0])
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.shape[0])
+
+    @property
+    def is_pure_decode(self) -> bool:
+        return self.num_decode == self.num_rows and self.num_rows > 0
+
+    @property
+    def all_greedy(self) -> bool:
+        return bool(self.temperature.size == 0 or (self.temperature < 1e-3).all())
+
+    @property
+    def needs_full_sampler(self) -> bool:
+        return (not self.all_greedy or self.pen_rows is not None or self.grammar_rows is not None
+                or self.logprobs_k > 0)
+
+
+def empty_plan(max_blocks: int = 1) -> StepPlan:
+    z = np.zeros(0, np.int32)
+    return StepPlan(z, z, z, np.zeros(1, np.int32), z, np.zeros((0, max_blocks), np.int32), 0, 0, 0, z,
+                    np.zeros(0, np.float32))
+
+
+def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int | None = None,
+               rows: list[int] | None = None) -> StepPlan:
+    """Plan for the given batch rows (one rank's share of a batch)."""
+    n = len(seqs)
+    rows = list(range(n)) if rows is None else rows
+    order = sorted(range(n), key=lambda i: (bool(prefill_flags[i]), i))
+    nd = sum(1 for i in range(n) if not prefill_flags[i])
+    qlens = np.fromiter((query_lens[i] for i in order), dtype=np.int64, count=n)
+    T = int(qlens.sum())
+    cu = np.zeros(n + 1, np.int32)
+    np.cumsum(qlens, out=cu[1:])
+    ids = np.empty(T, np.int32)
+    pos = np.empty(T, np.int32)
+    slots = np.empty(T, np.int32)
+    seq_lens = np.empty(n, np.int32)
+    mb = max_blocks or max((len(seqs[i].block_table) for i in order), default=1) or 1
+    tables = np.zeros((n, mb), np.int32)
+    for r, i in enumerate(order):
+        s = seqs[i]
+        q = int(qlens[r])
+        a, b = int(cu[r]), int(cu[r + 1])
+        if prefill_flags[i]:
+            start = s.num_cached_tokens
+            ids[a:b] = s.token_ids[start:start + q]
+        else:
+            start = len(s) - 1
+            ids[a] = s.last_token
+        p = np.arange(start, start + q, dtype=np.int64)
+        pos[a:b] = p
+        bt = np.asarray(s.block_table, dtype=np.int64)
+        need = int(p[-1]) // block_size + 1
+        if bt.size < need or bt.size > mb:
+            raise RuntimeError(f"seq {s.seq_id}: block table has {bt.size} blocks, step needs {need} (max {mb})")
+        slots[a:b] = bt[p // block_size] * block_size + p % block_size
+        seq_lens[r] = start + q
+        tables[r, :bt.size] = bt
+    temps = np.fromiter((seqs[i].temperature for i in order), dtype=np.float32, count=n)
+    plan = StepPlan(ids, pos, slots, cu, seq_lens, tables, nd,
+                    int(qlens[nd:].max()) if n > nd else 0,
+                    int(seq_lens.max()) if n else 0,
+                    np.asarray([rows[i] for i in order], np.int32), temps)
+    _sampling_meta(plan, [seqs[i] for i in order])
+    return plan
+
+
+def _sampling_meta(plan: StepPlan, seqs):
+    n = len(seqs)
+    if any(s.top_k != -1 for s in seqs):
+        plan.top_k = np.fromiter((s.top_k for s in seqs), np.int32, n)
+    if any(s.top_p < 1.0 for s in seqs):
+        plan.top_p = np.fromiter((s.top_p for s in seqs), np.float32, n)
+    if any(s.min_p > 0.0 for s in seqs):
+        plan.min_p = np.fromiter((s.min_p for s in seqs), np.float32, n)
+    if not plan.all_greedy:
+        plan.seeds = np.fromiter(((s.seed if s.seed is not None else s.seq_id * 7919 + 17) for s in seqs),
+                                 np.int64, n)
+        plan.offsets = np.fromiter((s.num_tokens for s in seqs), np.int64, n)
+    plan.logprobs_k = max((s.logprobs for s in seqs), default=0)
+    if any(s.has_penalty for s in seqs):
+        rws, ids, cnt = [], [], []
+        pres = np.zeros(n, np.float32)
+        freq = np.zeros(n, np.float32)
+        rep = np.ones(n, np.float32)
+        for r, s in enumerate(seqs):
+            if not s.has_penalty:
+                continue
+            pres[r], freq[r], rep[r] = s.presence_penalty, s.frequency_penalty, s.repetition_penalty
+            toks = dict(s.ensure_rep_counts()) if s.repetition_penalty != 1.0 else {}
+            for t in s.gen_counts:
+                toks.setdefault(t, 0)
+            for t in toks:
+                rws.append(r)
+                ids.append(t)
+                cnt.append(s.gen_counts.get(t, 0))
+        if rws:
+            plan.pen_rows = np.asarray(rws, np.int32)
+            plan.pen_ids = np.asarray(ids, np.int32)
+            plan.pen_counts = np.asarray(cnt, np.int32)
+            plan.presence, plan.frequency, plan.repetition = pres, freq, rep
+    g_rows = [r for r, s in enumerate(seqs) if s.grammar_matcher is not None]
+    if g_rows:
+        plan.grammar_rows = np.asarray(g_rows, np.int32)
+
+
+PACK_FIELDS = ("input_ids", "positions", "slot_mapping", "cu_seqlens_q", "seq_lens", "logits_indices",
+               "prefill_cu", "block_tables")
+
+
+def pack_plan(plan: StepPlan, out: np.ndarray | None = None) -> tuple[np.ndarray, dict]:
+    """Concatenate the int32 arrays into one buffer; returns (buffer, {name: (offset, size)})."""
+    nd = plan.num_decode
+    cu = plan.cu_seqlens_q
+    parts = {
+        "input_ids": plan.input_ids, "positions": plan.positions, "slot_mapping": plan.slot_mapping,
+        "cu_seqlens_q": cu, "seq_lens": plan.seq_lens,
+        "logits_indices": (cu[1:] - 1).astype(np.int32),
+        "prefill_cu": (cu[nd:] - cu[nd]).astype(np.int32),
+        "block_tables": plan.block_tables.reshape(-1),
+    }
+    total = sum(p.size for p in parts.values())
+    buf = out[:total] if out is not None and out.size >= total else np.empty(total, np.int32)
+    offs = {}
+    o = 0
+    for name in PACK_FIELDS:
+        arr = parts[name]
+        buf[o:o + arr.size] = arr
+        offs[name] = (o, arr.size)
+        o += arr.size
+    return buf, offs

@@ -1,0 +1,357 @@
+"""Python entry points of the sm_100a kernels.
+
+CUDA tensors always go to the native extension (``b200moe._C``); if it is
+missing on a GPU the call raises, it never falls back to a slower path.  CPU
+tensors take the plain-PyTorch fp32 definition of the same op, which is the
+numerics oracle used by the tests and by the CPU engine.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+try:  # the in-tree build (python setup.py build_ext --inplace)
+    from b200moe import _C  # type: ignore
+    _IMPORT_ERROR = None
+except Exception as exc:  # pragma: no cover - depends on the build
+    _C = None
+    _IMPORT_ERROR = exc
+
+EPI_BF16, EPI_F32, EPI_SILU_PAIR, EPI_SCATTER = 0, 1, 2, 3
+NUM_SMS = 148
+
+
+def native():
+    if _C is None:
+        raise RuntimeError(
+            "b200moe native extension is not built (run `python setup.py build_ext --inplace`): "
+            f"{_IMPORT_ERROR}")
+    return _C
+
+
+def native_available() -> bool:
+    return _C is not None
+
+
+_status_cache: dict = {}
+_count_cache: dict = {}
+
+
+def status_word(device) -> torch.Tensor:
+    """Per-device int32 status word that kernels set on a bounded-wait timeout."""
+    key = torch.device(device)
+    t = _status_cache.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=key)
+        _status_cache[key] = t
+    return t
+
+
+def check_status(device) -> None:
+    """Raise if a kernel on ``device`` recorded an error (reads one int: a sync)."""
+    t = _status_cache.get(torch.device(device))
+    if t is not None:
+        v = int(t.item())
+        if v != 0:
+            t.zero_()
+            raise RuntimeError(f"device kernel reported status {v} (bounded wait expired or bad input)")
+
+
+def count_tensor(n: int, device) -> torch.Tensor:
+    """Cached one-element int32 device tensor holding ``n`` (dense GEMM group count)."""
+    key = (n, torch.device(device))
+    t = _count_cache.get(key)
+    if t is None:
+        t = torch.tensor([n], dtype=torch.int32, device=device)
+        _count_cache[key] = t
+    return t
+
+
+# --------------------------------------------------------------- references
+def dequant_block_fp8(w: torch.Tensor, scale: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """fp32 value of a 128x128 block-scaled e4m3 weight ([..., N, K])."""
+    wf = w.float()
+    s = scale.float().repeat_interleave(block, dim=-2)[..., :wf.shape[-2], :]
+    s = s.repeat_interleave(block, dim=-1)[..., :wf.shape[-1]]
+    return wf * s
+
+
+def dequant_block_fp8_bf16(w, scale, block=128):
+    """The reference's load-time dequant: bf16(float(q) * scale) (loader.py:28-35)."""
+    return dequant_block_fp8(w, scale, block).to(torch.bfloat16)
+
+
+def pick_bn(rows: int, m_tiles: int, groups: int = 1, pair: bool = False, sms: int = NUM_SMS) -> int:
+    """Token tile of the tcgen05 GEMM: the largest tile that still gives the
+    persistent grid one work item per SM, and no larger than twice the rows a
+    group is expected to hold."""
+    per_group = max(1, math.ceil(rows / max(groups, 1)))
+    choices = (16, 32, 64, 128) if pair else (16, 32, 64, 128, 256)
+    best = choices[0]
+    for bn in choices[1:]:
+        if bn > 2 * per_group:
+            break
+        if groups * math.ceil(per_group / bn) * m_tiles < sms:
+            break
+        best = bn
+    return best
+
+
+# --------------------------------------------------------------------- GEMM
+def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, out_dtype=torch.bfloat16,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ W^T with W either block-scaled e4m3 (+ scale) or bf16/fp32."""
+    T = x.shape[0]
+    N = weight.shape[0]
+    if not x.is_cuda:
+        w = dequant_block_fp8(weight, scale) if scale is not None else weight.float()
+        y = x.float() @ w.t()
+        return y.to(out_dtype) if out is None else out.copy_(y)
+    C = native()
+    if out is None:
+        out = torch.empty(T, N, dtype=out_dtype, device=x.device)
+    if T == 0:
+        return out
+    m_tiles = N // 128
+    epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
+    C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, pick_bn(T, m_tiles), epi, m_tiles,
+           0, 0, None, None, status_word(x.device))
+    return out
+
+
+def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn: int | None = None):
+    """out[r] = silu(x_perm[r] @ Wg_e^T) * (x_perm[r] @ Wu_e^T) for the rows of expert e."""
+    C = native()
+    rows = x_perm.shape[0]
+    m_tiles = inter // 128
+    bn = bn or pick_bn(rows, m_tiles, groups=w13.shape[0], pair=True)
+    C.gemm(w13, s13, x_perm, counts, offsets, out, bn, EPI_SILU_PAIR, m_tiles, inter, 0, None, None,
+           status_word(x_perm.device))
+    return out
+
+
+def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weight, slots_out,
+                         bn: int | None = None):
+    """slots_out[slot_of_row[r]] = (h_perm[r] @ Wd_e^T) * slot_weight[slot] for the rows of expert e."""
+    C = native()
+    rows = h_perm.shape[0]
+    m_tiles = w2.shape[1] // 128
+    bn = bn or pick_bn(rows, m_tiles, groups=w2.shape[0])
+    C.gemm(w2, s2, h_perm, counts, offsets, slots_out, bn, EPI_SCATTER, m_tiles, 0, 0, slot_of_row, slot_weight,
+           status_word(h_perm.device))
+    return slots_out
+
+
+# -------------------------------------------------------------- fused ops
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if not ids.is_cuda:
+        return table[ids.long()].clone()
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=ids.device)
+    native().embed(ids, table, out, status_word(ids.device))
+    return out
+
+
+def rmsnorm(x, weight, eps, residual=None, out=None):
+    """Reference numerics (layernorm.py:18-38).  With ``residual`` the sum
+    x + residual is written back into ``residual`` (the new residual stream)."""
+    if not x.is_cuda:
+        xf = x.float()
+        if residual is not None:
+            xf = xf + residual.float()
+            residual.copy_(xf.to(residual.dtype))
+        var = xf.pow(2).mean(dim=-1, keepdim=True)
+        y = (xf * torch.rsqrt(var + eps)).to(x.dtype) * weight
+        return y if out is None else out.copy_(y)
+    if out is None:
+        out = torch.empty_like(x)
+    native().rmsnorm(x, residual, weight, out, residual, eps)
+    return out
+
+
+def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None):
+    """residual += sum_k slots[t, k] (fixed order); return rmsnorm(residual)."""
+    T, H = residual.shape
+    if not residual.is_cuda:
+        moe = slots[:T * topk].view(T, topk, H).float().sum(dim=1).to(residual.dtype)
+        return rmsnorm(moe, weight, eps, residual=residual, out=out)
+    if out is None:
+        out = torch.empty_like(residual)
+    native().moe_combine(slots, topk, residual, weight, out, eps)
+    return out
+
+
+def rope_cos_sin(head_dim: int, max_pos: int, theta: float, device) -> torch.Tensor:
+    """[max_pos, head_dim] fp32: cos | sin of the neox rotary (rotary_embedding.py:18-35)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float) / head_dim))
+    t = torch.arange(max_pos, dtype=torch.float)
+    freqs = torch.outer(t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(device)
+
+
+def qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer, nq, nkv, D,
+                        eps, q_out=None):
+    """Normalise + rotate q/k, write k (rotated) and v into the paged pool
+    (``kv_layer`` is a :class:`~b200moe.engine.kv_cache.KVLayer`)."""
+    T = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty(T, nq, D, dtype=qkv.dtype, device=qkv.device)
+    if not qkv.is_cuda:
+        q = qkv[:, :nq * D].reshape(T, nq, D)
+        k = qkv[:, nq * D:(nq + nkv) * D].reshape(T, nkv, D)
+        v = qkv[:, (nq + nkv) * D:].reshape(T, nkv, D)
+
+        def norm(x, w):
+            xf = x.float()
+            var = xf.pow(2).mean(dim=-1, keepdim=True)
+            return (xf * torch.rsqrt(var + eps)).to(x.dtype) * w
+
+        def rope(x):
+            cs = cos_sin[positions.long()]
+            c, s = cs.chunk(2, dim=-1)
+            c, s = c.unsqueeze(1), s.unsqueeze(1)
+            x1, x2 = x.float().chunk(2, dim=-1)
+            return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1).to(x.dtype)
+
+        q_out.copy_(rope(norm(q, q_norm_w)))
+        kv_layer.store(slot_mapping, rope(norm(k, k_norm_w)), v)
+        return q_out
+    native().qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer.k,
+                                 kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, q_out, nq, nkv, D,
+                                 kv_layer.block_size, kv_layer.block_stride, kv_layer.scale_block_stride, eps)
+    return q_out
+
+
+def router_topk(logits, num_experts, topk, renorm, ids, weights, counts=None):
+    """Softmax over the first ``num_experts`` logit columns (rounded to bf16
+    first, like the reference's bf16 gate output), top-k, renormalise, bf16
+    weights; optionally add the per-expert counts into ``counts``."""
+    if not logits.is_cuda:
+        p = torch.softmax(logits[:, :num_experts].to(torch.bfloat16).float(), dim=-1)
+        w, i = torch.topk(p, topk, dim=-1)
+        if renorm:
+            w = w / w.sum(dim=-1, keepdim=True)
+        ids.copy_(i.to(ids.dtype))
+        weights.copy_(w.to(torch.bfloat16).float())
+        if counts is not None:
+            counts.add_(torch.bincount(i.flatten(), minlength=counts.numel()).to(counts.dtype))
+        return
+    native().router_topk(logits, num_experts, topk, renorm, ids, weights, counts)
+
+
+def moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out=None):
+    native().moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out)
+
+
+def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len, num_splits, workspace):
+    """q [B, nq, D], one query per sequence; keys are the first seq_lens[b] slots."""
+    if not q.is_cuda:
+        return _attention_ref(q, kv_layer, block_tables, seq_lens,
+                              torch.arange(q.shape[0] + 1, dtype=torch.int32), scale, out)
+    part_o, part_m, part_l = workspace
+    native().decode_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, block_tables, seq_lens,
+                         out, part_o, part_m, part_l, kv_layer.block_size, kv_layer.block_stride,
+                         kv_layer.num_kv_heads, scale, num_splits, split_len)
+    return out
+
+
+def prefill_attention(q, kv_layer, cu_seqlens_q, seq_lens, block_tables, max_q_len, scale, out):
+    if not q.is_cuda:
+        return _attention_ref(q, kv_layer, block_tables, seq_lens, cu_seqlens_q, scale, out)
+    native().prefill_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, cu_seqlens_q, seq_lens,
+                          block_tables, out, max_q_len, kv_layer.block_size, kv_layer.block_stride,
+                          kv_layer.num_kv_heads, scale)
+    return out
+
+
+def _attention_ref(q, kv_layer, block_tables, seq_lens, cu_seqlens_q, scale, out):
+    """fp32 causal attention over the paged pool, one sequence at a time."""
+    nq, D = q.shape[1], q.shape[2]
+    nkv = kv_layer.num_kv_heads
+    G = nq // nkv
+    cu = cu_seqlens_q.tolist()
+    lens = seq_lens.tolist()
+    for b in range(len(lens)):
+        q0, q1 = cu[b], cu[b + 1]
+        qlen, L = q1 - q0, lens[b]
+        if qlen == 0:
+            continue
+        k, v = kv_layer.gather(block_tables[b], L)  # [L, nkv, D]
+        qf = q[q0:q1].float().view(qlen, nkv, G, D)
+        s = torch.einsum("qhgd,khd->hgqk", qf, k.float()) * scale
+        qpos = torch.arange(L - qlen, L, device=q.device).view(qlen, 1)
+        kpos = torch.arange(L, device=q.device).view(1, L)
+        s = s.masked_fill(kpos > qpos, float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        o = torch.einsum("hgqk,khd->qhgd", p, v.float()).reshape(qlen, nq, D)
+        out[q0:q1] = o.to(out.dtype)
+    return out
+
+
+# ---------------------------------------------------------------- sampler
+def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    if not logits.is_cuda:
+        return out.copy_(logits.float().argmax(dim=-1).to(torch.int32))
+    native().argmax(logits, out)
+    return out
+
+
+def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out=None):
+    """temperature / top-k / top-p / min-p / exponential-race sampling (greedy
+    rows where temperature < 1e-3)."""
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    if not logits.is_cuda:
+        return out.copy_(sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets))
+    native().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out)
+    return out
+
+
+def sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets):
+    """CPU sampler with the same filters (sorted-vocabulary definition) and a
+    torch generator per row in place of Philox."""
+    B, V = logits.shape
+    out = torch.empty(B, dtype=torch.int32)
+    for r in range(B):
+        row = logits[r].float()
+        t = float(temperature[r])
+        if t < 1e-3:
+            out[r] = int(row.argmax())
+            continue
+        x = row / t
+        keep = torch.ones(V, dtype=torch.bool)
+        if top_k is not None and 0 < int(top_k[r]) < V:
+            kth = torch.topk(x, int(top_k[r])).values[-1]
+            keep &= x >= kth
+        if top_p is not None and float(top_p[r]) < 1.0:
+            xs = torch.where(keep, x, torch.tensor(float("-inf")))
+            p = torch.softmax(xs, dim=-1)
+            sp, si = torch.sort(p, descending=True)
+            cum = sp.cumsum(0)
+            n_keep = int((cum - sp < float(top_p[r])).sum())
+            thresh = xs[si[max(n_keep, 1) - 1]]
+            keep &= x >= thresh
+        if min_p is not None and float(min_p[r]) > 0:
+            keep &= x >= x.max() + math.log(float(min_p[r]))
+        g = torch.Generator().manual_seed(int(seeds[r]) + int(offsets[r] if offsets is not None else 0))
+        e = torch.empty(V).exponential_(1.0, generator=g)
+        score = torch.where(keep, x - x.max() - e.log(), torch.tensor(float("-inf")))
+        out[r] = int(score.argmax())
+    return out
+
+
+def apply_penalties(logits, rows, ids, gen_counts, presence, frequency, repetition):
+    if not logits.is_cuda:
+        r, i = rows.long(), ids.long()
+        vals = logits[r, i]
+        rep = repetition[r]
+        vals = torch.where(vals < 0, vals * rep, vals / rep)
+        gc = gen_counts.float()
+        vals = torch.where(gc > 0, vals - presence[r] - frequency[r] * gc, vals)
+        logits[r, i] = vals
+        return logits
+    native().penalties(logits, rows, ids, gen_counts, presence, frequency, repetition)
+    return logits
