@@ -138,6 +138,12 @@ class Executor:
         self._gather()
         return res
 
+    def call_all(self, method: str, *args) -> list:
+        """Run ``runner.method(*args)`` on every rank; returns every rank's result."""
+        self._send_all(method, [args] * self.world)
+        res = getattr(self.runner, method)(*args)
+        return [res] + self._gather()
+
     def call_rank(self, rank: int, method: str, *args):
         """Run ``runner.method(*args)`` on one rank only (its private KV pool)."""
         if rank == 0:

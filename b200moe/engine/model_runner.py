@@ -69,7 +69,7 @@ class ModelRunner:
         if config.device == "cuda":
             if not torch.cuda.is_available():
                 raise RuntimeError("device='cuda' but no CUDA device is visible")
-            local = int(os.environ.get("LOCAL_RANK", rank)) % torch.cuda.device_count()
+            local = rank % torch.cuda.device_count()
             torch.cuda.set_device(local)
             self.device = torch.device("cuda", local)
             ops.native()  # fail loudly when the extension is missing on a GPU box
@@ -112,6 +112,9 @@ class ModelRunner:
         self.offloader = None
         self._pending = None
         self.steps = 0
+        self.h2d_bytes = 0
+        self._step_events: list = []
+        self._graph_kernels: dict[int, int] = {}
         if self.device.type == "cuda" and not config.enforce_eager:
             self.capture_cudagraphs()
 
@@ -158,6 +161,7 @@ class ModelRunner:
         self._pin_idx ^= 1
         buf, offs = pack_plan(plan, self._pinned_np[i])
         n = buf.size
+        self.h2d_bytes += 4 * n
         dev = self._dev_in if dev is None else dev
         if n > dev.numel():
             raise RuntimeError("step plan larger than the staging buffer")
@@ -225,12 +229,14 @@ class ModelRunner:
             ops.argmax(logits, tokens)
             torch.cuda.synchronize(self.device)
             g = torch.cuda.CUDAGraph()
+            n0 = ops.launch_count()
             stream.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.graph(g, pool=self.graph_pool, stream=stream):
                 h = self.model(inp, self.kv)
                 self.model.compute_logits(h, out=logits)
                 ops.argmax(logits, tokens)
             torch.cuda.synchronize(self.device)
+            self._graph_kernels[b] = ops.launch_count() - n0
             self.graphs[b] = (g, dev, logits, tokens)
         ops.check_status(self.device)
 
@@ -246,6 +252,10 @@ class ModelRunner:
         """Enqueue the step (no host sync); ``collect`` reads the result."""
         self.steps += 1
         B = plan.num_rows
+        t_start = None
+        if self.device.type == "cuda":
+            t_start = torch.cuda.Event(enable_timing=True)
+            t_start.record()
         if B == 0:
             if self.model.ep is not None:  # expert-parallel peers still need this rank's collectives
                 self.model(self._inputs(plan, self._upload(plan)), self.kv)
@@ -256,6 +266,7 @@ class ModelRunner:
             g, dev, logits, tokens = self.graphs[bucket]
             self._upload(self._pad_plan(plan, bucket), dev)
             g.replay()
+            ops.count_launches(self._graph_kernels.get(bucket, 0))
             logits, tokens = logits[:B], tokens[:B]
         else:
             views = self._upload(plan)
@@ -269,8 +280,9 @@ class ModelRunner:
         out = torch.empty(B, dtype=torch.int32, pin_memory=self.device.type == "cuda")
         out.copy_(tokens, non_blocking=True)
         if self.device.type == "cuda":
-            ev = torch.cuda.Event()
+            ev = torch.cuda.Event(enable_timing=True)
             ev.record()
+            self._step_events.append((t_start, ev))
         else:
             ev = None
         self._pending = (plan, out, (ev, lp))
@@ -342,6 +354,21 @@ class ModelRunner:
 
     def offload_release(self, slot: int):
         self.offloader.release(slot)
+
+    # ----------------------------------------------------------- timing
+    def reset_step_timing(self):
+        self._step_events.clear()
+        ops.reset_launch_count()
+
+    def step_device_ms(self) -> float:
+        """Sum of device time (upload start -> sampled ids ready) of the steps
+        since the last reset."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        return float(sum(a.elapsed_time(b) for a, b in self._step_events))
+
+    def launch_count(self) -> int:
+        return ops.launch_count()
 
     # -------------------------------------------------------------- misc
     def warmup(self):

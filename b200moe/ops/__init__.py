@@ -22,6 +22,22 @@ EPI_BF16, EPI_F32, EPI_SILU_PAIR, EPI_SCATTER = 0, 1, 2, 3
 NUM_SMS = 148
 
 
+_launches = [0]
+
+
+def count_launches(n: int = 1):
+    _launches[0] += n
+
+
+def launch_count() -> int:
+    """Native kernels launched by this process since the last reset."""
+    return _launches[0]
+
+
+def reset_launch_count():
+    _launches[0] = 0
+
+
 def native():
     if _C is None:
         raise RuntimeError(
@@ -117,6 +133,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
     C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, pick_bn(T, m_tiles), epi, m_tiles,
            0, 0, None, None, status_word(x.device))
+    count_launches()
     return out
 
 
@@ -128,6 +145,7 @@ def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn:
     bn = bn or pick_bn(rows, m_tiles, groups=w13.shape[0], pair=True)
     C.gemm(w13, s13, x_perm, counts, offsets, out, bn, EPI_SILU_PAIR, m_tiles, inter, 0, None, None,
            status_word(x_perm.device))
+    count_launches()
     return out
 
 
@@ -140,6 +158,7 @@ def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weig
     bn = bn or pick_bn(rows, m_tiles, groups=w2.shape[0])
     C.gemm(w2, s2, h_perm, counts, offsets, slots_out, bn, EPI_SCATTER, m_tiles, 0, 0, slot_of_row, slot_weight,
            status_word(h_perm.device))
+    count_launches()
     return slots_out
 
 
@@ -150,6 +169,7 @@ def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = Non
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=ids.device)
     native().embed(ids, table, out, status_word(ids.device))
+    count_launches()
     return out
 
 
@@ -167,6 +187,7 @@ def rmsnorm(x, weight, eps, residual=None, out=None):
     if out is None:
         out = torch.empty_like(x)
     native().rmsnorm(x, residual, weight, out, residual, eps)
+    count_launches()
     return out
 
 
@@ -179,6 +200,7 @@ def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None):
     if out is None:
         out = torch.empty_like(residual)
     native().moe_combine(slots, topk, residual, weight, out, eps)
+    count_launches()
     return out
 
 
@@ -220,6 +242,7 @@ def qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_si
     native().qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer.k,
                                  kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, q_out, nq, nkv, D,
                                  kv_layer.block_size, kv_layer.block_stride, kv_layer.scale_block_stride, eps)
+    count_launches()
     return q_out
 
 
@@ -238,10 +261,12 @@ def router_topk(logits, num_experts, topk, renorm, ids, weights, counts=None):
             counts.add_(torch.bincount(i.flatten(), minlength=counts.numel()).to(counts.dtype))
         return
     native().router_topk(logits, num_experts, topk, renorm, ids, weights, counts)
+    count_launches()
 
 
 def moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out=None):
     native().moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out)
+    count_launches()
 
 
 def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len, num_splits, workspace):
@@ -253,6 +278,7 @@ def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len,
     native().decode_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, block_tables, seq_lens,
                          out, part_o, part_m, part_l, kv_layer.block_size, kv_layer.block_stride,
                          kv_layer.num_kv_heads, scale, num_splits, split_len)
+    count_launches(2 if num_splits > 1 else 1)
     return out
 
 
@@ -262,6 +288,7 @@ def prefill_attention(q, kv_layer, cu_seqlens_q, seq_lens, block_tables, max_q_l
     native().prefill_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, cu_seqlens_q, seq_lens,
                           block_tables, out, max_q_len, kv_layer.block_size, kv_layer.block_stride,
                           kv_layer.num_kv_heads, scale)
+    count_launches()
     return out
 
 
@@ -296,6 +323,7 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     if not logits.is_cuda:
         return out.copy_(logits.float().argmax(dim=-1).to(torch.int32))
     native().argmax(logits, out)
+    count_launches()
     return out
 
 
@@ -307,6 +335,7 @@ def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out=None):
     if not logits.is_cuda:
         return out.copy_(sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets))
     native().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out)
+    count_launches()
     return out
 
 
@@ -354,4 +383,5 @@ def apply_penalties(logits, rows, ids, gen_counts, presence, frequency, repetiti
         logits[r, i] = vals
         return logits
     native().penalties(logits, rows, ids, gen_counts, presence, frequency, repetition)
+    count_launches()
     return logits

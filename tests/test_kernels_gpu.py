@@ -1,0 +1,267 @@
+"""Native sm_100a kernels against plain-PyTorch fp32 references of the same op."""
+import math
+
+import pytest
+import torch
+
+from b200moe import ops
+from b200moe.engine.kv_cache import KVPool
+from b200moe.utils.weights import quantize_block_fp8
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _fp8_weight(groups, n, k, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    w = torch.randn(groups, n, k, generator=g, device=DEV) * 0.05
+    return quantize_block_fp8(w)
+
+
+def _ref_w(q, s):
+    # the kernel dequantises to bf16 before the MMA
+    return ops.dequant_block_fp8(q, s).to(torch.bfloat16).float()
+
+
+def _close(out, ref, tol=2e-2):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max err {err:.4g} vs scale {scale:.4g}"
+
+
+@pytest.mark.parametrize("T", [1, 7, 64, 300])
+@pytest.mark.parametrize("n,k", [(512, 256), (5120, 2048)])
+def test_gemm_fp8_dense(T, n, k):
+    q, s = _fp8_weight(1, n, k, 1)
+    x = (torch.randn(T, k, device=DEV) * 0.5).to(torch.bfloat16)
+    out = ops.linear(x, q[0], s[0])
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    _close(out, x.float() @ _ref_w(q[0], s[0]).t())
+
+
+@pytest.mark.parametrize("T", [3, 200])
+def test_gemm_bf16_f32_out(T):
+    w = (torch.randn(256, 2048, device=DEV) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, 2048, device=DEV).to(torch.bfloat16)
+    out = ops.linear(x, w, None, out_dtype=torch.float32)
+    _close(out, x.float() @ w.float().t(), tol=1e-2)
+
+
+@pytest.mark.parametrize("bn", [16, 32, 128])
+def test_grouped_gate_up_and_down(bn):
+    E, I, H = 8, 128, 256
+    torch.manual_seed(0)
+    counts = torch.tensor([5, 0, 17, 1, 40, 3, 0, 9], dtype=torch.int32, device=DEV)
+    rows = int(counts.sum())
+    offsets = torch.zeros(E + 1, dtype=torch.int32, device=DEV)
+    offsets[1:] = torch.cumsum(counts, 0)
+    q13, s13 = _fp8_weight(E, 2 * I, H, 2)
+    q2, s2 = _fp8_weight(E, H, I, 3)
+    x = (torch.randn(rows, H, device=DEV) * 0.5).to(torch.bfloat16)
+    h = torch.empty(rows, I, dtype=torch.bfloat16, device=DEV)
+    ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I, bn=bn)
+    slot_of_row = torch.randperm(rows, device=DEV).to(torch.int32)
+    wts = torch.rand(rows, device=DEV)
+    slots = torch.zeros(rows, H, dtype=torch.bfloat16, device=DEV)
+    ops.grouped_down_scatter(h, q2, s2, counts, offsets, slot_of_row, wts, slots, bn=bn)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    cpu_off = offsets.tolist()
+    href = torch.empty(rows, I, device=DEV)
+    yref = torch.empty(rows, H, device=DEV)
+    for e in range(E):
+        a, b = cpu_off[e], cpu_off[e + 1]
+        if a == b:
+            continue
+        gu = x[a:b].float() @ _ref_w(q13[e], s13[e]).t()
+        he = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+        href[a:b] = he
+        yref[a:b] = h[a:b].float() @ _ref_w(q2[e], s2[e]).t()
+    _close(h, href)
+    ref_slots = torch.empty_like(yref)
+    ref_slots[slot_of_row.long()] = yref * wts[slot_of_row.long()].unsqueeze(1)
+    _close(slots, ref_slots)
+
+
+def test_rmsnorm_and_add():
+    T, H = 33, 2048
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    r = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    out = ops.rmsnorm(x, w, 1e-6)
+    ref = ops.rmsnorm(x.cpu(), w.cpu(), 1e-6)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2e-2, rtol=1e-2)
+    r_gpu, r_cpu = r.clone(), r.cpu().clone()
+    out = ops.rmsnorm(x, w, 1e-6, residual=r_gpu)
+    ref = ops.rmsnorm(x.cpu(), w.cpu(), 1e-6, residual=r_cpu)
+    torch.testing.assert_close(r_gpu.cpu().float(), r_cpu.float(), atol=1e-2, rtol=1e-2)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2e-2, rtol=1e-2)
+
+
+def test_moe_combine():
+    T, k, H = 9, 8, 2048
+    slots = torch.randn(T * k, H, device=DEV).to(torch.bfloat16)
+    r = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    w = torch.ones(H, device=DEV, dtype=torch.bfloat16)
+    r_gpu, r_cpu = r.clone(), r.cpu().clone()
+    out = ops.moe_combine_add_rmsnorm(slots, k, r_gpu, w, 1e-6)
+    ref = ops.moe_combine_add_rmsnorm(slots.cpu(), k, r_cpu, w.cpu(), 1e-6)
+    torch.testing.assert_close(r_gpu.cpu().float(), r_cpu.float(), atol=3e-2, rtol=1e-2)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=3e-2, rtol=1e-2)
+
+
+def _pool(num_blocks, bs, nkv, D, int8=False, device=DEV):
+    return KVPool(num_blocks, 2, nkv, bs, D, torch.bfloat16, device, int8=int8)
+
+
+@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 4), (64, 4, 2)])
+def test_qknorm_rope_kvstore(D, nq, nkv):
+    T, bs = 20, 16
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device=DEV).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=DEV)
+    slots = torch.randperm(8 * bs, device=DEV)[:T].to(torch.int32)
+    qw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    cs = ops.rope_cos_sin(D, 4096, 1e6, DEV)
+    pg, pc = _pool(9, bs, nkv, D), _pool(9, bs, nkv, D, device="cpu")
+    qg = ops.qknorm_rope_kvstore(qkv, pos, slots, qw, kw, cs, pg.layer(1), nq, nkv, D, 1e-6)
+    qc = ops.qknorm_rope_kvstore(qkv.cpu(), pos.cpu(), slots.cpu(), qw.cpu(), kw.cpu(), cs.cpu(), pc.layer(1),
+                                 nq, nkv, D, 1e-6)
+    torch.testing.assert_close(qg.cpu().float(), qc.float(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(pg.data.cpu().float(), pc.data.float(), atol=2e-2, rtol=2e-2)
+
+
+def test_router_topk():
+    T, E, k = 77, 128, 8
+    logits = torch.randn(T, 256, device=DEV)
+    ids = torch.empty(T, k, dtype=torch.int32, device=DEV)
+    w = torch.empty(T, k, device=DEV)
+    counts = torch.zeros(E, dtype=torch.int32, device=DEV)
+    ops.router_topk(logits, E, k, True, ids, w, counts)
+    ids_c, w_c = torch.empty(T, k, dtype=torch.int32), torch.empty(T, k)
+    counts_c = torch.zeros(E, dtype=torch.int32)
+    ops.router_topk(logits.cpu(), E, k, True, ids_c, w_c, counts_c)
+    assert torch.equal(ids.cpu().sort(dim=1).values, ids_c.sort(dim=1).values)
+    torch.testing.assert_close(w.cpu().sort(dim=1).values, w_c.sort(dim=1).values, atol=1e-2, rtol=1e-2)
+    assert torch.equal(counts.cpu(), counts_c)
+
+
+def test_moe_permute():
+    T, k, E, H = 50, 8, 128, 2048
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device=DEV)[:k] for _ in range(T)]).to(torch.int32)
+    counts = torch.bincount(ids.flatten().long(), minlength=E).to(torch.int32)
+    cursor = torch.zeros(E, dtype=torch.int32, device=DEV)
+    xp = torch.empty(T * k, H, dtype=torch.bfloat16, device=DEV)
+    sor = torch.empty(T * k, dtype=torch.int32, device=DEV)
+    offs = torch.empty(E + 1, dtype=torch.int32, device=DEV)
+    ops.moe_permute(x, ids, counts, cursor, xp, sor, offs)
+    torch.cuda.synchronize()
+    assert torch.equal(xp, x[(sor // k).long()])
+    ref_off = torch.zeros(E + 1, dtype=torch.int32)
+    ref_off[1:] = torch.cumsum(counts.cpu(), 0)
+    assert torch.equal(offs.cpu(), ref_off)
+    e_of_row = ids.flatten()[sor.long()].cpu()
+    for e in range(E):
+        a, b = ref_off[e], ref_off[e + 1]
+        assert bool((e_of_row[a:b] == e).all())
+
+
+def _fill_pool(pool, seq_lens, bs, nkv, D, int8=False):
+    """Random K/V for sequences on shuffled blocks; returns block tables."""
+    nb = [math.ceil(L / bs) for L in seq_lens]
+    perm = torch.randperm(pool.num_blocks - 1).tolist()
+    tables = torch.zeros(len(seq_lens), max(nb), dtype=torch.int32)
+    i = 0
+    for b, n in enumerate(nb):
+        tables[b, :n] = torch.tensor(perm[i:i + n])
+        i += n
+    for b, L in enumerate(seq_lens):
+        pos = torch.arange(L)
+        slots = (tables[b][pos // bs].long() * bs + pos % bs).to(torch.int32).to(pool.data.device)
+        for l in range(pool.num_layers):
+            k = torch.randn(L, nkv, D, device=pool.data.device).to(torch.bfloat16)
+            v = torch.randn(L, nkv, D, device=pool.data.device).to(torch.bfloat16)
+            pool.layer(l).store(slots, k, v)
+    return tables.to(pool.data.device)
+
+
+@pytest.mark.parametrize("int8", [False, True])
+@pytest.mark.parametrize("D,nq,nkv,bs", [(128, 32, 4, 256), (128, 32, 4, 16), (64, 4, 2, 16)])
+def test_decode_attention(D, nq, nkv, bs, int8):
+    seq_lens = [1, 17, 255, 256, 257, 700, 1300]
+    B = len(seq_lens)
+    nblocks = sum(math.ceil(L / bs) for L in seq_lens) + 2
+    pool = _pool(nblocks, bs, nkv, D, int8=int8)
+    tables = _fill_pool(pool, seq_lens, bs, nkv, D, int8)
+    q = torch.randn(B, nq, D, device=DEV).to(torch.bfloat16)
+    lens = torch.tensor(seq_lens, dtype=torch.int32, device=DEV)
+    for split_len, nsplit in [(2048, 1), (256, 6), (64, 21)]:
+        ws = (torch.empty(B * nq * nsplit, D, device=DEV), torch.empty(B * nq * nsplit, device=DEV),
+              torch.empty(B * nq * nsplit, device=DEV))
+        out = torch.empty(B, nq, D, dtype=torch.bfloat16, device=DEV)
+        ops.decode_attention(q, pool.layer(1), tables, lens, D ** -0.5, out, split_len, nsplit, ws)
+        ref = torch.empty(B, nq, D, device=DEV)
+        ops._attention_ref(q, pool.layer(1), tables, lens, torch.arange(B + 1, dtype=torch.int32),
+                           D ** -0.5, ref)
+        torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("int8", [False, True])
+@pytest.mark.parametrize("D,nq,nkv,bs", [(128, 32, 4, 256), (64, 4, 2, 16)])
+def test_prefill_attention(D, nq, nkv, bs, int8):
+    # (query length, total length): fresh prompts, chunk continuations, prefix hits
+    shapes = [(5, 5), (64, 64), (100, 100), (37, 300), (256, 512), (1, 90)]
+    seq_lens = [L for _, L in shapes]
+    nblocks = sum(math.ceil(L / bs) for L in seq_lens) + 2
+    pool = _pool(nblocks, bs, nkv, D, int8=int8)
+    tables = _fill_pool(pool, seq_lens, bs, nkv, D, int8)
+    cu = [0]
+    for qn, _ in shapes:
+        cu.append(cu[-1] + qn)
+    T = cu[-1]
+    q = torch.randn(T, nq, D, device=DEV).to(torch.bfloat16)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    lens = torch.tensor(seq_lens, dtype=torch.int32, device=DEV)
+    out = torch.empty(T, nq, D, dtype=torch.bfloat16, device=DEV)
+    ops.prefill_attention(q, pool.layer(0), cu_t, lens, tables, max(s for s, _ in shapes), D ** -0.5, out)
+    ref = torch.empty(T, nq, D, device=DEV)
+    ops._attention_ref(q, pool.layer(0), tables, lens, cu_t, D ** -0.5, ref)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_argmax_and_sampler():
+    B, V = 6, 151936
+    logits = torch.randn(B, V, device=DEV)
+    logits[2, 12345] = 50.0
+    out = ops.argmax(logits)
+    assert torch.equal(out.cpu().long(), logits.argmax(dim=-1).cpu())
+    temp = torch.tensor([0.0, 0.7, 1.0, 0.7, 1.0, 0.5], device=DEV)
+    top_k = torch.tensor([-1, 5, -1, -1, 1, 50], dtype=torch.int32, device=DEV)
+    top_p = torch.tensor([1.0, 1.0, 0.9, 0.5, 1.0, 0.95], device=DEV)
+    seeds = torch.arange(B, dtype=torch.int64, device=DEV) + 11
+    s = ops.sample(logits, temp, top_k, top_p, None, seeds, None)
+    s2 = ops.sample(logits, temp, top_k, top_p, None, seeds, None)
+    assert torch.equal(s, s2), "same seed must give the same draw"
+    assert int(s[0]) == int(logits[0].argmax())
+    assert int(s[4]) == int(logits[4].argmax())  # top_k 1
+    assert int(s[2]) == 12345  # dominant logit survives top-p
+    top5 = set(torch.topk(logits[1], 5).indices.tolist())
+    assert int(s[1]) in top5
+
+
+def test_sampler_distribution():
+    """Exponential race draws follow softmax(logits / T) over the kept set."""
+    V, N = 8, 4000
+    base = torch.tensor([2.0, 1.0, 0.5, 0.0, -1.0, -2.0, -3.0, -4.0], device=DEV)
+    logits = base.repeat(N, 1).contiguous()
+    temp = torch.full((N,), 1.0, device=DEV)
+    seeds = torch.arange(N, dtype=torch.int64, device=DEV)
+    s = ops.sample(logits, temp, None, None, None, seeds, None)
+    freq = torch.bincount(s.long(), minlength=V).float() / N
+    p = torch.softmax(base, dim=0)
+    assert (freq - p).abs().max().item() < 0.03
+    tk = torch.full((N,), 3, dtype=torch.int32, device=DEV)
+    s = ops.sample(logits, temp, tk, None, None, seeds, None)
+    assert int(s.max()) <= 2
