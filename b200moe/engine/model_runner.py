@@ -115,7 +115,8 @@ class ModelRunner:
         self.h2d_bytes = 0
         self._step_events: list = []
         self._graph_kernels: dict[int, int] = {}
-        if self.device.type == "cuda" and not config.enforce_eager:
+        graph_ok = self.model.ep is None or self.model.ep.graph_safe
+        if self.device.type == "cuda" and not config.enforce_eager and graph_ok:
             self.capture_cudagraphs()
 
     # ------------------------------------------------------------- setup

@@ -1,0 +1,219 @@
+"""Kernel microbenchmarks on the 30B-A3B shapes, timed with CUDA events.
+
+    python -m b200moe.microbench <case> [--tokens T] [--iters N]
+
+cases:
+  moe        grouped gate_up+SiLU and down GEMMs of one MoE layer (128 experts,
+             T tokens x top-8, uniform random routing)
+  dense      QKV (5120x2048) and O-proj (2048x4096) block-scaled GEMMs, LM head
+  decode     paged decode attention, T sequences of --ctx tokens
+  prefill    paged prefill attention, T/--ctx sequences of --ctx tokens
+  step       whole-model forward (eager) of T decode rows at --ctx context
+  all        every kernel case above
+
+Each case prints a JSON line per kernel: milliseconds per call, the bytes or
+FLOPs it must move, and the achieved fraction of the measured peaks (copy
+bandwidth and cuBLAS bf16 throughput; MEASURED_PEAKS.json when present,
+else 6.65 TB/s and 1.59 PFLOP/s).  Inputs are larger than L2 for the
+bandwidth-bound cases, and a 256 MB buffer is rewritten between iterations.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from b200moe import ops
+from b200moe.utils.weights import quantize_block_fp8
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"] * 1e9, d["bf16_tflops"] * 1e12, "measured"
+    except Exception:
+        return 6.65e12, 1.59e15, "fallback"
+
+
+_flush = None
+
+
+def flush_l2():
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _flush.fill_(1)
+
+
+def timeit(fn, iters=20, warmup=3, flush=True):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(iters):
+        if flush:
+            flush_l2()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / iters
+
+
+def report(name, ms, bytes_=0, flops=0, **extra):
+    bw, tf, src = peaks()
+    d = {"kernel": name, "ms": round(ms, 4)}
+    if bytes_:
+        d["GB/s"] = round(bytes_ / ms / 1e6, 1)
+        d["hbm_frac"] = round(bytes_ / (ms / 1e3) / bw, 3)
+    if flops:
+        d["TFLOP/s"] = round(flops / ms / 1e9, 1)
+        d["tc_frac"] = round(flops / (ms / 1e3) / tf, 3)
+    d["peak"] = src
+    d.update(extra)
+    print(json.dumps(d), flush=True)
+    return d
+
+
+def fp8_weight(groups, n, k, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    qs, ss = [], []
+    for i in range(groups):
+        q, s = quantize_block_fp8(torch.randn(n, k, generator=g, device="cuda") * 0.02)
+        qs.append(q)
+        ss.append(s)
+    return torch.stack(qs), torch.stack(ss)
+
+
+def case_moe(T, iters, E=128, k=8, H=2048, I=768):
+    q13, s13 = fp8_weight(E, 2 * I, H, 1)
+    q2, s2 = fp8_weight(E, H, I, 2)
+    rows = T * k
+    ids = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]).flatten()
+    counts = torch.bincount(ids, minlength=E).to(torch.int32)
+    offsets = torch.zeros(E + 1, dtype=torch.int32, device="cuda")
+    offsets[1:] = torch.cumsum(counts, 0)
+    x = (torch.randn(rows, H, device="cuda") * 0.5).to(torch.bfloat16)
+    h = torch.empty(rows, I, dtype=torch.bfloat16, device="cuda")
+    slots = torch.empty(rows, H, dtype=torch.bfloat16, device="cuda")
+    sor = torch.randperm(rows, device="cuda").to(torch.int32)
+    w = torch.rand(rows, device="cuda")
+    used = int((counts > 0).sum())
+    ms = timeit(lambda: ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I), iters)
+    wbytes = used * 2 * I * H + rows * H * 2 + rows * I * 2
+    report("moe_gate_up_silu", ms, wbytes, 2 * rows * H * 2 * I, tokens=T,
+           bn=ops.pick_bn(rows, I // 128, E, pair=True))
+    ms = timeit(lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots), iters)
+    wbytes = used * H * I + rows * I * 2 + rows * H * 2
+    report("moe_down_scatter", ms, wbytes, 2 * rows * I * H, tokens=T, bn=ops.pick_bn(rows, H // 128, E))
+
+
+def case_dense(T, iters, H=2048):
+    x = (torch.randn(T, H, device="cuda") * 0.5).to(torch.bfloat16)
+    q, s = fp8_weight(1, 5120, H, 3)
+    ms = timeit(lambda: ops.linear(x, q[0], s[0]), iters)
+    report("qkv_proj", ms, 5120 * H + T * (H + 5120) * 2, 2 * T * H * 5120, tokens=T)
+    xo = (torch.randn(T, 4096, device="cuda") * 0.5).to(torch.bfloat16)
+    q, s = fp8_weight(1, H, 4096, 4)
+    ms = timeit(lambda: ops.linear(xo, q[0], s[0]), iters)
+    report("o_proj", ms, H * 4096 + T * (H + 4096) * 2, 2 * T * H * 4096, tokens=T)
+    lm = (torch.randn(151936, H, device="cuda") * 0.02).to(torch.bfloat16)
+    rows = min(T, 512)
+    ms = timeit(lambda: ops.linear(x[:rows], lm, None, out_dtype=torch.float32), iters)
+    report("lm_head", ms, 151936 * H * 2 + rows * 151936 * 4, 2 * rows * H * 151936, tokens=rows)
+
+
+def _kv(T, ctx, bs=256, nkv=4, D=128, layers=2):
+    from b200moe.engine.kv_cache import KVPool
+    nb = T * math.ceil(ctx / bs)
+    pool = KVPool(nb + 1, layers, nkv, bs, D, torch.bfloat16, "cuda")
+    pool.data.normal_()
+    tables = torch.arange(nb, dtype=torch.int32, device="cuda").view(T, -1)
+    return pool, tables
+
+
+def case_decode(T, ctx, iters, nq=32, nkv=4, D=128):
+    from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM
+    pool, tables = _kv(T, ctx)
+    q = torch.randn(T, nq, D, device="cuda").to(torch.bfloat16)
+    lens = torch.full((T,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    model = type("M", (), {"args": type("A", (), {"num_key_value_heads": nkv})()})()
+    split_len, nsplit = Qwen3MoeForCausalLM.decode_splits(model, T, ctx)
+    ws = (torch.empty(T * nq * nsplit, D, device="cuda"), torch.empty(T * nq * nsplit, device="cuda"),
+          torch.empty(T * nq * nsplit, device="cuda"))
+    ms = timeit(lambda: ops.decode_attention(q, pool.layer(0), tables, lens, D ** -0.5, out, split_len, nsplit, ws),
+                iters)
+    report("decode_attn", ms, T * ctx * nkv * D * 2 * 2, 4 * T * ctx * nq * D, seqs=T, ctx=ctx, splits=nsplit)
+
+
+def case_prefill(T, ctx, iters, nq=32, nkv=4, D=128):
+    B = max(1, T // ctx)
+    pool, tables = _kv(B, ctx)
+    q = torch.randn(B * ctx, nq, D, device="cuda").to(torch.bfloat16)
+    cu = torch.arange(0, B * ctx + 1, ctx, dtype=torch.int32, device="cuda")
+    lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    ms = timeit(lambda: ops.prefill_attention(q, pool.layer(0), cu, lens, tables, ctx, D ** -0.5, out), iters)
+    report("prefill_attn", ms, 0, 2 * B * ctx * ctx * nq * D, seqs=B, ctx=ctx)
+
+
+def case_step(T, ctx, iters, layers=48):
+    from b200moe.config import ModelArgs
+    from b200moe.engine.kv_cache import KVPool
+    from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM, StepInputs
+    from b200moe.utils.weights import random_init_
+    args = ModelArgs(num_hidden_layers=layers)
+    model = Qwen3MoeForCausalLM(args, "cuda")
+    random_init_(model)
+    bs = 256
+    nbs = math.ceil((ctx + 1) / bs)
+    model.reserve_workspace(max(T, 1), T, 64)
+    pool = KVPool(T * nbs + 1, layers, 4, bs, 128, torch.bfloat16, "cuda")
+    tables = torch.arange(T * nbs, dtype=torch.int32, device="cuda").view(T, -1)
+    i32 = lambda t: t.to(torch.int32)
+    pos = torch.full((T,), ctx, dtype=torch.int32, device="cuda")
+    slots = i32(tables[:, ctx // bs] * bs + ctx % bs)
+    inp = StepInputs(i32(torch.randint(0, 151936, (T,), device="cuda")), pos, slots,
+                     torch.arange(T + 1, dtype=torch.int32, device="cuda"), pos + 1, tables,
+                     torch.arange(T, dtype=torch.int32, device="cuda"), T, 0, ctx + 1, T)
+    fn = lambda: model.compute_logits(model(inp, pool))
+    ms = timeit(fn, iters, flush=False)
+    wbytes = layers * (128 * 3 * 2048 * 768 + (5120 + 2048) * 2048 * 1.0) + 151936 * 2048 * 2
+    kvbytes = T * (ctx + 1) * layers * 4 * 128 * 2 * 2
+    report("decode_step", ms, wbytes + kvbytes, 0, rows=T, ctx=ctx, layers=layers)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "all"])
+    p.add_argument("--tokens", type=int, default=256)
+    p.add_argument("--ctx", type=int, default=1152)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--layers", type=int, default=48)
+    a = p.parse_args()
+    torch.cuda.set_device(0)
+    if a.case in ("moe", "all"):
+        case_moe(a.tokens, a.iters)
+    if a.case in ("dense", "all"):
+        case_dense(a.tokens, a.iters)
+    if a.case in ("decode", "all"):
+        case_decode(a.tokens, a.ctx, a.iters)
+    if a.case in ("prefill", "all"):
+        case_prefill(max(a.tokens, a.ctx), a.ctx, a.iters)
+    if a.case == "step":
+        case_step(a.tokens, a.ctx, a.iters, a.layers)
+    ops.check_status("cuda")
+
+
+if __name__ == "__main__":
+    main()
