@@ -176,6 +176,7 @@ class LLMEngine:
         self.executor.launch(batch, self._grammar_masks(batch))
 
     def step(self):
+        self.last_token_events = []
         if self._overlap or self._pending is not None or self._sched_next is not None:
             return self._step_overlap()
         batch = self.scheduler.schedule()
