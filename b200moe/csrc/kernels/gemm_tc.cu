@@ -7,15 +7,19 @@
 // plain bf16 weight.  X (the "B" operand, N = tokens) is bf16.  One CTA per SM
 // runs a persistent loop over (group, n-tile, m-tile) work items computed on
 // the device from per-group token counts, so the launch needs no host sync and
-// is CUDA-graph safe.  Roles (320 threads):
+// is CUDA-graph safe.  Roles (448 threads):
 //
-//   warp 0     TMA producer: fp8/bf16 weight tile + bf16 activation tile per stage
-//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-5  dequantisers: e4m3 * scale -> bf16 into the 128B-swizzled UMMA
-//              layout (exactly bf16(float(q) * scale), the reference's
-//              load-time dequant, done per tile in shared memory)
-//   warps 6-9  epilogue: tcgen05.ld of the double-buffered TMEM accumulator,
-//              fused op, global store
+//   warp 0      TMA producer: fp8 (or bf16) weight tile + bf16 activation tile
+//               per stage into a deep ring that holds only the loaded bytes
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-9   dequantisers: e4m3 * scale -> bf16 into a separate, double-
+//               buffered ring in the 128B-swizzled UMMA layout (exactly
+//               bf16(float(q) * scale), the reference's load-time dequant, done
+//               per tile in shared memory).  Keeping the bf16 copies out of the
+//               load ring is what lets ~8 loads per SM stay in flight.
+//   warps 10-13 epilogue: tcgen05.ld of the double-buffered TMEM accumulator,
+//               fused op, global store; per-tile row metadata (scatter slots and
+//               routing weights) is staged in shared memory once per tile
 //
 // Epilogues: bf16 store, fp32 store (router / LM-head logits), SiLU(gate)*up of
 // a gate/up tile pair (two MMAs into adjacent TMEM columns), and the MoE "down"
@@ -39,7 +43,9 @@
 
 namespace b200 {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
+constexpr int kConvThreads = 256;   // warps 2..9
+constexpr int kEpiWarp0 = 10;       // warps 10..13
 constexpr int kMaxGroups = 512;
 constexpr int kBK = 64;            // K elements per pipeline stage (128 B of bf16)
 constexpr int kSmemBudget = 225 * 1024;
@@ -48,13 +54,18 @@ template <int BN, bool PAIR, bool AFP8>
 struct GemmCfg {
   static constexpr int NA = PAIR ? 2 : 1;
   static constexpr int A16_BYTES = 128 * kBK * 2;     // 16 KB bf16 tile
-  static constexpr int A8_BYTES = AFP8 ? 128 * kBK : 0;
+  static constexpr int A8_BYTES = 128 * kBK;          // 8 KB e4m3 tile
   static constexpr int B_BYTES = BN * kBK * 2;
-  static constexpr int STAGE_BYTES = NA * A16_BYTES + B_BYTES + NA * A8_BYTES;
-  static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4;
-  static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + EXTRA + 1024;
+  // load ring: what TMA writes (fp8 weights or, in bf16 mode, the UMMA-ready A tile)
+  static constexpr int ALOAD_BYTES = AFP8 ? A8_BYTES : A16_BYTES;
+  static constexpr int STAGE_BYTES = NA * ALOAD_BYTES + B_BYTES;
+  // bf16 ring fed by the dequantisers (fp8 mode only)
+  static constexpr int CONV_SLOTS = AFP8 ? 2 : 0;
+  static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
+  static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8;
+  static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + CONV_BYTES + EXTRA + 1024;
   static constexpr int ACC_COLS = NA * BN;
   static constexpr int TMEM_COLS_RAW = 2 * ACC_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
@@ -62,7 +73,7 @@ struct GemmCfg {
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(TMEM_COLS_RAW <= 512, "accumulators exceed TMEM");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16,256]");
-  static constexpr uint32_t TX_BYTES = NA * (AFP8 ? A8_BYTES : A16_BYTES) + B_BYTES;
+  static constexpr uint32_t TX_BYTES = NA * ALOAD_BYTES + B_BYTES;
 };
 
 struct TileCoord {
@@ -95,23 +106,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 
   // ---- shared-memory carve-up
   uint8_t* stage_base = smem;
-  uint8_t* extra = smem + C::STAGES * C::STAGE_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);
-  uint64_t* conv_bar = full_bar + 8;
-  uint64_t* empty_bar = conv_bar + 8;
-  uint64_t* accf_bar = empty_bar + 8;
+  uint8_t* conv_base = smem + C::STAGES * C::STAGE_BYTES;
+  uint8_t* extra = conv_base + C::CONV_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);   // [12] TMA landed
+  uint64_t* empty_bar = full_bar + 12;                       // [12] load slot free
+  uint64_t* cfull_bar = empty_bar + 12;                      // [2] bf16 slot written
+  uint64_t* cempty_bar = cfull_bar + 2;                      // [2] bf16 slot consumed
+  uint64_t* accf_bar = cempty_bar + 2;
   uint64_t* acce_bar = accf_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* conv_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);
   int* tile_prefix = reinterpret_cast<int*>(extra + 4096);
   int* row_off = tile_prefix + (kMaxGroups + 1);
+  int* meta_slot = row_off + (kMaxGroups + 1);                 // [2][256] scatter slot per column
+  float* meta_w = reinterpret_cast<float*>(meta_slot + 512);   // [2][256] routing weight per column
 
-  auto A16 = [&](int s, int a) { return stage_base + s * C::STAGE_BYTES + a * C::A16_BYTES; };
-  auto Bt = [&](int s) { return stage_base + s * C::STAGE_BYTES + C::NA * C::A16_BYTES; };
-  auto A8 = [&](int s, int a) {
-    return stage_base + s * C::STAGE_BYTES + C::NA * C::A16_BYTES + C::B_BYTES + a * C::A8_BYTES;
-  };
+  auto ALd = [&](int s, int a) { return stage_base + s * C::STAGE_BYTES + a * C::ALOAD_BYTES; };
+  auto Bt = [&](int s) { return stage_base + s * C::STAGE_BYTES + C::NA * C::ALOAD_BYTES; };
+  auto A16 = [&](int j, int a) { return conv_base + (j * C::NA + a) * C::A16_BYTES; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -148,8 +162,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   if (threadIdx.x == 32) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&conv_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&empty_bar[s], AFP8 ? 2 : 1);  // fp8: dequantisers (A) + MMA (B)
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&cfull_bar[j], 1);
+      mbar_init(&cempty_bar[j], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
@@ -189,13 +206,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           if (!mbar_wait(&empty_bar[s], phase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[s], C::TX_BYTES);
           const int x = ks * kBK;
-          if constexpr (AFP8) {
-            tma_load_2d(A8(s, 0), &tmap_a, &full_bar[s], x, a_row);
-            if constexpr (PAIR) tma_load_2d(A8(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
-          } else {
-            tma_load_2d(A16(s, 0), &tmap_a, &full_bar[s], x, a_row);
-            if constexpr (PAIR) tma_load_2d(A16(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
-          }
+          tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], x, a_row);
+          if constexpr (PAIR) tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
           tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
@@ -214,6 +226,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       int s = 0;
       uint32_t phase = 0;
       int lt = 0;
+      int gi = 0;  // global stage counter (bf16 ring index)
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
         const int abuf = lt & 1;
@@ -221,10 +234,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         if (!mbar_wait(&acce_bar[abuf], aphase ^ 1, status, kStatusTimeoutAccEmpty, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_base = tmem_base + abuf * C::ACC_COLS;
-        for (int ks = 0; ks < k_stages; ++ks) {
+        for (int ks = 0; ks < k_stages; ++ks, ++gi) {
           if (!mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) { ok = false; break; }
+          const int cj = gi & 1;
+          const uint32_t cph = (gi >> 1) & 1;
           if constexpr (AFP8) {
-            if (!mbar_wait(&conv_bar[s], phase, status, kStatusTimeoutConv, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&cfull_bar[cj], cph, status, kStatusTimeoutConv, abort_flag)) { ok = false; break; }
           }
           tc_fence_after();
           const uint32_t b_addr = smem_u32(Bt(s));
@@ -233,42 +248,51 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const uint64_t bdesc = umma_sdesc_sw128(b_addr + k * 32);
 #pragma unroll
             for (int a = 0; a < C::NA; ++a) {
-              const uint64_t adesc = umma_sdesc_sw128(smem_u32(A16(s, a)) + k * 32);
+              const uint8_t* abuf_ptr = AFP8 ? A16(cj, a) : ALd(s, a);
+              const uint64_t adesc = umma_sdesc_sw128(smem_u32(abuf_ptr) + k * 32);
               umma_f16_ss(d_base + a * BN, adesc, bdesc, idesc, (ks | k) != 0 ? 1u : 0u);
             }
           }
           umma_commit(&empty_bar[s]);
+          if constexpr (AFP8) umma_commit(&cempty_bar[cj]);
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
         if (!ok) break;
         umma_commit(&accf_bar[abuf]);
       }
     }
-  } else if (warp >= 2 && warp < 6) {
+  } else if (warp >= 2 && warp < kEpiWarp0) {
     // ================================================= dequantisers
     if constexpr (AFP8) {
-      const int c = threadIdx.x - 64;  // 0..127
+      const int c = threadIdx.x - 64;  // 0..255
       int s = 0;
       uint32_t phase = 0;
+      int gi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
         const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * args.scale_k_blocks;
-        for (int ks = 0; ks < k_stages; ++ks) {
-          // one thread waits, the verdict is broadcast so all 128 leave together
-          if (c == 0) *conv_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) ? 1 : 0;
-          named_barrier_sync(1, 128);
+        for (int ks = 0; ks < k_stages; ++ks, ++gi) {
+          const int cj = gi & 1;
+          const uint32_t cph = (gi >> 1) & 1;
+          // one thread waits, the verdict is broadcast so all 256 leave together
+          if (c == 0) {
+            bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) &&
+                        mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
+            *conv_ok = w_ok ? 1 : 0;
+          }
+          named_barrier_sync(1, kConvThreads);
           if (!*conv_ok) { ok = false; break; }
           const int kb = (ks * kBK) / 128;
 #pragma unroll
           for (int a = 0; a < C::NA; ++a) {
             const int mb = tc.i + (a ? args.pair_row_offset / 128 : 0);
             const float scale = __ldg(sc + mb * args.scale_k_blocks + kb);
-            const uint8_t* src = A8(s, a);
-            uint8_t* dst = A16(s, a);
+            const uint8_t* src = ALd(s, a);
+            uint8_t* dst = A16(cj, a);
 #pragma unroll
-            for (int it = 0; it < 4; ++it) {
-              const int chunk = c + 128 * it;
+            for (int it = 0; it < 2; ++it) {
+              const int chunk = c + kConvThreads * it;
               const int row = chunk >> 2, c16 = chunk & 3;
               const uint4 q = *reinterpret_cast<const uint4*>(src + row * 64 + c16 * 16);
               const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -291,8 +315,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             }
           }
           fence_proxy_async_smem();
-          named_barrier_sync(1, 128);
-          if (c == 0) mbar_arrive(&conv_bar[s]);
+          named_barrier_sync(1, kConvThreads);
+          if (c == 0) {
+            mbar_arrive(&empty_bar[s]);   // the e4m3 tile of this load slot is consumed
+            mbar_arrive(&cfull_bar[cj]);  // the bf16 tile is ready for the MMA
+          }
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
       }
@@ -301,17 +328,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     // ====================================================== epilogue
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     const int m_local = q * 32 + lane;
+    const int et = threadIdx.x - kEpiWarp0 * 32;  // 0..127
     int lt = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
       TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
       const int abuf = lt & 1;
       const uint32_t aphase = (lt >> 1) & 1;
-      if (!mbar_wait(&accf_bar[abuf], aphase, status, kStatusTimeoutAccFull, abort_flag)) { ok = false; break; }
-      tc_fence_after();
       const int count = args.group_count[tc.g];
       const int ncols = min(BN, count - tc.j * BN);
       const int row0 = row_off[tc.g] + tc.j * BN;
+      int* mslot = meta_slot + abuf * 256;
+      float* mw = meta_w + abuf * 256;
+      if constexpr (EPI == kEpiScatter) {
+        // stage the tile's scatter slots and routing weights once (while the MMAs run)
+        for (int col = et; col < ncols; col += 128) {
+          const int slot = args.slot_of_row[row0 + col];
+          mslot[col] = slot;
+          mw[col] = args.slot_weight[slot];
+        }
+      }
+      // one thread waits for the accumulator, the verdict is broadcast so the
+      // four warps always leave (or continue) together
+      if (et == 0) epi_ok[0] = mbar_wait(&accf_bar[abuf], aphase, status, kStatusTimeoutAccFull, abort_flag) ? 1 : 0;
+      named_barrier_sync(2, 128);
+      if (!epi_ok[0]) { ok = false; break; }
+      tc_fence_after();
       const uint32_t t_base = tmem_base + (uint32_t(q * 32) << 16) + abuf * C::ACC_COLS;
       const int m_out = tc.i * 128 + m_local;
 #pragma unroll 1
@@ -346,10 +388,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 float* out = reinterpret_cast<float*>(args.out);
                 out[(size_t)row * args.ld_out + m_glob] = v[n];
               } else {  // kEpiScatter
-                const int slot = args.slot_of_row[row];
-                const float w = args.slot_weight[slot];
                 __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-                out[(size_t)slot * args.ld_out + m_out] = __float2bfloat16(v[n] * w);
+                out[(size_t)mslot[col] * args.ld_out + m_out] = __float2bfloat16(v[n] * mw[col]);
               }
             }
           }

@@ -16,12 +16,12 @@ pytestmark = pytest.mark.gpu
 
 
 def _inputs(seq_lens, q_lens, bs, device, vocab):
-    """StepInputs for sequences whose first (L - q) tokens are cached."""
+    """StepInputs for sequences whose first (L - q) tokens are cached.
+    Decode rows (q == 1) first; blocks assigned consecutively."""
     B = len(seq_lens)
     order = sorted(range(B), key=lambda i: (q_lens[i] != 1, i))
-    ids, pos, slots, cu, tables = [], [], [0], [], []
     nb = [-(-L // bs) for L in seq_lens]
-    base = 0
+    ids, pos, slots, tables, base = [], [], [], [], 0
     for i in order:
         L, q = seq_lens[i], q_lens[i]
         blocks = list(range(base, base + nb[i]))
@@ -29,14 +29,12 @@ def _inputs(seq_lens, q_lens, bs, device, vocab):
         tables.append(blocks + [0] * (max(nb) - nb[i]))
         p = list(range(L - q, L))
         pos += p
-        slots_i = [blocks[x // bs] * bs + x % bs for x in p]
+        slots += [blocks[x // bs] * bs + x % bs for x in p]
         ids += [random.randrange(vocab) for _ in p]
-        cu.append(slots_i)
     cu_q = np.cumsum([0] + [q_lens[i] for i in order]).astype(np.int32)
     nd = sum(1 for q in q_lens if q == 1)
     t = lambda a: torch.tensor(np.asarray(a), dtype=torch.int32, device=device)
-    flat_slots = [s for lst in cu[1:] for s in lst]
-    return StepInputs(t(ids), t(pos), t(flat_slots), t(cu_q), t([seq_lens[i] for i in order]), t(tables),
+    return StepInputs(t(ids), t(pos), t(slots), t(cu_q), t([seq_lens[i] for i in order]), t(tables),
                       t(cu_q[1:] - 1), nd, max([q_lens[i] for i in order if q_lens[i] != 1] or [0]),
                       max(seq_lens), B, t(cu_q[nd:] - cu_q[nd])), base
 
