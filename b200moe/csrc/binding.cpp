@@ -5,7 +5,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <vector>
+
 #include "attention.h"
+#include "ep_p2p.h"
 #include "fused_ops.h"
 #include "gemm_tc.h"
 #include "sampler.h"
@@ -51,6 +54,7 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
     CHECK_CONTIG((*weight_scale));
     TORCH_CHECK(weight_scale->numel() == groups * (rows_per_group / 128) * (K / 128),
                 "weight_scale must be [groups, N/128, K/128]");
+    TORCH_CHECK(K <= 8192, "K must be at most 8192 (64 scale blocks per tile)");
   }
   if (group_offset.has_value()) {
     CHECK_DT((*group_offset), torch::kInt32);
@@ -101,6 +105,115 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
   L.epi = (int)epi;
   b200::gemm_tc_launch(L, stream());
 }
+
+// Down GEMM whose epilogue writes each weighted row into its source rank's
+// slot buffer (peer memory): slot_code = rank * slot_cap + slot.
+void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor group_count, Tensor group_offset,
+                       int64_t bn, Tensor slot_code, Tensor slot_w, std::vector<int64_t> peer_ptrs, int64_t slot_cap,
+                       int64_t ld_out, Tensor status) {
+  CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CONTIG(weight);
+  TORCH_CHECK(weight.dim() == 3 && weight.scalar_type() == torch::kFloat8_e4m3fn, "expert weights must be [E, N, K] e4m3");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.scalar_type() == torch::kBFloat16, "x must be [rows, K] bf16");
+  TORCH_CHECK(peer_ptrs.size() >= 1 && peer_ptrs.size() <= 8, "1..8 peer pointers");
+  CHECK_DT(slot_code, torch::kInt32); CHECK_DT(slot_w, torch::kFloat32);
+  const int64_t groups = weight.size(0), N = weight.size(1), K = weight.size(2);
+  TORCH_CHECK(x.size(1) == K, "K mismatch");
+  TORCH_CHECK(weight_scale.numel() == groups * (N / 128) * (K / 128), "weight_scale shape");
+  if (x.size(0) == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  b200::GemmLaunch L{};
+  L.args.a_scale = weight_scale.data_ptr<float>();
+  L.args.a_rows_per_group = (int)N;
+  L.args.m_tiles = (int)(N / 128);
+  L.args.k_stages = (int)(K / 64);
+  L.args.scale_m_blocks = (int)(N / 128);
+  L.args.scale_k_blocks = (int)(K / 128);
+  L.args.num_groups = (int)groups;
+  L.args.group_count = group_count.data_ptr<int>();
+  L.args.group_offset = group_offset.data_ptr<int>();
+  L.args.out = nullptr;
+  L.args.ld_out = (int)ld_out;
+  L.args.slot_of_row = slot_code.data_ptr<int>();
+  L.args.slot_weight = slot_w.data_ptr<float>();
+  L.args.status = status.data_ptr<int>();
+  L.args.peer_scatter = 1;
+  L.args.slot_cap = (int)slot_cap;
+  for (size_t i = 0; i < peer_ptrs.size(); ++i) L.args.peer_out[i] = reinterpret_cast<void*>(peer_ptrs[i]);
+  L.a = weight.data_ptr();
+  L.a_row_stride_bytes = K;
+  L.b = x.data_ptr();
+  L.b_rows = x.size(0);
+  L.b_row_stride_bytes = x.stride(0) * 2;
+  L.K = (int)K;
+  L.bn = (int)bn;
+  L.a_fp8 = true;
+  L.pair = false;
+  L.epi = b200::kEpiScatter;
+  b200::gemm_tc_launch(L, stream());
+}
+
+b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor send_cursor, Tensor done_blocks,
+                     Tensor epoch, Tensor status, std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta,
+                     std::vector<int64_t> counts, std::vector<int64_t> flags, std::vector<int64_t> done) {
+  TORCH_CHECK(dims.size() == 5, "dims = (world, rank, hidden, cap, slot_cap)");
+  b200::EpArgs a{};
+  a.world = (int)dims[0];
+  a.rank = (int)dims[1];
+  a.hidden = (int)dims[2];
+  a.cap = (int)dims[3];
+  a.slot_cap = (int)dims[4];
+  TORCH_CHECK(a.world >= 1 && a.world <= b200::kEpMaxWorld && a.rank >= 0 && a.rank < a.world, "bad world/rank");
+  TORCH_CHECK((int)recv_x.size() == a.world && (int)recv_meta.size() == a.world && (int)counts.size() == a.world &&
+              (int)flags.size() == a.world && (int)done.size() == a.world, "one pointer per rank");
+  CHECK_DT(owner, torch::kInt32); CHECK_DT(g2l, torch::kInt32); CHECK_DT(send_cursor, torch::kInt32);
+  CHECK_DT(done_blocks, torch::kInt32); CHECK_DT(status, torch::kInt32);
+  a.owner = owner.data_ptr<int>();
+  a.g2l = g2l.data_ptr<int>();
+  a.send_cursor = send_cursor.data_ptr<int>();
+  a.done_blocks = done_blocks.data_ptr<int>();
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  a.status = status.data_ptr<int>();
+  for (int r = 0; r < a.world; ++r) {
+    a.recv_x[r] = reinterpret_cast<void*>(recv_x[r]);
+    a.recv_meta[r] = reinterpret_cast<void*>(recv_meta[r]);
+    a.counts[r] = reinterpret_cast<void*>(counts[r]);
+    a.flags[r] = reinterpret_cast<void*>(flags[r]);
+    a.done[r] = reinterpret_cast<void*>(done[r]);
+  }
+  return a;
+}
+
+#define EP_ARGS_DECL std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor send_cursor, Tensor done_blocks, \
+  Tensor epoch, Tensor status, std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta, \
+  std::vector<int64_t> counts, std::vector<int64_t> flags, std::vector<int64_t> done
+#define EP_ARGS ep_args(dims, owner, g2l, send_cursor, done_blocks, epoch, status, recv_x, recv_meta, counts, flags, done)
+
+void ep_dispatch(EP_ARGS_DECL, Tensor x, Tensor ids, Tensor w) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16); CHECK_DT(ids, torch::kInt32);
+  CHECK_DT(w, torch::kFloat32); CHECK_CONTIG(ids); CHECK_CONTIG(w);
+  auto a = EP_ARGS;
+  TORCH_CHECK(x.size(1) == a.hidden, "hidden mismatch");
+  b200::ep_dispatch(a, x.data_ptr(), ids.data_ptr<int>(), w.data_ptr<float>(), (int)x.size(0), (int)ids.size(1),
+                    stream());
+}
+
+void ep_count(EP_ARGS_DECL, Tensor local_counts) {
+  CHECK_DT(local_counts, torch::kInt32);
+  b200::ep_count(EP_ARGS, local_counts.data_ptr<int>(), stream());
+}
+
+void ep_scatter(EP_ARGS_DECL, Tensor local_counts, Tensor cursor, Tensor x_perm, Tensor slot_code, Tensor slot_w,
+                Tensor offsets_out) {
+  CHECK_CONTIG(x_perm); CHECK_DT(slot_code, torch::kInt32); CHECK_DT(slot_w, torch::kFloat32);
+  auto a = EP_ARGS;
+  TORCH_CHECK(x_perm.size(0) >= (int64_t)a.world * a.cap, "x_perm must hold world * cap rows");
+  b200::ep_scatter(a, local_counts.data_ptr<int>(), cursor.data_ptr<int>(), (int)local_counts.numel(),
+                   x_perm.data_ptr(), slot_code.data_ptr<int>(), slot_w.data_ptr<float>(),
+                   offsets_out.data_ptr<int>(), a.world * a.cap, stream());
+}
+
+void ep_signal(EP_ARGS_DECL) { b200::ep_signal(EP_ARGS, stream()); }
+void ep_wait_done(EP_ARGS_DECL) { b200::ep_wait_done(EP_ARGS, stream()); }
 
 void embed(Tensor ids, Tensor table, Tensor out, Tensor status) {
   CHECK_CUDA(ids); CHECK_CUDA(table); CHECK_CUDA(out);
@@ -310,6 +423,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attn", &decode_attn);
   m.def("prefill_attn", &prefill_attn);
   m.def("argmax", &argmax);
+  m.def("gemm_peer_scatter", &gemm_peer_scatter);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_count", &ep_count);
+  m.def("ep_scatter", &ep_scatter);
+  m.def("ep_signal", &ep_signal);
+  m.def("ep_wait_done", &ep_wait_done);
   m.def("sample", &sample);
   m.def("penalties", &penalties);
   m.attr("EPI_BF16") = (int)b200::kEpiBf16;

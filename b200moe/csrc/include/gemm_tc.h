@@ -29,8 +29,12 @@ struct GemmArgs {
   int ld_out;                  // output row stride (elements)
   int out_group_stride;        // column offset per group for kEpiBf16/kEpiF32
   const int* slot_of_row;      // kEpiScatter
-  const float* slot_weight;    // kEpiScatter
+  const float* slot_weight;    // kEpiScatter: routing weight per output row (indexed by row)
   int* status;                 // device status word (0 = ok)
+  // kEpiScatter into peers' memory (expert parallel): slot code = rank * slot_cap + slot
+  int peer_scatter;
+  int slot_cap;
+  void* peer_out[8];
 };
 
 struct GemmLaunch {

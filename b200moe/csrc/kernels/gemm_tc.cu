@@ -62,7 +62,7 @@ struct GemmCfg {
   // bf16 ring fed by the dequantisers (fp8 mode only)
   static constexpr int CONV_SLOTS = AFP8 ? 2 : 0;
   static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
-  static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8;
+  static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
   static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   static constexpr int SMEM = STAGES * STAGE_BYTES + CONV_BYTES + EXTRA + 1024;
@@ -122,6 +122,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   int* row_off = tile_prefix + (kMaxGroups + 1);
   int* meta_slot = row_off + (kMaxGroups + 1);                 // [2][256] scatter slot per column
   float* meta_w = reinterpret_cast<float*>(meta_slot + 512);   // [2][256] routing weight per column
+  float* tile_sc = meta_w + 512;                               // [2 * 64] block scales of the current tile
 
   auto ALd = [&](int s, int a) { return stage_base + s * C::STAGE_BYTES + a * C::ALOAD_BYTES; };
   auto Bt = [&](int s) { return stage_base + s * C::STAGE_BYTES + C::NA * C::ALOAD_BYTES; };
@@ -269,9 +270,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       uint32_t phase = 0;
       int gi = 0;
       bool ok = true;
+      const int nkb = args.scale_k_blocks;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
-        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * args.scale_k_blocks;
+        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * nkb;
+        // the tile's block scales, fetched once: a global load per stage would put
+        // an L2 round trip on the critical path of every stage
+        for (int i = c; i < C::NA * nkb; i += kConvThreads) {
+          const int a = i / nkb, kb = i % nkb;
+          const int mb = tc.i + (a ? args.pair_row_offset / 128 : 0);
+          tile_sc[i] = __ldg(sc + mb * nkb + kb);
+        }
         for (int ks = 0; ks < k_stages; ++ks, ++gi) {
           const int cj = gi & 1;
           const uint32_t cph = (gi >> 1) & 1;
@@ -286,8 +295,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           const int kb = (ks * kBK) / 128;
 #pragma unroll
           for (int a = 0; a < C::NA; ++a) {
-            const int mb = tc.i + (a ? args.pair_row_offset / 128 : 0);
-            const float scale = __ldg(sc + mb * args.scale_k_blocks + kb);
+            const float scale = tile_sc[a * nkb + kb];
             const uint8_t* src = ALd(s, a);
             uint8_t* dst = A16(cj, a);
 #pragma unroll
@@ -345,7 +353,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         for (int col = et; col < ncols; col += 128) {
           const int slot = args.slot_of_row[row0 + col];
           mslot[col] = slot;
-          mw[col] = args.slot_weight[slot];
+          mw[col] = args.peer_scatter ? args.slot_weight[row0 + col] : args.slot_weight[slot];
         }
       }
       // one thread waits for the accumulator, the verdict is broadcast so the
@@ -388,8 +396,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 float* out = reinterpret_cast<float*>(args.out);
                 out[(size_t)row * args.ld_out + m_glob] = v[n];
               } else {  // kEpiScatter
-                __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-                out[(size_t)mslot[col] * args.ld_out + m_out] = __float2bfloat16(v[n] * mw[col]);
+                const int code = mslot[col];
+                __nv_bfloat16* out;
+                size_t r;
+                if (args.peer_scatter) {  // the row goes to its source rank's slots (peer memory)
+                  out = reinterpret_cast<__nv_bfloat16*>(args.peer_out[code / args.slot_cap]);
+                  r = (size_t)(code % args.slot_cap);
+                } else {
+                  out = reinterpret_cast<__nv_bfloat16*>(args.out);
+                  r = (size_t)code;
+                }
+                out[r * args.ld_out + m_out] = __float2bfloat16(v[n] * mw[col]);
               }
             }
           }

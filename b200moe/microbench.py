@@ -51,22 +51,43 @@ def flush_l2():
     _flush.fill_(1)
 
 
-def timeit(fn, iters=20, warmup=3, flush=True):
+def _graph(fn, reps):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(reps):
+            fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def _time_graph(g, iters):
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    g.replay()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(iters):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def timeit(fn, iters=20, warmup=3, flush=True, reps=10):
+    """Device time of one call: ``reps`` calls (each after an L2 flush) are
+    captured in a CUDA graph so host launch cost is excluded; the flush-only
+    graph's time is subtracted."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    tot = 0.0
-    for _ in range(iters):
-        if flush:
-            flush_l2()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        torch.cuda.synchronize()
-        tot += a.elapsed_time(b)
-    return tot / iters
+    if flush:
+        flush_l2()
+        work = _graph(lambda: (flush_l2(), fn()), reps)
+        base = _graph(flush_l2, reps)
+        return max(0.0, (_time_graph(work, iters) - _time_graph(base, iters)) / reps)
+    return _time_graph(_graph(fn, reps), iters) / reps
 
 
 def report(name, ms, bytes_=0, flops=0, **extra):
@@ -187,7 +208,7 @@ def case_step(T, ctx, iters, layers=48):
                      torch.arange(T + 1, dtype=torch.int32, device="cuda"), pos + 1, tables,
                      torch.arange(T, dtype=torch.int32, device="cuda"), T, 0, ctx + 1, T)
     fn = lambda: model.compute_logits(model(inp, pool))
-    ms = timeit(fn, iters, flush=False)
+    ms = timeit(fn, iters, flush=False, reps=1)
     wbytes = layers * (128 * 3 * 2048 * 768 + (5120 + 2048) * 2048 * 1.0) + 151936 * 2048 * 2
     kvbytes = T * (ctx + 1) * layers * 4 * 128 * 2 * 2
     report("decode_step", ms, wbytes + kvbytes, 0, rows=T, ctx=ctx, layers=layers)

@@ -310,8 +310,7 @@ class Qwen3MoeForCausalLM(nn.Module):
             ids, w = self.route(layer, x, counts[:E] if self.ep is None else None)
         if self.ep is not None:
             with self._range("moe.ep"):
-                self.ep.moe_fused(self, layer, x, ids, w, slots)
-            return slots
+                return self.ep.moe_fused(self, layer, x, ids, w, slots)
         rows = T * k
         with self._range("moe.permute"):
             x_perm = self._buf("x_perm", (rows, H), self.dtype)
