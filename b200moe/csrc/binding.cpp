@@ -32,7 +32,7 @@ T* ptr_or_null(const c10::optional<Tensor>& t) {
 void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor group_count,
           c10::optional<Tensor> group_offset, Tensor out, int64_t bn, int64_t epi, int64_t m_tiles,
           int64_t pair_row_offset, int64_t out_group_stride, c10::optional<Tensor> slot_of_row,
-          c10::optional<Tensor> slot_weight, Tensor status) {
+          c10::optional<Tensor> slot_weight, Tensor status, c10::optional<Tensor> trace) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(group_count); CHECK_CUDA(status);
   CHECK_CONTIG(weight); CHECK_CONTIG(group_count);
   TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
@@ -93,6 +93,11 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
   L.args.slot_of_row = ptr_or_null<int>(slot_of_row);
   L.args.slot_weight = ptr_or_null<float>(slot_weight);
   L.args.status = status.data_ptr<int>();
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->is_contiguous(), "trace must be int64");
+    L.args.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
+    L.args.trace_cap = (int)((trace->numel() - 1) / 2);
+  }
   L.a = weight.data_ptr();
   L.a_row_stride_bytes = K * weight.element_size();
   L.b = x.data_ptr();

@@ -35,6 +35,9 @@ struct GemmArgs {
   int peer_scatter;
   int slot_cap;
   void* peer_out[8];
+  // optional pipeline trace of CTA 0: pairs (role << 32 | index, %globaltimer); entry 0 = count
+  unsigned long long* trace;
+  int trace_cap;
 };
 
 struct GemmLaunch {

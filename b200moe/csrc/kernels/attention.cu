@@ -37,6 +37,7 @@ namespace b200 {
 
 using bf16 = __nv_bfloat16;
 constexpr int kKT = 64;  // keys per tile
+constexpr int kKVStages = 3;  // K/V tiles in flight (cp.async groups)
 
 // ------------------------------------------------------------- primitives
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -217,11 +218,11 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   const int64_t sbs = a.block_stride / a.head_dim;  // int8 scale pool block stride
 
   uint8_t* sQ = smem;                                   // [16][D]
-  uint8_t* sK = sQ + 16 * D * 2;                        // 2 x [64][D]
-  uint8_t* sV = sK + 2 * kKT * D * 2;                   // 2 x [64][D]
-  float* sM = reinterpret_cast<float*>(sV + 2 * kKT * D * 2);  // [4][16]
+  uint8_t* sK = sQ + 16 * D * 2;                        // kKVStages x [64][D]
+  uint8_t* sV = sK + kKVStages * kKT * D * 2;           // kKVStages x [64][D]
+  float* sM = reinterpret_cast<float*>(sV + kKVStages * kKT * D * 2);  // [4][16]
   float* sL = sM + 64;                                  // [4][16]
-  float* sO = sL + 64;                                  // [16][D]
+  float* sO = reinterpret_cast<float*>(sK);             // [16][D], reuses the K tiles after the loop
 
   const bf16* qsrc = static_cast<const bf16*>(a.q) + ((size_t)b * nq + (size_t)h * G) * D;
   for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += NT) {
@@ -233,10 +234,14 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   const int* btab = a.block_tables + (size_t)b * a.max_blocks;
   const uint32_t sk0 = smem_u32(sK), sv0 = smem_u32(sV);
   const int ntiles = k_end > k_begin ? (k_end - k_begin + kKT - 1) / kKT : 0;
-  if (ntiles > 0)
-    load_kv_tile<D, NT>(sk0, sv0, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab, a.block_size,
-                        a.block_stride, sbs, h, k_begin, k_end, sK, sV);
-  cp_async_commit();
+  constexpr int TB = kKT * D * 2;  // bytes of one K (or V) tile
+#pragma unroll
+  for (int p = 0; p < kKVStages - 1; ++p) {
+    if (p < ntiles)
+      load_kv_tile<D, NT>(sk0 + p * TB, sv0 + p * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
+                          a.block_size, a.block_stride, sbs, h, k_begin + p * kKT, k_end, sK + p * TB, sV + p * TB);
+    cp_async_commit();
+  }
   __syncthreads();
 
   uint32_t qf[D / 16][4];
@@ -257,17 +262,17 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
     for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
 
   for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) {
-      const int nb = buf ^ 1;
-      load_kv_tile<D, NT>(sk0 + nb * kKT * D * 2, sv0 + nb * kKT * D * 2, a.k_cache, a.v_cache, a.k_scale,
-                          a.v_scale, int8, btab, a.block_size, a.block_stride, sbs, h, k_begin + (t + 1) * kKT,
-                          k_end, sK + nb * kKT * D * 2, sV + nb * kKT * D * 2);
+    const int buf = t % kKVStages;
+    if (t + kKVStages - 1 < ntiles) {
+      const int nb = (t + kKVStages - 1) % kKVStages;
+      load_kv_tile<D, NT>(sk0 + nb * TB, sv0 + nb * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
+                          a.block_size, a.block_stride, sbs, h, k_begin + (t + kKVStages - 1) * kKT, k_end,
+                          sK + nb * TB, sV + nb * TB);
     }
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<kKVStages - 1>();
     __syncthreads();
-    const uint32_t sk = sk0 + buf * kKT * D * 2, sv = sv0 + buf * kKT * D * 2;
+    const uint32_t sk = sk0 + buf * TB, sv = sv0 + buf * TB;
     float s[2][4];
     qk_mma<D, 2>(s, qf, sk, warp * 16, lane);
     const int key0 = k_begin + t * kKT + warp * 16;
@@ -310,6 +315,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
     sL[warp * 16 + r0] = l_r[0];
     sL[warp * 16 + r0 + 8] = l_r[1];
   }
+  __syncthreads();  // every warp is done with the K/V tiles that sO reuses
   for (int i = threadIdx.x; i < 16 * D; i += NT) sO[i] = 0.f;
   __syncthreads();
   float wscale[2];
@@ -402,8 +408,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
   const int64_t sbs = a.block_stride / a.head_dim;
 
   uint8_t* sQ = smem;                     // [64][D]
-  uint8_t* sK = sQ + 64 * D * 2;          // 2 x [64][D]
-  uint8_t* sV = sK + 2 * kKT * D * 2;     // 2 x [64][D]
+  uint8_t* sK = sQ + 64 * D * 2;          // kKVStages x [64][D]
+  uint8_t* sV = sK + kKVStages * kKT * D * 2;
 
   const bf16* q = static_cast<const bf16*>(a.q);
   for (int idx = threadIdx.x; idx < 64 * (D / 8); idx += NT) {
@@ -418,9 +424,14 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
   const int k_end = min(kv_len, pos0 + last_q + 1);  // causal bound of the block's last query
   const int ntiles = (k_end + kKT - 1) / kKT;
   const uint32_t sk0 = smem_u32(sK), sv0 = smem_u32(sV);
-  load_kv_tile<D, NT>(sk0, sv0, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab, a.block_size,
-                      a.block_stride, sbs, h, 0, k_end, sK, sV);
-  cp_async_commit();
+  constexpr int TB = kKT * D * 2;
+#pragma unroll
+  for (int p = 0; p < kKVStages - 1; ++p) {
+    if (p < ntiles)
+      load_kv_tile<D, NT>(sk0 + p * TB, sv0 + p * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
+                          a.block_size, a.block_stride, sbs, h, p * kKT, k_end, sK + p * TB, sV + p * TB);
+    cp_async_commit();
+  }
   __syncthreads();
 
   uint32_t qf[D / 16][4];
@@ -446,17 +457,17 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
     for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
 
   for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) {
-      const int nb = buf ^ 1;
-      load_kv_tile<D, NT>(sk0 + nb * kKT * D * 2, sv0 + nb * kKT * D * 2, a.k_cache, a.v_cache, a.k_scale,
-                          a.v_scale, int8, btab, a.block_size, a.block_stride, sbs, h, (t + 1) * kKT, k_end,
-                          sK + nb * kKT * D * 2, sV + nb * kKT * D * 2);
+    const int buf = t % kKVStages;
+    if (t + kKVStages - 1 < ntiles) {
+      const int nb = (t + kKVStages - 1) % kKVStages;
+      load_kv_tile<D, NT>(sk0 + nb * TB, sv0 + nb * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
+                          a.block_size, a.block_stride, sbs, h, (t + kKVStages - 1) * kKT, k_end, sK + nb * TB,
+                          sV + nb * TB);
     }
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<kKVStages - 1>();
     __syncthreads();
-    const uint32_t sk = sk0 + buf * kKT * D * 2, sv = sv0 + buf * kKT * D * 2;
+    const uint32_t sk = sk0 + buf * TB, sv = sv0 + buf * TB;
     float s[8][4];
     qk_mma<D, 8>(s, qf, sk, 0, lane);
 #pragma unroll
@@ -515,9 +526,9 @@ static void check_launch(const char* what) {
 }
 
 template <int D>
-static int decode_smem() { return 16 * D * 2 + 4 * kKT * D * 2 + 2 * 64 * 4 + 16 * D * 4; }
+static int decode_smem() { return 16 * D * 2 + 2 * kKVStages * kKT * D * 2 + 2 * 64 * 4; }
 template <int D>
-static int prefill_smem() { return 64 * D * 2 + 4 * kKT * D * 2; }
+static int prefill_smem() { return 64 * D * 2 + 2 * kKVStages * kKT * D * 2; }
 
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
   if (B == 0) return;

@@ -60,7 +60,9 @@ struct GemmCfg {
   static constexpr int ALOAD_BYTES = AFP8 ? A8_BYTES : A16_BYTES;
   static constexpr int STAGE_BYTES = NA * ALOAD_BYTES + B_BYTES;
   // bf16 ring fed by the dequantisers (fp8 mode only)
-  static constexpr int CONV_SLOTS = AFP8 ? 2 : 0;
+  // enough bf16 slots that dequantisation runs ahead of MMA completion (the
+  // commit round trip, not the conversion itself, bounds a short ring)
+  static constexpr int CONV_SLOTS = AFP8 ? (PAIR ? 3 : 4) : 0;
   static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
   static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
   static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES) / STAGE_BYTES;
@@ -96,6 +98,17 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, 
   return c;
 }
 
+// Pipeline trace (debug/profiling): role 0 TMA issued, 1 dequant start, 2 dequant
+// done, 3 MMA issue, 4 accumulator ready (epilogue start), 5 epilogue done.
+__device__ __forceinline__ void trace_ev(const GemmArgs& a, int role, int idx) {
+  if (a.trace == nullptr || blockIdx.x != 0) return;
+  const unsigned long long n = atomicAdd(a.trace, 1ull);
+  if ((int)n < a.trace_cap) {
+    a.trace[1 + 2 * n] = ((unsigned long long)role << 32) | (unsigned)idx;
+    a.trace[2 + 2 * n] = globaltimer_ns();
+  }
+}
+
 template <int BN, bool PAIR, bool AFP8, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -110,9 +123,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   uint8_t* extra = conv_base + C::CONV_BYTES;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);   // [12] TMA landed
   uint64_t* empty_bar = full_bar + 12;                       // [12] load slot free
-  uint64_t* cfull_bar = empty_bar + 12;                      // [2] bf16 slot written
-  uint64_t* cempty_bar = cfull_bar + 2;                      // [2] bf16 slot consumed
-  uint64_t* accf_bar = cempty_bar + 2;
+  uint64_t* cfull_bar = empty_bar + 12;                      // [4] bf16 slot written
+  uint64_t* cempty_bar = cfull_bar + 4;                      // [4] bf16 slot consumed
+  uint64_t* accf_bar = cempty_bar + 4;
   uint64_t* acce_bar = accf_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -165,7 +178,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], AFP8 ? 2 : 1);  // fp8: dequantisers (A) + MMA (B)
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < 4; ++j) {
       mbar_init(&cfull_bar[j], 1);
       mbar_init(&cempty_bar[j], 1);
     }
@@ -198,6 +211,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     if (elect_one()) {
       int s = 0;
       uint32_t phase = 0;
+      int pi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
@@ -210,6 +224,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], x, a_row);
           if constexpr (PAIR) tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
           tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
+          trace_ev(args, 0, pi++);
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
       }
@@ -237,12 +252,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         const uint32_t d_base = tmem_base + abuf * C::ACC_COLS;
         for (int ks = 0; ks < k_stages; ++ks, ++gi) {
           if (!mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) { ok = false; break; }
-          const int cj = gi & 1;
-          const uint32_t cph = (gi >> 1) & 1;
+          const int cj = AFP8 ? gi % C::CONV_SLOTS : 0;
+          const uint32_t cph = AFP8 ? (gi / C::CONV_SLOTS) & 1 : 0;
           if constexpr (AFP8) {
             if (!mbar_wait(&cfull_bar[cj], cph, status, kStatusTimeoutConv, abort_flag)) { ok = false; break; }
           }
           tc_fence_after();
+          trace_ev(args, 3, gi);
           const uint32_t b_addr = smem_u32(Bt(s));
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
@@ -282,13 +298,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           tile_sc[i] = __ldg(sc + mb * nkb + kb);
         }
         for (int ks = 0; ks < k_stages; ++ks, ++gi) {
-          const int cj = gi & 1;
-          const uint32_t cph = (gi >> 1) & 1;
+          const int cj = gi % C::CONV_SLOTS;
+          const uint32_t cph = (gi / C::CONV_SLOTS) & 1;
           // one thread waits, the verdict is broadcast so all 256 leave together
           if (c == 0) {
             bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) &&
                         mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
             *conv_ok = w_ok ? 1 : 0;
+            trace_ev(args, 1, gi);
           }
           named_barrier_sync(1, kConvThreads);
           if (!*conv_ok) { ok = false; break; }
@@ -327,6 +344,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           if (c == 0) {
             mbar_arrive(&empty_bar[s]);   // the e4m3 tile of this load slot is consumed
             mbar_arrive(&cfull_bar[cj]);  // the bf16 tile is ready for the MMA
+            trace_ev(args, 2, gi);
           }
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
@@ -358,7 +376,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       }
       // one thread waits for the accumulator, the verdict is broadcast so the
       // four warps always leave (or continue) together
-      if (et == 0) epi_ok[0] = mbar_wait(&accf_bar[abuf], aphase, status, kStatusTimeoutAccFull, abort_flag) ? 1 : 0;
+      if (et == 0) {
+        epi_ok[0] = mbar_wait(&accf_bar[abuf], aphase, status, kStatusTimeoutAccFull, abort_flag) ? 1 : 0;
+        trace_ev(args, 4, lt);
+      }
       named_barrier_sync(2, 128);
       if (!epi_ok[0]) { ok = false; break; }
       tc_fence_after();
@@ -415,6 +436,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[abuf]);
+      if (et == 0) trace_ev(args, 5, lt);
     }
   }
 

@@ -214,9 +214,73 @@ def case_step(T, ctx, iters, layers=48):
     report("decode_step", ms, wbytes + kvbytes, 0, rows=T, ctx=ctx, layers=layers)
 
 
+def _trace_summary(name, buf):
+    import statistics
+    n = min(int(buf[0]), (buf.numel() - 1) // 2)
+    ev = buf[1:1 + 2 * n].view(n, 2).tolist()
+    by = {}
+    for key, t in ev:
+        by.setdefault(key >> 32, {})[key & 0xFFFFFFFF] = t
+    med = lambda xs: round(statistics.median(xs) / 1e3, 3) if xs else None
+    issue, c0, c1, mma = (by.get(r, {}) for r in (0, 1, 2, 3))
+    idx = sorted(set(issue) & set(c0) & set(c1) & set(mma)) or sorted(set(issue) & set(mma))
+    d = {"kernel": name, "stages_traced": len(idx)}
+    if len(idx) > 2:
+        d["us_between_tma_issues"] = med([issue[b] - issue[a] for a, b in zip(idx, idx[1:])])
+        d["us_between_mma_issues"] = med([mma[b] - mma[a] for a, b in zip(idx, idx[1:])])
+        if c0:
+            d["us_issue_to_dequant_start"] = med([c0[i] - issue[i] for i in idx])
+            d["us_dequant"] = med([c1[i] - c0[i] for i in idx])
+            d["us_dequant_done_to_mma"] = med([mma[i] - c1[i] for i in idx])
+        else:
+            d["us_issue_to_mma"] = med([mma[i] - issue[i] for i in idx])
+    e0, e1 = by.get(4, {}), by.get(5, {})
+    tiles = sorted(set(e0) & set(e1))
+    if tiles:
+        d["tiles"] = len(tiles)
+        d["us_epilogue"] = med([e1[i] - e0[i] for i in tiles])
+    print(json.dumps(d), flush=True)
+
+
+def case_trace(T):
+    """Per-stage timeline of CTA 0 for the decode-size GEMMs."""
+    buf = torch.zeros(1 + 2 * 16384, dtype=torch.int64, device="cuda")
+    H, I, E, k = 2048, 768, 128, 8
+    x = (torch.randn(T, 4096, device="cuda") * 0.5).to(torch.bfloat16)
+    q, s = fp8_weight(1, H, 4096, 4)
+    for name, fn in (("o_proj", lambda: ops.linear(x, q[0], s[0])),):
+        fn()
+        torch.cuda.synchronize()
+        buf.zero_()
+        ops.set_gemm_trace(buf)
+        flush_l2()
+        fn()
+        torch.cuda.synchronize()
+        ops.set_gemm_trace(None)
+        _trace_summary(name, buf.cpu())
+    q13, s13 = fp8_weight(E, 2 * I, H, 1)
+    rows = T * k
+    ids = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]).flatten()
+    counts = torch.bincount(ids, minlength=E).to(torch.int32)
+    offsets = torch.zeros(E + 1, dtype=torch.int32, device="cuda")
+    offsets[1:] = torch.cumsum(counts, 0)
+    xm = (torch.randn(rows, H, device="cuda") * 0.5).to(torch.bfloat16)
+    h = torch.empty(rows, I, dtype=torch.bfloat16, device="cuda")
+    fn = lambda: ops.grouped_gate_up_silu(xm, q13, s13, counts, offsets, h, I)
+    fn()
+    torch.cuda.synchronize()
+    buf.zero_()
+    ops.set_gemm_trace(buf)
+    flush_l2()
+    fn()
+    torch.cuda.synchronize()
+    ops.set_gemm_trace(None)
+    _trace_summary("moe_gate_up", buf.cpu())
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "all"])
+    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "all"])
     p.add_argument("--tokens", type=int, default=256)
     p.add_argument("--ctx", type=int, default=1152)
     p.add_argument("--iters", type=int, default=20)
@@ -231,6 +295,8 @@ def main():
         case_decode(a.tokens, a.ctx, a.iters)
     if a.case in ("prefill", "all"):
         case_prefill(max(a.tokens, a.ctx), a.ctx, a.iters)
+    if a.case == "trace":
+        case_trace(a.tokens)
     if a.case == "step":
         case_step(a.tokens, a.ctx, a.iters, a.layers)
     ops.check_status("cuda")

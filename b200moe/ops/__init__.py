@@ -50,6 +50,13 @@ def native_available() -> bool:
     return _C is not None
 
 
+_trace = [None]  # optional int64 buffer: GEMM pipeline trace of CTA 0 (profiling only)
+
+
+def set_gemm_trace(buf: torch.Tensor | None):
+    _trace[0] = buf
+
+
 _status_cache: dict = {}
 _count_cache: dict = {}
 
@@ -132,7 +139,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
     m_tiles = N // 128
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
     C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, pick_bn(T, m_tiles), epi, m_tiles,
-           0, 0, None, None, status_word(x.device))
+           0, 0, None, None, status_word(x.device), _trace[0])
     count_launches()
     return out
 
@@ -144,7 +151,7 @@ def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn:
     m_tiles = inter // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w13.shape[0], pair=True)
     C.gemm(w13, s13, x_perm, counts, offsets, out, bn, EPI_SILU_PAIR, m_tiles, inter, 0, None, None,
-           status_word(x_perm.device))
+           status_word(x_perm.device), _trace[0])
     count_launches()
     return out
 
@@ -157,7 +164,7 @@ def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weig
     m_tiles = w2.shape[1] // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w2.shape[0])
     C.gemm(w2, s2, h_perm, counts, offsets, slots_out, bn, EPI_SCATTER, m_tiles, 0, 0, slot_of_row, slot_weight,
-           status_word(h_perm.device))
+           status_word(h_perm.device), _trace[0])
     count_launches()
     return slots_out
 

@@ -58,22 +58,31 @@ def workload(args):
     return [[rng.randrange(vocab) for _ in range(args.input_len)] for _ in range(args.num_requests)]
 
 
-def reference_arm(args):
-    print(json.dumps({"impl": "reference", "unavailable":
-                      "reference arm not wired yet: needs an on-disk 30B fp8 checkpoint + tokenizer for its loader"}))
-    return 0
+METRIC = "output tok/s (Qwen3-30B-A3B FP8, EP8, 256 concurrent) + p50 TTFT/TPOT"
+
+
+def reference_arm(args, store=None):
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    import reference_arm as ref
+    rc = ref.run(args, workload(args), METRIC)
+    if store is not None:
+        store.set("driver_done", "1")
+    return rc
 
 
 def main():
     args = parse()
-    if args.impl == "reference":
-        return reference_arm(args)
     rank = int(os.environ.get("RANK", "0"))
-    if args.gpus > 1 and rank != 0:
-        # torchrun-launched non-driver ranks: the engine on rank 0 spawns its own
-        # per-GPU workers; these processes only wait for the driver to finish.
-        from b200moe.parallel.launch import wait_for_driver
-        return wait_for_driver()
+    store = None
+    if args.gpus > 1 and "MASTER_ADDR" in os.environ:
+        from b200moe.parallel.launch import driver_store, wait_for_driver
+        if rank != 0:
+            # torchrun-launched non-driver ranks: the engine on rank 0 spawns its own
+            # per-GPU workers; these processes only wait for the driver to finish.
+            return wait_for_driver()
+        store = driver_store()
+    if args.impl == "reference":
+        return reference_arm(args, store)
     import torch
     from b200moe import LLM, SamplingParams, ops
     from b200moe.utils.gpu_clock import ClockSampler
@@ -112,7 +121,7 @@ def main():
     value = total_out / (dev_ms / 1e3)
     e2e = total_out / wall
     line = {
-        "metric": "output tok/s (Qwen3-30B-A3B FP8, EP8, 256 concurrent) + p50 TTFT/TPOT",
+        "metric": METRIC,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 2), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None if BASELINE_TOKS is None else round(value / BASELINE_TOKS, 3),
@@ -135,6 +144,8 @@ def main():
         line["p50_tpot_s"] = round(tpot[len(tpot) // 2], 5)
     print(json.dumps(line), flush=True)
     llm.exit()
+    if store is not None:
+        store.set("driver_done", "1")
     return 0
 
 
