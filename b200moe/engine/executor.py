@@ -191,10 +191,36 @@ class Executor:
                     p.grammar_mask = np.stack([m for _, m in g]).astype(np.int32)
         return plans
 
+    def check_alive(self):
+        for r, p in enumerate(self.procs, start=1):
+            if not p.is_alive():
+                raise RankFailure(f"rank {r} exited with code {p.exitcode}")
+
     def launch(self, batch, grammar_masks: dict | None = None):
         plans = self.plans(batch, grammar_masks)
+        self.check_alive()
         self._send_all("run", [(p,) for p in plans])
-        self.runner.launch(plans[0])
+        try:
+            self.runner.launch(plans[0])
+        except RankFailure:
+            raise
+        except Exception as exc:
+            # a collective that failed because a peer vanished or raised: report it
+            for r, (p, c) in enumerate(zip(self.procs, self.conns), start=1):
+                if not p.is_alive():
+                    raise RankFailure(f"rank {r} exited with code {p.exitcode}") from exc
+                try:
+                    if c.poll(0):
+                        status, payload = c.recv()
+                        if status == "error":
+                            raise RankFailure(f"rank {r} raised:\n{payload}") from exc
+                except (EOFError, OSError):
+                    raise RankFailure(f"rank {r} is gone") from exc
+            if self.world > 1:
+                # a collective timed out on a peer that neither exited nor reported
+                # an error (hung): the rank group is out of step, fail the step
+                raise RankFailure(f"collective failed with {self.world} ranks: {exc}") from exc
+            raise
         self._inflight = (plans, len(batch.sequences))
 
     def collect(self):

@@ -168,7 +168,7 @@ class ModelRunner:
             raise RuntimeError("step plan larger than the staging buffer")
         dev[:n].copy_(self._pinned[i][:n], non_blocking=True)
         views = {k: dev[o:o + s] for k, (o, s) in offs.items()}
-        views["block_tables"] = views["block_tables"].view(plan.num_rows, -1)
+        views["block_tables"] = views["block_tables"].view(plan.num_rows, plan.block_tables.shape[1])
         return views
 
     def _inputs(self, plan: StepPlan, v: dict, max_seq_len: int | None = None) -> StepInputs:

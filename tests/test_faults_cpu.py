@@ -1,0 +1,111 @@
+"""Failure detection on the host (no GPU is ever faulted): a worker rank that
+dies or stops answering is detected within the bound and surfaces as
+RankFailure; an engine step exception fails every in-flight request and the
+server keeps serving; the exit watchdog bounds a wedged teardown."""
+import asyncio
+import os
+import signal
+import subprocess
+import sys
+import textwrap
+import time
+
+import pytest
+
+from b200moe import LLM, SamplingParams
+from b200moe.async_engine import AsyncLLMEngine
+from b200moe.engine.executor import RankFailure
+
+KW = dict(device="cpu", kvcache_block_size=16, num_kvcache_blocks=64, max_num_batched_tokens=256,
+          max_num_seqs=8, max_model_len=256, enforce_eager=True)
+SP = SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True)
+
+
+def test_dead_worker_detected():
+    llm = LLM("tiny-moe", tensor_parallel_size=2, rank_timeout_s=20, **KW)
+    try:
+        assert llm.generate([[1, 2, 3]], SP, use_tqdm=False)[0]["token_ids"]
+        proc = llm.executor.procs[0]
+        os.kill(proc.pid, signal.SIGKILL)
+        proc.join(5)
+        t0 = time.monotonic()
+        with pytest.raises(RankFailure):
+            llm.generate([[4, 5, 6]], SP, use_tqdm=False)
+        assert time.monotonic() - t0 < 20
+    finally:
+        llm.exit()
+
+
+def test_hung_worker_times_out():
+    llm = LLM("tiny-moe", tensor_parallel_size=2, rank_timeout_s=3, **KW)
+    try:
+        proc = llm.executor.procs[0]
+        os.kill(proc.pid, signal.SIGSTOP)  # alive but never answers
+        t0 = time.monotonic()
+        with pytest.raises(RankFailure):
+            llm.generate([[4, 5, 6]], SP, use_tqdm=False)
+        assert time.monotonic() - t0 < 15
+        os.kill(proc.pid, signal.SIGKILL)
+    finally:
+        llm.exit()
+
+
+def test_step_exception_fails_requests_and_engine_keeps_serving():
+    eng = AsyncLLMEngine("tiny-moe", **KW)
+    try:
+        real_step = eng.engine.step
+        calls = {"n": 0}
+
+        def flaky():
+            calls["n"] += 1
+            if calls["n"] == 1:
+                raise RuntimeError("injected step failure")
+            return real_step()
+
+        eng.engine.step = flaky
+
+        async def one():
+            h = await eng.add_request([1, 2, 3, 4], SP)
+            toks, err = [], None
+            while True:
+                ev = await eng.next_event(h)
+                if ev.error:
+                    err = ev.error
+                    break
+                if ev.token_id is not None:
+                    toks.append(ev.token_id)
+                if ev.finished:
+                    break
+            return toks, err
+
+        _, err = asyncio.run(one())
+        assert err and "injected step failure" in err
+        toks, err = asyncio.run(one())  # the engine thread survived
+        assert err is None and len(toks) == 4
+        assert eng.metrics()["requests_errors"] >= 1
+    finally:
+        asyncio.run(eng.close())
+
+
+def test_exit_watchdog_bounds_wedged_teardown(tmp_path):
+    """A teardown that never returns is killed by the watchdog (runs in a child)."""
+    code = textwrap.dedent("""
+        import os, sys, time
+        sys.path.insert(0, %r)
+        os.environ["B200MOE_EXIT_TIMEOUT_S"] = "2"
+        from b200moe.engine.llm_engine import LLMEngine
+        eng = LLMEngine.__new__(LLMEngine)
+        eng._exited = False
+        class Wedged:
+            procs = []
+            def exit(self):
+                time.sleep(3600)
+        eng.executor = Wedged()
+        eng.exit()
+        print("unreachable")
+    """ % os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    t0 = time.monotonic()
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60)
+    assert time.monotonic() - t0 < 30
+    assert "unreachable" not in r.stdout
+    assert "watchdog" in r.stderr
