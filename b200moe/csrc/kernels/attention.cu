@@ -573,3 +573,106 @@ void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t
 }
 
 }  // namespace b200
+
+// ====================================================== no-allocation entry
+// Split-KV decode attention whose partial results live in a file-scope device
+// array instead of a caller-provided workspace; the contract (limits, set-up,
+// races) is in include/noalloc.h.  It launches the same kernels as
+// paged_decode_attn and allocates no device memory.
+#include <cstdio>
+#include <mutex>
+#include "noalloc.h"
+
+namespace {
+
+constexpr int kNoAllocRows = B200MOE_NOALLOC_MAX_ROWS;
+constexpr int kNoAllocMaxD = 128;
+// [rows][128] part_o, then [rows] part_m, then [rows] part_l.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocRows * (kNoAllocMaxD + 2)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_fail(char* err, int err_len, int code, const char* msg) {
+  if (err != nullptr && err_len > 0) std::snprintf(err, (size_t)err_len, "%s", msg);
+  return code;
+}
+
+// Address of this device's scratch array, resolved once per device (with it current).
+int noalloc_scratch(float** out, char* err, int err_len) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return noalloc_fail(err, err_len, 3, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      char msg[256];
+      std::snprintf(msg, sizeof(msg), "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+      return noalloc_fail(err, err_len, 3, msg);
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int b200moe_decode_attn_noalloc_max_rows(void) { return kNoAllocRows; }
+
+extern "C" int b200moe_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                           const float* k_scale, const float* v_scale, int kv_int8,
+                                           const int* block_tables, const int* seq_lens, int batch,
+                                           int max_blocks, int block_size, long long block_stride,
+                                           int num_q_heads, int num_kv_heads, int head_dim, float scale,
+                                           int num_splits, int split_len, void* out, void* stream, char* err,
+                                           int err_len) {
+  if (batch < 0 || num_splits < 1 || num_kv_heads < 1 || num_q_heads % num_kv_heads != 0 || block_size < 1)
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: bad batch / splits / head counts / block_size");
+  if (head_dim != 64 && head_dim != kNoAllocMaxD)
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: head_dim must be 64 or 128");
+  const long long rows = (long long)batch * num_q_heads * num_splits;
+  if (num_splits > 1 && rows > kNoAllocRows) {
+    char msg[256];
+    std::snprintf(msg, sizeof(msg),
+                  "decode_attn_noalloc: batch*q_heads*num_splits = %lld exceeds the scratch limit of %d rows",
+                  rows, kNoAllocRows);
+    return noalloc_fail(err, err_len, 2, msg);
+  }
+  float* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch, err, err_len);
+  if (rc != 0) return rc;
+  b200::DecodeArgs a{};
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.kv_int8 = kv_int8;
+  a.block_tables = block_tables;
+  a.seq_lens = seq_lens;
+  a.max_blocks = max_blocks;
+  a.block_size = block_size;
+  a.block_stride = block_stride;
+  a.num_kv_heads = num_kv_heads;
+  a.group = num_q_heads / num_kv_heads;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.num_splits = num_splits;
+  a.split_len = split_len;
+  a.part_o = scratch;
+  a.part_m = scratch + (size_t)kNoAllocRows * kNoAllocMaxD;
+  a.part_l = a.part_m + kNoAllocRows;
+  a.out = out;
+  try {
+    b200::paged_decode_attn(a, batch, static_cast<cudaStream_t>(stream));
+  } catch (const std::exception& ex) {
+    const bool launch = std::string(ex.what()).find("paged_decode_attn:") == 0;
+    return noalloc_fail(err, err_len, launch ? 3 : 1, ex.what());
+  }
+  return 0;
+}
