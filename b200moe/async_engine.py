@@ -77,9 +77,17 @@ class AsyncLLMEngine:
         self.commands.put(("cancel", (seq_id,), None))
 
     async def close(self):
+        """Stop the engine thread and release the engine; later calls return at once."""
+        if not self.thread.is_alive():
+            return
         ack: Queue = Queue(maxsize=1)
         self.commands.put(("close", (), ack))
-        await asyncio.to_thread(ack.get)
+        while self.thread.is_alive():  # the thread may exit without answering (closed elsewhere)
+            try:
+                await asyncio.to_thread(ack.get, True, 0.5)
+                break
+            except Empty:
+                continue
         await asyncio.to_thread(self.thread.join)
 
     def metrics(self) -> dict:

@@ -32,7 +32,8 @@ T* ptr_or_null(const c10::optional<Tensor>& t) {
 void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor group_count,
           c10::optional<Tensor> group_offset, Tensor out, int64_t bn, int64_t epi, int64_t m_tiles,
           int64_t pair_row_offset, int64_t out_group_stride, c10::optional<Tensor> slot_of_row,
-          c10::optional<Tensor> slot_weight, Tensor status, c10::optional<Tensor> trace) {
+          c10::optional<Tensor> slot_weight, Tensor status, c10::optional<Tensor> trace, int64_t k_splits,
+          int64_t split_stride) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(group_count); CHECK_CUDA(status);
   CHECK_CONTIG(weight); CHECK_CONTIG(group_count);
   TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
@@ -72,6 +73,12 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
     CHECK_DT(out, torch::kBFloat16);
   }
   TORCH_CHECK(m_tiles * 128 <= rows_per_group, "m_tiles exceeds weight rows");
+  TORCH_CHECK(k_splits >= 1 && k_splits <= K / 64, "k_splits must be in [1, K/64]");
+  if (k_splits > 1) {
+    TORCH_CHECK(epi == b200::kEpiF32 && groups == 1, "split-K: single group, fp32 partials only");
+    TORCH_CHECK(out.is_contiguous() && out.numel() >= k_splits * split_stride &&
+                split_stride >= x.size(0) * out.stride(0), "split-K partial buffer too small");
+  }
   if (pair) TORCH_CHECK(pair_row_offset + m_tiles * 128 <= rows_per_group, "pair rows out of range");
   if (x.size(0) == 0) return;
 
@@ -93,6 +100,8 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
   L.args.slot_of_row = ptr_or_null<int>(slot_of_row);
   L.args.slot_weight = ptr_or_null<float>(slot_weight);
   L.args.status = status.data_ptr<int>();
+  L.args.k_splits = (int)k_splits;
+  L.args.split_stride = split_stride;
   if (trace.has_value()) {
     TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->is_contiguous(), "trace must be int64");
     L.args.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
@@ -303,6 +312,16 @@ void router_topk(Tensor logits, int64_t num_experts, int64_t topk, bool renorm, 
                     stream());
 }
 
+void splitk_reduce(Tensor part, int64_t splits, Tensor out) {
+  CHECK_CUDA(part); CHECK_CONTIG(part); CHECK_DT(part, torch::kFloat32);
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out must be [T, N] with unit inner stride");
+  const int64_t T = out.size(0), N = out.size(1);
+  TORCH_CHECK(part.numel() >= splits * T * N, "partials too small");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kFloat32, "out bf16 or fp32");
+  b200::splitk_reduce(part.data_ptr<float>(), (int)splits, (int)T, (int)N, out.data_ptr(), (int)out.stride(0),
+                      out.scalar_type() == torch::kBFloat16, stream());
+}
+
 void moe_permute(Tensor x, Tensor ids, Tensor counts, Tensor cursor, Tensor x_perm, Tensor slot_of_row,
                  c10::optional<Tensor> offsets_out) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_CONTIG(x_perm); CHECK_DT(ids, torch::kInt32); CHECK_CONTIG(ids);
@@ -425,6 +444,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qknorm_rope_kvstore", &qknorm_rope_kvstore);
   m.def("router_topk", &router_topk);
   m.def("moe_permute", &moe_permute);
+  m.def("splitk_reduce", &splitk_reduce);
   m.def("decode_attn", &decode_attn);
   m.def("prefill_attn", &prefill_attn);
   m.def("argmax", &argmax);

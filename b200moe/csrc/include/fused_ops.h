@@ -39,6 +39,10 @@ void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const 
 void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s);
 void router_topk(const float* logits, int ld, int T, int E, int topk, bool renorm, int* ids, float* weights,
                  int* counts, cudaStream_t s);
+// out[t, n] = sum_s part[s, t, n] (fp32 partials of a split-K GEMM, rows of N
+// floats, split stride T*N) stored as bf16 (out_bf16) or fp32 with row stride ld_out.
+void splitk_reduce(const float* part, int splits, int T, int N, void* out, int ld_out, bool out_bf16,
+                   cudaStream_t s);
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
                  void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s);
 

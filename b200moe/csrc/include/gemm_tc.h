@@ -28,6 +28,11 @@ struct GemmArgs {
   void* out;
   int ld_out;                  // output row stride (elements)
   int out_group_stride;        // column offset per group for kEpiBf16/kEpiF32
+  // split-K (kEpiF32 only): work item (tile, split) sums K stages
+  // [split * ceil(k_stages / k_splits), ...) and stores its fp32 partial at
+  // out + split * split_stride; the caller reduces the partials
+  int k_splits;
+  long long split_stride;
   const int* slot_of_row;      // kEpiScatter
   const float* slot_weight;    // kEpiScatter: routing weight per output row (indexed by row)
   int* status;                 // device status word (0 = ok)

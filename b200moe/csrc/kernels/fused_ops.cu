@@ -340,6 +340,42 @@ static void check_launch(const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Split-K reduction: 4 consecutive outputs per thread (float4 loads of each
+// partial; the partials of a decode-size GEMM sit in L2).
+template <bool BF16>
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int T, int N, void* out,
+                                     int ld_out) {
+  const int n4 = N / 4;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)T * n4) return;
+  const int t = (int)(idx / n4), c = (int)(idx % n4) * 4;
+  const size_t stride = (size_t)T * N;
+  const float* p = part + (size_t)t * N + c;
+  float4 acc = *reinterpret_cast<const float4*>(p);
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = *reinterpret_cast<const float4*>(p + s * stride);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if constexpr (BF16) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    *reinterpret_cast<uint2*>(static_cast<bf16*>(out) + (size_t)t * ld_out + c) = packed;
+  } else {
+    *reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * ld_out + c) = acc;
+  }
+}
+
+void splitk_reduce(const float* part, int splits, int T, int N, void* out, int ld_out, bool out_bf16,
+                   cudaStream_t s) {
+  if (T == 0) return;
+  if (N % 4 || ld_out % 4) throw std::runtime_error("splitk_reduce: N and ld_out must be multiples of 4");
+  const int64_t work = (int64_t)T * (N / 4);
+  const int blocks = (int)((work + 255) / 256);
+  if (out_bf16) splitk_reduce_kernel<true><<<blocks, 256, 0, s>>>(part, splits, T, N, out, ld_out);
+  else splitk_reduce_kernel<false><<<blocks, 256, 0, s>>>(part, splits, T, N, out, ld_out);
+  check_launch("splitk_reduce");
+}
+
 void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,
                   cudaStream_t s) {
   if (T == 0) return;

@@ -7,17 +7,21 @@
 // plain bf16 weight.  X (the "B" operand, N = tokens) is bf16.  One CTA per SM
 // runs a persistent loop over (group, n-tile, m-tile) work items computed on
 // the device from per-group token counts, so the launch needs no host sync and
-// is CUDA-graph safe.  Roles (448 threads):
+// is CUDA-graph safe.  Roles (fp8: 704 threads, bf16: 192):
 //
 //   warp 0      TMA producer: fp8 (or bf16) weight tile + bf16 activation tile
 //               per stage into a deep ring that holds only the loaded bytes
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-9   dequantisers: e4m3 * scale -> bf16 into a separate, double-
-//               buffered ring in the 128B-swizzled UMMA layout (exactly
-//               bf16(float(q) * scale), the reference's load-time dequant, done
-//               per tile in shared memory).  Keeping the bf16 copies out of the
-//               load ring is what lets ~8 loads per SM stay in flight.
-//   warps 10-13 epilogue: tcgen05.ld of the double-buffered TMEM accumulator,
+//   warps 2-17  (fp8 only) 16 independent dequantiser warps: e4m3 * scale ->
+//               bf16 into a separate ring in the 128B-swizzled UMMA layout
+//               (exactly bf16(float(q) * scale), the reference's load-time
+//               dequant, done per tile in shared memory).  Each warp converts
+//               one 16-byte chunk per lane of every weight tile and arrives on
+//               the stage barriers itself: no CTA-level barrier on the path,
+//               and 4 warps per scheduler hide the conversion latency.
+//               Keeping the bf16 copies out of the load ring is what lets
+//               several loads per SM stay in flight.
+//   last 4      epilogue: tcgen05.ld of the double-buffered TMEM accumulator,
 //               fused op, global store; per-tile row metadata (scatter slots and
 //               routing weights) is staged in shared memory once per tile
 //
@@ -43,9 +47,6 @@
 
 namespace b200 {
 
-constexpr int kThreads = 448;
-constexpr int kConvThreads = 256;   // warps 2..9
-constexpr int kEpiWarp0 = 10;       // warps 10..13
 constexpr int kMaxGroups = 512;
 constexpr int kBK = 64;            // K elements per pipeline stage (128 B of bf16)
 constexpr int kSmemBudget = 225 * 1024;
@@ -53,6 +54,9 @@ constexpr int kSmemBudget = 225 * 1024;
 template <int BN, bool PAIR, bool AFP8>
 struct GemmCfg {
   static constexpr int NA = PAIR ? 2 : 1;
+  static constexpr int CONV_WARPS = AFP8 ? 16 : 0;    // one 16-byte chunk per lane of a 128x64 e4m3 tile
+  static constexpr int EPI_WARP0 = 2 + CONV_WARPS;
+  static constexpr int THREADS = (EPI_WARP0 + 4) * 32;
   static constexpr int A16_BYTES = 128 * kBK * 2;     // 16 KB bf16 tile
   static constexpr int A8_BYTES = 128 * kBK;          // 8 KB e4m3 tile
   static constexpr int B_BYTES = BN * kBK * 2;
@@ -79,12 +83,16 @@ struct GemmCfg {
 };
 
 struct TileCoord {
-  int g, j, i;
+  int g, j, i;   // group, token tile, weight tile
+  int ks0, ks1;  // K stages [ks0, ks1) of this work item (split-K)
+  int sp;        // split index
 };
 
-// tile_prefix[g] = first tile of group g (exclusive prefix, ngroups+1 entries);
-// the owner of tile t is the last g with tile_prefix[g] <= t.
-__device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, int ngroups, int m_tiles) {
+// tile_prefix[g] = first work item of group g (exclusive prefix, ngroups+1
+// entries); the owner of item t is the last g with tile_prefix[g] <= t.  Items
+// of a group are ordered (token tile, weight tile, split).
+__device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, int ngroups, int m_tiles,
+                                                 int k_stages, int k_splits) {
   int lo = 0, hi = ngroups;
   while (hi - lo > 1) {
     int mid = (lo + hi) >> 1;
@@ -93,8 +101,13 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, 
   int local = t - tile_prefix[lo];
   TileCoord c;
   c.g = lo;
+  c.sp = local % k_splits;
+  local /= k_splits;
   c.j = local / m_tiles;
   c.i = local % m_tiles;
+  const int per = (k_stages + k_splits - 1) / k_splits;
+  c.ks0 = c.sp * per;
+  c.ks1 = min(k_stages, c.ks0 + per);
   return c;
 }
 
@@ -109,8 +122,44 @@ __device__ __forceinline__ void trace_ev(const GemmArgs& a, int role, int idx) {
   }
 }
 
+// Two fp32 products in one instruction (sm_100 packed f32x2 multiply, IEEE
+// round-to-nearest per lane, denormals kept).
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// 16 e4m3 -> 16 bf16 = bf16(float(q) * scale): e4m3 -> f16 and f16 -> f32 are
+// exact, the fp32 product is rounded once, then rounded to bf16 (the
+// reference's load-time dequantisation, bit for bit).
+__device__ __forceinline__ void dequant16(const uint4 q, float sc, uint32_t (&o)[8]) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  const float2 s2 = make_float2(sc, sc);
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] & 0xFFFFu), __NV_E4M3);
+    __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] >> 16), __NV_E4M3);
+    const float2 flo = fmul2(__half22float2(*reinterpret_cast<__half2*>(&lo)), s2);
+    const float2 fhi = fmul2(__half22float2(*reinterpret_cast<__half2*>(&hi)), s2);
+    o[2 * h] = pack_bf16x2(flo.x, flo.y);
+    o[2 * h + 1] = pack_bf16x2(fhi.x, fhi.y);
+  }
+}
+
 template <int BN, bool PAIR, bool AFP8, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, PAIR, AFP8>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                const GemmArgs args) {
   using C = GemmCfg<BN, PAIR, AFP8>;
@@ -129,13 +178,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   uint64_t* acce_bar = accf_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* conv_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);
   int* tile_prefix = reinterpret_cast<int*>(extra + 4096);
   int* row_off = tile_prefix + (kMaxGroups + 1);
   int* meta_slot = row_off + (kMaxGroups + 1);                 // [2][256] scatter slot per column
   float* meta_w = reinterpret_cast<float*>(meta_slot + 512);   // [2][256] routing weight per column
-  float* tile_sc = meta_w + 512;                               // [2 * 64] block scales of the current tile
 
   auto ALd = [&](int s, int a) { return stage_base + s * C::STAGE_BYTES + a * C::ALOAD_BYTES; };
   auto Bt = [&](int s) { return stage_base + s * C::STAGE_BYTES + C::NA * C::ALOAD_BYTES; };
@@ -145,6 +192,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   const int lane = threadIdx.x & 31;
   const int ngroups = args.num_groups;
   const int m_tiles = args.m_tiles;
+  const int k_splits = args.k_splits > 0 ? args.k_splits : 1;
 
   // ---- per-CTA schedule: prefix sums of tiles and rows over groups (one warp)
   if (warp == 0) {
@@ -153,7 +201,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     int tiles = 0, rows = 0;
     for (int g = g0; g < g1; ++g) {
       int c = args.group_count[g];
-      tiles += (c + BN - 1) / BN * m_tiles;
+      tiles += (c + BN - 1) / BN * m_tiles * k_splits;
       rows += c;
     }
     int tincl = tiles, rincl = rows;
@@ -168,7 +216,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       int c = args.group_count[g];
       tile_prefix[g] = tpre;
       row_off[g] = args.group_offset ? args.group_offset[g] : rpre;
-      tpre += (c + BN - 1) / BN * m_tiles;
+      tpre += (c + BN - 1) / BN * m_tiles * k_splits;
       rpre += c;
     }
     if (lane == 31) tile_prefix[ngroups] = tincl;
@@ -176,10 +224,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   if (threadIdx.x == 32) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], AFP8 ? 2 : 1);  // fp8: dequantisers (A) + MMA (B)
+      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS + 1 : 1);  // fp8: every dequant warp + the MMA
     }
     for (int j = 0; j < 4; ++j) {
-      mbar_init(&cfull_bar[j], 1);
+      mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS : 1);
       mbar_init(&cempty_bar[j], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -204,6 +252,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = tile_prefix[ngroups];
   const int k_stages = args.k_stages;
+  auto tile_of = [&](int t) { return decode_tile(t, tile_prefix, ngroups, m_tiles, k_stages, k_splits); };
   int* status = args.status;
 
   if (warp == 0) {
@@ -214,10 +263,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       int pi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
+        TileCoord tc = tile_of(t);
         const int a_row = tc.g * args.a_rows_per_group + tc.i * 128;
         const int b_row = row_off[tc.g] + tc.j * BN;
-        for (int ks = 0; ks < k_stages; ++ks) {
+        for (int ks = tc.ks0; ks < tc.ks1; ++ks) {
           if (!mbar_wait(&empty_bar[s], phase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[s], C::TX_BYTES);
           const int x = ks * kBK;
@@ -245,12 +294,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       int gi = 0;  // global stage counter (bf16 ring index)
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
+        const TileCoord tc = tile_of(t);
         const int abuf = lt & 1;
         const uint32_t aphase = (lt >> 1) & 1;
         if (!mbar_wait(&acce_bar[abuf], aphase ^ 1, status, kStatusTimeoutAccEmpty, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_base = tmem_base + abuf * C::ACC_COLS;
-        for (int ks = 0; ks < k_stages; ++ks, ++gi) {
+        for (int ks = tc.ks0; ks < tc.ks1; ++ks, ++gi) {
           if (!mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) { ok = false; break; }
           const int cj = AFP8 ? gi % C::CONV_SLOTS : 0;
           const uint32_t cph = AFP8 ? (gi / C::CONV_SLOTS) & 1 : 0;
@@ -267,7 +317,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             for (int a = 0; a < C::NA; ++a) {
               const uint8_t* abuf_ptr = AFP8 ? A16(cj, a) : ALd(s, a);
               const uint64_t adesc = umma_sdesc_sw128(smem_u32(abuf_ptr) + k * 32);
-              umma_f16_ss(d_base + a * BN, adesc, bdesc, idesc, (ks | k) != 0 ? 1u : 0u);
+              umma_f16_ss(d_base + a * BN, adesc, bdesc, idesc, (ks != tc.ks0 || k != 0) ? 1u : 0u);
             }
           }
           umma_commit(&empty_bar[s]);
@@ -278,87 +328,83 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         umma_commit(&accf_bar[abuf]);
       }
     }
-  } else if (warp >= 2 && warp < kEpiWarp0) {
+  } else if (warp >= 2 && warp < C::EPI_WARP0) {
     // ================================================= dequantisers
     if constexpr (AFP8) {
-      const int c = threadIdx.x - 64;  // 0..255
-      int s = 0;
-      uint32_t phase = 0;
-      int gi = 0;
-      bool ok = true;
+      const int chunk = (warp - 2) * 32 + lane;  // this lane's 16-byte chunk of every 128x64 tile
+      const int row = chunk >> 2, c16 = chunk & 3;
+      const int src_off = row * 64 + c16 * 16;
+      // 128B-swizzled K-major row: 16-byte unit u of row r lives at u ^ (r & 7)
+      const int dst0 = row * 128 + (((2 * c16) ^ (row & 7)) << 4);
+      const int dst1 = row * 128 + (((2 * c16 + 1) ^ (row & 7)) << 4);
+      const bool tracer = warp == 2 && lane == 0;
       const int nkb = args.scale_k_blocks;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
-        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * nkb;
-        // the tile's block scales, fetched once: a global load per stage would put
-        // an L2 round trip on the critical path of every stage
-        for (int i = c; i < C::NA * nkb; i += kConvThreads) {
-          const int a = i / nkb, kb = i % nkb;
-          const int mb = tc.i + (a ? args.pair_row_offset / 128 : 0);
-          tile_sc[i] = __ldg(sc + mb * nkb + kb);
+      const int pair_mb = C::NA > 1 ? args.pair_row_offset / 128 : 0;
+      // (tile, stage) cursor; the block scales of the NEXT stage are loaded while
+      // the current one converts, so no L2 round trip follows a barrier wait
+      int t = blockIdx.x, ks = 0, ks1 = 0;
+      TileCoord tc{};
+      auto advance = [&]() -> bool {  // moves the cursor to the next stage of this CTA
+        if (++ks < ks1) return true;
+        if (ks1 != 0) t += gridDim.x;
+        if (t >= total_tiles) return false;
+        tc = tile_of(t);
+        ks = tc.ks0;
+        ks1 = tc.ks1;
+        return true;
+      };
+      auto load_scales = [&](float (&out)[C::NA]) {
+        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * nkb + (ks * kBK) / 128;
+        out[0] = __ldg(sc + tc.i * nkb);
+        if constexpr (C::NA > 1) out[1] = __ldg(sc + (tc.i + pair_mb) * nkb);
+      };
+      ks = -1;  // so the first advance() lands on the first stage of the first tile
+      bool have = advance();
+      float next_scale[C::NA];
+      if (have) load_scales(next_scale);
+      for (int gi = 0; have; ++gi) {
+        const int s = gi % C::STAGES;
+        const uint32_t phase = (gi / C::STAGES) & 1;
+        const int cj = gi % C::CONV_SLOTS;
+        const uint32_t cph = (gi / C::CONV_SLOTS) & 1;
+        float scale[C::NA];
+#pragma unroll
+        for (int a = 0; a < C::NA; ++a) scale[a] = next_scale[a];
+        have = advance();
+        if (have) load_scales(next_scale);
+        const bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) &&
+                          mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) break;
+        if (tracer) trace_ev(args, 1, gi);
+        uint4 q[C::NA];
+#pragma unroll
+        for (int a = 0; a < C::NA; ++a) q[a] = *reinterpret_cast<const uint4*>(ALd(s, a) + src_off);
+#pragma unroll
+        for (int a = 0; a < C::NA; ++a) {
+          uint32_t o[8];
+          dequant16(q[a], scale[a], o);
+          uint8_t* dst = A16(cj, a);
+          *reinterpret_cast<uint4*>(dst + dst0) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(dst + dst1) = make_uint4(o[4], o[5], o[6], o[7]);
         }
-        for (int ks = 0; ks < k_stages; ++ks, ++gi) {
-          const int cj = gi % C::CONV_SLOTS;
-          const uint32_t cph = (gi / C::CONV_SLOTS) & 1;
-          // one thread waits, the verdict is broadcast so all 256 leave together
-          if (c == 0) {
-            bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) &&
-                        mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
-            *conv_ok = w_ok ? 1 : 0;
-            trace_ev(args, 1, gi);
-          }
-          named_barrier_sync(1, kConvThreads);
-          if (!*conv_ok) { ok = false; break; }
-          const int kb = (ks * kBK) / 128;
-#pragma unroll
-          for (int a = 0; a < C::NA; ++a) {
-            const float scale = tile_sc[a * nkb + kb];
-            const uint8_t* src = ALd(s, a);
-            uint8_t* dst = A16(cj, a);
-#pragma unroll
-            for (int it = 0; it < 2; ++it) {
-              const int chunk = c + kConvThreads * it;
-              const int row = chunk >> 2, c16 = chunk & 3;
-              const uint4 q = *reinterpret_cast<const uint4*>(src + row * 64 + c16 * 16);
-              const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-              uint32_t o[8];
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] & 0xFFFFu), __NV_E4M3);
-                __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] >> 16), __NV_E4M3);
-                float2 flo = __half22float2(*reinterpret_cast<__half2*>(&lo));
-                float2 fhi = __half22float2(*reinterpret_cast<__half2*>(&hi));
-                __nv_bfloat162 blo = __floats2bfloat162_rn(flo.x * scale, flo.y * scale);
-                __nv_bfloat162 bhi = __floats2bfloat162_rn(fhi.x * scale, fhi.y * scale);
-                o[2 * h] = *reinterpret_cast<uint32_t*>(&blo);
-                o[2 * h + 1] = *reinterpret_cast<uint32_t*>(&bhi);
-              }
-              const int sw = row & 7;
-              const int p0 = (2 * c16) ^ sw, p1 = (2 * c16 + 1) ^ sw;
-              *reinterpret_cast<uint4*>(dst + row * 128 + p0 * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-              *reinterpret_cast<uint4*>(dst + row * 128 + p1 * 16) = make_uint4(o[4], o[5], o[6], o[7]);
-            }
-          }
-          fence_proxy_async_smem();
-          named_barrier_sync(1, kConvThreads);
-          if (c == 0) {
-            mbar_arrive(&empty_bar[s]);   // the e4m3 tile of this load slot is consumed
-            mbar_arrive(&cfull_bar[cj]);  // the bf16 tile is ready for the MMA
-            trace_ev(args, 2, gi);
-          }
-          if (++s == C::STAGES) { s = 0; phase ^= 1; }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty_bar[s]);   // this warp is done with the e4m3 tile
+          mbar_arrive(&cfull_bar[cj]);  // and its slice of the bf16 tile is written
         }
+        if (tracer) trace_ev(args, 2, gi);
       }
     }
   } else {
     // ====================================================== epilogue
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     const int m_local = q * 32 + lane;
-    const int et = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    const int et = threadIdx.x - C::EPI_WARP0 * 32;  // 0..127
     int lt = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
-      TileCoord tc = decode_tile(t, tile_prefix, ngroups, m_tiles);
+      TileCoord tc = tile_of(t);
       const int abuf = lt & 1;
       const uint32_t aphase = (lt >> 1) & 1;
       const int count = args.group_count[tc.g];
@@ -414,7 +460,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
                 out[(size_t)row * args.ld_out + m_glob] = __float2bfloat16(v[n]);
               } else if constexpr (EPI == kEpiF32) {
-                float* out = reinterpret_cast<float*>(args.out);
+                float* out = reinterpret_cast<float*>(args.out) + (size_t)tc.sp * args.split_stride;
                 out[(size_t)row * args.ld_out + m_glob] = v[n];
               } else {  // kEpiScatter
                 const int code = mslot[col];
@@ -504,9 +550,9 @@ static void launch_impl(const GemmLaunch& L, cudaStream_t stream) {
                                 L.K, L.a_row_stride_bytes, kBK, 128, !AFP8);
   CUtensorMap tb = make_tmap_2d(L.b, true, L.b_rows, L.K, L.b_row_stride_bytes, kBK, BN, true);
   // upper bound of work items without reading device counts
-  int64_t max_tiles = ((int64_t)L.b_rows / BN + L.args.num_groups) * L.args.m_tiles;
+  int64_t max_tiles = ((int64_t)L.b_rows / BN + L.args.num_groups) * L.args.m_tiles * std::max(1, L.args.k_splits);
   int grid = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, max_tiles));
-  kern<<<grid, kThreads, C::SMEM, stream>>>(ta, tb, L.args);
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(ta, tb, L.args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_tc launch: ") + cudaGetErrorString(e));
 }
@@ -534,6 +580,11 @@ void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
     throw std::runtime_error("operands must be 16-byte aligned");
   if (L.b_row_stride_bytes % 16 != 0) throw std::runtime_error("activation row stride must be a multiple of 16 bytes");
   const int bn = L.bn;
+  if (L.args.k_splits > 1) {
+    if (L.epi != kEpiF32 || L.pair) throw std::runtime_error("split-K needs the fp32 epilogue");
+    const int per = (L.args.k_stages + L.args.k_splits - 1) / L.args.k_splits;
+    if ((L.args.k_splits - 1) * per >= L.args.k_stages) throw std::runtime_error("split-K leaves a split empty");
+  }
   if (L.pair) {
     if (!L.a_fp8 || L.epi != kEpiSiluPair) throw std::runtime_error("pair mode is fp8 + silu only");
     dispatch_bn<true, true, kEpiSiluPair>(bn, L, stream);
@@ -541,6 +592,7 @@ void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
   }
   if (L.a_fp8) {
     if (L.epi == kEpiBf16) dispatch_bn<false, true, kEpiBf16>(bn, L, stream);
+    else if (L.epi == kEpiF32) dispatch_bn<false, true, kEpiF32>(bn, L, stream);
     else if (L.epi == kEpiScatter) dispatch_bn<false, true, kEpiScatter>(bn, L, stream);
     else throw std::runtime_error("unsupported fp8 epilogue");
   } else {

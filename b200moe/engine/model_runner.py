@@ -83,6 +83,7 @@ class ModelRunner:
         self.model = Qwen3MoeForCausalLM(args, self.device, ep_rank=rank, ep_size=self.world_size,
                                          expert_ids=expert_ids)
         self.model.moe_backend = "loop" if config.moe_backend == "loop" else "fused"
+        self.model.attention_backend = config.attention_backend
         if self.world_size > 1:
             from b200moe.parallel.ep import ExpertParallel
             self.model.ep = ExpertParallel(self, config.moe_backend)
@@ -115,9 +116,74 @@ class ModelRunner:
         self.h2d_bytes = 0
         self._step_events: list = []
         self._graph_kernels: dict[int, int] = {}
-        graph_ok = self.model.ep is None or self.model.ep.graph_safe
-        if self.device.type == "cuda" and not config.enforce_eager and graph_ok:
+        if self._graphs_allowed():
             self.capture_cudagraphs()
+
+    def _graphs_allowed(self) -> bool:
+        """Decode graphs need the native paths: the per-expert loop and the
+        PyTorch attention read counts back to the host."""
+        ep_ok = self.model.ep is None or self.model.ep.graph_safe
+        return (self.device.type == "cuda" and not self.config.enforce_eager and ep_ok
+                and self.model.moe_backend == "fused" and self.model.attention_backend == "paged")
+
+    def _set_backend(self, attr: str, value: str):
+        if getattr(self.model, attr) == value:
+            return
+        setattr(self.model, attr, value)
+        self.graphs.clear()
+        self._graph_kernels.clear()
+        self.graph_pool = None
+        if self._graphs_allowed():
+            self.capture_cudagraphs()
+
+    def set_moe_backend(self, backend: str):
+        """Switch between the native grouped path ("fused") and the per-expert
+        PyTorch loop ("loop", the A/B and equivalence baseline) between steps."""
+        if backend not in ("fused", "loop"):
+            raise ValueError("runtime MoE backend must be 'fused' or 'loop'")
+        if backend == "loop" and self.model.ep is not None:
+            raise ValueError("the per-expert loop runs on one rank only")
+        self._set_backend("moe_backend", backend)
+
+    def set_cuda_graphs(self, enabled: bool):
+        """Turn decode CUDA graphs on or off between steps (graph A/B runs)."""
+        self.config.enforce_eager = not enabled
+        self.graphs.clear()
+        self._graph_kernels.clear()
+        self.graph_pool = None
+        if self._graphs_allowed():
+            self.capture_cudagraphs()
+
+    def memory_reserved(self) -> int:
+        return torch.cuda.memory_reserved(self.device) if self.device.type == "cuda" else 0
+
+    @torch.inference_mode()
+    def score_tokens(self, token_ids: list[int]) -> torch.Tensor:
+        """Teacher-forced logits [L, V] (fp32, host) at every position of one
+        sequence, prefilled from scratch.  It writes KV blocks 0..ceil(L/bs)-1,
+        so call it only while no request holds KV, and clear the prefix cache
+        afterwards (those blocks may back cached prefixes)."""
+        L = len(token_ids)
+        nb = -(-L // self.block_size)
+        if L == 0 or L > self.max_tokens or nb > self.max_blocks:
+            raise ValueError("sequence longer than max_num_batched_tokens / max_model_len")
+        ids = np.asarray(token_ids, np.int32)
+        pos = np.arange(L, dtype=np.int32)
+        tables = np.zeros((1, self.max_blocks), np.int32)
+        tables[0, :nb] = np.arange(nb, dtype=np.int32)
+        plan = StepPlan(ids, pos, pos.copy(), np.array([0, L], np.int32), np.array([L], np.int32), tables, 0, L, L,
+                        np.zeros(1, np.int32), np.zeros(1, np.float32))
+        inp = self._inputs(plan, self._upload(plan))
+        inp.logits_indices = torch.arange(L, dtype=torch.int32, device=self.device)
+        h = self.model(inp, self.kv)
+        return self.model.compute_logits(h).float().cpu()
+
+    def set_attention_backend(self, backend: str):
+        """"paged" (native kernels) or "sdpa" (per-sequence PyTorch attention
+        over the same paged pool, fp32 math)."""
+        if backend not in ("paged", "sdpa"):
+            raise ValueError("attention backend must be 'paged' or 'sdpa'")
+        self._set_backend("attention_backend", backend)
 
     # ------------------------------------------------------------- setup
     def _init_dist(self):

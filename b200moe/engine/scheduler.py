@@ -354,6 +354,11 @@ class Scheduler:
             seq.dp_rank = -1
         self.waiting.appendleft(seq)
 
+    def clear_prefix_cache(self):
+        """Drop every cached (unreferenced) prefix block on every rank."""
+        for bm in self.block_managers:
+            bm.clear_prefix_cache()
+
     def metrics(self) -> dict:
         m = dict(self.block_managers[0].metrics())
         for bm in self.block_managers[1:]:

@@ -125,6 +125,7 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.scale = args.head_dim ** -0.5
         self.ep = None          # expert-parallel communicator (multi-rank)
         self.moe_backend = "fused"
+        self.attention_backend = "paged"  # or "sdpa": per-sequence PyTorch attention (A/B, equivalence gate)
         self.profiler = None
         self._ws: dict = {}
 
@@ -210,19 +211,27 @@ class Qwen3MoeForCausalLM(nn.Module):
         out = self._buf("attn", (T, nq, D), self.dtype) if cuda else torch.empty(T, nq, D, dtype=q.dtype)
         nd = inp.num_decode
         with self._range("attn.core"):
-            if nd:
-                split_len, nsplit = self.decode_splits(nd, inp.max_seq_len)
-                ws = None
-                if cuda:
-                    ws = (self._buf("part_o", (nd * nq * nsplit, D), torch.float32),
-                          self._buf("part_m", (nd * nq * nsplit,), torch.float32),
-                          self._buf("part_l", (nd * nq * nsplit,), torch.float32))
-                ops.decode_attention(q[:nd], kvl, inp.block_tables[:nd], inp.seq_lens[:nd], self.scale,
-                                     out[:nd], split_len, nsplit, ws)
-            if inp.num_rows > nd:
-                cu = inp.prefill_cu if inp.prefill_cu is not None else inp.cu_seqlens_q
-                ops.prefill_attention(q[nd:], kvl, cu, inp.seq_lens[nd:], inp.block_tables[nd:],
-                                      inp.max_q_len, self.scale, out[nd:])
+            cu = inp.prefill_cu if inp.prefill_cu is not None else inp.cu_seqlens_q
+            if cuda and self.attention_backend == "sdpa":
+                if nd:
+                    ops._attention_ref(q[:nd], kvl, inp.block_tables[:nd], inp.seq_lens[:nd],
+                                       torch.arange(nd + 1, dtype=torch.int32), self.scale, out[:nd])
+                if inp.num_rows > nd:
+                    ops._attention_ref(q[nd:], kvl, inp.block_tables[nd:], inp.seq_lens[nd:], cu, self.scale,
+                                       out[nd:])
+            else:
+                if nd:
+                    split_len, nsplit = self.decode_splits(nd, inp.max_seq_len)
+                    ws = None
+                    if cuda:
+                        ws = (self._buf("part_o", (nd * nq * nsplit, D), torch.float32),
+                              self._buf("part_m", (nd * nq * nsplit,), torch.float32),
+                              self._buf("part_l", (nd * nq * nsplit,), torch.float32))
+                    ops.decode_attention(q[:nd], kvl, inp.block_tables[:nd], inp.seq_lens[:nd], self.scale,
+                                         out[:nd], split_len, nsplit, ws)
+                if inp.num_rows > nd:
+                    ops.prefill_attention(q[nd:], kvl, cu, inp.seq_lens[nd:], inp.block_tables[nd:],
+                                          inp.max_q_len, self.scale, out[nd:])
         with self._range("attn.o_proj"):
             return ops.linear(out.view(T, nq * D), layer.o_weight, layer.o_scale,
                               out=self._buf("o", (T, a.hidden_size), self.dtype) if cuda else None)

@@ -121,6 +121,43 @@ def pick_bn(rows: int, m_tiles: int, groups: int = 1, pair: bool = False, sms: i
     return best
 
 
+def _dense_cost_us(rows: int, m_tiles: int, k_stages: int, bn: int, splits: int, sms: int, fp8: bool) -> float:
+    """Rough time model of the persistent GEMM: waves of work items, each a
+    run of K stages costing the slower of weight-tile preparation (fp8
+    dequantisation or the bf16 tile load) and the MMA, plus its epilogue, plus
+    the partial-sum traffic of split-K.  Constants are B200 measurements of
+    this kernel, rounded."""
+    n_tiles = math.ceil(rows / bn)
+    items = m_tiles * n_tiles * splits
+    waves = math.ceil(items / sms)
+    per = math.ceil(k_stages / splits)
+    stage = max(0.15 if fp8 else 0.08, 0.0011 * bn) + 0.02
+    t = waves * (per * stage + 0.3 + 0.004 * bn) + 1.0
+    if splits > 1:
+        t += 2.0 + splits * rows * m_tiles * 128 * 4 * 2 / 5e6
+    return t
+
+
+def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: bool = True) -> tuple[int, int]:
+    """(token tile, K splits) of a single-group GEMM, the cheapest under
+    ``_dense_cost_us``.  Decode-size token counts give too few output tiles to
+    fill the grid (o_proj at 256 tokens is 16 weight tiles): a larger token
+    tile dequantises each weight tile fewer times, and splitting K spreads the
+    stages over the SMs; the fp32 partials are summed by a small kernel."""
+    best, best_t = (pick_bn(rows, m_tiles, sms=sms), 1), float("inf")
+    for bn in (16, 32, 64, 128, 256):
+        if bn > 16 and bn >= 2 * rows:
+            break
+        for splits in range(1, max(1, k_stages // 2) + 1):
+            per = math.ceil(k_stages / splits)
+            if math.ceil(k_stages / per) != splits:
+                continue  # would leave a split empty
+            t = _dense_cost_us(rows, m_tiles, k_stages, bn, splits, sms, fp8)
+            if t < best_t:
+                best, best_t = (bn, splits), t
+    return best
+
+
 # --------------------------------------------------------------------- GEMM
 def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, out_dtype=torch.bfloat16,
            out: torch.Tensor | None = None) -> torch.Tensor:
@@ -137,9 +174,17 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
     if T == 0:
         return out
     m_tiles = N // 128
+    bn, splits = plan_dense(T, m_tiles, x.shape[1] // 64, fp8=scale is not None)
+    if splits > 1:
+        part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
+        C.gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, m_tiles,
+               0, 0, None, None, status_word(x.device), _trace[0], splits, T * N)
+        C.splitk_reduce(part, splits, out)
+        count_launches(2)
+        return out
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
-    C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, pick_bn(T, m_tiles), epi, m_tiles,
-           0, 0, None, None, status_word(x.device), _trace[0])
+    C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, bn, epi, m_tiles,
+           0, 0, None, None, status_word(x.device), _trace[0], 1, 0)
     count_launches()
     return out
 
@@ -151,7 +196,7 @@ def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn:
     m_tiles = inter // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w13.shape[0], pair=True)
     C.gemm(w13, s13, x_perm, counts, offsets, out, bn, EPI_SILU_PAIR, m_tiles, inter, 0, None, None,
-           status_word(x_perm.device), _trace[0])
+           status_word(x_perm.device), _trace[0], 1, 0)
     count_launches()
     return out
 
@@ -164,7 +209,7 @@ def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weig
     m_tiles = w2.shape[1] // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w2.shape[0])
     C.gemm(w2, s2, h_perm, counts, offsets, slots_out, bn, EPI_SCATTER, m_tiles, 0, 0, slot_of_row, slot_weight,
-           status_word(h_perm.device), _trace[0])
+           status_word(h_perm.device), _trace[0], 1, 0)
     count_launches()
     return slots_out
 

@@ -40,6 +40,44 @@ def test_gemm_fp8_dense(T, n, k):
     _close(out, x.float() @ _ref_w(q[0], s[0]).t())
 
 
+@pytest.mark.parametrize("T", [1, 64, 256])
+def test_gemm_fp8_split_k(T):
+    """o_proj shape at decode token counts: the planner splits K; partials are summed."""
+    n, k = 2048, 4096
+    bn, splits = ops.plan_dense(T, n // 128, k // 64)
+    assert splits > 1
+    q, s = _fp8_weight(1, n, k, 5)
+    x = (torch.randn(T, k, device=DEV) * 0.5).to(torch.bfloat16)
+    out = ops.linear(x, q[0], s[0])
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    _close(out, x.float() @ _ref_w(q[0], s[0]).t())
+
+
+def test_fp8_dequant_bit_exact():
+    """One-hot activations read the dequantised weight back: it must equal
+    bf16(float(q) * scale) bit for bit (up to the sign of zero), for every
+    e4m3 code (subnormals included) and for tiny, ordinary and >= 256 block scales."""
+    n = k = 256
+    g = torch.Generator().manual_seed(7)
+    codes = torch.randint(0, 256, (n, k), generator=g, dtype=torch.int32)
+    codes = torch.where((codes & 0x7F) == 0x7F, codes - 1, codes)  # no NaN codes
+    q = codes.to(torch.uint8).view(torch.float8_e4m3fn).to(DEV)
+    s = torch.tensor([[3.1e-5, 0.0123], [300.0, 1.7]], dtype=torch.float32, device=DEV)
+    x = torch.eye(k, dtype=torch.bfloat16, device=DEV)
+    out = ops.linear(x, q, s)  # out[t, m] = W[m, t]
+    torch.cuda.synchronize()
+    sfull = s.repeat_interleave(128, 0).repeat_interleave(128, 1)
+    want = (q.float() * sfull).to(torch.bfloat16)
+    got = out.t().contiguous()
+    # bit-exact except the sign of zero (e4m3 -0 may come out as +0, identical in any product or sum)
+    diff = (got.view(torch.int16) != want.view(torch.int16)) & ~((got == 0) & (want == 0))
+    bad = diff.nonzero().tolist()
+    detail = [(m, t, int(codes[m, t]), float(sfull[m, t]), float(got[m, t]), float(want[m, t]))
+              for m, t in bad[:8]]
+    assert not bad, f"{len(bad)} mismatches (m, k, code, scale, got, want): {detail}"
+
+
 @pytest.mark.parametrize("T", [3, 200])
 def test_gemm_bf16_f32_out(T):
     w = (torch.randn(256, 2048, device=DEV) * 0.02).to(torch.bfloat16)
