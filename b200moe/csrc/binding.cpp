@@ -5,6 +5,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstring>
+#include <tuple>
 #include <vector>
 
 #include "attention.h"
@@ -312,6 +314,68 @@ void router_topk(Tensor logits, int64_t num_experts, int64_t topk, bool renorm, 
                     stream());
 }
 
+// ---------------------------------------------------------------- CUDA IPC
+// Expert-parallel peer buffers: one cudaMalloc per buffer, shared with the
+// other ranks through cudaIpcGetMemHandle and mapped on the caller's device
+// with cudaIpcOpenMemHandle (peer access enabled lazily).  These are plain
+// NVLink peer mappings: no multicast object is created, and nothing but this
+// extension's own ld/st kernels ever reads them.
+#define IPC_CHECK(x)                                                                    \
+  do {                                                                                  \
+    cudaError_t e_ = (x);                                                               \
+    TORCH_CHECK(e_ == cudaSuccess, #x " failed: ", cudaGetErrorString(e_));              \
+  } while (0)
+
+std::tuple<int64_t, Tensor> ipc_alloc(int64_t nbytes, int64_t device) {
+  TORCH_CHECK(nbytes > 0, "ipc_alloc: size must be positive");
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  IPC_CHECK(cudaMalloc(&p, (size_t)nbytes));
+  IPC_CHECK(cudaMemset(p, 0, (size_t)nbytes));
+  cudaIpcMemHandle_t h;
+  IPC_CHECK(cudaIpcGetMemHandle(&h, p));
+  Tensor ht = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  std::memcpy(ht.data_ptr(), &h, sizeof(h));
+  return {reinterpret_cast<int64_t>(p), ht};
+}
+
+int64_t ipc_open(Tensor handle, int64_t device) {
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t) && handle.scalar_type() == torch::kUInt8,
+              "ipc_open: expected a 64-byte handle");
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.contiguous().data_ptr(), sizeof(h));
+  void* p = nullptr;
+  IPC_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  IPC_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
+}
+
+void ipc_free(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  IPC_CHECK(cudaFree(reinterpret_cast<void*>(ptr)));
+}
+
+// A tensor view of device memory this module owns (no deleter: ipc_free releases it).
+Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, c10::ScalarType dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, (c10::DeviceIndex)device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), shape, opts);
+}
+
+void kv_blocks_copy(Tensor src_pool, Tensor src_ids, int64_t dst_ptr, Tensor dst_ids, int64_t block_bytes) {
+  CHECK_CUDA(src_pool); CHECK_CONTIG(src_pool);
+  CHECK_DT(src_ids, torch::kInt32); CHECK_DT(dst_ids, torch::kInt32); CHECK_CONTIG(src_ids); CHECK_CONTIG(dst_ids);
+  TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "kv_blocks_copy: id lists differ in length");
+  TORCH_CHECK(src_pool.numel() * src_pool.element_size() % block_bytes == 0, "kv_blocks_copy: pool / block size");
+  c10::cuda::CUDAGuard guard(src_pool.device());
+  b200::kv_blocks_copy(src_pool.data_ptr(), src_ids.data_ptr<int>(), reinterpret_cast<void*>(dst_ptr),
+                       dst_ids.data_ptr<int>(), (int)src_ids.numel(), block_bytes, stream());
+}
+
 void splitk_reduce(Tensor part, int64_t splits, Tensor out) {
   CHECK_CUDA(part); CHECK_CONTIG(part); CHECK_DT(part, torch::kFloat32);
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out must be [T, N] with unit inner stride");
@@ -445,6 +509,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &router_topk);
   m.def("moe_permute", &moe_permute);
   m.def("splitk_reduce", &splitk_reduce);
+  m.def("kv_blocks_copy", &kv_blocks_copy);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("ipc_free", &ipc_free);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("decode_attn", &decode_attn);
   m.def("prefill_attn", &prefill_attn);
   m.def("argmax", &argmax);

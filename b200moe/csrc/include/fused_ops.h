@@ -43,6 +43,10 @@ void router_topk(const float* logits, int ld, int T, int E, int topk, bool renor
 // floats, split stride T*N) stored as bf16 (out_bf16) or fp32 with row stride ld_out.
 void splitk_reduce(const float* part, int splits, int T, int N, void* out, int ld_out, bool out_bf16,
                    cudaStream_t s);
+// Whole KV-block copy: dst_base + dst_ids[i] * block_bytes <- src_base + src_ids[i] * block_bytes
+// (16-byte plain loads / stores; dst may be a peer GPU's pool mapped over NVLink).
+void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, const int* dst_ids, int n,
+                    int64_t block_bytes, cudaStream_t s);
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
                  void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s);
 

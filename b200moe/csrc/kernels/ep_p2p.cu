@@ -26,7 +26,8 @@
 //
 // Epochs live in device memory (incremented by ep_dispatch), so a replayed CUDA
 // graph keeps advancing them.  All waits are bounded (%globaltimer); on expiry
-// the kernel records a status code and returns.  No TMA multicast is used.
+// the kernel records a status code and returns.  Peer memory is accessed with
+// plain ld/st only (no TMA).
 //
 // Reference: the replicated-hidden all_reduce combine of
 // nanovllm/models/qwen3_moe.py:414-418 (one NCCL all-reduce per layer).
@@ -93,6 +94,7 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
       reinterpret_cast<int4*>(a.recv_meta[dest])[row] = m;
     }
   }
+  __threadfence_system();  // every thread orders its own peer stores before the block's arrival
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();

@@ -365,6 +365,28 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
   }
 }
 
+// KV handoff: grid (blocks, chunks); each CTA streams a contiguous part of one
+// block slab.  Used for prefill -> decode transfers into a peer's pool.
+__global__ void kv_blocks_copy_kernel(const uint4* __restrict__ src, const int* __restrict__ src_ids,
+                                      uint4* __restrict__ dst, const int* __restrict__ dst_ids, int64_t vecs) {
+  const int64_t s0 = (int64_t)src_ids[blockIdx.x] * vecs, d0 = (int64_t)dst_ids[blockIdx.x] * vecs;
+  const int64_t per = (vecs + gridDim.y - 1) / gridDim.y;
+  const int64_t lo = blockIdx.y * per, hi = min(vecs, lo + per);
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[d0 + i] = src[s0 + i];
+}
+
+void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, const int* dst_ids, int n,
+                    int64_t block_bytes, cudaStream_t s) {
+  if (n == 0) return;
+  if (block_bytes % 16 || (reinterpret_cast<uintptr_t>(src_base) & 15) || (reinterpret_cast<uintptr_t>(dst_base) & 15))
+    throw std::runtime_error("kv_blocks_copy: 16-byte aligned pools and block sizes required");
+  const int64_t vecs = block_bytes / 16;
+  const int chunks = (int)std::min<int64_t>(64, std::max<int64_t>(1, vecs / 4096));
+  kv_blocks_copy_kernel<<<dim3(n, chunks), 256, 0, s>>>(static_cast<const uint4*>(src_base), src_ids,
+                                                        static_cast<uint4*>(dst_base), dst_ids, vecs);
+  check_launch("kv_blocks_copy");
+}
+
 void splitk_reduce(const float* part, int splits, int T, int N, void* out, int ld_out, bool out_bf16,
                    cudaStream_t s) {
   if (T == 0) return;

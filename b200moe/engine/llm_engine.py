@@ -152,6 +152,56 @@ class LLMEngine:
     def cancel_request(self, seq_id: int) -> bool:
         return self.scheduler.cancel(seq_id)
 
+    # -------------------------------------- prefill / decode disaggregation
+    def prefilled_sequences(self) -> list[Sequence]:
+        """Running sequences whose prompt is computed and that hold their first
+        generated token: ready to hand off to a decode engine."""
+        return [s for s in self.scheduler.running if not s.is_finished and not s.is_prefill
+                and s.num_completion_tokens >= 1]
+
+    def detach(self, seq: Sequence):
+        """Stop scheduling a handed-off sequence but keep its KV blocks (they
+        are read by an in-flight transfer); ``release`` frees them."""
+        self.scheduler.running.remove(seq)
+
+    def release(self, seq: Sequence):
+        from b200moe.engine.sequence import SequenceStatus
+        if seq.block_table:
+            self.scheduler._bm(seq).deallocate(seq)
+        seq.status = SequenceStatus.FINISHED
+        seq.finish_reason = "handoff"
+        seq.finish_time = perf_counter()
+
+    def admit_prefilled(self, token_ids: list[int], num_prompt_tokens: int,
+                        sampling_params: SamplingParams) -> Sequence | None:
+        """Decode side of a handoff: reserve KV blocks for a sequence whose KV
+        (all tokens but the last) comes from a prefill engine.  Returns None
+        while the pool lacks room (back-pressure); after the KV import, call
+        ``activate``."""
+        seq = Sequence(list(token_ids), sampling_params)
+        seq.num_prompt_tokens = num_prompt_tokens
+        bm = self.scheduler.block_manager
+        if bm.num_free_blocks < seq.num_blocks:
+            return None
+        for _ in range(seq.num_blocks):
+            seq.block_table.append(bm._allocate_block())
+        seq.dp_rank = 0
+        seq.is_prefill = False
+        return seq
+
+    def activate(self, seq: Sequence):
+        """Start decoding a handed-off sequence whose KV has been imported.
+        Its full blocks join the prefix cache (their KV is exactly a local
+        prefill's), with the chained hashes a local prefill would give."""
+        from b200moe.engine.sequence import SequenceStatus
+        bm = self.scheduler.block_manager
+        seq.num_cached_tokens = 0
+        bm.hash_blocks(seq, seq.num_tokens - 1)
+        seq.num_cached_tokens = seq.num_tokens - 1
+        seq.status = SequenceStatus.RUNNING
+        seq.record_token(perf_counter())
+        self.scheduler.running.append(seq)
+
     def set_scheduler_overlap(self, enabled: bool):
         """Runtime switch; disabling drains the pipeline (parked batch launches)."""
         self._overlap = bool(enabled)

@@ -460,6 +460,10 @@ class ModelRunner:
     def exit(self):
         self.graphs.clear()
         self.graph_pool = None
+        ep = getattr(getattr(self, "model", None), "ep", None)
+        if ep is not None and getattr(ep, "p2p", None) is not None:
+            ep.p2p.close()  # collective: every rank reaches exit together
+            ep.p2p = None
         for attr in ("model", "kv"):
             if hasattr(self, attr):
                 delattr(self, attr)

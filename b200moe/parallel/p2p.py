@@ -1,7 +1,8 @@
 """Fused expert-parallel MoE over NVLink peer memory (kernels: csrc/kernels/ep_p2p.cu).
 
-Buffers are symmetric (``torch.distributed._symmetric_memory``): every rank
-allocates the same layout and gets the device addresses of every peer's copy.
+Buffers are symmetric: every rank allocates the same layout (one cudaMalloc
+per buffer), shares it through a CUDA IPC handle, and maps every peer's copy
+on its own device (plain NVLink peer mappings, no multicast object).
 Per MoE layer (no host synchronisation, CUDA-graph capturable):
 
     ep_dispatch  -> ep_count -> ep_scatter -> gate/up GEMM -> down GEMM with
@@ -9,8 +10,9 @@ Per MoE layer (no host synchronisation, CUDA-graph capturable):
 
 The routed rows cross NVLink once (source -> owner, as P2P stores from the
 dispatch kernel) and the weighted expert outputs cross once (owner -> source,
-as P2P stores from the down GEMM's epilogue).  No TMA multicast, no library
-kernel touches peer memory.
+as P2P stores from the down GEMM's epilogue).  Peer memory is touched only by
+plain loads and stores of these kernels; no TMA load and no library kernel
+ever reads it.
 """
 from __future__ import annotations
 
@@ -28,34 +30,67 @@ class P2PMoE:
 
     @staticmethod
     def create(ep) -> "P2PMoE | None":
-        import torch.distributed._symmetric_memory as symm_mem
         runner = ep.runner
         cfg = runner.config
         args = runner.args
+        C = ops.native()
         W, rank, dev = ep.world, ep.rank, ep.device
         H, k = args.hidden_size, args.num_experts_per_tok
         slot_cap = cfg.max_num_batched_tokens * k
         cap = slot_cap
-        group = dist.group.WORLD
-        try:
-            symm_mem.enable_symm_mem_for_group(group.group_name)
-        except Exception:
-            pass
+        di = dev.index if dev.index is not None else torch.cuda.current_device()
+        self = P2PMoE(ep, {})
+        self._owned, self._opened = [], []
+
+        ok = True
 
         def alloc(*shape, dtype):
-            t = symm_mem.empty(*shape, dtype=dtype, device=dev)
-            t.zero_()
-            h = symm_mem.rendezvous(t, group.group_name)
-            return t, [int(p) for p in h.buffer_ptrs]
+            # every rank joins every exchange even after a local failure, so the
+            # collective sequence stays aligned; the verdict is agreed below
+            nonlocal ok
+            nbytes = torch.empty(0, dtype=dtype).element_size()
+            for d in shape:
+                nbytes *= d
+            ptr, blob = None, None
+            if ok:
+                try:
+                    ptr, handle = C.ipc_alloc(nbytes, di)
+                    self._owned.append(ptr)
+                    blob = bytes(handle.numpy())
+                except Exception as exc:  # noqa: BLE001 - reported, then the NCCL path is used
+                    print(f"[ep] ipc_alloc failed on rank {rank}: {exc}", flush=True)
+                    ok = False
+            handles = [None] * W
+            dist.all_gather_object(handles, blob)
+            ptrs = []
+            for r, h in enumerate(handles):
+                if not ok or h is None:
+                    ok = False
+                    break
+                if r == rank:
+                    ptrs.append(ptr)
+                    continue
+                try:
+                    q = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), di)
+                    self._opened.append(q)
+                    ptrs.append(q)
+                except Exception as exc:  # noqa: BLE001
+                    print(f"[ep] ipc_open of rank {r} failed on rank {rank}: {exc}", flush=True)
+                    ok = False
+                    break
+            return (C.tensor_from_ptr(ptr, list(shape), dtype, di) if ok else None), ptrs
 
-        symm = {}
         for name, shape, dt in (("recv_x", (W * cap, H), torch.bfloat16), ("recv_meta", (W * cap, 4), torch.int32),
                                 ("counts", (W,), torch.int32), ("flags", (W,), torch.int32),
                                 ("done", (W,), torch.int32), ("slots", (slot_cap, H), torch.bfloat16)):
-            symm[name] = alloc(*shape, dtype=dt)
+            self.symm[name] = alloc(*shape, dtype=dt)
         torch.cuda.synchronize(dev)
-        dist.barrier()
-        self = P2PMoE(ep, symm)
+        verdict = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(verdict, op=dist.ReduceOp.MIN)
+        self.device_index = di
+        if int(verdict.item()) == 0:
+            self.close()
+            return None
         self.W, self.rank, self.H, self.cap, self.slot_cap = W, rank, H, cap, slot_cap
         self.owner = ep.owner.to(torch.int32)
         self.g2l = ep.g2l
@@ -64,6 +99,22 @@ class P2PMoE:
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = ops.status_word(dev)
         return self
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after a device sync and
+        a barrier, so no peer still writes into them)."""
+        if not getattr(self, "_owned", None):
+            return
+        C = ops.native()
+        torch.cuda.synchronize(self.device_index)
+        if dist.is_initialized():
+            dist.barrier()
+        for p in self._opened:
+            C.ipc_close(p, self.device_index)
+        self.symm.clear()
+        for p in self._owned:
+            C.ipc_free(p, self.device_index)
+        self._owned, self._opened = [], []
 
     def _a(self):
         s = self.symm
