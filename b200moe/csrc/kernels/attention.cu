@@ -85,17 +85,27 @@ __device__ __forceinline__ void load_kv_tile(uint32_t sk, uint32_t sv, const voi
   if (!int8) {
     const bf16* kc = static_cast<const bf16*>(kc_);
     const bf16* vc = static_cast<const bf16*>(vc_);
-    for (int idx = threadIdx.x; idx < kKT * CPR; idx += NT) {
-      const int r = idx / CPR, c = idx % CPR;
-      const int key = k0 + r;
-      const bool valid = key < k_end;
-      int64_t off = 0;
-      if (valid) {
-        const int blk = btab[key / bs];
-        off = (int64_t)blk * block_stride + ((int64_t)h * bs + key % bs) * D + c * 8;
-      }
-      cp_async16(sk + tile_off<D>(r, c), kc + off, valid);
-      cp_async16(sv + tile_off<D>(r, c), vc + off, valid);
+    // A thread's chunk column is fixed and its rows step by NT / CPR: gather all
+    // its block-table entries first (independent loads), then issue the copies,
+    // so no copy waits behind a table lookup.
+    static_assert(NT % CPR == 0 && kKT % (NT / CPR) == 0, "tile / thread mapping");
+    constexpr int RPI = NT / CPR;          // rows per iteration
+    constexpr int ITERS = kKT / RPI;
+    const int c = threadIdx.x % CPR, r0 = threadIdx.x / CPR;
+    int64_t off[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int key = k0 + r0 + i * RPI;
+      off[i] = key < k_end ? (int64_t)btab[key / bs] * block_stride + ((int64_t)h * bs + key % bs) * D + c * 8
+                           : -1;
+    }
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int r = r0 + i * RPI;
+      const bool valid = off[i] >= 0;
+      const int64_t o = valid ? off[i] : 0;
+      cp_async16(sk + tile_off<D>(r, c), kc + o, valid);
+      cp_async16(sv + tile_off<D>(r, c), vc + o, valid);
     }
     return;
   }

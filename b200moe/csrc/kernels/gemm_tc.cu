@@ -224,10 +224,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   if (threadIdx.x == 32) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS + 1 : 1);  // fp8: every dequant warp + the MMA
+      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS / 2 + 1 : 1);  // fp8: the stage's dequant group + the MMA
     }
     for (int j = 0; j < 4; ++j) {
-      mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS : 1);
+      mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS / 2 : 1);
       mbar_init(&cempty_bar[j], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -330,21 +330,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     }
   } else if (warp >= 2 && warp < C::EPI_WARP0) {
     // ================================================= dequantisers
+    // Two groups of 8 warps take alternate stages; a lane converts 2 chunks of
+    // every weight tile of its group's stages, so the per-stage wait / fence /
+    // arrive overhead is paid once per 32 values instead of once per 16.
     if constexpr (AFP8) {
-      const int chunk = (warp - 2) * 32 + lane;  // this lane's 16-byte chunk of every 128x64 tile
-      const int row = chunk >> 2, c16 = chunk & 3;
-      const int src_off = row * 64 + c16 * 16;
-      // 128B-swizzled K-major row: 16-byte unit u of row r lives at u ^ (r & 7)
-      const int dst0 = row * 128 + (((2 * c16) ^ (row & 7)) << 4);
-      const int dst1 = row * 128 + (((2 * c16 + 1) ^ (row & 7)) << 4);
-      const bool tracer = warp == 2 && lane == 0;
+      constexpr int kGroups = 2;
+      constexpr int GW = C::CONV_WARPS / kGroups;          // warps per group
+      constexpr int CPL = 128 * kBK / 16 / (GW * 32);      // 16-byte chunks per lane per tile
+      const int dw = warp - 2;
+      const int group = dw / GW;
+      int src_off[CPL], dst0[CPL], dst1[CPL];
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int chunk = (dw % GW) * 32 + lane + j * GW * 32;
+        const int row = chunk >> 2, c16 = chunk & 3;
+        src_off[j] = row * 64 + c16 * 16;
+        // 128B-swizzled K-major row: 16-byte unit u of row r lives at u ^ (r & 7)
+        dst0[j] = row * 128 + (((2 * c16) ^ (row & 7)) << 4);
+        dst1[j] = row * 128 + (((2 * c16 + 1) ^ (row & 7)) << 4);
+      }
+      const bool tracer = dw == 0 && lane == 0;
       const int nkb = args.scale_k_blocks;
       const int pair_mb = C::NA > 1 ? args.pair_row_offset / 128 : 0;
-      // (tile, stage) cursor; the block scales of the NEXT stage are loaded while
-      // the current one converts, so no L2 round trip follows a barrier wait
-      int t = blockIdx.x, ks = 0, ks1 = 0;
+      // (tile, stage) cursor over this CTA's stages; the group takes every kGroups-th
+      int t = blockIdx.x, ks = -1, ks1 = 0;
       TileCoord tc{};
-      auto advance = [&]() -> bool {  // moves the cursor to the next stage of this CTA
+      auto advance = [&]() -> bool {
         if (++ks < ks1) return true;
         if (ks1 != 0) t += gridDim.x;
         if (t >= total_tiles) return false;
@@ -358,34 +369,37 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         out[0] = __ldg(sc + tc.i * nkb);
         if constexpr (C::NA > 1) out[1] = __ldg(sc + (tc.i + pair_mb) * nkb);
       };
-      ks = -1;  // so the first advance() lands on the first stage of the first tile
       bool have = advance();
+      for (int i = 0; i < group && have; ++i) have = advance();
       float next_scale[C::NA];
       if (have) load_scales(next_scale);
-      for (int gi = 0; have; ++gi) {
-        const int s = gi % C::STAGES;
-        const uint32_t phase = (gi / C::STAGES) & 1;
-        const int cj = gi % C::CONV_SLOTS;
-        const uint32_t cph = (gi / C::CONV_SLOTS) & 1;
+      int gi = group, s = group % C::STAGES, cj = group % C::CONV_SLOTS;
+      uint32_t phase = (group / C::STAGES) & 1, cph = (group / C::CONV_SLOTS) & 1;
+      while (have) {
         float scale[C::NA];
 #pragma unroll
         for (int a = 0; a < C::NA; ++a) scale[a] = next_scale[a];
-        have = advance();
-        if (have) load_scales(next_scale);
+        for (int i = 0; i < kGroups && have; ++i) have = advance();
+        if (have) load_scales(next_scale);  // the group's next stage, fetched during this one
         const bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) &&
                           mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
         if (!__all_sync(0xffffffffu, w_ok)) break;
         if (tracer) trace_ev(args, 1, gi);
-        uint4 q[C::NA];
+        uint4 q[C::NA][CPL];
 #pragma unroll
-        for (int a = 0; a < C::NA; ++a) q[a] = *reinterpret_cast<const uint4*>(ALd(s, a) + src_off);
+        for (int a = 0; a < C::NA; ++a)
+#pragma unroll
+          for (int j = 0; j < CPL; ++j) q[a][j] = *reinterpret_cast<const uint4*>(ALd(s, a) + src_off[j]);
 #pragma unroll
         for (int a = 0; a < C::NA; ++a) {
-          uint32_t o[8];
-          dequant16(q[a], scale[a], o);
           uint8_t* dst = A16(cj, a);
-          *reinterpret_cast<uint4*>(dst + dst0) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(dst + dst1) = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll
+          for (int j = 0; j < CPL; ++j) {
+            uint32_t o[8];
+            dequant16(q[a][j], scale[a], o);
+            *reinterpret_cast<uint4*>(dst + dst0[j]) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(dst + dst1[j]) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -394,6 +408,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           mbar_arrive(&cfull_bar[cj]);  // and its slice of the bf16 tile is written
         }
         if (tracer) trace_ev(args, 2, gi);
+        // the group's next stage is kGroups stages further on
+        gi += kGroups;
+        s += kGroups;
+        if (s >= C::STAGES) { s -= C::STAGES; phase ^= 1; }
+        cj += kGroups;
+        if (cj >= C::CONV_SLOTS) { cj -= C::CONV_SLOTS; cph ^= 1; }
       }
     }
   } else {

@@ -81,6 +81,11 @@ class Executor:
         from b200moe.engine.model_runner import ModelRunner
         if self.world > 1:
             import multiprocessing as mp
+            # The engine's process group is its own, even inside a torchrun job:
+            # torchrun's agent-store flag would make every rank (rank 0 too) a
+            # client of the engine's tcp:// rendezvous, with no server to reach.
+            for var in ("TORCHELASTIC_USE_AGENT_STORE", "TORCHELASTIC_RESTART_COUNT"):
+                os.environ.pop(var, None)
             if not config.distributed_init_method:
                 config.distributed_init_method = f"tcp://127.0.0.1:{free_port()}"
             ctx = mp.get_context("spawn")
@@ -169,11 +174,14 @@ class Executor:
 
     # --------------------------------------------------------------- steps
     def plans(self, batch, grammar_masks: dict | None = None) -> list[StepPlan]:
-        """One plan per rank: all rows on rank 0 (shared attention), or each
-        sequence's rows on its data-parallel rank."""
+        """One plan per rank: every row on every rank (tensor-parallel
+        attention), or each sequence's rows on its data-parallel rank."""
         seqs, q, flags = batch.sequences, batch.query_lens, batch.prefill_flags
         bs = self.config.kvcache_block_size
-        if self.dp == 1:
+        if self.dp == 1 and self.config.attention_parallel == "tp" and self.world > 1:
+            plan = build_plan(seqs, q, flags, bs, self.max_blocks)
+            plans = [plan] * self.world  # tensor-parallel attention: every rank runs every row
+        elif self.dp == 1:
             plans = [build_plan(seqs, q, flags, bs, self.max_blocks)] + \
                     [empty_plan(self.max_blocks) for _ in range(self.world - 1)]
         else:

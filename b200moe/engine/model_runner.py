@@ -80,11 +80,13 @@ class ModelRunner:
         self.profiler = DeviceProfiler(self.device, enabled=config.enable_profiling)
         expert_ids = expert_placement(config, rank, self.world_size) if args.is_moe else []
         t0 = time.perf_counter()
+        # tensor-parallel attention: heads split over the ranks, every rank sees every token
+        self.attn_tp = self.world_size if (config.attention_parallel == "tp" and self.world_size > 1) else 1
         self.model = Qwen3MoeForCausalLM(args, self.device, ep_rank=rank, ep_size=self.world_size,
-                                         expert_ids=expert_ids)
+                                         expert_ids=expert_ids, attn_tp=self.attn_tp, attn_rank=rank)
         self.model.moe_backend = "loop" if config.moe_backend == "loop" else "fused"
         self.model.attention_backend = config.attention_backend
-        if self.world_size > 1:
+        if self.world_size > 1 and self.attn_tp == 1:
             from b200moe.parallel.ep import ExpertParallel
             self.model.ep = ExpertParallel(self, config.moe_backend)
         if config.random_init:
@@ -154,6 +156,9 @@ class ModelRunner:
         if self._graphs_allowed():
             self.capture_cudagraphs()
 
+    def kv_heads(self) -> int:
+        return self.kv.num_kv_heads
+
     def memory_reserved(self) -> int:
         return torch.cuda.memory_reserved(self.device) if self.device.type == "cuda" else 0
 
@@ -199,7 +204,7 @@ class ModelRunner:
     def allocate_kv_cache(self):
         c, a = self.config, self.args
         int8 = c.kv_cache_dtype == "int8"
-        nkv = a.num_key_value_heads
+        nkv = self.model.nkv_local
         block_bytes = KVPool.bytes_per_block(a.num_hidden_layers, nkv, self.block_size, a.head_dim,
                                              self.model.dtype, int8)
         if c.num_kvcache_blocks <= 0:

@@ -162,7 +162,7 @@ def _kv(T, ctx, bs=256, nkv=4, D=128, layers=2):
     return pool, tables
 
 
-def case_decode(T, ctx, iters, nq=32, nkv=4, D=128):
+def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0):
     from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM
     pool, tables = _kv(T, ctx)
     q = torch.randn(T, nq, D, device="cuda").to(torch.bfloat16)
@@ -170,6 +170,10 @@ def case_decode(T, ctx, iters, nq=32, nkv=4, D=128):
     out = torch.empty_like(q)
     model = type("M", (), {"args": type("A", (), {"num_key_value_heads": nkv})()})()
     split_len, nsplit = Qwen3MoeForCausalLM.decode_splits(model, T, ctx)
+    if splits:
+        per = -(-ctx // splits)
+        split_len = -(-per // 64) * 64
+        nsplit = -(-ctx // split_len)
     ws = (torch.empty(T * nq * nsplit, D, device="cuda"), torch.empty(T * nq * nsplit, device="cuda"),
           torch.empty(T * nq * nsplit, device="cuda"))
     ms = timeit(lambda: ops.decode_attention(q, pool.layer(0), tables, lens, D ** -0.5, out, split_len, nsplit, ws),
@@ -285,6 +289,7 @@ def main():
     p.add_argument("--ctx", type=int, default=1152)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--layers", type=int, default=48)
+    p.add_argument("--splits", type=int, default=0, help="decode: force this many KV splits (0 = heuristic)")
     a = p.parse_args()
     torch.cuda.set_device(0)
     if a.case in ("moe", "all"):
@@ -292,7 +297,7 @@ def main():
     if a.case in ("dense", "all"):
         case_dense(a.tokens, a.iters)
     if a.case in ("decode", "all"):
-        case_decode(a.tokens, a.ctx, a.iters)
+        case_decode(a.tokens, a.ctx, a.iters, splits=a.splits)
     if a.case in ("prefill", "all"):
         case_prefill(max(a.tokens, a.ctx), a.ctx, a.iters)
     if a.case == "trace":

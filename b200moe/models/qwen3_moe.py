@@ -25,6 +25,7 @@ from contextlib import nullcontext
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 from torch import nn
 
 from b200moe import ops
@@ -62,10 +63,13 @@ def _param(t: torch.Tensor) -> nn.Parameter:
 
 class Qwen3MoeLayer(nn.Module):
 
-    def __init__(self, args: ModelArgs, layer_id: int, num_local_experts: int, dtype, device, quant: bool):
+    def __init__(self, args: ModelArgs, layer_id: int, num_local_experts: int, dtype, device, quant: bool,
+                 nq: int | None = None, nkv: int | None = None):
         super().__init__()
         H, D = args.hidden_size, args.head_dim
-        nq, nkv = args.num_attention_heads, args.num_key_value_heads
+        # nq / nkv: this rank's query / KV heads (all of them unless attention is tensor-parallel)
+        nq = args.num_attention_heads if nq is None else nq
+        nkv = args.num_key_value_heads if nkv is None else nkv
         self.layer_id = layer_id
         self.is_moe = args.is_moe_layer(layer_id)
         wdt = torch.float8_e4m3fn if quant else dtype
@@ -100,9 +104,22 @@ class Qwen3MoeLayer(nn.Module):
 class Qwen3MoeForCausalLM(nn.Module):
 
     def __init__(self, args: ModelArgs, device, dtype=None, ep_rank: int = 0, ep_size: int = 1,
-                 expert_ids: list[int] | None = None):
+                 expert_ids: list[int] | None = None, attn_tp: int = 1, attn_rank: int = 0):
         super().__init__()
         self.args = args
+        # Tensor-parallel attention: this rank holds query heads
+        # [q_head0, q_head0 + nq_local) and KV heads [kv_head0, kv_head0 + nkv_local)
+        # (a KV head is replicated when there are more ranks than KV heads); the
+        # O projection's partial sums and the local experts' outputs are
+        # all-reduced over the ranks, which all see the same tokens.
+        nq, nkv = args.num_attention_heads, args.num_key_value_heads
+        if nq % attn_tp or (nkv % attn_tp and attn_tp % nkv):
+            raise ValueError("tensor-parallel attention needs heads % tp == 0 and kv heads dividing or divisible by tp")
+        self.attn_tp, self.attn_rank = attn_tp, attn_rank
+        self.nq_local = nq // attn_tp
+        self.nkv_local = max(1, nkv // attn_tp)
+        self.q_head0 = attn_rank * self.nq_local
+        self.kv_head0 = self.q_head0 // (nq // nkv)
         self.device = torch.device(device)
         self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else args.dtype)
         self.quant = args.quant_block is not None
@@ -119,7 +136,8 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.lm_head = self.embed_tokens if args.tie_word_embeddings else _param(
             torch.empty(V, H, dtype=self.dtype, device=self.device))
         self.layers = nn.ModuleList([
-            Qwen3MoeLayer(args, l, self.num_local_experts, self.dtype, self.device, self.quant)
+            Qwen3MoeLayer(args, l, self.num_local_experts, self.dtype, self.device, self.quant,
+                          self.nq_local, self.nkv_local)
             for l in range(args.num_hidden_layers)])
         self.cos_sin = ops.rope_cos_sin(args.head_dim, args.max_position_embeddings, args.rope_theta, self.device)
         self.scale = args.head_dim ** -0.5
@@ -128,6 +146,19 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.attention_backend = "paged"  # or "sdpa": per-sequence PyTorch attention (A/B, equivalence gate)
         self.profiler = None
         self._ws: dict = {}
+
+    def qkv_row_ranges(self) -> list[tuple[int, int]]:
+        """Rows of the full [q | k | v] projection held by this rank (q, k, v order)."""
+        a = self.args
+        D, nq, nkv = a.head_dim, a.num_attention_heads, a.num_key_value_heads
+        return [(self.q_head0 * D, (self.q_head0 + self.nq_local) * D),
+                ((nq + self.kv_head0) * D, (nq + self.kv_head0 + self.nkv_local) * D),
+                ((nq + nkv + self.kv_head0) * D, (nq + nkv + self.kv_head0 + self.nkv_local) * D)]
+
+    def o_col_range(self) -> tuple[int, int]:
+        """Input columns of the full O projection held by this rank."""
+        D = self.args.head_dim
+        return self.q_head0 * D, (self.q_head0 + self.nq_local) * D
 
     @property
     def cuda(self) -> bool:  # type: ignore[override]
@@ -148,7 +179,7 @@ class Qwen3MoeForCausalLM(nn.Module):
     def reserve_workspace(self, max_tokens: int, max_rows: int, max_splits: int):
         """Size every scratch buffer for the largest step up front."""
         a = self.args
-        H, D, nq, nkv = a.hidden_size, a.head_dim, a.num_attention_heads, a.num_key_value_heads
+        H, D, nq, nkv = a.hidden_size, a.head_dim, self.nq_local, self.nkv_local
         k = max(1, a.num_experts_per_tok)
         rows = max_tokens * k * max(1, self.ep_size)
         for name, shape, dt in (
@@ -186,6 +217,9 @@ class Qwen3MoeForCausalLM(nn.Module):
                         out=self._buf("x", (T, H), self.dtype) if cuda else None)
         for l, layer in enumerate(self.layers):
             o = self._attention(layer, x, inp, kv.layer(l))
+            if self.attn_tp > 1:
+                with self._range("attn.all_reduce"):
+                    dist.all_reduce(o)  # row-parallel O projection: sum of the ranks' partial products
             x = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=residual,
                             out=self._buf("x", (T, H), self.dtype) if cuda else None)
             nxt = self.layers[l + 1].input_layernorm if l + 1 < len(self.layers) else self.norm
@@ -199,7 +233,7 @@ class Qwen3MoeForCausalLM(nn.Module):
     def _attention(self, layer, x, inp: StepInputs, kvl):
         a = self.args
         T = inp.num_tokens
-        nq, nkv, D = a.num_attention_heads, a.num_key_value_heads, a.head_dim
+        nq, nkv, D = self.nq_local, self.nkv_local, a.head_dim
         cuda = self.cuda
         with self._range("attn.qkv"):
             qkv = ops.linear(x, layer.qkv_weight, layer.qkv_scale,
@@ -239,7 +273,7 @@ class Qwen3MoeForCausalLM(nn.Module):
     def decode_splits(self, rows: int, max_len: int) -> tuple[int, int]:
         """Keys per split and split count for flash-decoding: enough CTAs to
         cover the SMs a few times over, splits of at least 64 keys."""
-        nkv = self.args.num_key_value_heads
+        nkv = getattr(self, "nkv_local", self.args.num_key_value_heads)
         want = max(1, -(-4 * ops.NUM_SMS // max(1, rows * nkv)))
         split_len = max(64, -(-max(1, max_len) // want))
         split_len = -(-split_len // 64) * 64
@@ -251,6 +285,8 @@ class Qwen3MoeForCausalLM(nn.Module):
         eps = a.rms_norm_eps
         if not layer.is_moe:
             return self._dense_mlp(layer, x, residual, next_norm, T)
+        if self.attn_tp > 1:
+            return self._moe_tp(layer, x, residual, next_norm, T)
         if not self.cuda or self.moe_backend == "loop":
             moe_out = self._moe_reference(layer, x)
             return ops.rmsnorm(moe_out, next_norm, eps, residual=residual,
@@ -333,6 +369,59 @@ class Qwen3MoeForCausalLM(nn.Module):
             ops.grouped_down_scatter(h_perm, layer.w2, layer.s2, counts[:E], offsets, slot_of_row,
                                      w.view(-1), slots)
         return slots
+
+    def _moe_tp(self, layer, x, residual, next_norm, T):
+        """Tensor-parallel attention mode: every rank holds all T tokens; it runs
+        its own experts on the tokens routed to them, and the ranks' partial sums
+        are all-reduced before the residual add (the reference's EP combine,
+        nanovllm/models/qwen3_moe.py:414-418)."""
+        a = self.args
+        k, H, E, eps = a.num_experts_per_tok, a.hidden_size, a.num_experts, a.rms_norm_eps
+        El = self.num_local_experts
+        partial = self._buf("moe_partial", (T, H), self.dtype) if self.cuda else torch.zeros(T, H, dtype=x.dtype)
+        if not self.cuda or self.moe_backend == "loop":
+            ids, w = self.route(layer, x)
+            partial.copy_(self.experts_reference(layer, x, ids, w).sum(1).to(partial.dtype))
+        else:
+            counts = self._buf("counts", (2 * E + 1,), torch.int32)
+            counts.zero_()
+            ids, w = self.route(layer, x, counts[:E])
+            g2l = self._tp_maps()
+            ids_l = g2l.index_select(0, ids.reshape(-1).long()).view(T, k)   # -1: another rank's expert
+            counts_l = self._buf("counts_l", (2 * El,), torch.int32)
+            counts_l[:El].copy_(counts[:E].index_select(0, self._expert_ids_dev))
+            counts_l[El:].zero_()
+            rows = T * k
+            x_perm = self._buf("x_perm", (rows, H), self.dtype)
+            slot_of_row = self._buf("slot_of_row", (rows,), torch.int32)
+            offsets = self._buf("offsets", (El + 1,), torch.int32)
+            ops.moe_permute(x, ids_l, counts_l[:El], counts_l[El:], x_perm, slot_of_row, offsets)
+            I = layer.w2.shape[-1]
+            h_perm = self._buf("h_perm", (rows, I), self.dtype)
+            ops.grouped_gate_up_silu(x_perm, layer.w13, layer.s13, counts_l[:El], offsets, h_perm, I)
+            slots = self._buf("slots", (rows, H), self.dtype)
+            slots.zero_()  # slots of other ranks' experts stay zero
+            ops.grouped_down_scatter(h_perm, layer.w2, layer.s2, counts_l[:El], offsets, slot_of_row,
+                                     w.view(-1), slots)
+            # combine (fixed-order sum over k) into a zeroed residual: partial = sum_k slots
+            partial.zero_()
+            ops.moe_combine_add_rmsnorm(slots, k, partial, next_norm, eps,
+                                        out=self._buf("moe_norm_scratch", (T, H), self.dtype))
+        with self._range("moe.all_reduce"):
+            dist.all_reduce(partial)
+        return ops.rmsnorm(partial, next_norm, eps, residual=residual,
+                           out=self._buf("x", (T, H), self.dtype) if self.cuda else None)
+
+    def _tp_maps(self):
+        g2l = getattr(self, "_g2l_dev", None)
+        if g2l is None:
+            E = self.args.num_experts
+            m = torch.full((E,), -1, dtype=torch.int32)
+            for le, ge in enumerate(self.expert_ids):
+                m[ge] = le
+            self._g2l_dev = g2l = m.to(self.device)
+            self._expert_ids_dev = torch.tensor(self.expert_ids, dtype=torch.long, device=self.device)
+        return g2l
 
     def _dense_mlp(self, layer, x, residual, next_norm, T):
         a = self.args

@@ -65,13 +65,42 @@ def random_init_(model, seed: int = 0, std: float = 0.02):
             param.copy_(q)
             scale_param.copy_(s)
 
+    def fill_sliced(param, scale_param, key, full_shape, rows=None, cols=None):
+        """Draw the full weight (so every tensor-parallel rank holds a slice of
+        the same tensor), quantise it blockwise, keep this rank's rows / cols."""
+        full = gen(full_shape, key)
+        if scale_param is not None:
+            for lo, hi in (rows or []) + ([cols] if cols else []):
+                if lo % 128 or hi % 128:
+                    raise ValueError("tensor-parallel slices of fp8 weights must be 128-aligned")
+            q, sc = quantize_block_fp8(full)
+        else:
+            q, sc = full.to(param.dtype), None
+        if rows is not None:
+            param.copy_(torch.cat([q[a:b] for a, b in rows]))
+            if sc is not None:
+                scale_param.copy_(torch.cat([sc[a // 128:b // 128] for a, b in rows]))
+        else:
+            a, b = cols
+            param.copy_(q[:, a:b])
+            if sc is not None:
+                scale_param.copy_(sc[:, a // 128:b // 128])
+
     model.embed_tokens.copy_(gen(model.embed_tokens.shape, 1).to(model.embed_tokens.dtype))
     if model.lm_head is not model.embed_tokens:
         model.lm_head.copy_(gen(model.lm_head.shape, 2).to(model.lm_head.dtype))
     for l, layer in enumerate(model.layers):
         base = 100 + 16 * l
-        fill2d(layer.qkv_weight, layer.qkv_scale, base + 1)
-        fill2d(layer.o_weight, layer.o_scale, base + 2)
+        if getattr(model, "attn_tp", 1) > 1:
+            D = args.head_dim
+            nqkv = (args.num_attention_heads + 2 * args.num_key_value_heads) * D
+            fill_sliced(layer.qkv_weight, layer.qkv_scale, base + 1, (nqkv, args.hidden_size),
+                        rows=model.qkv_row_ranges())
+            fill_sliced(layer.o_weight, layer.o_scale, base + 2, (args.hidden_size, args.num_attention_heads * D),
+                        cols=model.o_col_range())
+        else:
+            fill2d(layer.qkv_weight, layer.qkv_scale, base + 1)
+            fill2d(layer.o_weight, layer.o_scale, base + 2)
         if layer.is_moe:
             E = args.num_experts
             layer.router.zero_()
@@ -214,12 +243,26 @@ def load_checkpoint(model, path: str):
                          ("post_attention_layernorm", layer.post_attention_layernorm),
                          ("self_attn.q_norm", layer.q_norm), ("self_attn.k_norm", layer.k_norm)):
             copy_into(dst, get(p + src + ".weight"))
-        bounds = [0, nq * D, (nq + nkv) * D, (nq + 2 * nkv) * D]
+        # this rank's rows of q / k / v (all of them unless attention is tensor-parallel)
+        local = model.qkv_row_ranges() if hasattr(model, "qkv_row_ranges") else \
+            [(0, nq * D), (nq * D, (nq + nkv) * D), ((nq + nkv) * D, (nq + 2 * nkv) * D)]
+        starts = [0, nq * D, (nq + nkv) * D]
+        r = 0
         for i, n in enumerate(("q_proj", "k_proj", "v_proj")):
-            r0, r1 = bounds[i], bounds[i + 1]
-            weight_pair(p + "self_attn." + n, layer.qkv_weight[r0:r1],
-                        layer.qkv_scale[r0 // 128:r1 // 128] if layer.qkv_scale is not None else None)
-        weight_pair(p + "self_attn.o_proj", layer.o_weight, layer.o_scale)
+            a0, a1 = local[i][0] - starts[i], local[i][1] - starts[i]  # rows within this projection
+            rows = a1 - a0
+            w_src = get(p + "self_attn." + n + ".weight")[a0:a1]
+            copy_into(layer.qkv_weight[r:r + rows], w_src)
+            if layer.qkv_scale is not None:
+                if a0 % 128 or a1 % 128:
+                    raise ValueError("tensor-parallel slices of fp8 weights must be 128-aligned")
+                s_src = get(p + "self_attn." + n + ".weight_scale_inv").float()[a0 // 128:a1 // 128]
+                copy_into(layer.qkv_scale[r // 128:(r + rows) // 128], s_src)
+            r += rows
+        c0, c1 = model.o_col_range() if hasattr(model, "o_col_range") else (0, nq * D)
+        copy_into(layer.o_weight, get(p + "self_attn.o_proj.weight")[:, c0:c1])
+        if layer.o_scale is not None:
+            copy_into(layer.o_scale, get(p + "self_attn.o_proj.weight_scale_inv").float()[:, c0 // 128:c1 // 128])
         I = layer.w2.shape[-1]
 
         def mlp(prefix, le):

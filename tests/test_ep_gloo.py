@@ -28,3 +28,22 @@ def test_gloo_world2_matches_single_rank():
     assert m["kv_blocks_capacity"] == 2 * 128
     agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
     assert agree > 0.98, agree
+
+
+def test_gloo_tensor_parallel_attention_matches_single_rank():
+    """attention_parallel="tp": heads split over 2 gloo ranks, O-projection and
+    expert partial sums all-reduced; tokens must match one rank."""
+    kw = dict(device="cpu", kvcache_block_size=16, num_kvcache_blocks=128, max_num_batched_tokens=512,
+              max_num_seqs=16, max_model_len=256, enforce_eager=True)
+    sp = SamplingParams(temperature=0.0, max_tokens=16, ignore_eos=True)
+    prompts = _prompts(seed=1)
+    one = LLM("tiny-moe", random_init="seeded", **kw)
+    a = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False)]
+    one.exit()
+    two = LLM("tiny-moe", tensor_parallel_size=2, attention_parallel="tp", random_init="seeded", **kw)
+    heads = two.executor.call_all("kv_heads")
+    b = [o["token_ids"] for o in two.generate(prompts, sp, use_tqdm=False)]
+    two.exit()
+    assert heads == [1, 1]  # tiny-moe has 2 KV heads: one per rank
+    agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
+    assert agree > 0.98, agree
