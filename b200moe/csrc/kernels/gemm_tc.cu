@@ -67,6 +67,9 @@ struct GemmCfg {
   // enough bf16 slots that dequantisation runs ahead of MMA completion (the
   // commit round trip, not the conversion itself, bounds a short ring)
   static constexpr int CONV_SLOTS = AFP8 ? (PAIR ? 3 : 4) : 0;
+  // dequantiser warp groups taking stages round robin (at most one stage per bf16 slot)
+  static constexpr int DEQ_GROUPS = AFP8 ? (PAIR ? 2 : 4) : 1;
+  static_assert(!AFP8 || (CONV_WARPS % DEQ_GROUPS == 0 && DEQ_GROUPS <= CONV_SLOTS), "dequant groups");
   static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
   static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
   static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES) / STAGE_BYTES;
@@ -224,10 +227,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   if (threadIdx.x == 32) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS / 2 + 1 : 1);  // fp8: the stage's dequant group + the MMA
+      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS + 1 : 1);  // fp8: the stage's dequant group + the MMA
     }
     for (int j = 0; j < 4; ++j) {
-      mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS / 2 : 1);
+      mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS : 1);
       mbar_init(&cempty_bar[j], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -330,11 +333,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     }
   } else if (warp >= 2 && warp < C::EPI_WARP0) {
     // ================================================= dequantisers
-    // Two groups of 8 warps take alternate stages; a lane converts 2 chunks of
-    // every weight tile of its group's stages, so the per-stage wait / fence /
-    // arrive overhead is paid once per 32 values instead of once per 16.
+    // DEQ_GROUPS groups of warps take stages round robin; a lane converts
+    // 16 / (warps per group) chunks of every weight tile of its group's stages,
+    // so the per-stage wait / fence / arrive overhead is amortised over more
+    // values (2 groups: 32 values per lane per tile, 4 groups: 64).
     if constexpr (AFP8) {
-      constexpr int kGroups = 2;
+      constexpr int kGroups = C::DEQ_GROUPS;
       constexpr int GW = C::CONV_WARPS / kGroups;          // warps per group
       constexpr int CPL = 128 * kBK / 16 / (GW * 32);      // 16-byte chunks per lane per tile
       const int dw = warp - 2;

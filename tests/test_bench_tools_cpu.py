@@ -118,3 +118,27 @@ def test_make_tiny_moe_roundtrip(tmp_path):
         assert [len(o["token_ids"]) for o in out] == [3, 3]
     finally:
         llm.exit()
+
+
+# ------------------------------------------------------------- charts
+def test_svg_charts(tmp_path):
+    import xml.etree.ElementTree as ET
+    from b200moe import charts
+    off = tmp_path / "off.json"
+    off.write_text(json.dumps({"summary": [
+        {"phase": "matrix", "backend": b, "attention_backend": "paged", "batch": n, "throughput_median": t}
+        for b, f in (("fused", 1.0), ("loop", 0.5)) for n, t in ((1, 100 * f), (8, 700 * f), (64, 3000 * f))]}))
+    onl = tmp_path / "on.json"
+    onl.write_text(json.dumps({"points": [{"achieved_qps": q, "slo_standard_rate": r, "slo_strict_rate": r * 0.9,
+                                           "tpot_p95_s": 0.05 * q} for q, r in ((1, 1.0), (2, 1.0), (4, 0.7))]}))
+    bl = tmp_path / "bench.jsonl"
+    bl.write_text("\n".join(json.dumps({"value": 9000.0 * n, "n_gpus": n, "unit": "tok/s"}) for n in (1, 2, 4, 8)))
+    mic = tmp_path / "micro.jsonl"
+    mic.write_text('{"kernel": "moe_gate_up_silu", "hbm_frac": 0.52, "tc_frac": 0.06, "tokens": 256}\nmicro rc=0\n')
+    files = charts.render(str(tmp_path / "charts"), off, onl, bl, mic)
+    assert len(files) == 4
+    for f in files:
+        root = ET.parse(f).getroot()  # well-formed SVG
+        assert root.tag.endswith("svg")
+        assert "sha256" in open(f).read()
+    assert open(files[0]).read().count("<polyline") == 2

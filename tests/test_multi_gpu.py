@@ -44,3 +44,23 @@ def test_ep2_matches_single_gpu(single, backend, eager):
     agree = np.mean([a == b for ra, rb in zip(out, single) for a, b in zip(ra, rb)])
     assert agree > 0.95, agree
     assert out == out2
+
+
+@needs2
+def test_tp2_attention_matches_single_gpu():
+    """Tensor-parallel attention over 2 GPUs (head-sharded QKV/O + NCCL
+    all-reduce, experts split): greedy tokens match one GPU on a 4-layer
+    Qwen3-30B-A3B-shaped model (128-row fp8 blocks align with the head split)."""
+    kw = dict(kvcache_block_size=64, max_num_seqs=8, max_num_batched_tokens=1024, max_model_len=512,
+              num_kvcache_blocks=64, random_init="seeded", enforce_eager=True)
+    prompts = [[(13 * i + 7 * j) % 150000 + 1 for j in range(40 + 17 * i)] for i in range(6)]
+    sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
+    one = LLM("qwen3-30b-a3b-4l", **kw)
+    a = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False)]
+    one.exit()
+    two = LLM("qwen3-30b-a3b-4l", tensor_parallel_size=2, attention_parallel="tp", **kw)
+    b = [o["token_ids"] for o in two.generate(prompts, sp, use_tqdm=False)]
+    two.executor.call("check_status")
+    two.exit()
+    agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
+    assert agree > 0.9, agree
