@@ -162,9 +162,11 @@ def _kv(T, ctx, bs=256, nkv=4, D=128, layers=2):
     return pool, tables
 
 
-def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0):
+def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0, pool_layers=2):
+    """pool_layers: layers interleaved in each KV block slab (the engine's pool
+    holds every layer of a block in one slab, so one layer's keys are strided)."""
     from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM
-    pool, tables = _kv(T, ctx)
+    pool, tables = _kv(T, ctx, layers=pool_layers)
     q = torch.randn(T, nq, D, device="cuda").to(torch.bfloat16)
     lens = torch.full((T,), ctx, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
@@ -178,7 +180,8 @@ def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0):
           torch.empty(T * nq * nsplit, device="cuda"))
     ms = timeit(lambda: ops.decode_attention(q, pool.layer(0), tables, lens, D ** -0.5, out, split_len, nsplit, ws),
                 iters)
-    report("decode_attn", ms, T * ctx * nkv * D * 2 * 2, 4 * T * ctx * nq * D, seqs=T, ctx=ctx, splits=nsplit)
+    report("decode_attn", ms, T * ctx * nkv * D * 2 * 2, 4 * T * ctx * nq * D, seqs=T, ctx=ctx, splits=nsplit,
+           pool_layers=pool_layers)
 
 
 def case_prefill(T, ctx, iters, nq=32, nkv=4, D=128):
@@ -290,6 +293,7 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--splits", type=int, default=0, help="decode: force this many KV splits (0 = heuristic)")
+    p.add_argument("--pool-layers", type=int, default=2, help="decode: layers per KV block slab")
     a = p.parse_args()
     torch.cuda.set_device(0)
     if a.case in ("moe", "all"):
@@ -297,7 +301,7 @@ def main():
     if a.case in ("dense", "all"):
         case_dense(a.tokens, a.iters)
     if a.case in ("decode", "all"):
-        case_decode(a.tokens, a.ctx, a.iters, splits=a.splits)
+        case_decode(a.tokens, a.ctx, a.iters, splits=a.splits, pool_layers=a.pool_layers)
     if a.case in ("prefill", "all"):
         case_prefill(max(a.tokens, a.ctx), a.ctx, a.iters)
     if a.case == "trace":

@@ -125,6 +125,11 @@ def run(args, prompts, metric: str) -> int:
         write_checkpoint(ckpt, ARCH[args.model], seed=args.seed)
     write_s = time.perf_counter() - t0
     sys.path.insert(0, REF)
+    # Under torchrun, the agent-store flag would make the reference engine's own
+    # rank 0 a client of its tcp:// rendezvous (no server): the reference is
+    # normally started with plain python, so drop what torchrun adds.
+    for var in ("TORCHELASTIC_USE_AGENT_STORE", "TORCHELASTIC_RESTART_COUNT"):
+        os.environ.pop(var, None)
     from nanovllm import LLM, SamplingParams  # the reference package
     t0 = time.perf_counter()
     llm = LLM(ckpt, tensor_parallel_size=args.gpus, max_num_seqs=max(args.num_requests, 1),

@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--scheduler-policy", default="fcfs")
     p.add_argument("--attention-parallel", default="dp")
     p.add_argument("--enforce-eager", action="store_true")
+    p.add_argument("--scheduler-overlap", type=int, choices=(0, 1), default=1,
+                   help="schedule step N+1 on the host while step N runs on the GPU")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -94,7 +96,7 @@ def main():
               max_num_batched_tokens=args.max_num_batched_tokens, max_model_len=args.input_len + args.output_len + 16,
               kvcache_block_size=256, scheduler_policy=args.scheduler_policy,
               attention_parallel=args.attention_parallel, enforce_eager=args.enforce_eager, seed=args.seed,
-              random_init="seeded")
+              scheduler_overlap=bool(args.scheduler_overlap), random_init="seeded")
     init_s = time.perf_counter() - t_init
     runners = llm.executor
     for _ in range(args.warmup):
@@ -130,6 +132,7 @@ def main():
         "config": {"model": args.model, "global_batch": args.num_requests, "seq_len": args.input_len,
                    "output_len": args.output_len, "parallelism": f"ep{args.gpus}+{args.attention_parallel}{args.gpus}-attn",
                    "l2": "inputs larger than L2 (30 GB of weights per pass), no flush",
+                   "scheduler_overlap": bool(args.scheduler_overlap),
                    "engine_steps_per_pass": nsteps // max(args.steps, 1), "init_s": round(init_s, 1)},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "wall_s_per_pass": round(wall / args.steps, 3)},

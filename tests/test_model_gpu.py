@@ -120,3 +120,39 @@ def test_int8_kv_generate():
     q.exit()
     agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
     assert agree > 0.6, agree
+
+
+def test_prefix_cache_and_kv_offload_same_tokens():
+    """Shared-prefix prompts: cache hits, then host offload of evicted prefix
+    blocks and their revival must reproduce the uncached tokens."""
+    rng = random.Random(9)
+    shared = [rng.randrange(1024) for _ in range(64)]
+    group_a = [shared + [rng.randrange(1024) for _ in range(16)] for _ in range(4)]
+    group_b = [[rng.randrange(1024) for _ in range(96)] for _ in range(12)]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    ref = _engine(enforce_eager=True)
+    want = [o["token_ids"] for o in ref.generate(group_a, sp, use_tqdm=False)]
+    ref.exit()
+    llm = _engine(enforce_eager=True, num_kvcache_blocks=40, kv_offload_enabled=True, kv_offload_host_blocks=64)
+    first = [o["token_ids"] for o in llm.generate(group_a, sp, use_tqdm=False)]
+    llm.generate(group_b, sp, use_tqdm=False)  # pushes group A's cached prefix out of the device pool
+    again = [o["token_ids"] for o in llm.generate(group_a, sp, use_tqdm=False)]
+    m = llm.metrics()
+    llm.exit()
+    assert first == want and again == want
+    assert m["kv_prefix_hit_tokens_total"] > 0
+    assert m["kv_offload_puts_total"] > 0 and m["kv_offload_revives_total"] > 0, m
+
+
+def test_overlap_pipeline_matches_serial():
+    """Overlap scheduling (schedule step N+1 while step N runs, CUDA graphs on)
+    must give the serial engine's tokens."""
+    sp = SamplingParams(temperature=0.0, max_tokens=20, ignore_eos=True)
+    prompts = _prompts(10, seed=4)
+    serial = _engine(cuda_graph_max_bs=16)
+    a = [o["token_ids"] for o in serial.generate(prompts, sp, use_tqdm=False)]
+    serial.exit()
+    ov = _engine(cuda_graph_max_bs=16, scheduler_overlap=True)
+    b = [o["token_ids"] for o in ov.generate(prompts, sp, use_tqdm=False)]
+    ov.exit()
+    assert a == b
