@@ -38,7 +38,14 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker_main(config: Config, rank: int, conn, parent_pid: int):
+def _use_shm() -> bool:
+    return os.environ.get("B200MOE_SHM_CHANNEL", "1") != "0"
+
+
+def _worker_main(config: Config, rank: int, conn, parent_pid: int, shm_spec=None):
+    if shm_spec is not None:
+        from b200moe.engine.shm_channel import ShmLink
+        conn = ShmLink(shm_spec[0], conn, 1, shm_spec[1])
     try:
         from b200moe.engine.model_runner import ModelRunner
         runner = ModelRunner(config, rank)
@@ -91,7 +98,14 @@ class Executor:
             ctx = mp.get_context("spawn")
             for r in range(1, self.world):
                 a, b = ctx.Pipe(duplex=True)
-                p = ctx.Process(target=_worker_main, args=(config, r, b, os.getpid()), daemon=True)
+                spec = None
+                if _use_shm():
+                    # per-step messages go through shared memory; the pipe stays for
+                    # wake-ups, oversize payloads and end-of-file on a dead peer
+                    from b200moe.engine.shm_channel import ShmLink
+                    a = ShmLink.create(a)
+                    spec = a.spec()
+                p = ctx.Process(target=_worker_main, args=(config, r, b, os.getpid(), spec), daemon=True)
                 p.start()
                 self.procs.append(p)
                 self.conns.append(a)
@@ -253,7 +267,10 @@ class Executor:
     def exit(self):
         for r, c in enumerate(self.conns, start=1):
             try:
-                c.send(("exit", ()))
+                if hasattr(c, "spec"):
+                    c.send(("exit", ()), timeout=2.0)  # a hung peer never consumes: do not wait long
+                else:
+                    c.send(("exit", ()))
             except Exception:
                 pass
         for r, c in enumerate(self.conns, start=1):
@@ -265,6 +282,9 @@ class Executor:
             p.join(timeout=10)
             if p.is_alive():
                 p.kill()
+        for c in self.conns:
+            if hasattr(c, "close") and hasattr(c, "spec"):
+                c.close()
         self.procs, self.conns = [], []
         if getattr(self, "runner", None) is not None:
             self.runner.exit()
