@@ -2,6 +2,7 @@
 // dtype, contiguity and shapes on the host before launching on the current
 // CUDA stream, so a bad call raises a Python exception instead of faulting.
 #include <torch/extension.h>
+#include <cuda.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -339,6 +340,29 @@ std::tuple<int64_t, Tensor> ipc_alloc(int64_t nbytes, int64_t device) {
   return {reinterpret_cast<int64_t>(p), ht};
 }
 
+// IPC handle of the cudaMalloc allocation that contains `ptr` (allocators hand out
+// pieces of larger segments): returns (handle bytes, offset of ptr in the allocation).
+std::tuple<Tensor, int64_t> ipc_export(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = nullptr;
+  if (range == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    IPC_CHECK(cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "cuMemGetAddressRange not available");
+    range = reinterpret_cast<RangeFn>(p);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  TORCH_CHECK(range(&base, &size, (CUdeviceptr)ptr) == CUDA_SUCCESS, "ipc_export: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  IPC_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  Tensor ht = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  std::memcpy(ht.data_ptr(), &h, sizeof(h));
+  return {ht, (int64_t)(ptr - (int64_t)base)};
+}
+
 int64_t ipc_open(Tensor handle, int64_t device) {
   TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t) && handle.scalar_type() == torch::kUInt8,
               "ipc_open: expected a 64-byte handle");
@@ -376,6 +400,29 @@ void kv_blocks_copy(Tensor src_pool, Tensor src_ids, int64_t dst_ptr, Tensor dst
                        dst_ids.data_ptr<int>(), (int)src_ids.numel(), block_bytes, stream());
 }
 
+void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
+                  c10::optional<Tensor> counts) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16);
+  CHECK_CONTIG(w); CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(ids, torch::kInt32); CHECK_DT(weights, torch::kFloat32);
+  TORCH_CHECK(x.size(1) == w.size(1) && w.size(0) >= num_experts, "router shapes");
+  TORCH_CHECK(ids.numel() >= x.size(0) * topk && weights.numel() >= x.size(0) * topk, "router outputs too small");
+  b200::router_fused(x.data_ptr(), w.data_ptr(), (int)x.size(0), (int)x.size(1), (int)num_experts, (int)topk, renorm,
+                     ids.data_ptr<int>(), weights.data_ptr<float>(), ptr_or_null<int>(counts), stream());
+}
+
+// residual += bf16(sum of split-K partials); out = rmsnorm(residual) * weight
+void rmsnorm_partials(Tensor part, int64_t splits, Tensor residual, Tensor weight, Tensor out, double eps) {
+  CHECK_CUDA(part); CHECK_CONTIG(part); CHECK_DT(part, torch::kFloat32);
+  CHECK_CONTIG(residual); CHECK_CONTIG(out); CHECK_DT(residual, torch::kBFloat16); CHECK_DT(out, torch::kBFloat16);
+  const int H = (int)residual.size(-1);
+  const int T = (int)(residual.numel() / H);
+  TORCH_CHECK(part.numel() >= splits * (int64_t)T * H && weight.numel() == H && out.numel() == residual.numel(),
+              "rmsnorm_partials shapes");
+  b200::rmsnorm(nullptr, residual.data_ptr(), weight.data_ptr(), out.data_ptr(), residual.data_ptr(), T, H, (float)eps,
+                stream(), part.data_ptr<float>(), (int)splits);
+}
+
 void splitk_reduce(Tensor part, int64_t splits, Tensor out) {
   CHECK_CUDA(part); CHECK_CONTIG(part); CHECK_DT(part, torch::kFloat32);
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out must be [T, N] with unit inner stride");
@@ -400,7 +447,7 @@ void moe_permute(Tensor x, Tensor ids, Tensor counts, Tensor cursor, Tensor x_pe
 void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
                  c10::optional<Tensor> v_scale, Tensor block_tables, Tensor seq_lens, Tensor out, Tensor part_o,
                  Tensor part_m, Tensor part_l, int64_t block_size, int64_t block_stride, int64_t num_kv_heads,
-                 double scale, int64_t num_splits, int64_t split_len) {
+                 double scale, int64_t num_splits, int64_t split_len, c10::optional<Tensor> status) {
   CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_DT(q, torch::kBFloat16);
   CHECK_DT(block_tables, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_CONTIG(block_tables);
   const int B = (int)q.size(0);
@@ -429,6 +476,8 @@ void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor>
   a.part_m = part_m.data_ptr<float>();
   a.part_l = part_l.data_ptr<float>();
   a.out = out.data_ptr();
+  a.num_blocks = (int)k_cache.size(0);
+  a.status = ptr_or_null<int>(status);
   if (num_splits > 1)
     TORCH_CHECK(part_m.numel() >= (int64_t)B * nq * num_splits && part_o.numel() >= (int64_t)B * nq * num_splits * D,
                 "split workspace too small");
@@ -509,9 +558,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &router_topk);
   m.def("moe_permute", &moe_permute);
   m.def("splitk_reduce", &splitk_reduce);
+  m.def("rmsnorm_partials", &rmsnorm_partials);
+  m.def("router_fused", &router_fused);
   m.def("kv_blocks_copy", &kv_blocks_copy);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
+  m.def("ipc_export", &ipc_export);
   m.def("ipc_close", &ipc_close);
   m.def("ipc_free", &ipc_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);

@@ -27,6 +27,8 @@ struct DecodeArgs {
   float* part_m;             // [B, q_heads, num_splits]
   float* part_l;
   void* out;                 // [B, q_heads, D] bf16
+  int num_blocks;            // blocks in the pool (TMA path: out-of-range block = zero fill)
+  int* status;               // device status word (bounded waits), may be null
 };
 
 struct PrefillArgs {

@@ -32,8 +32,10 @@ struct QkvArgs {
 
 void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,
                   cudaStream_t s);
+// part != null: x is given as `splits` fp32 partial sums [splits, T, H] (split-K GEMM
+// output), reduced and rounded to bf16 before the residual add.
 void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,
-             float eps, cudaStream_t s);
+             float eps, cudaStream_t s, const float* part = nullptr, int splits = 0);
 void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
                              int H, float eps, cudaStream_t s);
 void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s);
@@ -47,6 +49,10 @@ void splitk_reduce(const float* part, int splits, int T, int N, void* out, int l
 // (16-byte plain loads / stores; dst may be a peer GPU's pool mapped over NVLink).
 void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, const int* dst_ids, int n,
                     int64_t block_bytes, cudaStream_t s);
+// Router GEMM (x [T, H] bf16 . w[:E]^T, fp32 accumulate, bf16-rounded logits) +
+// softmax + top-k in one launch; E <= 128.
+void router_fused(const void* x, const void* w, int T, int H, int E, int topk, bool renorm, int* ids, float* weights,
+                  int* counts, cudaStream_t s);
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
                  void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s);
 

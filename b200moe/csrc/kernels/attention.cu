@@ -24,11 +24,16 @@
 // Reference: Triton paged decode kernel nanovllm/kernels/paged_attention.py:74-190
 // (one program per (batch, q head), no GQA sharing) and the per-sequence SDPA
 // prefill loop nanovllm/layers/attention.py:179-213.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "sm100.cuh"
 #include "attention.h"
@@ -140,8 +145,20 @@ __device__ __forceinline__ void load_kv_tile(uint32_t sk, uint32_t sv, const voi
   }
 }
 
+// 128B-swizzled tile as a TMA load with CU_TENSOR_MAP_SWIZZLE_128B writes it:
+// [D / 64 halves][kKT rows][128 B], 16-byte unit u of row r stored at u ^ (r & 7).
+template <int D>
+__device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
+  return (chunk >> 3) * (kKT * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+}
+template <int D, bool TMA>
+__device__ __forceinline__ uint32_t kv_off(int row, int chunk) {
+  if constexpr (TMA) return swz_off<D>(row, chunk);
+  else return tile_off<D>(row, chunk);
+}
+
 // S[16 x 8*NB] = Q(frag) * K^T for keys [kbase, kbase + 8*NB) of the smem tile
-template <int D, int NB>
+template <int D, int NB, bool TMA = false>
 __device__ __forceinline__ void qk_mma(float (&s)[NB][4], const uint32_t (&qf)[D / 16][4], uint32_t sk,
                                        int kbase, int lane) {
 #pragma unroll
@@ -157,7 +174,7 @@ __device__ __forceinline__ void qk_mma(float (&s)[NB][4], const uint32_t (&qf)[D
       const int key = kbase + n * 8 + (mi >> 1) * 8 + rr;
       const int chunk = ks * 2 + (mi & 1);
       uint32_t b0, b1, b2, b3;
-      ldmatrix_x4(sk + tile_off<D>(key, chunk), b0, b1, b2, b3);
+      ldmatrix_x4(sk + kv_off<D, TMA>(key, chunk), b0, b1, b2, b3);
       mma16816(s[n], qf[ks], b0, b1);
       mma16816(s[n + 1], qf[ks], b2, b3);
     }
@@ -165,7 +182,7 @@ __device__ __forceinline__ void qk_mma(float (&s)[NB][4], const uint32_t (&qf)[D
 }
 
 // O[16 x D] += P(16 x 16 keys, bf16 A fragment) * V[keys kbase.., D]
-template <int D>
+template <int D, bool TMA = false>
 __device__ __forceinline__ void pv_mma(float (&o)[D / 8][4], const uint32_t (&pf)[4], uint32_t sv, int kbase,
                                        int lane) {
 #pragma unroll
@@ -175,7 +192,7 @@ __device__ __forceinline__ void pv_mma(float (&o)[D / 8][4], const uint32_t (&pf
     const int key = kbase + (mi & 1) * 8 + rr;
     const int chunk = n + (mi >> 1);
     uint32_t b0, b1, b2, b3;
-    ldmatrix_x4_t(sv + tile_off<D>(key, chunk), b0, b1, b2, b3);
+    ldmatrix_x4_t(sv + kv_off<D, TMA>(key, chunk), b0, b1, b2, b3);
     mma16816(o[n], pf, b0, b1);
     mma16816(o[n + 1], pf, b2, b3);
   }
@@ -398,6 +415,262 @@ __global__ void decode_combine_kernel(const DecodeArgs a) {
   }
 }
 
+// ============================================================ decode (TMA)
+// Same math and CTA mapping as decode_attn_kernel, restructured for sm_100a:
+// a producer warp streams 64-key K/V tiles with TMA (128B-swizzled, one tensor
+// map over the layer's pool planes) into a 3-stage ring guarded by full /
+// empty mbarriers; four consumer warps (16 keys each) run the MMAs and an
+// online softmax whose running max is moved only when a row's max grows by
+// more than 2^8 (FlashAttention-3's lazy rescale), so the 64-multiply output
+// rescale is skipped on most tiles.  Consumers issue no loads.
+constexpr int kTmaStages = 3;
+constexpr float kLazyLog2 = 8.f;
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+template <int D>
+struct DecTma {
+  static constexpr int TILE = kKT * D * 2;                     // bytes of one K (or V) tile
+  static constexpr int RING = kTmaStages * 2 * TILE;
+  static constexpr int BTAB = 256;  // block-table entries of one split staged in shared memory
+  static constexpr int SMEM = 1024 + RING + 16 * D * 2 + 2 * 64 * 4 + 2 * kTmaStages * 8 + 16 + BTAB * 4;
+};
+
+template <int D>
+__global__ void __launch_bounds__(160) decode_attn_tma_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                             const DecodeArgs a, int sub_rows, int oob_block) {
+  constexpr int NC = 128;  // consumer threads
+  using C = DecTma<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;                                   // stage s: K tile at s*2*TILE, V tile after it
+  uint8_t* sQ = ring + C::RING;                           // [16][D]
+  float* sM = reinterpret_cast<float*>(sQ + 16 * D * 2);  // [4][16]
+  float* sL = sM + 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sL + 64);
+  uint64_t* empty = full + kTmaStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kTmaStages);
+  int* sBt = reinterpret_cast<int*>(empty + kTmaStages) + 4;  // [BTAB] block ids of this split
+  float* sO = reinterpret_cast<float*>(ring);             // [16][D], reuses the ring after the loop
+
+  const int b = blockIdx.z, h = blockIdx.y, split = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.group;
+  const int L = a.seq_lens[b];
+  const int k_begin = split * a.split_len;
+  const int k_end = min(L, k_begin + a.split_len);
+  const int nq = a.num_kv_heads * G;
+  const int ntiles = k_end > k_begin ? (k_end - k_begin + kKT - 1) / kKT : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTmaStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  const bf16* qsrc = static_cast<const bf16*>(a.q) + ((size_t)b * nq + (size_t)h * G) * D;
+  for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += blockDim.x) {
+    const int r = idx / (D / 8), c = idx % (D / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = *reinterpret_cast<const uint4*>(qsrc + (size_t)r * D + c * 8);
+    *reinterpret_cast<uint4*>(sQ + tile_off<D>(r, c)) = v;
+  }
+  __syncthreads();
+
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    // the split's block ids, gathered by the whole warp up front: no dependent
+    // global load sits between two tile issues
+    const int* btab = a.block_tables + (size_t)b * a.max_blocks;
+    const int blk0 = k_begin / a.block_size;
+    const int nblk = ntiles > 0 ? (k_end - 1) / a.block_size - blk0 + 1 : 0;
+    const bool staged = nblk <= C::BTAB;
+    if (staged)
+      for (int i = lane; i < nblk; i += 32) sBt[i] = btab[blk0 + i];
+    __syncwarp();
+    if (lane == 0 && ntiles > 0) {
+      tma_prefetch_desc(&kv_map);
+      const int nsub = kKT / sub_rows;
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t % kTmaStages;
+        const uint32_t ph = (t / kTmaStages) & 1;
+        if (!mbar_wait(&empty[st], ph ^ 1, a.status, kStatusTimeoutEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[st], 2 * C::TILE);
+        const uint32_t sk = smem_u32(ring + st * 2 * C::TILE), sv = sk + C::TILE;
+        const int k0 = k_begin + t * kKT;
+        for (int j = 0; j < nsub; ++j) {
+          const int key = k0 + j * sub_rows;
+          // keys past the sequence read a block coordinate outside the map: TMA zero-fills
+          const int blk = key >= k_end ? oob_block
+                          : staged ? sBt[key / a.block_size - blk0] : btab[key / a.block_size];
+          const int y = key % a.block_size;
+#pragma unroll
+          for (int hf = 0; hf < D / 64; ++hf) {
+            const uint32_t off = hf * (kKT * 128) + j * sub_rows * 128;
+            tma_load_4d(sk + off, &kv_map, &full[st], hf * 64, y, h, blk);
+            tma_load_4d(sv + off, &kv_map, &full[st], hf * 64, y, a.num_kv_heads + h, blk);
+          }
+        }
+      }
+      if (*abort_flag) {
+        // a wait gave up: let loads already issued (valid sources) land before the CTA exits
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) __nanosleep(1000);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    uint32_t qf[D / 16][4];
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int row = (mi & 1) * 8 + rr, chunk = ks * 2 + (mi >> 1);
+      ldmatrix_x4(smem_u32(sQ) + tile_off<D>(row, chunk), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    }
+    const float sl2 = a.scale * 1.4426950408889634f;
+    for (int t = 0; t < ntiles; ++t) {
+      const int st = t % kTmaStages;
+      const uint32_t ph = (t / kTmaStages) & 1;
+      const bool ok = mbar_wait(&full[st], ph, a.status, kStatusTimeoutFull, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint32_t sk = smem_u32(ring + st * 2 * C::TILE), sv = sk + C::TILE;
+      float sc[2][4];
+      qk_mma<D, 2, true>(sc, qf, sk, warp * 16, lane);
+      const int key0 = k_begin + t * kKT + warp * 16;
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + n * 8 + 2 * (lane & 3) + (e & 1);
+          sc[n][e] = key < k_end ? sc[n][e] * sl2 : -INFINITY;
+          mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      }
+      // lazy rescale: move the reference max only when a row grew by > 2^8
+      const bool grow0 = mx[0] > m_r[0] + kLazyLog2, grow1 = mx[1] > m_r[1] + kLazyLog2;
+      if (__any_sync(0xffffffffu, grow0 || grow1)) {
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const bool g = r ? grow1 : grow0;
+          const float mn = g ? mx[r] : m_r[r];
+          corr[r] = (m_r[r] == -INFINITY || !g) ? 1.f : exp2f(m_r[r] - mn);
+          m_r[r] = mn;
+          l_r[r] *= corr[r];
+        }
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) {
+          o[n][0] *= corr[0]; o[n][1] *= corr[0];
+          o[n][2] *= corr[1]; o[n][3] *= corr[1];
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mm = m_r[e >> 1];
+          const float p = mm == -INFINITY ? 0.f : exp2f(sc[n][e] - mm);
+          sc[n][e] = p;
+          l_r[e >> 1] += p;
+        }
+      uint32_t pf[4];
+      pf[0] = pack_bf16(sc[0][0], sc[0][1]);
+      pf[1] = pack_bf16(sc[0][2], sc[0][3]);
+      pf[2] = pack_bf16(sc[1][0], sc[1][1]);
+      pf[3] = pack_bf16(sc[1][2], sc[1][3]);
+      pv_mma<D, true>(o, pf, sv, warp * 16, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+    }
+  }
+
+  // ---- merge the 4 consumer warps (each saw different keys); the producer warp only syncs
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = l_r[r];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    l_r[r] = l;
+  }
+  const int r0 = lane >> 2;
+  if (warp < 4 && (lane & 3) == 0) {
+    sM[warp * 16 + r0] = m_r[0];
+    sM[warp * 16 + r0 + 8] = m_r[1];
+    sL[warp * 16 + r0] = l_r[0];
+    sL[warp * 16 + r0 + 8] = l_r[1];
+  }
+  __syncthreads();  // every TMA write and every consumer read of the ring is complete
+  for (int i = threadIdx.x; i < 16 * D; i += blockDim.x) sO[i] = 0.f;
+  __syncthreads();
+  if (warp < 4) {
+    float wscale[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = r0 + 8 * r;
+      float m = -INFINITY;
+      for (int w = 0; w < 4; ++w) m = fmaxf(m, sM[w * 16 + row]);
+      wscale[r] = (m == -INFINITY || m_r[r] == -INFINITY) ? 0.f : exp2f(m_r[r] - m);
+    }
+    for (int w = 0; w < 4; ++w) {
+      if (w == warp) {
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) {
+          const int col = n * 8 + 2 * (lane & 3);
+          sO[r0 * D + col] += o[n][0] * wscale[0];
+          sO[r0 * D + col + 1] += o[n][1] * wscale[0];
+          sO[(r0 + 8) * D + col] += o[n][2] * wscale[1];
+          sO[(r0 + 8) * D + col + 1] += o[n][3] * wscale[1];
+        }
+      }
+      named_barrier_sync(1, NC);
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int row = idx / D, col = idx % D;
+    float m = -INFINITY;
+    for (int w = 0; w < 4; ++w) m = fmaxf(m, sM[w * 16 + row]);
+    float l = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sM[w * 16 + row];
+      if (mw != -INFINITY) l += sL[w * 16 + row] * exp2f(mw - m);
+    }
+    const int head = h * G + row;
+    if (a.num_splits == 1) {
+      bf16* out = static_cast<bf16*>(a.out) + ((size_t)b * nq + head) * D;
+      out[col] = __float2bfloat16(l > 0.f ? sO[row * D + col] / l : 0.f);
+    } else {
+      const size_t pidx = ((size_t)b * nq + head) * a.num_splits + split;
+      a.part_o[pidx * D + col] = sO[row * D + col];
+      if (col == 0) {
+        a.part_m[pidx] = m;
+        a.part_l[pidx] = l;
+      }
+    }
+  }
+}
+
 // ================================================================= prefill
 // Packed rows: r -> query position qb*QPB + r / G, head h*G + r % G.
 template <int D>
@@ -540,8 +813,93 @@ static int decode_smem() { return 16 * D * 2 + 2 * kKVStages * kKT * D * 2 + 2 *
 template <int D>
 static int prefill_smem() { return 64 * D * 2 + 2 * kKVStages * kKT * D * 2; }
 
+// ---- TMA tensor map of one layer's pool planes: dims {D, block_size, 2 * kv_heads
+// (K heads then V heads), blocks}, box {64, rows, 1, 1}, 128-byte swizzle.
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+struct KvMapKey {
+  const void* base;
+  int D, bs, kvh, nblocks;
+  int64_t block_stride;
+  bool operator==(const KvMapKey& o) const {
+    return base == o.base && D == o.D && bs == o.bs && kvh == o.kvh && nblocks == o.nblocks &&
+           block_stride == o.block_stride;
+  }
+};
+
+static const CUtensorMap& kv_tensor_map(const DecodeArgs& a, int sub_rows) {
+  static std::vector<std::pair<KvMapKey, CUtensorMap>> cache;  // one entry per layer of a pool
+  const KvMapKey key{a.k_cache, a.head_dim, a.block_size, a.num_kv_heads, a.num_blocks, a.block_stride};
+  for (auto& e : cache)
+    if (e.first == key) return e.second;
+  CUtensorMap map;
+  const cuuint64_t dims[4] = {(cuuint64_t)a.head_dim, (cuuint64_t)a.block_size, (cuuint64_t)(2 * a.num_kv_heads),
+                              (cuuint64_t)a.num_blocks};
+  const cuuint64_t strides[3] = {(cuuint64_t)a.head_dim * 2, (cuuint64_t)a.block_size * a.head_dim * 2,
+                                 (cuuint64_t)a.block_stride * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)sub_rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.k_cache), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("kv tensor map: cuTensorMapEncodeTiled failed " + std::to_string((int)r));
+  if (cache.size() > 512) cache.clear();
+  cache.emplace_back(key, map);
+  return cache.back().second;
+}
+
+// The TMA kernel needs a bf16 pool whose V planes follow the K planes of the same
+// layer and block (the pool layout), 64-key tiles that stay inside one block or
+// cover whole blocks, and 16-byte aligned planes.
+static bool use_tma_decode(const DecodeArgs& a, int* sub_rows) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("B200MOE_DECODE_TMA");
+    return e == nullptr || std::string(e) != "0";
+  }();
+  if (!enabled || a.kv_int8 || a.num_blocks <= 0) return false;
+  if (a.head_dim != 64 && a.head_dim != 128) return false;
+  const bf16* k = static_cast<const bf16*>(a.k_cache);
+  if (static_cast<const bf16*>(a.v_cache) != k + (int64_t)a.num_kv_heads * a.block_size * a.head_dim) return false;
+  if ((reinterpret_cast<uintptr_t>(a.k_cache) & 15) || (a.block_stride * 2) % 16) return false;
+  if (a.block_size % kKT == 0) *sub_rows = kKT;
+  else if (kKT % a.block_size == 0 && a.block_size % 8 == 0) *sub_rows = a.block_size;
+  else return false;
+  return true;
+}
+
+template <int D>
+static void launch_decode_tma(const DecodeArgs& a, int B, int sub_rows, cudaStream_t s) {
+  const CUtensorMap& map = kv_tensor_map(a, sub_rows);
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(decode_attn_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecTma<D>::SMEM);
+    set = true;
+  }
+  dim3 grid(a.num_splits, a.num_kv_heads, B);
+  decode_attn_tma_kernel<D><<<grid, 160, DecTma<D>::SMEM, s>>>(map, a, sub_rows, a.num_blocks);
+  if (a.num_splits > 1) decode_combine_kernel<D><<<dim3(a.num_kv_heads * a.group, B), D, 0, s>>>(a);
+}
+
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
   if (B == 0) return;
+  int sub_rows = 0;
+  if (a.group <= 16 && 64 % a.group == 0 && a.split_len % kKT == 0 && use_tma_decode(a, &sub_rows)) {
+    if (a.head_dim == 128) launch_decode_tma<128>(a, B, sub_rows, s);
+    else launch_decode_tma<64>(a, B, sub_rows, s);
+    check_launch("paged_decode_attn (tma)");
+    return;
+  }
   if (a.group > 16 || 64 % a.group) throw std::runtime_error("decode attention: GQA group must divide 64 and be <= 16");
   if (a.split_len % kKT) throw std::runtime_error("decode attention: split_len % 64");
   if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("decode attention: int8 KV needs scales");

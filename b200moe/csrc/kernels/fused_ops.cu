@@ -78,7 +78,8 @@ __global__ void embed_gather_kernel(const int* __restrict__ ids, const bf16* __r
 template <int NT, int VPT>
 __global__ void __launch_bounds__(NT) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* res_in,
                                                      const bf16* __restrict__ w, bf16* __restrict__ out,
-                                                     bf16* res_out, int H, float eps) {
+                                                     bf16* res_out, int H, float eps, const float* __restrict__ part,
+                                                     int splits, size_t split_stride) {
   __shared__ float red[NT / 32];
   const size_t base = (size_t)blockIdx.x * H;
   float v[VPT][8];
@@ -86,7 +87,21 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const bf16* __restrict__ x,
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int idx = (threadIdx.x + j * NT) * 8;
-    unpack8(*reinterpret_cast<const uint4*>(x + base + idx), v[j]);
+    if (part != nullptr) {
+      // x is the split-K GEMM's fp32 partial sums: reduce them and round to bf16
+      // (the value the separate reduce kernel would have stored)
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4* q = reinterpret_cast<const float4*>(part + sp * split_stride + base + idx);
+        const float4 lo = q[0], hi = q[1];
+        acc[0] += lo.x; acc[1] += lo.y; acc[2] += lo.z; acc[3] += lo.w;
+        acc[4] += hi.x; acc[5] += hi.y; acc[6] += hi.z; acc[7] += hi.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = bf16r(acc[e]);
+    } else {
+      unpack8(*reinterpret_cast<const uint4*>(x + base + idx), v[j]);
+    }
     if (res_in != nullptr) {
       float r[8];
       unpack8(*reinterpret_cast<const uint4*>(res_in + base + idx), r);
@@ -232,20 +247,15 @@ __global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
 // --------------------------------------------------------------- router
 // One warp per token; E <= 32 * EPL.  Logits are rounded to bf16 first: the
 // reference's gate GEMM returns bf16 (qwen3_moe.py:390).
+// Softmax over E logits of one token held by one warp (EPL per lane, already
+// rounded to bf16 like the reference's bf16 gate output), top-k with the lowest
+// expert id winning ties, optional renormalisation, bf16-rounded weights.
 template <int EPL>
-__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int topk, int renorm,
-                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const float* row = logits + (size_t)warp * ld;
-  float p[EPL];
+__device__ __forceinline__ void topk_row(float (&p)[EPL], int E, int topk, int renorm, int tok, int lane,
+                                         int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = j * 32 + lane;
-    p[j] = e < E ? bf16r(row[e]) : -INFINITY;
-    mx = fmaxf(mx, p[j]);
-  }
+  for (int j = 0; j < EPL; ++j) mx = fmaxf(mx, p[j]);
   mx = warp_max(mx);
   float sum = 0.f;
 #pragma unroll
@@ -262,7 +272,6 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
   int sel_e[8];
   float wsum = 0.f;
   for (int k = 0; k < topk; ++k) {
-    // warp argmax, lowest expert id wins ties
     float bv = -2.f;
     int be = 1 << 30;
 #pragma unroll
@@ -290,9 +299,123 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
     for (int k = 0; k < 8; ++k)
       if (k == lane) { wv = sel_w[k]; ev = sel_e[k]; }
     if (renorm) wv = wv / wsum;
-    ids[(size_t)warp * topk + lane] = ev;
-    weights[(size_t)warp * topk + lane] = bf16r(wv);  // the reference casts weights to bf16
+    ids[(size_t)tok * topk + lane] = ev;
+    weights[(size_t)tok * topk + lane] = bf16r(wv);  // the reference casts weights to bf16
     if (counts != nullptr) atomicAdd(&counts[ev], 1);
+  }
+}
+
+template <int EPL>
+__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int topk, int renorm,
+                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* row = logits + (size_t)warp * ld;
+  float p[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = j * 32 + lane;
+    p[j] = e < E ? bf16r(row[e]) : -INFINITY;
+  }
+  topk_row<EPL>(p, E, topk, renorm, warp, lane, ids, weights, counts);
+}
+
+// ------------------------------------------------------------ fused router
+// Router GEMM + softmax + top-k in one launch (replaces GEMM, split-K reduce and
+// top-k).  CTA = 16 tokens x all experts (<= 128); warp w owns experts
+// [16w, 16w + 16).  x and router rows stream through a double-buffered
+// cp.async ring of 64-wide K chunks (128-byte rows, 16-byte units XOR-swizzled
+// by row) into the warp-level bf16 MMA with fp32 accumulation; the logits go
+// through shared memory to one warp per token for the top-k.
+constexpr int kRtTok = 16, kRtE = 128, kRtK = 64;
+
+__device__ __forceinline__ uint32_t rt_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+
+__device__ __forceinline__ void rt_cp16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+
+__global__ void __launch_bounds__(256) router_fused_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                           int T, int H, int E, int topk, int renorm,
+                                                           int* __restrict__ ids, float* __restrict__ weights,
+                                                           int* __restrict__ counts) {
+  constexpr int XB = kRtTok * 128, WB = kRtE * 128;  // bytes of one x / W chunk
+  __shared__ __align__(128) uint8_t ring[2][XB + WB];
+  __shared__ float logit[kRtTok][kRtE + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kRtTok;
+  const int nchunks = H / kRtK;
+  auto load = [&](int c, int buf) {
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(ring[buf]));
+    for (int i = threadIdx.x; i < (kRtTok + kRtE) * 8; i += 256) {
+      const int row = i >> 3, u = i & 7;
+      if (row < kRtTok) {
+        const int t = t0 + row;
+        rt_cp16(base + rt_off(row, u), x + (size_t)min(t, T - 1) * H + c * kRtK + u * 8, t < T);
+      } else {
+        const int e = row - kRtTok;
+        rt_cp16(base + XB + rt_off(e, u), w + (size_t)e * H + c * kRtK + u * 8, e < E);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float acc[2][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+  load(0, 0);
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) load(c + 1, (c + 1) & 1);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    const uint32_t xs = static_cast<uint32_t>(__cvta_generic_to_shared(ring[c & 1]));
+    const uint32_t ws = xs + XB;
+#pragma unroll
+    for (int ks = 0; ks < kRtK / 16; ++ks) {
+      const int mi = lane >> 3, rr = lane & 7;
+      uint32_t a[4];
+      {
+        const int row = (mi & 1) * 8 + rr, chunk = ks * 2 + (mi >> 1);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]) : "r"(xs + rt_off(row, chunk)));
+      }
+      uint32_t b0, b1, b2, b3;
+      {
+        const int e = warp * 16 + (mi >> 1) * 8 + rr, chunk = ks * 2 + (mi & 1);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(ws + rt_off(e, chunk)));
+      }
+      asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                   "{%0,%1,%2,%3};"
+                   : "+f"(acc[0][0]), "+f"(acc[0][1]), "+f"(acc[0][2]), "+f"(acc[0][3])
+                   : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                   "{%0,%1,%2,%3};"
+                   : "+f"(acc[1][0]), "+f"(acc[1][1]), "+f"(acc[1][2]), "+f"(acc[1][3])
+                   : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b2), "r"(b3));
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = (lane >> 2) + 8 * (e >> 1), col = warp * 16 + n * 8 + 2 * (lane & 3) + (e & 1);
+      logit[row][col] = acc[n][e];
+    }
+  __syncthreads();
+  for (int r = warp; r < kRtTok; r += 8) {
+    const int tok = t0 + r;
+    if (tok >= T) break;
+    float p[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = j * 32 + lane;
+      p[j] = e < E ? bf16r(logit[r][e]) : -INFINITY;
+    }
+    topk_row<4>(p, E, topk, renorm, tok, lane, ids, weights, counts);
   }
 }
 
@@ -407,15 +530,16 @@ void embed_gather(const int* ids, const void* table, void* out, int T, int H, in
 }
 
 void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,
-             float eps, cudaStream_t s) {
+             float eps, cudaStream_t s, const float* part, int splits) {
   if (T == 0) return;
   const bf16 *X = (const bf16*)x, *R = (const bf16*)res_in, *W = (const bf16*)w;
   bf16 *O = (bf16*)out, *RO = (bf16*)res_out;
-  if (H == 2048) rmsnorm_kernel<256, 1><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps);
-  else if (H == 4096) rmsnorm_kernel<256, 2><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps);
-  else if (H == 256) rmsnorm_kernel<32, 1><<<T, 32, 0, s>>>(X, R, W, O, RO, H, eps);
-  else if (H == 512) rmsnorm_kernel<64, 1><<<T, 64, 0, s>>>(X, R, W, O, RO, H, eps);
-  else if (H == 1024) rmsnorm_kernel<128, 1><<<T, 128, 0, s>>>(X, R, W, O, RO, H, eps);
+  const size_t ss = (size_t)T * H;
+  if (H == 2048) rmsnorm_kernel<256, 1><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 4096) rmsnorm_kernel<256, 2><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 256) rmsnorm_kernel<32, 1><<<T, 32, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 512) rmsnorm_kernel<64, 1><<<T, 64, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 1024) rmsnorm_kernel<128, 1><<<T, 128, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
   else throw std::runtime_error("rmsnorm: unsupported hidden size " + std::to_string(H));
   check_launch("rmsnorm");
 }
@@ -455,6 +579,16 @@ void router_topk(const float* logits, int ld, int T, int E, int topk, bool renor
   else if (E <= 256) router_topk_kernel<8><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
   else throw std::runtime_error("router_topk: at most 256 experts");
   check_launch("router_topk");
+}
+
+void router_fused(const void* x, const void* w, int T, int H, int E, int topk, bool renorm, int* ids, float* weights,
+                  int* counts, cudaStream_t s) {
+  if (T == 0) return;
+  if (E > kRtE || topk < 1 || topk > 8 || H % kRtK)
+    throw std::runtime_error("router_fused: needs <= 128 experts, top-k in [1, 8], hidden % 64 == 0");
+  router_fused_kernel<<<(T + kRtTok - 1) / kRtTok, 256, 0, s>>>((const bf16*)x, (const bf16*)w, T, H, E, topk,
+                                                                 renorm ? 1 : 0, ids, weights, counts);
+  check_launch("router_fused");
 }
 
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,

@@ -66,15 +66,21 @@ struct GemmCfg {
   // bf16 ring fed by the dequantisers (fp8 mode only)
   // enough bf16 slots that dequantisation runs ahead of MMA completion (the
   // commit round trip, not the conversion itself, bounds a short ring)
-  static constexpr int CONV_SLOTS = AFP8 ? (PAIR ? 3 : 4) : 0;
-  // dequantiser warp groups taking stages round robin (at most one stage per bf16 slot)
-  static constexpr int DEQ_GROUPS = AFP8 ? (PAIR ? 2 : 4) : 1;
-  static_assert(!AFP8 || (CONV_WARPS % DEQ_GROUPS == 0 && DEQ_GROUPS <= CONV_SLOTS), "dequant groups");
+  // bf16 slots: 4 (single tile) / 3 (gate+up pair: more would cost a load stage,
+  // measured slower) for decode-size tiles, 2 for BN >= 128 (MMA-bound: the shared
+  // memory goes to deeper load stages for the large B tiles)
+  static constexpr int CONV_SLOTS = !AFP8 ? 0 : BN >= 128 ? 2 : PAIR ? 3 : 4;
+
   static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
   static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
   static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   static constexpr int SMEM = STAGES * STAGE_BYTES + CONV_BYTES + EXTRA + 1024;
+  // dequantiser warp groups taking stages round robin: never more groups than
+  // load stages or bf16 slots (a group waits on its own stage and slot)
+  static constexpr int DEQ_GROUPS = !AFP8 ? 1 : (STAGES >= 4 && CONV_SLOTS >= 4) ? 4 : 2;
+  static_assert(!AFP8 || (CONV_WARPS % DEQ_GROUPS == 0 && DEQ_GROUPS <= CONV_SLOTS && DEQ_GROUPS <= STAGES),
+                "dequant groups must fit the load ring and the bf16 ring");
   static constexpr int ACC_COLS = NA * BN;
   static constexpr int TMEM_COLS_RAW = 2 * ACC_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
@@ -415,9 +421,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         // the group's next stage is kGroups stages further on
         gi += kGroups;
         s += kGroups;
-        if (s >= C::STAGES) { s -= C::STAGES; phase ^= 1; }
+        while (s >= C::STAGES) { s -= C::STAGES; phase ^= 1; }
         cj += kGroups;
-        if (cj >= C::CONV_SLOTS) { cj -= C::CONV_SLOTS; cph ^= 1; }
+        while (cj >= C::CONV_SLOTS) { cj -= C::CONV_SLOTS; cph ^= 1; }
       }
     }
   } else {

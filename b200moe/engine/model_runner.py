@@ -354,7 +354,7 @@ class ModelRunner:
         if self.device.type == "cuda":
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
-            self._step_events.append((t_start, ev))
+            self._step_events.append((t_start, ev, plan.is_pure_decode))
         else:
             ev = None
         self._pending = (plan, out, (ev, lp))
@@ -437,7 +437,19 @@ class ModelRunner:
         since the last reset."""
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
-        return float(sum(a.elapsed_time(b) for a, b in self._step_events))
+        return float(sum(a.elapsed_time(b) for a, b, _ in self._step_events))
+
+    def step_device_split(self) -> dict:
+        """Device milliseconds and step counts of pure-decode steps and of steps
+        that carry prefill rows, since the last reset."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        out = {"decode_ms": 0.0, "decode_steps": 0, "prefill_ms": 0.0, "prefill_steps": 0}
+        for a, b, decode in self._step_events:
+            k = "decode" if decode else "prefill"
+            out[k + "_ms"] += a.elapsed_time(b)
+            out[k + "_steps"] += 1
+        return out
 
     def launch_count(self) -> int:
         return ops.launch_count()

@@ -216,12 +216,19 @@ class Qwen3MoeForCausalLM(nn.Module):
         x = ops.rmsnorm(residual, self.layers[0].input_layernorm, eps,
                         out=self._buf("x", (T, H), self.dtype) if cuda else None)
         for l, layer in enumerate(self.layers):
-            o = self._attention(layer, x, inp, kv.layer(l))
+            attn = self._attention(layer, x, inp, kv.layer(l))
+            xbuf = self._buf("x", (T, H), self.dtype) if cuda else None
             if self.attn_tp > 1:
+                with self._range("attn.o_proj"):
+                    o = ops.linear(attn, layer.o_weight, layer.o_scale,
+                                   out=self._buf("o", (T, H), self.dtype) if cuda else None)
                 with self._range("attn.all_reduce"):
                     dist.all_reduce(o)  # row-parallel O projection: sum of the ranks' partial products
-            x = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=residual,
-                            out=self._buf("x", (T, H), self.dtype) if cuda else None)
+                x = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=residual, out=xbuf)
+            else:
+                with self._range("attn.o_proj_add_norm"):
+                    x = ops.linear_add_rmsnorm(attn, layer.o_weight, layer.o_scale, residual,
+                                               layer.post_attention_layernorm, eps, out=xbuf)
             nxt = self.layers[l + 1].input_layernorm if l + 1 < len(self.layers) else self.norm
             x = self._mlp(layer, x, residual, nxt, T)
         return x.index_select(0, inp.logits_indices.long())
@@ -266,9 +273,7 @@ class Qwen3MoeForCausalLM(nn.Module):
                 if inp.num_rows > nd:
                     ops.prefill_attention(q[nd:], kvl, cu, inp.seq_lens[nd:], inp.block_tables[nd:],
                                           inp.max_q_len, self.scale, out[nd:])
-        with self._range("attn.o_proj"):
-            return ops.linear(out.view(T, nq * D), layer.o_weight, layer.o_scale,
-                              out=self._buf("o", (T, a.hidden_size), self.dtype) if cuda else None)
+        return out.view(T, nq * D)  # the O projection is applied by the caller
 
     def decode_splits(self, rows: int, max_len: int) -> tuple[int, int]:
         """Keys per split and split count for flash-decoding: enough CTAs to
@@ -302,10 +307,13 @@ class Qwen3MoeForCausalLM(nn.Module):
         T = x.shape[0]
         k = a.num_experts_per_tok
         cuda = x.is_cuda
-        logits = ops.linear(x, layer.router, None, out_dtype=torch.float32,
-                            out=self._buf("rlogits", (T, layer.router.shape[0]), torch.float32) if cuda else None)
         ids = self._buf("ids", (T * k,), torch.int32).view(T, k) if cuda else torch.empty(T, k, dtype=torch.int32)
         w = self._buf("topw", (T * k,), torch.float32).view(T, k) if cuda else torch.empty(T, k)
+        if cuda and a.num_experts <= 128 and layer.router.dtype == torch.bfloat16:
+            ops.router_fused(x, layer.router, a.num_experts, k, a.norm_topk_prob, ids, w, counts)
+            return ids, w
+        logits = ops.linear(x, layer.router, None, out_dtype=torch.float32,
+                            out=self._buf("rlogits", (T, layer.router.shape[0]), torch.float32) if cuda else None)
         ops.router_topk(logits, a.num_experts, k, a.norm_topk_prob, ids, w, counts)
         return ids, w
 

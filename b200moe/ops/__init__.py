@@ -189,6 +189,26 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
     return out
 
 
+def linear_add_rmsnorm(x, weight, scale, residual, norm_w, eps, out):
+    """residual += bf16(x @ W^T); return rmsnorm(residual) * norm_w.  When the
+    planner splits K, the fp32 partial sums go straight into the norm kernel
+    (no separate reduce launch, no bf16 round trip through memory)."""
+    T, N = x.shape[0], weight.shape[0]
+    if not x.is_cuda or T == 0:
+        return rmsnorm(linear(x, weight, scale), norm_w, eps, residual=residual, out=out)
+    m_tiles = N // 128
+    bn, splits = plan_dense(T, m_tiles, x.shape[1] // 64, fp8=scale is not None)
+    if splits == 1:
+        return rmsnorm(linear(x, weight, scale), norm_w, eps, residual=residual, out=out)
+    C = native()
+    part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
+    C.gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, m_tiles,
+           0, 0, None, None, status_word(x.device), _trace[0], splits, T * N)
+    C.rmsnorm_partials(part, splits, residual, norm_w, out, eps)
+    count_launches(2)
+    return out
+
+
 def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn: int | None = None):
     """out[r] = silu(x_perm[r] @ Wg_e^T) * (x_perm[r] @ Wu_e^T) for the rows of expert e."""
     C = native()
@@ -316,6 +336,13 @@ def router_topk(logits, num_experts, topk, renorm, ids, weights, counts=None):
     count_launches()
 
 
+def router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts=None):
+    """Router GEMM + softmax + top-k in one native launch (num_experts <= 128);
+    same rounding points as ``linear`` + ``router_topk``."""
+    native().router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts)
+    count_launches()
+
+
 def moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out=None):
     native().moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out)
     count_launches()
@@ -329,7 +356,7 @@ def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len,
     part_o, part_m, part_l = workspace
     native().decode_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, block_tables, seq_lens,
                          out, part_o, part_m, part_l, kv_layer.block_size, kv_layer.block_stride,
-                         kv_layer.num_kv_heads, scale, num_splits, split_len)
+                         kv_layer.num_kv_heads, scale, num_splits, split_len, status_word(q.device))
     count_launches(2 if num_splits > 1 else 1)
     return out
 

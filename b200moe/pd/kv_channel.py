@@ -164,11 +164,12 @@ def export_pool_handle(pool) -> dict:
     if not pool.data.is_cuda:
         raise RuntimeError("NVLink KV transfer needs a CUDA pool")
 
+    from b200moe import ops
+    C = ops.native()
+
     def one(t: torch.Tensor) -> dict:
-        st = t.untyped_storage()
-        info = st._share_cuda_()
-        handle, storage_offset = info[1], info[3]
-        return {"handle": bytes(handle).hex(), "offset": int(storage_offset) + t.storage_offset() * t.element_size(),
+        handle, offset = C.ipc_export(t.data_ptr(), t.device.index)
+        return {"handle": bytes(handle.numpy()).hex(), "offset": int(offset),
                 "block_bytes": t[0].numel() * t.element_size(), "blocks": t.shape[0]}
     out = {"device": pool.data.device.index, "data": one(pool.data)}
     if pool.scales is not None:

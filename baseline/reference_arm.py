@@ -110,7 +110,8 @@ def unavailable(why: str) -> int:
     return 0
 
 
-def run(args, prompts, metric: str) -> int:
+def run(args, prompts_for, metric: str) -> int:
+    """``prompts_for(i)``: the prompts of pass i (fresh for every pass, like the main arm)."""
     if args.gpus > 4:
         return unavailable("reference asserts num_kv_heads % tp == 0 (nanovllm/models/qwen3.py:34); "
                            "Qwen3-30B-A3B has 4 KV heads, so 8 GPUs cannot run")
@@ -136,17 +137,21 @@ def run(args, prompts, metric: str) -> int:
               max_num_batched_tokens=args.max_num_batched_tokens,
               max_model_len=args.input_len + args.output_len + 16, kvcache_block_size=256,
               moe_backend="grouped_mm", attention_backend="triton_paged", scheduler_policy=args.scheduler_policy,
-              enforce_eager=args.enforce_eager)
+              # eager: the reference's production setting (its deploy/serve.env.example and
+              # scripts/p2_benchmark.py run enforce_eager); its CUDA-graph capture raises
+              # cudaErrorStreamCaptureUnsupported on this platform
+              enforce_eager=True)
     init_s = time.perf_counter() - t0
     sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)
-    for _ in range(args.warmup):
-        llm.generate(prompts, sp, use_tqdm=False)
+    for i in range(args.warmup):
+        llm.generate(prompts_for(i), sp, use_tqdm=False)
+    timed = [prompts_for(args.warmup + i) for i in range(args.steps)]
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     t0 = time.perf_counter()
     total = 0
-    for _ in range(args.steps):
+    for prompts in timed:
         outs = llm.generate(prompts, sp, use_tqdm=False)
         total += sum(len(o["token_ids"]) for o in outs)
     b.record()
@@ -162,7 +167,7 @@ def run(args, prompts, metric: str) -> int:
             "data": "synthetic uniform-random token ids; random-init fp8 checkpoint written at run time",
             "config": {"model": args.model, "global_batch": args.num_requests, "seq_len": args.input_len,
                        "output_len": args.output_len, "parallelism": f"tp{args.gpus}/ep{args.gpus}",
-                       "moe_backend": "grouped_mm", "attention_backend": "triton_paged",
+                       "moe_backend": "grouped_mm", "attention_backend": "triton_paged", "enforce_eager": True,
                        "ckpt_write_s": round(write_s, 1), "init_s": round(init_s, 1)},
             "e2e": {"value": round(total / wall, 1), "unit": "tok/s", "wall_s_per_pass": round(wall / args.steps, 2)}}
     if ttft:

@@ -54,8 +54,10 @@ def parse():
     return p.parse_args()
 
 
-def workload(args):
-    rng = random.Random(args.seed)
+def workload(args, pass_index: int = 0):
+    """Uniform-random prompts; every pass (warm-up or timed) draws its own, so no
+    pass reuses another's prompt KV through the prefix cache."""
+    rng = random.Random(args.seed * 1_000_003 + pass_index)
     vocab = 151936
     return [[rng.randrange(vocab) for _ in range(args.input_len)] for _ in range(args.num_requests)]
 
@@ -66,7 +68,7 @@ METRIC = "output tok/s (Qwen3-30B-A3B FP8, EP8, 256 concurrent) + p50 TTFT/TPOT"
 def reference_arm(args, store=None):
     sys.path.insert(0, os.path.join(ROOT, "baseline"))
     import reference_arm as ref
-    rc = ref.run(args, workload(args), METRIC)
+    rc = ref.run(args, lambda i: workload(args, i), METRIC)
     if store is not None:
         store.set("driver_done", "1")
     return rc
@@ -89,7 +91,6 @@ def main():
     from b200moe import LLM, SamplingParams, ops
     from b200moe.utils.gpu_clock import ClockSampler
 
-    prompts = workload(args)
     sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)
     t_init = time.perf_counter()
     llm = LLM(args.model, tensor_parallel_size=args.gpus, max_num_seqs=max(args.num_requests, 1),
@@ -99,8 +100,9 @@ def main():
               scheduler_overlap=bool(args.scheduler_overlap), random_init="seeded")
     init_s = time.perf_counter() - t_init
     runners = llm.executor
-    for _ in range(args.warmup):
-        llm.generate(prompts, sp, use_tqdm=False)
+    for i in range(args.warmup):
+        llm.generate(workload(args, i), sp, use_tqdm=False)
+    timed_prompts = [workload(args, args.warmup + i) for i in range(args.steps)]  # built before the clock starts
     torch.cuda.synchronize()
     ops.reset_launch_count()
     runners.call("reset_step_timing")
@@ -110,12 +112,13 @@ def main():
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         total_out = 0
-        for _ in range(args.steps):
+        for prompts in timed_prompts:
             outs = llm.generate(prompts, sp, use_tqdm=False)
             total_out += sum(len(o["token_ids"]) for o in outs)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     dev_ms = max(runners.call_all("step_device_ms"))
+    split = runners.call("step_device_split")  # rank 0: where the device time goes
     launches = sum(runners.call_all("launch_count"))
     nsteps = llm.step_count - steps0
     h2d = (runners.runner.h2d_bytes - h2d0) / max(nsteps, 1)
@@ -132,8 +135,10 @@ def main():
         "config": {"model": args.model, "global_batch": args.num_requests, "seq_len": args.input_len,
                    "output_len": args.output_len, "parallelism": f"ep{args.gpus}+{args.attention_parallel}{args.gpus}-attn",
                    "l2": "inputs larger than L2 (30 GB of weights per pass), no flush",
+                   "prompts": "fresh uniform-random prompts every pass (no cross-pass prefix-cache hits)",
                    "scheduler_overlap": bool(args.scheduler_overlap),
-                   "engine_steps_per_pass": nsteps // max(args.steps, 1), "init_s": round(init_s, 1)},
+                   "engine_steps_per_pass": nsteps // max(args.steps, 1), "init_s": round(init_s, 1),
+                   "device_ms_split_rank0": {k: round(v, 1) if isinstance(v, float) else v for k, v in split.items()}},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "wall_s_per_pass": round(wall / args.steps, 3)},
         "gpu_launches": int(launches),

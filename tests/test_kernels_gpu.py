@@ -78,6 +78,22 @@ def test_fp8_dequant_bit_exact():
     assert not bad, f"{len(bad)} mismatches (m, k, code, scale, got, want): {detail}"
 
 
+@pytest.mark.parametrize("T", [1, 64, 256])
+def test_linear_add_rmsnorm_fused_equals_separate(T):
+    """o_proj + residual + RMSNorm: split-K partials reduced inside the norm
+    kernel give the same bits as the separate reduce + rmsnorm."""
+    n, k = 2048, 4096
+    q, s = _fp8_weight(1, n, k, 11)
+    x = (torch.randn(T, k, device=DEV) * 0.5).to(torch.bfloat16)
+    res = (torch.randn(T, n, device=DEV)).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(n, device=DEV)).to(torch.bfloat16)
+    r1, r2 = res.clone(), res.clone()
+    a = ops.linear_add_rmsnorm(x, q[0], s[0], r1, nw, 1e-6, out=torch.empty_like(res))
+    b = ops.rmsnorm(ops.linear(x, q[0], s[0]), nw, 1e-6, residual=r2, out=torch.empty_like(res))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(r1, r2)
+
+
 @pytest.mark.parametrize("T", [3, 200])
 def test_gemm_bf16_f32_out(T):
     w = (torch.randn(256, 2048, device=DEV) * 0.02).to(torch.bfloat16)
@@ -86,7 +102,7 @@ def test_gemm_bf16_f32_out(T):
     _close(out, x.float() @ w.float().t(), tol=1e-2)
 
 
-@pytest.mark.parametrize("bn", [16, 32, 128])
+@pytest.mark.parametrize("bn", [16, 32, 64, 128, 256])
 def test_grouped_gate_up_and_down(bn):
     E, I, H = 8, 128, 256
     torch.manual_seed(0)
@@ -98,7 +114,7 @@ def test_grouped_gate_up_and_down(bn):
     q2, s2 = _fp8_weight(E, H, I, 3)
     x = (torch.randn(rows, H, device=DEV) * 0.5).to(torch.bfloat16)
     h = torch.empty(rows, I, dtype=torch.bfloat16, device=DEV)
-    ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I, bn=bn)
+    ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I, bn=min(bn, 128))  # the gate/up pair tile is at most 128 tokens
     slot_of_row = torch.randperm(rows, device=DEV).to(torch.int32)
     wts = torch.rand(rows, device=DEV)
     slots = torch.zeros(rows, H, dtype=torch.bfloat16, device=DEV)
@@ -189,6 +205,30 @@ def test_router_topk():
     assert (ids.cpu().sort(dim=1).values == ids_c.sort(dim=1).values).float().mean() > 0.95
     torch.testing.assert_close(w.cpu().sort(dim=1).values, w_c.sort(dim=1).values, atol=1e-2, rtol=1e-2)
     assert int(counts.sum()) == T * k and int(counts.max()) <= T
+
+
+@pytest.mark.parametrize("T", [1, 77, 300])
+def test_router_fused_matches_gemm_and_topk(T):
+    """One-launch router (GEMM + softmax + top-k) against the fp32 reference of
+    the same rounding points: bf16(x . w^T) logits, softmax, top-k, renorm."""
+    E, k, H = 128, 8, 2048
+    x = (torch.randn(T, H, device=DEV) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(E, H, device=DEV) * 0.05).to(torch.bfloat16)
+    ids = torch.empty(T, k, dtype=torch.int32, device=DEV)
+    wt = torch.empty(T, k, device=DEV)
+    counts = torch.zeros(E, dtype=torch.int32, device=DEV)
+    ops.router_fused(x, w, E, k, True, ids, wt, counts)
+    torch.cuda.synchronize()
+    logits = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+    p = torch.softmax(logits, dim=-1)
+    pg = p.gather(1, ids.long()).sort(dim=1, descending=True).values
+    pr = p.topk(k, dim=-1).values
+    # fp32 summation order differs from the reference matmul: compare the chosen
+    # probabilities (ties and 1-ulp logit differences may swap equal-valued experts)
+    torch.testing.assert_close(pg, pr, atol=2e-3, rtol=2e-2)
+    want_w = (pr / pr.sum(-1, keepdim=True)).to(torch.bfloat16).float()
+    torch.testing.assert_close(wt.sort(dim=1, descending=True).values, want_w, atol=1e-2, rtol=2e-2)
+    assert int(counts.sum()) == T * k
 
 
 def test_moe_permute():

@@ -38,6 +38,11 @@ def test_pd_handoff_matches_collocated(tmp_path, transport):
     try:
         res = run_client("127.0.0.1", p_port, [{"req_id": i, "prompt": p, "max_tokens": 9}
                                                for i, p in enumerate(prompts)], timeout_s=180)
+        if sorted(res) != [0, 1, 2, 3]:
+            for f in logs:
+                f.flush()
+            tails = {n: (tmp_path / n).read_text()[-3000:] for n in ("decode.log", "prefill.log")}
+            pytest.fail(f"missing results {sorted(res)}; role logs: {tails}")
         assert [res[i]["tokens"] for i in range(4)] == want
         assert pre.wait(120) == 0 and dec.wait(120) == 0
     finally:
