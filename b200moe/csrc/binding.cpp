@@ -487,7 +487,7 @@ void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor>
 void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
                   c10::optional<Tensor> v_scale, Tensor cu_seqlens_q, Tensor seq_lens, Tensor block_tables,
                   Tensor out, int64_t max_q_len, int64_t block_size, int64_t block_stride, int64_t num_kv_heads,
-                  double scale) {
+                  double scale, c10::optional<Tensor> status) {
   CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_DT(q, torch::kBFloat16);
   CHECK_DT(cu_seqlens_q, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_DT(block_tables, torch::kInt32);
   CHECK_CONTIG(block_tables); CHECK_CONTIG(cu_seqlens_q);
@@ -511,6 +511,8 @@ void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor
   a.head_dim = D;
   a.scale = (float)scale;
   a.out = out.data_ptr();
+  a.num_blocks = (int)k_cache.size(0);
+  a.status = ptr_or_null<int>(status);
   b200::paged_prefill_attn(a, B, (int)max_q_len, stream());
 }
 

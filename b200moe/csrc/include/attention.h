@@ -49,9 +49,15 @@ struct PrefillArgs {
   int head_dim;
   float scale;
   void* out;                 // [T, q_heads, D] bf16
+  int num_blocks;            // blocks in the pool (tensor-core path: out-of-range block = zero fill)
+  int* status;               // device status word (bounded waits), may be null
 };
 
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s);
 void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t s);
+
+// tcgen05 causal prefill (kernels/fmha_tc.cu): bf16 pool, head_dim 128.
+bool fmha_prefill_supported(const PrefillArgs& a, int* sub_rows);
+void fmha_prefill(const PrefillArgs& a, int B, int max_q_len, int sub_rows, cudaStream_t s);
 
 }  // namespace b200

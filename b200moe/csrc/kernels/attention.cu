@@ -924,6 +924,11 @@ void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t
   if (B == 0 || max_q_len == 0) return;
   if (a.group > 16 || 64 % a.group) throw std::runtime_error("prefill attention: GQA group must divide 64");
   if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("prefill attention: int8 KV needs scales");
+  int sub_rows = 0;
+  if (fmha_prefill_supported(a, &sub_rows)) {
+    fmha_prefill(a, B, max_q_len, sub_rows, s);
+    return;
+  }
   const int QPB = 64 / a.group;
   dim3 grid((max_q_len + QPB - 1) / QPB, a.num_kv_heads, B);
   if (a.head_dim == 128) {

@@ -115,7 +115,7 @@ def fp8_weight(groups, n, k, seed=0):
     return torch.stack(qs), torch.stack(ss)
 
 
-def case_moe(T, iters, E=128, k=8, H=2048, I=768):
+def case_moe(T, iters, E=128, k=8, H=2048, I=768, only=""):
     q13, s13 = fp8_weight(E, 2 * I, H, 1)
     q2, s2 = fp8_weight(E, H, I, 2)
     rows = T * k
@@ -129,10 +129,13 @@ def case_moe(T, iters, E=128, k=8, H=2048, I=768):
     sor = torch.randperm(rows, device="cuda").to(torch.int32)
     w = torch.rand(rows, device="cuda")
     used = int((counts > 0).sum())
-    ms = timeit(lambda: ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I), iters)
-    wbytes = used * 2 * I * H + rows * H * 2 + rows * I * 2
-    report("moe_gate_up_silu", ms, wbytes, 2 * rows * H * 2 * I, tokens=T,
-           bn=ops.pick_bn(rows, I // 128, E, pair=True))
+    if only != "down":
+        ms = timeit(lambda: ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I), iters)
+        wbytes = used * 2 * I * H + rows * H * 2 + rows * I * 2
+        report("moe_gate_up_silu", ms, wbytes, 2 * rows * H * 2 * I, tokens=T,
+               bn=ops.pick_bn(rows, I // 128, E, pair=True))
+    if only == "gate_up":
+        return
     ms = timeit(lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots), iters)
     wbytes = used * H * I + rows * I * 2 + rows * H * 2
     report("moe_down_scatter", ms, wbytes, 2 * rows * I * H, tokens=T, bn=ops.pick_bn(rows, H // 128, E))
@@ -243,6 +246,11 @@ def _trace_summary(name, buf):
             d["us_issue_to_mma"] = med([mma[i] - issue[i] for i in idx])
     e0, e1 = by.get(4, {}), by.get(5, {})
     tiles = sorted(set(e0) & set(e1))
+    allt = [t for r in by.values() for t in r.values()]
+    if allt:
+        d["us_cta0_span"] = round((max(allt) - min(allt)) / 1e3, 2)
+    if len(tiles) > 2:
+        d["us_per_tile"] = med([e0[b] - e0[a] for a, b in zip(tiles, tiles[1:])])
     if tiles:
         d["tiles"] = len(tiles)
         d["us_epilogue"] = med([e1[i] - e0[i] for i in tiles])
@@ -273,16 +281,21 @@ def case_trace(T):
     offsets[1:] = torch.cumsum(counts, 0)
     xm = (torch.randn(rows, H, device="cuda") * 0.5).to(torch.bfloat16)
     h = torch.empty(rows, I, dtype=torch.bfloat16, device="cuda")
-    fn = lambda: ops.grouped_gate_up_silu(xm, q13, s13, counts, offsets, h, I)
-    fn()
-    torch.cuda.synchronize()
-    buf.zero_()
-    ops.set_gemm_trace(buf)
-    flush_l2()
-    fn()
-    torch.cuda.synchronize()
-    ops.set_gemm_trace(None)
-    _trace_summary("moe_gate_up", buf.cpu())
+    q2, s2 = fp8_weight(E, H, I, 2)
+    slots = torch.empty(rows, H, dtype=torch.bfloat16, device="cuda")
+    sor = torch.randperm(rows, device="cuda").to(torch.int32)
+    w = torch.rand(rows, device="cuda")
+    for name, fn in (("moe_gate_up", lambda: ops.grouped_gate_up_silu(xm, q13, s13, counts, offsets, h, I)),
+                     ("moe_down", lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots))):
+        fn()
+        torch.cuda.synchronize()
+        buf.zero_()
+        ops.set_gemm_trace(buf)
+        flush_l2()
+        fn()
+        torch.cuda.synchronize()
+        ops.set_gemm_trace(None)
+        _trace_summary(name, buf.cpu())
 
 
 def main():
@@ -294,10 +307,11 @@ def main():
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--splits", type=int, default=0, help="decode: force this many KV splits (0 = heuristic)")
     p.add_argument("--pool-layers", type=int, default=2, help="decode: layers per KV block slab")
+    p.add_argument("--only", choices=["", "gate_up", "down"], default="", help="moe: time one of the two GEMMs")
     a = p.parse_args()
     torch.cuda.set_device(0)
     if a.case in ("moe", "all"):
-        case_moe(a.tokens, a.iters)
+        case_moe(a.tokens, a.iters, only=a.only)
     if a.case in ("dense", "all"):
         case_dense(a.tokens, a.iters)
     if a.case in ("decode", "all"):

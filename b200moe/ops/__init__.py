@@ -366,7 +366,7 @@ def prefill_attention(q, kv_layer, cu_seqlens_q, seq_lens, block_tables, max_q_l
         return _attention_ref(q, kv_layer, block_tables, seq_lens, cu_seqlens_q, scale, out)
     native().prefill_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, cu_seqlens_q, seq_lens,
                           block_tables, out, max_q_len, kv_layer.block_size, kv_layer.block_stride,
-                          kv_layer.num_kv_heads, scale)
+                          kv_layer.num_kv_heads, scale, status_word(q.device))
     count_launches()
     return out
 

@@ -315,6 +315,37 @@ def test_prefill_attention(D, nq, nkv, bs, int8):
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("bs", [16, 64, 128, 256])
+@pytest.mark.parametrize("nq,nkv", [(32, 4), (16, 4), (64, 4), (8, 8)])
+def test_prefill_attention_tensor_core(bs, nq, nkv, monkeypatch):
+    """tcgen05 prefill kernel (head_dim 128, bf16 KV) against the fp32 reference
+    and against the mma.sync kernel: long prompts, prefix hits, ragged tails."""
+    D = 128
+    shapes = [(700, 700), (300, 1000), (129, 129), (1, 257), (17, 17), (128, 383)]
+    seq_lens = [L for _, L in shapes]
+    nblocks = sum(math.ceil(L / bs) for L in seq_lens) + 2
+    pool = _pool(nblocks, bs, nkv, D)
+    tables = _fill_pool(pool, seq_lens, bs, nkv, D)
+    cu = [0]
+    for qn, _ in shapes:
+        cu.append(cu[-1] + qn)
+    T = cu[-1]
+    q = torch.randn(T, nq, D, device=DEV).to(torch.bfloat16)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    lens = torch.tensor(seq_lens, dtype=torch.int32, device=DEV)
+    mq = max(s for s, _ in shapes)
+    out_tc = torch.full((T, nq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.prefill_attention(q, pool.layer(1), cu_t, lens, tables, mq, D ** -0.5, out_tc)
+    ops.check_status(DEV)
+    monkeypatch.setenv("B200MOE_PREFILL_TC", "0")
+    out_mma = torch.empty_like(out_tc)
+    ops.prefill_attention(q, pool.layer(1), cu_t, lens, tables, mq, D ** -0.5, out_mma)
+    ref = torch.empty(T, nq, D, device=DEV)
+    ops._attention_ref(q, pool.layer(1), tables, lens, cu_t, D ** -0.5, ref)
+    torch.testing.assert_close(out_tc.float(), ref, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(out_tc.float(), out_mma.float(), atol=2e-2, rtol=2e-2)
+
+
 def test_argmax_and_sampler():
     B, V = 6, 151936
     logits = torch.randn(B, V, device=DEV)
