@@ -328,6 +328,11 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
 // by row) into the warp-level bf16 MMA with fp32 accumulation; the logits go
 // through shared memory to one warp per token for the top-k.
 constexpr int kRtTok = 16, kRtE = 128, kRtK = 64;
+// K chunks in flight: a CTA streams the whole router weight (E x H bf16), so the
+// ring must cover the load latency (two stages left each chunk waiting a round trip)
+constexpr int kRtStages = 8;
+constexpr int kRtChunkBytes = (kRtTok + kRtE) * 128;
+constexpr int kRtSmem = kRtStages * kRtChunkBytes + kRtTok * (kRtE + 1) * 4;
 
 __device__ __forceinline__ uint32_t rt_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
@@ -339,14 +344,15 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const bf16* __restric
                                                            int T, int H, int E, int topk, int renorm,
                                                            int* __restrict__ ids, float* __restrict__ weights,
                                                            int* __restrict__ counts) {
-  constexpr int XB = kRtTok * 128, WB = kRtE * 128;  // bytes of one x / W chunk
-  __shared__ __align__(128) uint8_t ring[2][XB + WB];
-  __shared__ float logit[kRtTok][kRtE + 1];
+  constexpr int XB = kRtTok * 128;  // bytes of one x chunk (the W chunk follows it)
+  extern __shared__ __align__(128) uint8_t rt_smem[];
+  uint8_t* ring = rt_smem;          // [kRtStages][kRtChunkBytes]
+  float(*logit)[kRtE + 1] = reinterpret_cast<float(*)[kRtE + 1]>(rt_smem + kRtStages * kRtChunkBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRtTok;
   const int nchunks = H / kRtK;
   auto load = [&](int c, int buf) {
-    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(ring[buf]));
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(ring + buf * kRtChunkBytes));
     for (int i = threadIdx.x; i < (kRtTok + kRtE) * 8; i += 256) {
       const int row = i >> 3, u = i & 7;
       if (row < kRtTok) {
@@ -364,13 +370,17 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const bf16* __restric
   for (int n = 0; n < 2; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-  load(0, 0);
-  for (int c = 0; c < nchunks; ++c) {
-    if (c + 1 < nchunks) load(c + 1, (c + 1) & 1);
+  for (int c = 0; c < kRtStages - 1; ++c) {
+    if (c < nchunks) load(c, c);
     else asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncthreads();
-    const uint32_t xs = static_cast<uint32_t>(__cvta_generic_to_shared(ring[c & 1]));
+  }
+  for (int c = 0; c < nchunks; ++c) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kRtStages - 2) : "memory");
+    __syncthreads();  // chunk c landed for every thread; chunk c-1's buffer is free
+    const int nc = c + kRtStages - 1;
+    if (nc < nchunks) load(nc, nc % kRtStages);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t xs = static_cast<uint32_t>(__cvta_generic_to_shared(ring + (c % kRtStages) * kRtChunkBytes));
     const uint32_t ws = xs + XB;
 #pragma unroll
     for (int ks = 0; ks < kRtK / 16; ++ks) {
@@ -396,8 +406,8 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const bf16* __restric
                    : "+f"(acc[1][0]), "+f"(acc[1][1]), "+f"(acc[1][2]), "+f"(acc[1][3])
                    : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b2), "r"(b3));
     }
-    __syncthreads();
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
   for (int n = 0; n < 2; ++n)
 #pragma unroll
@@ -586,8 +596,13 @@ void router_fused(const void* x, const void* w, int T, int H, int E, int topk, b
   if (T == 0) return;
   if (E > kRtE || topk < 1 || topk > 8 || H % kRtK)
     throw std::runtime_error("router_fused: needs <= 128 experts, top-k in [1, 8], hidden % 64 == 0");
-  router_fused_kernel<<<(T + kRtTok - 1) / kRtTok, 256, 0, s>>>((const bf16*)x, (const bf16*)w, T, H, E, topk,
-                                                                 renorm ? 1 : 0, ids, weights, counts);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(router_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem);
+    attr = true;
+  }
+  router_fused_kernel<<<(T + kRtTok - 1) / kRtTok, 256, kRtSmem, s>>>((const bf16*)x, (const bf16*)w, T, H, E,
+                                                                       topk, renorm ? 1 : 0, ids, weights, counts);
   check_launch("router_fused");
 }
 

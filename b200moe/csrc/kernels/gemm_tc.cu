@@ -56,7 +56,14 @@ struct GemmCfg {
   static constexpr int NA = PAIR ? 2 : 1;
   static constexpr int CONV_WARPS = AFP8 ? 16 : 0;    // one 16-byte chunk per lane of a 128x64 e4m3 tile
   static constexpr int EPI_WARP0 = 2 + CONV_WARPS;
-  static constexpr int THREADS = (EPI_WARP0 + 4) * 32;
+  // token tiles of 64+ (prefill): eight epilogue warps (two per TMEM lane quarter)
+  // that transpose each 16-column chunk through shared memory and write 16-byte
+  // pieces of output rows; decode-size tiles keep four warps and direct stores,
+  // whose shared memory goes to load stages instead
+  static constexpr bool EPI_STAGED = BN >= 64;
+  static constexpr int EPI_WARPS = EPI_STAGED ? 8 : 4;
+  static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+  static constexpr int EPI_STAGE = EPI_STAGED ? EPI_WARPS * 16 * 32 * 4 : 0;  // per warp: 16 cols x 32 rows x 4 B
   static constexpr int A16_BYTES = 128 * kBK * 2;     // 16 KB bf16 tile
   static constexpr int A8_BYTES = 128 * kBK;          // 8 KB e4m3 tile
   static constexpr int B_BYTES = BN * kBK * 2;
@@ -73,9 +80,9 @@ struct GemmCfg {
 
   static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
   static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
-  static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES - EPI_STAGE) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + CONV_BYTES + EXTRA + 1024;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + CONV_BYTES + EPI_STAGE + EXTRA + 1024;
   // dequantiser warp groups taking stages round robin: never more groups than
   // load stages or bf16 slots (a group waits on its own stage and slot)
   static constexpr int DEQ_GROUPS = !AFP8 ? 1 : (STAGES >= 4 && CONV_SLOTS >= 4) ? 4 : 2;
@@ -121,7 +128,8 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, 
 }
 
 // Pipeline trace (debug/profiling): role 0 TMA issued, 1 dequant start, 2 dequant
-// done, 3 MMA issue, 4 accumulator ready (epilogue start), 5 epilogue done.
+// done, 3 MMA issue, 4 accumulator ready (epilogue start), 5 epilogue done,
+// 6 e4m3 tile landed (seen by the dequantiser).
 __device__ __forceinline__ void trace_ev(const GemmArgs& a, int role, int idx) {
   if (a.trace == nullptr || blockIdx.x != 0) return;
   const unsigned long long n = atomicAdd(a.trace, 1ull);
@@ -178,7 +186,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   // ---- shared-memory carve-up
   uint8_t* stage_base = smem;
   uint8_t* conv_base = smem + C::STAGES * C::STAGE_BYTES;
-  uint8_t* extra = conv_base + C::CONV_BYTES;
+  uint8_t* epi_stage = conv_base + C::CONV_BYTES;            // [EPI_WARPS][16][32] 4-byte transpose buffers
+  uint8_t* extra = epi_stage + C::EPI_STAGE;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);   // [12] TMA landed
   uint64_t* empty_bar = full_bar + 12;                       // [12] load slot free
   uint64_t* cfull_bar = empty_bar + 12;                      // [4] bf16 slot written
@@ -241,7 +250,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 4);
+      mbar_init(&acce_bar[b], C::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -391,8 +400,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         for (int a = 0; a < C::NA; ++a) scale[a] = next_scale[a];
         for (int i = 0; i < kGroups && have; ++i) have = advance();
         if (have) load_scales(next_scale);  // the group's next stage, fetched during this one
-        const bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag) &&
-                          mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
+        bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag);
+        if (tracer) trace_ev(args, 6, gi);  // the e4m3 tile has landed
+        w_ok = w_ok && mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
         if (!__all_sync(0xffffffffu, w_ok)) break;
         if (tracer) trace_ev(args, 1, gi);
         uint4 q[C::NA][CPL];
@@ -428,9 +438,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     }
   } else {
     // ====================================================== epilogue
+    // EPI_WARPS warps; warp w reads TMEM lane quarter (w & 3) and the two warps of
+    // a quarter take alternate 16-column chunks.  A chunk (32 output features x 16
+    // tokens) is transposed through a per-warp shared buffer so every lane writes
+    // 16 contiguous bytes of one output row instead of one 2-byte value per column.
+    constexpr int ET = C::EPI_WARPS * 32;
     const int q = warp & 3;              // TMEM lane quarter this warp may access
-    const int m_local = q * 32 + lane;
-    const int et = threadIdx.x - C::EPI_WARP0 * 32;  // 0..127
+    const int ew = warp - C::EPI_WARP0;
+    constexpr int CSTEP = C::EPI_WARPS / 4;
+    const int chunk0 = ew >> 2;          // first 16-column chunk of this warp
+    const int et = threadIdx.x - C::EPI_WARP0 * 32;
+    uint8_t* stg = epi_stage + ew * (16 * 32 * 4);
     int lt = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++lt) {
@@ -444,25 +462,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       float* mw = meta_w + abuf * 256;
       if constexpr (EPI == kEpiScatter) {
         // stage the tile's scatter slots and routing weights once (while the MMAs run)
-        for (int col = et; col < ncols; col += 128) {
+        for (int col = et; col < ncols; col += ET) {
           const int slot = args.slot_of_row[row0 + col];
           mslot[col] = slot;
           mw[col] = args.peer_scatter ? args.slot_weight[row0 + col] : args.slot_weight[slot];
         }
       }
       // one thread waits for the accumulator, the verdict is broadcast so the
-      // four warps always leave (or continue) together
+      // epilogue warps always leave (or continue) together
       if (et == 0) {
         epi_ok[0] = mbar_wait(&accf_bar[abuf], aphase, status, kStatusTimeoutAccFull, abort_flag) ? 1 : 0;
         trace_ev(args, 4, lt);
       }
-      named_barrier_sync(2, 128);
+      named_barrier_sync(2, ET);
       if (!epi_ok[0]) { ok = false; break; }
       tc_fence_after();
       const uint32_t t_base = tmem_base + (uint32_t(q * 32) << 16) + abuf * C::ACC_COLS;
-      const int m_out = tc.i * 128 + m_local;
+      const int m0 = tc.i * 128 + q * 32;  // first output feature of this warp's rows
 #pragma unroll 1
-      for (int c16 = 0; c16 < BN / 16; ++c16) {
+      for (int c16 = chunk0; c16 < BN / 16; c16 += CSTEP) {
         if (c16 * 16 >= ncols) break;
         float v[16];
         tmem_ld16(t_base + c16 * 16, v);
@@ -471,43 +489,69 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           tmem_ld16(t_base + BN + c16 * 16, u);
           tmem_ld_wait();
 #pragma unroll
-          for (int n = 0; n < 16; ++n) {
-            const int col = c16 * 16 + n;
-            if (col < ncols) {
-              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-              out[(size_t)(row0 + col) * args.ld_out + m_out] = __float2bfloat16(silu(v[n]) * u[n]);
-            }
-          }
+          for (int n = 0; n < 16; ++n) v[n] = silu(v[n]) * u[n];
         } else {
           tmem_ld_wait();
+        }
+        if constexpr (EPI == kEpiScatter) {
+#pragma unroll
+          for (int n = 0; n < 16; ++n) v[n] *= mw[c16 * 16 + n];
+        }
+        // first element of output row `col` (this tile's features start at m0)
+        auto row_ptr = [&](int col) -> void* {
+          if constexpr (EPI == kEpiF32) {
+            return reinterpret_cast<float*>(args.out) + (size_t)tc.sp * args.split_stride +
+                   (size_t)(row0 + col) * args.ld_out + (size_t)tc.g * args.out_group_stride + m0;
+          } else if constexpr (EPI == kEpiScatter) {
+            const int code = mslot[col];
+            if (args.peer_scatter)  // the row goes to its source rank's slots (peer memory)
+              return reinterpret_cast<__nv_bfloat16*>(args.peer_out[code / args.slot_cap]) +
+                     (size_t)(code % args.slot_cap) * args.ld_out + m0;
+            return reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)code * args.ld_out + m0;
+          } else if constexpr (EPI == kEpiSiluPair) {
+            return reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)(row0 + col) * args.ld_out + m0;
+          } else {
+            return reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)(row0 + col) * args.ld_out +
+                   (size_t)tc.g * args.out_group_stride + m0;
+          }
+        };
+        if constexpr (!C::EPI_STAGED) {
 #pragma unroll
           for (int n = 0; n < 16; ++n) {
             const int col = c16 * 16 + n;
             if (col < ncols) {
-              const int row = row0 + col;
-              const int m_glob = tc.g * args.out_group_stride + m_out;
-              if constexpr (EPI == kEpiBf16) {
-                __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-                out[(size_t)row * args.ld_out + m_glob] = __float2bfloat16(v[n]);
-              } else if constexpr (EPI == kEpiF32) {
-                float* out = reinterpret_cast<float*>(args.out) + (size_t)tc.sp * args.split_stride;
-                out[(size_t)row * args.ld_out + m_glob] = v[n];
-              } else {  // kEpiScatter
-                const int code = mslot[col];
-                __nv_bfloat16* out;
-                size_t r;
-                if (args.peer_scatter) {  // the row goes to its source rank's slots (peer memory)
-                  out = reinterpret_cast<__nv_bfloat16*>(args.peer_out[code / args.slot_cap]);
-                  r = (size_t)(code % args.slot_cap);
-                } else {
-                  out = reinterpret_cast<__nv_bfloat16*>(args.out);
-                  r = (size_t)code;
-                }
-                out[r * args.ld_out + m_out] = __float2bfloat16(v[n] * mw[col]);
-              }
+              if constexpr (EPI == kEpiF32) reinterpret_cast<float*>(row_ptr(col))[lane] = v[n];
+              else reinterpret_cast<__nv_bfloat16*>(row_ptr(col))[lane] = __float2bfloat16(v[n]);
             }
           }
+        } else if constexpr (EPI == kEpiF32) {
+          float* s32 = reinterpret_cast<float*>(stg);
+#pragma unroll
+          for (int n = 0; n < 16; ++n) s32[n * 32 + lane] = v[n];
+          __syncwarp();
+#pragma unroll
+          for (int rd = 0; rd < 4; ++rd) {  // 16 columns x 8 four-float pieces
+            const int idx = rd * 32 + lane, n = idx >> 3, piece = idx & 7;
+            const int col = c16 * 16 + n;
+            if (col < ncols)
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(row_ptr(col)) + piece * 4) =
+                  *reinterpret_cast<const float4*>(s32 + n * 32 + piece * 4);
+          }
+        } else {
+          __nv_bfloat16* s16 = reinterpret_cast<__nv_bfloat16*>(stg);
+#pragma unroll
+          for (int n = 0; n < 16; ++n) s16[n * 32 + lane] = __float2bfloat16(v[n]);
+          __syncwarp();
+#pragma unroll
+          for (int rd = 0; rd < 2; ++rd) {  // 16 columns x 4 eight-value pieces
+            const int idx = rd * 32 + lane, n = idx >> 2, piece = idx & 3;
+            const int col = c16 * 16 + n;
+            if (col < ncols)
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(row_ptr(col)) + piece * 8) =
+                  *reinterpret_cast<const uint4*>(s16 + n * 32 + piece * 8);
+          }
         }
+        __syncwarp();  // the buffer is rewritten by the next chunk
       }
       tc_fence_before();
       __syncwarp();
@@ -609,6 +653,17 @@ void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(L.a) & 15) || (reinterpret_cast<uintptr_t>(L.b) & 15))
     throw std::runtime_error("operands must be 16-byte aligned");
   if (L.b_row_stride_bytes % 16 != 0) throw std::runtime_error("activation row stride must be a multiple of 16 bytes");
+  {
+    // the epilogue writes 16-byte pieces of output rows
+    const int vec = L.epi == kEpiF32 ? 4 : 8;
+    if (L.args.ld_out % vec || L.args.out_group_stride % vec || L.args.split_stride % vec ||
+        (reinterpret_cast<uintptr_t>(L.args.out) & 15))
+      throw std::runtime_error("output rows must be 16-byte aligned (row stride, group stride, split stride)");
+    if (L.args.peer_scatter)
+      for (int r = 0; r < 8; ++r)
+        if (reinterpret_cast<uintptr_t>(L.args.peer_out[r]) & 15)
+          throw std::runtime_error("peer scatter outputs must be 16-byte aligned");
+  }
   const int bn = L.bn;
   if (L.args.k_splits > 1) {
     if (L.epi != kEpiF32 || L.pair) throw std::runtime_error("split-K needs the fp32 epilogue");

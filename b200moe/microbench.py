@@ -238,6 +238,10 @@ def _trace_summary(name, buf):
     if len(idx) > 2:
         d["us_between_tma_issues"] = med([issue[b] - issue[a] for a, b in zip(idx, idx[1:])])
         d["us_between_mma_issues"] = med([mma[b] - mma[a] for a, b in zip(idx, idx[1:])])
+        landed = by.get(6, {})
+        if landed and all(i in landed for i in idx):
+            d["us_issue_to_landed"] = med([landed[i] - issue[i] for i in idx])
+            d["us_landed_to_dequant_start"] = med([c0[i] - landed[i] for i in idx])
         if c0:
             d["us_issue_to_dequant_start"] = med([c0[i] - issue[i] for i in idx])
             d["us_dequant"] = med([c1[i] - c0[i] for i in idx])
