@@ -36,7 +36,7 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
           c10::optional<Tensor> group_offset, Tensor out, int64_t bn, int64_t epi, int64_t m_tiles,
           int64_t pair_row_offset, int64_t out_group_stride, c10::optional<Tensor> slot_of_row,
           c10::optional<Tensor> slot_weight, Tensor status, c10::optional<Tensor> trace, int64_t k_splits,
-          int64_t split_stride) {
+          int64_t split_stride, bool a_tiled) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(group_count); CHECK_CUDA(status);
   CHECK_CONTIG(weight); CHECK_CONTIG(group_count);
   TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
@@ -105,6 +105,7 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
   L.args.status = status.data_ptr<int>();
   L.args.k_splits = (int)k_splits;
   L.args.split_stride = split_stride;
+  L.args.a_tiled = a_tiled ? 1 : 0;
   if (trace.has_value()) {
     TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->is_contiguous(), "trace must be int64");
     L.args.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
@@ -127,7 +128,7 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
 // slot buffer (peer memory): slot_code = rank * slot_cap + slot.
 void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor group_count, Tensor group_offset,
                        int64_t bn, Tensor slot_code, Tensor slot_w, std::vector<int64_t> peer_ptrs, int64_t slot_cap,
-                       int64_t ld_out, Tensor status) {
+                       int64_t ld_out, Tensor status, bool a_tiled) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CONTIG(weight);
   TORCH_CHECK(weight.dim() == 3 && weight.scalar_type() == torch::kFloat8_e4m3fn, "expert weights must be [E, N, K] e4m3");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.scalar_type() == torch::kBFloat16, "x must be [rows, K] bf16");
@@ -154,6 +155,7 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
   L.args.slot_weight = slot_w.data_ptr<float>();
   L.args.status = status.data_ptr<int>();
   L.args.peer_scatter = 1;
+  L.args.a_tiled = a_tiled ? 1 : 0;
   L.args.slot_cap = (int)slot_cap;
   for (size_t i = 0; i < peer_ptrs.size(); ++i) L.args.peer_out[i] = reinterpret_cast<void*>(peer_ptrs[i]);
   L.a = weight.data_ptr();

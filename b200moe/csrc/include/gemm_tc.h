@@ -43,6 +43,9 @@ struct GemmArgs {
   // optional pipeline trace of CTA 0: pairs (role << 32 | index, %globaltimer); entry 0 = count
   unsigned long long* trace;
   int trace_cap;
+  // e4m3 weights stored tile-major: [row tile][K / 64][128 rows][64 B], so the
+  // weight bytes of one pipeline stage are one contiguous 8 KB block
+  int a_tiled;
 };
 
 struct GemmLaunch {
@@ -61,6 +64,6 @@ struct GemmLaunch {
 
 void gemm_tc_launch(const GemmLaunch& launch, cudaStream_t stream);
 CUtensorMap make_tmap_2d(const void* base, bool is_bf16, int64_t rows, int64_t cols,
-                         int64_t row_stride_bytes, int box_cols, int box_rows, bool swizzle128);
+                         int64_t row_stride_bytes, int box_cols, int box_rows, int swizzle_bytes);
 
 }  // namespace b200

@@ -70,15 +70,19 @@ struct GemmCfg {
   // load ring: what TMA writes (fp8 weights or, in bf16 mode, the UMMA-ready A tile)
   static constexpr int ALOAD_BYTES = AFP8 ? A8_BYTES : A16_BYTES;
   static constexpr int STAGE_BYTES = NA * ALOAD_BYTES + B_BYTES;
-  // bf16 ring fed by the dequantisers (fp8 mode only)
-  // enough bf16 slots that dequantisation runs ahead of MMA completion (the
-  // commit round trip, not the conversion itself, bounds a short ring)
-  // bf16 slots: 4 (single tile) / 3 (gate+up pair: more would cost a load stage,
-  // measured slower) for decode-size tiles, 2 for BN >= 128 (MMA-bound: the shared
-  // memory goes to deeper load stages for the large B tiles)
-  static constexpr int CONV_SLOTS = !AFP8 ? 0 : BN >= 128 ? 2 : PAIR ? 3 : 4;
-
-  static constexpr int CONV_BYTES = CONV_SLOTS * NA * A16_BYTES;
+  static constexpr int ACC_COLS = NA * BN;
+  // Decode-size tiles (BN <= 64) keep the dequantised bf16 A tiles in TMEM
+  // (tcgen05.st by the dequantisers, MMA with A from TMEM): TMEM left over by the
+  // two accumulators holds the bf16 ring, and the shared memory it used to take
+  // goes to e4m3 load stages -- these GEMMs are bound by the bytes in flight per SM.
+  static constexpr bool A_TMEM = AFP8 && BN <= 64;
+  static constexpr int TSLOTS_RAW = A_TMEM ? (512 - 2 * ACC_COLS) / (NA * 32) : 0;
+  // bf16 slots: TMEM ring (up to 8) for decode-size tiles, else a shared-memory ring
+  // of 2 for BN >= 128 (MMA-bound: the shared memory goes to deeper load stages for
+  // the large B tiles)
+  static constexpr int CONV_SLOTS = !AFP8 ? 0 : A_TMEM ? (TSLOTS_RAW > 8 ? 8 : TSLOTS_RAW)
+                                    : BN >= 128 ? 2 : PAIR ? 3 : 4;
+  static constexpr int CONV_BYTES = A_TMEM ? 0 : CONV_SLOTS * NA * A16_BYTES;
   static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
   static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES - EPI_STAGE) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
@@ -88,10 +92,11 @@ struct GemmCfg {
   static constexpr int DEQ_GROUPS = !AFP8 ? 1 : (STAGES >= 4 && CONV_SLOTS >= 4) ? 4 : 2;
   static_assert(!AFP8 || (CONV_WARPS % DEQ_GROUPS == 0 && DEQ_GROUPS <= CONV_SLOTS && DEQ_GROUPS <= STAGES),
                 "dequant groups must fit the load ring and the bf16 ring");
-  static constexpr int ACC_COLS = NA * BN;
-  static constexpr int TMEM_COLS_RAW = 2 * ACC_COLS;
+  static_assert(!A_TMEM || CONV_SLOTS >= 2, "TMEM bf16 ring needs two slots");
+  static constexpr int TMEM_COLS_RAW = A_TMEM ? 512 : 2 * ACC_COLS;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                    : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
+  static constexpr int TSLOT_COL0 = 2 * ACC_COLS;       // first TMEM column of the bf16 ring
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(TMEM_COLS_RAW <= 512, "accumulators exceed TMEM");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16,256]");
@@ -190,9 +195,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   uint8_t* extra = epi_stage + C::EPI_STAGE;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);   // [12] TMA landed
   uint64_t* empty_bar = full_bar + 12;                       // [12] load slot free
-  uint64_t* cfull_bar = empty_bar + 12;                      // [4] bf16 slot written
-  uint64_t* cempty_bar = cfull_bar + 4;                      // [4] bf16 slot consumed
-  uint64_t* accf_bar = cempty_bar + 4;
+  uint64_t* cfull_bar = empty_bar + 12;                      // [8] bf16 slot written
+  uint64_t* cempty_bar = cfull_bar + 8;                      // [8] bf16 slot consumed
+  uint64_t* accf_bar = cempty_bar + 8;
   uint64_t* acce_bar = accf_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -244,7 +249,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS + 1 : 1);  // fp8: the stage's dequant group + the MMA
     }
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS : 1);
       mbar_init(&cempty_bar[j], 1);
     }
@@ -288,8 +293,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           if (!mbar_wait(&empty_bar[s], phase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[s], C::TX_BYTES);
           const int x = ks * kBK;
-          tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], x, a_row);
-          if constexpr (PAIR) tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
+          if (AFP8 && args.a_tiled) {
+            // tile-major weights: stage ks of row tile r is rows [(r * k_stages + ks) * 128, +128) of a [*, 64] map
+            tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], 0, ((a_row >> 7) * k_stages + ks) * 128);
+            if constexpr (PAIR)
+              tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], 0,
+                          (((a_row + args.pair_row_offset) >> 7) * k_stages + ks) * 128);
+          } else {
+            tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], x, a_row);
+            if constexpr (PAIR) tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
+          }
           tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
           trace_ev(args, 0, pi++);
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
@@ -333,9 +346,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const uint64_t bdesc = umma_sdesc_sw128(b_addr + k * 32);
 #pragma unroll
             for (int a = 0; a < C::NA; ++a) {
-              const uint8_t* abuf_ptr = AFP8 ? A16(cj, a) : ALd(s, a);
-              const uint64_t adesc = umma_sdesc_sw128(smem_u32(abuf_ptr) + k * 32);
-              umma_f16_ss(d_base + a * BN, adesc, bdesc, idesc, (ks != tc.ks0 || k != 0) ? 1u : 0u);
+              const uint32_t acc = (ks != tc.ks0 || k != 0) ? 1u : 0u;
+              if constexpr (C::A_TMEM) {
+                // bf16 A of slot cj: NA tiles x 32 columns, K = 16 per 8 columns
+                umma_f16_ts(d_base + a * BN, tmem_base + C::TSLOT_COL0 + cj * (C::NA * 32) + a * 32 + k * 8,
+                            bdesc, idesc, acc);
+              } else {
+                const uint8_t* abuf_ptr = AFP8 ? A16(cj, a) : ALd(s, a);
+                const uint64_t adesc = umma_sdesc_sw128(smem_u32(abuf_ptr) + k * 32);
+                umma_f16_ss(d_base + a * BN, adesc, bdesc, idesc, acc);
+              }
             }
           }
           umma_commit(&empty_bar[s]);
@@ -352,7 +372,91 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     // 16 / (warps per group) chunks of every weight tile of its group's stages,
     // so the per-stage wait / fence / arrive overhead is amortised over more
     // values (2 groups: 32 values per lane per tile, 4 groups: 64).
-    if constexpr (AFP8) {
+    if constexpr (AFP8 && C::A_TMEM) {
+      // bf16 ring in TMEM: a lane converts chunks of its own row (TMEM lane = row;
+      // warp w may only address lane quarter w & 3) and stores them with tcgen05.st.
+      // The e4m3 tile arrives 64-byte swizzled, so the 32 lanes' row reads are
+      // bank-conflict-free.
+      constexpr int kGroups = C::DEQ_GROUPS;
+      constexpr int GW = C::CONV_WARPS / kGroups;          // warps per group
+      constexpr int WPQ = GW / 4;                          // warps per lane quarter in a group
+      constexpr int CH = C::NA * 4 / WPQ;                  // 16-byte chunks of its row a lane converts per stage
+      const int dw = warp - 2;
+      const int group = dw / GW;
+      const int quarter = warp & 3;
+      const int wq = (dw % GW) / 4;
+      const int row = quarter * 32 + lane;
+      const bool tracer = dw == 0 && lane == 0;
+      const int nkb = args.scale_k_blocks;
+      const int pair_mb = C::NA > 1 ? args.pair_row_offset / 128 : 0;
+      const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16) + C::TSLOT_COL0;
+      int src_off[CH], col_off[CH], tile_of_chunk[CH];
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const int c = wq * CH + j, a = c >> 2, kc = c & 3;
+        tile_of_chunk[j] = a;
+        src_off[j] = row * 64 + ((kc ^ ((row >> 1) & 3)) << 4);
+        col_off[j] = a * 32 + kc * 8;
+      }
+      int t = blockIdx.x, ks = -1, ks1 = 0;
+      TileCoord tc{};
+      auto advance = [&]() -> bool {
+        if (++ks < ks1) return true;
+        if (ks1 != 0) t += gridDim.x;
+        if (t >= total_tiles) return false;
+        tc = tile_of(t);
+        ks = tc.ks0;
+        ks1 = tc.ks1;
+        return true;
+      };
+      auto load_scales = [&](float (&out)[C::NA]) {
+        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * nkb + (ks * kBK) / 128;
+        out[0] = __ldg(sc + tc.i * nkb);
+        if constexpr (C::NA > 1) out[1] = __ldg(sc + (tc.i + pair_mb) * nkb);
+      };
+      bool have = advance();
+      for (int i = 0; i < group && have; ++i) have = advance();
+      float next_scale[C::NA];
+      if (have) load_scales(next_scale);
+      int gi = group, s = group % C::STAGES, cj = group % C::CONV_SLOTS;
+      uint32_t phase = (group / C::STAGES) & 1, cph = (group / C::CONV_SLOTS) & 1;
+      while (have) {
+        float scale[C::NA];
+#pragma unroll
+        for (int a = 0; a < C::NA; ++a) scale[a] = next_scale[a];
+        for (int i = 0; i < kGroups && have; ++i) have = advance();
+        if (have) load_scales(next_scale);
+        bool w_ok = mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag);
+        if (tracer) trace_ev(args, 6, gi);
+        w_ok = w_ok && mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
+        if (!__all_sync(0xffffffffu, w_ok)) break;
+        if (tracer) trace_ev(args, 1, gi);
+        uint4 q[CH];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) q[j] = *reinterpret_cast<const uint4*>(ALd(s, tile_of_chunk[j]) + src_off[j]);
+        tc_fence_after();  // the MMAs that read this TMEM slot have completed (cempty)
+        const uint32_t slot_addr = lane_addr + cj * (C::NA * 32);
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          uint32_t o[8];
+          dequant16(q[j], scale[tile_of_chunk[j]], o);
+          tmem_st8(slot_addr + col_off[j], o);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty_bar[s]);   // this warp is done with the e4m3 tile
+          mbar_arrive(&cfull_bar[cj]);  // and its rows of the bf16 tile are in TMEM
+        }
+        if (tracer) trace_ev(args, 2, gi);
+        gi += kGroups;
+        s += kGroups;
+        while (s >= C::STAGES) { s -= C::STAGES; phase ^= 1; }
+        cj += kGroups;
+        while (cj >= C::CONV_SLOTS) { cj -= C::CONV_SLOTS; cph ^= 1; }
+      }
+    } else if constexpr (AFP8) {
       constexpr int kGroups = C::DEQ_GROUPS;
       constexpr int GW = C::CONV_WARPS / kGroups;          // warps per group
       constexpr int CPL = 128 * kBK / 16 / (GW * 32);      // 16-byte chunks per lane per tile
@@ -584,7 +688,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 CUtensorMap make_tmap_2d(const void* base, bool is_bf16, int64_t rows, int64_t cols,
-                         int64_t row_stride_bytes, int box_cols, int box_rows, bool swizzle128) {
+                         int64_t row_stride_bytes, int box_cols, int box_rows, int swizzle_bytes) {
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
@@ -593,7 +697,8 @@ CUtensorMap make_tmap_2d(const void* base, bool is_bf16, int64_t rows, int64_t c
   CUresult r = get_encode_fn()(
       &map, is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
       const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+      swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+      : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -619,10 +724,15 @@ static void launch_impl(const GemmLaunch& L, cudaStream_t stream) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr_set = true;
   }
-  // A: [groups * rows_per_group, K] row-major; box 64 x 128 rows
-  CUtensorMap ta = make_tmap_2d(L.a, !AFP8, (int64_t)L.args.num_groups * L.args.a_rows_per_group,
-                                L.K, L.a_row_stride_bytes, kBK, 128, !AFP8);
-  CUtensorMap tb = make_tmap_2d(L.b, true, L.b_rows, L.K, L.b_row_stride_bytes, kBK, BN, true);
+  // A: [groups * rows_per_group, K] row-major, box 64 x 128 rows; tile-major e4m3
+  // weights are addressed as [groups * rows_per_group * K / 64, 64]
+  const int64_t a_rows = (int64_t)L.args.num_groups * L.args.a_rows_per_group;
+  // (the TMEM-ring dequantisers read e4m3 rows one lane per row: 64-byte swizzle)
+  const int a_swz = !AFP8 ? 128 : C::A_TMEM ? 64 : 0;
+  CUtensorMap ta = (AFP8 && L.args.a_tiled)
+                       ? make_tmap_2d(L.a, false, a_rows * (L.K / kBK), kBK, kBK, kBK, 128, a_swz)
+                       : make_tmap_2d(L.a, !AFP8, a_rows, L.K, L.a_row_stride_bytes, kBK, 128, a_swz);
+  CUtensorMap tb = make_tmap_2d(L.b, true, L.b_rows, L.K, L.b_row_stride_bytes, kBK, BN, 128);
   // upper bound of work items without reading device counts
   int64_t max_tiles = ((int64_t)L.b_rows / BN + L.args.num_groups) * L.args.m_tiles * std::max(1, L.args.k_splits);
   int grid = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, max_tiles));
@@ -648,6 +758,8 @@ static void dispatch_bn(int bn, const GemmLaunch& L, cudaStream_t s) {
 
 void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
   if (L.args.num_groups < 1 || L.args.num_groups > kMaxGroups) throw std::runtime_error("bad group count");
+  if (L.args.a_tiled && (!L.a_fp8 || L.a_row_stride_bytes != L.K))
+    throw std::runtime_error("tile-major weights must be dense e4m3 [rows, K]");
   if (L.K % 128 != 0) throw std::runtime_error("K must be a multiple of 128");
   if (L.args.a_rows_per_group % 128 != 0) throw std::runtime_error("weight rows must be a multiple of 128");
   if ((reinterpret_cast<uintptr_t>(L.a) & 15) || (reinterpret_cast<uintptr_t>(L.b) & 15))

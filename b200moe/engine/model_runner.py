@@ -93,6 +93,8 @@ class ModelRunner:
             random_init_(self.model, seed=config.seed)
         else:
             load_checkpoint(self.model, config.model)
+        if os.environ.get("B200MOE_TILED_WEIGHTS", "1") != "0":
+            self.model.tile_weights_()  # e4m3 GEMM weights tile-major: one contiguous HBM block per stage
         self.model.profiler = self.profiler if config.enable_profiling else None
         self.load_s = time.perf_counter() - t0
         self.max_blocks = -(-config.max_model_len // self.block_size)

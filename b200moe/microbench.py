@@ -62,6 +62,10 @@ def _graph(fn, reps):
     return g
 
 
+# e4m3 weights in the tile-major layout the engine uses (B200MOE_TILED_WEIGHTS=0: row-major)
+TILED = os.environ.get("B200MOE_TILED_WEIGHTS", "1") != "0"
+
+
 def _time_graph(g, iters):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
@@ -118,6 +122,8 @@ def fp8_weight(groups, n, k, seed=0):
 def case_moe(T, iters, E=128, k=8, H=2048, I=768, only=""):
     q13, s13 = fp8_weight(E, 2 * I, H, 1)
     q2, s2 = fp8_weight(E, H, I, 2)
+    if TILED:
+        q13, q2 = ops.tile_fp8(q13), ops.tile_fp8(q2)
     rows = T * k
     ids = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]).flatten()
     counts = torch.bincount(ids, minlength=E).to(torch.int32)
@@ -130,13 +136,13 @@ def case_moe(T, iters, E=128, k=8, H=2048, I=768, only=""):
     w = torch.rand(rows, device="cuda")
     used = int((counts > 0).sum())
     if only != "down":
-        ms = timeit(lambda: ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I), iters)
+        ms = timeit(lambda: ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h, I, tiled=TILED), iters)
         wbytes = used * 2 * I * H + rows * H * 2 + rows * I * 2
         report("moe_gate_up_silu", ms, wbytes, 2 * rows * H * 2 * I, tokens=T,
                bn=ops.pick_bn(rows, I // 128, E, pair=True))
     if only == "gate_up":
         return
-    ms = timeit(lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots), iters)
+    ms = timeit(lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots, tiled=TILED), iters)
     wbytes = used * H * I + rows * I * 2 + rows * H * 2
     report("moe_down_scatter", ms, wbytes, 2 * rows * I * H, tokens=T, bn=ops.pick_bn(rows, H // 128, E))
 
@@ -144,11 +150,13 @@ def case_moe(T, iters, E=128, k=8, H=2048, I=768, only=""):
 def case_dense(T, iters, H=2048):
     x = (torch.randn(T, H, device="cuda") * 0.5).to(torch.bfloat16)
     q, s = fp8_weight(1, 5120, H, 3)
-    ms = timeit(lambda: ops.linear(x, q[0], s[0]), iters)
+    q = ops.tile_fp8(q) if TILED else q
+    ms = timeit(lambda: ops.linear(x, q[0], s[0], tiled=TILED), iters)
     report("qkv_proj", ms, 5120 * H + T * (H + 5120) * 2, 2 * T * H * 5120, tokens=T)
     xo = (torch.randn(T, 4096, device="cuda") * 0.5).to(torch.bfloat16)
     q, s = fp8_weight(1, H, 4096, 4)
-    ms = timeit(lambda: ops.linear(xo, q[0], s[0]), iters)
+    q = ops.tile_fp8(q) if TILED else q
+    ms = timeit(lambda: ops.linear(xo, q[0], s[0], tiled=TILED), iters)
     report("o_proj", ms, H * 4096 + T * (H + 4096) * 2, 2 * T * H * 4096, tokens=T)
     lm = (torch.randn(151936, H, device="cuda") * 0.02).to(torch.bfloat16)
     rows = min(T, 512)
@@ -206,6 +214,8 @@ def case_step(T, ctx, iters, layers=48):
     args = ModelArgs(num_hidden_layers=layers)
     model = Qwen3MoeForCausalLM(args, "cuda")
     random_init_(model)
+    if os.environ.get("B200MOE_TILED_WEIGHTS", "1") != "0":
+        model.tile_weights_()
     bs = 256
     nbs = math.ceil((ctx + 1) / bs)
     model.reserve_workspace(max(T, 1), T, 64)
@@ -267,7 +277,8 @@ def case_trace(T):
     H, I, E, k = 2048, 768, 128, 8
     x = (torch.randn(T, 4096, device="cuda") * 0.5).to(torch.bfloat16)
     q, s = fp8_weight(1, H, 4096, 4)
-    for name, fn in (("o_proj", lambda: ops.linear(x, q[0], s[0])),):
+    q = ops.tile_fp8(q) if TILED else q
+    for name, fn in (("o_proj", lambda: ops.linear(x, q[0], s[0], tiled=TILED)),):
         fn()
         torch.cuda.synchronize()
         buf.zero_()
@@ -278,6 +289,7 @@ def case_trace(T):
         ops.set_gemm_trace(None)
         _trace_summary(name, buf.cpu())
     q13, s13 = fp8_weight(E, 2 * I, H, 1)
+    q13 = ops.tile_fp8(q13) if TILED else q13
     rows = T * k
     ids = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]).flatten()
     counts = torch.bincount(ids, minlength=E).to(torch.int32)
@@ -286,11 +298,14 @@ def case_trace(T):
     xm = (torch.randn(rows, H, device="cuda") * 0.5).to(torch.bfloat16)
     h = torch.empty(rows, I, dtype=torch.bfloat16, device="cuda")
     q2, s2 = fp8_weight(E, H, I, 2)
+    q2 = ops.tile_fp8(q2) if TILED else q2
     slots = torch.empty(rows, H, dtype=torch.bfloat16, device="cuda")
     sor = torch.randperm(rows, device="cuda").to(torch.int32)
     w = torch.rand(rows, device="cuda")
-    for name, fn in (("moe_gate_up", lambda: ops.grouped_gate_up_silu(xm, q13, s13, counts, offsets, h, I)),
-                     ("moe_down", lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots))):
+    for name, fn in (("moe_gate_up", lambda: ops.grouped_gate_up_silu(xm, q13, s13, counts, offsets, h, I,
+                                                                      tiled=TILED)),
+                     ("moe_down", lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots,
+                                                                   tiled=TILED))):
         fn()
         torch.cuda.synchronize()
         buf.zero_()

@@ -146,6 +146,38 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.attention_backend = "paged"  # or "sdpa": per-sequence PyTorch attention (A/B, equivalence gate)
         self.profiler = None
         self._ws: dict = {}
+        self.weights_tiled = False  # e4m3 GEMM weights stored tile-major (tile_weights_)
+
+    # The e4m3 matrices the tcgen05 GEMM streams (QKV, O, expert gate/up and down).
+    _TILED = ("qkv_weight", "o_weight", "w13", "w2")
+
+    @torch.no_grad()
+    def tile_weights_(self) -> None:
+        """Re-lay every e4m3 GEMM weight tile-major in place (ops.tile_fp8): each
+        pipeline stage of the GEMM then reads one contiguous 8 KB block of HBM.
+        Loaders and reference paths see the natural layout through
+        ``untile_weights_`` / ``natural``."""
+        if self.weights_tiled or not self.quant or not self.cuda:
+            return
+        for layer in self.layers:
+            for name in self._TILED:
+                w = getattr(layer, name)
+                w.copy_(ops.tile_fp8(w))
+        self.weights_tiled = True
+
+    @torch.no_grad()
+    def untile_weights_(self) -> None:
+        if not self.weights_tiled:
+            return
+        for layer in self.layers:
+            for name in self._TILED:
+                w = getattr(layer, name)
+                w.copy_(ops.untile_fp8(w))
+        self.weights_tiled = False
+
+    def natural(self, w: torch.Tensor) -> torch.Tensor:
+        """``w`` (one of the tiled matrices or a leading-index slice of one) in row-major layout."""
+        return ops.untile_fp8(w) if self.weights_tiled else w
 
     def qkv_row_ranges(self) -> list[tuple[int, int]]:
         """Rows of the full [q | k | v] projection held by this rank (q, k, v order)."""
@@ -221,14 +253,15 @@ class Qwen3MoeForCausalLM(nn.Module):
             if self.attn_tp > 1:
                 with self._range("attn.o_proj"):
                     o = ops.linear(attn, layer.o_weight, layer.o_scale,
-                                   out=self._buf("o", (T, H), self.dtype) if cuda else None)
+                                   out=self._buf("o", (T, H), self.dtype) if cuda else None, tiled=self.weights_tiled)
                 with self._range("attn.all_reduce"):
                     dist.all_reduce(o)  # row-parallel O projection: sum of the ranks' partial products
                 x = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=residual, out=xbuf)
             else:
                 with self._range("attn.o_proj_add_norm"):
                     x = ops.linear_add_rmsnorm(attn, layer.o_weight, layer.o_scale, residual,
-                                               layer.post_attention_layernorm, eps, out=xbuf)
+                                               layer.post_attention_layernorm, eps, out=xbuf,
+                                               tiled=self.weights_tiled)
             nxt = self.layers[l + 1].input_layernorm if l + 1 < len(self.layers) else self.norm
             x = self._mlp(layer, x, residual, nxt, T)
         return x.index_select(0, inp.logits_indices.long())
@@ -244,7 +277,8 @@ class Qwen3MoeForCausalLM(nn.Module):
         cuda = self.cuda
         with self._range("attn.qkv"):
             qkv = ops.linear(x, layer.qkv_weight, layer.qkv_scale,
-                             out=self._buf("qkv", (T, (nq + 2 * nkv) * D), self.dtype) if cuda else None)
+                             out=self._buf("qkv", (T, (nq + 2 * nkv) * D), self.dtype) if cuda else None,
+                             tiled=self.weights_tiled)
         with self._range("attn.qknorm_rope_kvstore"):
             q = ops.qknorm_rope_kvstore(qkv, inp.positions, inp.slot_mapping, layer.q_norm, layer.k_norm,
                                         self.cos_sin, kvl, nq, nkv, D, a.rms_norm_eps,
@@ -338,8 +372,9 @@ class Qwen3MoeForCausalLM(nn.Module):
             if not bool(mask.any()):
                 continue
             t_idx, k_idx = mask.nonzero(as_tuple=True)
-            w13 = ops.dequant_block_fp8(layer.w13[le], layer.s13[le]) if self.quant else layer.w13[le].float()
-            w2 = ops.dequant_block_fp8(layer.w2[le], layer.s2[le]) if self.quant else layer.w2[le].float()
+            w13 = ops.dequant_block_fp8(self.natural(layer.w13[le]), layer.s13[le]) if self.quant \
+                else layer.w13[le].float()
+            w2 = ops.dequant_block_fp8(self.natural(layer.w2[le]), layer.s2[le]) if self.quant else layer.w2[le].float()
             if bf:  # the native GEMM dequantises to bf16 before the MMA
                 w13, w2 = w13.to(torch.bfloat16).float(), w2.to(torch.bfloat16).float()
             gu = x[t_idx].float() @ w13.t()
@@ -372,10 +407,11 @@ class Qwen3MoeForCausalLM(nn.Module):
             ops.moe_permute(x, ids, counts[:E], counts[E:2 * E], x_perm, slot_of_row, offsets)
         with self._range("moe.gate_up"):
             h_perm = self._buf("h_perm", (rows, I), self.dtype)
-            ops.grouped_gate_up_silu(x_perm, layer.w13, layer.s13, counts[:E], offsets, h_perm, I)
+            ops.grouped_gate_up_silu(x_perm, layer.w13, layer.s13, counts[:E], offsets, h_perm, I,
+                                     tiled=self.weights_tiled)
         with self._range("moe.down"):
             ops.grouped_down_scatter(h_perm, layer.w2, layer.s2, counts[:E], offsets, slot_of_row,
-                                     w.view(-1), slots)
+                                     w.view(-1), slots, tiled=self.weights_tiled)
         return slots
 
     def _moe_tp(self, layer, x, residual, next_norm, T):
@@ -406,11 +442,12 @@ class Qwen3MoeForCausalLM(nn.Module):
             ops.moe_permute(x, ids_l, counts_l[:El], counts_l[El:], x_perm, slot_of_row, offsets)
             I = layer.w2.shape[-1]
             h_perm = self._buf("h_perm", (rows, I), self.dtype)
-            ops.grouped_gate_up_silu(x_perm, layer.w13, layer.s13, counts_l[:El], offsets, h_perm, I)
+            ops.grouped_gate_up_silu(x_perm, layer.w13, layer.s13, counts_l[:El], offsets, h_perm, I,
+                                     tiled=self.weights_tiled)
             slots = self._buf("slots", (rows, H), self.dtype)
             slots.zero_()  # slots of other ranks' experts stay zero
             ops.grouped_down_scatter(h_perm, layer.w2, layer.s2, counts_l[:El], offsets, slot_of_row,
-                                     w.view(-1), slots)
+                                     w.view(-1), slots, tiled=self.weights_tiled)
             # combine (fixed-order sum over k) into a zeroed residual: partial = sum_k slots
             partial.zero_()
             ops.moe_combine_add_rmsnorm(slots, k, partial, next_norm, eps,
@@ -443,7 +480,8 @@ class Qwen3MoeForCausalLM(nn.Module):
             y = (h.float() @ w2.t()).to(x.dtype)
             return ops.rmsnorm(y, next_norm, eps, residual=residual)
         h = self._buf("h_perm", (T, I), self.dtype)
-        ops.grouped_gate_up_silu(x, layer.w13, layer.s13, ops.count_tensor(T, x.device), None, h, I)
-        y = ops.linear(h, layer.w2[0], layer.s2[0] if self.quant else None,
+        ops.grouped_gate_up_silu(x, layer.w13, layer.s13, ops.count_tensor(T, x.device), None, h, I,
+                                 tiled=self.weights_tiled)
+        y = ops.linear(h, layer.w2[0], layer.s2[0] if self.quant else None, tiled=self.weights_tiled,
                        out=self._buf("o", (T, a.hidden_size), self.dtype))
         return ops.rmsnorm(y, next_norm, eps, residual=residual, out=self._buf("x", (T, a.hidden_size), self.dtype))

@@ -158,13 +158,34 @@ def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: 
     return best
 
 
+# ------------------------------------------------------- weight layout
+def tile_fp8(w: torch.Tensor) -> torch.Tensor:
+    """[..., N, K] e4m3 -> the same shape holding the bytes tile-major:
+    [..., N / 128, K / 64, 128, 64].  One GEMM pipeline stage (128 rows x 64 K)
+    is then one contiguous 8 KB block instead of 128 rows of 64 bytes 'K' apart,
+    which HBM serves at streaming rate."""
+    *lead, n, k = w.shape
+    if n % 128 or k % 64:
+        raise ValueError("tile_fp8 needs N % 128 == 0 and K % 64 == 0")
+    return w.reshape(*lead, n // 128, 128, k // 64, 64).transpose(-3, -2).contiguous().view(w.shape)
+
+
+def untile_fp8(w: torch.Tensor) -> torch.Tensor:
+    """Inverse of ``tile_fp8``."""
+    *lead, n, k = w.shape
+    return w.reshape(*lead, n // 128, k // 64, 128, 64).transpose(-3, -2).contiguous().view(w.shape)
+
+
 # --------------------------------------------------------------------- GEMM
 def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, out_dtype=torch.bfloat16,
-           out: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x @ W^T with W either block-scaled e4m3 (+ scale) or bf16/fp32."""
+           out: torch.Tensor | None = None, tiled: bool = False) -> torch.Tensor:
+    """y = x @ W^T with W either block-scaled e4m3 (+ scale) or bf16/fp32.
+    ``tiled``: the e4m3 weight is stored tile-major (``tile_fp8``)."""
     T = x.shape[0]
     N = weight.shape[0]
     if not x.is_cuda:
+        if tiled:
+            weight = untile_fp8(weight)
         w = dequant_block_fp8(weight, scale) if scale is not None else weight.float()
         y = x.float() @ w.t()
         return y.to(out_dtype) if out is None else out.copy_(y)
@@ -178,58 +199,59 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
     if splits > 1:
         part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
         C.gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, m_tiles,
-               0, 0, None, None, status_word(x.device), _trace[0], splits, T * N)
+               0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled)
         C.splitk_reduce(part, splits, out)
         count_launches(2)
         return out
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
     C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, bn, epi, m_tiles,
-           0, 0, None, None, status_word(x.device), _trace[0], 1, 0)
+           0, 0, None, None, status_word(x.device), _trace[0], 1, 0, tiled)
     count_launches()
     return out
 
 
-def linear_add_rmsnorm(x, weight, scale, residual, norm_w, eps, out):
+def linear_add_rmsnorm(x, weight, scale, residual, norm_w, eps, out, tiled: bool = False):
     """residual += bf16(x @ W^T); return rmsnorm(residual) * norm_w.  When the
     planner splits K, the fp32 partial sums go straight into the norm kernel
     (no separate reduce launch, no bf16 round trip through memory)."""
     T, N = x.shape[0], weight.shape[0]
     if not x.is_cuda or T == 0:
-        return rmsnorm(linear(x, weight, scale), norm_w, eps, residual=residual, out=out)
+        return rmsnorm(linear(x, weight, scale, tiled=tiled), norm_w, eps, residual=residual, out=out)
     m_tiles = N // 128
     bn, splits = plan_dense(T, m_tiles, x.shape[1] // 64, fp8=scale is not None)
     if splits == 1:
-        return rmsnorm(linear(x, weight, scale), norm_w, eps, residual=residual, out=out)
+        return rmsnorm(linear(x, weight, scale, tiled=tiled), norm_w, eps, residual=residual, out=out)
     C = native()
     part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
     C.gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, m_tiles,
-           0, 0, None, None, status_word(x.device), _trace[0], splits, T * N)
+           0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled)
     C.rmsnorm_partials(part, splits, residual, norm_w, out, eps)
     count_launches(2)
     return out
 
 
-def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn: int | None = None):
+def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn: int | None = None,
+                         tiled: bool = False):
     """out[r] = silu(x_perm[r] @ Wg_e^T) * (x_perm[r] @ Wu_e^T) for the rows of expert e."""
     C = native()
     rows = x_perm.shape[0]
     m_tiles = inter // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w13.shape[0], pair=True)
     C.gemm(w13, s13, x_perm, counts, offsets, out, bn, EPI_SILU_PAIR, m_tiles, inter, 0, None, None,
-           status_word(x_perm.device), _trace[0], 1, 0)
+           status_word(x_perm.device), _trace[0], 1, 0, tiled)
     count_launches()
     return out
 
 
 def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weight, slots_out,
-                         bn: int | None = None):
+                         bn: int | None = None, tiled: bool = False):
     """slots_out[slot_of_row[r]] = (h_perm[r] @ Wd_e^T) * slot_weight[slot] for the rows of expert e."""
     C = native()
     rows = h_perm.shape[0]
     m_tiles = w2.shape[1] // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w2.shape[0])
     C.gemm(w2, s2, h_perm, counts, offsets, slots_out, bn, EPI_SCATTER, m_tiles, 0, 0, slot_of_row, slot_weight,
-           status_word(h_perm.device), _trace[0], 1, 0)
+           status_word(h_perm.device), _trace[0], 1, 0, tiled)
     count_launches()
     return slots_out
 

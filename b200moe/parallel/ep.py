@@ -142,8 +142,8 @@ class ExpertParallel:
             ops.moe_permute(recv_x, le, cnt[:El], cnt[El:], xp, sor, off)
             I = layer.w2.shape[-1]
             h = model._buf("h_perm", (R, I), model.dtype)
-            ops.grouped_gate_up_silu(xp, layer.w13, layer.s13, cnt[:El], off, h, I)
-            ops.grouped_down_scatter(h, layer.w2, layer.s2, cnt[:El], off, sor, rw, out)
+            ops.grouped_gate_up_silu(xp, layer.w13, layer.s13, cnt[:El], off, h, I, tiled=model.weights_tiled)
+            ops.grouped_down_scatter(h, layer.w2, layer.s2, cnt[:El], off, sor, rw, out, tiled=model.weights_tiled)
         back = torch.empty(T * k, H, dtype=x.dtype, device=dev)
         dist.all_to_all_single(back, out, sc, rc)
         slots.index_copy_(0, order, back)

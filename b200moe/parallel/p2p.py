@@ -143,10 +143,12 @@ class P2PMoE:
         h = model._buf("h_perm", (rows, I), model.dtype)
         expected = max(1, T * self.W)  # rows this rank expects on average
         ops.grouped_gate_up_silu(xp, layer.w13, layer.s13, cnt[:El], off, h, I,
-                                 bn=ops.pick_bn(expected * model.args.num_experts_per_tok, I // 128, El, pair=True))
+                                 bn=ops.pick_bn(expected * model.args.num_experts_per_tok, I // 128, El, pair=True),
+                                 tiled=model.weights_tiled)
         C.gemm_peer_scatter(layer.w2, layer.s2, h, cnt[:El], off,
                             ops.pick_bn(expected * model.args.num_experts_per_tok, self.H // 128, El),
-                            code, sw, self.symm["slots"][1], self.slot_cap, self.H, self.status)
+                            code, sw, self.symm["slots"][1], self.slot_cap, self.H, self.status,
+                            model.weights_tiled)
         C.ep_signal(*a)
         C.ep_wait_done(*a)
         ops.count_launches(6)

@@ -19,6 +19,7 @@ Experts not owned by this rank are skipped; every parameter must be written
 """
 from __future__ import annotations
 
+import contextlib
 import json
 import os
 from glob import glob
@@ -42,8 +43,27 @@ def quantize_block_fp8(w: torch.Tensor, block: int = 128) -> tuple[torch.Tensor,
 
 
 # ------------------------------------------------------------- random init
+@contextlib.contextmanager
+def natural_layout(model):
+    """Give the body the row-major weight layout that loaders and exporters
+    index; tile-major GEMM weights (model.tile_weights_) are restored after."""
+    tiled = getattr(model, "weights_tiled", False)
+    if tiled:
+        model.untile_weights_()
+    try:
+        yield
+    finally:
+        if tiled:
+            model.tile_weights_()
+
+
 @torch.no_grad()
 def random_init_(model, seed: int = 0, std: float = 0.02):
+    with natural_layout(model):
+        _random_init(model, seed, std)
+
+
+def _random_init(model, seed: int = 0, std: float = 0.02):
     """Seeded normal(0, std) init of every weight directly on the model's
     device (norm weights stay 1).  Quantised weights are drawn in fp32 and
     block-quantised, so the bytes look like a real fp8 checkpoint.  Expert
@@ -119,6 +139,11 @@ def random_init_(model, seed: int = 0, std: float = 0.02):
 @torch.no_grad()
 def export_state(model) -> dict[str, torch.Tensor]:
     """HF-named tensors of a model that holds every expert."""
+    with natural_layout(model):
+        return _export_state(model)
+
+
+def _export_state(model) -> dict[str, torch.Tensor]:
     args: ModelArgs = model.args
     if args.is_moe and model.num_local_experts != args.num_experts:
         raise ValueError("export needs a model holding every expert")
@@ -195,6 +220,11 @@ def save_checkpoint(model, path: str, max_shard_bytes: int = 4 << 30):
 @torch.no_grad()
 def load_checkpoint(model, path: str):
     """Load an HF checkpoint into ``model`` (this rank's experts only)."""
+    with natural_layout(model):
+        _load_checkpoint(model, path)
+
+
+def _load_checkpoint(model, path: str):
     from safetensors import safe_open
     args: ModelArgs = model.args
     D = args.head_dim

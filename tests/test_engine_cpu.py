@@ -131,3 +131,23 @@ def test_stop_tokens_and_sampling_cpu(baseline):
     a = llm.generate(prompts[:2], sp, use_tqdm=False)
     b = llm.generate(prompts[:2], sp, use_tqdm=False)
     assert [o["token_ids"] for o in a] == [o["token_ids"] for o in b]
+
+
+def test_tile_major_fp8_layout_roundtrip():
+    """tile_fp8 puts each (128-row, 64-K) block of an e4m3 matrix in one
+    contiguous 8 KB run; untile_fp8 inverts it, and the CPU linear path reads
+    either layout to the same result."""
+    import torch
+    from b200moe import ops
+    from b200moe.utils.weights import quantize_block_fp8
+    w = torch.randn(3, 256, 384) * 0.05
+    q = torch.stack([quantize_block_fp8(w[i])[0] for i in range(3)])
+    t = ops.tile_fp8(q)
+    assert t.shape == q.shape
+    # block (expert 1, row tile 1, K stage 2) is contiguous in the tiled bytes
+    blk = t[1].reshape(-1)[(1 * (384 // 64) + 2) * 8192:(1 * (384 // 64) + 3) * 8192].view(128, 64)
+    assert torch.equal(blk.view(torch.uint8), q[1, 128:256, 128:192].contiguous().view(torch.uint8))
+    assert torch.equal(ops.untile_fp8(t).view(torch.uint8), q.view(torch.uint8))
+    s = quantize_block_fp8(w[0])[1]
+    x = torch.randn(5, 384).to(torch.bfloat16)
+    assert torch.equal(ops.linear(x, q[0], s), ops.linear(x, t[0], s, tiled=True))

@@ -138,6 +138,38 @@ def test_grouped_gate_up_and_down(bn):
     _close(slots, ref_slots)
 
 
+@pytest.mark.parametrize("bn", [32, 128, 256])
+def test_tile_major_weights_same_bits(bn):
+    """e4m3 weights stored tile-major (one contiguous block per pipeline stage)
+    give bit-identical GEMM results: dense, split-K, gate/up pair and scatter."""
+    for T, n, k in [(300, 5120, 2048), (64, 2048, 4096), (7, 256, 256)]:
+        q, s = _fp8_weight(1, n, k, 1)
+        x = (torch.randn(T, k, device=DEV) * 0.5).to(torch.bfloat16)
+        a = ops.linear(x, q[0], s[0])
+        b = ops.linear(x, ops.tile_fp8(q[0]), s[0], tiled=True)
+        assert torch.equal(a, b), (T, n, k)
+    E, I, H = 8, 256, 512
+    counts = torch.tensor([5, 0, 17, 1, 300, 3, 0, 9], dtype=torch.int32, device=DEV)
+    rows = int(counts.sum())
+    offsets = torch.zeros(E + 1, dtype=torch.int32, device=DEV)
+    offsets[1:] = torch.cumsum(counts, 0)
+    q13, s13 = _fp8_weight(E, 2 * I, H, 2)
+    q2, s2 = _fp8_weight(E, H, I, 3)
+    x = (torch.randn(rows, H, device=DEV) * 0.5).to(torch.bfloat16)
+    h1, h2 = (torch.empty(rows, I, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+    ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h1, I, bn=min(bn, 128))
+    ops.grouped_gate_up_silu(x, ops.tile_fp8(q13), s13, counts, offsets, h2, I, bn=min(bn, 128), tiled=True)
+    assert torch.equal(h1, h2)
+    sor = torch.randperm(rows, device=DEV).to(torch.int32)
+    wts = torch.rand(rows, device=DEV)
+    y1, y2 = (torch.zeros(rows, H, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+    ops.grouped_down_scatter(h1, q2, s2, counts, offsets, sor, wts, y1, bn=bn)
+    ops.grouped_down_scatter(h1, ops.tile_fp8(q2), s2, counts, offsets, sor, wts, y2, bn=bn, tiled=True)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert torch.equal(y1, y2)
+
+
 def test_rmsnorm_and_add():
     T, H = 33, 2048
     x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
