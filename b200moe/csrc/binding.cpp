@@ -106,10 +106,11 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
   L.args.k_splits = (int)k_splits;
   L.args.split_stride = split_stride;
   L.args.a_tiled = a_tiled ? 1 : 0;
+  L.args.a_base = weight.data_ptr();
   if (trace.has_value()) {
     TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->is_contiguous(), "trace must be int64");
     L.args.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
-    L.args.trace_cap = (int)((trace->numel() - 1) / 2);
+    L.args.trace_cap = (int)((trace->numel() - 1) / 8);
   }
   L.a = weight.data_ptr();
   L.a_row_stride_bytes = K * weight.element_size();
@@ -156,6 +157,7 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
   L.args.status = status.data_ptr<int>();
   L.args.peer_scatter = 1;
   L.args.a_tiled = a_tiled ? 1 : 0;
+  L.args.a_base = weight.data_ptr();
   L.args.slot_cap = (int)slot_cap;
   for (size_t i = 0; i < peer_ptrs.size(); ++i) L.args.peer_out[i] = reinterpret_cast<void*>(peer_ptrs[i]);
   L.a = weight.data_ptr();

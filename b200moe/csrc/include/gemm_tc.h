@@ -43,9 +43,11 @@ struct GemmArgs {
   // optional pipeline trace of CTA 0: pairs (role << 32 | index, %globaltimer); entry 0 = count
   unsigned long long* trace;
   int trace_cap;
-  // e4m3 weights stored tile-major: [row tile][K / 64][128 rows][64 B], so the
-  // weight bytes of one pipeline stage are one contiguous 8 KB block
+  // e4m3 weights stored tile-major: [row tile][K / 64][128 rows][64 B] with the
+  // 16-byte chunks of each row in 64-byte-swizzle order, so one pipeline stage is
+  // one contiguous 8 KB block fetched by a single bulk copy
   int a_tiled;
+  const void* a_base;
 };
 
 struct GemmLaunch {

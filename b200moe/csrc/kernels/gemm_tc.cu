@@ -71,11 +71,11 @@ struct GemmCfg {
   static constexpr int ALOAD_BYTES = AFP8 ? A8_BYTES : A16_BYTES;
   static constexpr int STAGE_BYTES = NA * ALOAD_BYTES + B_BYTES;
   static constexpr int ACC_COLS = NA * BN;
-  // Decode-size tiles (BN <= 64) keep the dequantised bf16 A tiles in TMEM
+  // Decode-size tiles (BN <= 64, or 128 without the gate/up pair) keep the dequantised bf16 A tiles in TMEM
   // (tcgen05.st by the dequantisers, MMA with A from TMEM): TMEM left over by the
   // two accumulators holds the bf16 ring, and the shared memory it used to take
   // goes to e4m3 load stages -- these GEMMs are bound by the bytes in flight per SM.
-  static constexpr bool A_TMEM = AFP8 && BN <= 64;
+  static constexpr bool A_TMEM = AFP8 && (PAIR ? BN <= 64 : BN <= 128);
   static constexpr int TSLOTS_RAW = A_TMEM ? (512 - 2 * ACC_COLS) / (NA * 32) : 0;
   // bf16 slots: TMEM ring (up to 8) for decode-size tiles, else a shared-memory ring
   // of 2 for BN >= 128 (MMA-bound: the shared memory goes to deeper load stages for
@@ -84,9 +84,18 @@ struct GemmCfg {
                                     : BN >= 128 ? 2 : PAIR ? 3 : 4;
   static constexpr int CONV_BYTES = A_TMEM ? 0 : CONV_SLOTS * NA * A16_BYTES;
   static constexpr int EXTRA = 4096 + 2 * (kMaxGroups + 1) * 4 + 2 * 256 * 8 + 128 * 4;
-  static constexpr int STAGES_RAW = (kSmemBudget - EXTRA - 1024 - CONV_BYTES - EPI_STAGE) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + CONV_BYTES + EPI_STAGE + EXTRA + 1024;
+  // TMEM-ring tiles split the load ring: e4m3 stages (freed by the dequantisers as
+  // soon as they have read them) and a separate, deeper ring of activation tiles
+  // (freed by the MMA), so weight bytes never wait for the MMA to release a slot
+  static constexpr int SB = !A_TMEM ? 0 : BN <= 32 ? (PAIR ? 12 : 16) : BN == 64 ? (PAIR ? 8 : 12) : 6;
+  static constexpr int A_STAGE_BYTES = NA * ALOAD_BYTES;
+  static constexpr int STAGES_RAW = A_TMEM
+      ? (kSmemBudget - EXTRA - 1024 - EPI_STAGE - SB * B_BYTES) / A_STAGE_BYTES
+      : (kSmemBudget - EXTRA - 1024 - CONV_BYTES - EPI_STAGE) / STAGE_BYTES;
+  static constexpr int MAX_STAGES = A_TMEM ? 16 : 12;
+  static constexpr int STAGES = STAGES_RAW > MAX_STAGES ? MAX_STAGES : STAGES_RAW;
+  static constexpr int RING_BYTES = A_TMEM ? STAGES * A_STAGE_BYTES + SB * B_BYTES : STAGES * STAGE_BYTES;
+  static constexpr int SMEM = RING_BYTES + CONV_BYTES + EPI_STAGE + EXTRA + 1024;
   // dequantiser warp groups taking stages round robin: never more groups than
   // load stages or bf16 slots (a group waits on its own stage and slot)
   static constexpr int DEQ_GROUPS = !AFP8 ? 1 : (STAGES >= 4 && CONV_SLOTS >= 4) ? 4 : 2;
@@ -98,6 +107,7 @@ struct GemmCfg {
                                    : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int TSLOT_COL0 = 2 * ACC_COLS;       // first TMEM column of the bf16 ring
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
+  static_assert(STAGES <= 16 && SB <= 16, "barrier arrays hold 16 stages");
   static_assert(TMEM_COLS_RAW <= 512, "accumulators exceed TMEM");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16,256]");
   static constexpr uint32_t TX_BYTES = NA * ALOAD_BYTES + B_BYTES;
@@ -132,16 +142,14 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, 
   return c;
 }
 
-// Pipeline trace (debug/profiling): role 0 TMA issued, 1 dequant start, 2 dequant
-// done, 3 MMA issue, 4 accumulator ready (epilogue start), 5 epilogue done,
-// 6 e4m3 tile landed (seen by the dequantiser).
+// Pipeline trace (debug/profiling) of CTA 0: trace[1 + role * cap + index] =
+// %globaltimer for role 0 TMA issued, 1 dequant start, 2 dequant done, 3 MMA
+// issue, 4 accumulator ready (epilogue start), 5 epilogue done, 6 e4m3 tile
+// landed (seen by the dequantiser); cap = (entries - 1) / 8.
 __device__ __forceinline__ void trace_ev(const GemmArgs& a, int role, int idx) {
-  if (a.trace == nullptr || blockIdx.x != 0) return;
-  const unsigned long long n = atomicAdd(a.trace, 1ull);
-  if ((int)n < a.trace_cap) {
-    a.trace[1 + 2 * n] = ((unsigned long long)role << 32) | (unsigned)idx;
-    a.trace[2 + 2 * n] = globaltimer_ns();
-  }
+  // plain stores at [role][idx] (no atomics: a returned value would stall the recording role)
+  if (a.trace == nullptr || blockIdx.x != 0 || idx < 0 || idx >= a.trace_cap) return;
+  a.trace[1 + (size_t)role * a.trace_cap + idx] = globaltimer_ns();
 }
 
 // Two fp32 products in one instruction (sm_100 packed f32x2 multiply, IEEE
@@ -190,14 +198,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 
   // ---- shared-memory carve-up
   uint8_t* stage_base = smem;
-  uint8_t* conv_base = smem + C::STAGES * C::STAGE_BYTES;
+  uint8_t* conv_base = smem + C::RING_BYTES;
   uint8_t* epi_stage = conv_base + C::CONV_BYTES;            // [EPI_WARPS][16][32] 4-byte transpose buffers
   uint8_t* extra = epi_stage + C::EPI_STAGE;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);   // [12] TMA landed
-  uint64_t* empty_bar = full_bar + 12;                       // [12] load slot free
-  uint64_t* cfull_bar = empty_bar + 12;                      // [8] bf16 slot written
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(extra);   // [16] TMA landed
+  uint64_t* empty_bar = full_bar + 16;                       // [16] load slot free
+  uint64_t* cfull_bar = empty_bar + 16;                      // [8] bf16 slot written
   uint64_t* cempty_bar = cfull_bar + 8;                      // [8] bf16 slot consumed
-  uint64_t* accf_bar = cempty_bar + 8;
+  uint64_t* bfull_bar = cempty_bar + 8;                      // [16] activation tile landed (TMEM-ring mode)
+  uint64_t* bempty_bar = bfull_bar + 16;                     // [16] activation slot free
+  uint64_t* accf_bar = bempty_bar + 16;
   uint64_t* acce_bar = accf_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -207,8 +217,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   int* meta_slot = row_off + (kMaxGroups + 1);                 // [2][256] scatter slot per column
   float* meta_w = reinterpret_cast<float*>(meta_slot + 512);   // [2][256] routing weight per column
 
-  auto ALd = [&](int s, int a) { return stage_base + s * C::STAGE_BYTES + a * C::ALOAD_BYTES; };
-  auto Bt = [&](int s) { return stage_base + s * C::STAGE_BYTES + C::NA * C::ALOAD_BYTES; };
+  auto ALd = [&](int s, int a) {
+    return C::A_TMEM ? stage_base + s * C::A_STAGE_BYTES + a * C::ALOAD_BYTES
+                     : stage_base + s * C::STAGE_BYTES + a * C::ALOAD_BYTES;
+  };
+  // activation tile of load stage s (shared ring) or of B-ring slot s (TMEM-ring mode)
+  auto Bt = [&](int s) {
+    return C::A_TMEM ? stage_base + C::STAGES * C::A_STAGE_BYTES + s * C::B_BYTES
+                     : stage_base + s * C::STAGE_BYTES + C::NA * C::ALOAD_BYTES;
+  };
   auto A16 = [&](int j, int a) { return conv_base + (j * C::NA + a) * C::A16_BYTES; };
 
   const int warp = threadIdx.x >> 5;
@@ -247,7 +264,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   if (threadIdx.x == 32) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS + 1 : 1);  // fp8: the stage's dequant group + the MMA
+      // fp8: the stage's dequant group (+ the MMA when the stage also holds the activation tile)
+      mbar_init(&empty_bar[s], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS + (C::A_TMEM ? 0 : 1) : 1);
+    }
+    for (int s = 0; s < C::SB; ++s) {
+      mbar_init(&bfull_bar[s], 1);
+      mbar_init(&bempty_bar[s], 1);
     }
     for (int j = 0; j < 8; ++j) {
       mbar_init(&cfull_bar[j], AFP8 ? C::CONV_WARPS / C::DEQ_GROUPS : 1);
@@ -281,8 +303,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   if (warp == 0) {
     // ===================================================== TMA producer
     if (elect_one()) {
-      int s = 0;
-      uint32_t phase = 0;
+      int s = 0, sb = 0;
+      uint32_t phase = 0, bphase = 0;
       int pi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
@@ -291,19 +313,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         const int b_row = row_off[tc.g] + tc.j * BN;
         for (int ks = tc.ks0; ks < tc.ks1; ++ks) {
           if (!mbar_wait(&empty_bar[s], phase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_bar[s], C::TX_BYTES);
+          mbar_arrive_expect_tx(&full_bar[s], C::A_TMEM ? C::A_STAGE_BYTES : C::TX_BYTES);
           const int x = ks * kBK;
           if (AFP8 && args.a_tiled) {
-            // tile-major weights: stage ks of row tile r is rows [(r * k_stages + ks) * 128, +128) of a [*, 64] map
-            tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], 0, ((a_row >> 7) * k_stages + ks) * 128);
+            // tile-major weights: stage ks of row tile r is the 8 KB block r * k_stages + ks
+            const uint8_t* wb = static_cast<const uint8_t*>(args.a_base);
+            bulk_load(ALd(s, 0), wb + ((size_t)((a_row >> 7) * k_stages + ks) << 13), C::A8_BYTES, &full_bar[s]);
             if constexpr (PAIR)
-              tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], 0,
-                          (((a_row + args.pair_row_offset) >> 7) * k_stages + ks) * 128);
+              bulk_load(ALd(s, 1), wb + ((size_t)(((a_row + args.pair_row_offset) >> 7) * k_stages + ks) << 13),
+                        C::A8_BYTES, &full_bar[s]);
           } else {
             tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], x, a_row);
             if constexpr (PAIR) tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
           }
-          tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
+          if constexpr (C::A_TMEM) {
+            if (!mbar_wait(&bempty_bar[sb], bphase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&bfull_bar[sb], C::B_BYTES);
+            tma_load_2d(Bt(sb), &tmap_b, &bfull_bar[sb], x, b_row);
+            if (++sb == C::SB) { sb = 0; bphase ^= 1; }
+          } else {
+            tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
+          }
           trace_ev(args, 0, pi++);
           if (++s == C::STAGES) { s = 0; phase ^= 1; }
         }
@@ -319,7 +349,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     // ====================================================== MMA issuer
     if (elect_one()) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
-      int s = 0;
+      int s = 0;       // load stage (shared ring) or activation slot (TMEM-ring mode)
       uint32_t phase = 0;
       int lt = 0;
       int gi = 0;  // global stage counter (bf16 ring index)
@@ -332,7 +362,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         tc_fence_after();
         const uint32_t d_base = tmem_base + abuf * C::ACC_COLS;
         for (int ks = tc.ks0; ks < tc.ks1; ++ks, ++gi) {
-          if (!mbar_wait(&full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(C::A_TMEM ? &bfull_bar[s] : &full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
           const int cj = AFP8 ? gi % C::CONV_SLOTS : 0;
           const uint32_t cph = AFP8 ? (gi / C::CONV_SLOTS) & 1 : 0;
           if constexpr (AFP8) {
@@ -358,9 +391,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
               }
             }
           }
-          umma_commit(&empty_bar[s]);
+          umma_commit(C::A_TMEM ? &bempty_bar[s] : &empty_bar[s]);
           if constexpr (AFP8) umma_commit(&cempty_bar[cj]);
-          if (++s == C::STAGES) { s = 0; phase ^= 1; }
+          if (++s == (C::A_TMEM ? C::SB : C::STAGES)) { s = 0; phase ^= 1; }
         }
         if (!ok) break;
         umma_commit(&accf_bar[abuf]);
@@ -386,7 +419,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       const int quarter = warp & 3;
       const int wq = (dw % GW) / 4;
       const int row = quarter * 32 + lane;
-      const bool tracer = dw == 0 && lane == 0;
+      const bool tracer = (dw % GW) == 0 && lane == 0;  // one recorder per dequant group
       const int nkb = args.scale_k_blocks;
       const int pair_mb = C::NA > 1 ? args.pair_row_offset / 128 : 0;
       const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16) + C::TSLOT_COL0;
@@ -436,19 +469,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         for (int j = 0; j < CH; ++j) q[j] = *reinterpret_cast<const uint4*>(ALd(s, tile_of_chunk[j]) + src_off[j]);
         tc_fence_after();  // the MMAs that read this TMEM slot have completed (cempty)
         const uint32_t slot_addr = lane_addr + cj * (C::NA * 32);
+        uint32_t o[CH][8];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          uint32_t o[8];
-          dequant16(q[j], scale[tile_of_chunk[j]], o);
-          tmem_st8(slot_addr + col_off[j], o);
-        }
+        for (int j = 0; j < CH; ++j) dequant16(q[j], scale[tile_of_chunk[j]], o[j]);
+        // every lane's e4m3 reads have been consumed: the load slot is free for TMA
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+#pragma unroll
+        for (int j = 0; j < CH; ++j) tmem_st8(slot_addr + col_off[j], o[j]);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&empty_bar[s]);   // this warp is done with the e4m3 tile
-          mbar_arrive(&cfull_bar[cj]);  // and its rows of the bf16 tile are in TMEM
-        }
+        if (lane == 0) mbar_arrive(&cfull_bar[cj]);  // this warp's rows of the bf16 tile are in TMEM
         if (tracer) trace_ev(args, 2, gi);
         gi += kGroups;
         s += kGroups;
@@ -467,7 +499,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       for (int j = 0; j < CPL; ++j) {
         const int chunk = (dw % GW) * 32 + lane + j * GW * 32;
         const int row = chunk >> 2, c16 = chunk & 3;
-        src_off[j] = row * 64 + c16 * 16;
+        src_off[j] = row * 64 + ((c16 ^ ((row >> 1) & 3)) << 4);  // e4m3 tiles arrive 64-byte swizzled
         // 128B-swizzled K-major row: 16-byte unit u of row r lives at u ^ (r & 7)
         dst0[j] = row * 128 + (((2 * c16) ^ (row & 7)) << 4);
         dst1[j] = row * 128 + (((2 * c16 + 1) ^ (row & 7)) << 4);
@@ -727,11 +759,11 @@ static void launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   // A: [groups * rows_per_group, K] row-major, box 64 x 128 rows; tile-major e4m3
   // weights are addressed as [groups * rows_per_group * K / 64, 64]
   const int64_t a_rows = (int64_t)L.args.num_groups * L.args.a_rows_per_group;
-  // (the TMEM-ring dequantisers read e4m3 rows one lane per row: 64-byte swizzle)
-  const int a_swz = !AFP8 ? 128 : C::A_TMEM ? 64 : 0;
-  CUtensorMap ta = (AFP8 && L.args.a_tiled)
-                       ? make_tmap_2d(L.a, false, a_rows * (L.K / kBK), kBK, kBK, kBK, 128, a_swz)
-                       : make_tmap_2d(L.a, !AFP8, a_rows, L.K, L.a_row_stride_bytes, kBK, 128, a_swz);
+  // e4m3 tiles land 64-byte swizzled (the TMEM-ring dequantisers read one row per
+  // lane: conflict-free); tile-major weights carry the same order in memory
+  const int a_swz = !AFP8 ? 128 : 64;
+  // (tile-major e4m3 weights are fetched with bulk copies; the map is then unused)
+  CUtensorMap ta = make_tmap_2d(L.a, !AFP8, a_rows, L.K, L.a_row_stride_bytes, kBK, 128, a_swz);
   CUtensorMap tb = make_tmap_2d(L.b, true, L.b_rows, L.K, L.b_row_stride_bytes, kBK, BN, 128);
   // upper bound of work items without reading device counts
   int64_t max_tiles = ((int64_t)L.b_rows / BN + L.args.num_groups) * L.args.m_tiles * std::max(1, L.args.k_splits);
@@ -758,8 +790,8 @@ static void dispatch_bn(int bn, const GemmLaunch& L, cudaStream_t s) {
 
 void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
   if (L.args.num_groups < 1 || L.args.num_groups > kMaxGroups) throw std::runtime_error("bad group count");
-  if (L.args.a_tiled && (!L.a_fp8 || L.a_row_stride_bytes != L.K))
-    throw std::runtime_error("tile-major weights must be dense e4m3 [rows, K]");
+  if (L.args.a_tiled && (!L.a_fp8 || L.a_row_stride_bytes != L.K || (reinterpret_cast<uintptr_t>(L.args.a_base) & 15)))
+    throw std::runtime_error("tile-major weights must be dense, 16-byte aligned e4m3 [rows, K]");
   if (L.K % 128 != 0) throw std::runtime_error("K must be a multiple of 128");
   if (L.args.a_rows_per_group % 128 != 0) throw std::runtime_error("weight rows must be a multiple of 128");
   if ((reinterpret_cast<uintptr_t>(L.a) & 15) || (reinterpret_cast<uintptr_t>(L.b) & 15))

@@ -159,21 +159,38 @@ def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: 
 
 
 # ------------------------------------------------------- weight layout
+def _swizzle64_index(device) -> torch.Tensor:
+    # chunk u (16 bytes) of row r of a [128][64 B] block sits at chunk u ^ ((r >> 1) & 3)
+    r = torch.arange(128, device=device).view(128, 1)
+    u = torch.arange(4, device=device).view(1, 4)
+    return (u ^ ((r >> 1) & 3)).view(128, 4, 1).expand(128, 4, 16)
+
+
 def tile_fp8(w: torch.Tensor) -> torch.Tensor:
     """[..., N, K] e4m3 -> the same shape holding the bytes tile-major:
-    [..., N / 128, K / 64, 128, 64].  One GEMM pipeline stage (128 rows x 64 K)
-    is then one contiguous 8 KB block instead of 128 rows of 64 bytes 'K' apart,
-    which HBM serves at streaming rate."""
+    [..., N / 128, K / 64, 128, 64] with the four 16-byte chunks of each 64-byte
+    row in 64-byte-swizzle order (chunk u of row r at u ^ ((r >> 1) & 3)).  One
+    GEMM pipeline stage (128 rows x 64 K) is then one contiguous 8 KB block that a
+    single bulk copy brings into shared memory already in the layout the
+    dequantisers read without bank conflicts."""
     *lead, n, k = w.shape
     if n % 128 or k % 64:
         raise ValueError("tile_fp8 needs N % 128 == 0 and K % 64 == 0")
-    return w.reshape(*lead, n // 128, 128, k // 64, 64).transpose(-3, -2).contiguous().view(w.shape)
+    b = w.view(torch.uint8).reshape(*lead, n // 128, 128, k // 64, 64).transpose(-3, -2).contiguous()
+    b = b.view(-1, 128, 4, 16)
+    idx = _swizzle64_index(w.device).unsqueeze(0).expand(b.shape[0], 128, 4, 16)
+    out = torch.empty_like(b).scatter_(2, idx, b)
+    return out.view(w.shape).view(w.dtype)
 
 
 def untile_fp8(w: torch.Tensor) -> torch.Tensor:
     """Inverse of ``tile_fp8``."""
     *lead, n, k = w.shape
-    return w.reshape(*lead, n // 128, k // 64, 128, 64).transpose(-3, -2).contiguous().view(w.shape)
+    b = w.view(torch.uint8).reshape(-1, 128, 4, 16)
+    idx = _swizzle64_index(w.device).unsqueeze(0).expand(b.shape[0], 128, 4, 16)
+    b = torch.gather(b, 2, idx)
+    b = b.view(*lead, n // 128, k // 64, 128, 64).transpose(-3, -2).contiguous()
+    return b.view(w.shape).view(w.dtype)
 
 
 # --------------------------------------------------------------------- GEMM

@@ -144,9 +144,14 @@ def test_tile_major_fp8_layout_roundtrip():
     q = torch.stack([quantize_block_fp8(w[i])[0] for i in range(3)])
     t = ops.tile_fp8(q)
     assert t.shape == q.shape
-    # block (expert 1, row tile 1, K stage 2) is contiguous in the tiled bytes
-    blk = t[1].reshape(-1)[(1 * (384 // 64) + 2) * 8192:(1 * (384 // 64) + 3) * 8192].view(128, 64)
-    assert torch.equal(blk.view(torch.uint8), q[1, 128:256, 128:192].contiguous().view(torch.uint8))
+    # block (expert 1, row tile 1, K stage 2) is one contiguous 8 KB run; chunk u of
+    # row r sits at chunk u ^ ((r >> 1) & 3) (the 64-byte swizzle the GEMM reads)
+    blk = t[1].view(torch.uint8).reshape(-1)[(1 * (384 // 64) + 2) * 8192:(1 * (384 // 64) + 3) * 8192]
+    blk = blk.view(128, 4, 16)
+    want = q[1, 128:256, 128:192].contiguous().view(torch.uint8).view(128, 4, 16)
+    for r in (0, 1, 2, 5, 77, 127):
+        for u in range(4):
+            assert torch.equal(blk[r, u ^ ((r >> 1) & 3)], want[r, u])
     assert torch.equal(ops.untile_fp8(t).view(torch.uint8), q.view(torch.uint8))
     s = quantize_block_fp8(w[0])[1]
     x = torch.randn(5, 384).to(torch.bfloat16)
