@@ -110,7 +110,7 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
   if (trace.has_value()) {
     TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->is_contiguous(), "trace must be int64");
     L.args.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
-    L.args.trace_cap = (int)((trace->numel() - 1) / 8);
+    L.args.trace_cap = (int)((trace->numel() - 1) / 10);
   }
   L.a = weight.data_ptr();
   L.a_row_stride_bytes = K * weight.element_size();

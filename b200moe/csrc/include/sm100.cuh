@@ -82,6 +82,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Suspend-capable probe: the thread sleeps in hardware until the phase completes
+// or `hint_ns` elapses, so waiting warps leave the issue slots to working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Wake-up check interval of a suspended wait (the deadline and the abort flag are
+// re-read at least this often).
+constexpr uint32_t kWaitSleepNs = 20000;
+
 // Bounded parity wait.  Returns false (and records `code`) when the deadline
 // passes or another role already aborted (`*abort` set).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
@@ -89,7 +107,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
     if (abort != nullptr && *abort) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       record_status(status, code);

@@ -64,9 +64,15 @@ struct GemmCfg {
   static constexpr int EPI_WARPS = EPI_STAGED ? 8 : 4;
   static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
   static constexpr int EPI_STAGE = EPI_STAGED ? EPI_WARPS * 16 * 32 * 4 : 0;  // per warp: 16 cols x 32 rows x 4 B
+  // Single-tile TMEM-ring GEMMs (decode down / QKV / O) take 128 K per stage: the
+  // producer and MMA threads pay their per-stage cost (barrier probes, commits,
+  // descriptors) once per 8 MMAs instead of 4, which bounded them at decode size.
+  static constexpr bool WIDE_K = AFP8 && !PAIR && BN <= 128;
+  static constexpr int KS = WIDE_K ? 128 : kBK;       // K elements per pipeline stage
+  static constexpr int KSUB = KS / kBK;               // 64-wide sub-blocks per stage
   static constexpr int A16_BYTES = 128 * kBK * 2;     // 16 KB bf16 tile
-  static constexpr int A8_BYTES = 128 * kBK;          // 8 KB e4m3 tile
-  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int A8_BYTES = 128 * KS;           // e4m3 tile of one stage (8 or 16 KB)
+  static constexpr int B_BYTES = BN * KS * 2;         // KSUB 128-byte-swizzled [BN][64] atoms
   // load ring: what TMA writes (fp8 weights or, in bf16 mode, the UMMA-ready A tile)
   static constexpr int ALOAD_BYTES = AFP8 ? A8_BYTES : A16_BYTES;
   static constexpr int STAGE_BYTES = NA * ALOAD_BYTES + B_BYTES;
@@ -76,7 +82,8 @@ struct GemmCfg {
   // two accumulators holds the bf16 ring, and the shared memory it used to take
   // goes to e4m3 load stages -- these GEMMs are bound by the bytes in flight per SM.
   static constexpr bool A_TMEM = AFP8 && (PAIR ? BN <= 64 : BN <= 128);
-  static constexpr int TSLOTS_RAW = A_TMEM ? (512 - 2 * ACC_COLS) / (NA * 32) : 0;
+  static constexpr int SLOT_COLS = NA * KS / 2;       // TMEM columns of one bf16 ring slot
+  static constexpr int TSLOTS_RAW = A_TMEM ? (512 - 2 * ACC_COLS) / SLOT_COLS : 0;
   // bf16 slots: TMEM ring (up to 8) for decode-size tiles, else a shared-memory ring
   // of 2 for BN >= 128 (MMA-bound: the shared memory goes to deeper load stages for
   // the large B tiles)
@@ -87,7 +94,7 @@ struct GemmCfg {
   // TMEM-ring tiles split the load ring: e4m3 stages (freed by the dequantisers as
   // soon as they have read them) and a separate, deeper ring of activation tiles
   // (freed by the MMA), so weight bytes never wait for the MMA to release a slot
-  static constexpr int SB = !A_TMEM ? 0 : BN <= 32 ? (PAIR ? 12 : 16) : BN == 64 ? (PAIR ? 8 : 12) : 6;
+  static constexpr int SB = !A_TMEM ? 0 : PAIR ? (BN <= 32 ? 12 : 8) : BN <= 32 ? 8 : BN == 64 ? 6 : 3;
   static constexpr int A_STAGE_BYTES = NA * ALOAD_BYTES;
   static constexpr int STAGES_RAW = A_TMEM
       ? (kSmemBudget - EXTRA - 1024 - EPI_STAGE - SB * B_BYTES) / A_STAGE_BYTES
@@ -145,7 +152,8 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tile_prefix, 
 // Pipeline trace (debug/profiling) of CTA 0: trace[1 + role * cap + index] =
 // %globaltimer for role 0 TMA issued, 1 dequant start, 2 dequant done, 3 MMA
 // issue, 4 accumulator ready (epilogue start), 5 epilogue done, 6 e4m3 tile
-// landed (seen by the dequantiser); cap = (entries - 1) / 8.
+// landed (seen by the dequantiser), 7 producer reaches a stage, 8 its e4m3 slot
+// is free, 9 MMA thread reaches a stage; cap = (entries - 1) / 10.
 __device__ __forceinline__ void trace_ev(const GemmArgs& a, int role, int idx) {
   // plain stores at [role][idx] (no atomics: a returned value would stall the recording role)
   if (a.trace == nullptr || blockIdx.x != 0 || idx < 0 || idx >= a.trace_cap) return;
@@ -296,7 +304,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = tile_prefix[ngroups];
-  const int k_stages = args.k_stages;
+  const int k_stages = args.k_stages / C::KSUB;  // pipeline stages of K (the host counts 64-wide blocks)
   auto tile_of = [&](int t) { return decode_tile(t, tile_prefix, ngroups, m_tiles, k_stages, k_splits); };
   int* status = args.status;
 
@@ -312,24 +320,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         const int a_row = tc.g * args.a_rows_per_group + tc.i * 128;
         const int b_row = row_off[tc.g] + tc.j * BN;
         for (int ks = tc.ks0; ks < tc.ks1; ++ks) {
+          trace_ev(args, 7, pi);  // producer reaches the stage (before its slot waits)
           if (!mbar_wait(&empty_bar[s], phase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
+          trace_ev(args, 8, pi);  // A slot free
           mbar_arrive_expect_tx(&full_bar[s], C::A_TMEM ? C::A_STAGE_BYTES : C::TX_BYTES);
-          const int x = ks * kBK;
+          const int x = ks * C::KS;
           if (AFP8 && args.a_tiled) {
-            // tile-major weights: stage ks of row tile r is the 8 KB block r * k_stages + ks
+            // tile-major weights: 64-K block b of row tile r is the 8 KB block r * (K / 64) + b,
+            // so a stage (KSUB blocks) is one contiguous run
             const uint8_t* wb = static_cast<const uint8_t*>(args.a_base);
-            bulk_load(ALd(s, 0), wb + ((size_t)((a_row >> 7) * k_stages + ks) << 13), C::A8_BYTES, &full_bar[s]);
+            bulk_load(ALd(s, 0), wb + ((size_t)((a_row >> 7) * args.k_stages + ks * C::KSUB) << 13), C::A8_BYTES,
+                      &full_bar[s]);
             if constexpr (PAIR)
-              bulk_load(ALd(s, 1), wb + ((size_t)(((a_row + args.pair_row_offset) >> 7) * k_stages + ks) << 13),
+              bulk_load(ALd(s, 1),
+                        wb + ((size_t)(((a_row + args.pair_row_offset) >> 7) * args.k_stages + ks * C::KSUB) << 13),
                         C::A8_BYTES, &full_bar[s]);
           } else {
-            tma_load_2d(ALd(s, 0), &tmap_a, &full_bar[s], x, a_row);
-            if constexpr (PAIR) tma_load_2d(ALd(s, 1), &tmap_a, &full_bar[s], x, a_row + args.pair_row_offset);
+#pragma unroll
+            for (int sub = 0; sub < C::KSUB; ++sub) {
+              tma_load_2d(ALd(s, 0) + sub * 8192, &tmap_a, &full_bar[s], x + sub * kBK, a_row);
+              if constexpr (PAIR)
+                tma_load_2d(ALd(s, 1) + sub * 8192, &tmap_a, &full_bar[s], x + sub * kBK, a_row + args.pair_row_offset);
+            }
           }
           if constexpr (C::A_TMEM) {
             if (!mbar_wait(&bempty_bar[sb], bphase ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
             mbar_arrive_expect_tx(&bfull_bar[sb], C::B_BYTES);
-            tma_load_2d(Bt(sb), &tmap_b, &bfull_bar[sb], x, b_row);
+#pragma unroll
+            for (int sub = 0; sub < C::KSUB; ++sub)
+              tma_load_2d(Bt(sb) + sub * (BN * 128), &tmap_b, &bfull_bar[sb], x + sub * kBK, b_row);
             if (++sb == C::SB) { sb = 0; bphase ^= 1; }
           } else {
             tma_load_2d(Bt(s), &tmap_b, &full_bar[s], x, b_row);
@@ -362,6 +381,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         tc_fence_after();
         const uint32_t d_base = tmem_base + abuf * C::ACC_COLS;
         for (int ks = tc.ks0; ks < tc.ks1; ++ks, ++gi) {
+          trace_ev(args, 9, gi);  // MMA thread reaches the stage (before its waits)
           if (!mbar_wait(C::A_TMEM ? &bfull_bar[s] : &full_bar[s], phase, status, kStatusTimeoutFull, abort_flag)) {
             ok = false;
             break;
@@ -375,15 +395,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
           trace_ev(args, 3, gi);
           const uint32_t b_addr = smem_u32(Bt(s));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t bdesc = umma_sdesc_sw128(b_addr + k * 32);
+          for (int k = 0; k < C::KS / 16; ++k) {
+            const uint64_t bdesc = umma_sdesc_sw128(b_addr + (k >> 2) * (BN * 128) + (k & 3) * 32);
 #pragma unroll
             for (int a = 0; a < C::NA; ++a) {
               const uint32_t acc = (ks != tc.ks0 || k != 0) ? 1u : 0u;
               if constexpr (C::A_TMEM) {
-                // bf16 A of slot cj: NA tiles x 32 columns, K = 16 per 8 columns
-                umma_f16_ts(d_base + a * BN, tmem_base + C::TSLOT_COL0 + cj * (C::NA * 32) + a * 32 + k * 8,
-                            bdesc, idesc, acc);
+                // bf16 A of slot cj: NA tiles x KS/2 columns, K = 16 per 8 columns
+                umma_f16_ts(d_base + a * BN,
+                            tmem_base + C::TSLOT_COL0 + cj * C::SLOT_COLS + a * (C::KS / 2) + k * 8, bdesc, idesc,
+                            acc);
               } else {
                 const uint8_t* abuf_ptr = AFP8 ? A16(cj, a) : ALd(s, a);
                 const uint64_t adesc = umma_sdesc_sw128(smem_u32(abuf_ptr) + k * 32);
@@ -408,12 +429,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     if constexpr (AFP8 && C::A_TMEM) {
       // bf16 ring in TMEM: a lane converts chunks of its own row (TMEM lane = row;
       // warp w may only address lane quarter w & 3) and stores them with tcgen05.st.
-      // The e4m3 tile arrives 64-byte swizzled, so the 32 lanes' row reads are
-      // bank-conflict-free.
+      // The e4m3 tile arrives as 64-byte-swizzled [128][64] sub-blocks (8 KB each),
+      // so the 32 lanes' row reads are bank-conflict-free.
       constexpr int kGroups = C::DEQ_GROUPS;
       constexpr int GW = C::CONV_WARPS / kGroups;          // warps per group
       constexpr int WPQ = GW / 4;                          // warps per lane quarter in a group
-      constexpr int CH = C::NA * 4 / WPQ;                  // 16-byte chunks of its row a lane converts per stage
+      constexpr int CPT = C::KS / 16;                      // 16-byte chunks of a row per tile per stage
+      constexpr int CH = C::NA * CPT / WPQ;                // chunks of its row a lane converts per stage
+      constexpr int BATCH = CH < 4 ? CH : 4;               // chunks in registers at a time
+      static_assert(CH % BATCH == 0, "chunk batches");
       const int dw = warp - 2;
       const int group = dw / GW;
       const int quarter = warp & 3;
@@ -423,14 +447,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
       const int nkb = args.scale_k_blocks;
       const int pair_mb = C::NA > 1 ? args.pair_row_offset / 128 : 0;
       const uint32_t lane_addr = tmem_base + (uint32_t(quarter * 32) << 16) + C::TSLOT_COL0;
-      int src_off[CH], col_off[CH], tile_of_chunk[CH];
-#pragma unroll
-      for (int j = 0; j < CH; ++j) {
-        const int c = wq * CH + j, a = c >> 2, kc = c & 3;
-        tile_of_chunk[j] = a;
-        src_off[j] = row * 64 + ((kc ^ ((row >> 1) & 3)) << 4);
-        col_off[j] = a * 32 + kc * 8;
-      }
+      const int swz = (row >> 1) & 3;
       int t = blockIdx.x, ks = -1, ks1 = 0;
       TileCoord tc{};
       auto advance = [&]() -> bool {
@@ -443,7 +460,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         return true;
       };
       auto load_scales = [&](float (&out)[C::NA]) {
-        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * nkb + (ks * kBK) / 128;
+        const float* sc = args.a_scale + (size_t)tc.g * args.scale_m_blocks * nkb + (ks * C::KS) / 128;
         out[0] = __ldg(sc + tc.i * nkb);
         if constexpr (C::NA > 1) out[1] = __ldg(sc + (tc.i + pair_mb) * nkb);
       };
@@ -464,19 +481,33 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         w_ok = w_ok && mbar_wait(&cempty_bar[cj], cph ^ 1, status, kStatusTimeoutConv, abort_flag);
         if (!__all_sync(0xffffffffu, w_ok)) break;
         if (tracer) trace_ev(args, 1, gi);
-        uint4 q[CH];
-#pragma unroll
-        for (int j = 0; j < CH; ++j) q[j] = *reinterpret_cast<const uint4*>(ALd(s, tile_of_chunk[j]) + src_off[j]);
         tc_fence_after();  // the MMAs that read this TMEM slot have completed (cempty)
-        const uint32_t slot_addr = lane_addr + cj * (C::NA * 32);
-        uint32_t o[CH][8];
+        const uint32_t slot_addr = lane_addr + cj * C::SLOT_COLS;
 #pragma unroll
-        for (int j = 0; j < CH; ++j) dequant16(q[j], scale[tile_of_chunk[j]], o[j]);
-        // every lane's e4m3 reads have been consumed: the load slot is free for TMA
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        for (int j0 = 0; j0 < CH; j0 += BATCH) {
+          uint4 q[BATCH];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) tmem_st8(slot_addr + col_off[j], o[j]);
+          for (int j = 0; j < BATCH; ++j) {
+            const int c = wq * CH + j0 + j, a = c / CPT, kc = c % CPT;
+            q[j] = *reinterpret_cast<const uint4*>(ALd(s, a) + (kc >> 2) * 8192 + row * 64 + (((kc & 3) ^ swz) << 4));
+          }
+          uint32_t o[BATCH][8];
+#pragma unroll
+          for (int j = 0; j < BATCH; ++j) {
+            const int c = wq * CH + j0 + j;
+            dequant16(q[j], scale[c / CPT], o[j]);
+          }
+          if (j0 + BATCH == CH) {
+            // every lane's e4m3 reads have been consumed: the load slot is free for TMA
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[s]);
+          }
+#pragma unroll
+          for (int j = 0; j < BATCH; ++j) {
+            const int c = wq * CH + j0 + j, a = c / CPT, kc = c % CPT;
+            tmem_st8(slot_addr + a * (C::KS / 2) + kc * 8, o[j]);
+          }
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -811,8 +842,10 @@ void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
   const int bn = L.bn;
   if (L.args.k_splits > 1) {
     if (L.epi != kEpiF32 || L.pair) throw std::runtime_error("split-K needs the fp32 epilogue");
-    const int per = (L.args.k_stages + L.args.k_splits - 1) / L.args.k_splits;
-    if ((L.args.k_splits - 1) * per >= L.args.k_stages) throw std::runtime_error("split-K leaves a split empty");
+    // e4m3 single-tile GEMMs with token tiles up to 128 run 128-wide K stages
+    const int stages = (L.a_fp8 && bn <= 128) ? L.args.k_stages / 2 : L.args.k_stages;
+    const int per = (stages + L.args.k_splits - 1) / L.args.k_splits;
+    if ((L.args.k_splits - 1) * per >= stages) throw std::runtime_error("split-K leaves a split empty");
   }
   if (L.pair) {
     if (!L.a_fp8 || L.epi != kEpiSiluPair) throw std::runtime_error("pair mode is fp8 + silu only");

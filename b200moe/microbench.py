@@ -236,18 +236,20 @@ def case_step(T, ctx, iters, layers=48):
 
 def _trace_summary(name, buf):
     import statistics
-    cap = (buf.numel() - 1) // 8
-    slots = buf[1:1 + 8 * cap].view(8, cap).tolist()
+    cap = (buf.numel() - 1) // 10
+    slots = buf[1:1 + 10 * cap].view(10, cap).tolist()
     by = {r: {i: t for i, t in enumerate(row) if t} for r, row in enumerate(slots)}
     med = lambda xs: round(statistics.median(xs) / 1e3, 3) if xs else None
     issue, c0, c1, mma = (by.get(r, {}) for r in (0, 1, 2, 3))
     idx = sorted(set(issue) & set(c0) & set(c1) & set(mma)) or sorted(set(issue) & set(mma))
     d = {"kernel": name, "stages_traced": len(idx)}
     if os.environ.get("B200MOE_TRACE_DUMP") and idx:
-        # stage timeline (us from the first issue): issue, landed, dequant start/end, MMA issue
+        # stage timeline (us from the first issue): producer reaches, A slot free, issued, landed,
+        # dequant start/end, MMA thread reaches, MMA issued
         t0 = min(issue.values())
         for i in idx[40:72]:
-            row = [round((r[i] - t0) / 1e3, 2) if i in r else None for r in (issue, by.get(6, {}), c0, c1, mma)]
+            row = [round((r[i] - t0) / 1e3, 2) if i in r else None
+                   for r in (by.get(7, {}), by.get(8, {}), issue, by.get(6, {}), c0, c1, by.get(9, {}), mma)]
             print(json.dumps({"trace": name, "stage": i, "t": row}))
     if len(idx) > 2:
         d["us_between_tma_issues"] = med([issue[b] - issue[a] for a, b in zip(idx, idx[1:])])
@@ -277,7 +279,7 @@ def _trace_summary(name, buf):
 
 def case_trace(T):
     """Per-stage timeline of CTA 0 for the decode-size GEMMs."""
-    buf = torch.zeros(1 + 8 * 4096, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(1 + 10 * 4096, dtype=torch.int64, device="cuda")
     H, I, E, k = 2048, 768, 128, 8
     x = (torch.randn(T, 4096, device="cuda") * 0.5).to(torch.bfloat16)
     q, s = fp8_weight(1, H, 4096, 4)

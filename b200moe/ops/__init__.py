@@ -148,9 +148,11 @@ def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: 
     for bn in (16, 32, 64, 128, 256):
         if bn > 16 and bn >= 2 * rows:
             break
-        for splits in range(1, max(1, k_stages // 2) + 1):
-            per = math.ceil(k_stages / splits)
-            if math.ceil(k_stages / per) != splits:
+        # e4m3 tiles of up to 128 tokens run 128-wide K stages (two 64-wide blocks)
+        ks = k_stages // 2 if fp8 and bn <= 128 else k_stages
+        for splits in range(1, max(1, ks // 2) + 1):
+            per = math.ceil(ks / splits)
+            if math.ceil(ks / per) != splits:
                 continue  # would leave a split empty
             t = _dense_cost_us(rows, m_tiles, k_stages, bn, splits, sms, fp8)
             if t < best_t:
