@@ -405,14 +405,15 @@ void kv_blocks_copy(Tensor src_pool, Tensor src_ids, int64_t dst_ptr, Tensor dst
 }
 
 void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
-                  c10::optional<Tensor> counts) {
+                  c10::optional<Tensor> counts, c10::optional<Tensor> status) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16);
   CHECK_CONTIG(w); CHECK_DT(w, torch::kBFloat16);
   CHECK_DT(ids, torch::kInt32); CHECK_DT(weights, torch::kFloat32);
   TORCH_CHECK(x.size(1) == w.size(1) && w.size(0) >= num_experts, "router shapes");
   TORCH_CHECK(ids.numel() >= x.size(0) * topk && weights.numel() >= x.size(0) * topk, "router outputs too small");
-  b200::router_fused(x.data_ptr(), w.data_ptr(), (int)x.size(0), (int)x.size(1), (int)num_experts, (int)topk, renorm,
-                     ids.data_ptr<int>(), weights.data_ptr<float>(), ptr_or_null<int>(counts), stream());
+  b200::router_fused(x.data_ptr(), w.data_ptr(), (int)x.size(0), (int)x.size(1), (int)num_experts, (int)w.size(0),
+                     (int)topk, renorm, ids.data_ptr<int>(), weights.data_ptr<float>(), ptr_or_null<int>(counts),
+                     ptr_or_null<int>(status), stream());
 }
 
 // residual += bf16(sum of split-K partials); out = rmsnorm(residual) * weight

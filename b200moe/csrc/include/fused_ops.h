@@ -51,8 +51,8 @@ void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, co
                     int64_t block_bytes, cudaStream_t s);
 // Router GEMM (x [T, H] bf16 . w[:E]^T, fp32 accumulate, bf16-rounded logits) +
 // softmax + top-k in one launch; E <= 128.
-void router_fused(const void* x, const void* w, int T, int H, int E, int topk, bool renorm, int* ids, float* weights,
-                  int* counts, cudaStream_t s);
+void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows, int topk, bool renorm, int* ids,
+                  float* weights, int* counts, int* status, cudaStream_t s);
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
                  void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s);
 

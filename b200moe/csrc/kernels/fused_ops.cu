@@ -15,6 +15,8 @@
 //
 // Rows are processed with 16-byte vector accesses; one CTA (or warp) per token.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <vector>
 #include <cuda_bf16.h>
 #include <algorithm>
 #include <cstdint>
@@ -323,63 +325,62 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
 // ------------------------------------------------------------ fused router
 // Router GEMM + softmax + top-k in one launch (replaces GEMM, split-K reduce and
 // top-k).  CTA = 16 tokens x all experts (<= 128); warp w owns experts
-// [16w, 16w + 16).  x and router rows stream through a double-buffered
-// cp.async ring of 64-wide K chunks (128-byte rows, 16-byte units XOR-swizzled
-// by row) into the warp-level bf16 MMA with fp32 accumulation; the logits go
-// through shared memory to one warp per token for the top-k.
+// [16w, 16w + 16).  One thread streams 64-wide K chunks of x (box 64 x 16) and of
+// the router weight (box 64 x 128) with TMA into an 8-deep mbarrier ring
+// (128-byte swizzle: 16-byte unit u of row r at u ^ (r & 7), which the ldmatrix
+// addressing below reads without bank conflicts); the warp-level bf16 MMAs
+// accumulate in fp32 and the logits go through shared memory to one warp per
+// token for the top-k.  Per-thread 16-byte cp.async (about 1150 requests per
+// chunk) held a CTA near 20 GB/s; a TMA box is one request.
 constexpr int kRtTok = 16, kRtE = 128, kRtK = 64;
-// K chunks in flight: a CTA streams the whole router weight (E x H bf16), so the
-// ring must cover the load latency (two stages left each chunk waiting a round trip)
 constexpr int kRtStages = 8;
 constexpr int kRtChunkBytes = (kRtTok + kRtE) * 128;
-constexpr int kRtSmem = kRtStages * kRtChunkBytes + kRtTok * (kRtE + 1) * 4;
+constexpr int kRtSmem = 1024 + kRtStages * kRtChunkBytes + kRtTok * (kRtE + 1) * 4 + kRtStages * 8 + 16;
 
 __device__ __forceinline__ uint32_t rt_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
-__device__ __forceinline__ void rt_cp16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-
-__global__ void __launch_bounds__(256) router_fused_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                           int T, int H, int E, int topk, int renorm,
-                                                           int* __restrict__ ids, float* __restrict__ weights,
-                                                           int* __restrict__ counts) {
+__global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                           const __grid_constant__ CUtensorMap wmap, int T, int H,
+                                                           int E, int topk, int renorm, int* __restrict__ ids,
+                                                           float* __restrict__ weights, int* __restrict__ counts,
+                                                           int* __restrict__ status) {
   constexpr int XB = kRtTok * 128;  // bytes of one x chunk (the W chunk follows it)
-  extern __shared__ __align__(128) uint8_t rt_smem[];
-  uint8_t* ring = rt_smem;          // [kRtStages][kRtChunkBytes]
-  float(*logit)[kRtE + 1] = reinterpret_cast<float(*)[kRtE + 1]>(rt_smem + kRtStages * kRtChunkBytes);
+  extern __shared__ __align__(1024) uint8_t rt_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_raw) + 1023) & ~uintptr_t(1023));
+  float(*logit)[kRtE + 1] = reinterpret_cast<float(*)[kRtE + 1]>(ring + kRtStages * kRtChunkBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRtStages * kRtChunkBytes + kRtTok * (kRtE + 1) * 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + kRtStages);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRtTok;
   const int nchunks = H / kRtK;
-  auto load = [&](int c, int buf) {
-    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(ring + buf * kRtChunkBytes));
-    for (int i = threadIdx.x; i < (kRtTok + kRtE) * 8; i += 256) {
-      const int row = i >> 3, u = i & 7;
-      if (row < kRtTok) {
-        const int t = t0 + row;
-        rt_cp16(base + rt_off(row, u), x + (size_t)min(t, T - 1) * H + c * kRtK + u * 8, t < T);
-      } else {
-        const int e = row - kRtTok;
-        rt_cp16(base + XB + rt_off(e, u), w + (size_t)e * H + c * kRtK + u * 8, e < E);
-      }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRtStages; ++i) mbar_init(&full[i], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    uint8_t* dst = ring + (c % kRtStages) * kRtChunkBytes;
+    mbar_arrive_expect_tx(&full[c % kRtStages], kRtChunkBytes);
+    tma_load_2d(dst, &xmap, &full[c % kRtStages], c * kRtK, t0);        // rows >= T come back zero-filled
+    tma_load_2d(dst + XB, &wmap, &full[c % kRtStages], c * kRtK, 0);
   };
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&xmap);
+    tma_prefetch_desc(&wmap);
+    for (int c = 0; c < kRtStages - 1 && c < nchunks; ++c) issue(c);
+  }
   float acc[2][4];
 #pragma unroll
   for (int n = 0; n < 2; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-  for (int c = 0; c < kRtStages - 1; ++c) {
-    if (c < nchunks) load(c, c);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-  }
+  bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
-    asm volatile("cp.async.wait_group %0;" ::"n"(kRtStages - 2) : "memory");
-    __syncthreads();  // chunk c landed for every thread; chunk c-1's buffer is free
-    const int nc = c + kRtStages - 1;
-    if (nc < nchunks) load(nc, nc % kRtStages);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
+    // chunk c - 1's buffer was released by the barrier that ended the previous iteration
+    if (threadIdx.x == 0 && c + kRtStages - 1 < nchunks) issue(c + kRtStages - 1);
+    ok = mbar_wait(&full[c % kRtStages], (c / kRtStages) & 1, status, kStatusTimeoutFull, abort_flag);
+    if (!__syncthreads_and(ok)) { ok = false; break; }
     const uint32_t xs = static_cast<uint32_t>(__cvta_generic_to_shared(ring + (c % kRtStages) * kRtChunkBytes));
     const uint32_t ws = xs + XB;
 #pragma unroll
@@ -406,8 +407,16 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const bf16* __restric
                    : "+f"(acc[1][0]), "+f"(acc[1][1]), "+f"(acc[1][2]), "+f"(acc[1][3])
                    : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b2), "r"(b3));
     }
+    __syncthreads();  // every warp is done with chunk c: its buffer may be refilled
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (!ok) {
+    if (threadIdx.x == 0) {
+      // a wait gave up: let the copies already issued land before the CTA exits
+      const uint64_t tw = globaltimer_ns();
+      while (globaltimer_ns() - tw < 1000000ull) __nanosleep(1000);
+    }
+    return;
+  }
 #pragma unroll
   for (int n = 0; n < 2; ++n)
 #pragma unroll
@@ -591,18 +600,55 @@ void router_topk(const float* logits, int ld, int T, int E, int topk, bool renor
   check_launch("router_topk");
 }
 
-void router_fused(const void* x, const void* w, int T, int H, int E, int topk, bool renorm, int* ids, float* weights,
-                  int* counts, cudaStream_t s) {
+static PFN_cuTensorMapEncodeTiled_v12000 rt_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point not available");
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// [rows, H] bf16, box 64 x box_rows, 128-byte swizzle; the last few maps are cached
+static CUtensorMap rt_map(const void* base, int rows, int H, int box_rows) {
+  struct Entry { const void* base; int rows, H, box; CUtensorMap map; };
+  static thread_local std::vector<Entry> cache;
+  for (auto& e : cache)
+    if (e.base == base && e.rows == rows && e.H == H && e.box == box_rows) return e.map;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)H * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kRtK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = rt_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("router tensor map: encode failed " + std::to_string((int)r));
+  if (cache.size() >= 64) cache.erase(cache.begin());
+  cache.push_back({base, rows, H, box_rows, map});
+  return map;
+}
+
+void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows, int topk, bool renorm, int* ids,
+                  float* weights, int* counts, int* status, cudaStream_t s) {
   if (T == 0) return;
-  if (E > kRtE || topk < 1 || topk > 8 || H % kRtK)
-    throw std::runtime_error("router_fused: needs <= 128 experts, top-k in [1, 8], hidden % 64 == 0");
+  if (E > kRtE || w_rows < kRtE || topk < 1 || topk > 8 || H % kRtK)
+    throw std::runtime_error("router_fused: needs <= 128 experts (weight padded to 128 rows), top-k in [1, 8], "
+                             "hidden % 64 == 0");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    throw std::runtime_error("router_fused: operands must be 16-byte aligned");
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(router_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem);
     attr = true;
   }
-  router_fused_kernel<<<(T + kRtTok - 1) / kRtTok, 256, kRtSmem, s>>>((const bf16*)x, (const bf16*)w, T, H, E,
-                                                                       topk, renorm ? 1 : 0, ids, weights, counts);
+  const CUtensorMap xm = rt_map(x, T, H, kRtTok);
+  const CUtensorMap wm = rt_map(w, kRtE, H, kRtE);
+  router_fused_kernel<<<(T + kRtTok - 1) / kRtTok, 256, kRtSmem, s>>>(xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,
+                                                                       weights, counts, status);
   check_launch("router_fused");
 }
 

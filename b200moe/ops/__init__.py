@@ -380,7 +380,7 @@ def router_topk(logits, num_experts, topk, renorm, ids, weights, counts=None):
 def router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts=None):
     """Router GEMM + softmax + top-k in one native launch (num_experts <= 128);
     same rounding points as ``linear`` + ``router_topk``."""
-    native().router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts)
+    native().router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts, status_word(x.device))
     count_launches()
 
 
