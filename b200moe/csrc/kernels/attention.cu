@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <stdexcept>
@@ -671,6 +672,280 @@ __global__ void __launch_bounds__(160) decode_attn_tma_kernel(const __grid_const
   }
 }
 
+// ------------------------------------------------- persistent TMA decode
+// Same tile pipeline as decode_attn_tma_kernel, but a CTA (two per SM) walks a
+// strided list of (sequence, kv head, split) items and its producer warp streams
+// the next item's tiles while the consumer warps finish the current one: the
+// per-item set-up (Q staging, block-table gather, pipeline fill) and the
+// cross-warp merge no longer leave the ring idle, and there is no wave tail.
+template <int D>
+struct DecPersist {
+  static constexpr int TILE = kKT * D * 2;
+  static constexpr int RING = kTmaStages * 2 * TILE;
+  static constexpr int BTAB = 256;
+  static constexpr int SMEM = 1024 + RING + 16 * D * 2 + 16 * D * 4 + 2 * 64 * 4 + 2 * kTmaStages * 8 + 16 + BTAB * 4 + 16;
+};
+
+template <int D>
+__global__ void __launch_bounds__(160) decode_attn_persist_kernel(const __grid_constant__ CUtensorMap kv_map,
+                                                                 const DecodeArgs a, int sub_rows, int oob_block,
+                                                                 int n_items) {
+  constexpr int NC = 128;  // consumer threads
+  using C = DecPersist<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;                                      // stage s: K tile at s*2*TILE, V tile after it
+  uint8_t* sQ = ring + C::RING;                              // [16][D] bf16
+  float* sO = reinterpret_cast<float*>(sQ + 16 * D * 2);     // [16][D] merged output of the current item
+  float* sM = sO + 16 * D;                                   // [4][16]
+  float* sL = sM + 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sL + 64);
+  uint64_t* empty = full + kTmaStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kTmaStages);
+  int* sBt = reinterpret_cast<int*>(empty + kTmaStages) + 4;  // [BTAB] block ids of the producer's item
+  volatile int* sStop = sBt + C::BTAB;  // consumers' copy of the abort flag (read between their barriers)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.group;
+  const int nq = a.num_kv_heads * G;
+  const int S = a.num_splits;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTmaStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    *abort_flag = 0;
+    *sStop = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < 16 * D; i += blockDim.x) sO[i] = 0.f;
+  __syncthreads();
+
+  // item w -> (sequence b, kv head h, split), keys [k_begin, k_end)
+  struct Item { int b, h, split, k_begin, k_end, ntiles; };
+  auto item = [&](int w) {
+    Item it;
+    it.split = w % S;
+    w /= S;
+    it.h = w % a.num_kv_heads;
+    it.b = w / a.num_kv_heads;
+    const int L = a.seq_lens[it.b];
+    it.k_begin = it.split * a.split_len;
+    it.k_end = min(L, it.k_begin + a.split_len);
+    it.ntiles = it.k_end > it.k_begin ? (it.k_end - it.k_begin + kKT - 1) / kKT : 0;
+    return it;
+  };
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    int tc = 0;  // tiles issued by this CTA (ring position)
+    for (int w = blockIdx.x; w < n_items && !*abort_flag; w += gridDim.x) {
+      const Item it = item(w);
+      if (it.ntiles == 0) continue;
+      const int* btab = a.block_tables + (size_t)it.b * a.max_blocks;
+      const int blk0 = it.k_begin / a.block_size;
+      const int nblk = (it.k_end - 1) / a.block_size - blk0 + 1;
+      const bool staged = nblk <= C::BTAB;
+      if (staged)
+        for (int i = lane; i < nblk; i += 32) sBt[i] = btab[blk0 + i];
+      __syncwarp();
+      if (lane == 0) {
+        if (w == (int)blockIdx.x) tma_prefetch_desc(&kv_map);
+        const int nsub = kKT / sub_rows;
+        for (int t = 0; t < it.ntiles; ++t, ++tc) {
+          const int st = tc % kTmaStages;
+          const uint32_t ph = (tc / kTmaStages) & 1;
+          if (!mbar_wait(&empty[st], ph ^ 1, a.status, kStatusTimeoutEmpty, abort_flag)) break;
+          mbar_arrive_expect_tx(&full[st], 2 * C::TILE);
+          const uint32_t sk = smem_u32(ring + st * 2 * C::TILE), sv = sk + C::TILE;
+          const int k0 = it.k_begin + t * kKT;
+          for (int j = 0; j < nsub; ++j) {
+            const int key = k0 + j * sub_rows;
+            // keys past the sequence read a block coordinate outside the map: TMA zero-fills
+            const int blk = key >= it.k_end ? oob_block
+                            : staged ? sBt[key / a.block_size - blk0] : btab[key / a.block_size];
+            const int y = key % a.block_size;
+#pragma unroll
+            for (int hf = 0; hf < D / 64; ++hf) {
+              const uint32_t off = hf * (kKT * 128) + j * sub_rows * 128;
+              tma_load_4d(sk + off, &kv_map, &full[st], hf * 64, y, it.h, blk);
+              tma_load_4d(sv + off, &kv_map, &full[st], hf * 64, y, a.num_kv_heads + it.h, blk);
+            }
+          }
+        }
+      }
+      tc = __shfl_sync(0xffffffffu, tc, 0);
+      __syncwarp();  // lane 0 has issued every tile of the item before sBt is overwritten
+    }
+    if (lane == 0 && *abort_flag) {
+      // a wait gave up: let loads already issued (valid sources) land before the CTA exits
+      const uint64_t t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 1000000ull) __nanosleep(1000);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const float sl2 = a.scale * 1.4426950408889634f;
+    const int r0 = lane >> 2;
+    int tc = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+      const Item it = item(w);
+      if (it.ntiles == 0) continue;
+      named_barrier_sync(1, NC);  // the previous item's readers of sQ / sM / sL are done
+      // every consumer warp takes the same exit (a divergent one would strand the
+      // others at a named barrier): the flag copy was written before the last barrier
+      if (*sStop) break;
+      const bf16* qsrc = static_cast<const bf16*>(a.q) + ((size_t)it.b * nq + (size_t)it.h * G) * D;
+      for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += NC) {
+        const int r = idx / (D / 8), c = idx % (D / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < G) v = *reinterpret_cast<const uint4*>(qsrc + (size_t)r * D + c * 8);
+        *reinterpret_cast<uint4*>(sQ + tile_off<D>(r, c)) = v;
+      }
+      named_barrier_sync(1, NC);
+      uint32_t qf[D / 16][4];
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = (mi & 1) * 8 + rr, chunk = ks * 2 + (mi >> 1);
+        ldmatrix_x4(smem_u32(sQ) + tile_off<D>(row, chunk), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+      }
+      float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+      float o[D / 8][4];
+#pragma unroll
+      for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+      for (int t = 0; t < it.ntiles; ++t, ++tc) {
+        const int st = tc % kTmaStages;
+        const uint32_t ph = (tc / kTmaStages) & 1;
+        ok = mbar_wait(&full[st], ph, a.status, kStatusTimeoutFull, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        const uint32_t sk = smem_u32(ring + st * 2 * C::TILE), sv = sk + C::TILE;
+        float sc[2][4];
+        qk_mma<D, 2, true>(sc, qf, sk, warp * 16, lane);
+        const int key0 = it.k_begin + t * kKT + warp * 16;
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = key0 + n * 8 + 2 * (lane & 3) + (e & 1);
+            sc[n][e] = key < it.k_end ? sc[n][e] * sl2 : -INFINITY;
+            mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+          }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        }
+        // lazy rescale: move the reference max only when a row grew by > 2^8
+        const bool grow0 = mx[0] > m_r[0] + kLazyLog2, grow1 = mx[1] > m_r[1] + kLazyLog2;
+        if (__any_sync(0xffffffffu, grow0 || grow1)) {
+          float corr[2];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const bool g = r ? grow1 : grow0;
+            const float mn = g ? mx[r] : m_r[r];
+            corr[r] = (m_r[r] == -INFINITY || !g) ? 1.f : exp2f(m_r[r] - mn);
+            m_r[r] = mn;
+            l_r[r] *= corr[r];
+          }
+#pragma unroll
+          for (int n = 0; n < D / 8; ++n) {
+            o[n][0] *= corr[0]; o[n][1] *= corr[0];
+            o[n][2] *= corr[1]; o[n][3] *= corr[1];
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float mm = m_r[e >> 1];
+            const float p = mm == -INFINITY ? 0.f : exp2f(sc[n][e] - mm);
+            sc[n][e] = p;
+            l_r[e >> 1] += p;
+          }
+        uint32_t pf[4];
+        pf[0] = pack_bf16(sc[0][0], sc[0][1]);
+        pf[1] = pack_bf16(sc[0][2], sc[0][3]);
+        pf[2] = pack_bf16(sc[1][0], sc[1][1]);
+        pf[3] = pack_bf16(sc[1][2], sc[1][3]);
+        pv_mma<D, true>(o, pf, sv, warp * 16, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+      }
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; }
+      // ---- merge the 4 warps (each saw a quarter of every tile's keys) into sO
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        float l = l_r[r];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        l_r[r] = l;
+      }
+      if ((lane & 3) == 0) {
+        sM[warp * 16 + r0] = m_r[0];
+        sM[warp * 16 + r0 + 8] = m_r[1];
+        sL[warp * 16 + r0] = l_r[0];
+        sL[warp * 16 + r0 + 8] = l_r[1];
+      }
+      named_barrier_sync(1, NC);
+      float wscale[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = r0 + 8 * r;
+        float m = -INFINITY;
+        for (int q = 0; q < 4; ++q) m = fmaxf(m, sM[q * 16 + row]);
+        wscale[r] = (m == -INFINITY || m_r[r] == -INFINITY) ? 0.f : exp2f(m_r[r] - m);
+      }
+      if (r0 < G) {
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) {
+          const int col = n * 8 + 2 * (lane & 3);
+          atomicAdd(&sO[r0 * D + col], o[n][0] * wscale[0]);
+          atomicAdd(&sO[r0 * D + col + 1], o[n][1] * wscale[0]);
+        }
+      }
+      if (r0 + 8 < G) {
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) {
+          const int col = n * 8 + 2 * (lane & 3);
+          atomicAdd(&sO[(r0 + 8) * D + col], o[n][2] * wscale[1]);
+          atomicAdd(&sO[(r0 + 8) * D + col + 1], o[n][3] * wscale[1]);
+        }
+      }
+      if (threadIdx.x == 0) *sStop = *abort_flag;
+      named_barrier_sync(1, NC);
+      for (int idx = threadIdx.x; idx < G * D; idx += NC) {
+        const int row = idx / D, col = idx % D;
+        float m = -INFINITY;
+        for (int q = 0; q < 4; ++q) m = fmaxf(m, sM[q * 16 + row]);
+        float l = 0.f;
+        for (int q = 0; q < 4; ++q) {
+          const float mw = sM[q * 16 + row];
+          if (mw != -INFINITY) l += sL[q * 16 + row] * exp2f(mw - m);
+        }
+        const float v = sO[idx];
+        sO[idx] = 0.f;  // ready for the next item (only this thread touches idx here)
+        const int head = it.h * G + row;
+        if (S == 1) {
+          bf16* out = static_cast<bf16*>(a.out) + ((size_t)it.b * nq + head) * D;
+          out[col] = __float2bfloat16(l > 0.f ? v / l : 0.f);
+        } else {
+          const size_t pidx = ((size_t)it.b * nq + head) * S + it.split;
+          a.part_o[pidx * D + col] = v;
+          if (col == 0) {
+            a.part_m[pidx] = m;
+            a.part_l[pidx] = l;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
 // ================================================================= prefill
 // Packed rows: r -> query position qb*QPB + r / G, head h*G + r % G.
 template <int D>
@@ -878,9 +1153,36 @@ static bool use_tma_decode(const DecodeArgs& a, int* sub_rows) {
   return true;
 }
 
+static int num_sms_attn() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
 template <int D>
 static void launch_decode_tma(const DecodeArgs& a, int B, int sub_rows, cudaStream_t s) {
   const CUtensorMap& map = kv_tensor_map(a, sub_rows);
+  static const bool persist = [] {
+    const char* e = std::getenv("B200MOE_DECODE_PERSIST");
+    return e == nullptr || std::string(e) != "0";
+  }();
+  if (persist) {
+    static bool set_p = false;
+    if (!set_p) {
+      cudaFuncSetAttribute(decode_attn_persist_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecPersist<D>::SMEM);
+      set_p = true;
+    }
+    const int n_items = a.num_splits * a.num_kv_heads * B;
+    const int grid = std::max(1, std::min(n_items, 2 * num_sms_attn()));
+    decode_attn_persist_kernel<D><<<grid, 160, DecPersist<D>::SMEM, s>>>(map, a, sub_rows, a.num_blocks, n_items);
+    if (a.num_splits > 1) decode_combine_kernel<D><<<dim3(a.num_kv_heads * a.group, B), D, 0, s>>>(a);
+    return;
+  }
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(decode_attn_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecTma<D>::SMEM);
