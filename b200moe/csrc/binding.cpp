@@ -404,6 +404,17 @@ void kv_blocks_copy(Tensor src_pool, Tensor src_ids, int64_t dst_ptr, Tensor dst
                        dst_ids.data_ptr<int>(), (int)src_ids.numel(), block_bytes, stream());
 }
 
+void dequant_weights(Tensor q, Tensor scale, Tensor out, bool tiled) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(scale); CHECK_CONTIG(out);
+  TORCH_CHECK(q.scalar_type() == torch::kFloat8_e4m3fn, "weights must be e4m3");
+  CHECK_DT(scale, torch::kFloat32); CHECK_DT(out, torch::kBFloat16);
+  TORCH_CHECK(q.sizes() == out.sizes(), "out must have the weight's shape");
+  const int64_t K = q.size(-1), N = q.size(-2), G = q.numel() / (N * K);
+  TORCH_CHECK(scale.numel() == G * (N / 128) * (K / 128), "scale must be [G, N/128, K/128]");
+  c10::cuda::CUDAGuard guard(q.device());
+  b200::dequant_weights(q.data_ptr(), scale.data_ptr<float>(), out.data_ptr(), (int)G, (int)N, (int)K, tiled, stream());
+}
+
 void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
                   c10::optional<Tensor> counts, c10::optional<Tensor> status) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16);
@@ -567,6 +578,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("splitk_reduce", &splitk_reduce);
   m.def("rmsnorm_partials", &rmsnorm_partials);
   m.def("router_fused", &router_fused);
+  m.def("dequant_weights", &dequant_weights);
   m.def("kv_blocks_copy", &kv_blocks_copy);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);

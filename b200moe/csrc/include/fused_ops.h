@@ -51,6 +51,8 @@ void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, co
                     int64_t block_bytes, cudaStream_t s);
 // Router GEMM (x [T, H] bf16 . w[:E]^T, fp32 accumulate, bf16-rounded logits) +
 // softmax + top-k in one launch; E <= 128.
+// e4m3 [G, N, K] (row-major or tile-major) + 128x128 block scales -> bf16 row-major
+void dequant_weights(const void* q, const float* scale, void* out, int G, int N, int K, bool tiled, cudaStream_t s);
 void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows, int topk, bool renorm, int* ids,
                   float* weights, int* counts, int* status, cudaStream_t s);
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,

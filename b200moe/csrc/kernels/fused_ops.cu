@@ -18,6 +18,8 @@
 #include <cudaTypedefs.h>
 #include <vector>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <algorithm>
 #include <cstdint>
 #include <stdexcept>
@@ -515,6 +517,57 @@ __global__ void kv_blocks_copy_kernel(const uint4* __restrict__ src, const int* 
   const int64_t per = (vecs + gridDim.y - 1) / gridDim.y;
   const int64_t lo = blockIdx.y * per, hi = min(vecs, lo + per);
   for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[d0 + i] = src[s0 + i];
+}
+
+// e4m3 [G, N, K] (row-major, or tile-major as ops.tile_fp8 lays it out) with
+// 128x128 block scales -> bf16 [G, N, K] row-major, bf16(float(q) * scale): the
+// GEMM's per-tile dequantisation done once (large prefill batches re-read each
+// expert's weights for every token tile).  One thread per 16 consecutive K.
+__global__ void dequant_weights_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
+                                       bf16* __restrict__ out, int G, int N, int K, int tiled) {
+  const int64_t chunks = (int64_t)G * N * (K / 16);
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= chunks) return;
+  const int kc = (int)(i % (K / 16));
+  const int64_t gn = i / (K / 16);
+  const int n = (int)(gn % N), g = (int)(gn / N);
+  const int k = kc * 16;
+  size_t src;
+  if (tiled) {
+    const int r = n & 127, u = (k & 63) >> 4;
+    const size_t blk = ((size_t)g * (N / 128) + (n >> 7)) * (K / 64) + (k >> 6);
+    src = blk * 8192 + r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
+  } else {
+    src = ((size_t)g * N + n) * K + k;
+  }
+  const uint4 v = *reinterpret_cast<const uint4*>(q + src);
+  const float sc = scale[((size_t)g * (N / 128) + (n >> 7)) * (K / 128) + (k >> 7)];
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    // e4m3 -> f16 -> f32 are exact; one fp32 rounding of the product, then bf16
+    __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] & 0xFFFFu), __NV_E4M3);
+    __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[h] >> 16), __NV_E4M3);
+    const float2 flo = __half22float2(*reinterpret_cast<__half2*>(&lo));
+    const float2 fhi = __half22float2(*reinterpret_cast<__half2*>(&hi));
+    __nv_bfloat162 b0 = __floats2bfloat162_rn(__fmul_rn(flo.x, sc), __fmul_rn(flo.y, sc));
+    __nv_bfloat162 b1 = __floats2bfloat162_rn(__fmul_rn(fhi.x, sc), __fmul_rn(fhi.y, sc));
+    o[2 * h] = *reinterpret_cast<uint32_t*>(&b0);
+    o[2 * h + 1] = *reinterpret_cast<uint32_t*>(&b1);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)g * N + n) * K + k);
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+void dequant_weights(const void* q, const float* scale, void* out, int G, int N, int K, bool tiled, cudaStream_t s) {
+  if (N % 128 || K % 128) throw std::runtime_error("dequant_weights: N and K must be multiples of 128");
+  const int64_t chunks = (int64_t)G * N * (K / 16);
+  if (chunks == 0) return;
+  dequant_weights_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, s>>>(
+      static_cast<const uint8_t*>(q), scale, static_cast<bf16*>(out), G, N, K, tiled ? 1 : 0);
+  check_launch("dequant_weights");
 }
 
 void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, const int* dst_ids, int n,

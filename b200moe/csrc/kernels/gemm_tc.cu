@@ -848,8 +848,9 @@ void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
     if ((L.args.k_splits - 1) * per >= stages) throw std::runtime_error("split-K leaves a split empty");
   }
   if (L.pair) {
-    if (!L.a_fp8 || L.epi != kEpiSiluPair) throw std::runtime_error("pair mode is fp8 + silu only");
-    dispatch_bn<true, true, kEpiSiluPair>(bn, L, stream);
+    if (L.epi != kEpiSiluPair) throw std::runtime_error("pair mode is the silu epilogue only");
+    if (L.a_fp8) dispatch_bn<true, true, kEpiSiluPair>(bn, L, stream);
+    else dispatch_bn<true, false, kEpiSiluPair>(bn, L, stream);
     return;
   }
   if (L.a_fp8) {
@@ -860,6 +861,7 @@ void gemm_tc_launch(const GemmLaunch& L, cudaStream_t stream) {
   } else {
     if (L.epi == kEpiF32) dispatch_bn<false, false, kEpiF32>(bn, L, stream);
     else if (L.epi == kEpiBf16) dispatch_bn<false, false, kEpiBf16>(bn, L, stream);
+    else if (L.epi == kEpiScatter) dispatch_bn<false, false, kEpiScatter>(bn, L, stream);
     else throw std::runtime_error("unsupported bf16 epilogue");
   }
 }

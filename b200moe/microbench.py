@@ -140,6 +140,18 @@ def case_moe(T, iters, E=128, k=8, H=2048, I=768, only=""):
         wbytes = used * 2 * I * H + rows * H * 2 + rows * I * 2
         report("moe_gate_up_silu", ms, wbytes, 2 * rows * H * 2 * I, tokens=T,
                bn=ops.pick_bn(rows, I // 128, E, pair=True))
+    if rows >= 512 * E and only == "":
+        # large prefill batch path: dequantise once, bf16 GEMMs (the dequantisation is timed)
+        w13b = torch.empty(E, 2 * I, H, dtype=torch.bfloat16, device="cuda")
+        w2b = torch.empty(E, H, I, dtype=torch.bfloat16, device="cuda")
+        ms = timeit(lambda: (ops.dequant_weights(q13, s13, w13b, TILED),
+                             ops.grouped_gate_up_silu(x, w13b, None, counts, offsets, h, I)), iters)
+        report("moe_gate_up_silu_bf16once", ms, used * 2 * I * H * 3 + rows * H * 2 + rows * I * 2,
+               2 * rows * H * 2 * I, tokens=T)
+        ms = timeit(lambda: (ops.dequant_weights(q2, s2, w2b, TILED),
+                             ops.grouped_down_scatter(h, w2b, None, counts, offsets, sor, w, slots)), iters)
+        report("moe_down_scatter_bf16once", ms, used * H * I * 3 + rows * I * 2 + rows * H * 2,
+               2 * rows * I * H, tokens=T)
     if only == "gate_up":
         return
     ms = timeit(lambda: ops.grouped_down_scatter(h, q2, s2, counts, offsets, sor, w, slots, tiled=TILED), iters)

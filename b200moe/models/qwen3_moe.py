@@ -24,6 +24,8 @@ from __future__ import annotations
 from contextlib import nullcontext
 from dataclasses import dataclass
 
+import os
+
 import torch
 import torch.distributed as dist
 from torch import nn
@@ -231,6 +233,21 @@ class Qwen3MoeForCausalLM(nn.Module):
             self._buf("ids", (max_tokens * k,), torch.int32)
             self._buf("topw", (max_tokens * k,), torch.float32)
         self._buf("h_perm", (max(rows, max_tokens), I), self.dtype)
+        if self._bf16_experts(rows) and self.layers:
+            l0 = self.layers[0]
+            self._buf("w13_bf16", tuple(l0.w13.shape), torch.bfloat16)
+            self._buf("w2_bf16", tuple(l0.w2.shape), torch.bfloat16)
+
+    # Routed rows per expert from which a step dequantises the layer's expert
+    # weights to bf16 once and runs the bf16 grouped GEMMs: below it the e4m3
+    # GEMMs (dequantising per tile) win; above it every expert's weights are
+    # re-dequantised for many token tiles (B200MOE_BF16_EXPERT_ROWS, 0 = never).
+    BF16_EXPERT_ROWS = int(os.environ.get("B200MOE_BF16_EXPERT_ROWS", "512"))
+
+    def _bf16_experts(self, rows: int) -> bool:
+        E = max(1, self.num_local_experts)
+        return (self.cuda and self.quant and self.args.is_moe and self.BF16_EXPERT_ROWS > 0
+                and rows >= self.BF16_EXPERT_ROWS * E)
 
     def _range(self, name: str):
         return nullcontext() if self.profiler is None else self.profiler.range(name)
@@ -405,13 +422,23 @@ class Qwen3MoeForCausalLM(nn.Module):
             slot_of_row = self._buf("slot_of_row", (rows,), torch.int32)
             offsets = self._buf("offsets", (E + 1,), torch.int32)
             ops.moe_permute(x, ids, counts[:E], counts[E:2 * E], x_perm, slot_of_row, offsets)
+        if self._bf16_experts(rows):
+            # large prefill batch: dequantise once, then bf16 GEMMs (no per-tile dequantisation)
+            w13 = self._buf("w13_bf16", tuple(layer.w13.shape), torch.bfloat16)
+            w2 = self._buf("w2_bf16", tuple(layer.w2.shape), torch.bfloat16)
+            with self._range("moe.dequant"):
+                ops.dequant_weights(layer.w13, layer.s13, w13, self.weights_tiled)
+                ops.dequant_weights(layer.w2, layer.s2, w2, self.weights_tiled)
+            s13 = s2 = None
+            tiled = False
+        else:
+            w13, s13, w2, s2, tiled = layer.w13, layer.s13, layer.w2, layer.s2, self.weights_tiled
         with self._range("moe.gate_up"):
             h_perm = self._buf("h_perm", (rows, I), self.dtype)
-            ops.grouped_gate_up_silu(x_perm, layer.w13, layer.s13, counts[:E], offsets, h_perm, I,
-                                     tiled=self.weights_tiled)
+            ops.grouped_gate_up_silu(x_perm, w13, s13, counts[:E], offsets, h_perm, I, tiled=tiled)
         with self._range("moe.down"):
-            ops.grouped_down_scatter(h_perm, layer.w2, layer.s2, counts[:E], offsets, slot_of_row,
-                                     w.view(-1), slots, tiled=self.weights_tiled)
+            ops.grouped_down_scatter(h_perm, w2, s2, counts[:E], offsets, slot_of_row,
+                                     w.view(-1), slots, tiled=tiled)
         return slots
 
     def _moe_tp(self, layer, x, residual, next_norm, T):

@@ -275,6 +275,20 @@ def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weig
     return slots_out
 
 
+def dequant_weights(q: torch.Tensor, scale: torch.Tensor, out: torch.Tensor, tiled: bool = False) -> torch.Tensor:
+    """bf16(float(q) * block scale) of an e4m3 weight stack [..., N, K] into ``out``
+    (row-major bf16); ``tiled``: q is stored tile-major (``tile_fp8``)."""
+    if not q.is_cuda:
+        w = untile_fp8(q) if tiled else q
+        lead = w.shape[:-2]
+        flat_w, flat_s = w.reshape(-1, *w.shape[-2:]), scale.reshape(-1, *scale.shape[-2:])
+        res = torch.stack([dequant_block_fp8(flat_w[i], flat_s[i]) for i in range(flat_w.shape[0])])
+        return out.copy_(res.view(*lead, *w.shape[-2:]).to(out.dtype))
+    native().dequant_weights(q, scale, out, tiled)
+    count_launches()
+    return out
+
+
 # -------------------------------------------------------------- fused ops
 def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     if not ids.is_cuda:

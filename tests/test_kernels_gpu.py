@@ -170,6 +170,42 @@ def test_tile_major_weights_same_bits(bn):
     assert torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("tiled", [False, True])
+def test_bf16_expert_path_same_bits(tiled):
+    """Large prefill steps dequantise the expert weights once (dequant_weights)
+    and run the bf16 grouped GEMMs: the weights equal bf16(float(q) * scale) and
+    both GEMMs give the e4m3 path's bits."""
+    E, I, H = 8, 256, 512
+    counts = torch.tensor([5, 0, 17, 1, 300, 3, 0, 129], dtype=torch.int32, device=DEV)
+    rows = int(counts.sum())
+    offsets = torch.zeros(E + 1, dtype=torch.int32, device=DEV)
+    offsets[1:] = torch.cumsum(counts, 0)
+    q13, s13 = _fp8_weight(E, 2 * I, H, 2)
+    q2, s2 = _fp8_weight(E, H, I, 3)
+    w13 = torch.empty(E, 2 * I, H, dtype=torch.bfloat16, device=DEV)
+    w2 = torch.empty(E, H, I, dtype=torch.bfloat16, device=DEV)
+    ops.dequant_weights(ops.tile_fp8(q13) if tiled else q13, s13, w13, tiled)
+    ops.dequant_weights(ops.tile_fp8(q2) if tiled else q2, s2, w2, tiled)
+    for e in range(E):
+        want = (q13[e].float() * s13[e].repeat_interleave(128, 0).repeat_interleave(128, 1)).to(torch.bfloat16)
+        assert torch.equal(w13[e], want), e
+    x = (torch.randn(rows, H, device=DEV) * 0.5).to(torch.bfloat16)
+    h1, h2 = (torch.empty(rows, I, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+    for bn in (64, 128):
+        ops.grouped_gate_up_silu(x, q13, s13, counts, offsets, h1, I, bn=bn)
+        ops.grouped_gate_up_silu(x, w13, None, counts, offsets, h2, I, bn=bn)
+        assert torch.equal(h1, h2), bn
+    sor = torch.randperm(rows, device=DEV).to(torch.int32)
+    wts = torch.rand(rows, device=DEV)
+    for bn in (64, 256):
+        y1, y2 = (torch.zeros(rows, H, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+        ops.grouped_down_scatter(h1, q2, s2, counts, offsets, sor, wts, y1, bn=bn)
+        ops.grouped_down_scatter(h1, w2, None, counts, offsets, sor, wts, y2, bn=bn)
+        torch.cuda.synchronize()
+        ops.check_status(DEV)
+        assert torch.equal(y1, y2), bn
+
+
 def test_rmsnorm_and_add():
     T, H = 33, 2048
     x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
