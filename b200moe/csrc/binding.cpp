@@ -529,6 +529,8 @@ void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor
   a.out = out.data_ptr();
   a.num_blocks = (int)k_cache.size(0);
   a.status = ptr_or_null<int>(status);
+  a.q_rows = (int)q.size(0);
+  a.batch = B;
   b200::paged_prefill_attn(a, B, (int)max_q_len, stream());
 }
 

@@ -51,6 +51,8 @@ struct PrefillArgs {
   void* out;                 // [T, q_heads, D] bf16
   int num_blocks;            // blocks in the pool (tensor-core path: out-of-range block = zero fill)
   int* status;               // device status word (bounded waits), may be null
+  int q_rows;                // rows of q (tensor-core path: Q tensor map extent)
+  int batch;                 // sequences (set by the launcher)
 };
 
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s);

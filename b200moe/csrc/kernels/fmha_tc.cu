@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <mutex>
@@ -57,13 +58,15 @@ constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;            // S0 | S1 | O (| unused)
 
 struct Layout {
-  static constexpr int Q = 0;
-  static constexpr int P = Q + kTile;
+  static constexpr int Q = 0;                          // two Q buffers (items alternate)
+  static constexpr int P = Q + 2 * kTile;
   static constexpr int RING = P + kTile;
   static constexpr int BARS = RING + kSlots * kTile;
-  static constexpr int NBARS = 2 * kSlots + 2 + 4;  // kv full/empty, s_full[2], p_full, p_empty, q_full, fin
+  // kv full/empty, s_full[2], p_full, p_empty, q_full[2], q_empty[2], fin
+  static constexpr int NBARS = 2 * kSlots + 2 + 2 + 4 + 1;
   static constexpr int SMEM = BARS + NBARS * 8 + 16 + 1024;
 };
+static_assert(Layout::SMEM <= 232448, "shared memory budget");
 
 // 16-byte chunk u (0..7) of row r in a [rows][64] bf16 half with 128-byte swizzle
 __device__ __forceinline__ uint32_t sw_off(int r, int u) { return r * 128 + ((u ^ (r & 7)) << 4); }
@@ -74,6 +77,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];"
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                            int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -130,9 +142,33 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// One work item = (kv head h, sequence b, query tile qt): 128 packed rows.
+struct FmItem {
+  int h, b, qt, q0, q_len, pos0, ntiles;
+};
+
+__device__ __forceinline__ bool fm_item(const PrefillArgs& a, int qtiles, int w, FmItem& it) {
+  // heaviest query tiles (largest causal extent) first, then sequence, then kv head
+  const int B = a.batch;
+  it.h = w % a.num_kv_heads;
+  w /= a.num_kv_heads;
+  it.b = w % B;
+  it.qt = qtiles - 1 - w / B;
+  const int QPB = kRows / a.group;
+  it.q0 = a.cu_seqlens_q[it.b];
+  it.q_len = a.cu_seqlens_q[it.b + 1] - it.q0;
+  if (it.qt * QPB >= it.q_len) return false;
+  const int kv_len = a.seq_lens[it.b];
+  it.pos0 = kv_len - it.q_len;
+  const int last_q = min(it.q_len, (it.qt + 1) * QPB) - 1;
+  const int k_end = min(kv_len, it.pos0 + last_q + 1);
+  it.ntiles = (k_end + kKeys - 1) / kKeys;
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArgs a, int sub_rows, int oob_block,
-                    int qtiles) {
+fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
+                    const PrefillArgs a, int sub_rows, int oob_block, int qtiles, int n_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Layout::Q;
@@ -143,22 +179,13 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
   uint64_t* s_full = kv_empty + kSlots;
   uint64_t* p_full = s_full + 2;
   uint64_t* p_empty = p_full + 1;
-  uint64_t* q_full = p_empty + 1;
-  uint64_t* fin = q_full + 1;
+  uint64_t* q_full = p_empty + 1;     // [2]
+  uint64_t* q_empty = q_full + 2;     // [2]
+  uint64_t* fin = q_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // heaviest query tiles (largest causal extent) are launched first
-  const int h = blockIdx.x, b = blockIdx.y, qt = qtiles - 1 - (int)blockIdx.z;
-  const int G = a.group, QPB = kRows / G;
-  const int q0 = a.cu_seqlens_q[b];
-  const int q_len = a.cu_seqlens_q[b + 1] - q0;
-  if (qt * QPB >= q_len) return;  // uniform for the CTA, before any barrier or TMEM use
-  const int kv_len = a.seq_lens[b];
-  const int pos0 = kv_len - q_len;
-  const int last_q = min(q_len, (qt + 1) * QPB) - 1;
-  const int k_end = min(kv_len, pos0 + last_q + 1);
-  const int ntiles = (k_end + kKeys - 1) / kKeys;
+  const int G = a.group;
   const int nq = a.num_kv_heads * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* status = a.status;
@@ -172,7 +199,10 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 4);
     mbar_init(p_empty, 1);
-    mbar_init(q_full, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     mbar_init(fin, 1);
     fence_barrier_init();
     *abort_flag = 0;
@@ -191,22 +221,41 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
     // ================================================================ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&kv_map);
-      const int* btab = a.block_tables + (size_t)b * a.max_blocks;
+      tma_prefetch_desc(&q_map);
       const int nsub = kKeys / sub_rows;
-      for (int p = 0; p < 2 * ntiles; ++p) {
-        const int j = p >> 1, slot = p % kSlots;
-        const uint32_t ph = (p / kSlots) & 1;
-        if (!mbar_wait(&kv_empty[slot], ph ^ 1, status, kStatusTimeoutEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[slot], kTile);
-        const uint32_t dst = smem_u32(ring + slot * kTile);
-        const int plane = (p & 1) ? a.num_kv_heads + h : h;  // V planes follow the K planes
-        for (int sub = 0; sub < nsub; ++sub) {
-          const int key = j * kKeys + sub * sub_rows;
-          const int blk = key >= k_end ? oob_block : btab[key / a.block_size];
-          const int y = key % a.block_size;
+      const int QPB = kRows / G;
+      int p = 0, li = 0;  // K/V tiles issued; items begun by this CTA
+      bool ok = true;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+        FmItem it;
+        if (!fm_item(a, qtiles, w, it)) continue;
+        // Q tile: {64 d, G heads, QPB tokens} boxes land as [pos * G + g][64] rows, 128-byte swizzled
+        const int qb = li & 1;
+        if (!mbar_wait(&q_empty[qb], ((li >> 1) & 1) ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&q_full[qb], kTile);
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_4d(dst + hf * kHalf + sub * sub_rows * 128, &kv_map, &kv_full[slot], hf * 64, y, plane, blk);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem_u32(sQ + qb * kTile + hf * kHalf), &q_map, &q_full[qb], hf * 64, it.h * G,
+                      it.q0 + it.qt * QPB);
+        ++li;
+        const int* btab = a.block_tables + (size_t)it.b * a.max_blocks;
+        const int kv_len = it.pos0 + it.q_len;
+        const int k_end = min(kv_len, it.pos0 + min(it.q_len, (it.qt + 1) * QPB));
+        for (int e = 0; e < 2 * it.ntiles; ++e, ++p) {
+          const int j = e >> 1, slot = p % kSlots;
+          const uint32_t ph = (p / kSlots) & 1;
+          if (!mbar_wait(&kv_empty[slot], ph ^ 1, status, kStatusTimeoutEmpty, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[slot], kTile);
+          const uint32_t dst = smem_u32(ring + slot * kTile);
+          const int plane = (e & 1) ? a.num_kv_heads + it.h : it.h;  // V planes follow the K planes
+          for (int sub = 0; sub < nsub; ++sub) {
+            const int key = j * kKeys + sub * sub_rows;
+            const int blk = key >= k_end ? oob_block : btab[key / a.block_size];
+            const int y = key % a.block_size;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+              tma_load_4d(dst + hf * kHalf + sub * sub_rows * 128, &kv_map, &kv_full[slot], hf * 64, y, plane, blk);
+          }
         }
       }
       if (*abort_flag) {
@@ -218,47 +267,76 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
     __syncwarp();
   } else if (warp == 1) {
     // ================================================================ MMA issuer
+    // One stream of (item, key tile) across the CTA's items: S of tile g + 2 is
+    // issued right after PV of tile g, so the next item's first S products run
+    // while the softmax finishes the current item.
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_bf16(kRows, kKeys);
       const uint32_t idesc_pv = umma_idesc_bf16(kRows, kD) | (1u << 16);  // B (V) is MN-major
-      const uint32_t qb = smem_u32(sQ), pb = smem_u32(sP);
-      auto issue_s = [&](int j) -> bool {
-        const int p = 2 * j, slot = p % kSlots;
-        if (!mbar_wait(&kv_full[slot], (p / kSlots) & 1, status, kStatusTimeoutFull, abort_flag)) return false;
+      const uint32_t pb = smem_u32(sP);
+      struct Cursor {
+        int w, li, t, n;  // item index, local item number, tile in item, tiles in item
+      };
+      auto first = [&](Cursor& c, int w0) {
+        FmItem it;
+        for (c.w = w0; c.w < n_items; c.w += gridDim.x)
+          if (fm_item(a, qtiles, c.w, it)) { c.t = 0; c.n = it.ntiles; return; }
+        c.n = 0;
+      };
+      auto next = [&](Cursor& c) {
+        if (++c.t < c.n) return;
+        ++c.li;
+        first(c, c.w + gridDim.x);
+      };
+      Cursor cs{0, 0, 0, 0}, cp{0, 0, 0, 0};
+      first(cs, blockIdx.x);
+      first(cp, blockIdx.x);
+      int gs = 0, gp = 0;  // global tile counters of the S and PV streams
+      bool ok = true;
+      auto issue_s = [&]() -> bool {
+        const int qb = cs.li & 1;
+        if (cs.t == 0) {
+          if (!mbar_wait(&q_full[qb], (cs.li >> 1) & 1, status, kStatusTimeoutFull, abort_flag)) return false;
+        }
+        const int pk = 2 * gs, slot = pk % kSlots;
+        if (!mbar_wait(&kv_full[slot], (pk / kSlots) & 1, status, kStatusTimeoutFull, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t kb = smem_u32(ring + slot * kTile);
+        const uint32_t qa = smem_u32(sQ + qb * kTile), kb = smem_u32(ring + slot * kTile);
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
           const uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
-          umma_f16_ss(tmem + (j & 1) * kKeys, umma_sdesc_sw128(qb + off), umma_sdesc_sw128(kb + off), idesc_s,
+          umma_f16_ss(tmem + (gs & 1) * kKeys, umma_sdesc_sw128(qa + off), umma_sdesc_sw128(kb + off), idesc_s,
                       k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[gs & 1]);
         umma_commit(&kv_empty[slot]);
+        if (cs.t + 1 == cs.n) umma_commit(&q_empty[qb]);  // the item's Q is no longer read
+        ++gs;
+        next(cs);
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {
-        if (!mbar_wait(p_full, j & 1, status, kStatusTimeoutConv, abort_flag)) return false;
-        const int p = 2 * j + 1, slot = p % kSlots;
-        if (!mbar_wait(&kv_full[slot], (p / kSlots) & 1, status, kStatusTimeoutFull, abort_flag)) return false;
+      auto issue_pv = [&]() -> bool {
+        if (!mbar_wait(p_full, gp & 1, status, kStatusTimeoutConv, abort_flag)) return false;
+        const int pk = 2 * gp + 1, slot = pk % kSlots;
+        if (!mbar_wait(&kv_full[slot], (pk / kSlots) & 1, status, kStatusTimeoutFull, abort_flag)) return false;
         tc_fence_after();
         const uint32_t vb = smem_u32(ring + slot * kTile);
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k) {
           const uint64_t adesc = umma_sdesc_sw128(pb + (k >> 2) * kHalf + (k & 3) * 32);
           const uint64_t bdesc = sdesc_sw128_mn(vb + k * 16 * 128, kHalf);
-          umma_f16_ss(tO, adesc, bdesc, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ss(tO, adesc, bdesc, idesc_pv, (cp.t > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(p_empty);
         umma_commit(&kv_empty[slot]);
+        ++gp;
+        next(cp);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, status, kStatusTimeoutConv, abort_flag);
-      if (ok) tc_fence_after();
-      ok = ok && issue_s(0) && (ntiles < 2 || issue_s(1));
-      for (int j = 0; ok && j < ntiles; ++j) {
-        ok = issue_pv(j);
-        if (ok && j + 2 < ntiles) ok = issue_s(j + 2);
+      for (int i = 0; i < 2 && ok && cs.n > 0; ++i) ok = issue_s();
+      while (ok && cp.n > 0) {
+        ok = issue_pv();
+        if (ok && cs.n > 0) ok = issue_s();
       }
       // every MMA issued so far completes before TMEM is released
       umma_commit(fin);
@@ -269,60 +347,52 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
     // ================================================================ softmax
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int qi = qt * QPB + r / G, head = h * G + r % G;
-    const bool valid = qi < q_len;
-    const int qpos = valid ? pos0 + qi : -1;
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.q) +
-                                                        ((size_t)(q0 + (valid ? qi : 0)) * nq + head) * kD);
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sQ + (c >> 3) * kHalf + sw_off(r, c & 7)) = v;
-      }
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(q_full);
-
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float sl2 = a.scale * 1.4426950408889634f;
-    float m_run = -INFINITY, l_run = 0.f;
+    const int QPB = kRows / G;
+    int g = 0;  // global tile counter (S / P stream)
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, status, kStatusTimeoutAccFull, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      float s[kKeys];
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      FmItem it;
+      if (!fm_item(a, qtiles, w, it)) continue;
+      const int qi = it.qt * QPB + r / G, head = it.h * G + r % G;
+      const bool valid = qi < it.q_len;
+      const int qpos = valid ? it.pos0 + qi : -1;
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < it.ntiles; ++j, ++g) {
+        ok = mbar_wait(&s_full[g & 1], (g >> 1) & 1, status, kStatusTimeoutAccFull, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        float s[kKeys];
 #pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) tmem_ld32(tmem + lane_base + (j & 1) * kKeys + c * 32, s + c * 32);
-      tmem_ld_wait();
-      const int kbase = j * kKeys;
-      if (kbase + kKeys - 1 > qpos) {
+        for (int c = 0; c < kKeys / 32; ++c) tmem_ld32(tmem + lane_base + (g & 1) * kKeys + c * 32, s + c * 32);
+        tmem_ld_wait();
+        const int kbase = j * kKeys;
+        if (kbase + kKeys - 1 > qpos) {
 #pragma unroll
-        for (int c = 0; c < kKeys; ++c)
-          if (kbase + c > qpos) s[c] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kKeys; ++c) mx = fmaxf(mx, s[c]);
-      mx *= sl2;
-      const bool grow = mx > m_run + kLazyLog2;
-      bool waited = false;
-      if (__any_sync(0xffffffffu, grow)) {
-        float alpha = 1.f;
-        if (grow) {
-          alpha = m_run == -INFINITY ? 1.f : exp2f(m_run - mx);
-          m_run = mx;
-          l_run *= alpha;
+          for (int c = 0; c < kKeys; ++c)
+            if (kbase + c > qpos) s[c] = -INFINITY;
         }
-        if (j > 0) {
-          // O holds PV_0..PV_{j-1}: rescale it once PV_{j-1} has landed
-          waited = true;
-          ok = mbar_wait(p_empty, (j - 1) & 1, status, kStatusTimeoutAccEmpty, abort_flag);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kKeys; ++c) mx = fmaxf(mx, s[c]);
+        mx *= sl2;
+        const bool grow = mx > m_run + kLazyLog2;
+        // PV of the previous tile (of any item) must be done before P is rewritten,
+        // and before O is rescaled (same item)
+        if (g > 0) {
+          ok = mbar_wait(p_empty, (g - 1) & 1, status, kStatusTimeoutAccEmpty, abort_flag);
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
           tc_fence_after();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        }
+        if (__any_sync(0xffffffffu, grow)) {
+          float alpha = 1.f;
+          if (grow) {
+            alpha = m_run == -INFINITY ? 1.f : exp2f(m_run - mx);
+            m_run = mx;
+            l_run *= alpha;
+          }
+          if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < kD / 32; ++c) {
               float o[32];
@@ -335,39 +405,35 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
             tmem_st_wait();
           }
         }
-      }
-      if (j > 0 && !waited) {
-        // P is single-buffered: PV_{j-1} must have read it
-        ok = mbar_wait(p_empty, (j - 1) & 1, status, kStatusTimeoutAccEmpty, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        tc_fence_after();
-      }
-      const float mu = m_run == -INFINITY ? 0.f : m_run;
-      float sum = 0.f;
+        const float mu = m_run == -INFINITY ? 0.f : m_run;
+        float sum = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < kKeys / 8; ++cc) {  // 8 keys = one 16-byte chunk of P
-        uint32_t w[4];
+        for (int cc = 0; cc < kKeys / 8; ++cc) {  // 8 keys = one 16-byte chunk of P
+          uint32_t wv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(fmaf(s[cc * 8 + 2 * e], sl2, -mu));
-          const float p1 = exp2f(fmaf(s[cc * 8 + 2 * e + 1], sl2, -mu));
-          sum += p0 + p1;
-          w[e] = pack2(p0, p1);
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = exp2f(fmaf(s[cc * 8 + 2 * e], sl2, -mu));
+            const float p1 = exp2f(fmaf(s[cc * 8 + 2 * e + 1], sl2, -mu));
+            sum += p0 + p1;
+            wv[e] = pack2(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(sP + (cc >> 3) * kHalf + sw_off(r, cc & 7)) =
+              make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
-        *reinterpret_cast<uint4*>(sP + (cc >> 3) * kHalf + sw_off(r, cc & 7)) = make_uint4(w[0], w[1], w[2], w[3]);
+        l_run += sum;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
       }
-      l_run += sum;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    if (ok) ok = mbar_wait(p_empty, (ntiles - 1) & 1, status, kStatusTimeoutAccEmpty, abort_flag);
-    if (__all_sync(0xffffffffu, ok)) {
+      if (!ok) break;
+      // ---- item epilogue: O / l once the item's last PV has landed
+      ok = mbar_wait(p_empty, (g - 1) & 1, status, kStatusTimeoutAccEmpty, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(static_cast<bf16*>(a.out) +
-                                            ((size_t)(q0 + (valid ? qi : 0)) * nq + head) * kD);
+                                            ((size_t)(it.q0 + (valid ? qi : 0)) * nq + head) * kD);
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
         float o[32];
@@ -376,10 +442,13 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArg
         if (valid) {
 #pragma unroll
           for (int v = 0; v < 4; ++v)
-            dst[c * 4 + v] = make_uint4(pack2(o[8 * v] * inv, o[8 * v + 1] * inv), pack2(o[8 * v + 2] * inv, o[8 * v + 3] * inv),
-                                        pack2(o[8 * v + 4] * inv, o[8 * v + 5] * inv), pack2(o[8 * v + 6] * inv, o[8 * v + 7] * inv));
+            dst[c * 4 + v] = make_uint4(pack2(o[8 * v] * inv, o[8 * v + 1] * inv),
+                                        pack2(o[8 * v + 2] * inv, o[8 * v + 3] * inv),
+                                        pack2(o[8 * v + 4] * inv, o[8 * v + 5] * inv),
+                                        pack2(o[8 * v + 6] * inv, o[8 * v + 7] * inv));
         }
       }
+      tc_fence_before();  // O reads complete before the next item's first PV overwrites it
     }
   }
 
@@ -455,17 +524,57 @@ bool fmha_prefill_supported(const PrefillArgs& a, int* sub_rows) {
   return true;
 }
 
-void fmha_prefill(const PrefillArgs& a, int B, int max_q_len, int sub_rows, cudaStream_t s) {
-  const CUtensorMap& map = kv_map(a, sub_rows);
+// Q as a 3-D tensor {head_dim, q heads, rows}: a box {64, G, 128 / G} is one half of
+// a 128-row packed tile (row = position * G + group head).
+static CUtensorMap q_map(const PrefillArgs& a) {
+  struct Entry { const void* base; int rows, nq, G; CUtensorMap map; };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const int nq = a.num_kv_heads * a.group;
+  for (auto& e : cache)
+    if (e.base == a.q && e.rows == a.q_rows && e.nq == nq && e.G == a.group) return e.map;
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)nq, (cuuint64_t)a.q_rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)nq * kD * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)a.group, (cuuint32_t)(kRows / a.group)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(a.q), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("prefill q tensor map: encode failed " + std::to_string((int)r));
+  if (cache.size() >= 64) cache.erase(cache.begin());
+  cache.push_back({a.q, a.q_rows, nq, a.group, map});
+  return map;
+}
+
+static int num_sms_fmha() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void fmha_prefill(const PrefillArgs& a_in, int B, int max_q_len, int sub_rows, cudaStream_t s) {
+  PrefillArgs a = a_in;
+  a.batch = B;
+  if (a.q_rows <= 0 || (reinterpret_cast<uintptr_t>(a.q) & 15))
+    throw std::runtime_error("prefill attention: q rows / alignment");
+  const CUtensorMap& kvm = kv_map(a, sub_rows);
+  const CUtensorMap qm = q_map(a);
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::SMEM);
   });
   const int QPB = kRows / a.group;
   const int qtiles = (max_q_len + QPB - 1) / QPB;
-  if (qtiles > 65535) throw std::runtime_error("prefill attention: too many query tiles for one launch");
-  dim3 grid(a.num_kv_heads, B, qtiles);
-  fmha_prefill_kernel<<<grid, kThreads, Layout::SMEM, s>>>(map, a, sub_rows, a.num_blocks, qtiles);
+  const int64_t n_items = (int64_t)a.num_kv_heads * B * qtiles;
+  if (n_items > (1 << 30)) throw std::runtime_error("prefill attention: too many query tiles for one launch");
+  const int grid = (int)std::min<int64_t>(n_items, num_sms_fmha());
+  fmha_prefill_kernel<<<grid, kThreads, Layout::SMEM, s>>>(kvm, qm, a, sub_rows, a.num_blocks, qtiles, (int)n_items);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) throw std::runtime_error(std::string("fmha_prefill launch: ") + cudaGetErrorString(err));
 }

@@ -8,6 +8,7 @@ numerics oracle used by the tests and by the CPU engine.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -160,6 +161,22 @@ def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: 
     return best
 
 
+# Token count from which an e4m3 dense GEMM dequantises its weight once and runs
+# in bf16 (B200MOE_BF16_DENSE_ROWS, 0 = never).
+BF16_DENSE_ROWS = int(os.environ.get("B200MOE_BF16_DENSE_ROWS", "2048"))
+_scratch_bufs: dict = {}
+
+
+def _scratch(name: str, numel: int, dtype, device) -> torch.Tensor:
+    """Grow-only per-device scratch (eager prefill paths only, never inside a graph capture)."""
+    key = (name, dtype, torch.device(device))
+    t = _scratch_bufs.get(key)
+    if t is None or t.numel() < numel:
+        t = torch.empty(numel, dtype=dtype, device=device)
+        _scratch_bufs[key] = t
+    return t[:numel]
+
+
 # ------------------------------------------------------- weight layout
 def _swizzle64_index(device) -> torch.Tensor:
     # chunk u (16 bytes) of row r of a [128][64 B] block sits at chunk u ^ ((r >> 1) & 3)
@@ -213,6 +230,12 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
         out = torch.empty(T, N, dtype=out_dtype, device=x.device)
     if T == 0:
         return out
+    if scale is not None and T >= BF16_DENSE_ROWS > 0 and weight.dim() == 2:
+        # prefill-size batch: one dequantisation of the (small) weight into a scratch,
+        # then the bf16 GEMM instead of dequantising every weight tile per token tile
+        wb = _scratch("dense_bf16", weight.numel(), torch.bfloat16, x.device).view(weight.shape)
+        dequant_weights(weight, scale, wb, tiled)
+        weight, scale, tiled = wb, None, False
     m_tiles = N // 128
     bn, splits = plan_dense(T, m_tiles, x.shape[1] // 64, fp8=scale is not None)
     if splits > 1:

@@ -206,6 +206,22 @@ def test_bf16_expert_path_same_bits(tiled):
         assert torch.equal(y1, y2), bn
 
 
+@pytest.mark.parametrize("tiled", [False, True])
+def test_dense_bf16_once_same_bits(tiled, monkeypatch):
+    """Prefill-size dense GEMMs dequantise the weight once and run in bf16: the
+    result equals the e4m3 path's bits."""
+    T, n, k = 2100, 1024, 2048
+    q, s = _fp8_weight(1, n, k, 6)
+    w = ops.tile_fp8(q[0]) if tiled else q[0]
+    x = (torch.randn(T, k, device=DEV) * 0.5).to(torch.bfloat16)
+    a = ops.linear(x, w, s[0], tiled=tiled)
+    monkeypatch.setattr(ops, "BF16_DENSE_ROWS", 0)
+    b = ops.linear(x, w, s[0], tiled=tiled)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    _close(a, x.float() @ _ref_w(q[0], s[0]).t())
+
+
 def test_rmsnorm_and_add():
     T, H = 33, 2048
     x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
