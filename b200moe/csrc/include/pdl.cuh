@@ -1,0 +1,54 @@
+// Programmatic dependent launch: every kernel of this library is launched with
+// the programmatic-stream-serialization attribute and starts with pdl_enter():
+// it lets the next grid in the stream be scheduled as soon as all of its own CTAs
+// are running, then waits for the previous grid to complete (and its memory to be
+// visible) before touching any global memory.  Dependencies are exactly those of
+// plain stream order; what overlaps is the next grid's launch and CTA ramp-up
+// with this grid's tail.  Grids launched without the attribute (or by other
+// libraries) are waited for in full, and griddepcontrol.wait returns at once in a
+// grid that was not launched programmatically.
+//
+// Off by default (B200MOE_PDL=1 turns it on): with the trigger at kernel entry the
+// 48-layer decode step measured 16.93 ms against 16.50 ms without it -- the early
+// dependents' CTAs compete with the running grid for SM slots.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <stdexcept>
+#include <string>
+#include <utility>
+
+namespace b200 {
+
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B200MOE_PDL");
+    return e != nullptr && std::string(e) == "1";
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline void pdl_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("kernel launch: ") + cudaGetErrorString(e));
+}
+
+}  // namespace b200

@@ -37,6 +37,7 @@
 #include <vector>
 
 #include "sm100.cuh"
+#include "pdl.cuh"
 #include "attention.h"
 
 namespace b200 {
@@ -233,6 +234,7 @@ __device__ __forceinline__ void softmax_update(float (&s)[NB][4], float (&m_r)[2
 // Q rows: r < G are heads h*G + r of the sequence's single query.
 template <int D>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
+  pdl_enter();
   constexpr int NT = 128;
   extern __shared__ __align__(128) uint8_t smem[];
   const int b = blockIdx.z, h = blockIdx.y, split = blockIdx.x;
@@ -393,6 +395,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
 
 template <int D>
 __global__ void decode_combine_kernel(const DecodeArgs a) {
+  pdl_enter();
   const int b = blockIdx.y, head = blockIdx.x;
   const int nq = a.num_kv_heads * a.group;
   const int L = a.seq_lens[b];
@@ -447,6 +450,7 @@ struct DecTma {
 template <int D>
 __global__ void __launch_bounds__(160) decode_attn_tma_kernel(const __grid_constant__ CUtensorMap kv_map,
                                                              const DecodeArgs a, int sub_rows, int oob_block) {
+  pdl_enter();
   constexpr int NC = 128;  // consumer threads
   using C = DecTma<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -690,6 +694,7 @@ template <int D>
 __global__ void __launch_bounds__(160) decode_attn_persist_kernel(const __grid_constant__ CUtensorMap kv_map,
                                                                  const DecodeArgs a, int sub_rows, int oob_block,
                                                                  int n_items) {
+  pdl_enter();
   constexpr int NC = 128;  // consumer threads
   using C = DecPersist<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -950,6 +955,7 @@ __global__ void __launch_bounds__(160) decode_attn_persist_kernel(const __grid_c
 // Packed rows: r -> query position qb*QPB + r / G, head h*G + r % G.
 template <int D>
 __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) {
+  pdl_enter();
   constexpr int NT = 128;
   extern __shared__ __align__(128) uint8_t smem[];
   const int b = blockIdx.z, h = blockIdx.y, qb = blockIdx.x;
@@ -1179,8 +1185,8 @@ static void launch_decode_tma(const DecodeArgs& a, int B, int sub_rows, cudaStre
     }
     const int n_items = a.num_splits * a.num_kv_heads * B;
     const int grid = std::max(1, std::min(n_items, 2 * num_sms_attn()));
-    decode_attn_persist_kernel<D><<<grid, 160, DecPersist<D>::SMEM, s>>>(map, a, sub_rows, a.num_blocks, n_items);
-    if (a.num_splits > 1) decode_combine_kernel<D><<<dim3(a.num_kv_heads * a.group, B), D, 0, s>>>(a);
+    pdl_launch(decode_attn_persist_kernel<D>, grid, 160, DecPersist<D>::SMEM, s, map, a, sub_rows, a.num_blocks, n_items);
+    if (a.num_splits > 1) pdl_launch(decode_combine_kernel<D>, dim3(a.num_kv_heads * a.group, B), D, 0, s, a);
     return;
   }
   static bool set = false;
@@ -1189,8 +1195,8 @@ static void launch_decode_tma(const DecodeArgs& a, int B, int sub_rows, cudaStre
     set = true;
   }
   dim3 grid(a.num_splits, a.num_kv_heads, B);
-  decode_attn_tma_kernel<D><<<grid, 160, DecTma<D>::SMEM, s>>>(map, a, sub_rows, a.num_blocks);
-  if (a.num_splits > 1) decode_combine_kernel<D><<<dim3(a.num_kv_heads * a.group, B), D, 0, s>>>(a);
+  pdl_launch(decode_attn_tma_kernel<D>, grid, 160, DecTma<D>::SMEM, s, map, a, sub_rows, a.num_blocks);
+  if (a.num_splits > 1) pdl_launch(decode_combine_kernel<D>, dim3(a.num_kv_heads * a.group, B), D, 0, s, a);
 }
 
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
@@ -1209,13 +1215,13 @@ void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
   if (a.head_dim == 128) {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<128>()); set = true; }
-    decode_attn_kernel<128><<<grid, 128, decode_smem<128>(), s>>>(a);
-    if (a.num_splits > 1) decode_combine_kernel<128><<<dim3(a.num_kv_heads * a.group, B), 128, 0, s>>>(a);
+    pdl_launch(decode_attn_kernel<128>, grid, 128, decode_smem<128>(), s, a);
+    if (a.num_splits > 1) pdl_launch(decode_combine_kernel<128>, dim3(a.num_kv_heads * a.group, B), 128, 0, s, a);
   } else if (a.head_dim == 64) {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<64>()); set = true; }
-    decode_attn_kernel<64><<<grid, 128, decode_smem<64>(), s>>>(a);
-    if (a.num_splits > 1) decode_combine_kernel<64><<<dim3(a.num_kv_heads * a.group, B), 64, 0, s>>>(a);
+    pdl_launch(decode_attn_kernel<64>, grid, 128, decode_smem<64>(), s, a);
+    if (a.num_splits > 1) pdl_launch(decode_combine_kernel<64>, dim3(a.num_kv_heads * a.group, B), 64, 0, s, a);
   } else {
     throw std::runtime_error("decode attention: head_dim must be 64 or 128");
   }
@@ -1236,11 +1242,11 @@ void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t
   if (a.head_dim == 128) {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<128>()); set = true; }
-    prefill_attn_kernel<128><<<grid, 128, prefill_smem<128>(), s>>>(a);
+    pdl_launch(prefill_attn_kernel<128>, grid, 128, prefill_smem<128>(), s, a);
   } else if (a.head_dim == 64) {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(prefill_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<64>()); set = true; }
-    prefill_attn_kernel<64><<<grid, 128, prefill_smem<64>(), s>>>(a);
+    pdl_launch(prefill_attn_kernel<64>, grid, 128, prefill_smem<64>(), s, a);
   } else {
     throw std::runtime_error("prefill attention: head_dim must be 64 or 128");
   }

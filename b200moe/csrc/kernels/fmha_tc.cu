@@ -41,6 +41,7 @@
 
 #include "attention.h"
 #include "sm100.cuh"
+#include "pdl.cuh"
 
 namespace b200 {
 namespace {
@@ -169,6 +170,7 @@ __device__ __forceinline__ bool fm_item(const PrefillArgs& a, int qtiles, int w,
 __global__ void __launch_bounds__(kThreads, 1)
 fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap q_map,
                     const PrefillArgs a, int sub_rows, int oob_block, int qtiles, int n_items) {
+  pdl_enter();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Layout::Q;
@@ -574,7 +576,7 @@ void fmha_prefill(const PrefillArgs& a_in, int B, int max_q_len, int sub_rows, c
   const int64_t n_items = (int64_t)a.num_kv_heads * B * qtiles;
   if (n_items > (1 << 30)) throw std::runtime_error("prefill attention: too many query tiles for one launch");
   const int grid = (int)std::min<int64_t>(n_items, num_sms_fmha());
-  fmha_prefill_kernel<<<grid, kThreads, Layout::SMEM, s>>>(kvm, qm, a, sub_rows, a.num_blocks, qtiles, (int)n_items);
+  pdl_launch(fmha_prefill_kernel, grid, kThreads, Layout::SMEM, s, kvm, qm, a, sub_rows, a.num_blocks, qtiles, (int)n_items);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) throw std::runtime_error(std::string("fmha_prefill launch: ") + cudaGetErrorString(err));
 }

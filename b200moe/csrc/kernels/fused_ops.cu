@@ -26,6 +26,7 @@
 #include <string>
 
 #include "sm100.cuh"
+#include "pdl.cuh"
 #include "fused_ops.h"
 
 namespace b200 {
@@ -66,6 +67,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // ------------------------------------------------------------ embedding
 __global__ void embed_gather_kernel(const int* __restrict__ ids, const bf16* __restrict__ table,
                                     bf16* __restrict__ out, int H, int V, int* status) {
+  pdl_enter();
   const int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= V) {  // the host validates ids; never read out of bounds
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const bf16* __restrict__ x,
                                                      const bf16* __restrict__ w, bf16* __restrict__ out,
                                                      bf16* res_out, int H, float eps, const float* __restrict__ part,
                                                      int splits, size_t split_stride) {
+  pdl_enter();
   __shared__ float red[NT / 32];
   const size_t base = (size_t)blockIdx.x * H;
   float v[VPT][8];
@@ -134,6 +137,7 @@ template <int NT, int VPT>
 __global__ void __launch_bounds__(NT) moe_combine_kernel(const bf16* __restrict__ slots, int topk,
                                                          bf16* residual, const bf16* __restrict__ w,
                                                          bf16* __restrict__ out, int H, float eps) {
+  pdl_enter();
   __shared__ float red[NT / 32];
   const int t = blockIdx.x;
   const size_t base = (size_t)t * H;
@@ -174,6 +178,7 @@ __global__ void __launch_bounds__(NT) moe_combine_kernel(const bf16* __restrict_
 // Lane l owns elements {l*E2 .. l*E2+E2-1} of each half (E2 = D/64).
 template <int D>
 __global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
+  pdl_enter();
   constexpr int E2 = D / 64;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -312,6 +317,7 @@ __device__ __forceinline__ void topk_row(float (&p)[EPL], int E, int topk, int r
 template <int EPL>
 __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int topk, int renorm,
                                    int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
+  pdl_enter();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* row = logits + (size_t)warp * ld;
@@ -346,6 +352,7 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
                                                            int E, int topk, int renorm, int* __restrict__ ids,
                                                            float* __restrict__ weights, int* __restrict__ counts,
                                                            int* __restrict__ status) {
+  pdl_enter();
   constexpr int XB = kRtTok * 128;  // bytes of one x chunk (the W chunk follows it)
   extern __shared__ __align__(1024) uint8_t rt_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_raw) + 1023) & ~uintptr_t(1023));
@@ -445,6 +452,7 @@ __global__ void moe_permute_kernel(const bf16* __restrict__ x, const int* __rest
                                    int E, int H, const int* __restrict__ counts, int* __restrict__ cursor,
                                    bf16* __restrict__ x_perm, int* __restrict__ slot_of_row,
                                    int* __restrict__ offsets_out) {
+  pdl_enter();
   __shared__ int offs[kMaxExperts + 1];
   if (threadIdx.x < 32) {
     const int per = (E + 31) / 32;
@@ -489,6 +497,7 @@ static void check_launch(const char* what) {
 template <bool BF16>
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int T, int N, void* out,
                                      int ld_out) {
+  pdl_enter();
   const int n4 = N / 4;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)T * n4) return;
@@ -513,6 +522,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 // block slab.  Used for prefill -> decode transfers into a peer's pool.
 __global__ void kv_blocks_copy_kernel(const uint4* __restrict__ src, const int* __restrict__ src_ids,
                                       uint4* __restrict__ dst, const int* __restrict__ dst_ids, int64_t vecs) {
+  pdl_enter();
   const int64_t s0 = (int64_t)src_ids[blockIdx.x] * vecs, d0 = (int64_t)dst_ids[blockIdx.x] * vecs;
   const int64_t per = (vecs + gridDim.y - 1) / gridDim.y;
   const int64_t lo = blockIdx.y * per, hi = min(vecs, lo + per);
@@ -525,6 +535,7 @@ __global__ void kv_blocks_copy_kernel(const uint4* __restrict__ src, const int* 
 // expert's weights for every token tile).  One thread per 16 consecutive K.
 __global__ void dequant_weights_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
                                        bf16* __restrict__ out, int G, int N, int K, int tiled) {
+  pdl_enter();
   const int64_t chunks = (int64_t)G * N * (K / 16);
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= chunks) return;
@@ -565,7 +576,7 @@ void dequant_weights(const void* q, const float* scale, void* out, int G, int N,
   if (N % 128 || K % 128) throw std::runtime_error("dequant_weights: N and K must be multiples of 128");
   const int64_t chunks = (int64_t)G * N * (K / 16);
   if (chunks == 0) return;
-  dequant_weights_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, s>>>(
+  pdl_launch(dequant_weights_kernel, (unsigned)((chunks + 255) / 256), 256, 0, s, 
       static_cast<const uint8_t*>(q), scale, static_cast<bf16*>(out), G, N, K, tiled ? 1 : 0);
   check_launch("dequant_weights");
 }
@@ -577,7 +588,7 @@ void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, co
     throw std::runtime_error("kv_blocks_copy: 16-byte aligned pools and block sizes required");
   const int64_t vecs = block_bytes / 16;
   const int chunks = (int)std::min<int64_t>(64, std::max<int64_t>(1, vecs / 4096));
-  kv_blocks_copy_kernel<<<dim3(n, chunks), 256, 0, s>>>(static_cast<const uint4*>(src_base), src_ids,
+  pdl_launch(kv_blocks_copy_kernel, dim3(n, chunks), 256, 0, s, static_cast<const uint4*>(src_base), src_ids,
                                                         static_cast<uint4*>(dst_base), dst_ids, vecs);
   check_launch("kv_blocks_copy");
 }
@@ -588,8 +599,8 @@ void splitk_reduce(const float* part, int splits, int T, int N, void* out, int l
   if (N % 4 || ld_out % 4) throw std::runtime_error("splitk_reduce: N and ld_out must be multiples of 4");
   const int64_t work = (int64_t)T * (N / 4);
   const int blocks = (int)((work + 255) / 256);
-  if (out_bf16) splitk_reduce_kernel<true><<<blocks, 256, 0, s>>>(part, splits, T, N, out, ld_out);
-  else splitk_reduce_kernel<false><<<blocks, 256, 0, s>>>(part, splits, T, N, out, ld_out);
+  if (out_bf16) pdl_launch(splitk_reduce_kernel<true>, blocks, 256, 0, s, part, splits, T, N, out, ld_out);
+  else pdl_launch(splitk_reduce_kernel<false>, blocks, 256, 0, s, part, splits, T, N, out, ld_out);
   check_launch("splitk_reduce");
 }
 
@@ -597,7 +608,7 @@ void embed_gather(const int* ids, const void* table, void* out, int T, int H, in
                   cudaStream_t s) {
   if (T == 0) return;
   if (H % 8) throw std::runtime_error("embed_gather: H % 8");
-  embed_gather_kernel<<<T, 256, 0, s>>>(ids, (const bf16*)table, (bf16*)out, H, V, status);
+  pdl_launch(embed_gather_kernel, T, 256, 0, s, ids, (const bf16*)table, (bf16*)out, H, V, status);
   check_launch("embed_gather");
 }
 
@@ -607,11 +618,11 @@ void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* 
   const bf16 *X = (const bf16*)x, *R = (const bf16*)res_in, *W = (const bf16*)w;
   bf16 *O = (bf16*)out, *RO = (bf16*)res_out;
   const size_t ss = (size_t)T * H;
-  if (H == 2048) rmsnorm_kernel<256, 1><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
-  else if (H == 4096) rmsnorm_kernel<256, 2><<<T, 256, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
-  else if (H == 256) rmsnorm_kernel<32, 1><<<T, 32, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
-  else if (H == 512) rmsnorm_kernel<64, 1><<<T, 64, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
-  else if (H == 1024) rmsnorm_kernel<128, 1><<<T, 128, 0, s>>>(X, R, W, O, RO, H, eps, part, splits, ss);
+  if (H == 2048) pdl_launch(rmsnorm_kernel<256, 1>, T, 256, 0, s, X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 4096) pdl_launch(rmsnorm_kernel<256, 2>, T, 256, 0, s, X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 256) pdl_launch(rmsnorm_kernel<32, 1>, T, 32, 0, s, X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 512) pdl_launch(rmsnorm_kernel<64, 1>, T, 64, 0, s, X, R, W, O, RO, H, eps, part, splits, ss);
+  else if (H == 1024) pdl_launch(rmsnorm_kernel<128, 1>, T, 128, 0, s, X, R, W, O, RO, H, eps, part, splits, ss);
   else throw std::runtime_error("rmsnorm: unsupported hidden size " + std::to_string(H));
   check_launch("rmsnorm");
 }
@@ -621,11 +632,11 @@ void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const 
   if (T == 0) return;
   const bf16 *S = (const bf16*)slots, *W = (const bf16*)w;
   bf16 *R = (bf16*)residual, *O = (bf16*)out;
-  if (H == 2048) moe_combine_kernel<256, 1><<<T, 256, 0, s>>>(S, topk, R, W, O, H, eps);
-  else if (H == 4096) moe_combine_kernel<256, 2><<<T, 256, 0, s>>>(S, topk, R, W, O, H, eps);
-  else if (H == 256) moe_combine_kernel<32, 1><<<T, 32, 0, s>>>(S, topk, R, W, O, H, eps);
-  else if (H == 512) moe_combine_kernel<64, 1><<<T, 64, 0, s>>>(S, topk, R, W, O, H, eps);
-  else if (H == 1024) moe_combine_kernel<128, 1><<<T, 128, 0, s>>>(S, topk, R, W, O, H, eps);
+  if (H == 2048) pdl_launch(moe_combine_kernel<256, 1>, T, 256, 0, s, S, topk, R, W, O, H, eps);
+  else if (H == 4096) pdl_launch(moe_combine_kernel<256, 2>, T, 256, 0, s, S, topk, R, W, O, H, eps);
+  else if (H == 256) pdl_launch(moe_combine_kernel<32, 1>, T, 32, 0, s, S, topk, R, W, O, H, eps);
+  else if (H == 512) pdl_launch(moe_combine_kernel<64, 1>, T, 64, 0, s, S, topk, R, W, O, H, eps);
+  else if (H == 1024) pdl_launch(moe_combine_kernel<128, 1>, T, 128, 0, s, S, topk, R, W, O, H, eps);
   else throw std::runtime_error("moe_combine: unsupported hidden size " + std::to_string(H));
   check_launch("moe_combine_add_rmsnorm");
 }
@@ -634,8 +645,8 @@ void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s) {
   if (T == 0) return;
   const int heads = a.num_q_heads + 2 * a.num_kv_heads;
   const int threads = 32 * std::min(heads, 16);
-  if (a.head_dim == 128) qknorm_rope_kvstore_kernel<128><<<T, threads, 0, s>>>(a);
-  else if (a.head_dim == 64) qknorm_rope_kvstore_kernel<64><<<T, threads, 0, s>>>(a);
+  if (a.head_dim == 128) pdl_launch(qknorm_rope_kvstore_kernel<128>, T, threads, 0, s, a);
+  else if (a.head_dim == 64) pdl_launch(qknorm_rope_kvstore_kernel<64>, T, threads, 0, s, a);
   else throw std::runtime_error("qknorm_rope_kvstore: head_dim must be 64 or 128");
   check_launch("qknorm_rope_kvstore");
 }
@@ -645,10 +656,10 @@ void router_topk(const float* logits, int ld, int T, int E, int topk, bool renor
   if (T == 0) return;
   if (topk > 8 || topk < 1) throw std::runtime_error("router_topk: topk must be in [1, 8]");
   const int blocks = (T * 32 + 255) / 256;
-  if (E <= 32) router_topk_kernel<1><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
-  else if (E <= 64) router_topk_kernel<2><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
-  else if (E <= 128) router_topk_kernel<4><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
-  else if (E <= 256) router_topk_kernel<8><<<blocks, 256, 0, s>>>(logits, ld, T, E, topk, renorm, ids, weights, counts);
+  if (E <= 32) pdl_launch(router_topk_kernel<1>, blocks, 256, 0, s, logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else if (E <= 64) pdl_launch(router_topk_kernel<2>, blocks, 256, 0, s, logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else if (E <= 128) pdl_launch(router_topk_kernel<4>, blocks, 256, 0, s, logits, ld, T, E, topk, renorm, ids, weights, counts);
+  else if (E <= 256) pdl_launch(router_topk_kernel<8>, blocks, 256, 0, s, logits, ld, T, E, topk, renorm, ids, weights, counts);
   else throw std::runtime_error("router_topk: at most 256 experts");
   check_launch("router_topk");
 }
@@ -700,7 +711,7 @@ void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows,
   }
   const CUtensorMap xm = rt_map(x, T, H, kRtTok);
   const CUtensorMap wm = rt_map(w, kRtE, H, kRtE);
-  router_fused_kernel<<<(T + kRtTok - 1) / kRtTok, 256, kRtSmem, s>>>(xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,
+  pdl_launch(router_fused_kernel, (T + kRtTok - 1) / kRtTok, 256, kRtSmem, s, xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,
                                                                        weights, counts, status);
   check_launch("router_fused");
 }
@@ -710,7 +721,7 @@ void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, c
   if (E > kMaxExperts) throw std::runtime_error("moe_permute: too many experts");
   const int rows = T * topk;
   const int blocks = std::max(1, (rows * 32 + 255) / 256);
-  moe_permute_kernel<<<blocks, 256, 0, s>>>((const bf16*)x, ids, T, topk, E, H, counts, cursor, (bf16*)x_perm,
+  pdl_launch(moe_permute_kernel, blocks, 256, 0, s, (const bf16*)x, ids, T, topk, E, H, counts, cursor, (bf16*)x_perm,
                                             slot_of_row, offsets_out);
   check_launch("moe_permute");
 }

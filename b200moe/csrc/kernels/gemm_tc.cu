@@ -43,6 +43,7 @@
 #include <string>
 
 #include "sm100.cuh"
+#include "pdl.cuh"
 #include "gemm_tc.h"
 
 namespace b200 {
@@ -200,6 +201,7 @@ template <int BN, bool PAIR, bool AFP8, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, PAIR, AFP8>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                const GemmArgs args) {
+  pdl_enter();
   using C = GemmCfg<BN, PAIR, AFP8>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -799,7 +801,7 @@ static void launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   // upper bound of work items without reading device counts
   int64_t max_tiles = ((int64_t)L.b_rows / BN + L.args.num_groups) * L.args.m_tiles * std::max(1, L.args.k_splits);
   int grid = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, max_tiles));
-  kern<<<grid, C::THREADS, C::SMEM, stream>>>(ta, tb, L.args);
+  pdl_launch(kern, grid, C::THREADS, C::SMEM, stream, ta, tb, L.args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_tc launch: ") + cudaGetErrorString(e));
 }

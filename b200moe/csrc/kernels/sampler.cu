@@ -23,6 +23,7 @@
 #include <string>
 
 #include "sm100.cuh"
+#include "pdl.cuh"
 #include "sampler.h"
 
 namespace b200 {
@@ -114,6 +115,7 @@ __device__ __forceinline__ void block_argmax(float& v, int& idx, float* redv, in
 
 __global__ void __launch_bounds__(kST) argmax_kernel(const float* __restrict__ logits, int V, int64_t ld,
                                                      int* __restrict__ out) {
+  pdl_enter();
   __shared__ float redv[32];
   __shared__ int redi[32];
   const float* row = logits + (size_t)blockIdx.x * ld;
@@ -207,6 +209,7 @@ __device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t 
 
 __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ logits, int V, int64_t ld,
                                                      SampleArgs a, int* __restrict__ out) {
+  pdl_enter();
   __shared__ float red[32];
   __shared__ int redi[32];
   __shared__ uint32_t hist_u[260];
@@ -271,6 +274,7 @@ __global__ void penalty_kernel(float* __restrict__ logits, int64_t ld, const int
                                const int* __restrict__ ids, const int* __restrict__ gen_counts,
                                const float* __restrict__ presence, const float* __restrict__ frequency,
                                const float* __restrict__ repetition, int n) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int r = rows[i];
@@ -290,13 +294,13 @@ static void check_launch(const char* what) {
 
 void argmax_rows(const float* logits, int B, int V, int64_t ld, int* out, cudaStream_t s) {
   if (B == 0) return;
-  argmax_kernel<<<B, kST, 0, s>>>(logits, V, ld, out);
+  pdl_launch(argmax_kernel, B, kST, 0, s, logits, V, ld, out);
   check_launch("argmax_rows");
 }
 
 void sample_rows(const float* logits, int B, int V, int64_t ld, const SampleArgs& a, int* out, cudaStream_t s) {
   if (B == 0) return;
-  sample_kernel<<<B, kST, 0, s>>>(logits, V, ld, a, out);
+  pdl_launch(sample_kernel, B, kST, 0, s, logits, V, ld, a, out);
   check_launch("sample_rows");
 }
 
@@ -304,7 +308,7 @@ void apply_penalties(float* logits, int64_t ld, const int* rows, const int* ids,
                      const float* presence, const float* frequency, const float* repetition, int n,
                      cudaStream_t s) {
   if (n == 0) return;
-  penalty_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, ld, rows, ids, gen_counts, presence, frequency,
+  pdl_launch(penalty_kernel, (n + 255) / 256, 256, 0, s, logits, ld, rows, ids, gen_counts, presence, frequency,
                                                  repetition, n);
   check_launch("apply_penalties");
 }
