@@ -262,14 +262,22 @@ void rmsnorm(Tensor x, c10::optional<Tensor> residual_in, Tensor weight, Tensor 
                 stream());
 }
 
-void moe_combine(Tensor slots, int64_t topk, Tensor residual, Tensor weight, Tensor out, double eps) {
+void moe_combine(Tensor slots, int64_t topk, Tensor residual, Tensor weight, Tensor out, double eps,
+                 c10::optional<Tensor> zero) {
   CHECK_CUDA(slots); CHECK_CONTIG(slots); CHECK_CONTIG(residual); CHECK_CONTIG(out);
   CHECK_DT(slots, torch::kBFloat16); CHECK_DT(residual, torch::kBFloat16);
   const int H = (int)residual.size(-1);
   const int T = (int)residual.size(0);
   TORCH_CHECK(slots.numel() >= (int64_t)T * topk * H, "slots too small");
+  int* zp = nullptr;
+  int zn = 0;
+  if (zero.has_value()) {
+    CHECK_DT((*zero), torch::kInt32); CHECK_CONTIG((*zero));
+    zp = zero->data_ptr<int>();
+    zn = (int)zero->numel();
+  }
   b200::moe_combine_add_rmsnorm(slots.data_ptr(), (int)topk, residual.data_ptr(), weight.data_ptr(),
-                                out.data_ptr(), T, H, (float)eps, stream());
+                                out.data_ptr(), T, H, (float)eps, stream(), zp, zn);
 }
 
 void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tensor q_norm_w, Tensor k_norm_w,

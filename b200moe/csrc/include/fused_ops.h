@@ -37,7 +37,8 @@ void embed_gather(const int* ids, const void* table, void* out, int T, int H, in
 void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,
              float eps, cudaStream_t s, const float* part = nullptr, int splits = 0);
 void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
-                             int H, float eps, cudaStream_t s);
+                             int H, float eps, cudaStream_t s,
+                             int* zero_buf = nullptr, int zero_n = 0);
 void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s);
 void router_topk(const float* logits, int ld, int T, int E, int topk, bool renorm, int* ids, float* weights,
                  int* counts, cudaStream_t s);

@@ -136,8 +136,13 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const bf16* __restrict__ x,
 template <int NT, int VPT>
 __global__ void __launch_bounds__(NT) moe_combine_kernel(const bf16* __restrict__ slots, int topk,
                                                          bf16* residual, const bf16* __restrict__ w,
-                                                         bf16* __restrict__ out, int H, float eps) {
+                                                         bf16* __restrict__ out, int H, float eps,
+                                                         int* __restrict__ zero_buf, int zero_n) {
   pdl_enter();
+  // the layer's routing counters are dead once the down GEMM has run: clear them
+  // for the next layer here instead of in a separate fill launch
+  if (blockIdx.x == 0 && zero_buf != nullptr)
+    for (int i = threadIdx.x; i < zero_n; i += NT) zero_buf[i] = 0;
   __shared__ float red[NT / 32];
   const int t = blockIdx.x;
   const size_t base = (size_t)t * H;
@@ -628,15 +633,15 @@ void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* 
 }
 
 void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
-                             int H, float eps, cudaStream_t s) {
+                             int H, float eps, cudaStream_t s, int* zero_buf, int zero_n) {
   if (T == 0) return;
   const bf16 *S = (const bf16*)slots, *W = (const bf16*)w;
   bf16 *R = (bf16*)residual, *O = (bf16*)out;
-  if (H == 2048) pdl_launch(moe_combine_kernel<256, 1>, T, 256, 0, s, S, topk, R, W, O, H, eps);
-  else if (H == 4096) pdl_launch(moe_combine_kernel<256, 2>, T, 256, 0, s, S, topk, R, W, O, H, eps);
-  else if (H == 256) pdl_launch(moe_combine_kernel<32, 1>, T, 32, 0, s, S, topk, R, W, O, H, eps);
-  else if (H == 512) pdl_launch(moe_combine_kernel<64, 1>, T, 64, 0, s, S, topk, R, W, O, H, eps);
-  else if (H == 1024) pdl_launch(moe_combine_kernel<128, 1>, T, 128, 0, s, S, topk, R, W, O, H, eps);
+  if (H == 2048) pdl_launch(moe_combine_kernel<256, 1>, T, 256, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
+  else if (H == 4096) pdl_launch(moe_combine_kernel<256, 2>, T, 256, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
+  else if (H == 256) pdl_launch(moe_combine_kernel<32, 1>, T, 32, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
+  else if (H == 512) pdl_launch(moe_combine_kernel<64, 1>, T, 64, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
+  else if (H == 1024) pdl_launch(moe_combine_kernel<128, 1>, T, 128, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
   else throw std::runtime_error("moe_combine: unsupported hidden size " + std::to_string(H));
   check_launch("moe_combine_add_rmsnorm");
 }

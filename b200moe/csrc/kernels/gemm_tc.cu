@@ -68,6 +68,8 @@ struct GemmCfg {
   // Single-tile TMEM-ring GEMMs (decode down / QKV / O) take 128 K per stage: the
   // producer and MMA threads pay their per-stage cost (barrier probes, commits,
   // descriptors) once per 8 MMAs instead of 4, which bounded them at decode size.
+  // (The gate/up pair already issues 8 MMAs per 64-wide stage; 128-wide stages
+  // leave it 3 TMEM slots and measured no faster: 97 vs 99 us at 256 tokens.)
   static constexpr bool WIDE_K = AFP8 && !PAIR && BN <= 128;
   static constexpr int KS = WIDE_K ? 128 : kBK;       // K elements per pipeline stage
   static constexpr int KSUB = KS / kBK;               // 64-wide sub-blocks per stage

@@ -349,8 +349,12 @@ class Qwen3MoeForCausalLM(nn.Module):
                                out=self._buf("x", (T, a.hidden_size), self.dtype) if self.cuda else None)
         slots = self._moe_fused(layer, x, T)
         with self._range("moe.combine_norm"):
-            return ops.moe_combine_add_rmsnorm(slots, a.num_experts_per_tok, residual, next_norm, eps,
-                                               out=self._buf("x", (T, a.hidden_size), self.dtype))
+            # the combine kernel also clears the routing counters for the next layer
+            counts = self._buf("counts", (2 * a.num_experts + 1,), torch.int32) if self.ep is None else None
+            out = ops.moe_combine_add_rmsnorm(slots, a.num_experts_per_tok, residual, next_norm, eps,
+                                              out=self._buf("x", (T, a.hidden_size), self.dtype), zero=counts)
+            self._counts_clear = counts is not None
+            return out
 
     def route(self, layer, x, counts=None):
         """Router GEMM + top-k: (ids [T, k] int32, weights [T, k] fp32)."""
@@ -411,7 +415,9 @@ class Qwen3MoeForCausalLM(nn.Module):
         slots = self._buf("slots", (T * k, H), self.dtype)
         counts = self._buf("counts", (2 * E + 1,), torch.int32)
         with self._range("moe.router"):
-            counts.zero_()
+            if self.ep is None and not getattr(self, "_counts_clear", False):
+                counts.zero_()  # otherwise the previous layer's combine kernel cleared them
+            self._counts_clear = False
             ids, w = self.route(layer, x, counts[:E] if self.ep is None else None)
         if self.ep is not None:
             with self._range("moe.ep"):

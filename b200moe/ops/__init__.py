@@ -341,15 +341,18 @@ def rmsnorm(x, weight, eps, residual=None, out=None):
     return out
 
 
-def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None):
-    """residual += sum_k slots[t, k] (fixed order); return rmsnorm(residual)."""
+def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None, zero=None):
+    """residual += sum_k slots[t, k] (fixed order); return rmsnorm(residual).
+    ``zero``: an int32 buffer the kernel also clears (the layer's routing counters)."""
     T, H = residual.shape
     if not residual.is_cuda:
+        if zero is not None:
+            zero.zero_()
         moe = slots[:T * topk].view(T, topk, H).float().sum(dim=1).to(residual.dtype)
         return rmsnorm(moe, weight, eps, residual=residual, out=out)
     if out is None:
         out = torch.empty_like(residual)
-    native().moe_combine(slots, topk, residual, weight, out, eps)
+    native().moe_combine(slots, topk, residual, weight, out, eps, zero)
     count_launches()
     return out
 
