@@ -156,3 +156,61 @@ def test_tile_major_fp8_layout_roundtrip():
     s = quantize_block_fp8(w[0])[1]
     x = torch.randn(5, 384).to(torch.bfloat16)
     assert torch.equal(ops.linear(x, q[0], s), ops.linear(x, t[0], s, tiled=True))
+
+
+def test_dense_planner_splits_are_valid_for_wide_stages():
+    """plan_dense picks K splits in units of the stage width the kernel will use
+    (128-wide stages for e4m3 tiles of <= 128 tokens): no split is ever empty."""
+    import math
+    from b200moe import ops
+    for rows in (1, 7, 64, 256, 300, 1024):
+        for n, k in ((5120, 2048), (2048, 4096), (2048, 768), (256, 256)):
+            bn, splits = ops.plan_dense(rows, n // 128, k // 64)
+            stages = k // 128 if bn <= 128 else k // 64
+            per = math.ceil(stages / splits)
+            assert (splits - 1) * per < stages, (rows, n, k, bn, splits)
+
+
+def test_dequant_weights_cpu_matches_block_dequant():
+    """ops.dequant_weights (row-major or tile-major e4m3 input) equals
+    bf16(float(q) * block scale) per expert."""
+    import torch
+    from b200moe import ops
+    from b200moe.utils.weights import quantize_block_fp8
+    w = torch.randn(2, 256, 384) * 0.05
+    qs = [quantize_block_fp8(w[i]) for i in range(2)]
+    q = torch.stack([a for a, _ in qs])
+    s = torch.stack([b for _, b in qs])
+    want = torch.stack([ops.dequant_block_fp8(q[i], s[i]) for i in range(2)]).to(torch.bfloat16)
+    for tiled in (False, True):
+        out = torch.empty(2, 256, 384, dtype=torch.bfloat16)
+        ops.dequant_weights(ops.tile_fp8(q) if tiled else q, s, out, tiled)
+        assert torch.equal(out, want)
+
+
+def test_natural_layout_restores_tiling():
+    """Loaders run on the row-major layout and the tile-major layout comes back after."""
+    from b200moe.utils.weights import natural_layout
+
+    class Fake:
+        def __init__(self):
+            self.weights_tiled = True
+            self.calls = []
+
+        def untile_weights_(self):
+            self.calls.append("untile")
+            self.weights_tiled = False
+
+        def tile_weights_(self):
+            self.calls.append("tile")
+            self.weights_tiled = True
+
+    m = Fake()
+    with natural_layout(m):
+        assert not m.weights_tiled
+    assert m.weights_tiled and m.calls == ["untile", "tile"]
+    m2 = Fake()
+    m2.weights_tiled = False
+    with natural_layout(m2):
+        pass
+    assert m2.calls == []
