@@ -236,13 +236,20 @@ void ep_scatter(EP_ARGS_DECL, Tensor local_counts, Tensor cursor, Tensor x_perm,
 void ep_signal(EP_ARGS_DECL) { b200::ep_signal(EP_ARGS, stream()); }
 void ep_wait_done(EP_ARGS_DECL) { b200::ep_wait_done(EP_ARGS, stream()); }
 
-void embed(Tensor ids, Tensor table, Tensor out, Tensor status) {
+void embed(Tensor ids, Tensor table, Tensor out, Tensor status, c10::optional<Tensor> feed_src,
+           c10::optional<Tensor> feed_tokens) {
   CHECK_CUDA(ids); CHECK_CUDA(table); CHECK_CUDA(out);
   CHECK_DT(ids, torch::kInt32); CHECK_DT(table, torch::kBFloat16); CHECK_DT(out, torch::kBFloat16);
   CHECK_CONTIG(table); CHECK_CONTIG(out); CHECK_CONTIG(ids);
   TORCH_CHECK(out.size(0) == ids.numel() && out.size(1) == table.size(1), "embed shape mismatch");
+  TORCH_CHECK(feed_src.has_value() == feed_tokens.has_value(), "feed needs both the source rows and the tokens");
+  if (feed_src.has_value()) {
+    CHECK_DT((*feed_src), torch::kInt32); CHECK_DT((*feed_tokens), torch::kInt32);
+    TORCH_CHECK(feed_src->numel() >= ids.numel(), "feed_src too short");
+  }
   b200::embed_gather(ids.data_ptr<int>(), table.data_ptr(), out.data_ptr(), (int)ids.numel(), (int)table.size(1),
-                     (int)table.size(0), status.data_ptr<int>(), stream());
+                     (int)table.size(0), status.data_ptr<int>(), stream(), ptr_or_null<int>(feed_src),
+                     ptr_or_null<int>(feed_tokens));
 }
 
 void rmsnorm(Tensor x, c10::optional<Tensor> residual_in, Tensor weight, Tensor out,

@@ -31,7 +31,8 @@ struct QkvArgs {
 };
 
 void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,
-                  cudaStream_t s);
+                  cudaStream_t s,
+                  const int* feed_src = nullptr, const int* feed_tokens = nullptr);
 // part != null: x is given as `splits` fp32 partial sums [splits, T, H] (split-K GEMM
 // output), reduced and rounded to bf16 before the residual add.
 void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,

@@ -65,11 +65,19 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // ------------------------------------------------------------ embedding
+// feed_src (optional): token t reads its id from feed_tokens[feed_src[t]] when
+// feed_src[t] >= 0 -- the previous step's sampled token, still on the device, so a
+// decode step can be launched before the host has read that token back.
 __global__ void embed_gather_kernel(const int* __restrict__ ids, const bf16* __restrict__ table,
-                                    bf16* __restrict__ out, int H, int V, int* status) {
+                                    bf16* __restrict__ out, int H, int V, int* status,
+                                    const int* __restrict__ feed_src, const int* __restrict__ feed_tokens) {
   pdl_enter();
   const int t = blockIdx.x;
   int id = ids[t];
+  if (feed_src != nullptr) {
+    const int f = feed_src[t];
+    if (f >= 0) id = feed_tokens[f];
+  }
   if (id < 0 || id >= V) {  // the host validates ids; never read out of bounds
     record_status(status, kStatusBadShape);
     id = 0;
@@ -610,10 +618,11 @@ void splitk_reduce(const float* part, int splits, int T, int N, void* out, int l
 }
 
 void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,
-                  cudaStream_t s) {
+                  cudaStream_t s, const int* feed_src, const int* feed_tokens) {
   if (T == 0) return;
   if (H % 8) throw std::runtime_error("embed_gather: H % 8");
-  pdl_launch(embed_gather_kernel, T, 256, 0, s, ids, (const bf16*)table, (bf16*)out, H, V, status);
+  pdl_launch(embed_gather_kernel, T, 256, 0, s, ids, (const bf16*)table, (bf16*)out, H, V, status, feed_src,
+             feed_tokens);
   check_launch("embed_gather");
 }
 

@@ -17,6 +17,7 @@ command (nanovllm/engine/model_runner.py:168-246) and the exit watchdog
 """
 from __future__ import annotations
 
+import collections
 import os
 import socket
 import time
@@ -115,7 +116,7 @@ class Executor:
             if status != "ready":
                 raise RankFailure(f"rank {r} failed to start:\n{payload}")
         self.max_blocks = self.runner.max_blocks
-        self._inflight = None
+        self._inflight: collections.deque = collections.deque()  # (plans, rows) of launched steps
 
     # ------------------------------------------------------------ plumbing
     def _recv(self, rank: int, conn, timeout: float | None = None):
@@ -187,24 +188,27 @@ class Executor:
         return _Caller()
 
     # --------------------------------------------------------------- steps
-    def plans(self, batch, grammar_masks: dict | None = None) -> list[StepPlan]:
+    def plans(self, batch, grammar_masks: dict | None = None, feed_from=None) -> list[StepPlan]:
         """One plan per rank: every row on every rank (tensor-parallel
-        attention), or each sequence's rows on its data-parallel rank."""
+        attention), or each sequence's rows on its data-parallel rank.
+        ``feed_from``: the batch still in flight whose sampled tokens the decode
+        rows of this batch read on the device (launch-ahead decode)."""
         seqs, q, flags = batch.sequences, batch.query_lens, batch.prefill_flags
         bs = self.config.kvcache_block_size
+        feeds = self._feed_maps(feed_from) if feed_from is not None else [None] * self.world
         if self.dp == 1 and self.config.attention_parallel == "tp" and self.world > 1:
-            plan = build_plan(seqs, q, flags, bs, self.max_blocks)
+            plan = build_plan(seqs, q, flags, bs, self.max_blocks, feed=feeds[0])
             plans = [plan] * self.world  # tensor-parallel attention: every rank runs every row
         elif self.dp == 1:
-            plans = [build_plan(seqs, q, flags, bs, self.max_blocks)] + \
+            plans = [build_plan(seqs, q, flags, bs, self.max_blocks, feed=feeds[0])] + \
                     [empty_plan(self.max_blocks) for _ in range(self.world - 1)]
         else:
             parts: list[list[int]] = [[] for _ in range(self.world)]
             for i, s in enumerate(seqs):
                 parts[max(s.dp_rank, 0)].append(i)
             plans = [build_plan([seqs[i] for i in idx], [q[i] for i in idx], [flags[i] for i in idx], bs,
-                                self.max_blocks, rows=idx) if idx else empty_plan(self.max_blocks)
-                     for idx in parts]
+                                self.max_blocks, rows=idx, feed=feeds[r]) if idx else empty_plan(self.max_blocks)
+                     for r, idx in enumerate(parts)]
         if grammar_masks:
             for p in plans:
                 g = [(r, grammar_masks[br]) for r, br in enumerate(p.rows.tolist()) if br in grammar_masks]
@@ -213,13 +217,20 @@ class Executor:
                     p.grammar_mask = np.stack([m for _, m in g]).astype(np.int32)
         return plans
 
+    def _feed_maps(self, batch) -> list[dict]:
+        """Per rank, {id(sequence): plan row} of the newest launched step, which
+        must be ``batch``: its rank-local sampled-token order."""
+        plans, _ = self._inflight[-1]
+        seqs = batch.sequences
+        return [{id(seqs[br]): r for r, br in enumerate(p.rows.tolist())} for p in plans]
+
     def check_alive(self):
         for r, p in enumerate(self.procs, start=1):
             if not p.is_alive():
                 raise RankFailure(f"rank {r} exited with code {p.exitcode}")
 
-    def launch(self, batch, grammar_masks: dict | None = None):
-        plans = self.plans(batch, grammar_masks)
+    def launch(self, batch, grammar_masks: dict | None = None, feed_from=None):
+        plans = self.plans(batch, grammar_masks, feed_from)
         self.check_alive()
         self._send_all("run", [(p,) for p in plans])
         try:
@@ -243,11 +254,11 @@ class Executor:
                 # an error (hung): the rank group is out of step, fail the step
                 raise RankFailure(f"collective failed with {self.world} ranks: {exc}") from exc
             raise
-        self._inflight = (plans, len(batch.sequences))
+        self._inflight.append((plans, len(batch.sequences)))
 
     def collect(self):
-        plans, n = self._inflight
-        self._inflight = None
+        """Tokens (batch-row order) of the oldest launched step."""
+        plans, n = self._inflight.popleft()
         results = [self.runner.collect()] + self._gather()
         tokens = [0] * n
         logprobs = None

@@ -72,6 +72,9 @@ class LLMEngine:
         self._pending_launch_time = 0.0
         self.overlap_defers = 0
         self.overlap_pruned_rows = 0
+        # launch-ahead decode (B200MOE_DECODE_FEED=0 disables it)
+        self._decode_feed = os.environ.get("B200MOE_DECODE_FEED", "1") != "0"
+        self.decode_feed_steps = 0
         self._grammar = None
         self._grammar_cache: dict = {}
         self._exited = False
@@ -221,9 +224,24 @@ class LLMEngine:
                 masks[i] = buf[0].numpy().copy()
         return masks
 
-    def _launch(self, batch: ScheduledBatch):
+    def _launch(self, batch: ScheduledBatch, feed_from: ScheduledBatch | None = None):
         self._pending_launch_time = perf_counter()
-        self.executor.launch(batch, self._grammar_masks(batch))
+        self.executor.launch(batch, self._grammar_masks(batch), feed_from)
+
+    def _feedable(self, nxt: ScheduledBatch, cur: ScheduledBatch) -> bool:
+        """Launch-ahead decode: the next decode batch can be enqueued before the
+        current one's tokens are read back when every row continues a row of
+        the current decode batch (its input token is read on the device) and
+        nothing on the host depends on the token values in between: greedy
+        sampling, no penalties, log-probs or grammar constraints."""
+        if not self._decode_feed or cur.mode != "decode" or nxt.mode != "decode" or any(nxt.prefill_flags):
+            return False
+        live = {id(s) for s in cur.sequences}
+        for s in nxt.sequences:
+            if (id(s) not in live or s.temperature >= 1e-3 or s.has_penalty or s.logprobs
+                    or s.grammar_matcher is not None):
+                return False
+        return True
 
     def step(self):
         self.last_token_events = []
@@ -238,6 +256,22 @@ class LLMEngine:
         return self._finish_step(batch, token_ids, logprobs)
 
     def _step_overlap(self):
+        if (self._pending is not None and self._sched_next is not None
+                and self._feedable(self._sched_next, self._pending)):
+            # launch-ahead: enqueue step N+1 (decode rows read N's tokens on the device),
+            # then read back and apply step N while N+1 runs.  Rows of sequences that
+            # finish at N run once more in N+1; their tokens are dropped by postprocess.
+            nxt, self._sched_next = self._sched_next, None
+            self._launch(nxt, feed_from=self._pending)
+            token_ids, logprobs = self.executor.collect()
+            outputs, num_tokens = self._finish_step(self._pending, token_ids, logprobs)
+            self._pending = nxt
+            spec = self.scheduler.schedule(speculative=True, inflight=nxt.sequences)
+            if spec.mode == "defer":
+                self.overlap_defers += 1
+            self._sched_next = None if (spec.mode == "defer" or not spec.sequences) else spec
+            self.decode_feed_steps += 1
+            return outputs, num_tokens
         outputs, num_tokens = [], 0
         collected = False
         if self._pending is not None:
@@ -308,6 +342,7 @@ class LLMEngine:
         decode_tokens = sum(q for q, f in zip(qlens, flags) if not f)
         num_tokens = batch.num_scheduled_tokens if mode != "decode" else -len(seqs)
         forward_s = perf_counter() - self._pending_launch_time
+        done_before = {id(s) for s in seqs if s.is_finished}  # finished by the previous step (launch-ahead rows)
         self.last_token_events = self.scheduler.postprocess(seqs, token_ids, mode, logprobs, qlens, flags)
         self.step_count += 1
         self.prefill_tokens_total += prefill_tokens
@@ -322,7 +357,8 @@ class LLMEngine:
                    "context_lens": batch.context_lens, "schedule_s": batch.schedule_s, "forward_s": forward_s}
             with open(self.metrics_path, "a", encoding="utf-8") as f:
                 f.write(json.dumps(rec, separators=(",", ":")) + "\n")
-        outputs = [(s.seq_id, s.completion_token_ids, s.metrics()) for s in seqs if s.is_finished]
+        outputs = [(s.seq_id, s.completion_token_ids, s.metrics()) for s in seqs
+                   if s.is_finished and id(s) not in done_before]
         return outputs, num_tokens
 
     # -------------------------------------------------------------- public
@@ -338,6 +374,7 @@ class LLMEngine:
             m[f"engine_{mode}_steps_total"] = n
         m["engine_overlap_defers_total"] = self.overlap_defers
         m["engine_overlap_pruned_rows_total"] = self.overlap_pruned_rows
+        m["engine_decode_feed_steps_total"] = self.decode_feed_steps
         m.update(self.scheduler.metrics())
         return m
 

@@ -12,6 +12,7 @@ per-tensor pinned copies, whole-graph capture per batch bucket).
 """
 from __future__ import annotations
 
+import collections
 import gc
 import math
 import os
@@ -110,12 +111,15 @@ class ModelRunner:
         self._pinned = [torch.empty(words, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self._pinned_np = [p.numpy() for p in self._pinned]
         self._dev_in = torch.empty(words, dtype=torch.int32, device=self.device)
+        # the last step's sampled tokens (plan-row order), read by the next step's
+        # embedding for rows launched before the host collected them
+        self._feed_tokens = torch.zeros(max(self.max_rows, 1), dtype=torch.int32, device=self.device)
         self._pin_idx = 0
         self._logits = None
         self.graphs: dict[int, tuple] = {}
         self.graph_pool = None
         self.offloader = None
-        self._pending = None
+        self._pending: collections.deque = collections.deque()  # steps launched, not yet collected
         self.steps = 0
         self.h2d_bytes = 0
         self._step_events: list = []
@@ -244,14 +248,16 @@ class ModelRunner:
         views["block_tables"] = views["block_tables"].view(plan.num_rows, plan.block_tables.shape[1])
         return views
 
-    def _inputs(self, plan: StepPlan, v: dict, max_seq_len: int | None = None) -> StepInputs:
+    def _inputs(self, plan: StepPlan, v: dict, max_seq_len: int | None = None, feed: bool = False) -> StepInputs:
         nd = plan.num_decode
         return StepInputs(
             input_ids=v["input_ids"], positions=v["positions"], slot_mapping=v["slot_mapping"],
             cu_seqlens_q=v["cu_seqlens_q"], seq_lens=v["seq_lens"], block_tables=v["block_tables"],
             logits_indices=v["logits_indices"], num_decode=nd, max_q_len=plan.max_q_len,
             max_seq_len=max_seq_len or plan.max_seq_len, num_rows=plan.num_rows,
-            prefill_cu=v["prefill_cu"] if plan.num_rows > nd else None)
+            prefill_cu=v["prefill_cu"] if plan.num_rows > nd else None,
+            feed_src=v["feed_src"] if (feed or plan.feed_src is not None) else None,
+            feed_tokens=self._feed_tokens if (feed or plan.feed_src is not None) else None)
 
     def _pad_plan(self, plan: StepPlan, rows: int) -> StepPlan:
         """A decode plan padded to ``rows`` rows; padding rows write the scratch block."""
@@ -262,12 +268,14 @@ class ModelRunner:
         tables[:B, :plan.block_tables.shape[1]] = plan.block_tables
         tables[:B, plan.block_tables.shape[1]:] = 0
         pad_i = np.zeros(p, np.int32)
+        feed = plan.feed_src if plan.feed_src is not None else np.full(B, -1, np.int32)
         return StepPlan(
             np.concatenate([plan.input_ids, pad_i]), np.concatenate([plan.positions, pad_i]),
             np.concatenate([plan.slot_mapping, np.full(p, self.scratch_block * self.block_size, np.int32)]),
             np.arange(rows + 1, dtype=np.int32), np.concatenate([plan.seq_lens, np.ones(p, np.int32)]),
             tables, rows, 0, plan.max_seq_len, np.arange(rows, dtype=np.int32),
-            np.concatenate([plan.temperature, np.zeros(p, np.float32)]))
+            np.concatenate([plan.temperature, np.zeros(p, np.float32)]),
+            feed_src=np.concatenate([feed, np.full(p, -1, np.int32)]))
 
     # ------------------------------------------------------------ graphs
     def _bucket(self, rows: int) -> int | None:
@@ -294,7 +302,7 @@ class ModelRunner:
             dummy.max_seq_len = self.config.max_model_len
             dev = torch.empty(words, dtype=torch.int32, device=self.device)
             views = self._upload(dummy, dev)
-            inp = self._inputs(dummy, views, max_seq_len=self.config.max_model_len)
+            inp = self._inputs(dummy, views, max_seq_len=self.config.max_model_len, feed=True)
             logits = self._graph_logits[:b]
             tokens = self._graph_tokens[:b]
             # warm-up run outside capture (first-use allocations, cached tensors)
@@ -333,7 +341,7 @@ class ModelRunner:
         if B == 0:
             if self.model.ep is not None:  # expert-parallel peers still need this rank's collectives
                 self.model(self._inputs(plan, self._upload(plan)), self.kv)
-            self._pending = (plan, None, None)
+            self._pending.append((plan, None, None))
             return
         bucket = self._bucket(B) if (plan.is_pure_decode and self.graphs) else None
         if bucket is not None:
@@ -353,17 +361,18 @@ class ModelRunner:
         lp = self._logprobs(plan, logits, tokens) if plan.logprobs_k else None
         out = torch.empty(B, dtype=torch.int32, pin_memory=self.device.type == "cuda")
         out.copy_(tokens, non_blocking=True)
+        self._feed_tokens[:B].copy_(tokens, non_blocking=True)  # the next step may read them on the device
         if self.device.type == "cuda":
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             self._step_events.append((t_start, ev, plan.is_pure_decode))
         else:
             ev = None
-        self._pending = (plan, out, (ev, lp))
+        self._pending.append((plan, out, (ev, lp)))
 
     def collect(self):
-        plan, out, extra = self._pending
-        self._pending = None
+        """Tokens of the oldest launched step."""
+        plan, out, extra = self._pending.popleft()
         if out is None:
             return [], None
         ev, lp = extra

@@ -45,6 +45,9 @@ class StepPlan:
     logprobs_k: int = 0
     grammar_rows: np.ndarray | None = None
     grammar_mask: np.ndarray | None = None   # int32 [n, words] allowed-token bitmask
+    # int32 [T]: row of the previous step whose sampled token (still on the
+    # device) is this token's id, -1 = use input_ids (launch-ahead decode)
+    feed_src: np.ndarray | None = None
 
     @property
     def num_rows(self) -> int:
@@ -75,8 +78,12 @@ def empty_plan(max_blocks: int = 1) -> StepPlan:
 
 
 def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int | None = None,
-               rows: list[int] | None = None) -> StepPlan:
-    """Plan for the given batch rows (one rank's share of a batch)."""
+               rows: list[int] | None = None, feed: dict | None = None) -> StepPlan:
+    """Plan for the given batch rows (one rank's share of a batch).
+
+    ``feed``: {id(sequence): row of the previous step's plan} for decode rows whose
+    input token is the previous step's sampled token, not yet read back to the host
+    (the sequence is one token longer than its host state)."""
     n = len(seqs)
     rows = list(range(n)) if rows is None else rows
     order = sorted(range(n), key=lambda i: (bool(prefill_flags[i]), i))
@@ -91,6 +98,7 @@ def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int
     seq_lens = np.empty(n, np.int32)
     mb = max_blocks or max((len(seqs[i].block_table) for i in order), default=1) or 1
     tables = np.zeros((n, mb), np.int32)
+    feed_src = np.full(T, -1, np.int32) if feed else None
     for r, i in enumerate(order):
         s = seqs[i]
         q = int(qlens[r])
@@ -98,6 +106,10 @@ def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int
         if prefill_flags[i]:
             start = s.num_cached_tokens
             ids[a:b] = s.token_ids[start:start + q]
+        elif feed is not None and id(s) in feed:
+            start = len(s)  # the token sampled by the step in flight
+            ids[a] = 0
+            feed_src[a] = feed[id(s)]
         else:
             start = len(s) - 1
             ids[a] = s.last_token
@@ -115,6 +127,7 @@ def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int
                     int(qlens[nd:].max()) if n > nd else 0,
                     int(seq_lens.max()) if n else 0,
                     np.asarray([rows[i] for i in order], np.int32), temps)
+    plan.feed_src = feed_src
     _sampling_meta(plan, [seqs[i] for i in order])
     return plan
 
@@ -159,7 +172,7 @@ def _sampling_meta(plan: StepPlan, seqs):
 
 
 PACK_FIELDS = ("input_ids", "positions", "slot_mapping", "cu_seqlens_q", "seq_lens", "logits_indices",
-               "prefill_cu", "block_tables")
+               "prefill_cu", "feed_src", "block_tables")
 
 
 def pack_plan(plan: StepPlan, out: np.ndarray | None = None) -> tuple[np.ndarray, dict]:
@@ -171,6 +184,7 @@ def pack_plan(plan: StepPlan, out: np.ndarray | None = None) -> tuple[np.ndarray
         "cu_seqlens_q": cu, "seq_lens": plan.seq_lens,
         "logits_indices": (cu[1:] - 1).astype(np.int32),
         "prefill_cu": (cu[nd:] - cu[nd]).astype(np.int32),
+        "feed_src": plan.feed_src if plan.feed_src is not None else np.full(plan.input_ids.size, -1, np.int32),
         "block_tables": plan.block_tables.reshape(-1),
     }
     total = sum(p.size for p in parts.values())

@@ -53,6 +53,8 @@ class StepInputs:
     max_seq_len: int               # over all rows (decode split sizing)
     num_rows: int
     prefill_cu: torch.Tensor | None = None  # cu_seqlens of the prefill rows, rebased to 0
+    feed_src: torch.Tensor | None = None    # int32 [T]: >= 0 -> the id is feed_tokens[feed_src[t]]
+    feed_tokens: torch.Tensor | None = None  # previous step's sampled tokens (device)
 
     @property
     def num_tokens(self) -> int:
@@ -261,7 +263,9 @@ class Qwen3MoeForCausalLM(nn.Module):
         H = a.hidden_size
         eps = a.rms_norm_eps
         cuda = self.cuda
-        residual = ops.embed(inp.input_ids, self.embed_tokens, out=self._buf("h", (T, H), self.dtype) if cuda else None)
+        feed = (inp.feed_src, inp.feed_tokens) if inp.feed_src is not None else None
+        residual = ops.embed(inp.input_ids, self.embed_tokens, out=self._buf("h", (T, H), self.dtype) if cuda else None,
+                             feed=feed)
         x = ops.rmsnorm(residual, self.layers[0].input_layernorm, eps,
                         out=self._buf("x", (T, H), self.dtype) if cuda else None)
         for l, layer in enumerate(self.layers):

@@ -313,12 +313,20 @@ def dequant_weights(q: torch.Tensor, scale: torch.Tensor, out: torch.Tensor, til
 
 
 # -------------------------------------------------------------- fused ops
-def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None,
+          feed: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+    """Embedding rows of ``ids``; ``feed = (src, tokens)``: token t takes its id
+    from ``tokens[src[t]]`` where ``src[t] >= 0`` (the previous step's sampled
+    tokens, still on the device)."""
     if not ids.is_cuda:
+        if feed is not None:
+            src, toks = feed
+            src = src[:ids.numel()].long()
+            ids = torch.where(src >= 0, toks.long()[src.clamp(min=0)], ids.long())
         return table[ids.long()].clone()
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=ids.device)
-    native().embed(ids, table, out, status_word(ids.device))
+    native().embed(ids, table, out, status_word(ids.device), *(feed if feed is not None else (None, None)))
     count_launches()
     return out
 

@@ -214,3 +214,22 @@ def test_natural_layout_restores_tiling():
     with natural_layout(m2):
         pass
     assert m2.calls == []
+
+
+def test_launch_ahead_decode_matches_plain_steps():
+    """Decode steps launched before the previous step's tokens are read back
+    (their input token read on the device) give the tokens of plain stepping,
+    with sequences finishing at different steps (length limits and stop tokens)."""
+    import random as _r
+    rng = _r.Random(3)
+    prompts = [[rng.randrange(1, 400) for _ in range(rng.randrange(5, 60))] for _ in range(7)]
+    sps = [SamplingParams(temperature=0.0, max_tokens=rng.randrange(1, 25), ignore_eos=bool(i % 2),
+                          stop_token_ids=[rng.randrange(1, 400)]) for i in range(len(prompts))]
+    base = dict(kvcache_block_size=16, max_num_seqs=8, max_num_batched_tokens=256, max_model_len=256,
+                num_kvcache_blocks=128, device="cpu", enforce_eager=True)
+    ahead = LLM("tiny-moe-fp8", scheduler_overlap=True, **base)
+    plain = LLM("tiny-moe-fp8", scheduler_overlap=False, **base)
+    a = ahead.generate(prompts, sps, use_tqdm=False)
+    b = plain.generate(prompts, sps, use_tqdm=False)
+    assert [x["token_ids"] for x in a] == [x["token_ids"] for x in b]
+    assert ahead.metrics()["engine_decode_feed_steps_total"] > 0
