@@ -63,7 +63,7 @@ def _worker_main(config: Config, rank: int, conn, parent_pid: int, shm_spec=None
             continue
         try:
             cmd, args = conn.recv()
-        except EOFError:
+        except (EOFError, OSError):  # driver gone, or a frame failed its checks
             os._exit(1)
         if cmd == "exit":
             try:
@@ -71,11 +71,14 @@ def _worker_main(config: Config, rank: int, conn, parent_pid: int, shm_spec=None
             finally:
                 conn.send(("ok", None))
             return
+        # replies carry their command's kind: a step's reply may still be
+        # uncollected when the driver issues a call (KV offload under overlap)
+        kind = "run" if cmd == "run" else "call"
         try:
             res = getattr(runner, cmd)(*args)
-            conn.send(("ok", res))
+            conn.send(("ok", res, kind))
         except BaseException:
-            conn.send(("error", traceback.format_exc()))
+            conn.send(("error", traceback.format_exc(), kind))
 
 
 class Executor:
@@ -117,6 +120,8 @@ class Executor:
                 raise RankFailure(f"rank {r} failed to start:\n{payload}")
         self.max_blocks = self.runner.max_blocks
         self._inflight: collections.deque = collections.deque()  # (plans, rows) of launched steps
+        # per worker, replies that arrived while another kind was awaited
+        self._stash = [collections.deque() for _ in self.conns]
 
     # ------------------------------------------------------------ plumbing
     def _recv(self, rank: int, conn, timeout: float | None = None):
@@ -135,6 +140,22 @@ class Executor:
             if not proc.is_alive():
                 raise RankFailure(f"rank {rank} exited with code {proc.exitcode}")
 
+    def _reply(self, rank: int, conn, kind: str, timeout: float | None = None):
+        """The oldest reply of ``kind`` ("run" or "call") from ``rank``.  A
+        worker answers in command order, so a call issued while steps are in
+        flight first meets their replies: those wait in the stash, in order,
+        for ``collect``."""
+        stash = self._stash[rank - 1]
+        for i, msg in enumerate(stash):
+            if msg[2] == kind:
+                del stash[i]
+                return msg[0], msg[1]
+        while True:
+            msg = self._recv(rank, conn, timeout)
+            if len(msg) < 3 or msg[2] == kind:
+                return msg[0], msg[1]
+            stash.append(msg)
+
     def _send_all(self, cmd: str, per_rank_args: list[tuple]):
         for r, c in enumerate(self.conns, start=1):
             try:
@@ -142,10 +163,10 @@ class Executor:
             except (BrokenPipeError, OSError) as exc:
                 raise RankFailure(f"rank {r} is gone ({exc!r})") from exc
 
-    def _gather(self) -> list:
+    def _gather(self, kind: str = "call") -> list:
         out = []
         for r, c in enumerate(self.conns, start=1):
-            status, payload = self._recv(r, c)
+            status, payload = self._reply(r, c, kind)
             if status != "ok":
                 raise RankFailure(f"rank {r} raised:\n{payload}")
             out.append(payload)
@@ -173,7 +194,7 @@ class Executor:
             c.send((method, args))
         except (BrokenPipeError, OSError) as exc:
             raise RankFailure(f"rank {rank} is gone ({exc!r})") from exc
-        status, payload = self._recv(rank, c)
+        status, payload = self._reply(rank, c, "call")
         if status != "ok":
             raise RankFailure(f"rank {rank} raised:\n{payload}")
         return payload
@@ -244,7 +265,7 @@ class Executor:
                     raise RankFailure(f"rank {r} exited with code {p.exitcode}") from exc
                 try:
                     if c.poll(0):
-                        status, payload = c.recv()
+                        status, payload = c.recv()[:2]
                         if status == "error":
                             raise RankFailure(f"rank {r} raised:\n{payload}") from exc
                 except (EOFError, OSError):
@@ -259,7 +280,7 @@ class Executor:
     def collect(self):
         """Tokens (batch-row order) of the oldest launched step."""
         plans, n = self._inflight.popleft()
-        results = [self.runner.collect()] + self._gather()
+        results = [self.runner.collect()] + self._gather("run")
         tokens = [0] * n
         logprobs = None
         for plan, (toks, lps) in zip(plans, results):

@@ -8,6 +8,12 @@ receiver sees a message in a few microseconds instead of the ~70 us a pipe
 wake-up costs.  The pipe also carries messages larger than the segment and
 reports a peer that died (EOF).
 
+Every message is framed as ``<QI`` (sequence number, CRC-32 of the body)
+followed by the pickled body.  The receiver checks that the sequence number is
+the one it expects next and that the CRC matches before unpickling; a frame
+that fails either check raises ``ControlMessageError`` (an ``OSError``, so the
+executor reports the rank as failed instead of acting on a torn or stale plan).
+
 ``ShmLink`` exposes the ``send`` / ``poll`` / ``recv`` subset of
 ``multiprocessing.Connection`` that the executor uses, so the failure handling
 around it (bounded waits, liveness checks) is unchanged.  It plays the role of
@@ -18,7 +24,9 @@ from __future__ import annotations
 
 import os
 import pickle
+import struct
 import time
+import zlib
 from multiprocessing import shared_memory
 
 import numpy as np
@@ -26,6 +34,28 @@ import numpy as np
 CTL = 4096           # control words, then the two data regions
 _SEQ, _LEN, _SLEEP, _DONE = 0, 2, 4, 6   # + direction (0: driver -> worker, 1: worker -> driver)
 _BIG = -1            # payload travels on the pipe
+HEADER = struct.Struct("<QI")   # (sequence number, crc32 of the body)
+
+
+class ControlMessageError(OSError):
+    """A control frame failed its sequence or checksum check."""
+
+
+def frame(seq: int, body: bytes) -> bytes:
+    return HEADER.pack(seq, zlib.crc32(body)) + body
+
+
+def unframe(data, want_seq: int):
+    """Validate one frame and return the unpickled body."""
+    if len(data) < HEADER.size:
+        raise ControlMessageError(f"control frame of {len(data)} bytes is shorter than its header")
+    seq, crc = HEADER.unpack_from(data)
+    body = data[HEADER.size:]
+    if seq != want_seq:
+        raise ControlMessageError(f"control frame carries sequence {seq}, expected {want_seq}")
+    if zlib.crc32(body) != crc:
+        raise ControlMessageError(f"control frame {seq} failed its checksum")
+    return pickle.loads(body)
 
 
 def _spin_s() -> float:
@@ -71,9 +101,10 @@ class ShmLink:
             if time.monotonic() > deadline:
                 raise BrokenPipeError("peer did not consume the previous message")
             time.sleep(0)
-        data = pickle.dumps(obj, protocol=5)
+        data = frame(self.sent + 1, pickle.dumps(obj, protocol=5))
         if len(data) <= self.capacity:
-            self._region(self.out_dir)[:len(data)] = data
+            with self._region(self.out_dir) as region:
+                region[:len(data)] = data
             self.ctl[_LEN + self.out_dir] = len(data)
         else:
             self.ctl[_LEN + self.out_dir] = _BIG
@@ -124,9 +155,10 @@ class ShmLink:
                 if msg[:1] == b"P":
                     data = msg[1:]
             self._stash = None
-            obj = pickle.loads(data)
         else:
-            obj = pickle.loads(self._region(self.in_dir)[:n])
+            with self._region(self.in_dir) as region:
+                data = bytes(region[:n])
+        obj = unframe(data, self.seen + 1)
         self.seen += 1
         self.ctl[_DONE + self.in_dir] = self.seen
         return obj

@@ -109,3 +109,76 @@ def test_exit_watchdog_bounds_wedged_teardown(tmp_path):
     assert time.monotonic() - t0 < 30
     assert "unreachable" not in r.stdout
     assert "watchdog" in r.stderr
+
+
+def _link_pair(capacity=1 << 16):
+    import multiprocessing as mp
+    from b200moe.engine.shm_channel import ShmLink
+    a, b = mp.Pipe(duplex=True)
+    drv = ShmLink.create(a, capacity=capacity)
+    wrk = ShmLink(drv.spec()[0], b, 1, capacity)
+    return drv, wrk
+
+
+def test_control_frame_checks_reject_torn_and_stale_messages():
+    from b200moe.engine import shm_channel as sc
+    drv, wrk = _link_pair()
+    try:
+        drv.send(("step", [1, 2, 3]))
+        assert wrk.recv() == ("step", [1, 2, 3])
+        wrk.send(("ok", 7))
+        assert drv.recv() == ("ok", 7)
+        # a flipped byte in the body fails the checksum
+        drv.send(("step", list(range(100))))
+        with wrk._region(0) as region:
+            region[sc.HEADER.size + 20] ^= 0xFF
+        with pytest.raises(sc.ControlMessageError, match="checksum"):
+            wrk.recv()
+    finally:
+        wrk.close()
+        drv.close()
+    drv, wrk = _link_pair()
+    try:
+        drv.send(("a", 1))
+        # a frame stamped with another sequence number (a stale or replayed plan)
+        with wrk._region(0) as region:
+            sc.HEADER.pack_into(region, 0, 5, 0)
+        with pytest.raises(sc.ControlMessageError, match="sequence 5, expected 1"):
+            wrk.recv()
+    finally:
+        wrk.close()
+        drv.close()
+
+
+def test_oversize_frames_travel_on_the_pipe_and_are_checked():
+    from b200moe.engine import shm_channel as sc
+    drv, wrk = _link_pair(capacity=4096)
+    try:
+        big = bytes(range(256)) * 64
+        drv.send(("big", big))
+        assert wrk.recv() == ("big", big)
+        wrk.send(("ok", None))
+        assert drv.recv() == ("ok", None)
+    finally:
+        wrk.close()
+        drv.close()
+    assert issubclass(sc.ControlMessageError, OSError)  # the executor's liveness path catches OSError
+
+
+def test_corrupt_step_plan_fails_the_rank_not_the_model(monkeypatch):
+    """The driver's frames to rank 1 go out with a wrong checksum: the worker
+    rejects the frame and leaves, and the driver reports RankFailure within
+    the rank timeout instead of running a torn step."""
+    from b200moe.engine import shm_channel as sc
+    llm = LLM("tiny-moe", tensor_parallel_size=2, rank_timeout_s=20, **KW)
+    try:
+        assert llm.generate([[1, 2, 3]], SP, use_tqdm=False)[0]["token_ids"]
+        real = sc.frame
+        monkeypatch.setattr(sc, "frame", lambda seq, body: real(seq, body[:-1] + bytes([body[-1] ^ 1])))
+        t0 = time.monotonic()
+        with pytest.raises(RankFailure):
+            llm.generate([[4, 5, 6]], SP, use_tqdm=False)
+        assert time.monotonic() - t0 < 20
+        monkeypatch.setattr(sc, "frame", real)
+    finally:
+        llm.exit()
