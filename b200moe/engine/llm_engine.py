@@ -209,6 +209,30 @@ class LLMEngine:
         """Runtime switch; disabling drains the pipeline (parked batch launches)."""
         self._overlap = bool(enabled)
 
+    # ----------------------------------------------------------- profiling
+    def set_profiling(self, enabled: bool):
+        """Start or stop the device-timed ranges on every rank."""
+        self.executor.call("set_profiling", bool(enabled))
+
+    def start_profiling(self):
+        self.set_profiling(True)
+
+    def stop_profiling(self):
+        self.set_profiling(False)
+
+    def profile_snapshot(self, reset: bool = True) -> dict:
+        """Every rank's per-range p50 / p95 (reference: nanovllm/engine/model_runner.py:377-383
+        gathers the ranks' snapshots).  ``max_over_ranks`` keeps, per range,
+        the slowest rank's figures: a step waits for its slowest rank."""
+        per_rank = self.executor.call_all("profile_snapshot", reset)
+        worst: dict[str, dict] = {}
+        for snap in per_rank:
+            for name, st in snap["segments"].items():
+                w = worst.setdefault(name, {"count": 0, "total_ms": 0.0, "p50_ms": 0.0, "p95_ms": 0.0})
+                for key in w:
+                    w[key] = max(w[key], st[key])
+        return {"ranks": per_rank, "max_over_ranks": worst}
+
     # --------------------------------------------------------------- steps
     def _grammar_masks(self, batch: ScheduledBatch):
         """Allowed-token bitmask per guided row (batch row -> int32 words)."""

@@ -24,8 +24,9 @@ import torch
 from b200moe import ops
 from b200moe.config import Config
 from b200moe.engine.kv_cache import KVPool
-from b200moe.engine.step_plan import StepPlan, empty_plan, pack_plan
+from b200moe.engine.step_plan import StepPlan, empty_plan, pack_plan, validate_plan
 from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM, StepInputs
+from b200moe.utils.init_trace import InitTrace
 from b200moe.utils.profiler import DeviceProfiler
 from b200moe.utils.weights import load_checkpoint, random_init_
 
@@ -63,6 +64,7 @@ class ModelRunner:
     def __init__(self, config: Config, rank: int = 0, world_size: int | None = None, init_dist: bool = True):
         self.config = config
         self.rank = rank
+        trace = InitTrace(rank)
         self.world_size = world_size or config.world_size
         self.block_size = config.kvcache_block_size
         args = config.hf_config
@@ -76,8 +78,10 @@ class ModelRunner:
             ops.native()  # fail loudly when the extension is missing on a GPU box
         else:
             self.device = torch.device("cpu")
+        trace.mark("device")
         if self.world_size > 1 and init_dist:
             self._init_dist()
+            trace.mark("process_group")
         self.profiler = DeviceProfiler(self.device, enabled=config.enable_profiling)
         expert_ids = expert_placement(config, rank, self.world_size) if args.is_moe else []
         t0 = time.perf_counter()
@@ -90,12 +94,15 @@ class ModelRunner:
         if self.world_size > 1 and self.attn_tp == 1:
             from b200moe.parallel.ep import ExpertParallel
             self.model.ep = ExpertParallel(self, config.moe_backend)
+        trace.mark("model")
         if config.random_init:
             random_init_(self.model, seed=config.seed)
         else:
             load_checkpoint(self.model, config.model)
+        trace.mark("weights")
         if os.environ.get("B200MOE_TILED_WEIGHTS", "1") != "0":
             self.model.tile_weights_()  # e4m3 GEMM weights tile-major: one contiguous HBM block per stage
+            trace.mark("tile_weights")
         self.model.profiler = self.profiler if config.enable_profiling else None
         self.load_s = time.perf_counter() - t0
         self.max_blocks = -(-config.max_model_len // self.block_size)
@@ -104,7 +111,9 @@ class ModelRunner:
         self.max_splits = self.model.decode_splits(1, config.max_model_len)[1]
         if self.device.type == "cuda":
             self.model.reserve_workspace(self.max_tokens, self.max_rows, self.max_splits)
+            trace.mark("workspace")
         self.allocate_kv_cache()
+        trace.mark("kv_cache")
         # two pinned staging buffers: a step may be uploaded while the previous one's copy is in flight
         words = 8 * self.max_tokens + 8 * self.max_rows + self.max_rows * self.max_blocks + 16
         pin = self.device.type == "cuda"
@@ -115,6 +124,7 @@ class ModelRunner:
         # embedding for rows launched before the host collected them
         self._feed_tokens = torch.zeros(max(self.max_rows, 1), dtype=torch.int32, device=self.device)
         self._pin_idx = 0
+        self._validate = os.environ.get("B200MOE_VALIDATE_PLANS", "1") != "0"
         self._logits = None
         self.graphs: dict[int, tuple] = {}
         self.graph_pool = None
@@ -126,6 +136,8 @@ class ModelRunner:
         self._graph_kernels: dict[int, int] = {}
         if self._graphs_allowed():
             self.capture_cudagraphs()
+            trace.mark("cuda_graphs")
+        self.init_stages = trace.done()
 
     def _graphs_allowed(self) -> bool:
         """Decode graphs need the native paths: the per-expert loop and the
@@ -288,7 +300,15 @@ class ModelRunner:
     def capture_cudagraphs(self):
         """One graph per decode bucket: forward + LM head + greedy argmax into
         static buffers.  Decode split sizing uses max_model_len so the graph
-        is valid for any context length."""
+        is valid for any context length.  Profiler ranges stay out of the
+        graphs: a replayed step is timed as one "forward" range."""
+        prof, self.model.profiler = self.model.profiler, None
+        try:
+            self._capture_cudagraphs()
+        finally:
+            self.model.profiler = prof
+
+    def _capture_cudagraphs(self):
         max_bs = min(self.config.cuda_graph_max_bs, self.max_rows)
         buckets = [b for b in GRAPH_BUCKETS if b <= max_bs]
         V = self.args.vocab_size
@@ -332,6 +352,9 @@ class ModelRunner:
     @torch.inference_mode()
     def launch(self, plan: StepPlan):
         """Enqueue the step (no host sync); ``collect`` reads the result."""
+        if self._validate:
+            validate_plan(plan, self.config.num_kvcache_blocks, self.block_size, self.args.vocab_size,
+                          self._feed_tokens.numel())
         self.steps += 1
         B = plan.num_rows
         t_start = None
@@ -484,6 +507,22 @@ class ModelRunner:
     def check_status(self):
         if self.device.type == "cuda":
             ops.check_status(self.device)
+
+    # ------------------------------------------------------------ profiling
+    def set_profiling(self, enabled: bool):
+        """Start or stop the device-timed ranges on this rank (the model's
+        per-segment ranges run on eager steps; graph replays time as one range)."""
+        if enabled:
+            self.profiler.start()
+        else:
+            self.profiler.stop()
+        self.model.profiler = self.profiler if enabled else None
+
+    def profile_snapshot(self, reset: bool = True) -> dict:
+        """This rank's per-range and per-layer p50 / p95 (one device sync)."""
+        out = self.profiler.snapshot(reset)
+        out["rank"] = self.rank
+        return out
 
     def exit(self):
         self.graphs.clear()

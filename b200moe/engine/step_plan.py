@@ -132,6 +132,33 @@ def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int
     return plan
 
 
+def validate_plan(plan: StepPlan, num_blocks: int, block_size: int, vocab: int, feed_rows: int) -> None:
+    """Reject a plan whose indices would make a kernel read or write outside its
+    buffers: block ids outside the pool, KV slots outside the pool, token ids
+    outside the vocabulary, feed rows outside the previous step's token buffer.
+    The kernels trust these indices (the embedding kernel alone re-checks its
+    ids), so this host check stands in for device bounds checks on the hot path.
+    A few vectorised min / max reductions: microseconds for a 256-row plan."""
+    if plan.num_rows == 0:
+        return
+
+    def bad(what, lo, hi, arr):
+        raise ValueError(f"step plan: {what} outside [{lo}, {hi}) (min {int(arr.min())}, max {int(arr.max())})")
+
+    if plan.block_tables.size and (plan.block_tables.min() < 0 or plan.block_tables.max() >= num_blocks):
+        bad("block id", 0, num_blocks, plan.block_tables)
+    limit = num_blocks * block_size
+    if plan.slot_mapping.size and (plan.slot_mapping.min() < 0 or plan.slot_mapping.max() >= limit):
+        bad("KV slot", 0, limit, plan.slot_mapping)
+    if plan.input_ids.size and (plan.input_ids.min() < 0 or plan.input_ids.max() >= vocab):
+        bad("token id", 0, vocab, plan.input_ids)
+    if plan.feed_src is not None and plan.feed_src.size and plan.feed_src.max() >= feed_rows:
+        bad("feed row", -1, feed_rows, plan.feed_src)
+    cap = plan.block_tables.shape[1] * block_size
+    if plan.seq_lens.min() < 1 or plan.seq_lens.max() > cap:
+        bad("context length", 1, cap + 1, plan.seq_lens)
+
+
 def _sampling_meta(plan: StepPlan, seqs):
     n = len(seqs)
     if any(s.top_k != -1 for s in seqs):

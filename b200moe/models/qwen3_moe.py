@@ -432,6 +432,8 @@ class Qwen3MoeForCausalLM(nn.Module):
             slot_of_row = self._buf("slot_of_row", (rows,), torch.int32)
             offsets = self._buf("offsets", (E + 1,), torch.int32)
             ops.moe_permute(x, ids, counts[:E], counts[E:2 * E], x_perm, slot_of_row, offsets)
+        if self.profiler is not None:
+            self.profiler.observe("moe.max_expert_rows", counts[:E].max())  # routing imbalance
         if self._bf16_experts(rows):
             # large prefill batch: dequantise once, then bf16 GEMMs (no per-tile dequantisation)
             w13 = self._buf("w13_bf16", tuple(layer.w13.shape), torch.bfloat16)

@@ -121,6 +121,8 @@ class ExpertParallel:
         counts = torch.stack([send_counts, recv_counts]).cpu()  # the one host sync per layer
         sc, rc = counts[0].tolist(), counts[1].tolist()
         R = sum(rc)
+        if model.profiler is not None:
+            model.profiler.observe("moe.local_pairs", R)  # expert-parallel load on this rank
         send_x = x.index_select(0, order // k)
         meta = torch.stack([flat_ids[order].to(torch.int32),
                             w.reshape(-1)[order].contiguous().view(torch.int32)], dim=1)

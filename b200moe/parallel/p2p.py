@@ -134,6 +134,8 @@ class P2PMoE:
         cnt = model._buf("ep_counts", (2 * El,), torch.int32)
         cnt.zero_()
         C.ep_count(*a, cnt[:El])
+        if model.profiler is not None:
+            model.profiler.observe("moe.local_pairs", cnt[:El].sum())
         rows = self.W * self.cap
         xp = model._buf("x_perm", (rows, self.H), model.dtype)
         code = model._buf("slot_of_row", (rows,), torch.int32)

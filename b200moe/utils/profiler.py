@@ -63,9 +63,11 @@ class DeviceProfiler:
                 b = time.perf_counter()
             self._pending.append((name, layer, a, b))
 
-    def observe(self, name: str, value: float):
+    def observe(self, name, value):
+        """A scalar observation; a device tensor is read at ``snapshot()``
+        (its one sync), not here."""
         if self.enabled:
-            self._obs[name].append(float(value))
+            self._obs[name].append(value.detach() if isinstance(value, torch.Tensor) else float(value))
 
     def snapshot(self, reset: bool = True) -> dict:
         if self.device.type == "cuda" and self._pending:
@@ -82,9 +84,10 @@ class DeviceProfiler:
             return {k: {"count": len(v), "total_ms": sum(v), "p50_ms": percentile(v, 50),
                         "p95_ms": percentile(v, 95)} for k, v in d.items()}
 
+        obs = {k: [float(x) for x in v] for k, v in self._obs.items()}
         out = {"segments": summ(seg), "layers": summ(per_layer),
                "observations": {k: {"count": len(v), "mean": sum(v) / len(v), "p50": percentile(v, 50),
-                                    "p95": percentile(v, 95)} for k, v in self._obs.items() if v}}
+                                    "p95": percentile(v, 95)} for k, v in obs.items() if v}}
         if reset:
             self._pending.clear()
             self._obs.clear()

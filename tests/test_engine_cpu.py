@@ -233,3 +233,61 @@ def test_launch_ahead_decode_matches_plain_steps():
     b = plain.generate(prompts, sps, use_tqdm=False)
     assert [x["token_ids"] for x in a] == [x["token_ids"] for x in b]
     assert ahead.metrics()["engine_decode_feed_steps_total"] > 0
+
+
+def test_plan_validation_rejects_out_of_range_indices():
+    """The host check in front of every launch: block ids, KV slots, token ids,
+    feed rows and context lengths outside their buffers raise before any
+    kernel sees them; the engine's own plans pass it."""
+    from b200moe.engine.sequence import Sequence
+    from b200moe.engine.step_plan import build_plan, validate_plan
+    Sequence.block_size = 16
+    s = Sequence(list(range(40)), SamplingParams(max_tokens=4))
+    s.block_table = [3, 5, 7]
+    plan = build_plan([s], [40], [True], 16, max_blocks=4)
+    validate_plan(plan, num_blocks=8, block_size=16, vocab=1000, feed_rows=8)
+    for field, value, msg in (("block_tables", 8, "block id"), ("slot_mapping", 8 * 16, "KV slot"),
+                              ("input_ids", 1000, "token id"), ("seq_lens", 65, "context length")):
+        bad = build_plan([s], [40], [True], 16, max_blocks=4)
+        getattr(bad, field).reshape(-1)[0] = value
+        with pytest.raises(ValueError, match=msg):
+            validate_plan(bad, num_blocks=8, block_size=16, vocab=1000, feed_rows=8)
+    s2 = Sequence(list(range(20)), SamplingParams(max_tokens=4))
+    s2.block_table = [1, 2]
+    s2.num_cached_tokens = 19
+    fed = build_plan([s2], [1], [False], 16, max_blocks=4, feed={id(s2): 9})
+    with pytest.raises(ValueError, match="feed row"):
+        validate_plan(fed, num_blocks=8, block_size=16, vocab=1000, feed_rows=8)
+    llm = LLM("tiny-moe", device="cpu", kvcache_block_size=16, num_kvcache_blocks=8, max_num_batched_tokens=128,
+              max_num_seqs=4, max_model_len=64, enforce_eager=True)
+    try:
+        plan.block_tables[0, 0] = 8 + 1  # the runner's pool has 8 blocks (+ its scratch block)
+        with pytest.raises(ValueError, match="block id"):
+            llm.model_runner.launch(plan)
+        assert not llm.model_runner._pending
+        out = llm.generate([[1, 2, 3]], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True),
+                           use_tqdm=False)
+        assert len(out[0]["token_ids"]) == 3
+    finally:
+        llm.exit()
+
+
+def test_per_step_jsonl_trace(tmp_path):
+    """``metrics_path``: one JSON line per step with mode, batch, token counts,
+    query / context lengths and schedule / forward seconds
+    (reference: nanovllm/engine/llm_engine.py:459-474)."""
+    import json
+    path = tmp_path / "steps.jsonl"
+    llm = LLM("tiny-moe", device="cpu", kvcache_block_size=16, num_kvcache_blocks=32, max_num_batched_tokens=128,
+              max_num_seqs=4, max_model_len=128, enforce_eager=True, metrics_path=str(path))
+    try:
+        llm.generate([[1, 2, 3, 4], list(range(10, 40))],
+                     SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True), use_tqdm=False)
+    finally:
+        llm.exit()
+    recs = [json.loads(line) for line in path.read_text().splitlines()]
+    assert recs and all(r["kind"] == "step" for r in recs)
+    assert recs[0]["mode"] == "prefill" and recs[0]["prefill_tokens"] == 34 and recs[0]["query_lens"] == [4, 30]
+    assert recs[-1]["mode"] == "decode" and recs[-1]["decode_tokens"] == 2
+    assert sum(r["prefill_tokens"] for r in recs) == 34 and sum(r["decode_tokens"] for r in recs) == 4
+    assert all(r["forward_s"] >= 0 and r["schedule_s"] >= 0 for r in recs)

@@ -4,6 +4,7 @@ single-rank engine (fp32 tiny model)."""
 import random
 
 import numpy as np
+import pytest
 
 from b200moe import LLM, SamplingParams
 
@@ -68,3 +69,62 @@ def test_gloo_world2_launch_ahead_decode():
     assert [len(x) for x in a] == [len(x) for x in b]
     agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
     assert agree > 0.98, agree
+
+
+def _offload_run(llm):
+    rng = random.Random(9)
+    shared = [rng.randrange(500) for _ in range(64)]
+    group_a = [shared + [rng.randrange(500) for _ in range(16)] for _ in range(4)]
+    group_b = [[rng.randrange(500) for _ in range(96)] for _ in range(12)]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    try:
+        first = [o["token_ids"] for o in llm.generate(group_a, sp, use_tqdm=False)]
+        llm.generate(group_b, sp, use_tqdm=False)  # evicts group A's prefix to the host pool
+        again = [o["token_ids"] for o in llm.generate(group_a, sp, use_tqdm=False)]
+        return first, again, llm.metrics()
+    finally:
+        llm.exit()
+
+
+@pytest.mark.parametrize("attention_parallel", ["dp", "tp"])
+def test_gloo_world2_overlap_with_kv_offload(attention_parallel):
+    """Two gloo ranks, overlap pipeline, a device pool small enough that the
+    speculative schedule moves blocks to and from the host pool while a step
+    is in flight: the workers' offload replies and step replies are matched
+    by kind, and the tokens match one rank without offload."""
+    kw = dict(device="cpu", kvcache_block_size=16, max_num_batched_tokens=256, max_num_seqs=8, max_model_len=256,
+              enforce_eager=True, rank_timeout_s=60)
+    ref, _, _ = _offload_run(LLM("tiny-moe", num_kvcache_blocks=64, **kw))
+    first, again, m = _offload_run(LLM("tiny-moe", num_kvcache_blocks=24, kv_offload_enabled=True,
+                                       kv_offload_host_blocks=64, tensor_parallel_size=2, scheduler_overlap=True,
+                                       attention_parallel=attention_parallel, **kw))
+    assert m["kv_offload_puts_total"] > 0 and m["kv_offload_revives_total"] > 0, m
+    for got in (first, again):
+        agree = np.mean([x == y for ra, rb in zip(ref, got) for x, y in zip(ra, rb)])
+        assert agree > 0.98, agree
+
+
+def test_gloo_world2_profile_snapshot_and_init_trace(monkeypatch, capfd):
+    """Device-timed ranges switched on at run time on both ranks, gathered by
+    the engine with the slowest rank per range; init milestones are timed on
+    every rank and printed under B200MOE_TRACE_INIT."""
+    monkeypatch.setenv("B200MOE_TRACE_INIT", "1")
+    kw = dict(device="cpu", kvcache_block_size=16, num_kvcache_blocks=128, max_num_batched_tokens=512,
+              max_num_seqs=16, max_model_len=256, enforce_eager=True)
+    llm = LLM("tiny-moe", tensor_parallel_size=2, **kw)
+    try:
+        stages = llm.model_runner.init_stages
+        assert {"device", "process_group", "model", "weights", "kv_cache", "total"} <= set(stages)
+        out = capfd.readouterr().out
+        assert "[init] rank 0 weights" in out and "[init] rank 1 ready" in out
+        llm.start_profiling()
+        llm.generate(_prompts(4), SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True), use_tqdm=False)
+        snap = llm.profile_snapshot()
+        llm.stop_profiling()
+    finally:
+        llm.exit()
+    assert [s["rank"] for s in snap["ranks"]] == [0, 1]
+    worst = snap["max_over_ranks"]
+    assert worst["forward"]["count"] > 0 and worst["attn.core"]["p50_ms"] > 0
+    for name, w in worst.items():
+        assert w["p95_ms"] == max(s["segments"].get(name, {"p95_ms": 0.0})["p95_ms"] for s in snap["ranks"])

@@ -464,3 +464,39 @@ def test_sampler_distribution():
     tk = torch.full((N,), 3, dtype=torch.int32, device=DEV)
     s = ops.sample(logits, temp, tk, None, None, seeds, None)
     assert int(s.max()) <= 2
+
+
+def _ep_wait_args(world, epoch, done, status):
+    """EpArgs for one GPU whose every per-rank pointer is local memory: the
+    wait kernel reads done[rank][r] for r < world and nothing else."""
+    i32 = dict(dtype=torch.int32, device=DEV)
+    local = [done.data_ptr()] * world
+    return ([world, 0, 8, 1, 1], torch.zeros(1, **i32), torch.zeros(1, **i32), torch.zeros(world, **i32),
+            torch.zeros(1, **i32), epoch, status, local, local, local, local,
+            [done.data_ptr() + 4 * world * r for r in range(world)])
+
+
+def test_bounded_flag_wait_returns_status_instead_of_hanging():
+    """A flag that nothing sets: the wait gives up after its limit (2 s of
+    %globaltimer), records the timeout code and returns, leaving the context
+    usable; a flag that is set passes at once with status 0."""
+    import time
+    C = ops.native()
+    i32 = dict(dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, **i32)
+    done = torch.zeros(16, **i32)
+    epoch = torch.ones(1, **i32)
+    # world 1: ep_signal releases this rank's own entry, the wait sees it
+    C.ep_signal(*_ep_wait_args(1, epoch, done, status))
+    C.ep_wait_done(*_ep_wait_args(1, epoch, done, status))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0 and int(done[0].item()) == 1
+    # world 2: rank 1's entry is never released
+    t0 = time.monotonic()
+    C.ep_wait_done(*_ep_wait_args(2, epoch, done, status))
+    torch.cuda.synchronize()
+    waited = time.monotonic() - t0
+    assert int(status.item()) == 6, "kStatusTimeoutFlag"
+    assert 1.5 < waited < 20.0, waited
+    x = torch.randn(4, 1000, device=DEV)  # the context still runs kernels
+    assert torch.equal(ops.argmax(x).cpu().long(), x.argmax(dim=-1).cpu())

@@ -279,3 +279,90 @@ def test_dp_ranks_bind_and_balance():
         assert len(bm.used_block_ids) == sum(len(s.block_table) for s in owned)
     m = sch.metrics()
     assert m["kv_blocks_capacity"] == 16
+
+
+# ------------------------------------------------------------------- fuzzer
+def _check_invariants(sch, live, offloads, carried):
+    for r, bm in enumerate(sch.block_managers):
+        fresh, lru, used = set(bm._fresh), set(bm._lru), bm.used_block_ids
+        assert not fresh & lru and not (fresh | lru) & used
+        assert fresh | lru | used == set(range(len(bm.blocks)))
+        refs = [0] * len(bm.blocks)
+        for s in live:
+            if max(s.dp_rank, 0) != r or not s.block_table:
+                continue
+            assert len(set(s.block_table)) == len(s.block_table), "a block twice in one table"
+            assert len(s.block_table) * BS >= s.num_cached_tokens + s.num_scheduled_tokens
+            for b in s.block_table:
+                refs[b] += 1
+        for b, blk in enumerate(bm.blocks):
+            assert blk.ref_count == refs[b], (b, blk.ref_count, refs[b])
+            assert (refs[b] > 0) == (b in used)
+            if refs[b] == 0:
+                carried[r].discard(b)
+            elif refs[b] > 1 and b not in carried[r]:
+                assert blk.hash != -1, "only hashed full blocks are shared"
+        for h, b in bm.hash_to_block_id.items():
+            assert bm.blocks[b].hash == h
+        if offloads:
+            ex = offloads[r]
+            assert len(ex.in_use) == len(bm._host_map)
+            assert not set(bm._host_map) & set(bm.hash_to_block_id)
+
+
+@pytest.mark.parametrize("policy", ["fcfs", "stall_free", "stall_free_lpm"])
+@pytest.mark.parametrize("lru,offload,dp", [(True, False, 1), (False, False, 1), (True, True, 1), (True, False, 2)])
+def test_scheduler_block_manager_fuzz(policy, lru, offload, dp, monkeypatch):
+    """Random arrivals sharing prefixes, chunked prefills, preemption under a
+    small pool, cancels, prefix-cache clears and EOS finishes; the block pool
+    invariants (tiers partition the ids, reference counts equal table
+    occurrences, only hashed blocks are shared, offload slots match the host
+    map) hold after every step, and every block is free at the end."""
+    monkeypatch.setenv("B200MOE_LRU_EVICT", "1" if lru else "0")
+    rng = random.Random(hash((policy, lru, offload, dp)) & 0xFFFF)
+    sch = Scheduler(cfg(scheduler_policy=policy, num_kvcache_blocks=24, max_num_batched_tokens=64,
+                        prefill_chunk_size=32, max_num_seqs=6, eos=3, dp_size=dp), dp_size=dp)
+    offloads = []
+    if offload:
+        for bm in sch.block_managers:
+            offloads.append(FakeOffload(6))
+            bm.set_offload_executor(offloads[-1])
+    prefixes = [[rng.randrange(5, 50) for _ in range(rng.choice([16, 32, 48]))] for _ in range(4)]
+    pending = []
+    for _ in range(60):
+        n = rng.randrange(1, 100)
+        base = rng.choice(prefixes) if rng.random() < 0.6 else []
+        toks = (base + [rng.randrange(5, 50) for _ in range(n)])[:120]
+        pending.append(Sequence(toks, SamplingParams(max_tokens=rng.randrange(1, 24), ignore_eos=rng.random() < 0.5,
+                                                     priority=rng.randrange(4), temperature=0.0)))
+    all_seqs = list(pending)
+    carried = [set() for _ in range(dp)]
+    steps = 0
+    while pending or not sch.is_finished():
+        steps += 1
+        assert steps < 5000, "scheduler made no progress"
+        for _ in range(rng.randrange(0, 3)):
+            if pending:
+                sch.add(pending.pop())
+        if rng.random() < 0.05:
+            live = list(sch.waiting) + list(sch.running)
+            if live:
+                assert sch.cancel(rng.choice(live).seq_id)
+        if rng.random() < 0.01:
+            # blocks held across a clear keep their sharers but lose their hash
+            for r, bm in enumerate(sch.block_managers):
+                carried[r] |= set(bm.used_block_ids)
+            sch.clear_prefix_cache()
+        batch = sch.schedule()
+        live = list(sch.waiting) + list(sch.running)
+        _check_invariants(sch, live, offloads, carried)
+        if batch.sequences:
+            toks = [rng.choice([3, 7, 11, 13]) for _ in batch.sequences]
+            sch.postprocess(batch.sequences, toks, batch.mode, None, batch.query_lens, batch.prefill_flags)
+        live = list(sch.waiting) + list(sch.running)
+        _check_invariants(sch, live, offloads, carried)
+    for bm in sch.block_managers:
+        assert not bm.used_block_ids and bm.num_free_blocks == len(bm.blocks)
+    assert all(s.finish_reason in ("length", "stop", "cancelled") for s in all_seqs)
+    assert {s.finish_reason for s in all_seqs} >= {"length", "stop"}
+    assert sum(bm.prefix_cache_hit_tokens for bm in sch.block_managers) > 0
