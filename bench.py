@@ -31,7 +31,7 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_TOKS = None  # BASELINE.md has no published number for this config/hardware
+BASELINE_TOKS = None  # the reference publishes no number for this config on this hardware
 
 
 def parse():

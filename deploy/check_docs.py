@@ -2,7 +2,8 @@
 
     python deploy/check_docs.py [--root DIR] [FILES...]
 
-Checks, in README.md, DESIGN.md and docs/**/*.md (or the files given):
+Checks, in the product documents (the root-level readme and design notes, and
+docs/**/*.md; or the files given):
   1. relative links ``[text](path)`` point at files that exist;
   2. image targets ``![..](path)`` exist;
   3. code spans (inline and fenced) that name a repository file
