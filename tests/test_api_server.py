@@ -184,3 +184,48 @@ def test_real_async_engine_cpu_stream():
         assert c.post("/v1/completions", json={"prompt": [1] * 300, "max_tokens": 4}).status_code == 400
     finally:
         asyncio.run(eng.close())
+
+
+def test_client_disconnect_cancels_stream():
+    """A streaming client that goes away: the request is cancelled in the
+    engine (its KV blocks freed) instead of decoding to max_tokens
+    (reference: nanovllm/entrypoints/api_server.py:224-226)."""
+
+    class Endless(FakeEngine):
+        async def add_request(self, prompt, sp):
+            self._id += 1
+            return RequestHandle(self._id, None)
+
+        async def next_event(self, h):
+            await asyncio.sleep(0.002)
+            return TokenEvent(token_id=104, finished=False)
+
+    eng = Endless()
+    app = create_app(eng, "tiny")
+    body = json.dumps({"model": "tiny", "prompt": "hi", "max_tokens": 100000, "stream": True}).encode()
+    sent = []
+
+    async def run():
+        calls = {"n": 0}
+
+        async def receive():
+            calls["n"] += 1
+            if calls["n"] == 1:
+                return {"type": "http.request", "body": body, "more_body": False}
+            await asyncio.sleep(0.05)  # the client reads a few chunks, then disconnects
+            return {"type": "http.disconnect"}
+
+        async def send(msg):
+            sent.append(msg)
+
+        scope = {"type": "http", "asgi": {"version": "3.0"}, "http_version": "1.1", "method": "POST",
+                 "scheme": "http", "path": "/v1/completions", "raw_path": b"/v1/completions", "query_string": b"",
+                 "headers": [(b"content-type", b"application/json"), (b"host", b"test")],
+                 "client": ("127.0.0.1", 1), "server": ("127.0.0.1", 80), "root_path": ""}
+        await asyncio.wait_for(app(scope, receive, send), 10)
+
+    asyncio.run(run())
+    assert eng.cancelled == [1]
+    chunks = [m for m in sent if m["type"] == "http.response.body" and m.get("body")]
+    assert 0 < len(chunks) < 1000
+    assert not any(b"[DONE]" in m["body"] for m in chunks)
