@@ -21,6 +21,10 @@ Behaviour follows the reference's offline driver (scripts/p2_benchmark.py:34-448
   ``hot`` (kept).  Prompts share ``--shared-prefix-len`` tokens.
 * **Probe phase** (``--probe-batches``): the same in one model load with a
   long shared prefix, to measure prefix-cache hits.
+* ``--workload offline|longctx|235b`` presets the headline family's shapes
+  (256 x 1024 -> 256 on Qwen3-30B-A3B; 8 x 32768 -> 512 with 256-token
+  blocks, with ``--kv-cache-dtype int8`` and ``--kv-offload`` variants;
+  Qwen3-235B-A22B 128 x 2048 -> 256); explicit flags override the preset.
 * Every record streams to a JSONL file as it completes; the JSON payload
   (schema 2: records, per-point summary with median / CV, verification,
   provenance, environment) is written at the end.
@@ -50,6 +54,18 @@ VERIFY_PROMPTS = [
     "请用 Python 写一个快速排序，附注释。",
 ]
 CACHE_MODES = ("none", "cold", "hot")
+# named workloads of the headline benchmark family; explicit flags override them
+WORKLOADS = {
+    # 8 concurrent 32k-token prompts, 512 decode tokens, 256-token KV blocks (bf16 or
+    # --kv-cache-dtype int8; --kv-offload with --num-kvcache-blocks below the demand
+    # exercises host offload once HBM blocks run out)
+    "longctx": dict(model="qwen3-30b-a3b", batches="8", prompt_len=32768, output_len=512, kvcache_block_size=256,
+                    max_num_batched_tokens=32768),
+    # Qwen3-235B-A22B: 128 concurrent 2048-token prompts, 256 output tokens
+    "235b": dict(model="qwen3-235b-a22b", batches="128", prompt_len=2048, output_len=256, kvcache_block_size=256),
+    # the offline headline: 256 x 1024 -> 256 on Qwen3-30B-A3B
+    "offline": dict(model="qwen3-30b-a3b", batches="256", prompt_len=1024, output_len=256, kvcache_block_size=256),
+}
 
 
 def make_prompts(batch: int, prompt_len: int, vocab_size: int, seed: int, shared_prefix_len: int = 0):
@@ -159,6 +175,17 @@ def parse_args(argv=None):
     p.add_argument("--probe-cache-modes", default="cold,hot")
     p.add_argument("--device", default=None)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                   help="preset model / batch / lengths of a named workload")
+    p.add_argument("--kv-cache-dtype", choices=("bf16", "int8"), default="bf16")
+    p.add_argument("--kv-offload", action="store_true", help="host KV offload of evicted prefix blocks")
+    p.add_argument("--kv-offload-host-blocks", type=int, default=256)
+    p.add_argument("--num-kvcache-blocks", type=int, default=-1, help="-1: size the pool from free memory")
+    p.add_argument("--attention-parallel", choices=("dp", "tp"), default="dp")
+    p.add_argument("--prefill-chunk-size", type=int, default=0)
+    pre, _ = p.parse_known_args(argv)
+    if pre.workload:
+        p.set_defaults(**WORKLOADS[pre.workload])
     args = p.parse_args(argv)
     args.cache_modes = _csv(args.cache_modes)
     args.probe_cache_modes = _csv(args.probe_cache_modes)
@@ -175,6 +202,31 @@ def parse_args(argv=None):
     return args
 
 
+def engine_kwargs(args) -> dict:
+    """``LLM(**kw)`` for the parsed options."""
+    batches = [int(x) for x in _csv(args.batches)]
+    probe_batches = [int(x) for x in _csv(args.probe_batches)]
+    max_len = max(args.prompt_len, args.probe_prompt_len if probe_batches else 0) + args.output_len + 16
+    kw = dict(tensor_parallel_size=args.tensor_parallel_size, enforce_eager=args.enforce_eager,
+              moe_backend=_csv(args.moe_backends)[0], attention_backend=_csv(args.attention_backends)[0],
+              expert_placement=args.expert_placement, expert_map_path=args.expert_map_path,
+              scheduler_policy=args.scheduler_policy, max_model_len=max(max_len, 256),
+              max_num_seqs=max(batches + probe_batches + [len(VERIFY_PROMPTS)]),
+              max_num_batched_tokens=args.max_num_batched_tokens, kvcache_block_size=args.kvcache_block_size,
+              seed=args.seed, kv_cache_dtype=args.kv_cache_dtype, attention_parallel=args.attention_parallel)
+    if args.kv_offload:
+        kw.update(kv_offload_enabled=True, kv_offload_host_blocks=args.kv_offload_host_blocks)
+    if args.num_kvcache_blocks > 0:
+        kw["num_kvcache_blocks"] = args.num_kvcache_blocks
+    if args.prefill_chunk_size > 0:
+        kw["prefill_chunk_size"] = args.prefill_chunk_size
+    if args.random_init:
+        kw["random_init"] = "seeded"
+    if args.device:
+        kw["device"] = args.device
+    return kw
+
+
 def main(argv=None):
     args = parse_args(argv)
     from b200moe import LLM, SamplingParams
@@ -187,17 +239,7 @@ def main(argv=None):
     if any(g not in (None, "eager", "graphs") for g in graph_modes):
         raise SystemExit("--graph-modes takes eager and/or graphs")
     graph_mem: dict[str, int] = {}
-    max_len = max(args.prompt_len, args.probe_prompt_len if probe_batches else 0) + args.output_len + 16
-    kw = dict(tensor_parallel_size=args.tensor_parallel_size, enforce_eager=args.enforce_eager,
-              moe_backend=backends[0], attention_backend=attn_backends[0], expert_placement=args.expert_placement,
-              expert_map_path=args.expert_map_path, scheduler_policy=args.scheduler_policy,
-              max_model_len=max(max_len, 256), max_num_seqs=max(batches + probe_batches + [len(VERIFY_PROMPTS)]),
-              max_num_batched_tokens=args.max_num_batched_tokens, kvcache_block_size=args.kvcache_block_size,
-              seed=args.seed)
-    if args.random_init:
-        kw["random_init"] = "seeded"
-    if args.device:
-        kw["device"] = args.device
+    kw = engine_kwargs(args)
     llm = LLM(args.model, **kw)
     vocab = llm.config.hf_config.vocab_size
     params = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)

@@ -142,3 +142,23 @@ def test_svg_charts(tmp_path):
         assert root.tag.endswith("svg")
         assert "sha256" in open(f).read()
     assert open(files[0]).read().count("<polyline") == 2
+
+
+def test_offline_driver_workload_presets():
+    """Named workloads fill in the model and shapes; explicit flags win; the
+    KV options reach the engine's keyword arguments."""
+    from b200moe.bench_offline import engine_kwargs, parse_args
+    a = parse_args(["--workload", "longctx", "--kv-offload", "--num-kvcache-blocks", "600", "--random-init",
+                    "--skip-verification"])
+    assert (a.model, a.batches, a.prompt_len, a.output_len, a.kvcache_block_size) == \
+        ("qwen3-30b-a3b", "8", 32768, 512, 256)
+    kw = engine_kwargs(a)
+    assert kw["kv_cache_dtype"] == "bf16" and kw["kv_offload_enabled"] and kw["num_kvcache_blocks"] == 600
+    assert kw["max_model_len"] == 32768 + 512 + 16 and kw["max_num_seqs"] == 8
+    assert engine_kwargs(parse_args(["--workload", "longctx", "--kv-cache-dtype", "int8"]))["kv_cache_dtype"] == "int8"
+    b = parse_args(["--workload", "235b", "--batches", "4", "--output-len", "32"])
+    assert (b.model, b.batches, b.prompt_len, b.output_len) == ("qwen3-235b-a22b", "4", 2048, 32)
+    kw = engine_kwargs(b)
+    assert "kv_offload_enabled" not in kw and kw["kv_cache_dtype"] == "bf16" and kw["attention_parallel"] == "dp"
+    c = parse_args([])
+    assert c.model == "qwen3-30b-a3b" and c.prompt_len == 128
