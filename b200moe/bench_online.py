@@ -15,8 +15,18 @@ output schema version 3):
   3:4:3 short / medium / long mix.  ``--prompt-tokens`` calibrates word counts
   to a token target with ``--tokenizer``; ``--prompt-seed-per-repeat`` keeps
   repeats cold.
-* **Per request** (streamed ``/v1/chat/completions`` with usage and server
-  metrics): TTFT, ITLs, TPOT, e2e, token counts, ``[DONE]`` seen, HTTP status,
+* **Token-id prompts.** ``--prompt-dist lognormal`` sends random token ids
+  (below ``--prompt-vocab``) to ``/v1/completions`` with lognormal lengths
+  (``--prompt-median``, ``--prompt-sigma``, clipped to ``--prompt-min`` /
+  ``--prompt-max``); ``--output-len-range LO,HI`` draws each request's
+  ``max_tokens`` uniformly (with ``ignore_eos``); ``--temperature`` / ``--top-p``
+  set the sampling; ``--max-concurrency`` caps in-flight Poisson requests
+  (a request waits for a slot and is timed from when it is sent).
+  ``--workload online`` presets all of these to the headline online shape:
+  lognormal median 1500 in [128, 8192], outputs 64..512, T 0.7, top-p 0.9,
+  at most 64 in flight.
+* **Per request** (streamed ``/v1/chat/completions``, or ``/v1/completions``
+  for token-id prompts, with usage and server metrics): TTFT, ITLs, TPOT, e2e, token counts, ``[DONE]`` seen, HTTP status,
   timeout, error bucket.
 * **Per point**: throughput, goodput (requests and tokens), standard / strict
   SLO rates with Wilson intervals, admission counts (429s), latency
@@ -41,6 +51,13 @@ from b200moe.benchmarking import (classify_error, coefficient_of_variation, conf
                                   error_bucket_counts, percentile, request_tpot, token_goodput, wilson_ci)
 
 SCHEMA_VERSION = 3
+# named workloads; explicit flags override them
+WORKLOADS = {
+    # Poisson arrivals, at most 64 in flight; lognormal prompts of random token ids
+    # (median 1500, clipped to [128, 8192]); outputs uniform in [64, 512]; T 0.7, top-p 0.9
+    "online": dict(mode="poisson", prompt_dist="lognormal", prompt_median=1500.0, prompt_min=128, prompt_max=8192,
+                   output_len_range=(64, 512), temperature=0.7, top_p=0.9, max_concurrency=64),
+}
 METRIC_PREFIX = "b200moe_"
 PROMPT_SEED_STRIDE = 1_000_003
 
@@ -177,17 +194,71 @@ def arrival_offsets(count: int, qps: float, pattern: str, seed: int) -> list[flo
 
 
 # ------------------------------------------------------------------ requests
+class RequestShape:
+    """Endpoint, sampling fields and per-request output length of a run."""
+
+    def __init__(self, args=None):
+        self.temperature = getattr(args, "temperature", 0.0)
+        self.top_p = getattr(args, "top_p", 1.0)
+        self.token_prompts = getattr(args, "prompt_dist", "words") == "lognormal"
+        self.out_range = getattr(args, "output_len_range", None)
+        self.seed = getattr(args, "seed", 0)
+        self.semaphore = None
+        if getattr(args, "max_concurrency", 0):
+            self.semaphore = asyncio.Semaphore(args.max_concurrency)
+
+    def max_tokens(self, default: int, request_id: int) -> int:
+        if not self.out_range:
+            return default
+        lo, hi = self.out_range
+        return random.Random(self.seed * 7919 + request_id).randint(lo, hi)
+
+    def body(self, model, prompt, max_tokens, include_metrics) -> dict:
+        b = {"model": model, "temperature": self.temperature, "max_tokens": max_tokens, "stream": True,
+             "stream_options": {"include_usage": True, "include_metrics": include_metrics}}
+        if self.top_p < 1.0:
+            b["top_p"] = self.top_p
+        if self.out_range:
+            b["ignore_eos"] = True  # the drawn length is the output length
+        if self.token_prompts:
+            b["prompt"] = prompt
+        else:
+            b["messages"] = [{"role": "user", "content": prompt}]
+        return b
+
+
+def lognormal_prompt(seed: int, request_id: int, median: float, sigma: float, lo: int, hi: int,
+                     vocab: int) -> list[int]:
+    """Random token ids; length lognormal(ln median, sigma) clipped to [lo, hi]."""
+    import math
+    rng = random.Random(seed * PROMPT_SEED_STRIDE + request_id)
+    n = int(round(rng.lognormvariate(math.log(median), sigma)))
+    n = max(lo, min(hi, n))
+    return [rng.randrange(vocab) for _ in range(n)]
+
+
 async def one_request(client, url, model, prompt, max_tokens, request_id, due, tracker, tokenizer=None,
-                      request_timeout_s=None, include_metrics=True) -> dict:
+                      request_timeout_s=None, include_metrics=True, shape: RequestShape | None = None) -> dict:
+    shape = shape or RequestShape()
     await asyncio.sleep(max(0.0, due - time.perf_counter()))
+    if shape.semaphore is not None:
+        await shape.semaphore.acquire()
+    try:
+        return await _one_request(client, url, model, prompt, shape.max_tokens(max_tokens, request_id), request_id,
+                                  due, tracker, tokenizer, request_timeout_s, include_metrics, shape)
+    finally:
+        if shape.semaphore is not None:
+            shape.semaphore.release()
+
+
+async def _one_request(client, url, model, prompt, max_tokens, request_id, due, tracker, tokenizer,
+                       request_timeout_s, include_metrics, shape) -> dict:
     start = time.perf_counter()
     tracker.enter()
     st = {"first": None, "done": False, "usage": None, "finish": None, "server": None, "text": "", "status": None}
     times: list[float] = []
     error, timed_out = None, False
-    body = {"model": model, "messages": [{"role": "user", "content": prompt}], "temperature": 0,
-            "max_tokens": max_tokens, "stream": True,
-            "stream_options": {"include_usage": True, "include_metrics": include_metrics}}
+    body = shape.body(model, prompt, max_tokens, include_metrics)
 
     async def consume():
         async with client.stream("POST", url, json=body, timeout=None) as resp:
@@ -206,7 +277,8 @@ async def one_request(client, url, model, prompt, max_tokens, request_id, due, t
                 if not choices:
                     continue
                 st["finish"] = choices[0].get("finish_reason") or st["finish"]
-                content = (choices[0].get("delta") or {}).get("content")
+                content = (choices[0].get("delta") or {}).get("content") if "delta" in choices[0] \
+                    else choices[0].get("text")
                 if content:
                     now = time.perf_counter()
                     st["text"] += content
@@ -230,7 +302,8 @@ async def one_request(client, url, model, prompt, max_tokens, request_id, due, t
         end = time.perf_counter()
         tracker.exit()
     usage = st["usage"]
-    prompt_tokens = usage.get("prompt_tokens") if usage else token_count(tokenizer, prompt)
+    prompt_tokens = usage.get("prompt_tokens") if usage else (
+        len(prompt) if isinstance(prompt, list) else token_count(tokenizer, prompt))
     output_tokens = usage.get("completion_tokens") if usage else token_count(tokenizer, st["text"])
     if error is None and not st["done"]:
         error = "stream ended before [DONE]"
@@ -253,7 +326,8 @@ async def one_request(client, url, model, prompt, max_tokens, request_id, due, t
 
 
 def _url(args) -> str:
-    return f"{args.base_url.rstrip('/')}/v1/chat/completions"
+    route = "completions" if getattr(args, "prompt_dist", "words") == "lognormal" else "chat/completions"
+    return f"{args.base_url.rstrip('/')}/v1/{route}"
 
 
 async def warmup(client, args, prompt_for, tokenizer, point_index):
@@ -262,7 +336,8 @@ async def warmup(client, args, prompt_for, tokenizer, point_index):
     tr, t0 = ConcurrencyTracker(), time.perf_counter() + 0.05
     rows = await asyncio.gather(*[
         one_request(client, _url(args), args.model, prompt_for(-1 - point_index * args.warmup_requests - i),
-                    args.max_tokens, -i - 1, t0 + i * 0.05, tr, tokenizer, args.request_timeout_s)
+                    args.max_tokens, -i - 1, t0 + i * 0.05, tr, tokenizer, args.request_timeout_s,
+                    shape=args.shape)
         for i in range(args.warmup_requests)])
     bad = [r for r in rows if not r["ok"]]
     if bad:
@@ -278,7 +353,8 @@ async def run_point_poisson(client, args, fraction, point_index, repeat, prompt_
     tr = ConcurrencyTracker()
     rows = await asyncio.gather(*[
         one_request(client, _url(args), args.model, prompt_for(point_index * args.requests + i), args.max_tokens, i,
-                    t0 + offs[i], tr, tokenizer, args.request_timeout_s) for i in range(args.requests)])
+                    t0 + offs[i], tr, tokenizer, args.request_timeout_s, shape=args.shape)
+        for i in range(args.requests)])
     after = await scrape_metrics(client, args.base_url)
     for r in rows:
         r.update({"load_fraction": fraction, "target_qps": qps, "repeat": repeat})
@@ -298,7 +374,7 @@ async def run_point_concurrency(client, args, concurrency, point_index, repeat, 
             if i >= args.requests or (deadline is not None and time.perf_counter() > deadline):
                 return
             r = await one_request(client, _url(args), args.model, prompt_for(point_index * args.requests + i),
-                                  args.max_tokens, i, t0, tr, tokenizer, args.request_timeout_s)
+                                  args.max_tokens, i, t0, tr, tokenizer, args.request_timeout_s, shape=args.shape)
             r.update({"concurrency": concurrency, "repeat": repeat})
             rows.append(r)
 
@@ -405,6 +481,7 @@ def aggregate(summaries: list[dict], key_fields: tuple) -> list[dict]:
 async def async_main(args) -> dict:
     import httpx
 
+    args.shape = RequestShape(args)  # its semaphore belongs to this event loop
     sampler = GpuSampler(args.gpu_sample_interval_s, enabled=not args.no_gpu_sample)
     sampler.start()
     tokenizer = None
@@ -434,6 +511,9 @@ async def async_main(args) -> dict:
                 seed = repeat_prompt_seed(args.seed, repeat, args.prompt_seed_per_repeat)
 
                 def prompt_for(rid, seed=seed):
+                    if args.prompt_dist == "lognormal":
+                        return lognormal_prompt(seed, rid, args.prompt_median, args.prompt_sigma, args.prompt_min,
+                                                args.prompt_max, args.prompt_vocab)
                     if args.prompt_mode == "mixed":
                         return build_prompt(args.prompt_word, words[mixed_bucket(abs(rid))], "unique", seed, rid)
                     return build_prompt(args.prompt_word, words["fixed"], args.prompt_mode, seed, rid)
@@ -499,7 +579,28 @@ def parse_args(argv=None):
     p.add_argument("--gpu-sample-interval-s", type=float, default=2.0)
     p.add_argument("--no-gpu-sample", action="store_true")
     p.add_argument("--output", default="online_benchmark.json")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                   help="preset prompt / output / sampling / concurrency of a named workload")
+    p.add_argument("--prompt-dist", choices=("words", "lognormal"), default="words")
+    p.add_argument("--prompt-median", type=float, default=1500.0)
+    p.add_argument("--prompt-sigma", type=float, default=0.6)
+    p.add_argument("--prompt-min", type=int, default=128)
+    p.add_argument("--prompt-max", type=int, default=8192)
+    p.add_argument("--prompt-vocab", type=int, default=32000, help="token ids are drawn below this")
+    p.add_argument("--output-len-range", type=lambda v: tuple(int(x) for x in v.split(",")), default=None,
+                   help="LO,HI: per-request max_tokens uniform in [LO, HI], with ignore_eos")
+    p.add_argument("--temperature", type=float, default=0.0)
+    p.add_argument("--top-p", type=float, default=1.0)
+    p.add_argument("--max-concurrency", type=int, default=0, help="cap on in-flight Poisson requests (0: none)")
+    pre, _ = p.parse_known_args(argv)
+    if pre.workload:
+        p.set_defaults(**WORKLOADS[pre.workload])
     args = p.parse_args(argv)
+    if args.output_len_range is not None and (len(args.output_len_range) != 2
+                                              or not 0 < args.output_len_range[0] <= args.output_len_range[1]):
+        p.error("--output-len-range takes LO,HI with 0 < LO <= HI")
+    if not 0 < args.prompt_min <= args.prompt_max:
+        p.error("--prompt-min / --prompt-max must satisfy 0 < min <= max")
     if not (args.max_qps > 0 and args.requests > 0 and args.warmup_requests >= 0 and args.repeats >= 1):
         p.error("max-qps, requests, repeats must be positive; warmup-requests >= 0")
     if not all(f > 0 for f in args.fractions):

@@ -6,7 +6,8 @@ streaming.  Request fields: max_tokens, temperature, top_p, top_k, min_p,
 presence/frequency/repetition penalties, stop (strings, with retraction of the
 matched text), stop_token_ids, logprobs (chat: bool + top_logprobs;
 completions: int), response_format json_schema / guided_json / guided_regex,
-priority, stream, stream_options.include_usage / include_metrics.
+priority, ignore_eos (decode to max_tokens), stream,
+stream_options.include_usage / include_metrics.
 Errors: 400 invalid request, 401 bad API key, 429 queue full / KV capacity,
 500 engine error.  A client disconnect cancels the request.
 
@@ -64,7 +65,8 @@ def parse_sampling(body: dict, chat: bool) -> tuple[SamplingParams, list[str], d
               presence_penalty=num("presence_penalty", float, 0.0),
               frequency_penalty=num("frequency_penalty", float, 0.0),
               repetition_penalty=num("repetition_penalty", float, 1.0),
-              skip_special_tokens=bool(body.get("skip_special_tokens", True)))
+              skip_special_tokens=bool(body.get("skip_special_tokens", True)),
+              ignore_eos=bool(body.get("ignore_eos", False)))
     if body.get("seed") is not None:
         kw["seed"] = num("seed", int, 0)
     stop_ids = body.get("stop_token_ids")

@@ -69,3 +69,22 @@ def test_unreachable_server_buckets_errors(tmp_path):
     s = p["points"][0]
     assert s["success_rate"] == 0.0 and s["error_buckets"]["stream"] == 6
     assert s["admission_counts"]["unknown"] == 6
+
+
+def test_online_workload_token_prompts(server, tmp_path):
+    """The online workload's shape at tiny scale: lognormal token-id prompts to
+    /v1/completions, per-request output lengths decoded in full (ignore_eos),
+    sampling at T 0.7 / top-p 0.9, and a cap on in-flight Poisson requests."""
+    p = bench_online.main(_args(server, tmp_path / "o.json", "--workload", "online", "--max-qps", "50",
+                                "--fractions", "1", "--prompt-median", "40", "--prompt-min", "16",
+                                "--prompt-max", "64", "--prompt-vocab", "1000", "--output-len-range", "2,6",
+                                "--max-concurrency", "2"))
+    s = p["points"][0]
+    assert s["success_rate"] == 1.0 and s["max_concurrency"] <= 2
+    shape = bench_online.RequestShape(bench_online.parse_args(_args(server, "x", "--workload", "online",
+                                                                    "--output-len-range", "2,6")))
+    for r in p["records"]:
+        assert 16 <= r["prompt_tokens"] <= 64
+        assert r["output_tokens"] == shape.max_tokens(5, r["request_id"])  # ignore_eos: the drawn length
+    lens = {r["prompt_tokens"] for r in p["records"]}
+    assert len(lens) > 1
