@@ -291,3 +291,36 @@ def test_per_step_jsonl_trace(tmp_path):
     assert recs[-1]["mode"] == "decode" and recs[-1]["decode_tokens"] == 2
     assert sum(r["prefill_tokens"] for r in recs) == 34 and sum(r["decode_tokens"] for r in recs) == 4
     assert all(r["forward_s"] >= 0 and r["schedule_s"] >= 0 for r in recs)
+
+
+def test_overlap_toggled_mid_run_drains_and_matches():
+    """Overlap switched off and on again while requests are in flight (on ->
+    off -> on): the parked and launched steps drain without losing or
+    repeating a token, and the outputs equal a run without overlap."""
+    import random as _r
+    rng = _r.Random(5)
+    prompts = [[rng.randrange(1, 400) for _ in range(rng.randrange(5, 50))] for _ in range(6)]
+    sps = [SamplingParams(temperature=0.0, max_tokens=rng.randrange(4, 30), ignore_eos=True) for _ in prompts]
+    base = dict(kvcache_block_size=16, max_num_seqs=8, max_num_batched_tokens=256, max_model_len=256,
+                num_kvcache_blocks=128, device="cpu", enforce_eager=True)
+    plain = LLM("tiny-moe-fp8", scheduler_overlap=False, **base)
+    want = [o["token_ids"] for o in plain.generate(prompts, sps, use_tqdm=False)]
+    plain.exit()
+    eng = LLM("tiny-moe-fp8", scheduler_overlap=True, **base)
+    try:
+        ids = [eng.add_request(p, sp) for p, sp in zip(prompts, sps)]
+        got, steps = {}, 0
+        while not eng.is_finished():
+            steps += 1
+            assert steps < 500
+            if steps == 4:
+                eng.set_scheduler_overlap(False)
+            if steps == 9:
+                eng.set_scheduler_overlap(True)
+            out, _ = eng.step()
+            for sid, toks, _m in out:
+                assert sid not in got, "a request finished twice"
+                got[sid] = toks
+        assert [got[i] for i in ids] == want
+    finally:
+        eng.exit()
