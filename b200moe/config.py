@@ -185,6 +185,9 @@ class Config:
     random_init: str = ""
     seed: int = 0
     cuda_graph_max_bs: int = 512
+    # bound on a worker rank's reply and on every collective (the process-group
+    # timeout, which also bounds the ranks' start-up rendezvous: keep it above a
+    # cold start's import time)
     rank_timeout_s: float = 120.0
 
     def __post_init__(self):
