@@ -21,6 +21,7 @@ import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.path.join(ROOT, "baseline", "_ref")
+COMPLETE = ".checkpoint_complete"
 
 ARCH = {
     "qwen3-30b-a3b": dict(hidden_size=2048, num_hidden_layers=48, num_attention_heads=32, num_key_value_heads=4,
@@ -92,6 +93,8 @@ def write_checkpoint(path: str, arch: dict, seed: int = 0, device: str = "cuda")
             put(d, q + "up_proj", rnd(I, H))
             put(d, q + "down_proj", rnd(H, I))
         save_file(d, os.path.join(path, f"model-layer{l:03d}.safetensors"))
+    with open(os.path.join(path, COMPLETE), "w") as f:  # written last: a partial checkpoint is rewritten
+        f.write("ok\n")
 
 
 def _write_tokenizer(path: str, vocab_size: int):
@@ -122,7 +125,7 @@ def run(args, prompts_for, metric: str) -> int:
     import torch
     ckpt = os.environ.get("B200MOE_REF_CKPT", os.path.join("/tmp", f"ref_ckpt_{args.model}"))
     t0 = time.perf_counter()
-    if not os.path.exists(os.path.join(ckpt, "config.json")):
+    if not os.path.exists(os.path.join(ckpt, COMPLETE)):
         write_checkpoint(ckpt, ARCH[args.model], seed=args.seed)
     write_s = time.perf_counter() - t0
     sys.path.insert(0, REF)
