@@ -378,6 +378,17 @@ def build_parser() -> argparse.ArgumentParser:
                    help="random weights of the checkpoint's architecture (no weight files needed)")
     p.add_argument("--metrics-path", default=_env("METRICS_PATH"))
     p.add_argument("--device", default=_env("DEVICE", "cuda"), choices=["cuda", "cpu"])
+    p.add_argument("--attention-backend", default=_env("ATTENTION_BACKEND", "paged"))
+    p.add_argument("--decode-moe-backend", default=_env("DECODE_MOE_BACKEND"))
+    p.add_argument("--expert-placement", default=_env("EXPERT_PLACEMENT", "linear"),
+                   choices=["linear", "round_robin", "profiled"])
+    p.add_argument("--expert-map-path", default=_env("EXPERT_MAP_PATH"))
+    p.add_argument("--allow-insecure", action="store_true", default=_env("ALLOW_INSECURE", "0") == "1",
+                   help="allow a non-loopback bind without an API key (trusted networks only)")
+    p.add_argument("--log-level", default=_env("LOG_LEVEL", "info"),
+                   choices=["critical", "error", "warning", "info", "debug", "trace"])
+    from b200moe import __version__
+    p.add_argument("--version", action="version", version=f"%(prog)s {__version__}")
     return p
 
 
@@ -390,7 +401,9 @@ def engine_kwargs(a) -> dict:
                 prefill_chunk_size=a.prefill_chunk_size, scheduler_overlap=a.scheduler_overlap,
                 kv_offload_enabled=a.kv_offload, kv_offload_host_blocks=a.kv_offload_host_blocks,
                 enforce_eager=a.enforce_eager, max_queue_size=a.max_queue_size, metrics_path=a.metrics_path,
-                random_init="seeded" if a.random_init else "", device=a.device)
+                random_init="seeded" if a.random_init else "", device=a.device,
+                attention_backend=a.attention_backend, decode_moe_backend=a.decode_moe_backend or None,
+                expert_placement=a.expert_placement, expert_map_path=a.expert_map_path or None)
 
 
 def is_loopback(host: str) -> bool:
@@ -401,13 +414,13 @@ def main(argv=None):
     a = build_parser().parse_args(argv)
     if not a.model:
         raise SystemExit("--model (or B200MOE_MODEL) is required")
-    if not is_loopback(a.host) and not a.api_key:
-        raise SystemExit(f"refusing to bind {a.host} without --api-key")
+    if not is_loopback(a.host) and not a.api_key and not a.allow_insecure:
+        raise SystemExit(f"refusing to bind {a.host} without --api-key (or --allow-insecure on a trusted network)")
     import uvicorn
     from b200moe.async_engine import AsyncLLMEngine
     engine = AsyncLLMEngine(a.model, **engine_kwargs(a))
     app = create_app(engine, a.served_model_name or os.path.basename(a.model.rstrip("/")), a.api_key)
-    uvicorn.run(app, host=a.host, port=a.port, log_level="info")
+    uvicorn.run(app, host=a.host, port=a.port, log_level=a.log_level)
 
 
 if __name__ == "__main__":

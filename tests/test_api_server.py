@@ -229,3 +229,28 @@ def test_client_disconnect_cancels_stream():
     chunks = [m for m in sent if m["type"] == "http.response.body" and m.get("body")]
     assert 0 < len(chunks) < 1000
     assert not any(b"[DONE]" in m["body"] for m in chunks)
+
+
+def test_cli_reference_flags(monkeypatch, capsys):
+    """The reference server's remaining flags: backends and expert placement
+    reach the engine, --allow-insecure permits a non-loopback bind without a
+    key, --log-level reaches uvicorn, --version prints the version."""
+    import uvicorn
+
+    import b200moe
+    import b200moe.async_engine as ae
+    from b200moe.entrypoints.openai.api_server import engine_kwargs
+    a = build_parser().parse_args(["--attention-backend", "triton_paged", "--decode-moe-backend", "grouped_mm",
+                                   "--expert-placement", "round_robin", "--expert-map-path", "/x.json"])
+    kw = engine_kwargs(a)
+    assert (kw["attention_backend"], kw["decode_moe_backend"], kw["expert_placement"], kw["expert_map_path"]) == \
+        ("triton_paged", "grouped_mm", "round_robin", "/x.json")
+    assert engine_kwargs(build_parser().parse_args([]))["decode_moe_backend"] is None
+    seen = {}
+    monkeypatch.setattr(ae, "AsyncLLMEngine", lambda model, **kw: seen.update(kw=kw) or FakeEngine())
+    monkeypatch.setattr(uvicorn, "run", lambda app, **kw: seen.update(run=kw))
+    main(["--model", "tiny-moe", "--host", "0.0.0.0", "--allow-insecure", "--log-level", "warning"])
+    assert seen["run"]["host"] == "0.0.0.0" and seen["run"]["log_level"] == "warning"
+    with pytest.raises(SystemExit):
+        build_parser().parse_args(["--version"])
+    assert b200moe.__version__ in capsys.readouterr().out
