@@ -118,6 +118,7 @@ class Executor:
             status, payload = self._recv(r, c, timeout=max(600.0, config.rank_timeout_s))
             if status != "ready":
                 raise RankFailure(f"rank {r} failed to start:\n{payload}")
+        self.runner._executor = self  # runner.call(...) reaches every rank
         self.max_blocks = self.runner.max_blocks
         self._inflight: collections.deque = collections.deque()  # (plans, rows) of launched steps
         # per worker, replies that arrived while another kind was awaited

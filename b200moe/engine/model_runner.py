@@ -518,6 +518,36 @@ class ModelRunner:
             self.profiler.stop()
         self.model.profiler = self.profiler if enabled else None
 
+    def start_profiling(self):
+        self.set_profiling(True)
+
+    def stop_profiling(self):
+        self.set_profiling(False)
+
+    # ------------------------------------------- reference-compatible reports
+    def call(self, method: str, *args):
+        """Run ``method`` on every rank, returning this rank's result (the
+        reference's ``model_runner.call``); without worker ranks, only here."""
+        ex = getattr(self, "_executor", None)
+        return ex.call(method, *args) if ex is not None else getattr(self, method)(*args)
+
+    def memory_report(self) -> dict:
+        gib = 2 ** 30
+        cuda = self.device.type == "cuda"
+        get = (lambda fn: fn(self.device) / gib) if cuda else (lambda fn: None)
+        return {"rank": self.rank, "allocated_gib": get(torch.cuda.memory_allocated),
+                "reserved_gib": get(torch.cuda.memory_reserved), "peak_gib": get(torch.cuda.max_memory_allocated)}
+
+    def graph_report(self) -> dict:
+        return {"rank": self.rank, "enabled": bool(self.graphs), "buckets": sorted(self.graphs),
+                "kernels_per_replay": dict(self._graph_kernels), "memory": self.memory_report()}
+
+    def set_enforce_eager(self, enabled: bool):
+        self.set_cuda_graphs(not enabled)
+
+    def warmup_model(self):
+        self.warmup()
+
     def profile_snapshot(self, reset: bool = True) -> dict:
         """This rank's per-range and per-layer p50 / p95 (one device sync)."""
         out = self.profiler.snapshot(reset)

@@ -117,10 +117,12 @@ def test_gloo_world2_profile_snapshot_and_init_trace(monkeypatch, capfd):
         assert {"device", "process_group", "model", "weights", "kv_cache", "total"} <= set(stages)
         out = capfd.readouterr().out
         assert "[init] rank 0 weights" in out and "[init] rank 1 ready" in out
-        llm.start_profiling()
+        llm.model_runner.call("start_profiling")  # the reference's spelling reaches every rank
         llm.generate(_prompts(4), SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True), use_tqdm=False)
         snap = llm.profile_snapshot()
         llm.stop_profiling()
+        assert llm.model_runner.call("memory_report")["rank"] == 0
+        assert [r["rank"] for r in llm.executor.call_all("graph_report")] == [0, 1]
     finally:
         llm.exit()
     assert [s["rank"] for s in snap["ranks"]] == [0, 1]
