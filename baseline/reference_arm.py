@@ -63,12 +63,14 @@ def write_checkpoint(path: str, arch: dict, seed: int = 0, device: str = "cuda")
         return torch.randn(*shape, generator=g, device=device) * 0.02
 
     def fp8(w):
-        n, k = w.shape
-        b = w.reshape(n // 128, 128, k // 128, 128)
-        amax = b.abs().amax(dim=(1, 3), keepdim=True).clamp_min(1e-12)
+        """[..., n, k] fp32 -> (e4m3 [..., n, k], fp32 scale_inv [..., n/128, k/128]) on the host,
+        one device->host copy for the whole stack."""
+        *lead, n, k = w.shape
+        b = w.reshape(*lead, n // 128, 128, k // 128, 128)
+        amax = b.abs().amax(dim=(-3, -1), keepdim=True).clamp_min(1e-12)
         s = amax / 448.0
-        q = (b / s).clamp(-448, 448).to(torch.float8_e4m3fn).reshape(n, k)
-        return q.cpu(), s.reshape(n // 128, k // 128).float().cpu()
+        q = (b / s).clamp(-448, 448).to(torch.float8_e4m3fn).reshape(*lead, n, k)
+        return q.cpu(), s.reshape(*lead, n // 128, k // 128).float().cpu()
 
     def put(d, name, w):
         q, s = fp8(w)
@@ -87,11 +89,14 @@ def write_checkpoint(path: str, arch: dict, seed: int = 0, device: str = "cuda")
         put(d, p + "self_attn.k_proj", rnd(nkv * D, H))
         put(d, p + "self_attn.v_proj", rnd(nkv * D, H))
         put(d, p + "self_attn.o_proj", rnd(H, nq * D))
-        for e in range(E):
-            q = f"{p}mlp.experts.{e}."
-            put(d, q + "gate_proj", rnd(I, H))
-            put(d, q + "up_proj", rnd(I, H))
-            put(d, q + "down_proj", rnd(H, I))
+        # all experts of a projection are drawn and quantised as one stack; safetensors
+        # refuses tensors that share storage, so each expert's slice is cloned on the host
+        for proj, shape in (("gate_proj", (I, H)), ("up_proj", (I, H)), ("down_proj", (H, I))):
+            q, s = fp8(rnd(E, *shape))
+            for e in range(E):
+                name = f"{p}mlp.experts.{e}.{proj}"
+                d[name + ".weight"] = q[e].clone()
+                d[name + ".weight_scale_inv"] = s[e].clone()
         save_file(d, os.path.join(path, f"model-layer{l:03d}.safetensors"))
     with open(os.path.join(path, COMPLETE), "w") as f:  # written last: a partial checkpoint is rewritten
         f.write("ok\n")
@@ -108,6 +113,61 @@ def _write_tokenizer(path: str, vocab_size: int):
                    "pad_token": "<151643>", "unk_token": "<0>", "model_max_length": 40960}, f)
 
 
+CKPT_BYTES = {"qwen3-30b-a3b": 33 << 30, "qwen3-30b-a3b-4l": 4 << 30}
+
+
+def checkpoint_dir(model: str) -> str:
+    """Where the random checkpoint goes: ``B200MOE_REF_CKPT`` if set, else the first of the
+    system temp dir and the repository's ``_refckpt`` that has room for it (~31 GiB for
+    the 30B model; a finished checkpoint is reused)."""
+    import shutil
+    import tempfile
+    if os.environ.get("B200MOE_REF_CKPT"):
+        return os.environ["B200MOE_REF_CKPT"]
+    need = CKPT_BYTES.get(model, 40 << 30)
+    for base in (tempfile.gettempdir(), os.path.join(ROOT, "_refckpt")):
+        path = os.path.join(base, f"ref_ckpt_{model}")
+        if os.path.exists(os.path.join(path, COMPLETE)):
+            return path
+        os.makedirs(base, exist_ok=True)
+        if shutil.disk_usage(base).free >= need:
+            return path
+    return os.path.join(tempfile.gettempdir(), f"ref_ckpt_{model}")
+
+
+class _Clocks:
+    """``nvidia-smi`` SM clock and throttle-reason samples every 200 ms while the timed passes run."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, n_gpus: int):
+        import subprocess
+        import tempfile
+        self.log = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ",".join(str(i) for i in range(n_gpus)), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.log, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"samples": 0}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.log.seek(0)
+        rows = [[c.strip() for c in line.split(",")] for line in self.log if line.count(",") == 5]
+        os.unlink(self.log.name)
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        mhz = sorted(float(r[0]) for r in rows if r[0].replace(".", "").isdigit())
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None,
+                "sm_max_mhz": float(rows[0][1]) if rows and rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": [n for i, n in enumerate(names) if any(r[2 + i] == "Active" for r in rows)],
+                "samples": len(rows)}
+
+
 def unavailable(why: str) -> int:
     print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
     return 0
@@ -121,9 +181,9 @@ def run(args, prompts_for, metric: str) -> int:
     if args.model not in ARCH:
         return unavailable(f"no reference-format checkpoint writer for {args.model}")
     if not os.path.isdir(os.path.join(REF, "nanovllm")):
-        return unavailable("reference not installed in baseline/_ref")
+        return unavailable(f"reference not installed: no package at {os.path.join(REF, 'nanovllm')}")
     import torch
-    ckpt = os.environ.get("B200MOE_REF_CKPT", os.path.join("/tmp", f"ref_ckpt_{args.model}"))
+    ckpt = checkpoint_dir(args.model)
     t0 = time.perf_counter()
     if not os.path.exists(os.path.join(ckpt, COMPLETE)):
         write_checkpoint(ckpt, ARCH[args.model], seed=args.seed)
@@ -135,22 +195,27 @@ def run(args, prompts_for, metric: str) -> int:
     for var in ("TORCHELASTIC_USE_AGENT_STORE", "TORCHELASTIC_RESTART_COUNT"):
         os.environ.pop(var, None)
     from nanovllm import LLM, SamplingParams  # the reference package
+    eager = os.environ.get("B200MOE_REF_EAGER", "1") != "0"
     t0 = time.perf_counter()
     llm = LLM(ckpt, tensor_parallel_size=args.gpus, max_num_seqs=max(args.num_requests, 1),
               max_num_batched_tokens=args.max_num_batched_tokens,
               max_model_len=args.input_len + args.output_len + 16, kvcache_block_size=256,
               moe_backend="grouped_mm", attention_backend="triton_paged", scheduler_policy=args.scheduler_policy,
-              # eager: the reference's production setting (its deploy/serve.env.example and
-              # scripts/p2_benchmark.py run enforce_eager); its CUDA-graph capture raises
-              # cudaErrorStreamCaptureUnsupported on this platform
-              enforce_eager=True)
+              # eager by default: the reference's production setting (its deploy/serve.env.example
+              # and scripts/p2_benchmark.py run enforce_eager); B200MOE_REF_EAGER=0 tries its
+              # CUDA-graph decode instead
+              enforce_eager=eager)
     init_s = time.perf_counter() - t0
     sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)
+    warm_s = []
     for i in range(args.warmup):
+        tw = time.perf_counter()
         llm.generate(prompts_for(i), sp, use_tqdm=False)
+        warm_s.append(round(time.perf_counter() - tw, 2))
     timed = [prompts_for(args.warmup + i) for i in range(args.steps)]
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = _Clocks(args.gpus)
     a.record()
     t0 = time.perf_counter()
     total = 0
@@ -160,6 +225,7 @@ def run(args, prompts_for, metric: str) -> int:
     b.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    clocks = clk.stop()
     dev_s = a.elapsed_time(b) / 1e3
     ttft = sorted(o["metrics"]["ttft_s"] for o in outs if o["metrics"].get("ttft_s") is not None)
     tpot = sorted(o["metrics"]["tpot_s"] for o in outs if o["metrics"].get("tpot_s") is not None)
@@ -170,9 +236,13 @@ def run(args, prompts_for, metric: str) -> int:
             "data": "synthetic uniform-random token ids; random-init fp8 checkpoint written at run time",
             "config": {"model": args.model, "global_batch": args.num_requests, "seq_len": args.input_len,
                        "output_len": args.output_len, "parallelism": f"tp{args.gpus}/ep{args.gpus}",
-                       "moe_backend": "grouped_mm", "attention_backend": "triton_paged", "enforce_eager": True,
-                       "ckpt_write_s": round(write_s, 1), "init_s": round(init_s, 1)},
-            "e2e": {"value": round(total / wall, 1), "unit": "tok/s", "wall_s_per_pass": round(wall / args.steps, 2)}}
+                       "moe_backend": "grouped_mm", "attention_backend": "triton_paged", "enforce_eager": eager,
+                       "ckpt_dir": ckpt, "ckpt_write_s": round(write_s, 1), "init_s": round(init_s, 1),
+                       "warmup_pass_s": warm_s,
+                       "timing": "CUDA events on rank 0's stream around the K passes; rank 0 waits on every "
+                                 "collective, so this is the slowest rank's time"},
+            "e2e": {"value": round(total / wall, 1), "unit": "tok/s", "wall_s_per_pass": round(wall / args.steps, 2)},
+            "clocks": clocks}
     if ttft:
         line["p50_ttft_s"] = round(ttft[len(ttft) // 2], 4)
     if tpot:
