@@ -33,9 +33,22 @@ extern "C" {
 
 // Returns 0 on success.  On failure returns a non-zero code and writes a
 // NUL-terminated message into err[0..err_len) (when err is not null):
-//   1  invalid argument (shape, head_dim, GQA group, split_len)
+//   1  invalid argument: a count below 1 (q / kv heads, num_splits, block_size,
+//      max_blocks, block_stride, split_len), q_heads not a multiple of kv_heads,
+//      a GQA group above 16 or not dividing 64, split_len not a multiple of 64,
+//      head_dim other than 64 / 128, int8 KV without scales, a null pointer
 //   2  size above B200MOE_NOALLOC_MAX_ROWS
 //   3  CUDA error (device query, symbol lookup or launch)
+// Nothing is launched when the code is non-zero.
+// Two preconditions live in device memory, so they cannot be checked here and
+// are the caller's to keep:
+//   * num_splits * split_len >= the longest seq_lens[b]: keys past that are not
+//     attended to (the split count is capped, not grown);
+//   * block_tables row b holds ceil(seq_lens[b] / block_size) <= max_blocks valid
+//     block ids: the kernel reads those entries without a bounds check.
+// The kernel is the cp.async split-KV decode kernel (bf16 or int8 KV), not the
+// TMA kernel the PyTorch binding uses for bf16 pools: the TMA kernel needs the
+// pool's block count, which this signature does not carry.
 // q [batch, num_q_heads, head_dim] bf16; k_cache / v_cache the layer base of
 // the paged pool [blocks, kv_heads, block_size, head_dim] (bf16, or int8 with
 // per-token-head fp32 scales k_scale / v_scale); block_tables [batch,

@@ -15,8 +15,11 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <mutex>
+#include <set>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <utility>
 
 namespace b200 {
@@ -49,6 +52,44 @@ inline void pdl_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   if (e != cudaSuccess) throw std::runtime_error(std::string("kernel launch: ") + cudaGetErrorString(e));
+}
+
+inline int current_device() {
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  return dev;
+}
+
+// Dynamic shared memory above 48 KB needs an opt-in per kernel AND per device: a
+// process that launches on several GPUs sets it once on each (thread-safe).
+template <typename... KArgs>
+inline void smem_opt_in(void (*kern)(KArgs...), int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;  // (kernel, device, bytes)
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done.insert({reinterpret_cast<const void*>(kern), dev, bytes}).second) return;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    done.erase({reinterpret_cast<const void*>(kern), dev, bytes});
+    throw std::runtime_error(std::string("cudaFuncSetAttribute(max dynamic smem): ") + cudaGetErrorString(e));
+  }
+}
+
+// SM count of the current device, queried once per device.
+inline int device_sm_count() {
+  constexpr int kMaxDev = 64;
+  static int count[kMaxDev] = {};
+  static std::mutex mu;
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDev) throw std::runtime_error("device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (count[dev] == 0) {
+    const cudaError_t e = cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("SM count: ") + cudaGetErrorString(e));
+  }
+  return count[dev];
 }
 
 }  // namespace b200

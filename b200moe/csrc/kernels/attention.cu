@@ -31,6 +31,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstdlib>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -1111,17 +1112,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct KvMapKey {
   const void* base;
-  int D, bs, kvh, nblocks;
+  int dev, D, bs, kvh, nblocks, sub_rows;
   int64_t block_stride;
   bool operator==(const KvMapKey& o) const {
-    return base == o.base && D == o.D && bs == o.bs && kvh == o.kvh && nblocks == o.nblocks &&
-           block_stride == o.block_stride;
+    return base == o.base && dev == o.dev && D == o.D && bs == o.bs && kvh == o.kvh && nblocks == o.nblocks &&
+           sub_rows == o.sub_rows && block_stride == o.block_stride;
   }
 };
 
-static const CUtensorMap& kv_tensor_map(const DecodeArgs& a, int sub_rows) {
+// Returned by value: the cache may be cleared by another thread's call.
+static CUtensorMap kv_tensor_map(const DecodeArgs& a, int sub_rows) {
+  static std::mutex mu;
   static std::vector<std::pair<KvMapKey, CUtensorMap>> cache;  // one entry per layer of a pool
-  const KvMapKey key{a.k_cache, a.head_dim, a.block_size, a.num_kv_heads, a.num_blocks, a.block_stride};
+  const KvMapKey key{a.k_cache, current_device(), a.head_dim, a.block_size, a.num_kv_heads, a.num_blocks,
+                     sub_rows, a.block_stride};
+  std::lock_guard<std::mutex> lock(mu);
   for (auto& e : cache)
     if (e.first == key) return e.second;
   CUtensorMap map;
@@ -1159,41 +1164,24 @@ static bool use_tma_decode(const DecodeArgs& a, int* sub_rows) {
   return true;
 }
 
-static int num_sms_attn() {
-  static int n = 0;
-  if (n == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
+static int num_sms_attn() { return device_sm_count(); }
 
 template <int D>
 static void launch_decode_tma(const DecodeArgs& a, int B, int sub_rows, cudaStream_t s) {
-  const CUtensorMap& map = kv_tensor_map(a, sub_rows);
+  const CUtensorMap map = kv_tensor_map(a, sub_rows);
   static const bool persist = [] {
     const char* e = std::getenv("B200MOE_DECODE_PERSIST");
     return e == nullptr || std::string(e) != "0";
   }();
   if (persist) {
-    static bool set_p = false;
-    if (!set_p) {
-      cudaFuncSetAttribute(decode_attn_persist_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           DecPersist<D>::SMEM);
-      set_p = true;
-    }
+    smem_opt_in(decode_attn_persist_kernel<D>, DecPersist<D>::SMEM);
     const int n_items = a.num_splits * a.num_kv_heads * B;
     const int grid = std::max(1, std::min(n_items, 2 * num_sms_attn()));
     pdl_launch(decode_attn_persist_kernel<D>, grid, 160, DecPersist<D>::SMEM, s, map, a, sub_rows, a.num_blocks, n_items);
     if (a.num_splits > 1) pdl_launch(decode_combine_kernel<D>, dim3(a.num_kv_heads * a.group, B), D, 0, s, a);
     return;
   }
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(decode_attn_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecTma<D>::SMEM);
-    set = true;
-  }
+  smem_opt_in(decode_attn_tma_kernel<D>, DecTma<D>::SMEM);
   dim3 grid(a.num_splits, a.num_kv_heads, B);
   pdl_launch(decode_attn_tma_kernel<D>, grid, 160, DecTma<D>::SMEM, s, map, a, sub_rows, a.num_blocks);
   if (a.num_splits > 1) pdl_launch(decode_combine_kernel<D>, dim3(a.num_kv_heads * a.group, B), D, 0, s, a);
@@ -1213,13 +1201,11 @@ void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
   if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("decode attention: int8 KV needs scales");
   dim3 grid(a.num_splits, a.num_kv_heads, B);
   if (a.head_dim == 128) {
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<128>()); set = true; }
+    smem_opt_in(decode_attn_kernel<128>, decode_smem<128>());
     pdl_launch(decode_attn_kernel<128>, grid, 128, decode_smem<128>(), s, a);
     if (a.num_splits > 1) pdl_launch(decode_combine_kernel<128>, dim3(a.num_kv_heads * a.group, B), 128, 0, s, a);
   } else if (a.head_dim == 64) {
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<64>()); set = true; }
+    smem_opt_in(decode_attn_kernel<64>, decode_smem<64>());
     pdl_launch(decode_attn_kernel<64>, grid, 128, decode_smem<64>(), s, a);
     if (a.num_splits > 1) pdl_launch(decode_combine_kernel<64>, dim3(a.num_kv_heads * a.group, B), 64, 0, s, a);
   } else {
@@ -1240,12 +1226,10 @@ void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t
   const int QPB = 64 / a.group;
   dim3 grid((max_q_len + QPB - 1) / QPB, a.num_kv_heads, B);
   if (a.head_dim == 128) {
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<128>()); set = true; }
+    smem_opt_in(prefill_attn_kernel<128>, prefill_smem<128>());
     pdl_launch(prefill_attn_kernel<128>, grid, 128, prefill_smem<128>(), s, a);
   } else if (a.head_dim == 64) {
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(prefill_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<64>()); set = true; }
+    smem_opt_in(prefill_attn_kernel<64>, prefill_smem<64>());
     pdl_launch(prefill_attn_kernel<64>, grid, 128, prefill_smem<64>(), s, a);
   } else {
     throw std::runtime_error("prefill attention: head_dim must be 64 or 128");
@@ -1258,8 +1242,10 @@ void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t
 // ====================================================== no-allocation entry
 // Split-KV decode attention whose partial results live in a file-scope device
 // array instead of a caller-provided workspace; the contract (limits, set-up,
-// races) is in include/noalloc.h.  It launches the same kernels as
-// paged_decode_attn and allocates no device memory.
+// races) is in include/noalloc.h.  It goes through paged_decode_attn with the
+// pool's block count left at 0, which selects the cp.async split kernel
+// (decode_attn_kernel) and its combine: the TMA kernels need the block count for
+// their tensor map.  It allocates no device memory.
 #include <cstdio>
 #include <mutex>
 #include "noalloc.h"
@@ -1312,10 +1298,22 @@ extern "C" int b200moe_decode_attn_noalloc(const void* q, const void* k_cache, c
                                            int num_q_heads, int num_kv_heads, int head_dim, float scale,
                                            int num_splits, int split_len, void* out, void* stream, char* err,
                                            int err_len) {
-  if (batch < 0 || num_splits < 1 || num_kv_heads < 1 || num_q_heads % num_kv_heads != 0 || block_size < 1)
-    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: bad batch / splits / head counts / block_size");
+  if (batch < 0 || num_splits < 1 || num_kv_heads < 1 || num_q_heads < 1 || num_q_heads % num_kv_heads != 0)
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: bad batch / splits / head counts");
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 16 || 64 % group != 0)
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: q_heads / kv_heads must divide 64 and be <= 16");
+  if (block_size < 1 || max_blocks < 1 || block_stride <= 0)
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: block_size, max_blocks and block_stride must be > 0");
+  if (split_len < 1 || split_len % 64 != 0)
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: split_len must be a positive multiple of 64");
   if (head_dim != 64 && head_dim != kNoAllocMaxD)
     return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: head_dim must be 64 or 128");
+  if (kv_int8 && (k_scale == nullptr || v_scale == nullptr))
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: int8 KV needs k_scale and v_scale");
+  if (batch > 0 && (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_tables == nullptr ||
+                    seq_lens == nullptr || out == nullptr))
+    return noalloc_fail(err, err_len, 1, "decode_attn_noalloc: null tensor pointer");
   const long long rows = (long long)batch * num_q_heads * num_splits;
   if (num_splits > 1 && rows > kNoAllocRows) {
     char msg[256];
@@ -1340,7 +1338,7 @@ extern "C" int b200moe_decode_attn_noalloc(const void* q, const void* k_cache, c
   a.block_size = block_size;
   a.block_stride = block_stride;
   a.num_kv_heads = num_kv_heads;
-  a.group = num_q_heads / num_kv_heads;
+  a.group = group;
   a.head_dim = head_dim;
   a.scale = scale;
   a.num_splits = num_splits;
@@ -1349,6 +1347,7 @@ extern "C" int b200moe_decode_attn_noalloc(const void* q, const void* k_cache, c
   a.part_m = scratch + (size_t)kNoAllocRows * kNoAllocMaxD;
   a.part_l = a.part_m + kNoAllocRows;
   a.out = out;
+  a.num_blocks = 0;  // no pool size: the cp.async kernel, not the TMA one
   try {
     b200::paged_decode_attn(a, batch, static_cast<cudaStream_t>(stream));
   } catch (const std::exception& ex) {

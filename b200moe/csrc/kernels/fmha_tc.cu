@@ -477,19 +477,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapKey {
   const void* base;
-  int bs, kvh, nblocks, rows;
+  int dev, bs, kvh, nblocks, rows;
   int64_t block_stride;
   bool operator==(const MapKey& o) const {
-    return base == o.base && bs == o.bs && kvh == o.kvh && nblocks == o.nblocks && rows == o.rows &&
-           block_stride == o.block_stride;
+    return base == o.base && dev == o.dev && bs == o.bs && kvh == o.kvh && nblocks == o.nblocks &&
+           rows == o.rows && block_stride == o.block_stride;
   }
 };
 
-const CUtensorMap& kv_map(const PrefillArgs& a, int sub_rows) {
+// Returned by value: another thread's call may clear the cache.
+CUtensorMap kv_map(const PrefillArgs& a, int sub_rows) {
   static std::mutex mu;
   static std::vector<std::pair<MapKey, CUtensorMap>> cache;  // one entry per layer of a pool
+  const MapKey key{a.k_cache, current_device(), a.block_size, a.num_kv_heads, a.num_blocks, sub_rows,
+                   a.block_stride};
   std::lock_guard<std::mutex> lock(mu);
-  const MapKey key{a.k_cache, a.block_size, a.num_kv_heads, a.num_blocks, sub_rows, a.block_stride};
   for (auto& e : cache)
     if (e.first == key) return e.second;
   CUtensorMap map;
@@ -550,27 +552,16 @@ static CUtensorMap q_map(const PrefillArgs& a) {
   return map;
 }
 
-static int num_sms_fmha() {
-  static int n = 0;
-  if (n == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
+static int num_sms_fmha() { return device_sm_count(); }
 
 void fmha_prefill(const PrefillArgs& a_in, int B, int max_q_len, int sub_rows, cudaStream_t s) {
   PrefillArgs a = a_in;
   a.batch = B;
   if (a.q_rows <= 0 || (reinterpret_cast<uintptr_t>(a.q) & 15))
     throw std::runtime_error("prefill attention: q rows / alignment");
-  const CUtensorMap& kvm = kv_map(a, sub_rows);
+  const CUtensorMap kvm = kv_map(a, sub_rows);
   const CUtensorMap qm = q_map(a);
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::SMEM);
-  });
+  smem_opt_in(fmha_prefill_kernel, Layout::SMEM);
   const int QPB = kRows / a.group;
   const int qtiles = (max_q_len + QPB - 1) / QPB;
   const int64_t n_items = (int64_t)a.num_kv_heads * B * qtiles;

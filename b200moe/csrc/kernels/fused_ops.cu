@@ -718,11 +718,7 @@ void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows,
                              "hidden % 64 == 0");
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     throw std::runtime_error("router_fused: operands must be 16-byte aligned");
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(router_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem);
-    attr = true;
-  }
+  smem_opt_in(router_fused_kernel, kRtSmem);
   const CUtensorMap xm = rt_map(x, T, H, kRtTok);
   const CUtensorMap wm = rt_map(w, kRtE, H, kRtE);
   pdl_launch(router_fused_kernel, (T + kRtTok - 1) / kRtTok, 256, kRtSmem, s, xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,

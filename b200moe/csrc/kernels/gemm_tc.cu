@@ -772,25 +772,13 @@ CUtensorMap make_tmap_2d(const void* base, bool is_bf16, int64_t rows, int64_t c
   return map;
 }
 
-static int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
+static int num_sms() { return device_sm_count(); }
 
 template <int BN, bool PAIR, bool AFP8, int EPI>
 static void launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   using C = GemmCfg<BN, PAIR, AFP8>;
   auto kern = gemm_tc_kernel<BN, PAIR, AFP8, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    attr_set = true;
-  }
+  smem_opt_in(kern, C::SMEM);
   // A: [groups * rows_per_group, K] row-major, box 64 x 128 rows; tile-major e4m3
   // weights are addressed as [groups * rows_per_group * K / 64, 64]
   const int64_t a_rows = (int64_t)L.args.num_groups * L.args.a_rows_per_group;

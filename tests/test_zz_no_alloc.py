@@ -91,3 +91,35 @@ def test_noalloc_rejects_oversize():
     assert out.abs().sum().item() == 0  # nothing was launched
     rc, msg = _call(lib, q, layer, tables, lens, D ** -0.5, out, 100, 2)
     assert rc == 1 and "split_len" in msg
+
+
+def test_noalloc_rejects_invalid_arguments():
+    """Every malformed shape returns code 1 before anything is launched (a zero head
+    count once reached an integer division on the host, a zero split length one on
+    the device)."""
+    lib = _lib()
+    D, nq, nkv, bs = 128, 32, 4, 16
+    layer, tables, lens, q = _setup([64, 64], nq, nkv, D, bs, False)
+    out = torch.zeros(2, nq, D, dtype=torch.bfloat16, device=DEV)
+    good = dict(nq=nq, nkv=nkv, max_blocks=tables.shape[1], block_size=bs, block_stride=layer.block_stride,
+                split_len=64, nsplit=2, head_dim=D)
+    bad = [dict(nq=0), dict(nkv=0), dict(nq=33), dict(nq=128, nkv=4), dict(nq=12, nkv=4), dict(split_len=0),
+           dict(split_len=-64), dict(max_blocks=0), dict(block_stride=0), dict(block_stride=-1), dict(block_size=0),
+           dict(nsplit=0), dict(head_dim=96)]
+    for case in bad:
+        a = {**good, **case}
+        err = ctypes.create_string_buffer(512)
+        rc = lib.b200moe_decode_attn_noalloc(
+            q.data_ptr(), layer.k.data_ptr(), layer.v.data_ptr(), None, None, 0, tables.data_ptr(), lens.data_ptr(),
+            2, a["max_blocks"], a["block_size"], a["block_stride"], a["nq"], a["nkv"], a["head_dim"], D ** -0.5,
+            a["nsplit"], a["split_len"], out.data_ptr(), torch.cuda.current_stream().cuda_stream, err, len(err))
+        assert rc == 1, (case, rc, err.value)
+        assert err.value, case
+    err = ctypes.create_string_buffer(512)
+    rc = lib.b200moe_decode_attn_noalloc(  # int8 KV without scales
+        q.data_ptr(), layer.k.data_ptr(), layer.v.data_ptr(), None, None, 1, tables.data_ptr(), lens.data_ptr(), 2,
+        good["max_blocks"], bs, good["block_stride"], nq, nkv, D, D ** -0.5, 2, 64, out.data_ptr(),
+        torch.cuda.current_stream().cuda_stream, err, len(err))
+    assert rc == 1 and b"scale" in err.value
+    torch.cuda.synchronize()
+    assert out.abs().sum().item() == 0  # nothing was launched
