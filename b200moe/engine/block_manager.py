@@ -169,7 +169,7 @@ class BlockManager:
         cached = 0
         new_blocks = seq.num_blocks
         for i in range(seq.num_blocks - 1):
-            toks = seq.block(i)
+            toks = seq.block_tokens(i)
             h = self.compute_hash(toks, h)
             bid = self.hash_to_block_id.get(h, -1)
             if bid != -1 and self.blocks[bid].token_ids == toks:
@@ -195,7 +195,7 @@ class BlockManager:
         self.prefix_cache_hit_tokens += num_cached_blocks * self.block_size
         h = -1
         for i in range(num_cached_blocks):
-            h = self.compute_hash(seq.block(i), h)
+            h = self.compute_hash(seq.block_tokens(i), h)
             if h not in self.hash_to_block_id:
                 seq.block_table.append(self._revive_from_host(h))
                 continue
@@ -210,7 +210,7 @@ class BlockManager:
             seq.block_table.append(bid)
         for _ in range(num_cached_blocks, seq.num_blocks):
             seq.block_table.append(self._allocate_block())
-        seq.num_cached_tokens = num_cached_blocks * self.block_size
+        seq.cached_len = num_cached_blocks * self.block_size
 
     def deallocate(self, seq: Sequence):
         for bid in reversed(seq.block_table):
@@ -218,7 +218,7 @@ class BlockManager:
             block.ref_count -= 1
             if block.ref_count == 0:
                 self._deallocate_block(bid)
-        seq.num_cached_tokens = 0
+        seq.cached_len = 0
         seq.block_table.clear()
 
     def can_append(self, seq: Sequence) -> bool:
@@ -247,15 +247,15 @@ class BlockManager:
 
     def hash_blocks(self, seq: Sequence, num_new_tokens: int | None = None):
         """Register hashes of blocks that became full during the last step."""
-        q = seq.num_scheduled_tokens if num_new_tokens is None else num_new_tokens
-        start = seq.num_cached_tokens // self.block_size
-        end = (seq.num_cached_tokens + q) // self.block_size
+        q = seq.chunk_len if num_new_tokens is None else num_new_tokens
+        start = seq.cached_len // self.block_size
+        end = (seq.cached_len + q) // self.block_size
         if start == end:
             return
         h = self.blocks[seq.block_table[start - 1]].hash if start > 0 else -1
         for i in range(start, end):
             block = self.blocks[seq.block_table[i]]
-            toks = seq.block(i)
+            toks = seq.block_tokens(i)
             h = self.compute_hash(toks, h)
             block.update(h, toks)
             if h in self._host_map:

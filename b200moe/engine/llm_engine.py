@@ -127,7 +127,7 @@ class LLMEngine:
         if lo < 0 or hi >= vocab:
             raise ValueError(f"prompt token id {hi if hi >= vocab else lo} outside vocab range [0, {vocab})")
         seq = Sequence(prompt, sampling_params)
-        if seq.guided_json is not None or seq.guided_regex is not None:
+        if seq.params.guided_json is not None or seq.params.guided_regex is not None:
             self._attach_grammar(seq)
         self.scheduler.add(seq)
         return seq.seq_id
@@ -142,15 +142,15 @@ class LLMEngine:
             info = xg.TokenizerInfo.from_huggingface(self.tokenizer, vocab_size=self.config.hf_config.vocab_size)
             self._grammar = (xg, info, xg.GrammarCompiler(info))
         xg, info, compiler = self._grammar
-        if seq.guided_json is not None:
-            schema = seq.guided_json if isinstance(seq.guided_json, str) else json.dumps(seq.guided_json, sort_keys=True)
+        if seq.params.guided_json is not None:
+            schema = seq.params.guided_json if isinstance(seq.params.guided_json, str) else json.dumps(seq.params.guided_json, sort_keys=True)
             key, build = ("json", schema), (lambda: compiler.compile_json_schema(schema))
         else:
-            key, build = ("regex", seq.guided_regex), (lambda: compiler.compile_regex(seq.guided_regex))
+            key, build = ("regex", seq.params.guided_regex), (lambda: compiler.compile_regex(seq.params.guided_regex))
         compiled = self._grammar_cache.get(key)
         if compiled is None:
             compiled = self._grammar_cache[key] = build()
-        seq.grammar_matcher = xg.GrammarMatcher(compiled)
+        seq.grammar = xg.GrammarMatcher(compiled)
 
     def cancel_request(self, seq_id: int) -> bool:
         return self.scheduler.cancel(seq_id)
@@ -159,8 +159,8 @@ class LLMEngine:
     def prefilled_sequences(self) -> list[Sequence]:
         """Running sequences whose prompt is computed and that hold their first
         generated token: ready to hand off to a decode engine."""
-        return [s for s in self.scheduler.running if not s.is_finished and not s.is_prefill
-                and s.num_completion_tokens >= 1]
+        return [s for s in self.scheduler.running if not s.is_finished and not s.in_prefill
+                and s.output_len >= 1]
 
     def detach(self, seq: Sequence):
         """Stop scheduling a handed-off sequence but keep its KV blocks (they
@@ -171,9 +171,7 @@ class LLMEngine:
         from b200moe.engine.sequence import SequenceStatus
         if seq.block_table:
             self.scheduler._bm(seq).deallocate(seq)
-        seq.status = SequenceStatus.FINISHED
-        seq.finish_reason = "handoff"
-        seq.finish_time = perf_counter()
+        seq.finish("handoff")
 
     def admit_prefilled(self, token_ids: list[int], num_prompt_tokens: int,
                         sampling_params: SamplingParams) -> Sequence | None:
@@ -182,14 +180,14 @@ class LLMEngine:
         while the pool lacks room (back-pressure); after the KV import, call
         ``activate``."""
         seq = Sequence(list(token_ids), sampling_params)
-        seq.num_prompt_tokens = num_prompt_tokens
+        seq.prompt_len = num_prompt_tokens
         bm = self.scheduler.block_manager
         if bm.num_free_blocks < seq.num_blocks:
             return None
         for _ in range(seq.num_blocks):
             seq.block_table.append(bm._allocate_block())
         seq.dp_rank = 0
-        seq.is_prefill = False
+        seq.in_prefill = False
         return seq
 
     def activate(self, seq: Sequence):
@@ -198,11 +196,11 @@ class LLMEngine:
         prefill's), with the chained hashes a local prefill would give."""
         from b200moe.engine.sequence import SequenceStatus
         bm = self.scheduler.block_manager
-        seq.num_cached_tokens = 0
+        seq.cached_len = 0
         bm.hash_blocks(seq, seq.num_tokens - 1)
-        seq.num_cached_tokens = seq.num_tokens - 1
+        seq.cached_len = seq.num_tokens - 1
         seq.status = SequenceStatus.RUNNING
-        seq.record_token(perf_counter())
+        seq.timing.stamp(perf_counter())
         self.scheduler.running.append(seq)
 
     def set_scheduler_overlap(self, enabled: bool):
@@ -236,15 +234,15 @@ class LLMEngine:
     # --------------------------------------------------------------- steps
     def _grammar_masks(self, batch: ScheduledBatch):
         """Allowed-token bitmask per guided row (batch row -> int32 words)."""
-        if not any(s.grammar_matcher is not None for s in batch.sequences):
+        if not any(s.grammar is not None for s in batch.sequences):
             return None
         import torch
         words = (self.config.hf_config.vocab_size + 31) // 32
         masks = {}
         for i, s in enumerate(batch.sequences):
-            if s.grammar_matcher is not None:
+            if s.grammar is not None:
                 buf = torch.zeros(1, words, dtype=torch.int32)
-                s.grammar_matcher.fill_next_token_bitmask(buf, 0)
+                s.grammar.fill_next_token_bitmask(buf, 0)
                 masks[i] = buf[0].numpy().copy()
         return masks
 
@@ -262,8 +260,8 @@ class LLMEngine:
             return False
         live = {id(s) for s in cur.sequences}
         for s in nxt.sequences:
-            if (id(s) not in live or s.temperature >= 1e-3 or s.has_penalty or s.logprobs
-                    or s.grammar_matcher is not None):
+            if (id(s) not in live or s.params.temperature >= 1e-3 or s.penalty is not None or s.params.logprobs
+                    or s.grammar is not None):
                 return False
         return True
 
@@ -336,27 +334,27 @@ class LLMEngine:
                 self.overlap_pruned_rows += 1
                 continue
             if was_prefill:
-                if not seq.is_prefill:
+                if not seq.in_prefill:
                     self.overlap_pruned_rows += 1
-                    seq.num_scheduled_tokens = 0
+                    seq.chunk_len = 0
                     continue
-                q = min(q, seq.num_tokens - seq.num_cached_tokens)
+                q = min(q, seq.num_tokens - seq.cached_len)
             if q <= 0:
                 self.overlap_pruned_rows += 1
-                seq.num_scheduled_tokens = 0
-                seq.is_prefill = False
+                seq.chunk_len = 0
+                seq.in_prefill = False
                 continue
-            seq.num_scheduled_tokens = q
-            seq.is_prefill = was_prefill
+            seq.chunk_len = q
+            seq.in_prefill = was_prefill
             kept.append(seq)
             flags.append(was_prefill)
         if not kept:
             return None
         has_dec, has_pre = (not all(flags)), any(flags)
         mode = "mixed" if (has_dec and has_pre) else ("decode" if has_dec else "prefill")
-        return ScheduledBatch(kept, [s.num_scheduled_tokens for s in kept],
-                              [s.num_cached_tokens + s.num_scheduled_tokens for s in kept],
-                              sum(s.num_scheduled_tokens for s in kept), mode, batch.schedule_s, flags)
+        return ScheduledBatch(kept, [s.chunk_len for s in kept],
+                              [s.cached_len + s.chunk_len for s in kept],
+                              sum(s.chunk_len for s in kept), mode, batch.schedule_s, flags)
 
     def _finish_step(self, batch: ScheduledBatch, token_ids, logprobs):
         seqs, mode = batch.sequences, batch.mode
@@ -381,7 +379,7 @@ class LLMEngine:
                    "context_lens": batch.context_lens, "schedule_s": batch.schedule_s, "forward_s": forward_s}
             with open(self.metrics_path, "a", encoding="utf-8") as f:
                 f.write(json.dumps(rec, separators=(",", ":")) + "\n")
-        outputs = [(s.seq_id, s.completion_token_ids, s.metrics()) for s in seqs
+        outputs = [(s.seq_id, s.output_ids(), s.metrics()) for s in seqs
                    if s.is_finished and id(s) not in done_before]
         return outputs, num_tokens
 

@@ -90,9 +90,7 @@ class Scheduler:
                 queue.remove(seq)
                 if seq.block_table:
                     self._bm(seq).deallocate(seq)
-                seq.status = SequenceStatus.FINISHED
-                seq.finish_time = perf_counter()
-                seq.finish_reason = "cancelled"
+                seq.finish("cancelled")
                 return True
         return False
 
@@ -110,12 +108,12 @@ class Scheduler:
             return ScheduledBatch([], [], [], 0, mode, perf_counter() - t0)
         return ScheduledBatch(
             sequences=seqs,
-            query_lens=[s.num_scheduled_tokens for s in seqs],
-            context_lens=[s.num_cached_tokens + s.num_scheduled_tokens for s in seqs],
-            num_scheduled_tokens=sum(s.num_scheduled_tokens for s in seqs),
+            query_lens=[s.chunk_len for s in seqs],
+            context_lens=[s.cached_len + s.chunk_len for s in seqs],
+            num_scheduled_tokens=sum(s.chunk_len for s in seqs),
             mode=mode,
             schedule_s=perf_counter() - t0,
-            prefill_flags=[s.is_prefill for s in seqs],
+            prefill_flags=[s.in_prefill for s in seqs],
         )
 
     def _speculative_precheck(self, inflight) -> tuple[bool, dict]:
@@ -176,8 +174,8 @@ class Scheduler:
                 if preempted_self:
                     continue
                 bm.may_append(seq)
-            seq.num_scheduled_tokens = 1
-            seq.is_prefill = False
+            seq.chunk_len = 1
+            seq.in_prefill = False
             scheduled.append(seq)
             counts[r] += 1
             if budgets is not None:
@@ -215,8 +213,7 @@ class Scheduler:
         counts = [0] * self.dp_size
         while self.waiting and sum(counts) < self.max_num_seqs * self.dp_size:
             seq = self.waiting[0]
-            if seq.first_scheduled_time is None:
-                seq.first_scheduled_time = perf_counter()
+            seq.timing.mark_scheduled(perf_counter())
             if not seq.block_table:
                 if max(budgets) == 0:
                     break
@@ -232,13 +229,13 @@ class Scheduler:
                 r = max(seq.dp_rank, 0)
                 if budgets[r] == 0 or counts[r] >= self.max_num_seqs:
                     break
-                num_tokens = seq.num_tokens - seq.num_cached_tokens
+                num_tokens = seq.num_tokens - seq.cached_len
                 if budgets[r] < num_tokens and counts[r] > 0:
                     break
-            seq.num_scheduled_tokens = min(num_tokens, budgets[r])
-            budgets[r] -= seq.num_scheduled_tokens
+            seq.chunk_len = min(num_tokens, budgets[r])
+            budgets[r] -= seq.chunk_len
             counts[r] += 1
-            if seq.num_cached_tokens + seq.num_scheduled_tokens == seq.num_tokens:
+            if seq.cached_len + seq.chunk_len == seq.num_tokens:
                 seq.status = SequenceStatus.RUNNING
                 self.waiting.popleft()
                 self.running.append(seq)
@@ -256,15 +253,15 @@ class Scheduler:
         prefix).  Sequences waiting ``starvation_steps`` passes outrank all."""
         starved = [s for s in self.waiting if s.wait_steps >= self.starvation_steps]
         if starved:
-            cand = max(starved, key=lambda s: (s.wait_steps, -s.priority))
+            cand = max(starved, key=lambda s: (s.wait_steps, -s.params.priority))
         else:
-            cand = min(self.waiting, key=lambda s: s.priority)
+            cand = min(self.waiting, key=lambda s: s.params.priority)
             if self.policy == "stall_free_lpm":
-                tier = [s for s in self.waiting if s.priority == cand.priority]
+                tier = [s for s in self.waiting if s.params.priority == cand.params.priority]
                 if len(tier) > 1:
                     def cached_blocks(s):
                         if s.block_table:
-                            return s.num_cached_tokens // self.block_size
+                            return s.cached_len // self.block_size
                         return max(bm.can_allocate(s, touch=touch) for bm in self.block_managers)
                     cand = max(tier, key=cached_blocks)
         self.waiting.remove(cand)
@@ -278,12 +275,12 @@ class Scheduler:
         for i, s in enumerate(self.running):
             if rank is not None and max(s.dp_rank, 0) != rank:
                 continue
-            if idx is None or s.priority >= self.running[idx].priority:
+            if idx is None or s.params.priority >= self.running[idx].params.priority:
                 idx = i
         if idx is None:
             return None
         victim = self.running[idx]
-        if requester is not None and victim.priority < requester.priority:
+        if requester is not None and victim.params.priority < requester.params.priority:
             return None
         del self.running[idx]
         return victim
@@ -310,8 +307,7 @@ class Scheduler:
             if max(budgets) == 0 or all(c >= self.max_num_seqs for c in counts):
                 break
             seq = self._waiting_candidate()
-            if seq.first_scheduled_time is None:
-                seq.first_scheduled_time = perf_counter()
+            seq.timing.mark_scheduled(perf_counter())
             if not seq.block_table:
                 probe = self._probe_rank(seq, budgets, counts)
                 if probe is None:
@@ -323,13 +319,13 @@ class Scheduler:
             if budgets[r] == 0 or counts[r] >= self.max_num_seqs:
                 skipped.append(seq)
                 continue
-            remaining = seq.num_tokens - seq.num_cached_tokens
-            seq.num_scheduled_tokens = min(remaining, budgets[r], self.prefill_chunk_size)
+            remaining = seq.num_tokens - seq.cached_len
+            seq.chunk_len = min(remaining, budgets[r], self.prefill_chunk_size)
             seq.wait_steps = 0
-            budgets[r] -= seq.num_scheduled_tokens
+            budgets[r] -= seq.chunk_len
             counts[r] += 1
             prefill.append(seq)
-            if seq.num_cached_tokens + seq.num_scheduled_tokens == seq.num_tokens:
+            if seq.cached_len + seq.chunk_len == seq.num_tokens:
                 seq.status = SequenceStatus.RUNNING
                 self.running.append(seq)
             else:
@@ -348,7 +344,7 @@ class Scheduler:
     def preempt(self, seq: Sequence):
         self.preemptions += 1
         seq.status = SequenceStatus.WAITING
-        seq.is_prefill = True
+        seq.in_prefill = True
         self._bm(seq).deallocate(seq)
         if self.dp_size > 1:
             seq.dp_rank = -1
@@ -389,38 +385,36 @@ class Scheduler:
         metadata (``query_lens`` / ``prefill_flags``).  Returns token events
         ``(seq_id, token, finished, metrics|None, logprobs|None)``."""
         if query_lens is None:
-            query_lens = [s.num_scheduled_tokens for s in seqs]
+            query_lens = [s.chunk_len for s in seqs]
         if prefill_flags is None:
-            prefill_flags = [s.is_prefill for s in seqs]
+            prefill_flags = [s.in_prefill for s in seqs]
         events = []
         for row, (seq, tok) in enumerate(zip(seqs, token_ids)):
             if seq.is_finished:
                 continue
             q = query_lens[row]
             was_prefill = prefill_flags[row]
-            seq.is_prefill = was_prefill
+            seq.in_prefill = was_prefill
             bm = self._bm(seq)
             bm.hash_blocks(seq, q)
-            seq.num_cached_tokens += q
-            seq.num_scheduled_tokens = 0
-            if was_prefill and seq.num_cached_tokens < seq.num_tokens:
+            seq.cached_len += q
+            seq.chunk_len = 0
+            if was_prefill and seq.cached_len < seq.num_tokens:
                 continue
-            seq.append_token(tok)
+            seq.append(tok)
             if was_prefill:
-                seq.is_prefill = False
+                seq.in_prefill = False
             now = perf_counter()
-            seq.record_token(now)
-            hit_eos = not seq.ignore_eos and tok == self.eos
-            hit_stop = tok in seq.stop_token_ids
+            seq.timing.stamp(now)
+            hit_eos = not seq.params.ignore_eos and tok == self.eos
+            hit_stop = seq.params.stop_token_ids is not None and tok in seq.params.stop_token_ids
             hit_grammar = False
-            if seq.grammar_matcher is not None:
-                seq.grammar_matcher.accept_token(tok)
-                hit_grammar = seq.grammar_matcher.is_terminated()
-            hit_len = seq.num_completion_tokens == seq.max_tokens
+            if seq.grammar is not None:
+                seq.grammar.accept_token(tok)
+                hit_grammar = seq.grammar.is_terminated()
+            hit_len = seq.output_len == seq.params.max_tokens
             if hit_eos or hit_stop or hit_grammar or hit_len:
-                seq.status = SequenceStatus.FINISHED
-                seq.finish_time = now
-                seq.finish_reason = "stop" if (hit_eos or hit_stop or hit_grammar) else "length"
+                seq.finish("stop" if (hit_eos or hit_stop or hit_grammar) else "length", now)
                 bm.deallocate(seq)
                 self._remove_from_queues(seq)
             elif was_prefill and seq in self.waiting:

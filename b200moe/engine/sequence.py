@@ -1,150 +1,172 @@
-"""Per-request state (reference: nanovllm/engine/sequence.py:16-173).
+"""The driver's record of one request.
 
-Holds token ids, the KV block table, cached/scheduled token counts, sampling
-knobs, penalty counters and request timing.  ``metrics()`` returns the same
-keys as the reference so benchmark readers carry over.  Worker ranks never see
-a ``Sequence``: the driver ships them a flat step plan instead.
+Worker ranks never see this object: the driver packs what a step needs into a
+flat plan (``engine/step_plan.py``).  So the record is organised around its
+three readers on the driver:
+
+* the scheduler and block manager: token ids, the KV block table and the
+  prefill cursor (``cached_len`` tokens already in KV, ``chunk_len`` tokens in
+  the step being launched);
+* the plan packer: the request's :class:`SamplingParams` (held as given, not
+  copied field by field) and, only when a penalty is set, a
+  :class:`PenaltyCounts`;
+* metrics: a :class:`RequestTiming`, whose ``report`` produces the per-request
+  dict the reference's benchmark readers expect (keys of
+  nanovllm/engine/sequence.py ``metrics``).
 """
 from __future__ import annotations
 
-from collections import Counter
-from enum import Enum, auto
-from itertools import count
+import enum
+import itertools
+from dataclasses import dataclass, field
 from time import perf_counter
 
 from b200moe.sampling_params import SamplingParams
 
 
-class SequenceStatus(Enum):
-    WAITING = auto()
-    RUNNING = auto()
-    FINISHED = auto()
+class SequenceStatus(enum.IntEnum):
+    WAITING = 0
+    RUNNING = 1
+    FINISHED = 2
+
+
+@dataclass(slots=True)
+class RequestTiming:
+    """Host timestamps of one request (``perf_counter`` seconds)."""
+    arrival: float = field(default_factory=perf_counter)
+    scheduled: float | None = None   # first time a step included it
+    finished: float | None = None
+    stamps: list[float] = field(default_factory=list)  # one per output token
+
+    def stamp(self, t: float):
+        self.stamps.append(t)
+
+    def mark_scheduled(self, t: float):
+        if self.scheduled is None:
+            self.scheduled = t
+
+    def report(self, prompt_tokens: int, output_tokens: int, finish_reason: str | None) -> dict:
+        first = self.stamps[0] if self.stamps else None
+        end = self.finished if self.finished is not None else (self.stamps[-1] if self.stamps else None)
+        since = lambda t: None if t is None else t - self.arrival
+        ttft, e2e = since(first), since(end)
+        per_token = None
+        if ttft is not None and e2e is not None and output_tokens > 1:
+            per_token = (e2e - ttft) / (output_tokens - 1)
+        intervals = [b - a for a, b in itertools.pairwise(self.stamps)]
+        return {"prompt_tokens": prompt_tokens, "output_tokens": output_tokens, "queue_s": since(self.scheduled),
+                "ttft_s": ttft, "e2e_s": e2e, "tpot_s": per_token, "mean_tpot_s": per_token,
+                "itls_s": intervals, "token_intervals_s": intervals, "finish_reason": finish_reason}
+
+
+class PenaltyCounts:
+    """Token occurrence counts for presence / frequency / repetition penalties.
+
+    ``generated`` counts output tokens (presence and frequency penalties).  The
+    repetition penalty also looks at the prompt; that table is built on first
+    use from the prompt as it stands then, so a prefilled hand-over that moves
+    the prompt boundary before any step is still counted right."""
+    __slots__ = ("generated", "_seen")
+
+    def __init__(self):
+        self.generated: dict[int, int] = {}
+        self._seen: dict[int, int] | None = None
+
+    def add(self, token: int):
+        self.generated[token] = self.generated.get(token, 0) + 1
+        if self._seen is not None:
+            self._seen[token] = self._seen.get(token, 0) + 1
+
+    def seen(self, prompt) -> dict[int, int]:
+        if self._seen is None:
+            table: dict[int, int] = {}
+            for t in prompt:
+                table[t] = table.get(t, 0) + 1
+            for t, c in self.generated.items():
+                table[t] = table.get(t, 0) + c
+            self._seen = table
+        return self._seen
+
+
+def _wants_penalty(sp: SamplingParams) -> bool:
+    return sp.presence_penalty != 0.0 or sp.frequency_penalty != 0.0 or sp.repetition_penalty != 1.0
 
 
 class Sequence:
-    block_size = 256
-    counter = count()
+    """One request: tokens, KV blocks, prefill cursor, sampling and timing."""
+
+    block_size = 256           # KV block size; the engine sets it from its config
+    _ids = itertools.count()
+
+    __slots__ = ("seq_id", "status", "tokens", "prompt_len", "cached_len", "chunk_len", "in_prefill",
+                 "block_table", "params", "penalty", "grammar", "timing", "wait_steps", "finish_reason",
+                 "dp_rank")
 
     def __init__(self, token_ids: list[int], sampling_params: SamplingParams | None = None):
-        sp = sampling_params or SamplingParams()
-        self.seq_id = next(Sequence.counter)
+        self.seq_id = next(Sequence._ids)
         self.status = SequenceStatus.WAITING
-        self.token_ids = list(token_ids)
-        self.last_token = self.token_ids[-1]
-        self.num_tokens = len(self.token_ids)
-        self.num_prompt_tokens = len(self.token_ids)
-        self.num_cached_tokens = 0
-        self.num_scheduled_tokens = 0
-        self.is_prefill = True
+        self.tokens = list(token_ids)
+        self.prompt_len = len(self.tokens)
+        self.cached_len = 0          # tokens whose KV is in the pool
+        self.chunk_len = 0           # tokens the current step computes
+        self.in_prefill = True
         self.block_table: list[int] = []
-        self.temperature = sp.temperature
-        self.max_tokens = sp.max_tokens
-        self.ignore_eos = sp.ignore_eos
-        self.priority = sp.priority
-        self.top_p = sp.top_p
-        self.top_k = sp.top_k
-        self.min_p = sp.min_p
-        self.presence_penalty = sp.presence_penalty
-        self.frequency_penalty = sp.frequency_penalty
-        self.repetition_penalty = sp.repetition_penalty
-        self.logprobs = sp.logprobs or 0
-        self.stop_token_ids = tuple(sp.stop_token_ids or ())
-        self.guided_json = sp.guided_json
-        self.guided_regex = sp.guided_regex
-        self.seed = sp.seed
-        self.grammar_matcher = None
-        self.gen_counts: dict[int, int] = {}
-        self.rep_counts: dict[int, int] | None = None
-        self.arrival_time = perf_counter()
-        self.first_scheduled_time: float | None = None
-        self.first_token_time: float | None = None
-        self.finish_time: float | None = None
-        self.token_times: list[float] = []
-        self.wait_steps = 0
+        self.params = sampling_params or SamplingParams()
+        self.penalty = PenaltyCounts() if _wants_penalty(self.params) else None
+        self.grammar = None          # xgrammar matcher of a guided request
+        self.timing = RequestTiming()
+        self.wait_steps = 0          # scheduler passes spent waiting (starvation guard)
         self.finish_reason: str | None = None
-        # data-parallel attention: rank that owns this sequence's KV (-1 = unassigned)
-        self.dp_rank = -1
+        self.dp_rank = -1            # data-parallel rank owning the KV (-1 = unassigned)
 
-    def __len__(self):
-        return self.num_tokens
-
-    def __getitem__(self, key):
-        return self.token_ids[key]
+    # ------------------------------------------------------------------ tokens
+    def __len__(self) -> int:
+        return len(self.tokens)
 
     @property
-    def is_finished(self) -> bool:
-        return self.status == SequenceStatus.FINISHED
+    def num_tokens(self) -> int:
+        return len(self.tokens)
 
     @property
-    def num_completion_tokens(self) -> int:
-        return self.num_tokens - self.num_prompt_tokens
+    def last(self) -> int:
+        return self.tokens[-1]
 
     @property
-    def prompt_token_ids(self) -> list[int]:
-        return self.token_ids[:self.num_prompt_tokens]
+    def output_len(self) -> int:
+        return len(self.tokens) - self.prompt_len
 
-    @property
-    def completion_token_ids(self) -> list[int]:
-        return self.token_ids[self.num_prompt_tokens:]
+    def output_ids(self) -> list[int]:
+        return self.tokens[self.prompt_len:]
 
+    def prompt_ids(self) -> list[int]:
+        return self.tokens[:self.prompt_len]
+
+    def append(self, token: int):
+        self.tokens.append(token)
+        if self.penalty is not None:
+            self.penalty.add(token)
+
+    # ------------------------------------------------------------------ blocks
     @property
     def num_blocks(self) -> int:
-        return (self.num_tokens + self.block_size - 1) // self.block_size
+        return -(-len(self.tokens) // self.block_size)
 
+    def block_tokens(self, i: int) -> list[int]:
+        """Token ids held by logical block ``i`` (the last may be partial)."""
+        if i < 0 or i >= self.num_blocks:
+            raise IndexError(f"block {i} of a {self.num_blocks}-block sequence")
+        lo = i * self.block_size
+        return self.tokens[lo:lo + self.block_size]
+
+    # ------------------------------------------------------------------ status
     @property
-    def last_block_num_tokens(self) -> int:
-        return self.num_tokens - (self.num_blocks - 1) * self.block_size
+    def is_finished(self) -> bool:
+        return self.status is SequenceStatus.FINISHED
 
-    @property
-    def has_penalty(self) -> bool:
-        return (self.presence_penalty != 0.0 or self.frequency_penalty != 0.0
-                or self.repetition_penalty != 1.0)
-
-    def ensure_rep_counts(self) -> dict[int, int]:
-        """Prompt+generated counts for repetition_penalty, built lazily so a
-        PD handoff that rewrites ``num_prompt_tokens`` stays correct."""
-        if self.rep_counts is None:
-            self.rep_counts = dict(Counter(self.prompt_token_ids))
-            for t, c in self.gen_counts.items():
-                self.rep_counts[t] = self.rep_counts.get(t, 0) + c
-        return self.rep_counts
-
-    def block(self, i: int) -> list[int]:
-        if not 0 <= i < self.num_blocks:
-            raise IndexError(i)
-        return self.token_ids[i * self.block_size:(i + 1) * self.block_size]
-
-    def append_token(self, token_id: int):
-        self.token_ids.append(token_id)
-        self.last_token = token_id
-        self.num_tokens += 1
-        self.gen_counts[token_id] = self.gen_counts.get(token_id, 0) + 1
-        if self.rep_counts is not None:
-            self.rep_counts[token_id] = self.rep_counts.get(token_id, 0) + 1
-
-    def record_token(self, timestamp: float):
-        if self.first_token_time is None:
-            self.first_token_time = timestamp
-        self.token_times.append(timestamp)
+    def finish(self, reason: str, t: float | None = None):
+        self.status = SequenceStatus.FINISHED
+        self.finish_reason = reason
+        self.timing.finished = perf_counter() if t is None else t
 
     def metrics(self) -> dict:
-        finish = self.finish_time or (self.token_times[-1] if self.token_times else None)
-        ttft = None if self.first_token_time is None else self.first_token_time - self.arrival_time
-        e2e = None if finish is None else finish - self.arrival_time
-        gaps = [b - a for a, b in zip(self.token_times, self.token_times[1:])]
-        tpot = None
-        if e2e is not None and ttft is not None and self.num_completion_tokens > 1:
-            tpot = (e2e - ttft) / (self.num_completion_tokens - 1)
-        queue = None if self.first_scheduled_time is None else self.first_scheduled_time - self.arrival_time
-        return {
-            "prompt_tokens": self.num_prompt_tokens,
-            "output_tokens": self.num_completion_tokens,
-            "queue_s": queue,
-            "ttft_s": ttft,
-            "e2e_s": e2e,
-            "tpot_s": tpot,
-            "mean_tpot_s": tpot,
-            "itls_s": gaps,
-            "token_intervals_s": gaps,
-            "finish_reason": self.finish_reason,
-        }
+        return self.timing.report(self.prompt_len, self.output_len, self.finish_reason)

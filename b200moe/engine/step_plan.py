@@ -14,6 +14,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import itertools
+
 import numpy as np
 
 
@@ -104,15 +106,15 @@ def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int
         q = int(qlens[r])
         a, b = int(cu[r]), int(cu[r + 1])
         if prefill_flags[i]:
-            start = s.num_cached_tokens
-            ids[a:b] = s.token_ids[start:start + q]
+            start = s.cached_len
+            ids[a:b] = s.tokens[start:start + q]
         elif feed is not None and id(s) in feed:
             start = len(s)  # the token sampled by the step in flight
             ids[a] = 0
             feed_src[a] = feed[id(s)]
         else:
             start = len(s) - 1
-            ids[a] = s.last_token
+            ids[a] = s.last
         p = np.arange(start, start + q, dtype=np.int64)
         pos[a:b] = p
         bt = np.asarray(s.block_table, dtype=np.int64)
@@ -122,7 +124,7 @@ def build_plan(seqs, query_lens, prefill_flags, block_size: int, max_blocks: int
         slots[a:b] = bt[p // block_size] * block_size + p % block_size
         seq_lens[r] = start + q
         tables[r, :bt.size] = bt
-    temps = np.fromiter((seqs[i].temperature for i in order), dtype=np.float32, count=n)
+    temps = np.fromiter((seqs[i].params.temperature for i in order), dtype=np.float32, count=n)
     plan = StepPlan(ids, pos, slots, cu, seq_lens, tables, nd,
                     int(qlens[nd:].max()) if n > nd else 0,
                     int(seq_lens.max()) if n else 0,
@@ -161,39 +163,40 @@ def validate_plan(plan: StepPlan, num_blocks: int, block_size: int, vocab: int, 
 
 def _sampling_meta(plan: StepPlan, seqs):
     n = len(seqs)
-    if any(s.top_k != -1 for s in seqs):
-        plan.top_k = np.fromiter((s.top_k for s in seqs), np.int32, n)
-    if any(s.top_p < 1.0 for s in seqs):
-        plan.top_p = np.fromiter((s.top_p for s in seqs), np.float32, n)
-    if any(s.min_p > 0.0 for s in seqs):
-        plan.min_p = np.fromiter((s.min_p for s in seqs), np.float32, n)
+    if any(s.params.top_k != -1 for s in seqs):
+        plan.top_k = np.fromiter((s.params.top_k for s in seqs), np.int32, n)
+    if any(s.params.top_p < 1.0 for s in seqs):
+        plan.top_p = np.fromiter((s.params.top_p for s in seqs), np.float32, n)
+    if any(s.params.min_p > 0.0 for s in seqs):
+        plan.min_p = np.fromiter((s.params.min_p for s in seqs), np.float32, n)
     if not plan.all_greedy:
-        plan.seeds = np.fromiter(((s.seed if s.seed is not None else s.seq_id * 7919 + 17) for s in seqs),
+        plan.seeds = np.fromiter(((s.params.seed if s.params.seed is not None else s.seq_id * 7919 + 17) for s in seqs),
                                  np.int64, n)
         plan.offsets = np.fromiter((s.num_tokens for s in seqs), np.int64, n)
-    plan.logprobs_k = max((s.logprobs for s in seqs), default=0)
-    if any(s.has_penalty for s in seqs):
+    plan.logprobs_k = max((s.params.logprobs or 0 for s in seqs), default=0)
+    penalised = [(r, s) for r, s in enumerate(seqs) if s.penalty is not None]
+    if penalised:
         rws, ids, cnt = [], [], []
         pres = np.zeros(n, np.float32)
         freq = np.zeros(n, np.float32)
         rep = np.ones(n, np.float32)
-        for r, s in enumerate(seqs):
-            if not s.has_penalty:
-                continue
-            pres[r], freq[r], rep[r] = s.presence_penalty, s.frequency_penalty, s.repetition_penalty
-            toks = dict(s.ensure_rep_counts()) if s.repetition_penalty != 1.0 else {}
-            for t in s.gen_counts:
-                toks.setdefault(t, 0)
-            for t in toks:
+        for r, s in penalised:
+            p = s.params
+            pres[r], freq[r], rep[r] = p.presence_penalty, p.frequency_penalty, p.repetition_penalty
+            generated = s.penalty.generated
+            # the repetition penalty covers prompt tokens too; its table includes every generated token
+            table = (s.penalty.seen(itertools.islice(s.tokens, s.prompt_len)) if p.repetition_penalty != 1.0
+                     else generated)
+            for t in table:
                 rws.append(r)
                 ids.append(t)
-                cnt.append(s.gen_counts.get(t, 0))
+                cnt.append(generated.get(t, 0))
         if rws:
             plan.pen_rows = np.asarray(rws, np.int32)
             plan.pen_ids = np.asarray(ids, np.int32)
             plan.pen_counts = np.asarray(cnt, np.int32)
             plan.presence, plan.frequency, plan.repetition = pres, freq, rep
-    g_rows = [r for r, s in enumerate(seqs) if s.grammar_matcher is not None]
+    g_rows = [r for r, s in enumerate(seqs) if s.grammar is not None]
     if g_rows:
         plan.grammar_rows = np.asarray(g_rows, np.int32)
 

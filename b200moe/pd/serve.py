@@ -230,10 +230,10 @@ def role_prefill(args):
             sent.add(seq.seq_id)
             prefill_s[rid] = time.perf_counter() - t_add[seq.seq_id]
             nblocks = -(-(seq.num_tokens - 1) // eng.config.kvcache_block_size)  # blocks holding computed KV
-            send_json(ctrl, {"type": "handoff", "req_id": rid, "token_ids": list(seq.token_ids),
-                             "num_prompt_tokens": seq.num_prompt_tokens, "max_tokens": seq.max_tokens,
-                             "temperature": seq.temperature, "ignore_eos": seq.ignore_eos,
-                             "priority": seq.priority, "nblocks": nblocks})
+            send_json(ctrl, {"type": "handoff", "req_id": rid, "token_ids": list(seq.tokens),
+                             "num_prompt_tokens": seq.prompt_len, "max_tokens": seq.params.max_tokens,
+                             "temperature": seq.params.temperature, "ignore_eos": seq.params.ignore_eos,
+                             "priority": seq.params.priority, "nblocks": nblocks})
             if args.kv_transport == "nvlink":
                 handed[rid] = (seq, nblocks)  # blocks stay allocated until the copy ("blocks")
                 eng.detach(seq)

@@ -254,7 +254,7 @@ def test_plan_validation_rejects_out_of_range_indices():
             validate_plan(bad, num_blocks=8, block_size=16, vocab=1000, feed_rows=8)
     s2 = Sequence(list(range(20)), SamplingParams(max_tokens=4))
     s2.block_table = [1, 2]
-    s2.num_cached_tokens = 19
+    s2.cached_len = 19
     fed = build_plan([s2], [1], [False], 16, max_blocks=4, feed={id(s2): 9})
     with pytest.raises(ValueError, match="feed row"):
         validate_plan(fed, num_blocks=8, block_size=16, vocab=1000, feed_rows=8)

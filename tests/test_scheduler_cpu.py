@@ -64,7 +64,7 @@ def test_fresh_blocks_before_lru_and_touch_on_hit():
         s = seq(16 + 1, start=1000 * (i + 1))  # one full block + 1
         bm.allocate(s, bm.can_allocate(s))
         bm.hash_blocks(s, 17)
-        cached.append((s.block_table[0], list(s.token_ids)))
+        cached.append((s.block_table[0], list(s.tokens)))
         bm.deallocate(s)
     # all free; 3 cached blocks in LRU order (0 oldest)
     assert len(bm._lru) == 3
@@ -170,7 +170,7 @@ def test_fcfs_first_sequence_chunked():
     b3 = sch.schedule()
     assert b3.query_lens == [20]
     run_step(sch, b3)
-    assert a.num_completion_tokens == 1
+    assert a.output_len == 1
     assert sch.schedule().mode == "decode"
 
 
@@ -207,7 +207,7 @@ def test_priority_and_starvation():
     for i in range(6):
         sch.add(seq(16, start=100 * (i + 1), priority=0))
         batch = sch.schedule()
-        order.append(max((s.priority for s, f in zip(batch.sequences, batch.prefill_flags) if f), default=None))
+        order.append(max((s.params.priority for s, f in zip(batch.sequences, batch.prefill_flags) if f), default=None))
         run_step(sch, batch)
     assert 5 in order, "the starved low-priority request must eventually run"
     assert order[0] == 0 and order.index(5) >= 2
@@ -252,7 +252,7 @@ def test_finish_on_eos_stop_length():
     assert not fin[a.seq_id]
     while not a.is_finished:
         run_step(sch, sch.schedule(), tok=5)
-    assert a.finish_reason == "length" and a.num_completion_tokens == 3
+    assert a.finish_reason == "length" and a.output_len == 3
 
 
 def test_speculative_schedule_defers_instead_of_preempting():
@@ -292,7 +292,7 @@ def _check_invariants(sch, live, offloads, carried):
             if max(s.dp_rank, 0) != r or not s.block_table:
                 continue
             assert len(set(s.block_table)) == len(s.block_table), "a block twice in one table"
-            assert len(s.block_table) * BS >= s.num_cached_tokens + s.num_scheduled_tokens
+            assert len(s.block_table) * BS >= s.cached_len + s.chunk_len
             for b in s.block_table:
                 refs[b] += 1
         for b, blk in enumerate(bm.blocks):
