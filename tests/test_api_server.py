@@ -254,3 +254,52 @@ def test_cli_reference_flags(monkeypatch, capsys):
     with pytest.raises(SystemExit):
         build_parser().parse_args(["--version"])
     assert b200moe.__version__ in capsys.readouterr().out
+
+
+def test_async_engine_many_streams_one_loop_queue_limit_and_cancel():
+    """Real engine on CPU: eight concurrent streams on one event loop each get their
+    tokens in order; with the queue at its limit a further request is refused
+    (OverflowError) and counted; a cancelled stream ends with a cancelled event and
+    its slot is free again."""
+    from b200moe.sampling_params import SamplingParams
+    eng = AsyncLLMEngine("tiny-moe", device="cpu", kvcache_block_size=16, num_kvcache_blocks=128,
+                         max_num_batched_tokens=512, max_num_seqs=8, max_model_len=256, enforce_eager=True,
+                         max_queue_size=8)
+    sp = SamplingParams(temperature=0.0, max_tokens=5, ignore_eos=True)
+
+    async def drain(h):
+        toks = []
+        while True:
+            ev = await eng.next_event(h)
+            assert ev.error is None
+            if ev.token_id is not None:
+                toks.append(ev.token_id)
+            if ev.finished:
+                return toks, ev
+
+    async def run():
+        handles = [await eng.add_request(list(range(3 + i, 20 + i)), sp) for i in range(8)]
+        with pytest.raises(OverflowError):
+            await eng.add_request([1, 2, 3], sp)
+        results = await asyncio.gather(*(drain(h) for h in handles))
+        assert all(len(t) == 5 and ev.metrics["output_tokens"] == 5 for t, ev in results)
+        long_sp = SamplingParams(temperature=0.0, max_tokens=200, ignore_eos=True)
+        h = await eng.add_request(list(range(10)), long_sp)
+        first = await eng.next_event(h)
+        assert first.token_id is not None
+        eng.cancel(h.seq_id)
+        while True:
+            ev = await eng.next_event(h)
+            if ev.finished:
+                break
+        assert ev.cancelled
+        toks, _ = await drain(await eng.add_request([7, 8, 9], sp))  # the slot is usable again
+        assert len(toks) == 5
+
+    try:
+        asyncio.run(run())
+        m = eng.metrics()
+        assert m["requests_rejected"] == 1 and m["requests_cancelled"] == 1
+        assert m["requests_finished"] == 9 and m["active_requests"] == 0
+    finally:
+        asyncio.run(eng.close())
