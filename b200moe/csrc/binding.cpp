@@ -174,7 +174,8 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
 }
 
 b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor send_cursor, Tensor done_blocks,
-                     Tensor epoch, Tensor status, std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta,
+                     Tensor epoch, Tensor status, Tensor wait_ns, std::vector<int64_t> recv_x,
+                     std::vector<int64_t> recv_meta,
                      std::vector<int64_t> counts, std::vector<int64_t> flags, std::vector<int64_t> done) {
   TORCH_CHECK(dims.size() == 5, "dims = (world, rank, hidden, cap, slot_cap)");
   b200::EpArgs a{};
@@ -194,6 +195,9 @@ b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor
   a.done_blocks = done_blocks.data_ptr<int>();
   a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
   a.status = status.data_ptr<int>();
+  TORCH_CHECK(wait_ns.scalar_type() == torch::kInt64 && wait_ns.numel() >= 2 * a.world && wait_ns.is_contiguous(),
+              "wait_ns: int64 [2 * world]");
+  a.wait_ns = reinterpret_cast<unsigned long long*>(wait_ns.data_ptr<int64_t>());
   for (int r = 0; r < a.world; ++r) {
     a.recv_x[r] = reinterpret_cast<void*>(recv_x[r]);
     a.recv_meta[r] = reinterpret_cast<void*>(recv_meta[r]);
@@ -205,9 +209,10 @@ b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor
 }
 
 #define EP_ARGS_DECL std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor send_cursor, Tensor done_blocks, \
-  Tensor epoch, Tensor status, std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta, \
+  Tensor epoch, Tensor status, Tensor wait_ns, std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta, \
   std::vector<int64_t> counts, std::vector<int64_t> flags, std::vector<int64_t> done
-#define EP_ARGS ep_args(dims, owner, g2l, send_cursor, done_blocks, epoch, status, recv_x, recv_meta, counts, flags, done)
+#define EP_ARGS ep_args(dims, owner, g2l, send_cursor, done_blocks, epoch, status, wait_ns, recv_x, recv_meta, counts, \
+                        flags, done)
 
 void ep_dispatch(EP_ARGS_DECL, Tensor x, Tensor ids, Tensor w) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16); CHECK_DT(ids, torch::kInt32);

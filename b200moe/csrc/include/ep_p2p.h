@@ -21,6 +21,10 @@ struct EpArgs {
   int* done_blocks;              // local scratch counter, zero between layers
   uint32_t* epoch;               // local epoch counter
   int* status;
+  // [2 * world] ns spent waiting, accumulated on the device: [0, world) for each
+  // source's dispatch flag (ep_count), [world, 2 * world) for each owner's done
+  // epoch (ep_wait_done).  A large entry names the rank the others wait for.
+  unsigned long long* wait_ns;
   void* recv_x[kEpMaxWorld];
   void* recv_meta[kEpMaxWorld];
   void* counts[kEpMaxWorld];

@@ -52,17 +52,22 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Bounded wait until *p >= want (wrap-safe compare).  False on timeout.
-__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t want, int* status) {
+// Bounded wait until *p >= want (wrap-safe compare).  False on timeout.  The
+// time spent is added to *waited (when not null).
+__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t want, int* status,
+                                           unsigned long long* waited) {
   const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
   while ((int32_t)(ld_acquire_sys(p) - want) < 0) {
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       record_status(status, kStatusTimeoutFlag);
-      return false;
+      ok = false;
+      break;
     }
     __nanosleep(64);
   }
-  return true;
+  if (waited != nullptr) atomicAdd(waited, (unsigned long long)(globaltimer_ns() - t0));
+  return ok;
 }
 
 __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ ids,
@@ -124,7 +129,7 @@ __global__ void ep_count_kernel(const EpArgs a, int* __restrict__ local_counts) 
   const uint32_t epoch = *a.epoch;
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags[a.rank]);
   if (threadIdx.x == 0) {
-    ok_s = wait_epoch(my_flags + src, epoch, a.status) ? 1 : 0;
+    ok_s = wait_epoch(my_flags + src, epoch, a.status, a.wait_ns ? a.wait_ns + src : nullptr) ? 1 : 0;
     n_s = ok_s ? reinterpret_cast<volatile int*>(a.counts[a.rank])[src] : 0;
   }
   __syncthreads();
@@ -188,7 +193,9 @@ __global__ void ep_signal_kernel(const EpArgs a) {
 __global__ void ep_wait_done_kernel(const EpArgs a) {
   const int r = threadIdx.x;
   const uint32_t epoch = *a.epoch;
-  if (r < a.world) wait_epoch(reinterpret_cast<const uint32_t*>(a.done[a.rank]) + r, epoch, a.status);
+  if (r < a.world)
+    wait_epoch(reinterpret_cast<const uint32_t*>(a.done[a.rank]) + r, epoch, a.status,
+               a.wait_ns ? a.wait_ns + a.world + r : nullptr);
   __syncthreads();
 }
 

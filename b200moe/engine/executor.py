@@ -56,6 +56,7 @@ def _worker_main(config: Config, rank: int, conn, parent_pid: int, shm_spec=None
             conn.send(("error", traceback.format_exc()))
         finally:
             return
+    failed_launches = 0
     while True:
         if not conn.poll(1.0):
             if os.getppid() != parent_pid:  # driver is gone: leave
@@ -71,9 +72,23 @@ def _worker_main(config: Config, rank: int, conn, parent_pid: int, shm_spec=None
             finally:
                 conn.send(("ok", None))
             return
+        if cmd == "launch":
+            # enqueue the step and return to the pipe at once: the next plan can be
+            # enqueued behind it before this one finishes (launch-ahead decode keeps
+            # every rank's stream fed).  No reply on success; a failure is reported as
+            # the step's reply, which the driver reads at its collect.
+            try:
+                runner.launch(*args)
+            except BaseException:
+                conn.send(("error", traceback.format_exc(), "run"))
+                failed_launches += 1
+            continue
+        if cmd == "collect" and failed_launches:
+            failed_launches -= 1  # that step's reply (its error) is already sent
+            continue
         # replies carry their command's kind: a step's reply may still be
         # uncollected when the driver issues a call (KV offload under overlap)
-        kind = "run" if cmd == "run" else "call"
+        kind = "run" if cmd in ("run", "collect") else "call"
         try:
             res = getattr(runner, cmd)(*args)
             conn.send(("ok", res, kind))
@@ -254,7 +269,7 @@ class Executor:
     def launch(self, batch, grammar_masks: dict | None = None, feed_from=None):
         plans = self.plans(batch, grammar_masks, feed_from)
         self.check_alive()
-        self._send_all("run", [(p,) for p in plans])
+        self._send_all("launch", [(p,) for p in plans])
         try:
             self.runner.launch(plans[0])
         except RankFailure:
@@ -281,6 +296,7 @@ class Executor:
     def collect(self):
         """Tokens (batch-row order) of the oldest launched step."""
         plans, n = self._inflight.popleft()
+        self._send_all("collect", [()] * self.world)  # the workers wait on their own steps meanwhile
         results = [self.runner.collect()] + self._gather("run")
         tokens = [0] * n
         logprobs = None

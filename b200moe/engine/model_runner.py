@@ -465,6 +465,19 @@ class ModelRunner:
     def reset_step_timing(self):
         self._step_events.clear()
         ops.reset_launch_count()
+        if self.model.ep is not None and self.model.ep.p2p is not None:
+            self.model.ep.p2p.wait_stats(reset=True)
+
+    def parallel_report(self) -> dict:
+        """Which expert-parallel path and decode mode this rank runs, and (fused path)
+        the device time its kernels waited on each peer since the last reset."""
+        ep = self.model.ep
+        rep = {"ep_backend": None if ep is None else ep.backend, "decode_graphs": sorted(self.graphs),
+               "attention_parallel": "tp" if self.attn_tp > 1 else "dp"}
+        if ep is not None and ep.p2p is not None:
+            torch.cuda.synchronize(self.device)
+            rep["ep_wait"] = ep.p2p.wait_stats(reset=False)
+        return rep
 
     def step_device_ms(self) -> float:
         """Sum of device time (upload start -> sampled ids ready) of the steps

@@ -23,6 +23,8 @@ nanovllm/models/qwen3_moe.py:69-75, 414-418.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -59,14 +61,22 @@ class ExpertParallel:
             self.backend = "nccl_a2a" if backend in ("nccl_a2a", "fused") else backend
         self.p2p = None
         if cuda and backend == "fused":
+            # B200MOE_EP_STRICT=1 (set by bench.py): a fused path that cannot be set up
+            # is an error, not a silent fall-back to the NCCL baseline
+            strict = os.environ.get("B200MOE_EP_STRICT", "0") == "1"
             try:
                 from b200moe.parallel.p2p import P2PMoE
                 self.p2p = P2PMoE.create(self)
                 if self.p2p is not None:
                     self.backend = "fused"
             except Exception as exc:  # no peer access: NCCL baseline
+                if strict:
+                    raise
                 print(f"[ep] fused P2P path unavailable ({exc}); using nccl_a2a", flush=True)
                 self.p2p = None
+            if self.p2p is None and strict:
+                raise RuntimeError("expert parallelism: the fused peer-memory path was requested "
+                                   "(B200MOE_EP_STRICT=1) but could not be set up on every rank")
 
     @property
     def graph_safe(self) -> bool:

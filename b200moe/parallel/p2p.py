@@ -98,7 +98,20 @@ class P2PMoE:
         self.done_blocks = torch.zeros(1, dtype=torch.int32, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = ops.status_word(dev)
+        # device ns waited per layer-wait, summed: [source flags (ep_count) | owner done epochs (ep_wait_done)]
+        self.wait_ns = torch.zeros(2 * W, dtype=torch.int64, device=dev)
         return self
+
+    def wait_stats(self, reset: bool = True) -> dict:
+        """Milliseconds this rank's kernels spent waiting on each peer since the last reset:
+        ``dispatch_ms[r]`` for rank r's rows to arrive, ``combine_ms[r]`` for rank r's
+        expert outputs.  The rank the others wait on most is the straggler."""
+        v = self.wait_ns.cpu().tolist()
+        if reset:
+            self.wait_ns.zero_()
+        W = self.W
+        return {"dispatch_ms": [round(x / 1e6, 2) for x in v[:W]],
+                "combine_ms": [round(x / 1e6, 2) for x in v[W:2 * W]]}
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (after a device sync and
@@ -119,8 +132,8 @@ class P2PMoE:
     def _a(self):
         s = self.symm
         return ([self.W, self.rank, self.H, self.cap, self.slot_cap], self.owner, self.g2l, self.send_cursor,
-                self.done_blocks, self.epoch, self.status, s["recv_x"][1], s["recv_meta"][1], s["counts"][1],
-                s["flags"][1], s["done"][1])
+                self.done_blocks, self.epoch, self.status, self.wait_ns, s["recv_x"][1], s["recv_meta"][1],
+                s["counts"][1], s["flags"][1], s["done"][1])
 
     def moe(self, model, layer, x, ids, w, slots):
         """Returns the tensor holding this rank's (token, k) slots."""

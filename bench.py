@@ -83,6 +83,7 @@ def main():
         return 0
     if args.impl == "reference":
         return reference_arm(args)
+    os.environ.setdefault("B200MOE_EP_STRICT", "1")  # the fused EP path runs, or the bench fails
     import torch
     from b200moe import LLM, SamplingParams, ops
     from b200moe.utils.gpu_clock import ClockSampler
@@ -116,6 +117,7 @@ def main():
     dev_ms = max(runners.call_all("step_device_ms"))
     split = runners.call("step_device_split")  # rank 0: where the device time goes
     launches = sum(runners.call_all("launch_count"))
+    par = runners.call_all("parallel_report")
     nsteps = llm.step_count - steps0
     h2d = (runners.runner.h2d_bytes - h2d0) / max(nsteps, 1)
     d2h = 4 * total_out / max(nsteps, 1)
@@ -134,12 +136,23 @@ def main():
                    "prompts": "fresh uniform-random prompts every pass (no cross-pass prefix-cache hits)",
                    "scheduler_overlap": bool(args.scheduler_overlap),
                    "engine_steps_per_pass": nsteps // max(args.steps, 1), "init_s": round(init_s, 1),
-                   "device_ms_split_rank0": {k: round(v, 1) if isinstance(v, float) else v for k, v in split.items()}},
+                   "device_ms_split_rank0": {k: round(v, 1) if isinstance(v, float) else v for k, v in split.items()},
+                   "ep_backend": par[0]["ep_backend"], "decode_graph_buckets": len(par[0]["decode_graphs"]),
+                   "cuda_graphs": bool(par[0]["decode_graphs"])},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "wall_s_per_pass": round(wall / args.steps, 3)},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if any("ep_wait" in p for p in par):
+        # device ms each rank's EP kernels waited, summed over the timed passes: per rank, the
+        # total, and which peer it waited on longest (the straggler)
+        line["ep_wait_ms"] = [
+            {"rank": r, "dispatch": round(sum(p["ep_wait"]["dispatch_ms"]), 1),
+             "combine": round(sum(p["ep_wait"]["combine_ms"]), 1),
+             "worst_peer": max(range(len(p["ep_wait"]["dispatch_ms"])),
+                               key=lambda q: p["ep_wait"]["dispatch_ms"][q] + p["ep_wait"]["combine_ms"][q])}
+            for r, p in enumerate(par) if "ep_wait" in p]
     ttft = sorted(o["metrics"]["ttft_s"] for o in outs if o["metrics"]["ttft_s"] is not None)
     tpot = sorted(o["metrics"]["tpot_s"] for o in outs if o["metrics"]["tpot_s"] is not None)
     if ttft:
