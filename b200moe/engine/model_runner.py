@@ -20,6 +20,7 @@ import time
 
 import numpy as np
 import torch
+import torch.distributed as dist
 
 from b200moe import ops
 from b200moe.config import Config
@@ -325,7 +326,13 @@ class ModelRunner:
             inp = self._inputs(dummy, views, max_seq_len=self.config.max_model_len, feed=True)
             logits = self._graph_logits[:b]
             tokens = self._graph_tokens[:b]
-            # warm-up run outside capture (first-use allocations, cached tensors)
+            # warm-up run outside capture (first-use allocations, cached tensors).  With
+            # expert parallelism it exchanges rows with every peer under bounded flag
+            # waits: line the ranks up first, as start-up work before the first capture
+            # (weight init, tiling, KV allocation) can leave them seconds apart.
+            if self.model.ep is not None and dist.is_initialized():
+                torch.cuda.synchronize(self.device)
+                dist.barrier()
             h = self.model(inp, self.kv)
             self.model.compute_logits(h, out=logits)
             ops.argmax(logits, tokens)
