@@ -156,3 +156,89 @@ def test_overlap_pipeline_matches_serial():
     b = [o["token_ids"] for o in ov.generate(prompts, sp, use_tqdm=False)]
     ov.exit()
     assert a == b
+
+
+def _plan_inputs(rows, tables, bs, device, all_logits=False):
+    """StepInputs for ``rows`` = [(start, token_ids, seq_blocks)] (decode rows, one
+    token, first); ``all_logits`` returns every token's logits (teacher forcing)."""
+    rows = sorted(rows, key=lambda r: len(r[1]) != 1)
+    ids, pos, slots, lens, tabs, q = [], [], [], [], [], []
+    mb = max(len(t) for t in tables)
+    for start, toks, blocks in rows:
+        p = list(range(start, start + len(toks)))
+        ids += toks
+        pos += p
+        slots += [blocks[x // bs] * bs + x % bs for x in p]
+        lens.append(start + len(toks))
+        tabs.append(blocks + [0] * (mb - len(blocks)))
+        q.append(len(toks))
+    cu = np.cumsum([0] + q).astype(np.int32)
+    nd = sum(1 for x in q if x == 1)
+    t = lambda a: torch.tensor(np.asarray(a), dtype=torch.int32, device=device)
+    li = np.arange(cu[-1]) if all_logits else cu[1:] - 1
+    return StepInputs(t(ids), t(pos), t(slots), t(cu), t(lens), t(tabs), t(li), nd,
+                      max([x for x in q if x != 1] or [0]), max(lens), len(rows), t(cu[nd:] - cu[nd]))
+
+
+def test_qwen3_30b_shape_matches_oracle(monkeypatch):
+    """Qwen3-30B-A3B-shaped model (4 layers: head_dim 128, 32/4 heads, 128 experts
+    top-8, e4m3 with 128x128 scales, tile-major weights as the engine stores them)
+    against the fp32 CPU oracle of the same weights, teacher forced over three steps
+    that between them take every branch the benchmark takes:
+
+      1. prefill of four prompts: tcgen05 FMHA on the paged pool; dense and expert
+         weights dequantised once to bf16 (thresholds lowered so 490 tokens take it);
+      2. decode of the four plus a chunk continuation of a fifth prompt: persistent
+         TMA decode attention, block-scaled e4m3 GEMMs with per-tile dequantisation;
+      3. pure decode: split-K dense GEMMs and the TMEM-ring expert tiles.
+
+    Bars (the reference's L2 gate, docs/numerics-policy.md): logit cosine > 0.999
+    on every row; argmax agreement >= 0.99 over rows whose top-2 gap is not a near
+    tie; the KV the kernels wrote matches the oracle's."""
+    from b200moe import ops
+    random.seed(0)
+    args = preset_args("qwen3-30b-a3b-4l")
+    cpu = Qwen3MoeForCausalLM(args, "cpu", dtype=torch.bfloat16)
+    random_init_(cpu, seed=11)
+    gpu = Qwen3MoeForCausalLM(args, "cuda", dtype=torch.bfloat16)
+    gpu.load_state_dict(cpu.state_dict())
+    gpu.tile_weights_()
+    assert gpu.weights_tiled
+    bs, V = 64, args.vocab_size
+    gpu.reserve_workspace(1024, 16, 8)
+    lens = [300, 129, 44, 17, 260]     # prompt lengths; the fifth is prefilled in two chunks
+    nblk = [-(-(L + 8) // bs) for L in lens]
+    tables, base = [], 1
+    for n in nblk:
+        tables.append(list(range(base, base + n)))
+        base += n
+    pools = [KVPool(base + 2, args.num_hidden_layers, args.num_key_value_heads, bs, args.head_dim,
+                    torch.bfloat16, d) for d in ("cpu", "cuda")]
+    prompts = [[random.randrange(V) for _ in range(L)] for L in lens]
+    steps = [
+        # (rows, all_logits, forced dequant-once thresholds)
+        ([(0, prompts[i], tables[i]) for i in range(4)] + [(0, prompts[4][:128], tables[4])], True, True),
+        ([(lens[i], [random.randrange(V)], tables[i]) for i in range(4)]
+         + [(128, prompts[4][128:], tables[4])], False, False),
+        ([(lens[i] + 1, [random.randrange(V)], tables[i]) for i in range(4)]
+         + [(lens[4], [random.randrange(V)], tables[4])], False, False),
+    ]
+    agree, counted = 0, 0
+    for rows, all_logits, dequant_once in steps:
+        if dequant_once:
+            monkeypatch.setattr(ops, "BF16_DENSE_ROWS", 256)
+            monkeypatch.setattr(Qwen3MoeForCausalLM, "BF16_EXPERT_ROWS", 1)
+        lc = cpu.compute_logits(cpu(_plan_inputs(rows, tables, bs, "cpu", all_logits), pools[0])).float()
+        lg = gpu.compute_logits(gpu(_plan_inputs(rows, tables, bs, "cuda", all_logits), pools[1])).float().cpu()
+        torch.cuda.synchronize()
+        ops.check_status(torch.device("cuda", 0))
+        monkeypatch.setattr(ops, "BF16_DENSE_ROWS", 2048)
+        monkeypatch.setattr(Qwen3MoeForCausalLM, "BF16_EXPERT_ROWS", 512)
+        cos = torch.nn.functional.cosine_similarity(lc, lg, dim=-1)
+        assert cos.min().item() > 0.999, (all_logits, cos.min().item())
+        top2 = lc.topk(2, dim=-1).values
+        clear = (top2[:, 0] - top2[:, 1]) > 0.01 * lc.std(dim=-1)
+        agree += int(((lc.argmax(-1) == lg.argmax(-1)) & clear).sum())
+        counted += int(clear.sum())
+    assert counted > 400 and agree / counted >= 0.99, (agree, counted)
+    torch.testing.assert_close(pools[1].data.cpu().float(), pools[0].data.float(), atol=5e-2, rtol=5e-2)
