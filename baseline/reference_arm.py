@@ -196,11 +196,15 @@ def run(args, prompts_for, metric: str) -> int:
         os.environ.pop(var, None)
     from nanovllm import LLM, SamplingParams  # the reference package
     eager = os.environ.get("B200MOE_REF_EAGER", "1") != "0"
+    # the reference's decode-only MoE backend (its config.decode_moe_backend); its
+    # documentation names bmm_dense as the one its decode graphs can capture
+    decode_moe = os.environ.get("B200MOE_REF_DECODE_MOE") or None
     t0 = time.perf_counter()
     llm = LLM(ckpt, tensor_parallel_size=args.gpus, max_num_seqs=max(args.num_requests, 1),
               max_num_batched_tokens=args.max_num_batched_tokens,
               max_model_len=args.input_len + args.output_len + 16, kvcache_block_size=256,
-              moe_backend="grouped_mm", attention_backend="triton_paged", scheduler_policy=args.scheduler_policy,
+              moe_backend="grouped_mm", decode_moe_backend=decode_moe, attention_backend="triton_paged",
+              scheduler_policy=args.scheduler_policy,
               # eager by default: the reference's production setting (its deploy/serve.env.example
               # and scripts/p2_benchmark.py run enforce_eager); B200MOE_REF_EAGER=0 tries its
               # CUDA-graph decode instead
@@ -236,7 +240,8 @@ def run(args, prompts_for, metric: str) -> int:
             "data": "synthetic uniform-random token ids; random-init fp8 checkpoint written at run time",
             "config": {"model": args.model, "global_batch": args.num_requests, "seq_len": args.input_len,
                        "output_len": args.output_len, "parallelism": f"tp{args.gpus}/ep{args.gpus}",
-                       "moe_backend": "grouped_mm", "attention_backend": "triton_paged", "enforce_eager": eager,
+                       "moe_backend": "grouped_mm", "decode_moe_backend": decode_moe,
+                       "attention_backend": "triton_paged", "enforce_eager": eager,
                        "ckpt_dir": ckpt, "ckpt_write_s": round(write_s, 1), "init_s": round(init_s, 1),
                        "warmup_pass_s": warm_s,
                        "timing": "CUDA events on rank 0's stream around the K passes; rank 0 waits on every "

@@ -466,13 +466,15 @@ def test_sampler_distribution():
     assert int(s.max()) <= 2
 
 
-def _ep_wait_args(world, epoch, done, status):
+def _ep_wait_args(world, epoch, done, status, wait_ns=None):
     """EpArgs for one GPU whose every per-rank pointer is local memory: the
     wait kernel reads done[rank][r] for r < world and nothing else."""
     i32 = dict(dtype=torch.int32, device=DEV)
     local = [done.data_ptr()] * world
+    if wait_ns is None:
+        wait_ns = torch.zeros(2 * world, dtype=torch.int64, device=DEV)
     return ([world, 0, 8, 1, 1], torch.zeros(1, **i32), torch.zeros(1, **i32), torch.zeros(world, **i32),
-            torch.zeros(1, **i32), epoch, status, local, local, local, local,
+            torch.zeros(1, **i32), epoch, status, wait_ns, local, local, local, local,
             [done.data_ptr() + 4 * world * r for r in range(world)])
 
 
@@ -493,10 +495,14 @@ def test_bounded_flag_wait_returns_status_instead_of_hanging():
     assert int(status.item()) == 0 and int(done[0].item()) == 1
     # world 2: rank 1's entry is never released
     t0 = time.monotonic()
-    C.ep_wait_done(*_ep_wait_args(2, epoch, done, status))
+    wait_ns = torch.zeros(4, dtype=torch.int64, device=DEV)
+    C.ep_wait_done(*_ep_wait_args(2, epoch, done, status, wait_ns))
     torch.cuda.synchronize()
     waited = time.monotonic() - t0
     assert int(status.item()) == 6, "kStatusTimeoutFlag"
     assert 1.5 < waited < 20.0, waited
+    # the device-side wait accounting charges the time to the peer that never answered
+    ns = wait_ns.cpu().tolist()
+    assert ns[0] == 0 and ns[1] == 0 and ns[2] < 1e8 and 1.5e9 < ns[3] < 2.5e9, ns
     x = torch.randn(4, 1000, device=DEV)  # the context still runs kernels
     assert torch.equal(ops.argmax(x).cpu().long(), x.argmax(dim=-1).cpu())
