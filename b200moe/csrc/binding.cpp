@@ -562,10 +562,13 @@ void argmax(Tensor logits, Tensor out) {
 }
 
 void sample(Tensor logits, Tensor temperature, c10::optional<Tensor> top_k, c10::optional<Tensor> top_p,
-            c10::optional<Tensor> min_p, Tensor seeds, c10::optional<Tensor> offsets, Tensor out) {
+            c10::optional<Tensor> min_p, Tensor seeds, c10::optional<Tensor> offsets, Tensor out,
+            c10::optional<Tensor> allow, c10::optional<Tensor> allow_row, int64_t lp_k,
+            c10::optional<Tensor> lp_top_v, c10::optional<Tensor> lp_top_i, c10::optional<Tensor> lp_chosen) {
   CHECK_CUDA(logits); CHECK_DT(logits, torch::kFloat32); CHECK_DT(temperature, torch::kFloat32);
   CHECK_DT(seeds, torch::kInt64); CHECK_DT(out, torch::kInt32);
   TORCH_CHECK(logits.stride(1) == 1, "logits inner stride must be 1");
+  const int64_t B = logits.size(0);
   b200::SampleArgs a{};
   a.temperature = temperature.data_ptr<float>();
   a.top_k = ptr_or_null<int>(top_k);
@@ -573,6 +576,25 @@ void sample(Tensor logits, Tensor temperature, c10::optional<Tensor> top_k, c10:
   a.min_p = ptr_or_null<float>(min_p);
   a.seeds = seeds.data_ptr<int64_t>();
   a.offsets = ptr_or_null<int64_t>(offsets);
+  if (allow.has_value()) {
+    TORCH_CHECK(allow_row.has_value(), "allow needs allow_row");
+    CHECK_DT((*allow), torch::kInt32); CHECK_DT((*allow_row), torch::kInt32); CHECK_CONTIG((*allow));
+    TORCH_CHECK(allow->dim() == 2 && allow_row->numel() >= B, "allow [masks, words], allow_row [B]");
+    a.allow = reinterpret_cast<const uint32_t*>(allow->data_ptr<int>());
+    a.allow_row = allow_row->data_ptr<int>();
+    a.mask_words = (int)allow->size(1);
+  }
+  a.lp_k = (int)lp_k;
+  if (lp_k > 0) {
+    TORCH_CHECK(lp_top_v.has_value() && lp_top_i.has_value() && lp_chosen.has_value(), "log-prob outputs");
+    CHECK_DT((*lp_top_v), torch::kFloat32); CHECK_DT((*lp_top_i), torch::kInt32);
+    CHECK_DT((*lp_chosen), torch::kFloat32);
+    TORCH_CHECK(lp_top_v->numel() >= B * lp_k && lp_top_i->numel() >= B * lp_k && lp_chosen->numel() >= B,
+                "log-prob outputs too small");
+    a.lp_top_v = lp_top_v->data_ptr<float>();
+    a.lp_top_i = lp_top_i->data_ptr<int>();
+    a.lp_chosen = lp_chosen->data_ptr<float>();
+  }
   b200::sample_rows(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1), logits.stride(0), a,
                     out.data_ptr<int>(), stream());
 }

@@ -5,6 +5,11 @@
 //                        exponential race: argmax_i p_i / E_i with E_i ~ Exp(1)
 //                        (the reference's sampler, nanovllm/layers/sampler.py:112-169,
 //                        which sorts the whole vocabulary for top-k / top-p)
+//   guided rows          an allowed-token bitmask removes tokens before all of the above
+//   log-probs            of the distribution the row samples from (temperature and
+//                        filters applied; greedy rows: the raw logits), the chosen
+//                        token's and the top lp_k (<= 20) -- reference semantics of
+//                        nanovllm/layers/sampler.py:_gather_logprobs
 //
 // No sort: the top-k and top-p thresholds come from an MSB-first radix select
 // over the order-preserving integer image of the scaled logits (4 passes of 8
@@ -129,12 +134,19 @@ __global__ void __launch_bounds__(kST) argmax_kernel(const float* __restrict__ l
   if (threadIdx.x == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
 }
 
-// Radix select over the ordered image of x/temp among tokens with image >= lo_bound.
+// Token i passes the allowed-token bitmask (null mask: every token does).
+__device__ __forceinline__ bool allowed(const uint32_t* am, int i) {
+  return am == nullptr || ((am[i >> 5] >> (i & 31)) & 1u);
+}
+
+// Radix select over the ordered image of x/temp among allowed tokens with image >= lo_bound.
 // mode 0: image of the k-th largest value (k counted from the top)
 // mode 1: largest image t such that the probability mass of tokens with image
 //         >= t reaches `target` (mass weight exp(x - M) * invZ)
+
 __device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t lo_bound, int mode, int k,
-                                 float target, float M, float invZ, uint32_t* hist_u, float* hist_f) {
+                                 float target, float M, float invZ, const uint32_t* am, uint32_t* hist_u,
+                                 float* hist_f) {
   uint32_t prefix = 0, mask = 0;
   float above_mass = 0.f;
   uint32_t above_cnt = 0;
@@ -142,6 +154,7 @@ __device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t 
     for (int i = threadIdx.x; i < 256; i += kST) { hist_u[i] = 0; hist_f[i] = 0.f; }
     __syncthreads();
     for (int i = threadIdx.x; i < V; i += kST) {
+      if (!allowed(am, i)) continue;
       const float x = row[i] * inv_t;
       const uint32_t o = f2ord(x);
       if (o < lo_bound || (o & mask) != prefix) continue;
@@ -207,6 +220,47 @@ __device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t 
   return prefix;
 }
 
+constexpr int kCand = 64;  // candidates gathered for the top log-probs (ties past it are dropped)
+
+// The k best (value, id) among allowed tokens whose scaled image is >= lo, best
+// first (ties: lower id first), written as log-probabilities x - M - logZ.
+__device__ void write_top_logprobs(const float* row, int V, float inv_t, uint32_t lo, const uint32_t* am, int k,
+                                   float M, float logZ, uint32_t* hist_u, float* hist_f, float* cv, int* ci,
+                                   int* nc, float* out_v, int* out_i) {
+  const uint32_t t = radix_select(row, V, inv_t, lo, 0, k, 0.f, M, 1.f, am, hist_u, hist_f);
+  const uint32_t bound = max(t, lo);
+  if (threadIdx.x == 0) *nc = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < V; i += kST) {
+    if (!allowed(am, i)) continue;
+    const float x = row[i] * inv_t;
+    if (f2ord(x) < bound) continue;
+    const int slot = atomicAdd(nc, 1);
+    if (slot < kCand) { cv[slot] = x; ci[slot] = i; }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int n = min(*nc, kCand);
+    for (int p = 1; p < n; ++p) {  // insertion sort of <= 64 entries
+      const float v = cv[p];
+      const int id = ci[p];
+      int q = p - 1;
+      while (q >= 0 && (cv[q] < v || (cv[q] == v && ci[q] > id))) {
+        cv[q + 1] = cv[q];
+        ci[q + 1] = ci[q];
+        --q;
+      }
+      cv[q + 1] = v;
+      ci[q + 1] = id;
+    }
+    for (int j = 0; j < k; ++j) {
+      out_v[j] = j < n ? cv[j] - M - logZ : -INFINITY;
+      out_i[j] = j < n ? ci[j] : -1;
+    }
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ logits, int V, int64_t ld,
                                                      SampleArgs a, int* __restrict__ out) {
   pdl_enter();
@@ -214,60 +268,97 @@ __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ l
   __shared__ int redi[32];
   __shared__ uint32_t hist_u[260];
   __shared__ float hist_f[260];
+  __shared__ float cand_v[kCand];
+  __shared__ int cand_i[kCand];
+  __shared__ int n_cand;
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * ld;
+  const uint32_t* am = nullptr;
+  if (a.allow != nullptr && a.allow_row != nullptr && a.allow_row[r] >= 0)
+    am = a.allow + (size_t)a.allow_row[r] * a.mask_words;
   const float temp = a.temperature[r];
-  if (temp < 1e-3f) {  // greedy row
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += kST) {
-      const float v = row[i];
-      if (v > bv) { bv = v; bi = i; }
-    }
-    block_argmax(bv, bi, red, redi);
-    if (threadIdx.x == 0) out[r] = bi == 0x7fffffff ? 0 : bi;
-    return;
-  }
-  const float inv_t = 1.f / temp;
-  float mx = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += kST) mx = fmaxf(mx, row[i] * inv_t);
-  const float M = block_reduce_max(mx, red);
-  float z = 0.f;
-  for (int i = threadIdx.x; i < V; i += kST) z += __expf(row[i] * inv_t - M);
-  const float Z = block_reduce_sum(z, red);
+  const bool greedy = temp < 1e-3f;
+  const float inv_t = greedy ? 1.f : 1.f / temp;
+  const int lp_k = a.lp_k;
 
-  uint32_t lo = 0;  // keep tokens with f2ord(x) >= lo
-  const int top_k = a.top_k ? a.top_k[r] : -1;
-  if (top_k > 0 && top_k < V) lo = radix_select(row, V, inv_t, 0, 0, top_k, 0.f, M, 1.f / Z, hist_u, hist_f);
-  const float top_p = a.top_p ? a.top_p[r] : 1.f;
-  if (top_p < 1.f) {
-    // nucleus mass is measured over the top-k survivors
-    float zk = 0.f;
-    for (int i = threadIdx.x; i < V; i += kST) {
-      const float x = row[i] * inv_t;
-      if (f2ord(x) >= lo) zk += __expf(x - M);
-    }
-    const float Zk = block_reduce_sum(zk, red);
-    const uint32_t tp = radix_select(row, V, inv_t, lo, 1, 0, top_p, M, 1.f / Zk, hist_u, hist_f);
-    lo = max(lo, tp);
-  }
-  const float min_p = a.min_p ? a.min_p[r] : 0.f;
-  if (min_p > 0.f) lo = max(lo, f2ord(M + __logf(min_p)));
-
-  const uint2 key = make_uint2((uint32_t)a.seeds[r], (uint32_t)((uint64_t)a.seeds[r] >> 32));
-  const uint32_t off = a.offsets ? (uint32_t)a.offsets[r] : 0u;
+  // best allowed token of the scaled logits: the greedy choice and the softmax max
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int i = threadIdx.x; i < V; i += kST) {
+    if (!allowed(am, i)) continue;
     const float x = row[i] * inv_t;
-    if (f2ord(x) < lo) continue;
-    const uint4 rnd = philox4x32(make_uint4((uint32_t)i, off, 0x5A3Cu, 0u), key);
-    const float e = -__logf(u01(rnd.x));  // Exp(1)
-    const float score = (x - M) - __logf(fmaxf(e, 1e-20f));
-    if (score > bv) { bv = score; bi = i; }
+    if (x > bv) { bv = x; bi = i; }  // strided scan: first hit per thread is its lowest index
   }
   block_argmax(bv, bi, red, redi);
-  if (threadIdx.x == 0) out[r] = bi == 0x7fffffff ? 0 : bi;
+  const float M = bv;
+  if (M == -INFINITY) {  // nothing allowed (or every logit -inf): token 0, no distribution
+    if (threadIdx.x == 0) out[r] = 0;
+    if (lp_k > 0 && threadIdx.x < lp_k) {
+      a.lp_top_v[(size_t)r * lp_k + threadIdx.x] = -INFINITY;
+      a.lp_top_i[(size_t)r * lp_k + threadIdx.x] = -1;
+    }
+    if (lp_k > 0 && threadIdx.x == 0) a.lp_chosen[r] = -INFINITY;
+    return;
+  }
+
+  uint32_t lo = 0;  // the distribution: allowed tokens with f2ord(x) >= lo
+  int tok;
+  if (greedy) {
+    tok = bi;
+  } else {
+    float z = 0.f;
+    for (int i = threadIdx.x; i < V; i += kST)
+      if (allowed(am, i)) z += __expf(row[i] * inv_t - M);
+    const float Z = block_reduce_sum(z, red);
+    const int top_k = a.top_k ? a.top_k[r] : -1;
+    if (top_k > 0 && top_k < V)
+      lo = radix_select(row, V, inv_t, 0, 0, top_k, 0.f, M, 1.f / Z, am, hist_u, hist_f);
+    const float top_p = a.top_p ? a.top_p[r] : 1.f;
+    if (top_p < 1.f) {
+      // nucleus mass is measured over the top-k survivors
+      float zk = 0.f;
+      for (int i = threadIdx.x; i < V; i += kST) {
+        if (!allowed(am, i)) continue;
+        const float x = row[i] * inv_t;
+        if (f2ord(x) >= lo) zk += __expf(x - M);
+      }
+      const float Zk = block_reduce_sum(zk, red);
+      const uint32_t tp = radix_select(row, V, inv_t, lo, 1, 0, top_p, M, 1.f / Zk, am, hist_u, hist_f);
+      lo = max(lo, tp);
+    }
+    const float min_p = a.min_p ? a.min_p[r] : 0.f;
+    if (min_p > 0.f) lo = max(lo, f2ord(M + __logf(min_p)));
+
+    const uint2 key = make_uint2((uint32_t)a.seeds[r], (uint32_t)((uint64_t)a.seeds[r] >> 32));
+    const uint32_t off = a.offsets ? (uint32_t)a.offsets[r] : 0u;
+    float sv = -INFINITY;
+    int si = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += kST) {
+      if (!allowed(am, i)) continue;
+      const float x = row[i] * inv_t;
+      if (f2ord(x) < lo) continue;
+      const uint4 rnd = philox4x32(make_uint4((uint32_t)i, off, 0x5A3Cu, 0u), key);
+      const float e = -__logf(u01(rnd.x));  // Exp(1)
+      const float score = (x - M) - __logf(fmaxf(e, 1e-20f));
+      if (score > sv) { sv = score; si = i; }
+    }
+    block_argmax(sv, si, red, redi);
+    tok = si == 0x7fffffff ? bi : si;
+  }
+  if (threadIdx.x == 0) out[r] = tok;
+  if (lp_k <= 0) return;
+
+  // log-probabilities of the distribution just sampled from
+  float zs = 0.f;
+  for (int i = threadIdx.x; i < V; i += kST) {
+    if (!allowed(am, i)) continue;
+    const float x = row[i] * inv_t;
+    if (f2ord(x) >= lo) zs += expf(x - M);
+  }
+  const float logZ = logf(block_reduce_sum(zs, red));
+  if (threadIdx.x == 0) a.lp_chosen[r] = row[tok] * inv_t - M - logZ;
+  write_top_logprobs(row, V, inv_t, lo, am, lp_k, M, logZ, hist_u, hist_f, cand_v, cand_i, &n_cand,
+                     a.lp_top_v + (size_t)r * lp_k, a.lp_top_i + (size_t)r * lp_k);
 }
 
 __global__ void penalty_kernel(float* __restrict__ logits, int64_t ld, const int* __restrict__ rows,
@@ -300,6 +391,11 @@ void argmax_rows(const float* logits, int B, int V, int64_t ld, int* out, cudaSt
 
 void sample_rows(const float* logits, int B, int V, int64_t ld, const SampleArgs& a, int* out, cudaStream_t s) {
   if (B == 0) return;
+  if (a.lp_k < 0 || a.lp_k > kMaxLogprobs) throw std::runtime_error("sample_rows: lp_k out of [0, 20]");
+  if (a.lp_k > 0 && (a.lp_top_v == nullptr || a.lp_top_i == nullptr || a.lp_chosen == nullptr))
+    throw std::runtime_error("sample_rows: log-prob outputs missing");
+  if ((a.allow == nullptr) != (a.allow_row == nullptr) || (a.allow != nullptr && a.mask_words * 32 < V))
+    throw std::runtime_error("sample_rows: allowed-token mask needs both arrays and ceil(V / 32) words");
   pdl_launch(sample_kernel, B, kST, 0, s, logits, V, ld, a, out);
   check_launch("sample_rows");
 }

@@ -25,7 +25,7 @@ import torch.distributed as dist
 from b200moe import ops
 from b200moe.config import Config
 from b200moe.engine.kv_cache import KVPool
-from b200moe.engine.step_plan import StepPlan, empty_plan, pack_plan, validate_plan
+from b200moe.engine.step_plan import StepPlan, empty_plan, pack_plan, pack_sampling, validate_plan
 from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM, StepInputs
 from b200moe.utils.init_trace import InitTrace
 from b200moe.utils.profiler import DeviceProfiler
@@ -124,6 +124,12 @@ class ModelRunner:
         # the last step's sampled tokens (plan-row order), read by the next step's
         # embedding for rows launched before the host collected them
         self._feed_tokens = torch.zeros(max(self.max_rows, 1), dtype=torch.int32, device=self.device)
+        # sampling arrays of a step (pack_sampling): two pinned staging buffers, one device buffer, grown on demand
+        self._samp_pinned = [torch.empty(16 * max(self.max_rows, 1), dtype=torch.int32, pin_memory=pin)
+                             for _ in range(2)]
+        self._samp_pinned_np = [p.numpy() for p in self._samp_pinned]
+        self._samp_dev = torch.empty(16 * max(self.max_rows, 1), dtype=torch.int32, device=self.device)
+        self._samp_idx = 0
         self._pin_idx = 0
         self._validate = os.environ.get("B200MOE_VALIDATE_PLANS", "1") != "0"
         self._logits = None
@@ -386,9 +392,14 @@ class ModelRunner:
                 h = self.model(self._inputs(plan, views), self.kv)
             logits = self.model.compute_logits(h)
             tokens = None
+        lp = None
         if plan.needs_full_sampler or tokens is None:
-            tokens = self._sample(plan, logits)
-        lp = self._logprobs(plan, logits, tokens) if plan.logprobs_k else None
+            tokens, lp_dev = self._sample(plan, logits)
+            if lp_dev is not None:  # log-probs ride the same device-to-host read as the tokens
+                pin = self.device.type == "cuda"
+                lp = tuple(torch.empty(t.shape, dtype=t.dtype, pin_memory=pin) for t in lp_dev)
+                for host, dev_t in zip(lp, lp_dev):
+                    host.copy_(dev_t, non_blocking=True)
         out = torch.empty(B, dtype=torch.int32, pin_memory=self.device.type == "cuda")
         out.copy_(tokens, non_blocking=True)
         self._feed_tokens[:B].copy_(tokens, non_blocking=True)  # the next step may read them on the device
@@ -412,48 +423,61 @@ class ModelRunner:
         logprobs = None
         if lp is not None:
             topv, topi, chosen = (t.tolist() for t in lp)
-            logprobs = [{"top": list(zip(topi[r], topv[r])), "chosen": chosen[r]} for r in range(len(toks))]
+            logprobs = [{"top": [(i, v) for i, v in zip(topi[r], topv[r]) if i >= 0], "chosen": chosen[r]}
+                        for r in range(len(toks))]
         return toks, logprobs
 
-    def _dev(self, arr, dtype):
-        t = torch.from_numpy(np.ascontiguousarray(arr))
-        if self.device.type == "cuda":
-            t = t.pin_memory().to(self.device, non_blocking=True)
-        return t.to(dtype)
+    def _upload_sampling(self, plan: StepPlan) -> dict:
+        """The step's sampling arrays (``pack_sampling``) in one host-to-device copy
+        from a pinned staging buffer; returns device views by name."""
+        if self.device.type != "cuda":
+            buf, layout = pack_sampling(plan)
+            dev = torch.from_numpy(buf)
+        else:
+            i = self._samp_idx
+            self._samp_idx ^= 1
+            buf, layout = pack_sampling(plan, self._samp_pinned_np[i])
+            n = buf.size
+            if buf.base is None or n > self._samp_pinned[i].numel():  # grew past the staging buffer
+                self._samp_pinned[i] = torch.empty(max(2 * n, 1024), dtype=torch.int32, pin_memory=True)
+                self._samp_pinned_np[i] = self._samp_pinned[i].numpy()
+                self._samp_pinned_np[i][:n] = buf
+            if n > self._samp_dev.numel():
+                self._samp_dev = torch.empty(max(2 * n, 1024), dtype=torch.int32, device=self.device)
+            dev = self._samp_dev
+            dev[:n].copy_(self._samp_pinned[i][:n], non_blocking=True)
+            self.h2d_bytes += 4 * n
+        views = {}
+        for name, (o, n, dt) in layout.items():
+            v = dev[o:o + n]
+            views[name] = v.view(torch.float32) if dt == np.float32 else v.view(torch.int64) if dt == np.int64 else v
+        if "allow" in views:
+            views["allow"] = views["allow"].view(plan.grammar_rows.size, -1)
+        return views
 
-    def _sample(self, plan: StepPlan, logits: torch.Tensor) -> torch.Tensor:
+    def _sample(self, plan: StepPlan, logits: torch.Tensor):
+        """Penalties, then ONE sampler kernel for every row (greedy, filtered and guided
+        rows alike) that also writes the log-probabilities a row asked for.  Returns
+        (tokens [B] int32, (top_v, top_i, chosen) device tensors or None)."""
+        v = self._upload_sampling(plan)
         if plan.pen_rows is not None:
-            ops.apply_penalties(logits, self._dev(plan.pen_rows, torch.int32), self._dev(plan.pen_ids, torch.int32),
-                                self._dev(plan.pen_counts, torch.int32), self._dev(plan.presence, torch.float32),
-                                self._dev(plan.frequency, torch.float32), self._dev(plan.repetition, torch.float32))
-        if plan.grammar_mask is not None:
-            rows = self._dev(plan.grammar_rows, torch.int64)
-            mask = self._dev(plan.grammar_mask, torch.int32)
-            V = logits.shape[1]
-            bits = torch.arange(V, device=logits.device)
-            allowed = ((mask[:, bits // 32] >> (bits % 32)) & 1).bool()
-            sub = logits.index_select(0, rows)
-            logits.index_copy_(0, rows, sub.masked_fill(~allowed, torch.finfo(torch.float32).min))
-        if plan.all_greedy:
-            return ops.argmax(logits)
-        n = plan.num_rows
-        return ops.sample(
-            logits, self._dev(plan.temperature, torch.float32),
-            None if plan.top_k is None else self._dev(plan.top_k, torch.int32),
-            None if plan.top_p is None else self._dev(plan.top_p, torch.float32),
-            None if plan.min_p is None else self._dev(plan.min_p, torch.float32),
-            self._dev(plan.seeds if plan.seeds is not None else np.zeros(n, np.int64), torch.int64),
-            None if plan.offsets is None else self._dev(plan.offsets, torch.int64))
-
-    @staticmethod
-    def _logprobs(plan: StepPlan, logits, tokens):
-        t = torch.from_numpy(plan.temperature).to(logits.device).clamp_min(1e-5).unsqueeze(1)
-        greedy = torch.from_numpy(plan.temperature < 1e-3).to(logits.device).unsqueeze(1)
-        scaled = torch.where(greedy, logits, logits / t)
-        lp = torch.log_softmax(scaled.float(), dim=-1)
-        chosen = lp.gather(1, tokens.long().unsqueeze(1)).squeeze(1)
-        topv, topi = lp.topk(min(plan.logprobs_k, lp.shape[1]), dim=-1)
-        return topv.cpu(), topi.cpu(), chosen.cpu()
+            ops.apply_penalties(logits, v["pen_rows"], v["pen_ids"], v["pen_counts"], v["presence"],
+                                v["frequency"], v["repetition"])
+        if plan.all_greedy and plan.grammar_rows is None and not plan.logprobs_k:
+            return ops.argmax(logits), None
+        B = plan.num_rows
+        lp = None
+        if plan.logprobs_k:
+            k = plan.logprobs_k
+            lp = (k, torch.empty(B, k, dtype=torch.float32, device=logits.device),
+                  torch.empty(B, k, dtype=torch.int32, device=logits.device),
+                  torch.empty(B, dtype=torch.float32, device=logits.device))
+        seeds = v.get("seeds")
+        if seeds is None:
+            seeds = torch.zeros(B, dtype=torch.int64, device=logits.device)
+        tokens = ops.sample(logits, v["temperature"], v.get("top_k"), v.get("top_p"), v.get("min_p"), seeds,
+                            v.get("offsets"), allow=v.get("allow"), allow_row=v.get("allow_row"), logprobs=lp)
+        return tokens, (lp[1:] if lp else None)
 
     # ----------------------------------------------------------- offload
     def offload_put(self, block_id: int) -> int:

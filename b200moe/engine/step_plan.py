@@ -227,3 +227,43 @@ def pack_plan(plan: StepPlan, out: np.ndarray | None = None) -> tuple[np.ndarray
         offs[name] = (o, arr.size)
         o += arr.size
     return buf, offs
+
+
+def pack_sampling(plan: StepPlan, out: np.ndarray | None = None) -> tuple[np.ndarray, dict]:
+    """Every per-row sampling array of a step in ONE int32 buffer, so the sampler's
+    inputs cross to the device in a single copy: temperature, top-k / top-p / min-p,
+    Philox seeds and counters, penalty triples and coefficients, and the grammar
+    bitmasks with the mask index of each row.  Floats travel as their bits; int64
+    fields start on an even word so their device views are 8-byte aligned.
+    Returns (buffer, {name: (word offset, words, numpy dtype)})."""
+    B = plan.num_rows
+    parts: list[tuple[str, np.ndarray]] = [("temperature", plan.temperature.astype(np.float32, copy=False))]
+    for name in ("top_k", "top_p", "min_p"):
+        arr = getattr(plan, name)
+        if arr is not None:
+            parts.append((name, arr))
+    if not plan.all_greedy:
+        seeds = plan.seeds if plan.seeds is not None else np.zeros(B, np.int64)
+        parts.append(("seeds", seeds.astype(np.int64, copy=False)))
+        if plan.offsets is not None:
+            parts.append(("offsets", plan.offsets.astype(np.int64, copy=False)))
+    if plan.pen_rows is not None:
+        parts += [("pen_rows", plan.pen_rows), ("pen_ids", plan.pen_ids), ("pen_counts", plan.pen_counts),
+                  ("presence", plan.presence), ("frequency", plan.frequency), ("repetition", plan.repetition)]
+    if plan.grammar_rows is not None:
+        row_mask = np.full(B, -1, np.int32)
+        row_mask[plan.grammar_rows] = np.arange(plan.grammar_rows.size, dtype=np.int32)
+        parts += [("allow_row", row_mask), ("allow", plan.grammar_mask.astype(np.int32, copy=False).reshape(-1))]
+    words = 0
+    layout = {}
+    for name, arr in parts:
+        if arr.dtype.itemsize == 8 and words % 2:
+            words += 1
+        n = arr.size * arr.dtype.itemsize // 4
+        layout[name] = (words, n, arr.dtype)
+        words += n
+    buf = out[:words] if out is not None and out.size >= words else np.empty(words, np.int32)
+    for name, arr in parts:
+        o, n, _ = layout[name]
+        buf[o:o + n] = np.ascontiguousarray(arr).view(np.int32).reshape(-1)
+    return buf, layout

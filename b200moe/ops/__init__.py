@@ -495,49 +495,92 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     return out
 
 
-def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out=None):
+def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out=None, allow=None, allow_row=None,
+           logprobs=None):
     """temperature / top-k / top-p / min-p / exponential-race sampling (greedy
-    rows where temperature < 1e-3)."""
+    rows where temperature < 1e-3) in one kernel per row.
+
+    ``allow`` [n_masks, ceil(V / 32)] int32 allowed-token bitmasks with ``allow_row``
+    [B] (mask of each row, -1 = unconstrained): guided decoding.  ``logprobs`` =
+    (k, top_v [B, k] f32, top_i [B, k] i32, chosen [B] f32) receives the
+    log-probabilities of the distribution each row sampled from (greedy rows: the
+    raw logits under the mask); top_i is -1 where fewer than k tokens survive."""
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
     if not logits.is_cuda:
-        return out.copy_(sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets))
-    native().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out)
+        toks, lp = sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets, allow, allow_row,
+                                    logprobs[0] if logprobs else 0)
+        if logprobs:
+            k, tv, ti, ch = logprobs
+            tv.copy_(lp[0])
+            ti.copy_(lp[1])
+            ch.copy_(lp[2])
+        return out.copy_(toks)
+    k, tv, ti, ch = logprobs if logprobs else (0, None, None, None)
+    native().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out, allow, allow_row, k, tv, ti, ch)
     count_launches()
     return out
 
 
-def sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets):
-    """CPU sampler with the same filters (sorted-vocabulary definition) and a
-    torch generator per row in place of Philox."""
+def sample_keep_reference(x: torch.Tensor, top_k: int, top_p: float, min_p: float) -> torch.Tensor:
+    """Tokens a sampled row may draw, from its scaled logits ``x`` (-inf = masked):
+    the sorted-vocabulary definition of top-k, then top-p over the top-k survivors,
+    then min-p; ties at a threshold are kept (the kernel's radix select keeps them)."""
+    V = x.shape[0]
+    keep = torch.isfinite(x)
+    if 0 < top_k < V:
+        kth = torch.topk(x, top_k).values[-1]
+        keep &= x >= kth
+    if top_p < 1.0:
+        xs = torch.where(keep, x, torch.tensor(float("-inf")))
+        p = torch.softmax(xs, dim=-1)
+        sp, si = torch.sort(p, descending=True)
+        cum = sp.cumsum(0)
+        n_keep = int((cum - sp < top_p).sum())
+        keep &= x >= xs[si[max(n_keep, 1) - 1]]
+    if min_p > 0:
+        keep &= x >= x.max() + math.log(min_p)
+    return keep
+
+
+def sample_reference(logits, temperature, top_k, top_p, min_p, seeds, offsets, allow=None, allow_row=None,
+                     lp_k: int = 0):
+    """CPU sampler with the same filters (sorted-vocabulary definition) and a torch
+    generator per row in place of Philox.  Returns (tokens, (top_v, top_i, chosen))
+    with the log-probabilities of each row's distribution (None when lp_k = 0)."""
     B, V = logits.shape
     out = torch.empty(B, dtype=torch.int32)
+    tv = torch.full((B, max(lp_k, 1)), float("-inf"))
+    ti = torch.full((B, max(lp_k, 1)), -1, dtype=torch.int32)
+    ch = torch.empty(B)
     for r in range(B):
-        row = logits[r].float()
+        row = logits[r].float().cpu()
+        if allow is not None and int(allow_row[r]) >= 0:
+            words = allow[int(allow_row[r])].cpu().to(torch.int64) & 0xFFFFFFFF
+            bits = torch.arange(V)
+            ok = ((words[bits // 32] >> (bits % 32)) & 1).bool()
+            row = torch.where(ok, row, torch.tensor(float("-inf")))
         t = float(temperature[r])
         if t < 1e-3:
-            out[r] = int(row.argmax())
-            continue
-        x = row / t
-        keep = torch.ones(V, dtype=torch.bool)
-        if top_k is not None and 0 < int(top_k[r]) < V:
-            kth = torch.topk(x, int(top_k[r])).values[-1]
-            keep &= x >= kth
-        if top_p is not None and float(top_p[r]) < 1.0:
-            xs = torch.where(keep, x, torch.tensor(float("-inf")))
-            p = torch.softmax(xs, dim=-1)
-            sp, si = torch.sort(p, descending=True)
-            cum = sp.cumsum(0)
-            n_keep = int((cum - sp < float(top_p[r])).sum())
-            thresh = xs[si[max(n_keep, 1) - 1]]
-            keep &= x >= thresh
-        if min_p is not None and float(min_p[r]) > 0:
-            keep &= x >= x.max() + math.log(float(min_p[r]))
-        g = torch.Generator().manual_seed(int(seeds[r]) + int(offsets[r] if offsets is not None else 0))
-        e = torch.empty(V).exponential_(1.0, generator=g)
-        score = torch.where(keep, x - x.max() - e.log(), torch.tensor(float("-inf")))
-        out[r] = int(score.argmax())
-    return out
+            x, keep = row, torch.isfinite(row)
+            tok = int(row.argmax())
+        else:
+            x = row / t
+            keep = sample_keep_reference(x, int(top_k[r]) if top_k is not None else -1,
+                                         float(top_p[r]) if top_p is not None else 1.0,
+                                         float(min_p[r]) if min_p is not None else 0.0)
+            g = torch.Generator().manual_seed(int(seeds[r]) + int(offsets[r] if offsets is not None else 0))
+            e = torch.empty(V).exponential_(1.0, generator=g)
+            score = torch.where(keep, x - x.max() - e.log(), torch.tensor(float("-inf")))
+            tok = int(score.argmax())
+        out[r] = tok
+        if lp_k:
+            lp = torch.log_softmax(torch.where(keep, x, torch.tensor(float("-inf"))), dim=-1)
+            ch[r] = lp[tok]
+            n = min(lp_k, int(keep.sum()))
+            v, i = lp.topk(n)
+            tv[r, :n], ti[r, :n] = v, i.to(torch.int32)
+    return out, ((tv[:, :lp_k], ti[:, :lp_k], ch) if lp_k else None)
 
 
 def apply_penalties(logits, rows, ids, gen_counts, presence, frequency, repetition):

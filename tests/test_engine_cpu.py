@@ -324,3 +324,34 @@ def test_overlap_toggled_mid_run_drains_and_matches():
         assert [got[i] for i in ids] == want
     finally:
         eng.exit()
+
+
+def test_logprobs_and_penalties_through_engine_cpu():
+    """Log-probs ride each step's token read-back: greedy rows report their token as
+    the top entry with the chosen log-prob equal to it; a sampled row with every
+    filter and penalty reports sorted top entries that bound its chosen log-prob."""
+    from b200moe.engine.llm_engine import LLMEngine
+    eng = LLMEngine("tiny-moe", device="cpu", kvcache_block_size=16, num_kvcache_blocks=64,
+                    max_num_batched_tokens=256, max_num_seqs=8, max_model_len=256, enforce_eager=True)
+    try:
+        a = eng.add_request(list(range(5, 25)), SamplingParams(temperature=0.0, max_tokens=5, ignore_eos=True,
+                                                               logprobs=4))
+        b = eng.add_request(list(range(30, 50)), SamplingParams(
+            temperature=0.9, top_k=40, top_p=0.9, min_p=0.02, max_tokens=5, ignore_eos=True, logprobs=2, seed=3,
+            repetition_penalty=1.2, presence_penalty=0.4, frequency_penalty=0.1))
+        events = {a: [], b: []}
+        while not eng.is_finished():
+            eng.step()
+            for sid, tok, _, _, lp in eng.last_token_events:
+                events[sid].append((tok, lp))
+        assert len(events[a]) == 5 and len(events[b]) == 5
+        for tok, lp in events[a]:
+            assert len(lp["top"]) >= 4 and lp["top"][0][0] == tok
+            assert abs(lp["top"][0][1] - lp["chosen"]) < 1e-5
+            vals = [v for _, v in lp["top"]]
+            assert vals == sorted(vals, reverse=True) and vals[0] <= 0.0
+        for tok, lp in events[b]:
+            vals = [v for _, v in lp["top"]]
+            assert vals == sorted(vals, reverse=True) and lp["chosen"] <= vals[0] + 1e-6 and lp["chosen"] <= 0.0
+    finally:
+        eng.exit()

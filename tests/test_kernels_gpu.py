@@ -450,6 +450,109 @@ def test_argmax_and_sampler():
     assert int(s[1]) in top5
 
 
+def _wide_logits(B, V=151936, seed=0, step=0.25):
+    """Wide rows whose values sit on a grid of ``step`` (many exact ties at any threshold)."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn(B, V, generator=g, device=DEV) * 3.0
+    return (x / step).round() * step
+
+
+def test_penalties_kernel_matches_reference():
+    B, V, n = 4, 151936, 3000
+    g = torch.Generator().manual_seed(1)
+    logits = torch.randn(B, V, generator=g) * 4
+    rows = torch.randint(0, B, (n,), generator=g, dtype=torch.int32)
+    ids = torch.randint(0, V, (n,), generator=g, dtype=torch.int32)
+    key = rows.long() * V + ids.long()  # one entry per (row, id), as the plan packer emits
+    keep = torch.ones(n, dtype=torch.bool)
+    seen = set()
+    for j, k in enumerate(key.tolist()):
+        keep[j] = k not in seen
+        seen.add(k)
+    rows, ids = rows[keep], ids[keep]
+    counts = torch.randint(0, 4, (rows.numel(),), generator=g, dtype=torch.int32)
+    pres = torch.tensor([0.0, 0.5, -0.3, 1.2])
+    freq = torch.tensor([0.0, 0.1, 0.4, -0.2])
+    rep = torch.tensor([1.0, 1.3, 0.8, 1.7])
+    want = ops.apply_penalties(logits.clone(), rows, ids, counts, pres, freq, rep)
+    got = logits.to(DEV)
+    ops.apply_penalties(got, rows.to(DEV), ids.to(DEV), counts.to(DEV), pres.to(DEV), freq.to(DEV), rep.to(DEV))
+    torch.testing.assert_close(got.cpu(), want, atol=1e-5, rtol=1e-6)
+    untouched = torch.ones(B, V, dtype=torch.bool)
+    untouched[rows.long(), ids.long()] = False
+    assert torch.equal(got.cpu()[untouched], logits[untouched])
+
+
+@pytest.mark.parametrize("mode", ["top_p", "min_p", "top_k_top_p"])
+def test_sampler_filters_on_wide_rows_with_ties(mode):
+    """151,936-wide rows on a value grid (ties at every threshold): every draw of
+    512 seeds lies in the kept set of the sorted-vocabulary definition (ties kept),
+    and the draws follow the renormalised distribution on its most likely tokens."""
+    N, V, T = 512, 151936, 0.7
+    base = _wide_logits(1, V, seed=3)
+    logits = base.expand(N, V).contiguous()
+    temp = torch.full((N,), T, device=DEV)
+    tk = torch.full((N,), 200 if mode == "top_k_top_p" else -1, dtype=torch.int32, device=DEV)
+    tp = torch.full((N,), 0.9 if mode != "min_p" else 1.0, device=DEV)
+    mp = torch.full((N,), 0.05 if mode == "min_p" else 0.0, device=DEV)
+    seeds = torch.arange(N, dtype=torch.int64, device=DEV) * 7919 + 1
+    toks = ops.sample(logits, temp, tk, tp, mp, seeds, None).cpu().long()
+    x = base[0].cpu() / T
+    keep = ops.sample_keep_reference(x, int(tk[0]), float(tp[0]), float(mp[0]))
+    assert keep[toks].all(), "a draw fell outside the kept set"
+    p = torch.softmax(torch.where(keep, x, torch.tensor(float("-inf"))), dim=-1)
+    top = p.topk(8)
+    freq = torch.stack([(toks == int(t)).float().mean() for t in top.indices])
+    assert (freq - top.values).abs().max().item() < 0.06, (freq, top.values)
+
+
+def test_sampler_guided_masks_and_logprobs():
+    """Allowed-token masks and the fused log-probs against the CPU sampler: greedy
+    rows pick the best allowed token; sampled rows draw inside mask and filters;
+    top / chosen log-probs equal a log-softmax over the row's distribution."""
+    B, V, k = 6, 151936, 5
+    logits = _wide_logits(B, V, seed=5, step=0.001)
+    words = (V + 31) // 32
+    g = torch.Generator().manual_seed(9)
+    masks = torch.randint(-2**31, 2**31 - 1, (3, words), generator=g, dtype=torch.int64).to(torch.int32)
+    masks[2] = 0
+    masks[2, 100 // 32] = 1 << (100 % 32)          # only token 100 allowed
+    allow_row = torch.tensor([0, -1, 1, 2, 0, -1], dtype=torch.int32)
+    temp = torch.tensor([0.0, 0.0, 0.8, 0.0, 1.1, 0.9])
+    tk = torch.tensor([-1, -1, 100, -1, -1, 50], dtype=torch.int32)
+    tp = torch.tensor([1.0, 1.0, 0.95, 1.0, 0.8, 1.0])
+    mp = torch.tensor([0.0, 0.0, 0.0, 0.0, 0.0, 0.01])
+    seeds = torch.arange(B, dtype=torch.int64) + 11
+    top_v = torch.empty(B, k, device=DEV)
+    top_i = torch.empty(B, k, dtype=torch.int32, device=DEV)
+    chosen = torch.empty(B, device=DEV)
+    toks = ops.sample(logits, temp.to(DEV), tk.to(DEV), tp.to(DEV), mp.to(DEV), seeds.to(DEV), None,
+                      allow=masks.to(DEV), allow_row=allow_row.to(DEV), logprobs=(k, top_v, top_i, chosen))
+    toks, top_v, top_i, chosen = toks.cpu().long(), top_v.cpu(), top_i.cpu(), chosen.cpu()
+    bits = torch.arange(V)
+    for r in range(B):
+        row = logits[r].cpu()
+        if allow_row[r] >= 0:
+            w = masks[int(allow_row[r])].to(torch.int64) & 0xFFFFFFFF
+            ok = ((w[bits // 32] >> (bits % 32)) & 1).bool()
+            row = torch.where(ok, row, torch.tensor(float("-inf")))
+        if temp[r] < 1e-3:
+            x, keep = row, torch.isfinite(row)
+            assert toks[r] == int(row.argmax()), r
+        else:
+            x = row / float(temp[r])
+            keep = ops.sample_keep_reference(x, int(tk[r]), float(tp[r]), float(mp[r]))
+            assert keep[toks[r]], r
+        lp = torch.log_softmax(torch.where(keep, x, torch.tensor(float("-inf"))), dim=-1)
+        assert abs(float(chosen[r]) - float(lp[toks[r]])) < 1e-4, r
+        n = min(k, int(keep.sum()))
+        want = lp.topk(n)
+        torch.testing.assert_close(top_v[r, :n], want.values, atol=1e-4, rtol=1e-5)
+        torch.testing.assert_close(lp[top_i[r, :n].long()], top_v[r, :n], atol=1e-4, rtol=1e-5)  # ids match values
+        assert (top_i[r, n:] == -1).all() and torch.isinf(top_v[r, n:]).all(), r
+    assert toks[3] == 100 and abs(float(chosen[3])) < 1e-6  # a single allowed token has log-prob 0
+
+
 def test_sampler_distribution():
     """Exponential race draws follow softmax(logits / T) over the kept set."""
     V, N = 8, 4000
