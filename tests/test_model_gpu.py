@@ -235,10 +235,15 @@ def test_qwen3_30b_shape_matches_oracle(monkeypatch):
         lg = gpu.compute_logits(gpu(_plan_inputs(rows, tables, bs, "cuda", all_logits), pools[1])).float().cpu()
         torch.cuda.synchronize()
         ops.check_status(torch.device("cuda", 0))
+        # the KV every kernel wrote so far matches the oracle's (attention inputs of later steps)
+        kv_g, kv_c = pools[1].data.cpu().float(), pools[0].data.float()
+        print(f"kv max abs diff {(kv_g - kv_c).abs().max().item():.4f}")
+        torch.testing.assert_close(kv_g, kv_c, atol=5e-2, rtol=5e-2)
         monkeypatch.setattr(ops, "BF16_DENSE_ROWS", 2048)
         monkeypatch.setattr(Qwen3MoeForCausalLM, "BF16_EXPERT_ROWS", 512)
         cos = torch.nn.functional.cosine_similarity(lc, lg, dim=-1)
-        print(f"step rows={cos.numel()} cos min {cos.min().item():.5f} mean {cos.mean().item():.6f}")
+        print(f"step rows={cos.numel()} cos min {cos.min().item():.5f} mean {cos.mean().item():.6f}"
+              + ("" if all_logits else f" per row {[round(c, 5) for c in cos.tolist()]}"))
         if all_logits:
             assert cos.mean().item() > 0.9995 and cos.min().item() > 0.998, (cos.mean().item(), cos.min().item())
         else:
@@ -248,4 +253,3 @@ def test_qwen3_30b_shape_matches_oracle(monkeypatch):
         agree += int(((lc.argmax(-1) == lg.argmax(-1)) & clear).sum())
         counted += int(clear.sum())
     assert counted > 400 and agree / counted >= 0.99, (agree, counted)
-    torch.testing.assert_close(pools[1].data.cpu().float(), pools[0].data.float(), atol=5e-2, rtol=5e-2)
