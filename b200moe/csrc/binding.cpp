@@ -129,7 +129,8 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
 // slot buffer (peer memory): slot_code = rank * slot_cap + slot.
 void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor group_count, Tensor group_offset,
                        int64_t bn, Tensor slot_code, Tensor slot_w, std::vector<int64_t> peer_ptrs, int64_t slot_cap,
-                       int64_t ld_out, Tensor status, bool a_tiled) {
+                       int64_t ld_out, Tensor status, bool a_tiled, c10::optional<Tensor> ep_epoch,
+                       c10::optional<Tensor> ep_cta_done, std::vector<int64_t> done_ptrs, int64_t ep_rank) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CONTIG(weight);
   TORCH_CHECK(weight.dim() == 3 && weight.scalar_type() == torch::kFloat8_e4m3fn, "expert weights must be [E, N, K] e4m3");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.scalar_type() == torch::kBFloat16, "x must be [rows, K] bf16");
@@ -138,7 +139,7 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
   const int64_t groups = weight.size(0), N = weight.size(1), K = weight.size(2);
   TORCH_CHECK(x.size(1) == K, "K mismatch");
   TORCH_CHECK(weight_scale.numel() == groups * (N / 128) * (K / 128), "weight_scale shape");
-  if (x.size(0) == 0) return;
+  TORCH_CHECK(x.size(0) > 0, "gemm_peer_scatter: x needs at least one row (the grid releases the done epoch)");
   c10::cuda::CUDAGuard guard(x.device());
   b200::GemmLaunch L{};
   L.args.a_scale = weight_scale.data_ptr<float>();
@@ -160,6 +161,15 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
   L.args.a_base = weight.data_ptr();
   L.args.slot_cap = (int)slot_cap;
   for (size_t i = 0; i < peer_ptrs.size(); ++i) L.args.peer_out[i] = reinterpret_cast<void*>(peer_ptrs[i]);
+  if (ep_epoch.has_value()) {  // the last CTA releases this rank's done epoch to every source
+    TORCH_CHECK(ep_cta_done.has_value() && done_ptrs.size() == peer_ptrs.size(), "done release arguments");
+    CHECK_DT((*ep_cta_done), torch::kInt32);
+    L.args.ep_epoch = reinterpret_cast<const uint32_t*>(ep_epoch->data_ptr());
+    L.args.ep_cta_done = ep_cta_done->data_ptr<int>();
+    for (size_t i = 0; i < done_ptrs.size(); ++i) L.args.ep_done[i] = reinterpret_cast<void*>(done_ptrs[i]);
+    L.args.ep_rank = (int)ep_rank;
+    L.args.ep_world = (int)done_ptrs.size();
+  }
   L.a = weight.data_ptr();
   L.a_row_stride_bytes = K;
   L.b = x.data_ptr();
@@ -173,17 +183,24 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
   b200::gemm_tc_launch(L, stream());
 }
 
-b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor send_cursor, Tensor done_blocks,
-                     Tensor epoch, Tensor status, Tensor wait_ns, std::vector<int64_t> recv_x,
-                     std::vector<int64_t> recv_meta,
+b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor ge_local, Tensor send_cursor,
+                     Tensor ecur, Tensor done_blocks, Tensor epoch, Tensor status, Tensor wait_ns,
+                     std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta,
                      std::vector<int64_t> counts, std::vector<int64_t> flags, std::vector<int64_t> done) {
-  TORCH_CHECK(dims.size() == 5, "dims = (world, rank, hidden, cap, slot_cap)");
+  TORCH_CHECK(dims.size() == 7, "dims = (world, rank, hidden, cap, slot_cap, num_local, num_experts)");
   b200::EpArgs a{};
   a.world = (int)dims[0];
   a.rank = (int)dims[1];
   a.hidden = (int)dims[2];
   a.cap = (int)dims[3];
   a.slot_cap = (int)dims[4];
+  a.num_local = (int)dims[5];
+  a.num_experts = (int)dims[6];
+  TORCH_CHECK(a.num_local >= 1 && a.num_local <= b200::kEpMaxLocalExperts && a.num_experts >= a.num_local,
+              "bad expert counts");
+  CHECK_DT(ge_local, torch::kInt32); CHECK_DT(ecur, torch::kInt32);
+  TORCH_CHECK(owner.numel() >= a.num_experts && g2l.numel() >= a.num_experts && ge_local.numel() >= a.num_experts &&
+              ecur.numel() >= a.num_experts, "per-expert tables must hold num_experts entries");
   TORCH_CHECK(a.world >= 1 && a.world <= b200::kEpMaxWorld && a.rank >= 0 && a.rank < a.world, "bad world/rank");
   TORCH_CHECK((int)recv_x.size() == a.world && (int)recv_meta.size() == a.world && (int)counts.size() == a.world &&
               (int)flags.size() == a.world && (int)done.size() == a.world, "one pointer per rank");
@@ -191,7 +208,9 @@ b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor
   CHECK_DT(done_blocks, torch::kInt32); CHECK_DT(status, torch::kInt32);
   a.owner = owner.data_ptr<int>();
   a.g2l = g2l.data_ptr<int>();
+  a.ge_local = ge_local.data_ptr<int>();
   a.send_cursor = send_cursor.data_ptr<int>();
+  a.ecur = ecur.data_ptr<int>();
   a.done_blocks = done_blocks.data_ptr<int>();
   a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
   a.status = status.data_ptr<int>();
@@ -208,11 +227,12 @@ b200::EpArgs ep_args(std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor
   return a;
 }
 
-#define EP_ARGS_DECL std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor send_cursor, Tensor done_blocks, \
-  Tensor epoch, Tensor status, Tensor wait_ns, std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta, \
+#define EP_ARGS_DECL std::vector<int64_t> dims, Tensor owner, Tensor g2l, Tensor ge_local, Tensor send_cursor, \
+  Tensor ecur, Tensor done_blocks, Tensor epoch, Tensor status, Tensor wait_ns, std::vector<int64_t> recv_x, \
+  std::vector<int64_t> recv_meta, \
   std::vector<int64_t> counts, std::vector<int64_t> flags, std::vector<int64_t> done
-#define EP_ARGS ep_args(dims, owner, g2l, send_cursor, done_blocks, epoch, status, wait_ns, recv_x, recv_meta, counts, \
-                        flags, done)
+#define EP_ARGS ep_args(dims, owner, g2l, ge_local, send_cursor, ecur, done_blocks, epoch, status, wait_ns, recv_x, \
+                        recv_meta, counts, flags, done)
 
 void ep_dispatch(EP_ARGS_DECL, Tensor x, Tensor ids, Tensor w) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16); CHECK_DT(ids, torch::kInt32);
@@ -223,19 +243,18 @@ void ep_dispatch(EP_ARGS_DECL, Tensor x, Tensor ids, Tensor w) {
                     stream());
 }
 
-void ep_count(EP_ARGS_DECL, Tensor local_counts) {
-  CHECK_DT(local_counts, torch::kInt32);
-  b200::ep_count(EP_ARGS, local_counts.data_ptr<int>(), stream());
-}
-
-void ep_scatter(EP_ARGS_DECL, Tensor local_counts, Tensor cursor, Tensor x_perm, Tensor slot_code, Tensor slot_w,
+void ep_scatter(EP_ARGS_DECL, Tensor local_counts, Tensor x_perm, Tensor slot_code, Tensor slot_w,
                 Tensor offsets_out) {
   CHECK_CONTIG(x_perm); CHECK_DT(slot_code, torch::kInt32); CHECK_DT(slot_w, torch::kFloat32);
+  CHECK_DT(local_counts, torch::kInt32); CHECK_DT(offsets_out, torch::kInt32);
   auto a = EP_ARGS;
   TORCH_CHECK(x_perm.size(0) >= (int64_t)a.world * a.cap, "x_perm must hold world * cap rows");
-  b200::ep_scatter(a, local_counts.data_ptr<int>(), cursor.data_ptr<int>(), (int)local_counts.numel(),
-                   x_perm.data_ptr(), slot_code.data_ptr<int>(), slot_w.data_ptr<float>(),
-                   offsets_out.data_ptr<int>(), a.world * a.cap, stream());
+  TORCH_CHECK(slot_code.numel() >= (int64_t)a.world * a.cap && slot_w.numel() >= (int64_t)a.world * a.cap,
+              "slot_code / slot_w must hold world * cap rows");
+  TORCH_CHECK(local_counts.numel() >= a.num_local && offsets_out.numel() >= a.num_local + 1,
+              "local_counts [El], offsets_out [El + 1]");
+  b200::ep_scatter(a, local_counts.data_ptr<int>(), x_perm.data_ptr(), slot_code.data_ptr<int>(),
+                   slot_w.data_ptr<float>(), offsets_out.data_ptr<int>(), a.world * a.cap, stream());
 }
 
 void ep_signal(EP_ARGS_DECL) { b200::ep_signal(EP_ARGS, stream()); }
@@ -275,7 +294,8 @@ void rmsnorm(Tensor x, c10::optional<Tensor> residual_in, Tensor weight, Tensor 
 }
 
 void moe_combine(Tensor slots, int64_t topk, Tensor residual, Tensor weight, Tensor out, double eps,
-                 c10::optional<Tensor> zero) {
+                 c10::optional<Tensor> zero, c10::optional<Tensor> wait_flags, c10::optional<Tensor> wait_epoch,
+                 c10::optional<Tensor> wait_status, c10::optional<Tensor> wait_ns) {
   CHECK_CUDA(slots); CHECK_CONTIG(slots); CHECK_CONTIG(residual); CHECK_CONTIG(out);
   CHECK_DT(slots, torch::kBFloat16); CHECK_DT(residual, torch::kBFloat16);
   const int H = (int)residual.size(-1);
@@ -288,8 +308,21 @@ void moe_combine(Tensor slots, int64_t topk, Tensor residual, Tensor weight, Ten
     zp = zero->data_ptr<int>();
     zn = (int)zero->numel();
   }
+  b200::CombineWait cw;
+  if (wait_flags.has_value()) {  // expert parallel: wait for every owner's done epoch first
+    TORCH_CHECK(wait_epoch.has_value() && wait_status.has_value(), "wait needs epoch and status");
+    CHECK_DT((*wait_flags), torch::kInt32); CHECK_DT((*wait_status), torch::kInt32);
+    cw.flags = reinterpret_cast<const uint32_t*>(wait_flags->data_ptr<int>());
+    cw.epoch = reinterpret_cast<const uint32_t*>(wait_epoch->data_ptr());
+    cw.world = (int)wait_flags->numel();
+    cw.status = wait_status->data_ptr<int>();
+    if (wait_ns.has_value()) {
+      TORCH_CHECK(wait_ns->scalar_type() == torch::kInt64 && wait_ns->numel() >= 2 * cw.world, "wait_ns [2 * world]");
+      cw.wait_ns = reinterpret_cast<unsigned long long*>(wait_ns->data_ptr<int64_t>());
+    }
+  }
   b200::moe_combine_add_rmsnorm(slots.data_ptr(), (int)topk, residual.data_ptr(), weight.data_ptr(),
-                                out.data_ptr(), T, H, (float)eps, stream(), zp, zn);
+                                out.data_ptr(), T, H, (float)eps, stream(), zp, zn, cw);
 }
 
 void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tensor q_norm_w, Tensor k_norm_w,
@@ -635,7 +668,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
   m.def("ep_dispatch", &ep_dispatch);
-  m.def("ep_count", &ep_count);
   m.def("ep_scatter", &ep_scatter);
   m.def("ep_signal", &ep_signal);
   m.def("ep_wait_done", &ep_wait_done);

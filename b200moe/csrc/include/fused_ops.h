@@ -37,9 +37,19 @@ void embed_gather(const int* ids, const void* table, void* out, int T, int H, in
 // output), reduced and rounded to bf16 before the residual add.
 void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* res_out, int T, int H,
              float eps, cudaStream_t s, const float* part = nullptr, int splits = 0);
+// Expert parallel: before combining, wait for every owner's done epoch, flags[r] >= *epoch
+// for r < world (bounded; the time waited on owner r is added to wait_ns[world + r]).
+struct CombineWait {
+  const uint32_t* flags = nullptr;   // this rank's done array [world]; null = no wait
+  const uint32_t* epoch = nullptr;
+  int world = 0;
+  int* status = nullptr;
+  unsigned long long* wait_ns = nullptr;
+};
+// T == 0 with a wait still launches one block, which only waits.
 void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
                              int H, float eps, cudaStream_t s,
-                             int* zero_buf = nullptr, int zero_n = 0);
+                             int* zero_buf = nullptr, int zero_n = 0, const CombineWait& cw = CombineWait{});
 void qknorm_rope_kvstore(const QkvArgs& a, int T, cudaStream_t s);
 void router_topk(const float* logits, int ld, int T, int E, int topk, bool renorm, int* ids, float* weights,
                  int* counts, cudaStream_t s);

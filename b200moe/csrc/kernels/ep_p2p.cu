@@ -3,31 +3,37 @@
 // Every rank owns a symmetric set of buffers (same layout on all ranks, peers'
 // copies mapped into this process):
 //   recv_x    [W * cap, H] bf16   rows routed to this rank's experts, segment per source
-//   recv_meta [W * cap, 4] int32  (global expert, source slot, weight bits, -)
-//   counts    [W] int32           rows received from each source
+//   recv_meta [W * cap, 4] int32  (global expert, source slot, weight bits, index among
+//                                 the source's rows for that expert)
+//   counts    [W * El] int32      rows from each source for each local expert
 //   flags     [W] uint32          dispatch epoch written by each source
 //   done      [W] uint32          combine epoch written by each expert owner
 //   slots     [cap, H] bf16       this rank's (token, k) slots, written by owners
 //
-// Per MoE layer (all launches stream-ordered, no host sync, graph-capturable):
+// Per MoE layer: five stream-ordered launches, no host sync, graph-capturable.
 //   ep_dispatch   warp per routed (token, k): claim a position in the owner's
-//                 segment for this source, store the row and its metadata with
-//                 plain 16-byte stores into the peer's memory; the last block
-//                 publishes counts and the epoch flag (release, system scope).
-//   ep_count      owner side: bounded wait for every source's flag, count the
-//                 received rows per local expert.
-//   ep_scatter    owner side: expert-sorted copy of the received rows (local)
-//                 plus the combine address (source, slot) and routing weight.
+//                 segment for this source and an index among this source's rows
+//                 for the expert, store the row and its metadata with plain
+//                 16-byte stores into the peer's memory; the last block writes
+//                 this source's per-expert counts into every owner's count
+//                 matrix and releases the epoch flag (release, system scope).
+//   ep_scatter    owner side: every block waits (bounded) for every source's
+//                 flag, derives expert offsets from the count matrix (no
+//                 counting pass), and copies each received row straight to its
+//                 expert-sorted position with its combine address and weight;
+//                 block 0 publishes the per-expert counts and offsets.
 //   gemm_tc x 2   gate/up + SiLU, then down whose epilogue writes each weighted
-//                 row straight into the source rank's slots (peer stores).
-//   ep_signal     owner side: release the done epoch to every source.
-//   ep_wait_done  source side: bounded wait for every owner's done epoch; then
-//                 the usual fixed-order moe_combine runs on local memory.
+//                 row straight into the source rank's slots (peer stores); the
+//                 down GEMM's last CTA releases this rank's done epoch to every
+//                 source.
+//   moe_combine   source side: waits (bounded) for every owner's done epoch, then
+//                 the fixed-order top-k sum + residual + next RMSNorm on local memory.
 //
 // Epochs live in device memory (incremented by ep_dispatch), so a replayed CUDA
 // graph keeps advancing them.  All waits are bounded (%globaltimer); on expiry
 // the kernel records a status code and returns.  Peer memory is accessed with
-// plain ld/st only (no TMA).
+// plain ld/st only (no TMA).  ep_signal / ep_wait_done are the stand-alone forms
+// of the release and the wait.
 //
 // Reference: the replicated-hidden all_reduce combine of
 // nanovllm/models/qwen3_moe.py:414-418 (one NCCL all-reduce per layer).
@@ -39,36 +45,10 @@
 #include <string>
 
 #include "sm100.cuh"
+#include "ep_sync.cuh"
 #include "ep_p2p.h"
 
 namespace b200 {
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Bounded wait until *p >= want (wrap-safe compare).  False on timeout.  The
-// time spent is added to *waited (when not null).
-__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t want, int* status,
-                                           unsigned long long* waited) {
-  const uint64_t t0 = globaltimer_ns();
-  bool ok = true;
-  while ((int32_t)(ld_acquire_sys(p) - want) < 0) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      record_status(status, kStatusTimeoutFlag);
-      ok = false;
-      break;
-    }
-    __nanosleep(64);
-  }
-  if (waited != nullptr) atomicAdd(waited, (unsigned long long)(globaltimer_ns() - t0));
-  return ok;
-}
 
 __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ ids,
                                    const float* __restrict__ w, int T, int topk) {
@@ -82,10 +62,18 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
   const int H8 = a.hidden / 8;
   for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < T * topk; p += gridDim.x * warps) {
     const int ge = ids[p];
+    if (ge < 0 || ge >= a.num_experts) {
+      if (lane == 0) record_status(a.status, kStatusBadShape);
+      continue;
+    }
     const int dest = a.owner[ge];
-    int pos = 0;
-    if (lane == 0) pos = atomicAdd(&a.send_cursor[dest], 1);
+    int pos = 0, idx = 0;
+    if (lane == 0) {
+      pos = atomicAdd(&a.send_cursor[dest], 1);
+      idx = atomicAdd(&a.ecur[ge], 1);
+    }
     pos = __shfl_sync(0xffffffffu, pos, 0);
+    idx = __shfl_sync(0xffffffffu, idx, 0);
     if (pos >= a.cap) {  // the host sizes cap for the worst case; never write past it
       if (lane == 0) record_status(a.status, kStatusBadShape);
       continue;
@@ -95,7 +83,7 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.recv_x[dest]) + row * a.hidden);
     for (int i = lane; i < H8; i += 32) dst[i] = src[i];
     if (lane == 0) {
-      int4 m = make_int4(ge, p, __float_as_int(w[p]), 0);
+      int4 m = make_int4(ge, p, __float_as_int(w[p]), idx);
       reinterpret_cast<int4*>(a.recv_meta[dest])[row] = m;
     }
   }
@@ -106,13 +94,19 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
     last_s = atomicAdd(a.done_blocks, 1) == (int)gridDim.x - 1;
   }
   __syncthreads();
-  if (last_s && threadIdx.x == 0) {
-    __threadfence_system();
-    for (int r = 0; r < a.world; ++r) {
-      const int n = min(atomicAdd(&a.send_cursor[r], 0), a.cap);
-      volatile int* cnt = reinterpret_cast<volatile int*>(a.counts[r]);
-      cnt[a.rank] = n;
-    }
+  if (!last_s) return;
+  // last block: every other block's rows are out.  Publish this source's row
+  // count per expert into each owner's count matrix, then the epoch flags.
+  __threadfence_system();
+  for (int ge = threadIdx.x; ge < a.num_experts; ge += blockDim.x) {
+    const int dest = a.owner[ge];
+    volatile int* cnt = reinterpret_cast<volatile int*>(a.counts[dest]);
+    cnt[a.rank * a.num_local + a.ge_local[ge]] = atomicAdd(&a.ecur[ge], 0);
+    a.ecur[ge] = 0;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
     __threadfence_system();
     for (int r = 0; r < a.world; ++r) st_release_sys(reinterpret_cast<uint32_t*>(a.flags[r]) + a.rank, epoch);
     for (int r = 0; r < a.world; ++r) a.send_cursor[r] = 0;
@@ -121,57 +115,86 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
   }
 }
 
-// One block per source segment: wait for the source's epoch, count rows per local expert.
-__global__ void ep_count_kernel(const EpArgs a, int* __restrict__ local_counts) {
-  __shared__ int ok_s;
-  __shared__ int n_s;
-  const int src = blockIdx.x;
-  const uint32_t epoch = *a.epoch;
-  uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags[a.rank]);
-  if (threadIdx.x == 0) {
-    ok_s = wait_epoch(my_flags + src, epoch, a.status, a.wait_ns ? a.wait_ns + src : nullptr) ? 1 : 0;
-    n_s = ok_s ? reinterpret_cast<volatile int*>(a.counts[a.rank])[src] : 0;
-  }
-  __syncthreads();
-  const int n = n_s;
-  const int4* meta = reinterpret_cast<const int4*>(a.recv_meta[a.rank]) + (int64_t)src * a.cap;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int le = a.g2l[meta[i].x];
-    if (le >= 0) atomicAdd(&local_counts[le], 1);
-  }
-}
-
-// Expert-sorted copy of the received rows; one warp per row.
-__global__ void ep_scatter_kernel(const EpArgs a, const int* __restrict__ local_counts, int* __restrict__ cursor,
-                                  int num_local, __nv_bfloat16* __restrict__ x_perm, int* __restrict__ slot_code,
-                                  float* __restrict__ slot_w, int* __restrict__ offsets_out) {
+// Owner side.  Every block waits for every source, then places each received row at
+//   offset[expert] + (rows of that expert from lower-numbered sources) + its index
+// among its source's rows for the expert, all read from the count matrix: the layout
+// is the same whatever the arrival order.  One warp per row.
+__global__ void ep_scatter_kernel(const EpArgs a, int* __restrict__ local_counts, __nv_bfloat16* __restrict__ x_perm,
+                                  int* __restrict__ slot_code, float* __restrict__ slot_w,
+                                  int* __restrict__ offsets_out) {
   __shared__ int offs[kEpMaxLocalExperts + 1];
+  __shared__ int base[kEpMaxWorld * kEpMaxLocalExperts];  // rows of expert e from sources < s, at s * El + e
   __shared__ int seg[kEpMaxWorld + 1];
-  if (threadIdx.x == 0) {
-    int s = 0;
-    for (int e = 0; e < num_local; ++e) { offs[e] = s; s += local_counts[e]; }
-    offs[num_local] = s;
-    int r = 0;
-    const volatile int* cnt = reinterpret_cast<const volatile int*>(a.counts[a.rank]);
-    for (int src = 0; src < a.world; ++src) { seg[src] = r; r += cnt[src]; }
-    seg[a.world] = r;
+  __shared__ int ok_s;
+  const int W = a.world, El = a.num_local;
+  const uint32_t epoch = *a.epoch;
+  const uint32_t* my_flags = reinterpret_cast<const uint32_t*>(a.flags[a.rank]);
+  if (threadIdx.x == 0) ok_s = 1;
+  __syncthreads();
+  if (threadIdx.x < W) {
+    // block 0 charges the wait to the source it waited for (the wait accounting)
+    if (!wait_epoch(my_flags + threadIdx.x, epoch, a.status,
+                    (blockIdx.x == 0 && a.wait_ns) ? a.wait_ns + threadIdx.x : nullptr))
+      ok_s = 0;
   }
   __syncthreads();
-  if (blockIdx.x == 0 && offsets_out != nullptr)
-    for (int e = threadIdx.x; e <= num_local; e += blockDim.x) offsets_out[e] = offs[e];
+  if (!ok_s) {  // a source never arrived (status recorded): leave the layer's expert work empty
+    if (blockIdx.x == 0)
+      for (int e = threadIdx.x; e <= El; e += blockDim.x) {
+        if (offsets_out != nullptr) offsets_out[e] = 0;
+        if (e < El) local_counts[e] = 0;
+      }
+    return;
+  }
+  const volatile int* cnt = reinterpret_cast<const volatile int*>(a.counts[a.rank]);
+  // per expert: sources in order (rank-major prefix), then the expert prefix
+  for (int e = threadIdx.x; e < El; e += blockDim.x) {
+    int run = 0;
+    for (int src = 0; src < W; ++src) {
+      base[src * El + e] = run;
+      run += cnt[src * El + e];
+    }
+    offs[e] = run;  // total of expert e, turned into the prefix below
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int sum = 0;
+    for (int e = 0; e < El; ++e) { const int n = offs[e]; offs[e] = sum; sum += n; }
+    offs[El] = sum;
+    int r = 0;
+    for (int src = 0; src < W; ++src) {
+      seg[src] = r;
+      int n = 0;
+      for (int e = 0; e < El; ++e) n += cnt[src * El + e];
+      r += min(n, a.cap);
+    }
+    seg[W] = r;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e <= El; e += blockDim.x) {
+      if (offsets_out != nullptr) offsets_out[e] = offs[e];
+      if (e < El) local_counts[e] = offs[e + 1] - offs[e];
+    }
+  }
   const int lane = threadIdx.x & 31;
-  const int total = seg[a.world];
+  const int total = seg[W];
   const int H8 = a.hidden / 8;
   for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += gridDim.x * (blockDim.x >> 5)) {
     int src = 0;
     while (seg[src + 1] <= i) ++src;
     const int64_t row = (int64_t)src * a.cap + (i - seg[src]);
     const int4 m = reinterpret_cast<const int4*>(a.recv_meta[a.rank])[row];
-    const int le = a.g2l[m.x];
-    if (le < 0) continue;
-    int pos = 0;
-    if (lane == 0) pos = offs[le] + atomicAdd(&cursor[le], 1);
-    pos = __shfl_sync(0xffffffffu, pos, 0);
+    const int le = (m.x >= 0 && m.x < a.num_experts) ? a.g2l[m.x] : -1;
+    if (le < 0) {
+      if (lane == 0) record_status(a.status, kStatusBadShape);
+      continue;
+    }
+    const int pos = offs[le] + base[src * El + le] + m.w;
+    if (m.w < 0 || pos >= offs[le + 1]) {
+      if (lane == 0) record_status(a.status, kStatusBadShape);
+      continue;
+    }
     const uint4* s = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.recv_x[a.rank]) +
                                                     row * a.hidden);
     uint4* d = reinterpret_cast<uint4*>(x_perm + (int64_t)pos * a.hidden);
@@ -217,19 +240,18 @@ void ep_dispatch(const EpArgs& a, const void* x, const int* ids, const float* w,
   check("ep_dispatch");
 }
 
-void ep_count(const EpArgs& a, int* local_counts, cudaStream_t s) {
+void ep_scatter(const EpArgs& a, int* local_counts, void* x_perm, int* slot_code, float* slot_w, int* offsets_out,
+                int max_rows, cudaStream_t s) {
   check_args(a);
-  ep_count_kernel<<<a.world, 256, 0, s>>>(a, local_counts);
-  check("ep_count");
-}
-
-void ep_scatter(const EpArgs& a, const int* local_counts, int* cursor, int num_local, void* x_perm, int* slot_code,
-                float* slot_w, int* offsets_out, int max_rows, cudaStream_t s) {
-  check_args(a);
-  if (num_local > kEpMaxLocalExperts) throw std::runtime_error("ep: too many local experts");
-  const int blocks = std::max(1, std::min(2048, (max_rows + 7) / 8));
-  ep_scatter_kernel<<<blocks, 256, 0, s>>>(a, local_counts, cursor, num_local,
-                                           static_cast<__nv_bfloat16*>(x_perm), slot_code, slot_w, offsets_out);
+  if (a.num_local < 1 || a.num_local > kEpMaxLocalExperts) throw std::runtime_error("ep: local experts out of range");
+  // two blocks per SM walk the rows grid-stride: every block waits and reads the
+  // count matrix, so fewer blocks mean less redundant work at decode sizes
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int blocks = std::max(1, std::min(2 * sms, (max_rows + 7) / 8));
+  ep_scatter_kernel<<<blocks, 256, 0, s>>>(a, local_counts, static_cast<__nv_bfloat16*>(x_perm), slot_code, slot_w,
+                                           offsets_out);
   check("ep_scatter");
 }
 

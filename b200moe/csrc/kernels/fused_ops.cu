@@ -27,6 +27,7 @@
 
 #include "sm100.cuh"
 #include "pdl.cuh"
+#include "ep_sync.cuh"
 #include "fused_ops.h"
 
 namespace b200 {
@@ -145,14 +146,25 @@ template <int NT, int VPT>
 __global__ void __launch_bounds__(NT) moe_combine_kernel(const bf16* __restrict__ slots, int topk,
                                                          bf16* residual, const bf16* __restrict__ w,
                                                          bf16* __restrict__ out, int H, float eps,
-                                                         int* __restrict__ zero_buf, int zero_n) {
+                                                         int* __restrict__ zero_buf, int zero_n, int T,
+                                                         CombineWait cw) {
   pdl_enter();
+  // expert parallel: the slots are written by the experts' owners; wait for every
+  // owner's done epoch first (block 0 charges the wait to the owner it waited for)
+  if (cw.flags != nullptr) {
+    const uint32_t epoch = *cw.epoch;
+    if (threadIdx.x < cw.world)
+      wait_epoch(cw.flags + threadIdx.x, epoch, cw.status,
+                 (blockIdx.x == 0 && cw.wait_ns) ? cw.wait_ns + cw.world + threadIdx.x : nullptr);
+    __syncthreads();
+  }
   // the layer's routing counters are dead once the down GEMM has run: clear them
   // for the next layer here instead of in a separate fill launch
   if (blockIdx.x == 0 && zero_buf != nullptr)
     for (int i = threadIdx.x; i < zero_n; i += NT) zero_buf[i] = 0;
   __shared__ float red[NT / 32];
   const int t = blockIdx.x;
+  if (t >= T) return;  // the one block of an empty batch that only waits
   const size_t base = (size_t)t * H;
   float v[VPT][8];
   float ss = 0.f;
@@ -642,15 +654,18 @@ void rmsnorm(const void* x, const void* res_in, const void* w, void* out, void* 
 }
 
 void moe_combine_add_rmsnorm(const void* slots, int topk, void* residual, const void* w, void* out, int T,
-                             int H, float eps, cudaStream_t s, int* zero_buf, int zero_n) {
-  if (T == 0) return;
+                             int H, float eps, cudaStream_t s, int* zero_buf, int zero_n, const CombineWait& cw) {
+  if (T == 0 && cw.flags == nullptr) return;
+  if (cw.flags != nullptr && (cw.world < 1 || cw.world > 32 || cw.epoch == nullptr))
+    throw std::runtime_error("moe_combine: bad expert-parallel wait arguments");
   const bf16 *S = (const bf16*)slots, *W = (const bf16*)w;
   bf16 *R = (bf16*)residual, *O = (bf16*)out;
-  if (H == 2048) pdl_launch(moe_combine_kernel<256, 1>, T, 256, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
-  else if (H == 4096) pdl_launch(moe_combine_kernel<256, 2>, T, 256, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
-  else if (H == 256) pdl_launch(moe_combine_kernel<32, 1>, T, 32, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
-  else if (H == 512) pdl_launch(moe_combine_kernel<64, 1>, T, 64, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
-  else if (H == 1024) pdl_launch(moe_combine_kernel<128, 1>, T, 128, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n);
+  const int G = T > 0 ? T : 1;
+  if (H == 2048) pdl_launch(moe_combine_kernel<256, 1>, G, 256, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n, T, cw);
+  else if (H == 4096) pdl_launch(moe_combine_kernel<256, 2>, G, 256, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n, T, cw);
+  else if (H == 256) pdl_launch(moe_combine_kernel<32, 1>, G, 32, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n, T, cw);
+  else if (H == 512) pdl_launch(moe_combine_kernel<64, 1>, G, 64, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n, T, cw);
+  else if (H == 1024) pdl_launch(moe_combine_kernel<128, 1>, G, 128, 0, s, S, topk, R, W, O, H, eps, zero_buf, zero_n, T, cw);
   else throw std::runtime_error("moe_combine: unsupported hidden size " + std::to_string(H));
   check_launch("moe_combine_add_rmsnorm");
 }

@@ -44,6 +44,7 @@
 
 #include "sm100.cuh"
 #include "pdl.cuh"
+#include "ep_sync.cuh"
 #include "gemm_tc.h"
 
 namespace b200 {
@@ -732,10 +733,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   }
 
   tc_fence_before();
+  if (args.ep_epoch != nullptr) __threadfence_system();  // this thread's peer stores, before the CTA's arrival
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (args.ep_epoch != nullptr && threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(args.ep_cta_done, 1) == (int)gridDim.x - 1) {  // every CTA's rows are out
+      *args.ep_cta_done = 0;
+      __threadfence_system();
+      const uint32_t epoch = *args.ep_epoch;
+      for (int r = 0; r < args.ep_world; ++r)
+        st_release_sys(reinterpret_cast<uint32_t*>(args.ep_done[r]) + args.ep_rank, epoch);
+    }
   }
 }
 

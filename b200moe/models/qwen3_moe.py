@@ -356,7 +356,8 @@ class Qwen3MoeForCausalLM(nn.Module):
             # the combine kernel also clears the routing counters for the next layer
             counts = self._buf("counts", (2 * a.num_experts + 1,), torch.int32) if self.ep is None else None
             out = ops.moe_combine_add_rmsnorm(slots, a.num_experts_per_tok, residual, next_norm, eps,
-                                              out=self._buf("x", (T, a.hidden_size), self.dtype), zero=counts)
+                                              out=self._buf("x", (T, a.hidden_size), self.dtype), zero=counts,
+                                              wait=self.ep.combine_wait() if self.ep is not None else None)
             self._counts_clear = counts is not None
             return out
 

@@ -349,9 +349,11 @@ def rmsnorm(x, weight, eps, residual=None, out=None):
     return out
 
 
-def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None, zero=None):
+def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None, zero=None, wait=None):
     """residual += sum_k slots[t, k] (fixed order); return rmsnorm(residual).
-    ``zero``: an int32 buffer the kernel also clears (the layer's routing counters)."""
+    ``zero``: an int32 buffer the kernel also clears (the layer's routing counters).
+    ``wait`` = (done flags [W], epoch, status, wait_ns): expert parallelism, the kernel
+    first waits (bounded) until every owner has released this layer's epoch."""
     T, H = residual.shape
     if not residual.is_cuda:
         if zero is not None:
@@ -360,7 +362,8 @@ def moe_combine_add_rmsnorm(slots, topk, residual, weight, eps, out=None, zero=N
         return rmsnorm(moe, weight, eps, residual=residual, out=out)
     if out is None:
         out = torch.empty_like(residual)
-    native().moe_combine(slots, topk, residual, weight, out, eps, zero)
+    flags, epoch, status, wait_ns = wait if wait is not None else (None, None, None, None)
+    native().moe_combine(slots, topk, residual, weight, out, eps, zero, flags, epoch, status, wait_ns)
     count_launches()
     return out
 

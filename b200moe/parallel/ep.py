@@ -43,17 +43,21 @@ class ExpertParallel:
         model = runner.model
         owner = torch.empty(self.E, dtype=torch.int64)
         g2l = torch.full((self.E,), -1, dtype=torch.int32)
+        ge_local = torch.full((self.E,), -1, dtype=torch.int32)  # index of each expert on its owner
         placement = [None] * self.world
         from b200moe.engine.model_runner import expert_placement
         for r in range(self.world):
             placement[r] = expert_placement(runner.config, r, self.world)
             for le, ge in enumerate(placement[r]):
                 owner[ge] = r
+                ge_local[ge] = le
                 if r == self.rank:
                     g2l[ge] = le
         assert placement[self.rank] == model.expert_ids
         self.owner = owner.to(self.device)
         self.g2l = g2l.to(self.device)
+        self.ge_local = ge_local.to(self.device)
+        self.num_local = len(placement[self.rank])
         cuda = self.device.type == "cuda"
         if backend == "loop" or not cuda:
             self.backend = "reference"
@@ -105,6 +109,10 @@ class ExpertParallel:
         dist.all_reduce(part)
         start = sum(sizes[:self.rank])
         return part[start:start + T].sum(dim=1).to(x.dtype)
+
+    def combine_wait(self):
+        """What the combine kernel waits on before reading the slots (fused path), else None."""
+        return self.p2p.combine_wait() if self.backend == "fused" else None
 
     # --------------------------------------------------------------- fused
     def moe_fused(self, model, layer, x, ids, w, slots):

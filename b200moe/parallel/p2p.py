@@ -3,10 +3,12 @@
 Buffers are symmetric: every rank allocates the same layout (one cudaMalloc
 per buffer), shares it through a CUDA IPC handle, and maps every peer's copy
 on its own device (plain NVLink peer mappings, no multicast object).
-Per MoE layer (no host synchronisation, CUDA-graph capturable):
+Per MoE layer, five launches, no host synchronisation, CUDA-graph capturable:
 
-    ep_dispatch  -> ep_count -> ep_scatter -> gate/up GEMM -> down GEMM with
-    peer-scatter epilogue -> ep_signal -> ep_wait_done -> (model) moe_combine
+    ep_dispatch (rows + per-expert counts to the owners, epoch flag)
+    -> ep_scatter (waits for every source; expert-sorted rows from the count matrix)
+    -> gate/up GEMM -> down GEMM (peer-scatter epilogue; its last CTA releases the
+       done epoch) -> (model) moe_combine (waits for every owner's done epoch)
 
 The routed rows cross NVLink once (source -> owner, as P2P stores from the
 dispatch kernel) and the weighted expert outputs cross once (owner -> source,
@@ -80,8 +82,9 @@ class P2PMoE:
                     break
             return (C.tensor_from_ptr(ptr, list(shape), dtype, di) if ok else None), ptrs
 
+        El = ep.num_local
         for name, shape, dt in (("recv_x", (W * cap, H), torch.bfloat16), ("recv_meta", (W * cap, 4), torch.int32),
-                                ("counts", (W,), torch.int32), ("flags", (W,), torch.int32),
+                                ("counts", (W * El,), torch.int32), ("flags", (W,), torch.int32),
                                 ("done", (W,), torch.int32), ("slots", (slot_cap, H), torch.bfloat16)):
             self.symm[name] = alloc(*shape, dtype=dt)
         torch.cuda.synchronize(dev)
@@ -92,9 +95,13 @@ class P2PMoE:
             self.close()
             return None
         self.W, self.rank, self.H, self.cap, self.slot_cap = W, rank, H, cap, slot_cap
+        self.El, self.E = El, ep.E
         self.owner = ep.owner.to(torch.int32)
         self.g2l = ep.g2l
+        self.ge_local = ep.ge_local
         self.send_cursor = torch.zeros(W, dtype=torch.int32, device=dev)
+        self.ecur = torch.zeros(ep.E, dtype=torch.int32, device=dev)
+        self.cta_done = torch.zeros(1, dtype=torch.int32, device=dev)
         self.done_blocks = torch.zeros(1, dtype=torch.int32, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = ops.status_word(dev)
@@ -131,40 +138,40 @@ class P2PMoE:
 
     def _a(self):
         s = self.symm
-        return ([self.W, self.rank, self.H, self.cap, self.slot_cap], self.owner, self.g2l, self.send_cursor,
-                self.done_blocks, self.epoch, self.status, self.wait_ns, s["recv_x"][1], s["recv_meta"][1],
-                s["counts"][1], s["flags"][1], s["done"][1])
+        return ([self.W, self.rank, self.H, self.cap, self.slot_cap, self.El, self.E], self.owner, self.g2l,
+                self.ge_local, self.send_cursor, self.ecur, self.done_blocks, self.epoch, self.status, self.wait_ns,
+                s["recv_x"][1], s["recv_meta"][1], s["counts"][1], s["flags"][1], s["done"][1])
+
+    def combine_wait(self):
+        """(this rank's done array, epoch, status, wait_ns) for the combine kernel's wait."""
+        return self.symm["done"][0], self.epoch, self.status, self.wait_ns
 
     def moe(self, model, layer, x, ids, w, slots):
-        """Returns the tensor holding this rank's (token, k) slots."""
+        """Returns the tensor holding this rank's (token, k) slots; the caller's combine
+        waits on ``combine_wait()`` before reading it."""
         C = ops.native()
         a = self._a()
         T = x.shape[0]
         El = model.num_local_experts
         I = layer.w2.shape[-1]
         C.ep_dispatch(*a, x, ids, w.contiguous())
-        ops.count_launches()
-        cnt = model._buf("ep_counts", (2 * El,), torch.int32)
-        cnt.zero_()
-        C.ep_count(*a, cnt[:El])
-        if model.profiler is not None:
-            model.profiler.observe("moe.local_pairs", cnt[:El].sum())
         rows = self.W * self.cap
+        cnt = model._buf("ep_counts", (El,), torch.int32)
+        off = model._buf("ep_offsets", (El + 1,), torch.int32)
         xp = model._buf("x_perm", (rows, self.H), model.dtype)
         code = model._buf("slot_of_row", (rows,), torch.int32)
         sw = model._buf("ep_slot_w", (rows,), torch.float32)
-        off = model._buf("ep_offsets", (El + 1,), torch.int32)
-        C.ep_scatter(*a, cnt[:El], cnt[El:], xp, code, sw, off)
+        C.ep_scatter(*a, cnt, xp, code, sw, off)
+        if model.profiler is not None:
+            model.profiler.observe("moe.local_pairs", cnt.sum())
         h = model._buf("h_perm", (rows, I), model.dtype)
         expected = max(1, T * self.W)  # rows this rank expects on average
-        ops.grouped_gate_up_silu(xp, layer.w13, layer.s13, cnt[:El], off, h, I,
+        ops.grouped_gate_up_silu(xp, layer.w13, layer.s13, cnt, off, h, I,
                                  bn=ops.pick_bn(expected * model.args.num_experts_per_tok, I // 128, El, pair=True),
                                  tiled=model.weights_tiled)
-        C.gemm_peer_scatter(layer.w2, layer.s2, h, cnt[:El], off,
+        C.gemm_peer_scatter(layer.w2, layer.s2, h, cnt, off,
                             ops.pick_bn(expected * model.args.num_experts_per_tok, self.H // 128, El),
                             code, sw, self.symm["slots"][1], self.slot_cap, self.H, self.status,
-                            model.weights_tiled)
-        C.ep_signal(*a)
-        C.ep_wait_done(*a)
-        ops.count_launches(6)
+                            model.weights_tiled, self.epoch, self.cta_done, self.symm["done"][1], self.rank)
+        ops.count_launches(3)
         return self.symm["slots"][0]

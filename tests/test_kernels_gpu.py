@@ -576,9 +576,9 @@ def _ep_wait_args(world, epoch, done, status, wait_ns=None):
     local = [done.data_ptr()] * world
     if wait_ns is None:
         wait_ns = torch.zeros(2 * world, dtype=torch.int64, device=DEV)
-    return ([world, 0, 8, 1, 1], torch.zeros(1, **i32), torch.zeros(1, **i32), torch.zeros(world, **i32),
-            torch.zeros(1, **i32), epoch, status, wait_ns, local, local, local, local,
-            [done.data_ptr() + 4 * world * r for r in range(world)])
+    return ([world, 0, 8, 1, 1, 1, 1], torch.zeros(1, **i32), torch.zeros(1, **i32), torch.zeros(1, **i32),
+            torch.zeros(world, **i32), torch.zeros(1, **i32), torch.zeros(1, **i32), epoch, status, wait_ns,
+            local, local, local, local, [done.data_ptr() + 4 * world * r for r in range(world)])
 
 
 def test_bounded_flag_wait_returns_status_instead_of_hanging():
