@@ -12,6 +12,7 @@
 
 #include "attention.h"
 #include "ep_p2p.h"
+#include "tp_comm.h"
 #include "fused_ops.h"
 #include "gemm_tc.h"
 #include "sampler.h"
@@ -36,7 +37,7 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
           c10::optional<Tensor> group_offset, Tensor out, int64_t bn, int64_t epi, int64_t m_tiles,
           int64_t pair_row_offset, int64_t out_group_stride, c10::optional<Tensor> slot_of_row,
           c10::optional<Tensor> slot_weight, Tensor status, c10::optional<Tensor> trace, int64_t k_splits,
-          int64_t split_stride, bool a_tiled) {
+          int64_t split_stride, bool a_tiled, std::vector<int64_t> release) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CUDA(out); CHECK_CUDA(group_count); CHECK_CUDA(status);
   CHECK_CONTIG(weight); CHECK_CONTIG(group_count);
   TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
@@ -111,6 +112,17 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
     TORCH_CHECK(trace->scalar_type() == torch::kInt64 && trace->is_contiguous(), "trace must be int64");
     L.args.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
     L.args.trace_cap = (int)((trace->numel() - 1) / 10);
+  }
+  if (!release.empty()) {
+    // [epoch ptr, CTA counter ptr, rank, epoch add, flag ptr of each rank...]: the last
+    // CTA releases *epoch + add into flags[r][rank] for every r (device pointers)
+    TORCH_CHECK(release.size() >= 5 && release.size() <= 4 + 8, "release: epoch, counter, rank, add, 1..8 flags");
+    L.args.ep_epoch = reinterpret_cast<const uint32_t*>(release[0]);
+    L.args.ep_cta_done = reinterpret_cast<int*>(release[1]);
+    L.args.ep_rank = (int)release[2];
+    L.args.ep_epoch_add = (int)release[3];
+    L.args.ep_world = (int)release.size() - 4;
+    for (int r = 0; r < L.args.ep_world; ++r) L.args.ep_done[r] = reinterpret_cast<void*>(release[4 + r]);
   }
   L.a = weight.data_ptr();
   L.a_row_stride_bytes = K * weight.element_size();
@@ -259,6 +271,56 @@ void ep_scatter(EP_ARGS_DECL, Tensor local_counts, Tensor x_perm, Tensor slot_co
 
 void ep_signal(EP_ARGS_DECL) { b200::ep_signal(EP_ARGS, stream()); }
 void ep_wait_done(EP_ARGS_DECL) { b200::ep_wait_done(EP_ARGS, stream()); }
+
+// Tensor-parallel all-reduce over peer memory.  dims = (world, rank, splits, split_stride);
+// part_ptrs / flag_ptrs hold every rank's partial buffer and flag array (device pointers).
+b200::TpArgs tp_args(std::vector<int64_t> dims, std::vector<int64_t> part_ptrs, std::vector<int64_t> flag_ptrs,
+                     Tensor epoch, Tensor counter, Tensor status, c10::optional<Tensor> wait_ns) {
+  TORCH_CHECK(dims.size() == 4, "dims = (world, rank, splits, split_stride)");
+  b200::TpArgs a{};
+  a.world = (int)dims[0];
+  a.rank = (int)dims[1];
+  a.splits = (int)dims[2];
+  a.split_stride = dims[3];
+  TORCH_CHECK(a.world >= 1 && a.world <= b200::kTpMaxWorld && (int)part_ptrs.size() == a.world &&
+              (int)flag_ptrs.size() == a.world, "one partial buffer and one flag array per rank");
+  for (int r = 0; r < a.world; ++r) {
+    a.part[r] = reinterpret_cast<const float*>(part_ptrs[r]);
+    a.flags[r] = reinterpret_cast<uint32_t*>(flag_ptrs[r]);
+  }
+  CHECK_DT(counter, torch::kInt32); CHECK_DT(status, torch::kInt32);
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  a.counter = counter.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  if (wait_ns.has_value()) {
+    TORCH_CHECK(wait_ns->scalar_type() == torch::kInt64 && wait_ns->numel() >= a.world, "wait_ns [world] int64");
+    a.wait_ns = reinterpret_cast<unsigned long long*>(wait_ns->data_ptr<int64_t>());
+  }
+  return a;
+}
+
+void tp_slots_partial(std::vector<int64_t> dims, std::vector<int64_t> part_ptrs, std::vector<int64_t> flag_ptrs,
+                      Tensor epoch, Tensor counter, Tensor status, c10::optional<Tensor> wait_ns, Tensor slots,
+                      int64_t topk, int64_t T, int64_t H, int64_t part_rows) {
+  CHECK_CUDA(slots); CHECK_CONTIG(slots); CHECK_DT(slots, torch::kBFloat16);
+  TORCH_CHECK(slots.numel() >= T * topk * H, "slots too small");
+  TORCH_CHECK(T <= part_rows, "partial buffer holds fewer rows than the batch");
+  auto a = tp_args(dims, part_ptrs, flag_ptrs, epoch, counter, status, wait_ns);
+  TORCH_CHECK(a.splits == 1, "slot partials are a single split");
+  b200::tp_slots_partial(a, slots.data_ptr(), (int)topk, (int)T, (int)H, stream());
+}
+
+void tp_allreduce_rmsnorm(std::vector<int64_t> dims, std::vector<int64_t> part_ptrs, std::vector<int64_t> flag_ptrs,
+                          Tensor epoch, Tensor counter, Tensor status, c10::optional<Tensor> wait_ns, Tensor residual,
+                          Tensor weight, Tensor out, double eps, int64_t part_rows) {
+  CHECK_CUDA(residual); CHECK_CONTIG(residual); CHECK_CONTIG(out);
+  CHECK_DT(residual, torch::kBFloat16); CHECK_DT(weight, torch::kBFloat16); CHECK_DT(out, torch::kBFloat16);
+  const int T = (int)residual.size(0), H = (int)residual.size(1);
+  TORCH_CHECK(T <= part_rows, "partial buffer holds fewer rows than the batch");
+  auto a = tp_args(dims, part_ptrs, flag_ptrs, epoch, counter, status, wait_ns);
+  TORCH_CHECK(a.split_stride >= (int64_t)T * H, "split stride below one partial");
+  b200::tp_allreduce_rmsnorm(a, residual.data_ptr(), weight.data_ptr(), out.data_ptr(), T, H, (float)eps, stream());
+}
 
 void embed(Tensor ids, Tensor table, Tensor out, Tensor status, c10::optional<Tensor> feed_src,
            c10::optional<Tensor> feed_tokens) {
@@ -668,6 +730,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
   m.def("ep_dispatch", &ep_dispatch);
+  m.def("tp_slots_partial", &tp_slots_partial);
+  m.def("tp_allreduce_rmsnorm", &tp_allreduce_rmsnorm);
   m.def("ep_scatter", &ep_scatter);
   m.def("ep_signal", &ep_signal);
   m.def("ep_wait_done", &ep_wait_done);

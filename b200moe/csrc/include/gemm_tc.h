@@ -48,10 +48,11 @@ struct GemmArgs {
   // one contiguous 8 KB block fetched by a single bulk copy
   int a_tiled;
   const void* a_base;
-  // expert parallel (peer scatter): the CTA that finishes last releases this rank's
-  // done epoch (*ep_epoch) into every source's done array at ep_done[r] + ep_rank,
-  // after every CTA has fenced its peer stores; null ep_epoch = no release
+  // cross-GPU release (expert-parallel peer scatter, tensor-parallel partials): the
+  // CTA that finishes last writes *ep_epoch + ep_epoch_add into ep_done[r] + ep_rank
+  // for every rank r, after every CTA has fenced its stores; null ep_epoch = none
   const uint32_t* ep_epoch;
+  int ep_epoch_add;
   int* ep_cta_done;            // local counter, zero between launches
   void* ep_done[8];
   int ep_rank;

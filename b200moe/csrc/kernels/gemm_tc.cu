@@ -744,7 +744,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     if (atomicAdd(args.ep_cta_done, 1) == (int)gridDim.x - 1) {  // every CTA's rows are out
       *args.ep_cta_done = 0;
       __threadfence_system();
-      const uint32_t epoch = *args.ep_epoch;
+      const uint32_t epoch = *args.ep_epoch + (uint32_t)args.ep_epoch_add;
       for (int r = 0; r < args.ep_world; ++r)
         st_release_sys(reinterpret_cast<uint32_t*>(args.ep_done[r]) + args.ep_rank, epoch);
     }

@@ -95,6 +95,9 @@ class ModelRunner:
         if self.world_size > 1 and self.attn_tp == 1:
             from b200moe.parallel.ep import ExpertParallel
             self.model.ep = ExpertParallel(self, config.moe_backend)
+        if self.attn_tp > 1 and self.device.type == "cuda":
+            from b200moe.parallel.tp import TpComm
+            self.model.tp_comm = TpComm.create(self)
         trace.mark("model")
         if config.random_init:
             random_init_(self.model, seed=config.seed)
@@ -336,7 +339,7 @@ class ModelRunner:
             # expert parallelism it exchanges rows with every peer under bounded flag
             # waits: line the ranks up first, as start-up work before the first capture
             # (weight init, tiling, KV allocation) can leave them seconds apart.
-            if self.model.ep is not None and dist.is_initialized():
+            if (self.model.ep is not None or self.model.tp_comm is not None) and dist.is_initialized():
                 torch.cuda.synchronize(self.device)
                 dist.barrier()
             h = self.model(inp, self.kv)
@@ -504,7 +507,8 @@ class ModelRunner:
         the device time its kernels waited on each peer since the last reset."""
         ep = self.model.ep
         rep = {"ep_backend": None if ep is None else ep.backend, "decode_graphs": sorted(self.graphs),
-               "attention_parallel": "tp" if self.attn_tp > 1 else "dp"}
+               "attention_parallel": "tp" if self.attn_tp > 1 else "dp",
+               "tp_fused": self.model.tp_comm is not None}
         if ep is not None and ep.p2p is not None:
             torch.cuda.synchronize(self.device)
             rep["ep_wait"] = ep.p2p.wait_stats(reset=False)
@@ -605,6 +609,10 @@ class ModelRunner:
         if ep is not None and getattr(ep, "p2p", None) is not None:
             ep.p2p.close()  # collective: every rank reaches exit together
             ep.p2p = None
+        tp = getattr(getattr(self, "model", None), "tp_comm", None)
+        if tp is not None:
+            tp.close()  # collective, like the expert-parallel buffers
+            self.model.tp_comm = None
         for attr in ("model", "kv"):
             if hasattr(self, attr):
                 delattr(self, attr)

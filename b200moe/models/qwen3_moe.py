@@ -146,6 +146,8 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.cos_sin = ops.rope_cos_sin(args.head_dim, args.max_position_embeddings, args.rope_theta, self.device)
         self.scale = args.head_dim ** -0.5
         self.ep = None          # expert-parallel communicator (multi-rank)
+        self.tp_comm = None     # tensor-parallel attention: fused peer-memory sums (parallel/tp.py)
+        self._tp_fused = False
         self.moe_backend = "fused"
         self.attention_backend = "paged"  # or "sdpa": per-sequence PyTorch attention (A/B, equivalence gate)
         self.profiler = None
@@ -268,10 +270,18 @@ class Qwen3MoeForCausalLM(nn.Module):
                              feed=feed)
         x = ops.rmsnorm(residual, self.layers[0].input_layernorm, eps,
                         out=self._buf("x", (T, H), self.dtype) if cuda else None)
+        # tensor-parallel attention: decode-size batches sum the ranks' partials over peer memory
+        self._tp_fused = self.attn_tp > 1 and self.tp_comm is not None and T <= self.tp_comm.max_tokens
+        if self._tp_fused:
+            self.tp_comm.begin_forward(len(self.layers) + sum(1 for ly in self.layers if ly.is_moe))
         for l, layer in enumerate(self.layers):
             attn = self._attention(layer, x, inp, kv.layer(l))
             xbuf = self._buf("x", (T, H), self.dtype) if cuda else None
-            if self.attn_tp > 1:
+            if self._tp_fused:
+                with self._range("attn.o_proj_allreduce_norm"):
+                    x = self.tp_comm.o_proj_add_norm(attn, layer.o_weight, layer.o_scale, residual,
+                                                     layer.post_attention_layernorm, eps, xbuf, self.weights_tiled)
+            elif self.attn_tp > 1:
                 with self._range("attn.o_proj"):
                     o = ops.linear(attn, layer.o_weight, layer.o_scale,
                                    out=self._buf("o", (T, H), self.dtype) if cuda else None, tiled=self.weights_tiled)
@@ -488,6 +498,10 @@ class Qwen3MoeForCausalLM(nn.Module):
             slots.zero_()  # slots of other ranks' experts stay zero
             ops.grouped_down_scatter(h_perm, layer.w2, layer.s2, counts_l[:El], offsets, slot_of_row,
                                      w.view(-1), slots, tiled=self.weights_tiled)
+            if self._tp_fused:
+                with self._range("moe.allreduce_norm"):
+                    return self.tp_comm.slots_add_norm(slots, k, residual, next_norm, eps,
+                                                       self._buf("x", (T, H), self.dtype))
             # combine (fixed-order sum over k) into a zeroed residual: partial = sum_k slots
             partial.zero_()
             ops.moe_combine_add_rmsnorm(slots, k, partial, next_norm, eps,

@@ -139,7 +139,8 @@ def _dense_cost_us(rows: int, m_tiles: int, k_stages: int, bn: int, splits: int,
     return t
 
 
-def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: bool = True) -> tuple[int, int]:
+def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: bool = True,
+               max_splits: int = 1 << 30) -> tuple[int, int]:
     """(token tile, K splits) of a single-group GEMM, the cheapest under
     ``_dense_cost_us``.  Decode-size token counts give too few output tiles to
     fill the grid (o_proj at 256 tokens is 16 weight tiles): a larger token
@@ -151,7 +152,7 @@ def plan_dense(rows: int, m_tiles: int, k_stages: int, sms: int = NUM_SMS, fp8: 
             break
         # e4m3 tiles of up to 128 tokens run 128-wide K stages (two 64-wide blocks)
         ks = k_stages // 2 if fp8 and bn <= 128 else k_stages
-        for splits in range(1, max(1, ks // 2) + 1):
+        for splits in range(1, max(1, min(ks // 2, max_splits)) + 1):
             per = math.ceil(ks / splits)
             if math.ceil(ks / per) != splits:
                 continue  # would leave a split empty
@@ -241,13 +242,13 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None, ou
     if splits > 1:
         part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
         C.gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, m_tiles,
-               0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled)
+               0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled, [])
         C.splitk_reduce(part, splits, out)
         count_launches(2)
         return out
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
     C.gemm(weight, scale, x, count_tensor(T, x.device), None, out, bn, epi, m_tiles,
-           0, 0, None, None, status_word(x.device), _trace[0], 1, 0, tiled)
+           0, 0, None, None, status_word(x.device), _trace[0], 1, 0, tiled, [])
     count_launches()
     return out
 
@@ -266,7 +267,7 @@ def linear_add_rmsnorm(x, weight, scale, residual, norm_w, eps, out, tiled: bool
     C = native()
     part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
     C.gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, m_tiles,
-           0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled)
+           0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled, [])
     C.rmsnorm_partials(part, splits, residual, norm_w, out, eps)
     count_launches(2)
     return out
@@ -280,7 +281,7 @@ def grouped_gate_up_silu(x_perm, w13, s13, counts, offsets, out, inter: int, bn:
     m_tiles = inter // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w13.shape[0], pair=True)
     C.gemm(w13, s13, x_perm, counts, offsets, out, bn, EPI_SILU_PAIR, m_tiles, inter, 0, None, None,
-           status_word(x_perm.device), _trace[0], 1, 0, tiled)
+           status_word(x_perm.device), _trace[0], 1, 0, tiled, [])
     count_launches()
     return out
 
@@ -293,7 +294,7 @@ def grouped_down_scatter(h_perm, w2, s2, counts, offsets, slot_of_row, slot_weig
     m_tiles = w2.shape[1] // 128
     bn = bn or pick_bn(rows, m_tiles, groups=w2.shape[0])
     C.gemm(w2, s2, h_perm, counts, offsets, slots_out, bn, EPI_SCATTER, m_tiles, 0, 0, slot_of_row, slot_weight,
-           status_word(h_perm.device), _trace[0], 1, 0, tiled)
+           status_word(h_perm.device), _trace[0], 1, 0, tiled, [])
     count_launches()
     return slots_out
 

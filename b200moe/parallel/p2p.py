@@ -24,6 +24,85 @@ import torch.distributed as dist
 from b200moe import ops
 
 
+class PeerBuffers:
+    """Symmetric device buffers: every rank allocates the same named buffers (one
+    cudaMalloc each), shares them through CUDA IPC handles and maps every peer's
+    copy on its own device -- plain NVLink peer mappings, no multicast object.
+    Every rank takes part in every exchange even after a local failure, so the
+    collective sequence stays aligned; ``agree`` settles whether all ranks
+    succeeded.  Peer memory is read and written only by this repository's own
+    ld/st kernels."""
+
+    def __init__(self, rank: int, world: int, device_index: int, tag: str):
+        self.rank, self.world, self.di, self.tag = rank, world, device_index, tag
+        self.ok = True
+        self.bufs: dict[str, tuple] = {}
+        self._owned, self._opened = [], []
+
+    def alloc(self, name: str, shape: tuple, dtype) -> tuple:
+        """(local tensor or None, [device pointer of every rank's copy])."""
+        C = ops.native()
+        nbytes = torch.empty(0, dtype=dtype).element_size()
+        for d in shape:
+            nbytes *= d
+        ptr, blob = None, None
+        if self.ok:
+            try:
+                ptr, handle = C.ipc_alloc(nbytes, self.di)
+                self._owned.append(ptr)
+                blob = bytes(handle.numpy())
+            except Exception as exc:  # noqa: BLE001 - reported, then the caller falls back
+                print(f"[{self.tag}] ipc_alloc failed on rank {self.rank}: {exc}", flush=True)
+                self.ok = False
+        handles = [None] * self.world
+        dist.all_gather_object(handles, blob)
+        ptrs = []
+        for r, h in enumerate(handles):
+            if not self.ok or h is None:
+                self.ok = False
+                break
+            if r == self.rank:
+                ptrs.append(ptr)
+                continue
+            try:
+                q = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), self.di)
+                self._opened.append(q)
+                ptrs.append(q)
+            except Exception as exc:  # noqa: BLE001
+                print(f"[{self.tag}] ipc_open of rank {r} failed on rank {self.rank}: {exc}", flush=True)
+                self.ok = False
+                break
+        out = ((C.tensor_from_ptr(ptr, list(shape), dtype, self.di) if self.ok else None), ptrs)
+        self.bufs[name] = out
+        return out
+
+    def __getitem__(self, name: str) -> tuple:
+        return self.bufs[name]
+
+    def agree(self) -> bool:
+        """True when every rank allocated and mapped every buffer (a collective)."""
+        torch.cuda.synchronize(self.di)
+        verdict = torch.tensor([1 if self.ok else 0], dtype=torch.int32, device=torch.device("cuda", self.di))
+        dist.all_reduce(verdict, op=dist.ReduceOp.MIN)
+        return bool(int(verdict.item()))
+
+    def release(self):
+        """Unmap the peers' buffers and free this rank's, after a device sync and a
+        barrier so that no peer still writes into them (a collective)."""
+        if not self._owned and not self._opened:
+            return
+        C = ops.native()
+        torch.cuda.synchronize(self.di)
+        if dist.is_initialized():
+            dist.barrier()
+        for p in self._opened:
+            C.ipc_close(p, self.di)
+        self.bufs.clear()
+        for p in self._owned:
+            C.ipc_free(p, self.di)
+        self._owned, self._opened = [], []
+
+
 class P2PMoE:
 
     def __init__(self, ep, symm):
@@ -35,63 +114,20 @@ class P2PMoE:
         runner = ep.runner
         cfg = runner.config
         args = runner.args
-        C = ops.native()
         W, rank, dev = ep.world, ep.rank, ep.device
         H, k = args.hidden_size, args.num_experts_per_tok
         slot_cap = cfg.max_num_batched_tokens * k
         cap = slot_cap
         di = dev.index if dev.index is not None else torch.cuda.current_device()
-        self = P2PMoE(ep, {})
-        self._owned, self._opened = [], []
-
-        ok = True
-
-        def alloc(*shape, dtype):
-            # every rank joins every exchange even after a local failure, so the
-            # collective sequence stays aligned; the verdict is agreed below
-            nonlocal ok
-            nbytes = torch.empty(0, dtype=dtype).element_size()
-            for d in shape:
-                nbytes *= d
-            ptr, blob = None, None
-            if ok:
-                try:
-                    ptr, handle = C.ipc_alloc(nbytes, di)
-                    self._owned.append(ptr)
-                    blob = bytes(handle.numpy())
-                except Exception as exc:  # noqa: BLE001 - reported, then the NCCL path is used
-                    print(f"[ep] ipc_alloc failed on rank {rank}: {exc}", flush=True)
-                    ok = False
-            handles = [None] * W
-            dist.all_gather_object(handles, blob)
-            ptrs = []
-            for r, h in enumerate(handles):
-                if not ok or h is None:
-                    ok = False
-                    break
-                if r == rank:
-                    ptrs.append(ptr)
-                    continue
-                try:
-                    q = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), di)
-                    self._opened.append(q)
-                    ptrs.append(q)
-                except Exception as exc:  # noqa: BLE001
-                    print(f"[ep] ipc_open of rank {r} failed on rank {rank}: {exc}", flush=True)
-                    ok = False
-                    break
-            return (C.tensor_from_ptr(ptr, list(shape), dtype, di) if ok else None), ptrs
-
+        symm = PeerBuffers(rank, W, di, "ep")
+        self = P2PMoE(ep, symm)
         El = ep.num_local
         for name, shape, dt in (("recv_x", (W * cap, H), torch.bfloat16), ("recv_meta", (W * cap, 4), torch.int32),
                                 ("counts", (W * El,), torch.int32), ("flags", (W,), torch.int32),
                                 ("done", (W,), torch.int32), ("slots", (slot_cap, H), torch.bfloat16)):
-            self.symm[name] = alloc(*shape, dtype=dt)
-        torch.cuda.synchronize(dev)
-        verdict = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
-        dist.all_reduce(verdict, op=dist.ReduceOp.MIN)
+            symm.alloc(name, shape, dt)
         self.device_index = di
-        if int(verdict.item()) == 0:
+        if not symm.agree():
             self.close()
             return None
         self.W, self.rank, self.H, self.cap, self.slot_cap = W, rank, H, cap, slot_cap
@@ -105,7 +141,7 @@ class P2PMoE:
         self.done_blocks = torch.zeros(1, dtype=torch.int32, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = ops.status_word(dev)
-        # device ns waited per layer-wait, summed: [source flags (ep_count) | owner done epochs (ep_wait_done)]
+        # device ns waited, summed: [each source's dispatch flag (ep_scatter) | each owner's done epoch (combine)]
         self.wait_ns = torch.zeros(2 * W, dtype=torch.int64, device=dev)
         return self
 
@@ -121,20 +157,8 @@ class P2PMoE:
                 "combine_ms": [round(x / 1e6, 2) for x in v[W:2 * W]]}
 
     def close(self):
-        """Unmap the peers' buffers and free this rank's (after a device sync and
-        a barrier, so no peer still writes into them)."""
-        if not getattr(self, "_owned", None):
-            return
-        C = ops.native()
-        torch.cuda.synchronize(self.device_index)
-        if dist.is_initialized():
-            dist.barrier()
-        for p in self._opened:
-            C.ipc_close(p, self.device_index)
-        self.symm.clear()
-        for p in self._owned:
-            C.ipc_free(p, self.device_index)
-        self._owned, self._opened = [], []
+        """Release the symmetric buffers (a collective: every rank reaches it together)."""
+        self.symm.release()
 
     def _a(self):
         s = self.symm

@@ -47,10 +47,15 @@ def test_ep2_matches_single_gpu(single, backend, eager):
 
 
 @needs2
-def test_tp2_attention_matches_single_gpu():
-    """Tensor-parallel attention over 2 GPUs (head-sharded QKV/O + NCCL
-    all-reduce, experts split): greedy tokens match one GPU on a 4-layer
-    Qwen3-30B-A3B-shaped model (128-row fp8 blocks align with the head split)."""
+@pytest.mark.parametrize("fused,eager", [(True, True), (True, False), (False, True)])
+def test_tp2_attention_matches_single_gpu(monkeypatch, fused, eager):
+    """Tensor-parallel attention over 2 GPUs (head-sharded QKV/O, experts split):
+    greedy tokens match one GPU on a 4-layer Qwen3-30B-A3B-shaped model (128-row
+    fp8 blocks align with the head split).  ``fused``: the O projection and the MoE
+    partials are summed over peer memory inside the residual RMSNorm
+    (parallel/tp.py); otherwise NCCL all-reduce.  ``eager=False`` replays the
+    fused sums inside CUDA graphs."""
+    monkeypatch.setenv("B200MOE_TP_FUSED", "1" if fused else "0")
     kw = dict(kvcache_block_size=64, max_num_seqs=8, max_num_batched_tokens=1024, max_model_len=512,
               num_kvcache_blocks=64, random_init="seeded", enforce_eager=True)
     prompts = [[(13 * i + 7 * j) % 150000 + 1 for j in range(40 + 17 * i)] for i in range(6)]
@@ -58,9 +63,13 @@ def test_tp2_attention_matches_single_gpu():
     one = LLM("qwen3-30b-a3b-4l", **kw)
     a = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False)]
     one.exit()
-    two = LLM("qwen3-30b-a3b-4l", tensor_parallel_size=2, attention_parallel="tp", **kw)
+    two = LLM("qwen3-30b-a3b-4l", tensor_parallel_size=2, attention_parallel="tp", **{**kw, "enforce_eager": eager})
     b = [o["token_ids"] for o in two.generate(prompts, sp, use_tqdm=False)]
+    b2 = [o["token_ids"] for o in two.generate(prompts, sp, use_tqdm=False)]
+    reports = two.executor.call_all("parallel_report")
     two.executor.call("check_status")
     two.exit()
+    assert all(r["tp_fused"] == fused for r in reports), reports
+    assert b == b2, "tensor-parallel decode must be run-to-run deterministic"
     agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
     assert agree > 0.9, agree
