@@ -531,15 +531,29 @@ void dequant_weights(Tensor q, Tensor scale, Tensor out, bool tiled) {
 }
 
 void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
-                  c10::optional<Tensor> counts, c10::optional<Tensor> status) {
+                  c10::optional<Tensor> counts, c10::optional<Tensor> status, c10::optional<Tensor> part,
+                  c10::optional<Tensor> tile_cnt) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16);
   CHECK_CONTIG(w); CHECK_DT(w, torch::kBFloat16);
   CHECK_DT(ids, torch::kInt32); CHECK_DT(weights, torch::kFloat32);
   TORCH_CHECK(x.size(1) == w.size(1) && w.size(0) >= num_experts, "router shapes");
   TORCH_CHECK(ids.numel() >= x.size(0) * topk && weights.numel() >= x.size(0) * topk, "router outputs too small");
+  // the split-K scratch is used only when there is a counter for every token tile
+  float* pp = nullptr;
+  int* cp = nullptr;
+  int part_tiles = 0;
+  if (part.has_value()) {
+    TORCH_CHECK(tile_cnt.has_value(), "router scratch needs the tile counters");
+    CHECK_DT((*part), torch::kFloat32); CHECK_DT((*tile_cnt), torch::kInt32);
+    if (tile_cnt->numel() >= (x.size(0) + 15) / 16) {
+      pp = part->data_ptr<float>();
+      cp = tile_cnt->data_ptr<int>();
+      part_tiles = (int)(part->numel() / (16 * 128));
+    }
+  }
   b200::router_fused(x.data_ptr(), w.data_ptr(), (int)x.size(0), (int)x.size(1), (int)num_experts, (int)w.size(0),
                      (int)topk, renorm, ids.data_ptr<int>(), weights.data_ptr<float>(), ptr_or_null<int>(counts),
-                     ptr_or_null<int>(status), stream());
+                     ptr_or_null<int>(status), stream(), pp, cp, part_tiles);
 }
 
 // residual += bf16(sum of split-K partials); out = rmsnorm(residual) * weight

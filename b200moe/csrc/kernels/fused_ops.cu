@@ -372,11 +372,17 @@ constexpr int kRtSmem = 1024 + kRtStages * kRtChunkBytes + kRtTok * (kRtE + 1) *
 
 __device__ __forceinline__ uint32_t rt_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
+// Decode-size batches have too few 16-token tiles to fill the SMs, and each CTA
+// would walk all H / 64 chunks serially: the grid's y dimension then splits K.
+// Each CTA writes its fp32 partial logits to `part`; the last CTA of a tile
+// (per-tile counter) adds the partials in K order -- the same on every run --
+// and does the top-k.
 __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant__ CUtensorMap xmap,
                                                            const __grid_constant__ CUtensorMap wmap, int T, int H,
                                                            int E, int topk, int renorm, int* __restrict__ ids,
                                                            float* __restrict__ weights, int* __restrict__ counts,
-                                                           int* __restrict__ status) {
+                                                           int* __restrict__ status, float* __restrict__ part,
+                                                           int* __restrict__ tile_cnt) {
   pdl_enter();
   constexpr int XB = kRtTok * 128;  // bytes of one x chunk (the W chunk follows it)
   extern __shared__ __align__(1024) uint8_t rt_raw[];
@@ -386,7 +392,9 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + kRtStages);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRtTok;
-  const int nchunks = H / kRtK;
+  const int KS = gridDim.y, ks = blockIdx.y;
+  const int c_begin = (int)((int64_t)(H / kRtK) * ks / KS), c_end = (int)((int64_t)(H / kRtK) * (ks + 1) / KS);
+  const int nchunks = c_end - c_begin;  // this CTA's K chunks; chunk j of them is global chunk c_begin + j
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRtStages; ++i) mbar_init(&full[i], 1);
     *abort_flag = 0;
@@ -396,8 +404,8 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
   auto issue = [&](int c) {
     uint8_t* dst = ring + (c % kRtStages) * kRtChunkBytes;
     mbar_arrive_expect_tx(&full[c % kRtStages], kRtChunkBytes);
-    tma_load_2d(dst, &xmap, &full[c % kRtStages], c * kRtK, t0);        // rows >= T come back zero-filled
-    tma_load_2d(dst + XB, &wmap, &full[c % kRtStages], c * kRtK, 0);
+    tma_load_2d(dst, &xmap, &full[c % kRtStages], (c_begin + c) * kRtK, t0);  // rows >= T come back zero-filled
+    tma_load_2d(dst + XB, &wmap, &full[c % kRtStages], (c_begin + c) * kRtK, 0);
   };
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&xmap);
@@ -451,13 +459,38 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
     }
     return;
   }
+  if (KS == 1) {
 #pragma unroll
-  for (int n = 0; n < 2; ++n)
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int row = (lane >> 2) + 8 * (e >> 1), col = warp * 16 + n * 8 + 2 * (lane & 3) + (e & 1);
-      logit[row][col] = acc[n][e];
+      for (int e = 0; e < 4; ++e) {
+        const int row = (lane >> 2) + 8 * (e >> 1), col = warp * 16 + n * 8 + 2 * (lane & 3) + (e & 1);
+        logit[row][col] = acc[n][e];
+      }
+  } else {
+    float* mine = part + ((size_t)blockIdx.x * KS + ks) * (kRtTok * kRtE);
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = (lane >> 2) + 8 * (e >> 1), col = warp * 16 + n * 8 + 2 * (lane & 3) + (e & 1);
+        mine[row * kRtE + col] = acc[n][e];
+      }
+    __threadfence();
+    __syncthreads();
+    __shared__ int last_s;
+    if (threadIdx.x == 0) last_s = atomicAdd(&tile_cnt[blockIdx.x], 1) == KS - 1;
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    const float* all = part + (size_t)blockIdx.x * KS * (kRtTok * kRtE);
+    for (int i = threadIdx.x; i < kRtTok * kRtE; i += blockDim.x) {
+      float v = 0.f;
+      for (int j = 0; j < KS; ++j) v += __ldcg(all + (size_t)j * (kRtTok * kRtE) + i);
+      logit[i / kRtE][i % kRtE] = v;
     }
+    if (threadIdx.x == 0) tile_cnt[blockIdx.x] = 0;  // ready for the next launch
+  }
   __syncthreads();
   for (int r = warp; r < kRtTok; r += 8) {
     const int tok = t0 + r;
@@ -726,7 +759,8 @@ static CUtensorMap rt_map(const void* base, int rows, int H, int box_rows) {
 }
 
 void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows, int topk, bool renorm, int* ids,
-                  float* weights, int* counts, int* status, cudaStream_t s) {
+                  float* weights, int* counts, int* status, cudaStream_t s, float* part, int* tile_cnt,
+                  int part_tiles) {
   if (T == 0) return;
   if (E > kRtE || w_rows < kRtE || topk < 1 || topk > 8 || H % kRtK)
     throw std::runtime_error("router_fused: needs <= 128 experts (weight padded to 128 rows), top-k in [1, 8], "
@@ -736,8 +770,16 @@ void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows,
   smem_opt_in(router_fused_kernel, kRtSmem);
   const CUtensorMap xm = rt_map(x, T, H, kRtTok);
   const CUtensorMap wm = rt_map(w, kRtE, H, kRtE);
-  pdl_launch(router_fused_kernel, (T + kRtTok - 1) / kRtTok, 256, kRtSmem, s, xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,
-                                                                       weights, counts, status);
+  const int tiles = (T + kRtTok - 1) / kRtTok;
+  // K splits: enough CTAs to cover the SMs once, at most 8 chunks' worth per split ... and never
+  // more partial tiles than the scratch holds
+  int ks = 1;
+  if (part != nullptr && tile_cnt != nullptr) {
+    const int sms = device_sm_count();
+    while (ks < 8 && tiles * ks * 2 <= sms && (H / kRtK) >= ks * 2 * 2 && tiles * ks * 2 <= part_tiles) ks *= 2;
+  }
+  pdl_launch(router_fused_kernel, dim3(tiles, ks), 256, kRtSmem, s, xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,
+             weights, counts, status, part, tile_cnt);
   check_launch("router_fused");
 }
 

@@ -429,10 +429,30 @@ def router_topk(logits, num_experts, topk, renorm, ids, weights, counts=None):
     count_launches()
 
 
+_router_scratch: dict = {}
+
+
+def router_scratch(device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fixed-size per-device scratch of the split-K router (partial logits of up to
+    2 x NUM_SMS tiles of 16 x 128, and zeroed per-tile counters).  Allocated on the
+    first call -- an eager step, before any graph capture -- and never resized, so
+    captured graphs keep valid addresses."""
+    key = torch.device(device)
+    s = _router_scratch.get(key)
+    if s is None:
+        s = (torch.empty(2 * NUM_SMS * 16 * 128, dtype=torch.float32, device=key),
+             torch.zeros(2 * NUM_SMS, dtype=torch.int32, device=key))
+        _router_scratch[key] = s
+    return s
+
+
 def router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts=None):
     """Router GEMM + softmax + top-k in one native launch (num_experts <= 128);
-    same rounding points as ``linear`` + ``router_topk``."""
-    native().router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts, status_word(x.device))
+    same rounding points as ``linear`` + ``router_topk``.  Batches with too few
+    16-token tiles to fill the SMs also split K across CTAs."""
+    part, cnt = router_scratch(x.device)
+    native().router_fused(x, router_w, num_experts, topk, renorm, ids, weights, counts, status_word(x.device),
+                          part, cnt)
     count_launches()
 
 

@@ -291,10 +291,12 @@ def test_router_topk():
     assert int(counts.sum()) == T * k and int(counts.max()) <= T
 
 
-@pytest.mark.parametrize("T", [1, 77, 300])
+@pytest.mark.parametrize("T", [1, 77, 300, 2048])
 def test_router_fused_matches_gemm_and_topk(T):
     """One-launch router (GEMM + softmax + top-k) against the fp32 reference of
-    the same rounding points: bf16(x . w^T) logits, softmax, top-k, renorm."""
+    the same rounding points: bf16(x . w^T) logits, softmax, top-k, renorm.
+    1 / 77 / 300 tokens split K across CTAs (the last CTA of a tile sums the
+    partials in K order); 2048 tokens fill the SMs with token tiles alone."""
     E, k, H = 128, 8, 2048
     x = (torch.randn(T, H, device=DEV) * 0.5).to(torch.bfloat16)
     w = (torch.randn(E, H, device=DEV) * 0.05).to(torch.bfloat16)
@@ -313,6 +315,9 @@ def test_router_fused_matches_gemm_and_topk(T):
     want_w = (pr / pr.sum(-1, keepdim=True)).to(torch.bfloat16).float()
     torch.testing.assert_close(wt.sort(dim=1, descending=True).values, want_w, atol=1e-2, rtol=2e-2)
     assert int(counts.sum()) == T * k
+    ids2, wt2 = torch.empty_like(ids), torch.empty_like(wt)
+    ops.router_fused(x, w, E, k, True, ids2, wt2, None)
+    assert torch.equal(ids, ids2) and torch.equal(wt, wt2), "the split-K sum must be deterministic"
 
 
 def test_moe_permute():
