@@ -73,3 +73,44 @@ def test_tp2_attention_matches_single_gpu(monkeypatch, fused, eager):
     assert b == b2, "tensor-parallel decode must be run-to-run deterministic"
     agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
     assert agree > 0.9, agree
+
+
+needs4 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4,
+                            reason="needs 4 or more GPUs")
+
+
+@needs4
+def test_tp_all_gpus_with_kv_replication_matches_single_gpu():
+    """Tensor-parallel attention over every visible GPU (8 on a full box): with 4 KV
+    heads, 8 ranks hold one KV head each twice over (replicated) and 4 query heads
+    each; the fused peer-memory sums run in CUDA graphs.  Greedy tokens match one GPU."""
+    W = 8 if torch.cuda.device_count() >= 8 else 4
+    kw = dict(kvcache_block_size=64, max_num_seqs=8, max_num_batched_tokens=1024, max_model_len=512,
+              num_kvcache_blocks=64, random_init="seeded")
+    prompts = [[(13 * i + 7 * j) % 150000 + 1 for j in range(40 + 17 * i)] for i in range(6)]
+    sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
+    one = LLM("qwen3-30b-a3b-4l", enforce_eager=True, **kw)
+    a = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False)]
+    one.exit()
+    many = LLM("qwen3-30b-a3b-4l", tensor_parallel_size=W, attention_parallel="tp", **kw)
+    b = [o["token_ids"] for o in many.generate(prompts, sp, use_tqdm=False)]
+    reports = many.executor.call_all("parallel_report")
+    many.executor.call("check_status")
+    many.exit()
+    assert all(r["tp_fused"] and r["decode_graphs"] for r in reports), reports
+    agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
+    assert agree > 0.9, agree
+
+
+@needs4
+def test_ep_all_gpus_fused_graphs_matches_single_gpu(single):
+    """Expert parallelism over every visible GPU, fused peer-memory path in CUDA graphs."""
+    W = 8 if torch.cuda.device_count() >= 8 else 4
+    llm = LLM("tiny-moe-fp8", tensor_parallel_size=W, moe_backend="fused", **KW)
+    out = [o["token_ids"] for o in llm.generate(_prompts(), SP, use_tqdm=False)]
+    rep = llm.executor.call_all("parallel_report")
+    llm.executor.call("check_status")
+    llm.exit()
+    assert all(r["ep_backend"] == "fused" for r in rep), rep
+    agree = np.mean([a == b for ra, rb in zip(out, single) for a, b in zip(ra, rb)])
+    assert agree > 0.95, agree
