@@ -391,7 +391,7 @@ void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tens
                          Tensor cos_sin, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
                          c10::optional<Tensor> v_scale, Tensor q_out, int64_t num_q_heads, int64_t num_kv_heads,
                          int64_t head_dim, int64_t block_size, int64_t block_stride, int64_t scale_block_stride,
-                         double eps) {
+                         double eps, c10::optional<Tensor> part, int64_t splits) {
   CHECK_CUDA(qkv); CHECK_DT(qkv, torch::kBFloat16); CHECK_DT(positions, torch::kInt32);
   CHECK_DT(slot_mapping, torch::kInt32); CHECK_DT(cos_sin, torch::kFloat32); CHECK_CONTIG(q_out);
   TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride must be 1");
@@ -420,6 +420,14 @@ void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tens
   a.num_kv_heads = (int)num_kv_heads;
   a.head_dim = (int)head_dim;
   a.eps = (float)eps;
+  if (part.has_value()) {
+    CHECK_DT((*part), torch::kFloat32); CHECK_CONTIG((*part));
+    TORCH_CHECK(splits >= 1 && part->numel() >= splits * (int64_t)T * qkv.stride(0),
+                "qkv partials must hold splits x T x qkv width floats");
+    a.part = part->data_ptr<float>();
+    a.splits = (int)splits;
+    a.part_stride = (int64_t)T * qkv.stride(0);
+  }
   b200::qknorm_rope_kvstore(a, T, stream());
 }
 

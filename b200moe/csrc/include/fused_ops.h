@@ -28,6 +28,12 @@ struct QkvArgs {
   int num_kv_heads;
   int head_dim;
   float eps;
+  // optional: q/k/v given as `splits` fp32 split-K partials of the QKV GEMM at
+  // part + s * part_stride + t * qkv_stride, summed in split order and rounded to
+  // bf16 here (the same bits as a separate split-K reduction); qkv is then unused
+  const float* part;
+  int splits;
+  int64_t part_stride;
 };
 
 void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,

@@ -211,15 +211,30 @@ __global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
   const int pos = a.positions[t];
   const int slot = a.slot_mapping[t];
   const bf16* row = static_cast<const bf16*>(a.qkv) + (size_t)t * a.qkv_stride;
+  const float* prow = a.part != nullptr ? a.part + (size_t)t * a.qkv_stride : nullptr;
   const float* cs = a.cos_sin + (size_t)pos * D;  // [cos(D/2) | sin(D/2)]
   for (int h = warp; h < nq + 2 * nkv; h += blockDim.x >> 5) {
     const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
-    const bf16* src = row + (size_t)h * D;
     float x1[E2], x2[E2];
+    if (prow != nullptr) {  // split-K partials: sum in split order, round to bf16
+      const float* p = prow + (size_t)h * D;
 #pragma unroll
-    for (int e = 0; e < E2; ++e) {
-      x1[e] = __bfloat162float(src[lane * E2 + e]);
-      x2[e] = __bfloat162float(src[D / 2 + lane * E2 + e]);
+      for (int e = 0; e < E2; ++e) {
+        float s1 = p[lane * E2 + e], s2 = p[D / 2 + lane * E2 + e];
+        for (int sp = 1; sp < a.splits; ++sp) {
+          s1 += p[sp * a.part_stride + lane * E2 + e];
+          s2 += p[sp * a.part_stride + D / 2 + lane * E2 + e];
+        }
+        x1[e] = bf16r(s1);
+        x2[e] = bf16r(s2);
+      }
+    } else {
+      const bf16* src = row + (size_t)h * D;
+#pragma unroll
+      for (int e = 0; e < E2; ++e) {
+        x1[e] = __bfloat162float(src[lane * E2 + e]);
+        x2[e] = __bfloat162float(src[D / 2 + lane * E2 + e]);
+      }
     }
     if (is_q || is_k) {
       const bf16* nw = static_cast<const bf16*>(is_q ? a.q_norm_w : a.k_norm_w);

@@ -306,14 +306,13 @@ class Qwen3MoeForCausalLM(nn.Module):
         T = inp.num_tokens
         nq, nkv, D = self.nq_local, self.nkv_local, a.head_dim
         cuda = self.cuda
-        with self._range("attn.qkv"):
-            qkv = ops.linear(x, layer.qkv_weight, layer.qkv_scale,
-                             out=self._buf("qkv", (T, (nq + 2 * nkv) * D), self.dtype) if cuda else None,
-                             tiled=self.weights_tiled)
-        with self._range("attn.qknorm_rope_kvstore"):
-            q = ops.qknorm_rope_kvstore(qkv, inp.positions, inp.slot_mapping, layer.q_norm, layer.k_norm,
-                                        self.cos_sin, kvl, nq, nkv, D, a.rms_norm_eps,
-                                        q_out=self._buf("q", (T, nq, D), self.dtype) if cuda else None)
+        with self._range("attn.qkv_norm_rope_kvstore"):
+            q = ops.qkv_norm_rope_kvstore(x, layer.qkv_weight, layer.qkv_scale, inp.positions, inp.slot_mapping,
+                                          layer.q_norm, layer.k_norm, self.cos_sin, kvl, nq, nkv, D,
+                                          a.rms_norm_eps,
+                                          self._buf("qkv", (T, (nq + 2 * nkv) * D), self.dtype) if cuda else None,
+                                          self._buf("q", (T, nq, D), self.dtype) if cuda else None,
+                                          tiled=self.weights_tiled)
         out = self._buf("attn", (T, nq, D), self.dtype) if cuda else torch.empty(T, nq, D, dtype=q.dtype)
         nd = inp.num_decode
         with self._range("attn.core"):

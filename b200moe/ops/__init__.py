@@ -377,10 +377,33 @@ def rope_cos_sin(head_dim: int, max_pos: int, theta: float, device) -> torch.Ten
     return torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(device)
 
 
+def qkv_norm_rope_kvstore(x, weight, scale, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer, nq,
+                          nkv, D, eps, qkv_out, q_out, tiled: bool = False):
+    """QKV projection, then q/k RMSNorm + RoPE, q out and k/v into the paged pool.  When
+    the planner splits the decode-size GEMM over K, the fp32 partials go straight into
+    the norm kernel (summed there in split order: the bits of a separate reduction),
+    one launch less per layer."""
+    T, K = x.shape
+    N = weight.shape[0]
+    if x.is_cuda and scale is not None and weight.dim() == 2 and 0 < T < BF16_DENSE_ROWS:
+        bn, splits = plan_dense(T, N // 128, K // 64, fp8=True)
+        if splits > 1:
+            part = torch.empty(splits * T, N, dtype=torch.float32, device=x.device)
+            native().gemm(weight, scale, x, count_tensor(T, x.device), None, part, bn, EPI_F32, N // 128,
+                          0, 0, None, None, status_word(x.device), _trace[0], splits, T * N, tiled, [])
+            count_launches()
+            return qknorm_rope_kvstore(qkv_out, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer,
+                                       nq, nkv, D, eps, q_out, part=part, splits=splits)
+    qkv = linear(x, weight, scale, out=qkv_out, tiled=tiled)
+    return qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer, nq, nkv, D,
+                               eps, q_out)
+
+
 def qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer, nq, nkv, D,
-                        eps, q_out=None):
+                        eps, q_out=None, part=None, splits: int = 1):
     """Normalise + rotate q/k, write k (rotated) and v into the paged pool
-    (``kv_layer`` is a :class:`~b200moe.engine.kv_cache.KVLayer`)."""
+    (``kv_layer`` is a :class:`~b200moe.engine.kv_cache.KVLayer`).  ``part``: the
+    QKV GEMM's fp32 split-K partials [splits * T, width] instead of ``qkv``."""
     T = qkv.shape[0]
     if q_out is None:
         q_out = torch.empty(T, nq, D, dtype=qkv.dtype, device=qkv.device)
@@ -406,7 +429,8 @@ def qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_si
         return q_out
     native().qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer.k,
                                  kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, q_out, nq, nkv, D,
-                                 kv_layer.block_size, kv_layer.block_stride, kv_layer.scale_block_stride, eps)
+                                 kv_layer.block_size, kv_layer.block_stride, kv_layer.scale_block_stride, eps,
+                                 part, splits)
     count_launches()
     return q_out
 

@@ -270,6 +270,29 @@ def test_qknorm_rope_kvstore(D, nq, nkv):
     torch.testing.assert_close(pg.data.cpu().float(), pc.data.float(), atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("T", [1, 32, 256])
+def test_qkv_splitk_partials_into_qknorm_same_bits(T):
+    """Decode-size QKV: the GEMM's split-K partials summed inside the q/k-norm
+    kernel give the same q and KV bits as linear (split-K + reduce) then q/k-norm."""
+    D, nq, nkv, bs = 128, 32, 4, 16
+    n, k = (nq + 2 * nkv) * D, 2048
+    assert ops.plan_dense(T, n // 128, k // 64)[1] > 1 or T >= 256
+    q8, s8 = _fp8_weight(1, n, k, 21)
+    x = (torch.randn(T, k, device=DEV) * 0.5).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=DEV)
+    slots = torch.randperm(40 * bs, device=DEV)[:T].to(torch.int32)
+    qw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    cs = ops.rope_cos_sin(D, 4096, 1e6, DEV)
+    pa, pb = _pool(41, bs, nkv, D), _pool(41, bs, nkv, D)
+    qkv = torch.empty(T, n, dtype=torch.bfloat16, device=DEV)
+    qa = ops.qkv_norm_rope_kvstore(x, q8[0], s8[0], pos, slots, qw, kw, cs, pa.layer(0), nq, nkv, D, 1e-6, qkv,
+                                   torch.empty(T, nq, D, dtype=torch.bfloat16, device=DEV))
+    qb = ops.qknorm_rope_kvstore(ops.linear(x, q8[0], s8[0]), pos, slots, qw, kw, cs, pb.layer(0), nq, nkv, D, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb) and torch.equal(pa.data, pb.data)
+
+
 def test_router_topk():
     T, E, k = 77, 128, 8
     logits = torch.randn(T, 256, device=DEV)
