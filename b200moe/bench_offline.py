@@ -178,6 +178,7 @@ def parse_args(argv=None):
     p.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
                    help="preset model / batch / lengths of a named workload")
     p.add_argument("--kv-cache-dtype", choices=("bf16", "int8"), default="bf16")
+    p.add_argument("--kv-int8-mode", choices=("token", "channel"), default="token")
     p.add_argument("--kv-offload", action="store_true", help="host KV offload of evicted prefix blocks")
     p.add_argument("--kv-offload-host-blocks", type=int, default=256)
     p.add_argument("--num-kvcache-blocks", type=int, default=-1, help="-1: size the pool from free memory")
@@ -213,7 +214,8 @@ def engine_kwargs(args) -> dict:
               scheduler_policy=args.scheduler_policy, max_model_len=max(max_len, 256),
               max_num_seqs=max(batches + probe_batches + [len(VERIFY_PROMPTS)]),
               max_num_batched_tokens=args.max_num_batched_tokens, kvcache_block_size=args.kvcache_block_size,
-              seed=args.seed, kv_cache_dtype=args.kv_cache_dtype, attention_parallel=args.attention_parallel)
+              seed=args.seed, kv_cache_dtype=args.kv_cache_dtype, kv_int8_mode=args.kv_int8_mode,
+              attention_parallel=args.attention_parallel)
     if args.kv_offload:
         kw.update(kv_offload_enabled=True, kv_offload_host_blocks=args.kv_offload_host_blocks)
     if args.num_kvcache_blocks > 0:

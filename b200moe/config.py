@@ -168,6 +168,9 @@ class Config:
     decode_moe_backend: str | None = None
     attention_backend: str = "paged"
     kv_cache_dtype: str = "bf16"
+    # int8 KV quantisation: "token" (per token-head absmax scales) or "channel" (the
+    # reference's calibrated per-channel scales + exact bf16 outlier dims)
+    kv_int8_mode: str = "token"
     expert_placement: str = "linear"
     expert_map_path: str | None = None
     scheduler_policy: str = "fcfs"
@@ -225,6 +228,8 @@ class Config:
             raise ValueError("attention_backend must be 'paged' (native) or 'sdpa'")
         if self.kv_cache_dtype not in ("bf16", "int8"):
             raise ValueError("kv_cache_dtype must be 'bf16' or 'int8'")
+        if self.kv_int8_mode not in ("token", "channel"):
+            raise ValueError("kv_int8_mode must be 'token' or 'channel'")
         if self.kv_offload_enabled:
             if self.kv_cache_dtype != "bf16":
                 raise ValueError("KV offload requires the bf16 KV cache")

@@ -391,7 +391,7 @@ void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tens
                          Tensor cos_sin, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
                          c10::optional<Tensor> v_scale, Tensor q_out, int64_t num_q_heads, int64_t num_kv_heads,
                          int64_t head_dim, int64_t block_size, int64_t block_stride, int64_t scale_block_stride,
-                         double eps, c10::optional<Tensor> part, int64_t splits) {
+                         double eps, c10::optional<Tensor> part, int64_t splits, std::vector<int64_t> chan) {
   CHECK_CUDA(qkv); CHECK_DT(qkv, torch::kBFloat16); CHECK_DT(positions, torch::kInt32);
   CHECK_DT(slot_mapping, torch::kInt32); CHECK_DT(cos_sin, torch::kFloat32); CHECK_CONTIG(q_out);
   TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride must be 1");
@@ -411,7 +411,7 @@ void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tens
   a.kv_int8 = k_cache.scalar_type() == torch::kInt8;
   a.k_scale = ptr_or_null<float>(k_scale);
   a.v_scale = ptr_or_null<float>(v_scale);
-  if (a.kv_int8) TORCH_CHECK(a.k_scale && a.v_scale, "int8 KV needs scale pools");
+  if (a.kv_int8 && chan.empty()) TORCH_CHECK(a.k_scale && a.v_scale, "int8 KV needs scale pools");
   a.block_size = (int)block_size;
   a.block_stride = block_stride;
   a.scale_block_stride = scale_block_stride;
@@ -427,6 +427,20 @@ void qknorm_rope_kvstore(Tensor qkv, Tensor positions, Tensor slot_mapping, Tens
     a.part = part->data_ptr<float>();
     a.splits = (int)splits;
     a.part_stride = (int64_t)T * qkv.stride(0);
+  }
+  if (!chan.empty()) {
+    // int8 channel mode: [scale, out_idx, n_out, side_k, side_v, side_block_stride, calib_amax, calib_sum]
+    TORCH_CHECK(chan.size() == 8 && a.kv_int8, "channel mode: 8 entries and an int8 pool");
+    a.kv_int8 = 2;
+    a.ch_scale = reinterpret_cast<const float*>(chan[0]);
+    a.out_idx = reinterpret_cast<const int*>(chan[1]);
+    a.n_out = reinterpret_cast<const int*>(chan[2]);
+    a.side_k = reinterpret_cast<void*>(chan[3]);
+    a.side_v = reinterpret_cast<void*>(chan[4]);
+    a.side_block_stride = chan[5];
+    a.calib_amax = reinterpret_cast<float*>(chan[6]);
+    a.calib_sum = reinterpret_cast<float*>(chan[7]);
+    TORCH_CHECK(a.ch_scale && a.out_idx && a.n_out && a.side_k && a.side_v, "channel mode pointers");
   }
   b200::qknorm_rope_kvstore(a, T, stream());
 }
@@ -597,10 +611,24 @@ void moe_permute(Tensor x, Tensor ids, Tensor counts, Tensor cursor, Tensor x_pe
                     x_perm.data_ptr(), slot_of_row.data_ptr<int>(), ptr_or_null<int>(offsets_out), stream());
 }
 
+// int8 channel mode of the attention kernels: [dscale, out_idx, n_out, side_k, side_v, side_block_stride]
+static void set_kv_channel(int* kv_int8, b200::KvChannel* ch, const std::vector<int64_t>& chan) {
+  if (chan.empty()) return;
+  TORCH_CHECK(chan.size() == 6 && *kv_int8, "channel mode: 6 entries and an int8 pool");
+  *kv_int8 = 2;
+  ch->dscale = reinterpret_cast<const float*>(chan[0]);
+  ch->out_idx = reinterpret_cast<const int*>(chan[1]);
+  ch->n_out = reinterpret_cast<const int*>(chan[2]);
+  ch->side_k = reinterpret_cast<const void*>(chan[3]);
+  ch->side_v = reinterpret_cast<const void*>(chan[4]);
+  ch->side_block_stride = chan[5];
+}
+
 void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
                  c10::optional<Tensor> v_scale, Tensor block_tables, Tensor seq_lens, Tensor out, Tensor part_o,
                  Tensor part_m, Tensor part_l, int64_t block_size, int64_t block_stride, int64_t num_kv_heads,
-                 double scale, int64_t num_splits, int64_t split_len, c10::optional<Tensor> status) {
+                 double scale, int64_t num_splits, int64_t split_len, c10::optional<Tensor> status,
+                 std::vector<int64_t> chan) {
   CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_DT(q, torch::kBFloat16);
   CHECK_DT(block_tables, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_CONTIG(block_tables);
   const int B = (int)q.size(0);
@@ -631,6 +659,7 @@ void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor>
   a.out = out.data_ptr();
   a.num_blocks = (int)k_cache.size(0);
   a.status = ptr_or_null<int>(status);
+  set_kv_channel(&a.kv_int8, &a.ch, chan);
   if (num_splits > 1)
     TORCH_CHECK(part_m.numel() >= (int64_t)B * nq * num_splits && part_o.numel() >= (int64_t)B * nq * num_splits * D,
                 "split workspace too small");
@@ -640,7 +669,7 @@ void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor>
 void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale,
                   c10::optional<Tensor> v_scale, Tensor cu_seqlens_q, Tensor seq_lens, Tensor block_tables,
                   Tensor out, int64_t max_q_len, int64_t block_size, int64_t block_stride, int64_t num_kv_heads,
-                  double scale, c10::optional<Tensor> status) {
+                  double scale, c10::optional<Tensor> status, std::vector<int64_t> chan) {
   CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_DT(q, torch::kBFloat16);
   CHECK_DT(cu_seqlens_q, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_DT(block_tables, torch::kInt32);
   CHECK_CONTIG(block_tables); CHECK_CONTIG(cu_seqlens_q);
@@ -668,6 +697,7 @@ void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor
   a.status = ptr_or_null<int>(status);
   a.q_rows = (int)q.size(0);
   a.batch = B;
+  set_kv_channel(&a.kv_int8, &a.ch, chan);
   b200::paged_prefill_attn(a, B, (int)max_q_len, stream());
 }
 

@@ -5,13 +5,27 @@
 
 namespace b200 {
 
+constexpr int kKvNoutMax = 4;  // exact bf16 outlier dims per (layer, kv head), int8 channel mode
+
+// int8 KV "channel" mode (kv_int8 == 2): per-channel read scales and up to
+// kKvNoutMax exact bf16 outlier dims per kv head, kept in a side pool.
+struct KvChannel {
+  const float* dscale;         // layer: [2, kv_heads, D] (k then v), 0 at outlier dims
+  const int* out_idx;          // layer: [kv_heads, kKvNoutMax]
+  const int* n_out;            // layer: [kv_heads]
+  const void* side_k;          // layer base of the side pool [blocks, kv_heads, block_size, kKvNoutMax] bf16
+  const void* side_v;
+  int64_t side_block_stride;   // elements between consecutive blocks
+};
+
 struct DecodeArgs {
   const void* q;             // [B, q_heads, D] bf16
   const void* k_cache;       // layer base of the pool, [blocks, kv_heads, block_size, D]
   const void* v_cache;
   const float* k_scale;      // int8 KV scales (unused for bf16)
   const float* v_scale;
-  int kv_int8;
+  int kv_int8;               // 0 bf16, 1 int8 per-token scales, 2 int8 channel mode (ch)
+  KvChannel ch;
   const int* block_tables;   // [B, max_blocks]
   const int* seq_lens;       // [B] keys per sequence (including the current token)
   int max_blocks;
@@ -37,7 +51,8 @@ struct PrefillArgs {
   const void* v_cache;
   const float* k_scale;
   const float* v_scale;
-  int kv_int8;
+  int kv_int8;               // 0 bf16, 1 int8 per-token scales, 2 int8 channel mode (ch)
+  KvChannel ch;
   const int* cu_seqlens_q;   // [B + 1]
   const int* seq_lens;       // [B] total keys (cached + new)
   const int* block_tables;   // [B, max_blocks]

@@ -34,6 +34,16 @@ struct QkvArgs {
   const float* part;
   int splits;
   int64_t part_stride;
+  // int8 channel mode (kv_int8 == 2): per-channel store scales, exact outlier dims
+  // in the side pool, and (while calibrating) running max / sum of |x| per channel
+  const float* ch_scale;    // layer: [2, kv_heads, D]
+  const int* out_idx;       // layer: [kv_heads, 4]
+  const int* n_out;         // layer: [kv_heads]
+  void* side_k;             // layer base of the side pool [blocks, kv_heads, block_size, 4] bf16
+  void* side_v;
+  int64_t side_block_stride;
+  float* calib_amax;        // layer: [2, kv_heads, D], or null when not calibrating
+  float* calib_sum;
 };
 
 void embed_gather(const int* ids, const void* table, void* out, int T, int H, int V, int* status,

@@ -88,7 +88,8 @@ template <int D, int NT>
 __device__ __forceinline__ void load_kv_tile(uint32_t sk, uint32_t sv, const void* kc_, const void* vc_,
                                              const float* ks, const float* vs, bool int8, const int* btab,
                                              int bs, int64_t block_stride, int64_t sblock_stride, int h,
-                                             int k0, int k_end, uint8_t* sk_gen, uint8_t* sv_gen) {
+                                             int k0, int k_end, uint8_t* sk_gen, uint8_t* sv_gen,
+                                             bool chan = false, KvChannel ch = KvChannel{}, int nkv = 0) {
   constexpr int CPR = D / 8;  // 16-byte chunks per bf16 row
   if (!int8) {
     const bf16* kc = static_cast<const bf16*>(kc_);
@@ -120,6 +121,59 @@ __device__ __forceinline__ void load_kv_tile(uint32_t sk, uint32_t sv, const voi
   // int8: 8 values per thread-iteration, dequantised into the bf16 tile
   const int8_t* kc = static_cast<const int8_t*>(kc_);
   const int8_t* vc = static_cast<const int8_t*>(vc_);
+  if (chan) {
+    // channel mode: q * per-channel read scale, then the head's exact outlier dims from the side pool
+    const float* kds = ch.dscale + (size_t)h * D;
+    const float* vds = ch.dscale + (size_t)(nkv + h) * D;
+    const int n_out = ch.n_out[h];
+    int od[kKvNoutMax];
+#pragma unroll
+    for (int i = 0; i < kKvNoutMax; ++i) od[i] = i < n_out ? ch.out_idx[h * kKvNoutMax + i] : -1;
+    const bf16* sdk = static_cast<const bf16*>(ch.side_k);
+    const bf16* sdv = static_cast<const bf16*>(ch.side_v);
+    for (int idx = threadIdx.x; idx < kKT * CPR; idx += NT) {
+      const int r = idx / CPR, c = idx % CPR;
+      const int key = k0 + r;
+      uint4 ko = make_uint4(0, 0, 0, 0), vo = make_uint4(0, 0, 0, 0);
+      if (key < k_end) {
+        const int blk = btab[key / bs];
+        const int64_t tok = (int64_t)h * bs + key % bs;
+        const int64_t off = (int64_t)blk * block_stride + tok * D + c * 8;
+        const uint2 kq = *reinterpret_cast<const uint2*>(kc + off);
+        const uint2 vq = *reinterpret_cast<const uint2*>(vc + off);
+        const int8_t* kb = reinterpret_cast<const int8_t*>(&kq);
+        const int8_t* vb = reinterpret_cast<const int8_t*>(&vq);
+        float kf[8], vf[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          kf[j] = (float)kb[j] * kds[c * 8 + j];
+          vf[j] = (float)vb[j] * vds[c * 8 + j];
+        }
+#pragma unroll
+        for (int i = 0; i < kKvNoutMax; ++i) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (od[i] == c * 8 + j) {  // an exact bf16 value replaces the (zero) int8 payload
+              const int64_t so = (int64_t)blk * ch.side_block_stride + tok * kKvNoutMax + i;
+              kf[j] = __bfloat162float(sdk[so]);
+              vf[j] = __bfloat162float(sdv[so]);
+            }
+          }
+        }
+        uint32_t kw[4], vw[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          kw[j] = pack_bf16(kf[2 * j], kf[2 * j + 1]);
+          vw[j] = pack_bf16(vf[2 * j], vf[2 * j + 1]);
+        }
+        ko = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+        vo = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      }
+      *reinterpret_cast<uint4*>(sk_gen + tile_off<D>(r, c)) = ko;
+      *reinterpret_cast<uint4*>(sv_gen + tile_off<D>(r, c)) = vo;
+    }
+    return;
+  }
   for (int idx = threadIdx.x; idx < kKT * CPR; idx += NT) {
     const int r = idx / CPR, c = idx % CPR;
     const int key = k0 + r;
@@ -270,7 +324,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   for (int p = 0; p < kKVStages - 1; ++p) {
     if (p < ntiles)
       load_kv_tile<D, NT>(sk0 + p * TB, sv0 + p * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
-                          a.block_size, a.block_stride, sbs, h, k_begin + p * kKT, k_end, sK + p * TB, sV + p * TB);
+                          a.block_size, a.block_stride, sbs, h, k_begin + p * kKT, k_end, sK + p * TB, sV + p * TB,
+                          a.kv_int8 == 2, a.ch, a.num_kv_heads);
     cp_async_commit();
   }
   __syncthreads();
@@ -298,7 +353,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
       const int nb = (t + kKVStages - 1) % kKVStages;
       load_kv_tile<D, NT>(sk0 + nb * TB, sv0 + nb * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
                           a.block_size, a.block_stride, sbs, h, k_begin + (t + kKVStages - 1) * kKT, k_end,
-                          sK + nb * TB, sV + nb * TB);
+                          sK + nb * TB, sV + nb * TB, a.kv_int8 == 2, a.ch, a.num_kv_heads);
     }
     cp_async_commit();
     cp_async_wait<kKVStages - 1>();
@@ -994,7 +1049,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
   for (int p = 0; p < kKVStages - 1; ++p) {
     if (p < ntiles)
       load_kv_tile<D, NT>(sk0 + p * TB, sv0 + p * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
-                          a.block_size, a.block_stride, sbs, h, p * kKT, k_end, sK + p * TB, sV + p * TB);
+                          a.block_size, a.block_stride, sbs, h, p * kKT, k_end, sK + p * TB, sV + p * TB,
+                          a.kv_int8 == 2, a.ch, a.num_kv_heads);
     cp_async_commit();
   }
   __syncthreads();
@@ -1027,7 +1083,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
       const int nb = (t + kKVStages - 1) % kKVStages;
       load_kv_tile<D, NT>(sk0 + nb * TB, sv0 + nb * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
                           a.block_size, a.block_stride, sbs, h, (t + kKVStages - 1) * kKT, k_end, sK + nb * TB,
-                          sV + nb * TB);
+                          sV + nb * TB, a.kv_int8 == 2, a.ch, a.num_kv_heads);
     }
     cp_async_commit();
     cp_async_wait<kKVStages - 1>();
@@ -1198,7 +1254,9 @@ void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
   }
   if (a.group > 16 || 64 % a.group) throw std::runtime_error("decode attention: GQA group must divide 64 and be <= 16");
   if (a.split_len % kKT) throw std::runtime_error("decode attention: split_len % 64");
-  if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("decode attention: int8 KV needs scales");
+  if (a.kv_int8 == 1 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("decode attention: int8 KV needs scales");
+  if (a.kv_int8 == 2 && (!a.ch.dscale || !a.ch.out_idx || !a.ch.n_out || !a.ch.side_k || !a.ch.side_v))
+    throw std::runtime_error("decode attention: int8 channel mode needs its scales and side pool");
   dim3 grid(a.num_splits, a.num_kv_heads, B);
   if (a.head_dim == 128) {
     smem_opt_in(decode_attn_kernel<128>, decode_smem<128>());
@@ -1217,7 +1275,9 @@ void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
 void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t s) {
   if (B == 0 || max_q_len == 0) return;
   if (a.group > 16 || 64 % a.group) throw std::runtime_error("prefill attention: GQA group must divide 64");
-  if (a.kv_int8 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("prefill attention: int8 KV needs scales");
+  if (a.kv_int8 == 1 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("prefill attention: int8 KV needs scales");
+  if (a.kv_int8 == 2 && (!a.ch.dscale || !a.ch.out_idx || !a.ch.n_out || !a.ch.side_k || !a.ch.side_v))
+    throw std::runtime_error("prefill attention: int8 channel mode needs its scales and side pool");
   int sub_rows = 0;
   if (fmha_prefill_supported(a, &sub_rows)) {
     fmha_prefill(a, B, max_q_len, sub_rows, s);

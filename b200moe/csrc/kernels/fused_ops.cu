@@ -267,7 +267,41 @@ __global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
       const int blk = slot / a.block_size, bo = slot % a.block_size;
       const int64_t off = (int64_t)blk * a.block_stride + ((int64_t)kvh * a.block_size + bo) * D;
       const int64_t soff = (int64_t)blk * a.scale_block_stride + (int64_t)kvh * a.block_size + bo;
-      if (a.kv_int8) {
+      if (a.kv_int8 == 2) {
+        // channel mode: q = clamp(floor(x / scale[d] + 0.5), +-127) per channel; the head's
+        // outlier dims store 0 and their exact bf16 value goes to the side pool
+        const int kv = is_k ? 0 : 1;
+        const float* sc = a.ch_scale + ((size_t)kv * nkv + kvh) * D;
+        int8_t* dst = reinterpret_cast<int8_t*>(is_k ? a.k_cache : a.v_cache) + off;
+        bf16* side = reinterpret_cast<bf16*>(is_k ? a.side_k : a.side_v) +
+                     (int64_t)blk * a.side_block_stride + ((int64_t)kvh * a.block_size + bo) * 4;
+        const int n_out = a.n_out[kvh];
+        int od[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) od[i] = i < n_out ? a.out_idx[kvh * 4 + i] : -1;
+        float* cmax = a.calib_amax != nullptr ? a.calib_amax + ((size_t)kv * nkv + kvh) * D : nullptr;
+        float* csum = a.calib_sum != nullptr ? a.calib_sum + ((size_t)kv * nkv + kvh) * D : nullptr;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int e = 0; e < E2; ++e) {
+            const int d = half * (D / 2) + lane * E2 + e;
+            const float xv = bf16r(half ? x2[e] : x1[e]);
+            int q = (int)fmaxf(-127.f, fminf(127.f, floorf(xv / sc[d] + 0.5f)));
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (od[i] == d) {
+                q = 0;
+                side[i] = __float2bfloat16(xv);
+              }
+            dst[d] = (int8_t)q;
+            if (cmax != nullptr) {  // |x| >= 0: its float bits order like the values
+              atomicMax(reinterpret_cast<int*>(cmax + d), __float_as_int(fabsf(xv)));
+              atomicAdd(csum + d, fabsf(xv));
+            }
+          }
+        }
+      } else if (a.kv_int8) {
         // per-(token, head) absmax scale, round-to-nearest into [-127, 127]
         float m = 0.f;
 #pragma unroll

@@ -79,6 +79,37 @@ class LLMEngine:
         self._grammar_cache: dict = {}
         self._exited = False
         atexit.register(self.exit)
+        self.kv_outlier_dims = None
+        if config.kv_cache_dtype == "int8" and config.kv_int8_mode == "channel":
+            self._calibrate_int8_kv()
+
+    def _calibrate_int8_kv(self):
+        """int8 channel mode: run a few prompts through every rank with statistics on,
+        freeze the per-channel scales and outlier dims, then forget the calibration
+        traffic (prefix cache, counters).  The reference does the same at start-up
+        with eight mixed-language prompts (nanovllm/engine/llm_engine.py:88-131);
+        here the prompts are fixed pseudo-random token ids, as the model may have no
+        real tokenizer."""
+        import random
+        rng = random.Random(1234)
+        vocab = self.config.hf_config.vocab_size
+        lens = [96, 160, 64, 224, 128, 192, 80, 144]
+        cap = max(8, self.config.max_model_len - 32)
+        prompts = [[rng.randrange(vocab) for _ in range(min(n, cap))] for n in lens]
+        try:
+            self.executor.call("kv_calibrate_begin")
+            self.generate(prompts, SamplingParams(temperature=0.0, max_tokens=16, ignore_eos=True), use_tqdm=False)
+            self.scheduler.clear_prefix_cache()
+            self.kv_outlier_dims = self.executor.call("kv_calibrate_freeze")
+        except Exception:
+            self.exit()
+            raise
+        self.step_count = 0
+        self.schedule_mode_counts.clear()
+        self.prefill_tokens_total = self.decode_tokens_total = 0
+        self.schedule_time_total = self.forward_time_total = 0.0
+        self.last_token_events = []
+        self.last_step_metrics = None
 
     # ------------------------------------------------------------ teardown
     def _force_exit(self):

@@ -234,7 +234,7 @@ class ModelRunner:
         int8 = c.kv_cache_dtype == "int8"
         nkv = self.model.nkv_local
         block_bytes = KVPool.bytes_per_block(a.num_hidden_layers, nkv, self.block_size, a.head_dim,
-                                             self.model.dtype, int8)
+                                             self.model.dtype, int8, c.kv_int8_mode)
         if c.num_kvcache_blocks <= 0:
             if self.device.type == "cuda":
                 free, total = torch.cuda.mem_get_info(self.device)
@@ -251,7 +251,8 @@ class ModelRunner:
         if c.num_kvcache_blocks <= 0:
             raise RuntimeError(f"no memory left for the KV cache (block = {block_bytes / 2**20:.1f} MiB)")
         self.kv = KVPool(c.num_kvcache_blocks + 1, a.num_hidden_layers, nkv, self.block_size, a.head_dim,
-                         self.model.dtype, self.device, int8=int8)
+                         self.model.dtype, self.device, int8=int8, int8_mode=c.kv_int8_mode)
+        self._calib_tokens = None  # int8 channel mode: tokens stored while calibrating
         self.block_bytes = block_bytes
         self.scratch_block = self.kv.scratch_block
 
@@ -391,6 +392,8 @@ class ModelRunner:
             logits, tokens = logits[:B], tokens[:B]
         else:
             views = self._upload(plan)
+            if self._calib_tokens is not None:
+                self._calib_tokens += plan.num_tokens
             with self.profiler.range("forward"):
                 h = self.model(self._inputs(plan, views), self.kv)
             logits = self.model.compute_logits(h)
@@ -496,6 +499,26 @@ class ModelRunner:
         self.offloader.release(slot)
 
     # ----------------------------------------------------------- timing
+    # ----------------------------------------------- int8 channel calibration
+    def kv_calibrate_begin(self):
+        """int8 channel mode: collect per-channel max |x| and sum |x| of every K / V the
+        eager steps store (graph-replayed decode steps are not counted, as in the
+        reference, whose hooks see prefill forwards only)."""
+        if self.kv.int8_mode != "channel":
+            raise RuntimeError("KV calibration needs kv_cache_dtype='int8' with kv_int8_mode='channel'")
+        self.kv.calibrate_begin()
+        self._calib_tokens = 0
+
+    def kv_calibrate_freeze(self) -> int:
+        """Freeze store / read scales and the outlier dims; returns the number of outlier dims."""
+        if self._calib_tokens is None:
+            raise RuntimeError("kv_calibrate_freeze without kv_calibrate_begin")
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        n = self.kv.calibrate_freeze(self._calib_tokens)
+        self._calib_tokens = None
+        return n
+
     def reset_step_timing(self):
         self._step_events.clear()
         ops.reset_launch_count()

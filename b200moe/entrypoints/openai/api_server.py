@@ -366,6 +366,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--gpu-memory-utilization", type=float, default=float(_env("GPU_MEMORY_UTILIZATION", "0.9")))
     p.add_argument("--kvcache-block-size", type=int, default=int(_env("KVCACHE_BLOCK_SIZE", "256")))
     p.add_argument("--kv-cache-dtype", default=_env("KV_CACHE_DTYPE", "bf16"), choices=["bf16", "int8"])
+    p.add_argument("--kv-int8-mode", default=_env("KV_INT8_MODE", "token"), choices=["token", "channel"],
+                   help="int8 KV: per token-head scales, or the reference's calibrated per-channel scales")
     p.add_argument("--scheduler-policy", default=_env("SCHEDULER_POLICY", "stall_free"),
                    choices=["fcfs", "stall_free", "stall_free_lpm"])
     p.add_argument("--prefill-chunk-size", type=int, default=int(_env("PREFILL_CHUNK_SIZE", "256")))
@@ -397,7 +399,7 @@ def engine_kwargs(a) -> dict:
                 attention_parallel=a.attention_parallel, moe_backend=a.moe_backend, max_model_len=a.max_model_len,
                 max_num_seqs=a.max_num_seqs, max_num_batched_tokens=a.max_num_batched_tokens,
                 gpu_memory_utilization=a.gpu_memory_utilization, kvcache_block_size=a.kvcache_block_size,
-                kv_cache_dtype=a.kv_cache_dtype, scheduler_policy=a.scheduler_policy,
+                kv_cache_dtype=a.kv_cache_dtype, kv_int8_mode=a.kv_int8_mode, scheduler_policy=a.scheduler_policy,
                 prefill_chunk_size=a.prefill_chunk_size, scheduler_overlap=a.scheduler_overlap,
                 kv_offload_enabled=a.kv_offload, kv_offload_host_blocks=a.kv_offload_host_blocks,
                 enforce_eager=a.enforce_eager, max_queue_size=a.max_queue_size, metrics_path=a.metrics_path,

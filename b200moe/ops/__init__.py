@@ -430,7 +430,7 @@ def qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_si
     native().qknorm_rope_kvstore(qkv, positions, slot_mapping, q_norm_w, k_norm_w, cos_sin, kv_layer.k,
                                  kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, q_out, nq, nkv, D,
                                  kv_layer.block_size, kv_layer.block_stride, kv_layer.scale_block_stride, eps,
-                                 part, splits)
+                                 part, splits, _chan_store(kv_layer))
     count_launches()
     return q_out
 
@@ -485,6 +485,25 @@ def moe_permute(x, ids, counts, cursor, x_perm, slot_of_row, offsets_out=None):
     count_launches()
 
 
+def _chan_read(kv_layer) -> list[int]:
+    """Device pointers of the int8 channel mode's read side (attention kernels), or []."""
+    c = kv_layer.chan
+    if c is None:
+        return []
+    return [c.dscale.data_ptr(), c.out_idx.data_ptr(), c.n_out.data_ptr(), c.side_k.data_ptr(),
+            c.side_v.data_ptr(), c.side_block_stride]
+
+
+def _chan_store(kv_layer) -> list[int]:
+    """Device pointers of the int8 channel mode's store side (KV-store kernel), or []."""
+    c = kv_layer.chan
+    if c is None:
+        return []
+    return [c.scale.data_ptr(), c.out_idx.data_ptr(), c.n_out.data_ptr(), c.side_k.data_ptr(), c.side_v.data_ptr(),
+            c.side_block_stride, c.calib_amax.data_ptr() if c.calibrating else 0,
+            c.calib_sum.data_ptr() if c.calibrating else 0]
+
+
 def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len, num_splits, workspace):
     """q [B, nq, D], one query per sequence; keys are the first seq_lens[b] slots."""
     if not q.is_cuda:
@@ -493,7 +512,8 @@ def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len,
     part_o, part_m, part_l = workspace
     native().decode_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, block_tables, seq_lens,
                          out, part_o, part_m, part_l, kv_layer.block_size, kv_layer.block_stride,
-                         kv_layer.num_kv_heads, scale, num_splits, split_len, status_word(q.device))
+                         kv_layer.num_kv_heads, scale, num_splits, split_len, status_word(q.device),
+                         _chan_read(kv_layer))
     count_launches(2 if num_splits > 1 else 1)
     return out
 
@@ -503,7 +523,7 @@ def prefill_attention(q, kv_layer, cu_seqlens_q, seq_lens, block_tables, max_q_l
         return _attention_ref(q, kv_layer, block_tables, seq_lens, cu_seqlens_q, scale, out)
     native().prefill_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, cu_seqlens_q, seq_lens,
                           block_tables, out, max_q_len, kv_layer.block_size, kv_layer.block_stride,
-                          kv_layer.num_kv_heads, scale, status_word(q.device))
+                          kv_layer.num_kv_heads, scale, status_word(q.device), _chan_read(kv_layer))
     count_launches()
     return out
 

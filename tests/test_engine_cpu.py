@@ -2,6 +2,7 @@
 import random
 
 import numpy as np
+import torch
 import pytest
 
 from b200moe import LLM, SamplingParams
@@ -355,3 +356,44 @@ def test_logprobs_and_penalties_through_engine_cpu():
             assert vals == sorted(vals, reverse=True) and lp["chosen"] <= vals[0] + 1e-6 and lp["chosen"] <= 0.0
     finally:
         eng.exit()
+
+
+def test_int8_channel_kv_store_gather_and_calibration_cpu():
+    """The reference's int8 channel mode on the CPU path: calibration finds a planted
+    outlier channel (amax / mean |x| > 10), which then round-trips exactly through
+    the bf16 side pool while the other channels come back within half a quantum."""
+    from b200moe.engine.kv_cache import KVPool, NOUT_MAX
+    g = torch.Generator().manual_seed(0)
+    H, D, bs = 2, 64, 16
+    pool = KVPool(9, 1, H, bs, D, torch.bfloat16, "cpu", int8=True, int8_mode="channel")
+    layer = pool.layer(0)
+    k = torch.randn(40, H, D, generator=g)
+    v = torch.randn(40, H, D, generator=g)
+    k[3, 1, 5] = 80.0               # one rare large value: an outlier channel of K, head 1
+    slots = torch.arange(40, dtype=torch.int32)
+    pool.calibrate_begin()
+    layer.store(slots, k.to(torch.bfloat16), v.to(torch.bfloat16))
+    n = pool.calibrate_freeze(tokens_seen=40)
+    assert n >= 1 and int(pool.n_out[0, 1]) >= 1 and 5 in pool.out_idx[0, 1].tolist()
+    assert pool.n_out.max() <= NOUT_MAX and float(pool.ch_dscale[0, 0, 1, 5]) == 0.0
+    layer.store(slots, k.to(torch.bfloat16), v.to(torch.bfloat16))
+    kk, vv = layer.gather(torch.arange(3), 40)
+    kb = k.to(torch.bfloat16).float()
+    assert torch.equal(kk[:, 1, 5].float(), kb[:, 1, 5])      # the outlier channel is exact
+    step = pool.ch_scale[0, 0]                                # [H, D] quantum of K
+    err = (kk.float() - kb).abs()
+    assert (err <= step * 0.5 + 1e-2 * kb.abs() + 1e-6).all()
+
+
+def test_int8_channel_kv_engine_cpu():
+    """An engine in int8 channel mode calibrates at start-up and then generates."""
+    llm = LLM("tiny-moe", device="cpu", kvcache_block_size=16, num_kvcache_blocks=128, max_num_batched_tokens=512,
+              max_num_seqs=8, max_model_len=512, enforce_eager=True, kv_cache_dtype="int8", kv_int8_mode="channel")
+    try:
+        assert llm.kv_outlier_dims is not None
+        assert float(llm.model_runner.kv.ch_scale.max()) != 1.0 / 127.0  # frozen from real statistics
+        out = llm.generate([[5, 6, 7, 8, 9], list(range(30, 70))],
+                           SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True), use_tqdm=False)
+        assert all(len(o["token_ids"]) == 6 for o in out)
+    finally:
+        llm.exit()

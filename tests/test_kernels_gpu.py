@@ -1,6 +1,7 @@
 """Native sm_100a kernels against plain-PyTorch fp32 references of the same op."""
 import math
 
+import numpy as np
 import pytest
 import torch
 
@@ -637,3 +638,80 @@ def test_bounded_flag_wait_returns_status_instead_of_hanging():
     assert ns[0] == 0 and ns[1] == 0 and ns[2] < 1e8 and 1.5e9 < ns[3] < 2.5e9, ns
     x = torch.randn(4, 1000, device=DEV)  # the context still runs kernels
     assert torch.equal(ops.argmax(x).cpu().long(), x.argmax(dim=-1).cpu())
+
+
+def _channel_pool(num_blocks, bs, nkv, D, device=DEV, seed=3):
+    """An int8 channel-mode pool with frozen scales and 0-2 outlier dims per head, as
+    after calibration (identical on every device for the same seed)."""
+    pool = KVPool(num_blocks, 2, nkv, bs, D, torch.bfloat16, device, int8=True, int8_mode="channel")
+    g = torch.Generator().manual_seed(seed)
+    pool.ch_scale.copy_(torch.rand(pool.ch_scale.shape, generator=g) * 0.03 + 0.01)
+    pool.ch_dscale.copy_(pool.ch_scale)
+    for l in range(2):
+        for h in range(nkv):
+            n = h % 3
+            dims = torch.randperm(D, generator=g)[:n]
+            pool.out_idx[l, h, :n] = dims.to(torch.int32)
+            pool.n_out[l, h] = n
+            pool.ch_dscale[l, :, h, dims] = 0.0
+    return pool
+
+
+@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 4), (64, 4, 2)])
+def test_int8_channel_store_matches_torch_reference(D, nq, nkv):
+    """The reference's int8 channel store on the GPU against the torch store of the same
+    values: V (not normalised, so the same bf16 inputs reach both) bit for bit -- int8
+    payload, outlier dims zeroed, exact side values, calibration max; K (after the
+    kernels' own q/k-norm + RoPE rounding) within one quantum."""
+    T, bs = 40, 16
+    qkv = (torch.randn(T, (nq + 2 * nkv) * D, device=DEV) * 2).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=DEV)
+    slots = torch.randperm(8 * bs, device=DEV)[:T].to(torch.int32)
+    qw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, device=DEV)).to(torch.bfloat16)
+    cs = ops.rope_cos_sin(D, 4096, 1e6, DEV)
+    pg, pc = _channel_pool(9, bs, nkv, D, DEV), _channel_pool(9, bs, nkv, D, "cpu")
+    pg.calibrate_begin()
+    pc.calibrate_begin()
+    ops.qknorm_rope_kvstore(qkv, pos, slots, qw, kw, cs, pg.layer(1), nq, nkv, D, 1e-6)
+    ops.qknorm_rope_kvstore(qkv.cpu(), pos.cpu(), slots.cpu(), qw.cpu(), kw.cpu(), cs.cpu(), pc.layer(1),
+                            nq, nkv, D, 1e-6)
+    torch.cuda.synchronize()
+    g, c = pg.data.cpu(), pc.data
+    assert torch.equal(g[:, 1, 1], c[:, 1, 1]), "V int8 payload"
+    assert torch.equal(pg.side.cpu()[:, 1, 1], pc.side[:, 1, 1]), "V side values"
+    assert torch.equal(pg.calib_amax.cpu()[1, 1], pc.calib_amax[1, 1]), "V calibration max"
+    torch.testing.assert_close(pg.calib_sum.cpu()[1, 1], pc.calib_sum[1, 1], rtol=1e-5, atol=1e-4)
+    assert (g[:, 1, 0].int() - c[:, 1, 0].int()).abs().max() <= 1, "K within one quantum"
+    torch.testing.assert_close(pg.side.cpu()[:, 1, 0].float(), pc.side[:, 1, 0].float(), atol=3e-2, rtol=3e-2)
+
+
+@pytest.mark.parametrize("D,nq,nkv,bs", [(128, 32, 4, 256), (64, 4, 2, 16)])
+def test_int8_channel_attention_decode_and_prefill(D, nq, nkv, bs):
+    """Decode (split-KV) and prefill attention over an int8 channel-mode pool against
+    the fp32 reference over the same pool's dequantised K/V (per-channel read scales,
+    exact outlier dims from the side pool)."""
+    seq_lens = [1, 17, 255, 256, 257, 700]
+    B = len(seq_lens)
+    pool = _channel_pool(sum(math.ceil(L / bs) for L in seq_lens) + 2, bs, nkv, D)
+    tables = _fill_pool(pool, seq_lens, bs, nkv, D, True)
+    lens = torch.tensor(seq_lens, dtype=torch.int32, device=DEV)
+    q = torch.randn(B, nq, D, device=DEV).to(torch.bfloat16)
+    for split_len, nsplit in [(2048, 1), (64, 12)]:
+        ws = (torch.empty(B * nq * nsplit, D, device=DEV), torch.empty(B * nq * nsplit, device=DEV),
+              torch.empty(B * nq * nsplit, device=DEV))
+        out = torch.empty(B, nq, D, dtype=torch.bfloat16, device=DEV)
+        ops.decode_attention(q, pool.layer(1), tables, lens, D ** -0.5, out, split_len, nsplit, ws)
+        ref = torch.empty(B, nq, D, device=DEV)
+        ops._attention_ref(q, pool.layer(1), tables, lens, torch.arange(B + 1, dtype=torch.int32), D ** -0.5, ref)
+        torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+    qn = [min(L, 64) for L in seq_lens]
+    cu = torch.tensor([0] + list(np.cumsum(qn)), dtype=torch.int32, device=DEV)
+    qp = torch.randn(int(sum(qn)), nq, D, device=DEV).to(torch.bfloat16)
+    out = torch.empty_like(qp)
+    ops.prefill_attention(qp, pool.layer(1), cu, lens, tables, max(qn), D ** -0.5, out)
+    ref = torch.empty(qp.shape, device=DEV)
+    ops._attention_ref(qp, pool.layer(1), tables, lens, cu.cpu(), D ** -0.5, ref)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
