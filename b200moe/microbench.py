@@ -9,6 +9,7 @@ cases:
   decode     paged decode attention, T sequences of --ctx tokens
   prefill    paged prefill attention, T/--ctx sequences of --ctx tokens
   step       whole-model forward (eager) of T decode rows at --ctx context
+  ep         one expert-parallel MoE layer per rank under torchrun (fused peer-memory path)
   all        every kernel case above
 
 Each case prints a JSON line per kernel: milliseconds per call, the bytes or
@@ -246,6 +247,78 @@ def case_step(T, ctx, iters, layers=48):
     report("decode_step", ms, wbytes + kvbytes, 0, rows=T, ctx=ctx, layers=layers)
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's NVSwitch systems
+
+
+def case_ep(T, iters, reps=10):
+    """One expert-parallel MoE layer of Qwen3-30B-A3B on every rank of a torchrun job
+    (``torchrun --nproc-per-node W -m b200moe.microbench ep --tokens T``): router,
+    dispatch, scatter, grouped GEMMs, peer-scatter combine -- the fused peer-memory
+    path, ``reps`` layers per CUDA graph, device time max over ranks.  The roofline
+    is the slowest of: NVLink bytes (rows out + weighted rows back) at the measured
+    peer bandwidth, this rank's expert weights at the measured HBM copy rate, and
+    the expert FLOPs at the measured bf16 peak."""
+    from types import SimpleNamespace
+
+    import torch.distributed as dist
+
+    from b200moe.config import Config
+    from b200moe.engine.model_runner import expert_placement
+    from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM
+    from b200moe.parallel.ep import ExpertParallel
+    from b200moe.utils.weights import random_init_
+    rank, W = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev)
+    cfg = Config("qwen3-30b-a3b", max_num_batched_tokens=max(T, 16), max_num_seqs=max(T, 1))
+    args = cfg.hf_config
+    args.num_hidden_layers = 1
+    model = Qwen3MoeForCausalLM(args, dev, ep_rank=rank, ep_size=W, expert_ids=expert_placement(cfg, rank, W))
+    random_init_(model, seed=7)
+    model.tile_weights_()
+    model.reserve_workspace(max(T, 16), max(T, 1), 8)
+    runner = SimpleNamespace(world_size=W, rank=rank, device=dev, args=args, config=cfg, model=model)
+    ep = ExpertParallel(runner, "fused")
+    assert ep.backend == "fused"
+    model.ep = ep
+    layer = model.layers[0]
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = (torch.randn(T, args.hidden_size, device=dev, generator=g)).to(torch.bfloat16)
+    res0 = torch.randn(T, args.hidden_size, device=dev, generator=g).to(torch.bfloat16)
+    res = res0.clone()
+    fn = lambda: model._mlp(layer, x, res, model.norm, T)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    graph = _graph(fn, reps)
+    dist.barrier()
+    ms = _time_graph(graph, iters) / reps
+    ms_max = torch.tensor([ms], device=dev)
+    dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
+    ms = float(ms_max)
+    k, H, I = args.num_experts_per_tok, args.hidden_size, args.moe_intermediate_size
+    nvlink = 2 * T * k * H * 2 * (W - 1) / W               # bf16 rows to the owners and back, per rank
+    wbytes = model.num_local_experts * 3 * H * I            # e4m3 expert weights of this rank
+    flops = 2 * T * k * H * 3 * I                           # gate, up and down of the rows this rank receives
+    bw, tf, src = peaks()
+    t_link, t_hbm, t_tc = nvlink / (NVLINK_GBS * 1e9), wbytes / bw, flops / tf
+    roof = max(t_link, t_hbm, t_tc)
+    waits = ep.p2p.wait_stats()
+    if rank == 0:
+        print(json.dumps({"kernel": "ep_moe_layer", "world": W, "tokens_per_rank": T, "ms": round(ms, 4),
+                          "roofline_ms": round(roof * 1e3, 4), "roofline_frac": round(roof / (ms / 1e3), 3),
+                          "bound": ["nvlink", "hbm", "tensor"][[t_link, t_hbm, t_tc].index(roof)],
+                          "nvlink_bytes": int(nvlink), "weight_bytes": int(wbytes), "flops": int(flops),
+                          "peak": src, "nvlink_gbs": NVLINK_GBS,
+                          "wait_ms_rank0_over_run": waits}), flush=True)
+    model.ep = None
+    del graph
+    ep.p2p.close()
+    dist.destroy_process_group()
+
+
 def _trace_summary(name, buf):
     import statistics
     cap = (buf.numel() - 1) // 10
@@ -337,7 +410,7 @@ def case_trace(T):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "all"])
+    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "ep", "all"])
     p.add_argument("--tokens", type=int, default=256)
     p.add_argument("--ctx", type=int, default=1152)
     p.add_argument("--iters", type=int, default=20)
@@ -346,6 +419,8 @@ def main():
     p.add_argument("--pool-layers", type=int, default=2, help="decode: layers per KV block slab")
     p.add_argument("--only", choices=["", "gate_up", "down"], default="", help="moe: time one of the two GEMMs")
     a = p.parse_args()
+    if a.case == "ep":
+        return case_ep(a.tokens, a.iters)
     torch.cuda.set_device(0)
     if a.case in ("moe", "all"):
         case_moe(a.tokens, a.iters, only=a.only)
