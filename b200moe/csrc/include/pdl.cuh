@@ -1,16 +1,17 @@
 // Programmatic dependent launch: every kernel of this library is launched with
-// the programmatic-stream-serialization attribute and starts with pdl_enter():
-// it lets the next grid in the stream be scheduled as soon as all of its own CTAs
-// are running, then waits for the previous grid to complete (and its memory to be
-// visible) before touching any global memory.  Dependencies are exactly those of
-// plain stream order; what overlaps is the next grid's launch and CTA ramp-up
-// with this grid's tail.  Grids launched without the attribute (or by other
-// libraries) are waited for in full, and griddepcontrol.wait returns at once in a
-// grid that was not launched programmatically.
+// the programmatic-stream-serialization attribute when B200MOE_PDL=1 and starts
+// with pdl_enter(), which waits for the previous grid to complete (and its memory
+// to be visible) before touching any global memory.  The hot kernels end with
+// pdl_trigger(): once every CTA of the grid has reached it (or exited), the next
+// grid in the stream may be scheduled, so its launch and CTA ramp-up overlap this
+// grid's tail.  Dependencies are exactly those of plain stream order.  Grids
+// launched without the attribute (or by other libraries) are waited for in full,
+// and griddepcontrol.wait returns at once in a grid that was not launched
+// programmatically.
 //
-// Off by default (B200MOE_PDL=1 turns it on): with the trigger at kernel entry the
-// 48-layer decode step measured 16.93 ms against 16.50 ms without it -- the early
-// dependents' CTAs compete with the running grid for SM slots.
+// An earlier placement triggered at kernel entry: the dependents' CTAs then held
+// SM slots while the running grid still needed them (decode step 16.93 ms against
+// 16.50 ms without PDL).
 #pragma once
 #include <cuda_runtime.h>
 
@@ -24,10 +25,10 @@
 
 namespace b200 {
 
-__device__ __forceinline__ void pdl_enter() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
+__device__ __forceinline__ void pdl_enter() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next programmatically launched grid be scheduled once every CTA has called it or exited.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 inline bool pdl_enabled() {
   static const bool on = [] {

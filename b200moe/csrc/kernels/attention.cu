@@ -447,6 +447,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
       }
     }
   }
+  pdl_trigger();
 }
 
 template <int D>
@@ -473,6 +474,7 @@ __global__ void decode_combine_kernel(const DecodeArgs a) {
     bf16* out = static_cast<bf16*>(a.out) + ((size_t)b * nq + head) * D;
     out[col] = __float2bfloat16(l > 0.f ? acc / l : 0.f);
   }
+  pdl_trigger();
 }
 
 // ============================================================ decode (TMA)
@@ -730,6 +732,7 @@ __global__ void __launch_bounds__(160) decode_attn_tma_kernel(const __grid_const
       }
     }
   }
+  pdl_trigger();
 }
 
 // ------------------------------------------------- persistent TMA decode
@@ -1005,6 +1008,7 @@ __global__ void __launch_bounds__(160) decode_attn_persist_kernel(const __grid_c
     }
   }
   __syncthreads();
+  pdl_trigger();
 }
 
 // ================================================================= prefill
@@ -1138,6 +1142,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
       *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
     }
   }
+  pdl_trigger();
 }
 
 // --------------------------------------------------------------- launchers

@@ -460,6 +460,7 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap kv_map, const __grid_con
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------------ host side

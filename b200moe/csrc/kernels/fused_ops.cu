@@ -86,6 +86,7 @@ __global__ void embed_gather_kernel(const int* __restrict__ ids, const bf16* __r
   const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
   uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------- RMSNorm
@@ -138,6 +139,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const bf16* __restrict__ x,
     for (int e = 0; e < 8; ++e) o[e] = bf16r(v[j][e] * inv) * wf[e];
     *reinterpret_cast<uint4*>(out + base + idx) = pack8(o);
   }
+  pdl_trigger();
 }
 
 // Combine the top-k expert slots of each token in fixed order, add the
@@ -196,6 +198,7 @@ __global__ void __launch_bounds__(NT) moe_combine_kernel(const bf16* __restrict_
     for (int e = 0; e < 8; ++e) o[e] = bf16r(v[j][e] * inv) * wf[e];
     *reinterpret_cast<uint4*>(out + base + idx) = pack8(o);
   }
+  pdl_trigger();
 }
 
 // ------------------------------------------------ q/k norm + RoPE + KV store
@@ -325,6 +328,7 @@ __global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
       }
     }
   }
+  pdl_trigger();
 }
 
 // --------------------------------------------------------------- router
@@ -402,6 +406,7 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
     p[j] = e < E ? bf16r(row[e]) : -INFINITY;
   }
   topk_row<EPL>(p, E, topk, renorm, warp, lane, ids, weights, counts);
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------ fused router
@@ -552,6 +557,7 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
     }
     topk_row<4>(p, E, topk, renorm, tok, lane, ids, weights, counts);
   }
+  pdl_trigger();
 }
 
 // Each warp copies one routed (token, k) row to its expert-sorted position.
@@ -591,6 +597,7 @@ __global__ void moe_permute_kernel(const bf16* __restrict__ x, const int* __rest
   const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * H);
   uint4* dst = reinterpret_cast<uint4*>(x_perm + (size_t)pos * H);
   for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+  pdl_trigger();
 }
 
 // --------------------------------------------------------------- launchers
@@ -623,6 +630,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
   } else {
     *reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * ld_out + c) = acc;
   }
+  pdl_trigger();
 }
 
 // KV handoff: grid (blocks, chunks); each CTA streams a contiguous part of one
@@ -634,6 +642,7 @@ __global__ void kv_blocks_copy_kernel(const uint4* __restrict__ src, const int* 
   const int64_t per = (vecs + gridDim.y - 1) / gridDim.y;
   const int64_t lo = blockIdx.y * per, hi = min(vecs, lo + per);
   for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[d0 + i] = src[s0 + i];
+  pdl_trigger();
 }
 
 // e4m3 [G, N, K] (row-major, or tile-major as ops.tile_fp8 lays it out) with
@@ -677,6 +686,7 @@ __global__ void dequant_weights_kernel(const uint8_t* __restrict__ q, const floa
   uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)g * N + n) * K + k);
   dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
   dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  pdl_trigger();
 }
 
 void dequant_weights(const void* q, const float* scale, void* out, int G, int N, int K, bool tiled, cudaStream_t s) {

@@ -749,6 +749,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         st_release_sys(reinterpret_cast<uint32_t*>(args.ep_done[r]) + args.ep_rank, epoch);
     }
   }
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------------ host side

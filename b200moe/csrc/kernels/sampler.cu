@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kST) argmax_kernel(const float* __restrict__ l
   }
   block_argmax(bv, bi, redv, redi);
   if (threadIdx.x == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  pdl_trigger();
 }
 
 // Token i passes the allowed-token bitmask (null mask: every token does).
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ l
   if (threadIdx.x == 0) a.lp_chosen[r] = row[tok] * inv_t - M - logZ;
   write_top_logprobs(row, V, inv_t, lo, am, lp_k, M, logZ, hist_u, hist_f, cand_v, cand_i, &n_cand,
                      a.lp_top_v + (size_t)r * lp_k, a.lp_top_i + (size_t)r * lp_k);
+  pdl_trigger();
 }
 
 __global__ void penalty_kernel(float* __restrict__ logits, int64_t ld, const int* __restrict__ rows,
@@ -376,6 +378,7 @@ __global__ void penalty_kernel(float* __restrict__ logits, int64_t ld, const int
   const int c = gen_counts[i];
   if (c > 0) v = v - presence[r] - frequency[r] * (float)c;
   *p = v;
+  pdl_trigger();
 }
 
 static void check_launch(const char* what) {

@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(NT) tp_slots_partial_kernel(TpArgs a, const bf
     const uint32_t e = *a.epoch + 1;
     for (int r = 0; r < a.world; ++r) st_release_sys(a.flags[r] + a.rank, e);
   });
+  pdl_trigger();
 }
 
 template <int NT, int VPT>
@@ -158,6 +159,7 @@ __global__ void __launch_bounds__(NT) tp_allreduce_rmsnorm_kernel(TpArgs a, bf16
     }
   }
   last_cta(a.counter, [&] { *a.epoch = want; });
+  pdl_trigger();
 }
 
 void check_args(const TpArgs& a, int H) {
