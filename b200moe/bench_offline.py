@@ -273,7 +273,8 @@ def main(argv=None):
             prompts = make_prompts(batch, prompt_len, vocab, seed=batch, shared_prefix_len=shared)
             llm.generate(prompts, params, use_tqdm=False)
             for rep in range(args.repeats):
-                if cache_mode == "cold":
+                if cache_mode in ("cold", "none"):
+                    # "none": no measured pass may reuse the warm-up's (or another pass's) prompt KV
                     llm.scheduler.clear_prefix_cache()
                 before = llm.scheduler.metrics()
                 llm.executor.call_all("reset_step_timing")
