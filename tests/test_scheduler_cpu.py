@@ -366,3 +366,57 @@ def test_scheduler_block_manager_fuzz(policy, lru, offload, dp, monkeypatch):
     assert all(s.finish_reason in ("length", "stop", "cancelled") for s in all_seqs)
     assert {s.finish_reason for s in all_seqs} >= {"length", "stop"}
     assert sum(bm.prefix_cache_hit_tokens for bm in sch.block_managers) > 0
+
+
+def test_build_plan_matches_per_row_definition():
+    """The vectorised decode rows of build_plan equal the per-row definition: decode
+    rows first (their id is the last token, or 0 with a feed row when the token is
+    still on the device), positions, KV slots through the block table, context
+    lengths, padded block tables; prefill rows continue from their cached length."""
+    import random as rnd
+    import numpy as np
+    from b200moe.engine.sequence import Sequence
+    from b200moe.engine.step_plan import build_plan
+    from b200moe.sampling_params import SamplingParams
+    rng = rnd.Random(5)
+    bs = 16
+    Sequence.block_size = bs
+    seqs, qlens, flags = [], [], []
+    for j in range(30):
+        n = rng.randint(1, 90)
+        s = Sequence([rng.randrange(1000) for _ in range(n)], SamplingParams(temperature=0.0))
+        prefill = j % 4 == 0
+        s.cached_len = rng.randint(0, n - 1) if prefill else n - 1
+        q = (n - s.cached_len) if prefill else 1
+        s.block_table = rng.sample(range(500), -(-(n + 1) // bs))
+        seqs.append(s)
+        qlens.append(q)
+        flags.append(prefill)
+    feed = {id(s): k for k, s in enumerate(seqs) if not flags[k] and k % 3 == 0}
+    plan = build_plan(seqs, qlens, flags, bs, max_blocks=8, feed=feed)
+    order = sorted(range(len(seqs)), key=lambda i: (flags[i], i))
+    ids, pos, slots, lens, src = [], [], [], [], []
+    for i in order:
+        s = seqs[i]
+        if flags[i]:
+            start = s.cached_len
+            toks = s.tokens[start:start + qlens[i]]
+            fs = [-1] * qlens[i]
+        elif id(s) in feed:
+            start, toks, fs = len(s), [0], [feed[id(s)]]
+        else:
+            start, toks, fs = len(s) - 1, [s.last], [-1]
+        p = list(range(start, start + qlens[i]))
+        ids += toks
+        pos += p
+        slots += [s.block_table[x // bs] * bs + x % bs for x in p]
+        lens.append(start + qlens[i])
+        src += fs
+    assert plan.num_decode == sum(1 for f in flags if not f)
+    assert plan.input_ids.tolist() == ids and plan.positions.tolist() == pos
+    assert plan.slot_mapping.tolist() == slots and plan.seq_lens.tolist() == lens
+    assert plan.feed_src.tolist() == src
+    for r, i in enumerate(order):
+        bt = seqs[i].block_table
+        assert plan.block_tables[r, :len(bt)].tolist() == bt and not plan.block_tables[r, len(bt):].any()
+    assert plan.rows.tolist() == order and np.all(np.diff(plan.cu_seqlens_q) == [qlens[i] for i in order])
