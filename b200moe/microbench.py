@@ -10,6 +10,7 @@ cases:
   prefill    paged prefill attention, T/--ctx sequences of --ctx tokens
   step       whole-model forward (eager) of T decode rows at --ctx context
   ep         one expert-parallel MoE layer per rank under torchrun (fused peer-memory path)
+  tp         tensor-parallel O projection + rank sum + RMSNorm under torchrun, fused vs NCCL
   all        every kernel case above
 
 Each case prints a JSON line per kernel: milliseconds per call, the bytes or
@@ -319,6 +320,72 @@ def case_ep(T, iters, reps=10):
     dist.destroy_process_group()
 
 
+def case_tp(T, iters, reps=10, H=2048, K_total=4096):
+    """Tensor-parallel O projection + sum over ranks + residual RMSNorm for T tokens on
+    every rank of a torchrun job (``--nproc-per-node W -m b200moe.microbench tp``):
+    the fused peer-memory path (parallel/tp.py) against the NCCL path (GEMM,
+    all-reduce, RMSNorm), ``reps`` calls per CUDA graph, max over ranks.  The fused
+    path's roofline is the slowest of this rank's e4m3 weight slice at the measured
+    HBM rate and the (W-1) fp32 partials it reads over NVLink."""
+    from types import SimpleNamespace
+
+    import torch.distributed as dist
+
+    from b200moe.parallel.tp import TpComm
+    from b200moe.utils.weights import quantize_block_fp8
+    rank, W = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev)
+    K = K_total // W
+    runner = SimpleNamespace(world_size=W, rank=rank, device=dev, args=SimpleNamespace(hidden_size=H),
+                             config=SimpleNamespace(max_num_batched_tokens=max(T, 16)))
+    tp = TpComm.create(runner)
+    assert tp is not None
+    g = torch.Generator(device=dev).manual_seed(rank)
+    q, sc = quantize_block_fp8(torch.randn(1, H, K, device=dev, generator=g) * 0.02)
+    w8 = ops.tile_fp8(q[0])
+    x = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+    res = torch.randn(T, H, device=dev).to(torch.bfloat16)
+    nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+    o = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+
+    def fused():
+        tp.begin_forward(1)
+        tp.o_proj_add_norm(x, w8, sc[0], res, nw, 1e-6, out, True)
+
+    def nccl():
+        ops.linear(x, w8, sc[0], out=o, tiled=True)
+        dist.all_reduce(o)
+        ops.rmsnorm(o, nw, 1e-6, residual=res, out=out)
+
+    times = {}
+    for name, fn in (("fused", fused), ("nccl", nccl)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = _graph(fn, reps)
+        dist.barrier()
+        t = torch.tensor([_time_graph(graph, iters) / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times[name] = float(t)
+        del graph
+    bw, tf, src = peaks()
+    wbytes = H * K                                   # this rank's e4m3 O slice
+    nvlink = (W - 1) * T * H * 4                     # fp32 partials read from every peer
+    roof = max(wbytes / bw, nvlink / (NVLINK_GBS * 1e9), 2 * T * H * K / tf)
+    if rank == 0:
+        print(json.dumps({"kernel": "tp_o_proj_allreduce_norm", "world": W, "tokens": T,
+                          "fused_ms": round(times["fused"], 4), "nccl_ms": round(times["nccl"], 4),
+                          "roofline_ms": round(roof * 1e3, 4), "fused_roofline_frac": round(roof * 1e3 / times["fused"], 3),
+                          "nvlink_bytes": nvlink, "weight_bytes": wbytes, "peak": src,
+                          "wait_ms_rank0": tp.wait_stats()}), flush=True)
+    tp.close()
+    dist.destroy_process_group()
+
+
 def _trace_summary(name, buf):
     import statistics
     cap = (buf.numel() - 1) // 10
@@ -410,7 +477,7 @@ def case_trace(T):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "ep", "all"])
+    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "ep", "tp", "all"])
     p.add_argument("--tokens", type=int, default=256)
     p.add_argument("--ctx", type=int, default=1152)
     p.add_argument("--iters", type=int, default=20)
@@ -421,6 +488,8 @@ def main():
     a = p.parse_args()
     if a.case == "ep":
         return case_ep(a.tokens, a.iters)
+    if a.case == "tp":
+        return case_tp(a.tokens, a.iters)
     torch.cuda.set_device(0)
     if a.case in ("moe", "all"):
         case_moe(a.tokens, a.iters, only=a.only)
