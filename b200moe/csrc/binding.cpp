@@ -701,6 +701,34 @@ void prefill_attn(Tensor q, Tensor k_cache, Tensor v_cache, c10::optional<Tensor
   b200::paged_prefill_attn(a, B, (int)max_q_len, stream());
 }
 
+void kv_int8_stage(Tensor k_cache, Tensor v_cache, c10::optional<Tensor> k_scale, c10::optional<Tensor> v_scale,
+                   Tensor block_tables, Tensor seq_lens, Tensor stage, int64_t block_size, int64_t block_stride,
+                   int64_t num_kv_heads, std::vector<int64_t> chan) {
+  CHECK_CUDA(k_cache); CHECK_DT(k_cache, torch::kInt8); CHECK_DT(v_cache, torch::kInt8);
+  CHECK_DT(block_tables, torch::kInt32); CHECK_DT(seq_lens, torch::kInt32); CHECK_CONTIG(block_tables);
+  CHECK_DT(stage, torch::kBFloat16); CHECK_CONTIG(stage);
+  const int64_t B = block_tables.size(0), mb = block_tables.size(1), D = k_cache.size(-1);
+  TORCH_CHECK(seq_lens.numel() >= B, "seq_lens rows");
+  TORCH_CHECK(stage.numel() >= B * mb * 2 * num_kv_heads * block_size * D, "stage too small");
+  b200::KvStageArgs a{};
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.kv_int8 = 1;
+  a.k_scale = ptr_or_null<float>(k_scale);
+  a.v_scale = ptr_or_null<float>(v_scale);
+  set_kv_channel(&a.kv_int8, &a.ch, chan);
+  a.block_tables = block_tables.data_ptr<int>();
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.batch = (int)B;
+  a.max_blocks = (int)mb;
+  a.block_size = (int)block_size;
+  a.block_stride = block_stride;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.head_dim = (int)D;
+  a.stage = stage.data_ptr();
+  b200::kv_int8_stage(a, stream());
+}
+
 void argmax(Tensor logits, Tensor out) {
   CHECK_CUDA(logits); CHECK_DT(logits, torch::kFloat32); CHECK_DT(out, torch::kInt32);
   TORCH_CHECK(logits.stride(1) == 1, "logits inner stride must be 1");
@@ -779,6 +807,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("decode_attn", &decode_attn);
   m.def("prefill_attn", &prefill_attn);
+  m.def("kv_int8_stage", &kv_int8_stage);
   m.def("argmax", &argmax);
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
   m.def("ep_dispatch", &ep_dispatch);

@@ -70,6 +70,30 @@ struct PrefillArgs {
   int batch;                 // sequences (set by the launcher)
 };
 
+// int8 KV -> bf16 staging pool for the tensor-core prefill.  Block j of sequence b
+// (j < ceil(seq_lens[b] / block_size)) is dequantised to staging block b * max_blocks + j,
+// laid out as the bf16 pool's blocks are ([k|v][kv_heads][block_size][head_dim]); slots
+// at or past seq_lens[b] are written as zeros.  Values are the ones the int8 attention
+// kernels compute while staging (fp32 product, rounded to bf16 once).
+struct KvStageArgs {
+  const void* k_cache;       // int8 layer bases
+  const void* v_cache;
+  const float* k_scale;      // kv_int8 == 1
+  const float* v_scale;
+  int kv_int8;               // 1 per-token scales, 2 channel mode (ch)
+  KvChannel ch;
+  const int* block_tables;   // [batch, max_blocks]
+  const int* seq_lens;       // [batch]
+  int batch;
+  int max_blocks;
+  int block_size;
+  int64_t block_stride;      // int8 elements between consecutive blocks of the layer
+  int num_kv_heads;
+  int head_dim;
+  void* stage;               // bf16 [batch * max_blocks][2][kv_heads][block_size][head_dim]
+};
+void kv_int8_stage(const KvStageArgs& a, cudaStream_t s);
+
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s);
 void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t s);
 

@@ -52,6 +52,11 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
   const int n = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
 }
+template <int N>  // 4 or 8 bytes (.ca: the 16-byte .cg form is cp_async16)
+__device__ __forceinline__ void cp_async_small(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? N : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(dst), "l"(src), "n"(N), "r"(n) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -202,6 +207,144 @@ __device__ __forceinline__ void load_kv_tile(uint32_t sk, uint32_t sv, const voi
   }
 }
 
+// ------------------------------------------------ int8 decode: raw staging
+// The int8 decode kernel copies each tile's raw payload (and its per-token scales,
+// or the channel mode's outlier side values) with cp.async into a ring of raw
+// slots, kKVStages tiles ahead, and dequantises one slot into the bf16 compute
+// tile just before its MMAs: the global loads stay asynchronous, as in the bf16
+// kernel, and the pool is read at one byte per value.
+template <int D>
+struct Int8Slots {
+  static constexpr int RAW = kKT * D;               // bytes of one raw K (or V) tile
+  static constexpr int SC = kKT * 4;                // per-token scales of one tile
+  static constexpr int SIDE = kKT * kKvNoutMax * 2; // outlier side values of one tile
+  static constexpr int BYTES = kKVStages * (RAW + SC + SIDE);
+  static_assert(BYTES <= (kKVStages - 1) * kKT * D * 2, "int8 slots fit in the bf16 stages 1..S-1");
+  __device__ static uint8_t* raw(uint8_t* base, int slot) { return base + slot * RAW; }
+  __device__ static float* scale(uint8_t* base, int slot) {
+    return reinterpret_cast<float*>(base + kKVStages * RAW + slot * SC);
+  }
+  __device__ static bf16* side(uint8_t* base, int slot) {
+    return reinterpret_cast<bf16*>(base + kKVStages * (RAW + SC) + slot * SIDE);
+  }
+};
+
+template <int D, int NT>
+__device__ __forceinline__ void issue_int8_tile(uint8_t* kb, uint8_t* vb, int slot, const DecodeArgs& a,
+                                                const int* btab, int64_t sbs, int h, int k0, int k_end) {
+  using S = Int8Slots<D>;
+  constexpr int CPR = D / 16;  // 16-byte chunks per int8 row
+  static_assert(NT % CPR == 0 && kKT % (NT / CPR) == 0, "tile / thread mapping");
+  constexpr int RPI = NT / CPR, ITERS = kKT / RPI;
+  const int8_t* kc = static_cast<const int8_t*>(a.k_cache);
+  const int8_t* vc = static_cast<const int8_t*>(a.v_cache);
+  const int bs = a.block_size;
+  const int c = threadIdx.x % CPR, r0 = threadIdx.x / CPR;
+  int64_t off[ITERS];
+#pragma unroll
+  for (int i = 0; i < ITERS; ++i) {  // all block-table lookups first, then the copies
+    const int key = k0 + r0 + i * RPI;
+    off[i] = key < k_end ? (int64_t)btab[key / bs] * a.block_stride + ((int64_t)h * bs + key % bs) * D + c * 16 : -1;
+  }
+  const uint32_t rk = smem_u32(S::raw(kb, slot)), rv = smem_u32(S::raw(vb, slot));
+#pragma unroll
+  for (int i = 0; i < ITERS; ++i) {
+    const int r = r0 + i * RPI;
+    const bool valid = off[i] >= 0;
+    const int64_t o = valid ? off[i] : 0;
+    cp_async16(rk + r * D + c * 16, kc + o, valid);
+    cp_async16(rv + r * D + c * 16, vc + o, valid);
+  }
+  for (int r = threadIdx.x; r < kKT; r += NT) {  // per-row metadata: one thread per key
+    const int key = k0 + r;
+    const bool valid = key < k_end;
+    const int blk = valid ? btab[key / bs] : 0;
+    const int64_t tok = valid ? (int64_t)h * bs + key % bs : 0;
+    if (a.kv_int8 == 2) {
+      const int64_t so = (int64_t)blk * a.ch.side_block_stride + tok * kKvNoutMax;
+      cp_async_small<8>(smem_u32(S::side(kb, slot) + r * kKvNoutMax), static_cast<const bf16*>(a.ch.side_k) + so, valid);
+      cp_async_small<8>(smem_u32(S::side(vb, slot) + r * kKvNoutMax), static_cast<const bf16*>(a.ch.side_v) + so, valid);
+    } else {
+      const int64_t so = (int64_t)blk * sbs + tok;
+      cp_async_small<4>(smem_u32(S::scale(kb, slot) + r), a.k_scale + so, valid);
+      cp_async_small<4>(smem_u32(S::scale(vb, slot) + r), a.v_scale + so, valid);
+    }
+  }
+}
+
+// Per-thread constants of the channel mode: the thread's 8-value column chunk is
+// fixed (NT is a multiple of D / 8), so its read scales and outlier slots are too.
+template <int D>
+struct Int8Col {
+  float kds[8], vds[8];
+  int od[kKvNoutMax];  // outlier dim relative to the chunk start, -1 if none / elsewhere
+};
+
+template <int D, int NT>
+__device__ __forceinline__ void int8_col_init(Int8Col<D>& col, const DecodeArgs& a, int h) {
+  const int c = threadIdx.x % (D / 8);
+  if (a.kv_int8 != 2) return;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    col.kds[e] = a.ch.dscale[(size_t)h * D + c * 8 + e];
+    col.vds[e] = a.ch.dscale[(size_t)(a.num_kv_heads + h) * D + c * 8 + e];
+  }
+  const int n_out = a.ch.n_out[h];
+#pragma unroll
+  for (int i = 0; i < kKvNoutMax; ++i) {
+    const int d = i < n_out ? a.ch.out_idx[h * kKvNoutMax + i] - c * 8 : -1;
+    col.od[i] = d >= 0 && d < 8 ? d : -1;
+  }
+}
+
+__device__ __forceinline__ void int8x8_to_float(uint2 q, float (&f)[8]) {
+  const uint32_t w[2] = {q.x, q.y};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) f[e] = (float)(int8_t)((w[e >> 2] >> (8 * (e & 3))) & 0xffu);
+}
+
+// raw slot -> bf16 compute tiles (tile_off layout), the values load_kv_tile computes
+template <int D, int NT>
+__device__ __forceinline__ void dequant_int8_tile(uint8_t* kb, uint8_t* vb, int slot, uint8_t* tk, uint8_t* tv,
+                                                  bool chan, const Int8Col<D>& col) {
+  using S = Int8Slots<D>;
+  constexpr int CPR = D / 8;
+  const uint8_t* rk = S::raw(kb, slot);
+  const uint8_t* rv = S::raw(vb, slot);
+  for (int idx = threadIdx.x; idx < kKT * CPR; idx += NT) {
+    const int r = idx / CPR, c = idx % CPR;
+    float kf[8], vf[8];
+    int8x8_to_float(*reinterpret_cast<const uint2*>(rk + r * D + c * 8), kf);
+    int8x8_to_float(*reinterpret_cast<const uint2*>(rv + r * D + c * 8), vf);
+    if (chan) {
+      const bf16* sk = S::side(kb, slot) + r * kKvNoutMax;
+      const bf16* sv = S::side(vb, slot) + r * kKvNoutMax;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float x = kf[e] * col.kds[e], y = vf[e] * col.vds[e];
+#pragma unroll
+        for (int i = 0; i < kKvNoutMax; ++i) {
+          x = col.od[i] == e ? __bfloat162float(sk[i]) : x;
+          y = col.od[i] == e ? __bfloat162float(sv[i]) : y;
+        }
+        kf[e] = x;
+        vf[e] = y;
+      }
+    } else {
+      const float skl = S::scale(kb, slot)[r], svl = S::scale(vb, slot)[r];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kf[e] *= skl;
+        vf[e] *= svl;
+      }
+    }
+    *reinterpret_cast<uint4*>(tk + tile_off<D>(r, c)) =
+        make_uint4(pack_bf16(kf[0], kf[1]), pack_bf16(kf[2], kf[3]), pack_bf16(kf[4], kf[5]), pack_bf16(kf[6], kf[7]));
+    *reinterpret_cast<uint4*>(tv + tile_off<D>(r, c)) =
+        make_uint4(pack_bf16(vf[0], vf[1]), pack_bf16(vf[2], vf[3]), pack_bf16(vf[4], vf[5]), pack_bf16(vf[6], vf[7]));
+  }
+}
+
 // 128B-swizzled tile as a TMA load with CU_TENSOR_MAP_SWIZZLE_128B writes it:
 // [D / 64 halves][kKT rows][128 B], 16-byte unit u of row r stored at u ^ (r & 7).
 template <int D>
@@ -287,7 +430,7 @@ __device__ __forceinline__ void softmax_update(float (&s)[NB][4], float (&m_r)[2
 
 // ================================================================== decode
 // Q rows: r < G are heads h*G + r of the sequence's single query.
-template <int D>
+template <int D, bool INT8>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   pdl_enter();
   constexpr int NT = 128;
@@ -299,7 +442,6 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   const int k_begin = split * a.split_len;
   const int k_end = min(L, k_begin + a.split_len);
   const int nq = a.num_kv_heads * G;
-  const bool int8 = a.kv_int8 != 0;
   const int64_t sbs = a.block_stride / a.head_dim;  // int8 scale pool block stride
 
   uint8_t* sQ = smem;                                   // [16][D]
@@ -320,12 +462,22 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
   const uint32_t sk0 = smem_u32(sK), sv0 = smem_u32(sV);
   const int ntiles = k_end > k_begin ? (k_end - k_begin + kKT - 1) / kKT : 0;
   constexpr int TB = kKT * D * 2;  // bytes of one K (or V) tile
+  // int8: raw slots live in the bf16 stages 1..S-1, stage 0 holds the dequantised compute tile
+  uint8_t* const rawK = sK + TB;
+  uint8_t* const rawV = sV + TB;
+  const bool chan = a.kv_int8 == 2;
+  Int8Col<D> col;
+  if constexpr (INT8) int8_col_init<D, NT>(col, a, h);
 #pragma unroll
   for (int p = 0; p < kKVStages - 1; ++p) {
-    if (p < ntiles)
-      load_kv_tile<D, NT>(sk0 + p * TB, sv0 + p * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
-                          a.block_size, a.block_stride, sbs, h, k_begin + p * kKT, k_end, sK + p * TB, sV + p * TB,
-                          a.kv_int8 == 2, a.ch, a.num_kv_heads);
+    if (p < ntiles) {
+      if constexpr (INT8)
+        issue_int8_tile<D, NT>(rawK, rawV, p, a, btab, sbs, h, k_begin + p * kKT, k_end);
+      else
+        load_kv_tile<D, NT>(sk0 + p * TB, sv0 + p * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, false, btab,
+                            a.block_size, a.block_stride, sbs, h, k_begin + p * kKT, k_end, sK + p * TB,
+                            sV + p * TB);
+    }
     cp_async_commit();
   }
   __syncthreads();
@@ -351,14 +503,24 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
     const int buf = t % kKVStages;
     if (t + kKVStages - 1 < ntiles) {
       const int nb = (t + kKVStages - 1) % kKVStages;
-      load_kv_tile<D, NT>(sk0 + nb * TB, sv0 + nb * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, int8, btab,
-                          a.block_size, a.block_stride, sbs, h, k_begin + (t + kKVStages - 1) * kKT, k_end,
-                          sK + nb * TB, sV + nb * TB, a.kv_int8 == 2, a.ch, a.num_kv_heads);
+      if constexpr (INT8)
+        issue_int8_tile<D, NT>(rawK, rawV, nb, a, btab, sbs, h, k_begin + (t + kKVStages - 1) * kKT, k_end);
+      else
+        load_kv_tile<D, NT>(sk0 + nb * TB, sv0 + nb * TB, a.k_cache, a.v_cache, a.k_scale, a.v_scale, false, btab,
+                            a.block_size, a.block_stride, sbs, h, k_begin + (t + kKVStages - 1) * kKT, k_end,
+                            sK + nb * TB, sV + nb * TB);
     }
     cp_async_commit();
     cp_async_wait<kKVStages - 1>();
     __syncthreads();
-    const uint32_t sk = sk0 + buf * TB, sv = sv0 + buf * TB;
+    uint32_t sk = sk0 + buf * TB, sv = sv0 + buf * TB;
+    if constexpr (INT8) {
+      // the previous tile's MMAs finished at the loop-end barrier: stage 0 is free
+      dequant_int8_tile<D, NT>(rawK, rawV, buf, sK, sV, chan, col);
+      __syncthreads();
+      sk = sk0;
+      sv = sv0;
+    }
     float s[2][4];
     qk_mma<D, 2>(s, qf, sk, warp * 16, lane);
     const int key0 = k_begin + t * kKT + warp * 16;
@@ -1248,6 +1410,18 @@ static void launch_decode_tma(const DecodeArgs& a, int B, int sub_rows, cudaStre
   if (a.num_splits > 1) pdl_launch(decode_combine_kernel<D>, dim3(a.num_kv_heads * a.group, B), D, 0, s, a);
 }
 
+template <int D>
+static void launch_decode_split(const DecodeArgs& a, int B, dim3 grid, cudaStream_t s) {
+  if (a.kv_int8) {
+    smem_opt_in(decode_attn_kernel<D, true>, decode_smem<D>());
+    pdl_launch(decode_attn_kernel<D, true>, grid, 128, decode_smem<D>(), s, a);
+  } else {
+    smem_opt_in(decode_attn_kernel<D, false>, decode_smem<D>());
+    pdl_launch(decode_attn_kernel<D, false>, grid, 128, decode_smem<D>(), s, a);
+  }
+  if (a.num_splits > 1) pdl_launch(decode_combine_kernel<D>, dim3(a.num_kv_heads * a.group, B), D, 0, s, a);
+}
+
 void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
   if (B == 0) return;
   int sub_rows = 0;
@@ -1264,17 +1438,113 @@ void paged_decode_attn(const DecodeArgs& a, int B, cudaStream_t s) {
     throw std::runtime_error("decode attention: int8 channel mode needs its scales and side pool");
   dim3 grid(a.num_splits, a.num_kv_heads, B);
   if (a.head_dim == 128) {
-    smem_opt_in(decode_attn_kernel<128>, decode_smem<128>());
-    pdl_launch(decode_attn_kernel<128>, grid, 128, decode_smem<128>(), s, a);
-    if (a.num_splits > 1) pdl_launch(decode_combine_kernel<128>, dim3(a.num_kv_heads * a.group, B), 128, 0, s, a);
+    launch_decode_split<128>(a, B, grid, s);
   } else if (a.head_dim == 64) {
-    smem_opt_in(decode_attn_kernel<64>, decode_smem<64>());
-    pdl_launch(decode_attn_kernel<64>, grid, 128, decode_smem<64>(), s, a);
-    if (a.num_splits > 1) pdl_launch(decode_combine_kernel<64>, dim3(a.num_kv_heads * a.group, B), 64, 0, s, a);
+    launch_decode_split<64>(a, B, grid, s);
   } else {
     throw std::runtime_error("decode attention: head_dim must be 64 or 128");
   }
   check_launch("paged_decode_attn");
+}
+
+// ========================================================= int8 -> bf16 stage
+// One CTA per (block of a sequence, k|v plane, kv head).  A thread owns one
+// 16-value column chunk (256 threads step whole rows), so its read scales
+// (channel mode) and outlier slots are loaded once.
+template <int D, bool CHAN>
+__global__ void __launch_bounds__(256) kv_int8_stage_kernel(const KvStageArgs a) {
+  pdl_enter();
+  constexpr int CPR = D / 16;  // 16-value chunks per row
+  static_assert(256 % CPR == 0, "thread / chunk mapping");
+  const int j = blockIdx.x, b = blockIdx.y;
+  const int kv = blockIdx.z / a.num_kv_heads, h = blockIdx.z % a.num_kv_heads;
+  const int bs = a.block_size;
+  const int L = a.seq_lens[b];
+  if ((int64_t)j * bs < L) {
+    const int valid = min(bs, L - j * bs);
+    const int blk = a.block_tables[(size_t)b * a.max_blocks + j];
+    const int8_t* src = static_cast<const int8_t*>(kv ? a.v_cache : a.k_cache) + (int64_t)blk * a.block_stride +
+                        (int64_t)h * bs * D;
+    bf16* dst = static_cast<bf16*>(a.stage) +
+                (((size_t)b * a.max_blocks + j) * 2 * a.num_kv_heads + (size_t)kv * a.num_kv_heads + h) * bs * D;
+    const int c = threadIdx.x % CPR;
+    float ds[16];
+    int od[kKvNoutMax];
+    const float* tsc = nullptr;
+    const bf16* side = nullptr;
+    if constexpr (CHAN) {
+      const float* row = a.ch.dscale + ((size_t)kv * a.num_kv_heads + h) * D + c * 16;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) ds[e] = row[e];
+      const int n_out = a.ch.n_out[h];
+#pragma unroll
+      for (int i = 0; i < kKvNoutMax; ++i) od[i] = i < n_out ? a.ch.out_idx[h * kKvNoutMax + i] - c * 16 : -1;
+      side = static_cast<const bf16*>(kv ? a.ch.side_v : a.ch.side_k) + (int64_t)blk * a.ch.side_block_stride +
+             (int64_t)h * bs * kKvNoutMax;
+    } else {
+      tsc = (kv ? a.v_scale : a.k_scale) + (int64_t)blk * (a.block_stride / D) + (int64_t)h * bs;
+    }
+    for (int tok = threadIdx.x / CPR; tok < bs; tok += 256 / CPR) {
+      uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
+      if (tok < valid) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(src + (int64_t)tok * D + c * 16);
+        const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+        float qv[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) qv[e] = (float)(int8_t)((rw[e >> 2] >> (8 * (e & 3))) & 0xff);
+        float f[16];
+        if constexpr (CHAN) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = qv[e] * ds[e];
+          float sd[kKvNoutMax];  // this token's exact outlier values (replacing a zero payload)
+#pragma unroll
+          for (int i = 0; i < kKvNoutMax; ++i)
+            sd[i] = od[i] >= 0 && od[i] < 16 ? __bfloat162float(side[(int64_t)tok * kKvNoutMax + i]) : 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float x = f[e];
+#pragma unroll
+            for (int i = 0; i < kKvNoutMax; ++i) x = od[i] == e ? sd[i] : x;
+            f[e] = x;
+          }
+        } else {
+          const float sc = tsc[tok];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = qv[e] * sc;
+        }
+        w0 = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+        w1 = make_uint4(pack_bf16(f[8], f[9]), pack_bf16(f[10], f[11]), pack_bf16(f[12], f[13]),
+                        pack_bf16(f[14], f[15]));
+      }
+      uint4* o = reinterpret_cast<uint4*>(dst + (int64_t)tok * D + c * 16);
+      o[0] = w0;
+      o[1] = w1;
+    }
+  }
+  pdl_trigger();
+}
+
+void kv_int8_stage(const KvStageArgs& a, cudaStream_t s) {
+  if (a.batch == 0 || a.max_blocks == 0) return;
+  if (a.kv_int8 == 1 && (!a.k_scale || !a.v_scale)) throw std::runtime_error("int8 stage: per-token mode needs scales");
+  if (a.kv_int8 == 2 && (!a.ch.dscale || !a.ch.out_idx || !a.ch.n_out || !a.ch.side_k || !a.ch.side_v))
+    throw std::runtime_error("int8 stage: channel mode needs its scales and side pool");
+  if (a.kv_int8 != 1 && a.kv_int8 != 2) throw std::runtime_error("int8 stage: the pool is not int8");
+  if (a.block_stride % 16 || (reinterpret_cast<uintptr_t>(a.k_cache) & 15) || (reinterpret_cast<uintptr_t>(a.v_cache) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.stage) & 15))
+    throw std::runtime_error("int8 stage: pool and stage must be 16-byte aligned");
+  dim3 grid(a.max_blocks, a.batch, 2 * a.num_kv_heads);
+  const bool chan = a.kv_int8 == 2;
+  if (a.head_dim == 128) {
+    if (chan) pdl_launch(kv_int8_stage_kernel<128, true>, grid, 256, 0, s, a);
+    else pdl_launch(kv_int8_stage_kernel<128, false>, grid, 256, 0, s, a);
+  } else if (a.head_dim == 64) {
+    if (chan) pdl_launch(kv_int8_stage_kernel<64, true>, grid, 256, 0, s, a);
+    else pdl_launch(kv_int8_stage_kernel<64, false>, grid, 256, 0, s, a);
+  } else {
+    throw std::runtime_error("int8 stage: head_dim must be 64 or 128");
+  }
+  check_launch("kv_int8_stage");
 }
 
 void paged_prefill_attn(const PrefillArgs& a, int B, int max_q_len, cudaStream_t s) {

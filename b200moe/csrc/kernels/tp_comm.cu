@@ -56,6 +56,8 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
   return u;
 }
 
+constexpr int kInFlight = 8;  // partial loads in flight per thread
+
 template <int NT>
 __device__ __forceinline__ float block_sum(float v, float* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -68,16 +70,19 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-// the last CTA of the grid to get here runs `fn` (after every CTA's stores are fenced at system scope)
-template <typename F>
+// The last CTA of the grid to get here runs `fn`.  SYS: every CTA's stores are
+// fenced at system scope first (fn publishes them to peers); otherwise fn only
+// needs every CTA to have arrived (a device-scope counter).
+template <bool SYS, typename F>
 __device__ __forceinline__ void last_cta(int* counter, F fn) {
-  __threadfence_system();
+  if constexpr (SYS) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    if constexpr (SYS) __threadfence_system();
+    else __threadfence();
     if (atomicAdd(counter, 1) == (int)gridDim.x - 1) {
       *counter = 0;
-      __threadfence_system();
+      if constexpr (SYS) __threadfence_system();
       fn();
     }
   }
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(NT) tp_slots_partial_kernel(TpArgs a, const bf
       *reinterpret_cast<float4*>(dst + idx + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
   }
-  last_cta(a.counter, [&] {
+  last_cta<true>(a.counter, [&] {
     const uint32_t e = *a.epoch + 1;
     for (int r = 0; r < a.world; ++r) st_release_sys(a.flags[r] + a.rank, e);
   });
@@ -130,13 +135,27 @@ __global__ void __launch_bounds__(NT) tp_allreduce_rmsnorm_kernel(TpArgs a, bf16
     for (int j = 0; j < VPT; ++j) {
       const int idx = (threadIdx.x + j * NT) * 8;
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int r = 0; r < a.world; ++r) {
-        for (int sp = 0; sp < a.splits; ++sp) {
-          const float* p = a.part[r] + sp * a.split_stride + base + idx;
-          const float4 x0 = *reinterpret_cast<const float4*>(p);
-          const float4 x1 = *reinterpret_cast<const float4*>(p + 4);
-          acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
-          acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+      // partial p = rank * splits + split, summed in that order; a batch of kInFlight
+      // loads is issued before any add, so peer round trips overlap
+      const int np = a.world * a.splits;
+      for (int p0 = 0; p0 < np; p0 += kInFlight) {
+        float4 x0[kInFlight], x1[kInFlight];
+#pragma unroll
+        for (int i = 0; i < kInFlight; ++i) {
+          const int pi = p0 + i;
+          if (pi < np) {
+            const int r = pi / a.splits, sp = pi - r * a.splits;
+            const float* p = a.part[r] + sp * a.split_stride + base + idx;
+            x0[i] = *reinterpret_cast<const float4*>(p);
+            x1[i] = *reinterpret_cast<const float4*>(p + 4);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kInFlight; ++i) {
+          if (p0 + i < np) {
+            acc[0] += x0[i].x; acc[1] += x0[i].y; acc[2] += x0[i].z; acc[3] += x0[i].w;
+            acc[4] += x1[i].x; acc[5] += x1[i].y; acc[6] += x1[i].z; acc[7] += x1[i].w;
+          }
         }
       }
       float rr[8];
@@ -158,7 +177,8 @@ __global__ void __launch_bounds__(NT) tp_allreduce_rmsnorm_kernel(TpArgs a, bf16
       *reinterpret_cast<uint4*>(out + base + idx) = pack8(o);
     }
   }
-  last_cta(a.counter, [&] { *a.epoch = want; });
+  // the epoch is read only by this GPU's later launches: a device-scope arrival suffices
+  last_cta<false>(a.counter, [&] { *a.epoch = want; });
   pdl_trigger();
 }
 

@@ -239,6 +239,8 @@ class ModelRunner:
             if self.device.type == "cuda":
                 free, total = torch.cuda.mem_get_info(self.device)
                 reserve = 3 << 30  # graphs, logits, transient allocator growth
+                if int8:
+                    reserve += ops.INT8_STAGE_MAX_BYTES  # bf16 staging of int8 blocks for the prefill kernel
                 budget = free - (1.0 - c.gpu_memory_utilization) * total - reserve
                 c.num_kvcache_blocks = int(budget // block_bytes)
             else:

@@ -518,9 +518,54 @@ def decode_attention(q, kv_layer, block_tables, seq_lens, scale, out, split_len,
     return out
 
 
+# int8 prefill: the referenced blocks are dequantised into a bf16 staging pool that
+# the tcgen05 prefill kernel reads.  Above this many staging bytes per call the
+# warp-MMA kernel that dequantises while staging runs instead.
+INT8_STAGE_MAX_BYTES = int(os.environ.get("B200MOE_INT8_STAGE_MB", "2048")) << 20
+_int8_stage: dict = {}
+
+
+def _int8_stage_buffers(device, blocks: int, block_elems: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-device bf16 staging pool and identity block ids, grown on demand (prefill
+    is never graph-captured, so growth cannot strand a captured address)."""
+    key = torch.device(device)
+    st = _int8_stage.get(key)
+    if st is None or st[0].numel() < blocks * block_elems or st[1].numel() < blocks:
+        st = (torch.empty(blocks * block_elems, dtype=torch.bfloat16, device=key),
+              torch.arange(blocks, dtype=torch.int32, device=key))
+        _int8_stage[key] = st
+    return st
+
+
+def _int8_prefill_staged(q, kv_layer, cu_seqlens_q, seq_lens, block_tables, max_q_len, scale, out) -> bool:
+    """int8 pool, head_dim 128: stage the rows' blocks as bf16 (one launch) and run
+    the tensor-core prefill on the stage (block b * max_blocks + j holds block j of
+    row b).  Returns False where the tensor-core kernel does not take the shape."""
+    D, nq = q.shape[2], q.shape[1]
+    nkv, bs = kv_layer.num_kv_heads, kv_layer.block_size
+    if (D != 128 or os.environ.get("B200MOE_PREFILL_TC") == "0" or os.environ.get("B200MOE_INT8_STAGE") == "0"
+            or 128 % (nq // nkv) or not (bs % 128 == 0 or (128 % bs == 0 and bs % 8 == 0))):
+        return False
+    B, mb = block_tables.shape
+    block_elems = 2 * nkv * bs * D
+    if B * mb * block_elems * 2 > INT8_STAGE_MAX_BYTES:
+        return False
+    stage, ids = _int8_stage_buffers(q.device, B * mb, block_elems)
+    native().kv_int8_stage(kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, block_tables, seq_lens,
+                           stage, bs, kv_layer.block_stride, nkv, _chan_read(kv_layer))
+    st = stage[:B * mb * block_elems].view(B * mb, 2, nkv * bs * D)
+    native().prefill_attn(q, st[:, 0], st[:, 1], None, None, cu_seqlens_q, seq_lens, ids[:B * mb].view(B, mb), out,
+                          max_q_len, bs, block_elems, nkv, scale, status_word(q.device), [])
+    count_launches(2)
+    return True
+
+
 def prefill_attention(q, kv_layer, cu_seqlens_q, seq_lens, block_tables, max_q_len, scale, out):
     if not q.is_cuda:
         return _attention_ref(q, kv_layer, block_tables, seq_lens, cu_seqlens_q, scale, out)
+    if kv_layer.k.dtype == torch.int8 and _int8_prefill_staged(q, kv_layer, cu_seqlens_q, seq_lens, block_tables,
+                                                               max_q_len, scale, out):
+        return out
     native().prefill_attn(q, kv_layer.k, kv_layer.v, kv_layer.k_scale, kv_layer.v_scale, cu_seqlens_q, seq_lens,
                           block_tables, out, max_q_len, kv_layer.block_size, kv_layer.block_stride,
                           kv_layer.num_kv_heads, scale, status_word(q.device), _chan_read(kv_layer))

@@ -71,6 +71,15 @@ def reference_arm(args):
     return ref.run(args, lambda i: workload(args, i), METRIC)
 
 
+def _parallelism(n: int, rep: dict) -> str:
+    """Layout label from what the engine reports: data-parallel attention with the experts
+    split by expert parallelism (``ep{n}+dp{n}-attn``), or head-sharded attention with the
+    experts split and every partial summed across ranks (``tp{n}``)."""
+    if rep.get("attention_parallel") == "tp":
+        return f"tp{n}" + ("-fused-peer-sums" if rep.get("tp_fused") else "-nccl")
+    return f"ep{n}+dp{n}-attn"
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -118,6 +127,7 @@ def main():
     split = runners.call("step_device_split")  # rank 0: where the device time goes
     launches = sum(runners.call_all("launch_count"))
     par = runners.call_all("parallel_report")
+    # the engine's actual layout, from rank 0's own report
     nsteps = llm.step_count - steps0
     h2d = (runners.runner.h2d_bytes - h2d0) / max(nsteps, 1)
     d2h = 4 * total_out / max(nsteps, 1)
@@ -131,7 +141,7 @@ def main():
         "dtype": "bf16 activations, e4m3 block-scaled weights",
         "data": "synthetic uniform-random token ids; random-init weights (seeded)",
         "config": {"model": args.model, "global_batch": args.num_requests, "seq_len": args.input_len,
-                   "output_len": args.output_len, "parallelism": f"ep{args.gpus}+{args.attention_parallel}{args.gpus}-attn",
+                   "output_len": args.output_len, "parallelism": _parallelism(args.gpus, par[0]),
                    "l2": "inputs larger than L2 (30 GB of weights per pass), no flush",
                    "prompts": "fresh uniform-random prompts every pass (no cross-pass prefix-cache hits)",
                    "scheduler_overlap": bool(args.scheduler_overlap),

@@ -657,6 +657,53 @@ def _channel_pool(num_blocks, bs, nkv, D, device=DEV, seed=3):
     return pool
 
 
+@pytest.mark.parametrize("mode", ["token", "channel"])
+@pytest.mark.parametrize("bs", [16, 256])
+def test_int8_prefill_staged_tensor_core(mode, bs, monkeypatch):
+    """int8 prefill through the bf16 staging pool and the tcgen05 kernel.  The stage
+    holds exactly the pool's dequantised values (torch dequantisation of the same
+    blocks, rounded to bf16 once) with zeros past each sequence, and the attention
+    matches the warp-MMA int8 kernel and the fp32 reference."""
+    D, nq, nkv = 128, 32, 4
+    shapes = [(300, 300), (64, 1000), (1, 257), (17, 17), (129, 400)]
+    seq_lens = [L for _, L in shapes]
+    nblocks = sum(math.ceil(L / bs) for L in seq_lens) + 2
+    pool = _channel_pool(nblocks, bs, nkv, D) if mode == "channel" else _pool(nblocks, bs, nkv, D, int8=True)
+    tables = _fill_pool(pool, seq_lens, bs, nkv, D, True)
+    layer = pool.layer(1)
+    lens = torch.tensor(seq_lens, dtype=torch.int32, device=DEV)
+    B, mb = tables.shape
+    stage = torch.full((B * mb * 2 * nkv * bs * D,), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.native().kv_int8_stage(layer.k, layer.v, layer.k_scale, layer.v_scale, tables, lens, stage, bs,
+                               layer.block_stride, nkv, ops._chan_read(layer))
+    torch.cuda.synchronize()
+    st = stage.view(B, mb, 2, nkv, bs, D)
+    for b, L in enumerate(seq_lens):
+        nb = math.ceil(L / bs)
+        k, v = layer.gather(tables[b], L)
+        for kv, want in ((0, k), (1, v)):
+            got = st[b, :nb, kv].permute(0, 2, 1, 3).reshape(nb * bs, nkv, D)
+            assert torch.equal(got[:L], want.to(torch.bfloat16)), (b, kv)
+            assert bool((got[L:] == 0).all()), "slots past the sequence are zero"
+    cu = [0]
+    for qn, _ in shapes:
+        cu.append(cu[-1] + qn)
+    q = torch.randn(cu[-1], nq, D, device=DEV).to(torch.bfloat16)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    mq = max(s for s, _ in shapes)
+    out_tc = torch.full((cu[-1], nq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.prefill_attention(q, layer, cu_t, lens, tables, mq, D ** -0.5, out_tc)
+    monkeypatch.setenv("B200MOE_INT8_STAGE", "0")
+    out_mma = torch.empty_like(out_tc)
+    ops.prefill_attention(q, layer, cu_t, lens, tables, mq, D ** -0.5, out_mma)
+    ref = torch.empty(q.shape, device=DEV)
+    ops._attention_ref(q, layer, tables, lens, cu_t.cpu(), D ** -0.5, ref)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    torch.testing.assert_close(out_tc.float(), ref, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(out_tc.float(), out_mma.float(), atol=2e-2, rtol=2e-2)
+
+
 @pytest.mark.parametrize("D,nq,nkv", [(128, 32, 4), (64, 4, 2)])
 def test_int8_channel_store_matches_torch_reference(D, nq, nkv):
     """The reference's int8 channel store on the GPU against the torch store of the same

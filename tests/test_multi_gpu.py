@@ -24,6 +24,38 @@ KW = dict(kvcache_block_size=16, max_num_seqs=16, max_num_batched_tokens=512, ma
 SP = SamplingParams(temperature=0.0, max_tokens=16, ignore_eos=True)
 
 
+def _greedy_trace(llm, prompts, n):
+    """Greedy tokens of every prompt with the top-2 log-probabilities at each position."""
+    sp = SamplingParams(temperature=0.0, max_tokens=n, ignore_eos=True, logprobs=2)
+    ids = [llm.add_request(p, sp) for p in prompts]
+    toks, tops = {i: [] for i in ids}, {i: [] for i in ids}
+    while not llm.is_finished():
+        llm.step()
+        for sid, tok, _, _, lp in llm.last_token_events:
+            if sid in toks:
+                toks[sid].append(tok)
+                tops[sid].append(lp["top"])
+    return [toks[i] for i in ids], [tops[i] for i in ids]
+
+
+def _assert_parts_only_at_near_ties(ref, ref_tops, other, max_gap=0.05):
+    """Two layouts of the same model sum partial results in different orders, so their
+    greedy runs may part where the reference's top two tokens are a near tie -- and then
+    only to the runner-up.  A part anywhere else is a numerical fault.  Returns the
+    fraction of positions before the first part (for the log)."""
+    same = 0
+    for i, (a, b) in enumerate(zip(ref, other)):
+        assert len(a) == len(b)
+        p = next((j for j, (x, y) in enumerate(zip(a, b)) if x != y), None)
+        same += len(a) if p is None else p
+        if p is None:
+            continue
+        (t1, v1), (t2, v2) = sorted(ref_tops[i][p], key=lambda tv: -tv[1])[:2]
+        assert t1 == a[p] and b[p] == t2 and v1 - v2 < max_gap, \
+            f"sequence {i} parts at {p}: ref {a[p]} (top-2 {t1}:{v1:.4f} {t2}:{v2:.4f}), other {b[p]}"
+    return same / sum(len(a) for a in ref)
+
+
 @pytest.fixture(scope="module")
 def single():
     llm = LLM("tiny-moe-fp8", enforce_eager=True, **KW)
@@ -51,7 +83,8 @@ def test_ep2_matches_single_gpu(single, backend, eager):
 def test_tp2_attention_matches_single_gpu(monkeypatch, fused, eager):
     """Tensor-parallel attention over 2 GPUs (head-sharded QKV/O, experts split):
     greedy tokens match one GPU on a 4-layer Qwen3-30B-A3B-shaped model (128-row
-    fp8 blocks align with the head split).  ``fused``: the O projection and the MoE
+    fp8 blocks align with the head split) up to a near tie of the single-GPU run's
+    top two tokens.  ``fused``: the O projection and the MoE
     partials are summed over peer memory inside the residual RMSNorm
     (parallel/tp.py); otherwise NCCL all-reduce.  ``eager=False`` replays the
     fused sums inside CUDA graphs."""
@@ -61,7 +94,7 @@ def test_tp2_attention_matches_single_gpu(monkeypatch, fused, eager):
     prompts = [[(13 * i + 7 * j) % 150000 + 1 for j in range(40 + 17 * i)] for i in range(6)]
     sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
     one = LLM("qwen3-30b-a3b-4l", **kw)
-    a = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False)]
+    a, a_tops = _greedy_trace(one, prompts, 12)
     one.exit()
     two = LLM("qwen3-30b-a3b-4l", tensor_parallel_size=2, attention_parallel="tp", **{**kw, "enforce_eager": eager})
     b = [o["token_ids"] for o in two.generate(prompts, sp, use_tqdm=False)]
@@ -71,8 +104,7 @@ def test_tp2_attention_matches_single_gpu(monkeypatch, fused, eager):
     two.exit()
     assert all(r["tp_fused"] == fused for r in reports), reports
     assert b == b2, "tensor-parallel decode must be run-to-run deterministic"
-    agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
-    assert agree > 0.9, agree
+    print("positions before the first part", _assert_parts_only_at_near_ties(a, a_tops, b))
 
 
 needs4 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4,
@@ -83,14 +115,15 @@ needs4 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_c
 def test_tp_all_gpus_with_kv_replication_matches_single_gpu():
     """Tensor-parallel attention over every visible GPU (8 on a full box): with 4 KV
     heads, 8 ranks hold one KV head each twice over (replicated) and 4 query heads
-    each; the fused peer-memory sums run in CUDA graphs.  Greedy tokens match one GPU."""
+    each; the fused peer-memory sums run in CUDA graphs.  Greedy tokens match one GPU up
+    to a near tie of its top two tokens."""
     W = 8 if torch.cuda.device_count() >= 8 else 4
     kw = dict(kvcache_block_size=64, max_num_seqs=8, max_num_batched_tokens=1024, max_model_len=512,
               num_kvcache_blocks=64, random_init="seeded")
     prompts = [[(13 * i + 7 * j) % 150000 + 1 for j in range(40 + 17 * i)] for i in range(6)]
     sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
     one = LLM("qwen3-30b-a3b-4l", enforce_eager=True, **kw)
-    a = [o["token_ids"] for o in one.generate(prompts, sp, use_tqdm=False)]
+    a, a_tops = _greedy_trace(one, prompts, 12)
     one.exit()
     many = LLM("qwen3-30b-a3b-4l", tensor_parallel_size=W, attention_parallel="tp", **kw)
     b = [o["token_ids"] for o in many.generate(prompts, sp, use_tqdm=False)]
@@ -98,8 +131,7 @@ def test_tp_all_gpus_with_kv_replication_matches_single_gpu():
     many.executor.call("check_status")
     many.exit()
     assert all(r["tp_fused"] and r["decode_graphs"] for r in reports), reports
-    agree = np.mean([x == y for ra, rb in zip(a, b) for x, y in zip(ra, rb)])
-    assert agree > 0.9, agree
+    print("positions before the first part", _assert_parts_only_at_near_ties(a, a_tops, b))
 
 
 @needs4
