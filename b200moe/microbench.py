@@ -178,20 +178,35 @@ def case_dense(T, iters, H=2048):
     report("lm_head", ms, 151936 * H * 2 + rows * 151936 * 4, 2 * rows * H * 151936, tokens=rows)
 
 
-def _kv(T, ctx, bs=256, nkv=4, D=128, layers=2):
+def _kv(T, ctx, bs=256, nkv=4, D=128, layers=2, kv="bf16"):
+    """A pool of random keys/values: bf16, or int8 ("int8": per-token-head scales,
+    "int8-channel": per-channel read scales with two exact outlier dims per head)."""
     from b200moe.engine.kv_cache import KVPool
     nb = T * math.ceil(ctx / bs)
-    pool = KVPool(nb + 1, layers, nkv, bs, D, torch.bfloat16, "cuda")
-    pool.data.normal_()
+    int8 = kv != "bf16"
+    pool = KVPool(nb + 1, layers, nkv, bs, D, torch.bfloat16, "cuda", int8=int8,
+                  int8_mode="channel" if kv == "int8-channel" else "token")
+    if int8:
+        pool.data.copy_(torch.randint(-127, 128, pool.data.shape, dtype=torch.int8, device="cuda"))
+        if pool.scales is not None:
+            pool.scales.uniform_(0.005, 0.02)
+        else:
+            pool.ch_dscale.uniform_(0.005, 0.02)
+            pool.out_idx[:, :, :2] = torch.tensor([3, 77], dtype=torch.int32, device="cuda")
+            pool.n_out.fill_(2)
+            pool.side.normal_()
+    else:
+        pool.data.normal_()
     tables = torch.arange(nb, dtype=torch.int32, device="cuda").view(T, -1)
     return pool, tables
 
 
-def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0, pool_layers=2):
+def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0, pool_layers=2, kv="bf16"):
     """pool_layers: layers interleaved in each KV block slab (the engine's pool
-    holds every layer of a block in one slab, so one layer's keys are strided)."""
+    holds every layer of a block in one slab, so one layer's keys are strided).
+    Bytes are the pool bytes read: 2 per value for bf16, 1 for int8."""
     from b200moe.models.qwen3_moe import Qwen3MoeForCausalLM
-    pool, tables = _kv(T, ctx, layers=pool_layers)
+    pool, tables = _kv(T, ctx, layers=pool_layers, kv=kv)
     q = torch.randn(T, nq, D, device="cuda").to(torch.bfloat16)
     lens = torch.full((T,), ctx, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
@@ -205,19 +220,19 @@ def case_decode(T, ctx, iters, nq=32, nkv=4, D=128, splits=0, pool_layers=2):
           torch.empty(T * nq * nsplit, device="cuda"))
     ms = timeit(lambda: ops.decode_attention(q, pool.layer(0), tables, lens, D ** -0.5, out, split_len, nsplit, ws),
                 iters)
-    report("decode_attn", ms, T * ctx * nkv * D * 2 * 2, 4 * T * ctx * nq * D, seqs=T, ctx=ctx, splits=nsplit,
-           pool_layers=pool_layers)
+    report("decode_attn", ms, T * ctx * nkv * D * 2 * (1 if kv != "bf16" else 2), 4 * T * ctx * nq * D, seqs=T,
+           ctx=ctx, splits=nsplit, pool_layers=pool_layers, kv=kv)
 
 
-def case_prefill(T, ctx, iters, nq=32, nkv=4, D=128):
+def case_prefill(T, ctx, iters, nq=32, nkv=4, D=128, kv="bf16"):
     B = max(1, T // ctx)
-    pool, tables = _kv(B, ctx)
+    pool, tables = _kv(B, ctx, kv=kv)
     q = torch.randn(B * ctx, nq, D, device="cuda").to(torch.bfloat16)
     cu = torch.arange(0, B * ctx + 1, ctx, dtype=torch.int32, device="cuda")
     lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
     ms = timeit(lambda: ops.prefill_attention(q, pool.layer(0), cu, lens, tables, ctx, D ** -0.5, out), iters)
-    report("prefill_attn", ms, 0, 2 * B * ctx * ctx * nq * D, seqs=B, ctx=ctx)
+    report("prefill_attn", ms, 0, 2 * B * ctx * ctx * nq * D, seqs=B, ctx=ctx, kv=kv)
 
 
 def case_step(T, ctx, iters, layers=48):
@@ -485,6 +500,7 @@ def main():
     p.add_argument("--splits", type=int, default=0, help="decode: force this many KV splits (0 = heuristic)")
     p.add_argument("--pool-layers", type=int, default=2, help="decode: layers per KV block slab")
     p.add_argument("--only", choices=["", "gate_up", "down"], default="", help="moe: time one of the two GEMMs")
+    p.add_argument("--kv", choices=["bf16", "int8", "int8-channel"], default="bf16", help="decode / prefill: pool type")
     a = p.parse_args()
     if a.case == "ep":
         return case_ep(a.tokens, a.iters)
@@ -496,9 +512,9 @@ def main():
     if a.case in ("dense", "all"):
         case_dense(a.tokens, a.iters)
     if a.case in ("decode", "all"):
-        case_decode(a.tokens, a.ctx, a.iters, splits=a.splits, pool_layers=a.pool_layers)
+        case_decode(a.tokens, a.ctx, a.iters, splits=a.splits, pool_layers=a.pool_layers, kv=a.kv)
     if a.case in ("prefill", "all"):
-        case_prefill(max(a.tokens, a.ctx), a.ctx, a.iters)
+        case_prefill(max(a.tokens, a.ctx), a.ctx, a.iters, kv=a.kv)
     if a.case == "trace":
         case_trace(a.tokens)
     if a.case == "step":
