@@ -270,7 +270,8 @@ def case_ep(T, iters, reps=10):
     """One expert-parallel MoE layer of Qwen3-30B-A3B on every rank of a torchrun job
     (``torchrun --nproc-per-node W -m b200moe.microbench ep --tokens T``): router,
     dispatch, scatter, grouped GEMMs, peer-scatter combine -- the fused peer-memory
-    path, ``reps`` layers per CUDA graph, device time max over ranks.  The roofline
+    path, ``reps`` layers (each with its own weights) per CUDA graph, device time max
+    over ranks.  The roofline
     is the slowest of: NVLink bytes (rows out + weighted rows back) at the measured
     peer bandwidth, this rank's expert weights at the measured HBM copy rate, and
     the expert FLOPs at the measured bf16 peak."""
@@ -289,7 +290,9 @@ def case_ep(T, iters, reps=10):
     dist.init_process_group("nccl", device_id=dev)
     cfg = Config("qwen3-30b-a3b", max_num_batched_tokens=max(T, 16), max_num_seqs=max(T, 1))
     args = cfg.hf_config
-    args.num_hidden_layers = 1
+    # one layer per rep: every rep reads its own expert weights from HBM (at 8 ranks one layer's
+    # 38 MB slice would otherwise stay in the 126 MB L2 across reps)
+    args.num_hidden_layers = reps
     model = Qwen3MoeForCausalLM(args, dev, ep_rank=rank, ep_size=W, expert_ids=expert_placement(cfg, rank, W))
     random_init_(model, seed=7)
     model.tile_weights_()
@@ -298,17 +301,20 @@ def case_ep(T, iters, reps=10):
     ep = ExpertParallel(runner, "fused")
     assert ep.backend == "fused"
     model.ep = ep
-    layer = model.layers[0]
     g = torch.Generator(device=dev).manual_seed(rank)
     x = (torch.randn(T, args.hidden_size, device=dev, generator=g)).to(torch.bfloat16)
     res0 = torch.randn(T, args.hidden_size, device=dev, generator=g).to(torch.bfloat16)
     res = res0.clone()
-    fn = lambda: model._mlp(layer, x, res, model.norm, T)
+
+    def fn():
+        for layer in model.layers:
+            model._mlp(layer, x, res, model.norm, T)
+
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
     dist.barrier()
-    graph = _graph(fn, reps)
+    graph = _graph(fn, 1)
     dist.barrier()
     ms = _time_graph(graph, iters) / reps
     ms_max = torch.tensor([ms], device=dev)
