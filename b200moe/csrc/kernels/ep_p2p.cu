@@ -87,24 +87,25 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
       reinterpret_cast<int4*>(a.recv_meta[dest])[row] = m;
     }
   }
-  __threadfence_system();  // every thread orders its own peer stores before the block's arrival
+  // The block's peer stores are ordered before thread 0's system-scope fence by the
+  // barrier (fences are cumulative over what the fencing thread has synchronised
+  // with), so one fence per block -- not one per thread -- publishes them.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
     last_s = atomicAdd(a.done_blocks, 1) == (int)gridDim.x - 1;
+    if (last_s) __threadfence_system();  // and every other block's, seen through the counter
   }
   __syncthreads();
   if (!last_s) return;
   // last block: every other block's rows are out.  Publish this source's row
   // count per expert into each owner's count matrix, then the epoch flags.
-  __threadfence_system();
   for (int ge = threadIdx.x; ge < a.num_experts; ge += blockDim.x) {
     const int dest = a.owner[ge];
     volatile int* cnt = reinterpret_cast<volatile int*>(a.counts[dest]);
     cnt[a.rank * a.num_local + a.ge_local[ge]] = atomicAdd(&a.ecur[ge], 0);
     a.ecur[ge] = 0;
   }
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -125,6 +126,7 @@ __global__ void ep_scatter_kernel(const EpArgs a, int* __restrict__ local_counts
   __shared__ int offs[kEpMaxLocalExperts + 1];
   __shared__ int base[kEpMaxWorld * kEpMaxLocalExperts];  // rows of expert e from sources < s, at s * El + e
   __shared__ int seg[kEpMaxWorld + 1];
+  __shared__ int src_rows[kEpMaxWorld];
   __shared__ int ok_s;
   const int W = a.world, El = a.num_local;
   const uint32_t epoch = *a.epoch;
@@ -147,28 +149,51 @@ __global__ void ep_scatter_kernel(const EpArgs a, int* __restrict__ local_counts
     return;
   }
   const volatile int* cnt = reinterpret_cast<const volatile int*>(a.counts[a.rank]);
-  // per expert: sources in order (rank-major prefix), then the expert prefix
+  if (threadIdx.x < W) src_rows[threadIdx.x] = 0;
+  __syncthreads();
+  // per expert: sources in order (rank-major prefix), then the expert prefix.  Each
+  // count is read once, by the thread of its expert (the W loads are independent);
+  // the per-source row totals are summed in shared memory, not by one thread.
   for (int e = threadIdx.x; e < El; e += blockDim.x) {
+    int c[kEpMaxWorld];
+#pragma unroll
+    for (int src = 0; src < kEpMaxWorld; ++src) c[src] = src < W ? cnt[src * El + e] : 0;
     int run = 0;
-    for (int src = 0; src < W; ++src) {
-      base[src * El + e] = run;
-      run += cnt[src * El + e];
+#pragma unroll
+    for (int src = 0; src < kEpMaxWorld; ++src) {
+      if (src < W) {
+        base[src * El + e] = run;
+        run += c[src];
+        atomicAdd(&src_rows[src], c[src]);
+      }
     }
     offs[e] = run;  // total of expert e, turned into the prefix below
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int sum = 0;
-    for (int e = 0; e < El; ++e) { const int n = offs[e]; offs[e] = sum; sum += n; }
-    offs[El] = sum;
-    int r = 0;
-    for (int src = 0; src < W; ++src) {
-      seg[src] = r;
-      int n = 0;
-      for (int e = 0; e < El; ++e) n += cnt[src * El + e];
-      r += min(n, a.cap);
+  if (threadIdx.x < 32) {  // expert prefix by one warp (shared memory), source segments by lane 0
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int e0 = 0; e0 < El; e0 += 32) {
+      const int e = e0 + lane;
+      const int n = e < El ? offs[e] : 0;
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (e < El) offs[e] = carry + incl - n;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    seg[W] = r;
+    if (lane == 0) {
+      offs[El] = carry;
+      int r = 0;
+      for (int src = 0; src < W; ++src) {
+        seg[src] = r;
+        r += min(src_rows[src], a.cap);
+      }
+      seg[W] = r;
+    }
   }
   __syncthreads();
   if (blockIdx.x == 0) {

@@ -733,7 +733,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
   }
 
   tc_fence_before();
-  if (args.ep_epoch != nullptr) __threadfence_system();  // this thread's peer stores, before the CTA's arrival
+  // the epilogue's peer stores are ordered before thread 0's system-scope fence below by
+  // this barrier (the fence is cumulative), so no thread fences on its own
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -71,11 +71,11 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // The last CTA of the grid to get here runs `fn`.  SYS: every CTA's stores are
-// fenced at system scope first (fn publishes them to peers); otherwise fn only
-// needs every CTA to have arrived (a device-scope counter).
+// published at system scope first (fn releases them to peers) -- the barrier orders
+// the CTA's stores before thread 0's fence, which is cumulative, so one fence per
+// CTA suffices; otherwise fn only needs every CTA to have arrived.
 template <bool SYS, typename F>
 __device__ __forceinline__ void last_cta(int* counter, F fn) {
-  if constexpr (SYS) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     if constexpr (SYS) __threadfence_system();
