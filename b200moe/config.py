@@ -137,6 +137,9 @@ PRESETS: dict[str, dict] = {
     "qwen3-30b-a3b": dict(),
     "qwen3-235b-a22b": dict(hidden_size=4096, num_hidden_layers=94, num_attention_heads=64,
                             num_key_value_heads=4, moe_intermediate_size=1536, intermediate_size=12288),
+    # 235B-A22B geometry (hidden 4096, GQA group 16, experts 4096 x 1536) with 2 layers: GPU tests.
+    "qwen3-235b-a22b-2l": dict(hidden_size=4096, num_hidden_layers=2, num_attention_heads=64,
+                               num_key_value_heads=4, moe_intermediate_size=1536, intermediate_size=12288),
 }
 
 

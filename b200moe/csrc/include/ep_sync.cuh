@@ -8,6 +8,12 @@
 
 namespace b200 {
 
+// Release / acquire fence at system scope.  The flag protocols here are release /
+// acquire patterns (stores -> fence -> flag or counter; counter -> fence -> reads), for
+// which acq_rel is enough; the sequentially consistent fence (__threadfence_system)
+// also orders store -> load pairs, which none of them needs, and costs more.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

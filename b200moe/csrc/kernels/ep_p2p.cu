@@ -92,9 +92,9 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
   // with), so one fence per block -- not one per thread -- publishes them.
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     last_s = atomicAdd(a.done_blocks, 1) == (int)gridDim.x - 1;
-    if (last_s) __threadfence_system();  // and every other block's, seen through the counter
+    if (last_s) fence_acq_rel_sys();  // and every other block's, seen through the counter
   }
   __syncthreads();
   if (!last_s) return;
@@ -108,7 +108,7 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     for (int r = 0; r < a.world; ++r) st_release_sys(reinterpret_cast<uint32_t*>(a.flags[r]) + a.rank, epoch);
     for (int r = 0; r < a.world; ++r) a.send_cursor[r] = 0;
     *a.done_blocks = 0;
@@ -234,7 +234,7 @@ __global__ void ep_scatter_kernel(const EpArgs a, int* __restrict__ local_counts
 __global__ void ep_signal_kernel(const EpArgs a) {
   const int r = threadIdx.x;
   const uint32_t epoch = *a.epoch;
-  __threadfence_system();
+  fence_acq_rel_sys();
   if (r < a.world) st_release_sys(reinterpret_cast<uint32_t*>(a.done[r]) + a.rank, epoch);
 }
 

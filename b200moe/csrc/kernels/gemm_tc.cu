@@ -741,10 +741,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if (args.ep_epoch != nullptr && threadIdx.x == 0) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     if (atomicAdd(args.ep_cta_done, 1) == (int)gridDim.x - 1) {  // every CTA's rows are out
       *args.ep_cta_done = 0;
-      __threadfence_system();
+      fence_acq_rel_sys();
       const uint32_t epoch = *args.ep_epoch + (uint32_t)args.ep_epoch_add;
       for (int r = 0; r < args.ep_world; ++r)
         st_release_sys(reinterpret_cast<uint32_t*>(args.ep_done[r]) + args.ep_rank, epoch);

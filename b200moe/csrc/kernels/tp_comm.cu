@@ -78,11 +78,11 @@ template <bool SYS, typename F>
 __device__ __forceinline__ void last_cta(int* counter, F fn) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    if constexpr (SYS) __threadfence_system();
+    if constexpr (SYS) fence_acq_rel_sys();
     else __threadfence();
     if (atomicAdd(counter, 1) == (int)gridDim.x - 1) {
       *counter = 0;
-      if constexpr (SYS) __threadfence_system();
+      if constexpr (SYS) fence_acq_rel_sys();
       fn();
     }
   }

@@ -381,8 +381,19 @@ def case_tp(T, iters, reps=10, H=2048, K_total=4096):
         dist.all_reduce(o)
         ops.rmsnorm(o, nw, 1e-6, residual=res, out=out)
 
+    def fused_gemm():  # the O GEMM alone, writing its peer-visible partials and releasing
+        T_, K_ = x.shape
+        bn, splits = ops.plan_dense(T_, H // 128, K_ // 64, fp8=True, max_splits=4)
+        part = tp.part[0][0][:splits * T_].view(splits * T_, H)
+        release = [tp.epoch.data_ptr(), tp.prod_counter.data_ptr(), tp.rank, 1, *tp.flag_ptrs]
+        ops.native().gemm(w8, sc[0], x, ops.count_tensor(T_, dev), None, part, bn, ops.EPI_F32, H // 128,
+                          0, 0, None, None, tp.status, ops._trace[0], splits, T_ * H, True, release)
+
+    def linear():
+        ops.linear(x, w8, sc[0], out=o, tiled=True)
+
     times = {}
-    for name, fn in (("fused", fused), ("nccl", nccl)):
+    for name, fn in (("fused", fused), ("nccl", nccl), ("fused_gemm", fused_gemm), ("linear", linear)):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -400,6 +411,7 @@ def case_tp(T, iters, reps=10, H=2048, K_total=4096):
     if rank == 0:
         print(json.dumps({"kernel": "tp_o_proj_allreduce_norm", "world": W, "tokens": T,
                           "fused_ms": round(times["fused"], 4), "nccl_ms": round(times["nccl"], 4),
+                          "fused_gemm_ms": round(times["fused_gemm"], 4), "linear_ms": round(times["linear"], 4),
                           "roofline_ms": round(roof * 1e3, 4), "fused_roofline_frac": round(roof * 1e3 / times["fused"], 3),
                           "nvlink_bytes": nvlink, "weight_bytes": wbytes, "peak": src,
                           "wait_ms_rank0": tp.wait_stats()}), flush=True)
