@@ -552,9 +552,9 @@ void dequant_weights(Tensor q, Tensor scale, Tensor out, bool tiled) {
   b200::dequant_weights(q.data_ptr(), scale.data_ptr<float>(), out.data_ptr(), (int)G, (int)N, (int)K, tiled, stream());
 }
 
-void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
-                  c10::optional<Tensor> counts, c10::optional<Tensor> status, c10::optional<Tensor> part,
-                  c10::optional<Tensor> tile_cnt) {
+static void router_impl(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids,
+                        Tensor weights, c10::optional<Tensor> counts, c10::optional<Tensor> status,
+                        c10::optional<Tensor> part, c10::optional<Tensor> tile_cnt, const b200::EpArgs* ep) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, torch::kBFloat16);
   CHECK_CONTIG(w); CHECK_DT(w, torch::kBFloat16);
   CHECK_DT(ids, torch::kInt32); CHECK_DT(weights, torch::kFloat32);
@@ -575,7 +575,21 @@ void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool re
   }
   b200::router_fused(x.data_ptr(), w.data_ptr(), (int)x.size(0), (int)x.size(1), (int)num_experts, (int)w.size(0),
                      (int)topk, renorm, ids.data_ptr<int>(), weights.data_ptr<float>(), ptr_or_null<int>(counts),
-                     ptr_or_null<int>(status), stream(), pp, cp, part_tiles);
+                     ptr_or_null<int>(status), stream(), pp, cp, part_tiles, ep);
+}
+
+void router_fused(Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids, Tensor weights,
+                  c10::optional<Tensor> counts, c10::optional<Tensor> status, c10::optional<Tensor> part,
+                  c10::optional<Tensor> tile_cnt) {
+  router_impl(x, w, num_experts, topk, renorm, ids, weights, counts, status, part, tile_cnt, nullptr);
+}
+
+// Router + expert-parallel dispatch in one launch (the top-k warps send the rows).
+void router_dispatch(EP_ARGS_DECL, Tensor x, Tensor w, int64_t num_experts, int64_t topk, bool renorm, Tensor ids,
+                     Tensor weights, c10::optional<Tensor> part, c10::optional<Tensor> tile_cnt) {
+  auto a = EP_ARGS;
+  TORCH_CHECK(x.size(1) == a.hidden, "hidden mismatch");
+  router_impl(x, w, num_experts, topk, renorm, ids, weights, c10::nullopt, status, part, tile_cnt, &a);
 }
 
 // residual += bf16(sum of split-K partials); out = rmsnorm(residual) * weight
@@ -806,6 +820,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_free", &ipc_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("decode_attn", &decode_attn);
+  m.def("router_dispatch", &router_dispatch);
   m.def("prefill_attn", &prefill_attn);
   m.def("kv_int8_stage", &kv_int8_stage);
   m.def("argmax", &argmax);

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "ep_p2p.h"
+
 namespace b200 {
 
 constexpr int kMaxExperts = 512;
@@ -83,9 +85,12 @@ void kv_blocks_copy(const void* src_base, const int* src_ids, void* dst_base, co
 void dequant_weights(const void* q, const float* scale, void* out, int G, int N, int K, bool tiled, cudaStream_t s);
 // part / tile_cnt (optional): fp32 scratch for part_tiles partial tiles of 16 x 128 logits and a
 // zeroed int per token tile; with them, batches too small to fill the SMs also split K.
+// ep (optional): expert parallelism -- the top-k warps also send each routed row to its
+// expert's owner and the grid publishes this rank's counts and epoch, which is what
+// ep_dispatch does as a separate launch.
 void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows, int topk, bool renorm, int* ids,
                   float* weights, int* counts, int* status, cudaStream_t s, float* part = nullptr,
-                  int* tile_cnt = nullptr, int part_tiles = 0);
+                  int* tile_cnt = nullptr, int part_tiles = 0, const EpArgs* ep = nullptr);
 void moe_permute(const void* x, const int* ids, int T, int topk, int E, int H, const int* counts, int* cursor,
                  void* x_perm, int* slot_of_row, int* offsets_out, cudaStream_t s);
 

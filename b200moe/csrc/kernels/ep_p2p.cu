@@ -47,6 +47,7 @@
 #include "sm100.cuh"
 #include "ep_sync.cuh"
 #include "ep_p2p.h"
+#include "ep_dispatch.cuh"
 
 namespace b200 {
 
@@ -59,61 +60,9 @@ __global__ void ep_dispatch_kernel(const EpArgs a, const __nv_bfloat16* __restri
   const uint32_t epoch = epoch_s;
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int H8 = a.hidden / 8;
-  for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < T * topk; p += gridDim.x * warps) {
-    const int ge = ids[p];
-    if (ge < 0 || ge >= a.num_experts) {
-      if (lane == 0) record_status(a.status, kStatusBadShape);
-      continue;
-    }
-    const int dest = a.owner[ge];
-    int pos = 0, idx = 0;
-    if (lane == 0) {
-      pos = atomicAdd(&a.send_cursor[dest], 1);
-      idx = atomicAdd(&a.ecur[ge], 1);
-    }
-    pos = __shfl_sync(0xffffffffu, pos, 0);
-    idx = __shfl_sync(0xffffffffu, idx, 0);
-    if (pos >= a.cap) {  // the host sizes cap for the worst case; never write past it
-      if (lane == 0) record_status(a.status, kStatusBadShape);
-      continue;
-    }
-    const int64_t row = (int64_t)a.rank * a.cap + pos;
-    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(p / topk) * a.hidden);
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.recv_x[dest]) + row * a.hidden);
-    for (int i = lane; i < H8; i += 32) dst[i] = src[i];
-    if (lane == 0) {
-      int4 m = make_int4(ge, p, __float_as_int(w[p]), idx);
-      reinterpret_cast<int4*>(a.recv_meta[dest])[row] = m;
-    }
-  }
-  // The block's peer stores are ordered before thread 0's system-scope fence by the
-  // barrier (fences are cumulative over what the fencing thread has synchronised
-  // with), so one fence per block -- not one per thread -- publishes them.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    fence_acq_rel_sys();
-    last_s = atomicAdd(a.done_blocks, 1) == (int)gridDim.x - 1;
-    if (last_s) fence_acq_rel_sys();  // and every other block's, seen through the counter
-  }
-  __syncthreads();
-  if (!last_s) return;
-  // last block: every other block's rows are out.  Publish this source's row
-  // count per expert into each owner's count matrix, then the epoch flags.
-  for (int ge = threadIdx.x; ge < a.num_experts; ge += blockDim.x) {
-    const int dest = a.owner[ge];
-    volatile int* cnt = reinterpret_cast<volatile int*>(a.counts[dest]);
-    cnt[a.rank * a.num_local + a.ge_local[ge]] = atomicAdd(&a.ecur[ge], 0);
-    a.ecur[ge] = 0;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    fence_acq_rel_sys();
-    for (int r = 0; r < a.world; ++r) st_release_sys(reinterpret_cast<uint32_t*>(a.flags[r]) + a.rank, epoch);
-    for (int r = 0; r < a.world; ++r) a.send_cursor[r] = 0;
-    *a.done_blocks = 0;
-    *a.epoch = epoch;
-  }
+  for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < T * topk; p += gridDim.x * warps)
+    ep_send_row(a, x + (int64_t)(p / topk) * a.hidden, p, ids[p], w[p], lane);
+  if (ep_block_arrive(a, gridDim.x, &last_s)) ep_publish(a, epoch);
 }
 
 // Owner side.  Every block waits for every source, then places each received row at

@@ -28,6 +28,7 @@
 #include "sm100.cuh"
 #include "pdl.cuh"
 #include "ep_sync.cuh"
+#include "ep_dispatch.cuh"
 #include "fused_ops.h"
 
 namespace b200 {
@@ -339,7 +340,8 @@ __global__ void qknorm_rope_kvstore_kernel(const QkvArgs a) {
 // expert id winning ties, optional renormalisation, bf16-rounded weights.
 template <int EPL>
 __device__ __forceinline__ void topk_row(float (&p)[EPL], int E, int topk, int renorm, int tok, int lane,
-                                         int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
+                                         int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts,
+                                         int* ev_out = nullptr, float* wv_out = nullptr) {
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < EPL; ++j) mx = fmaxf(mx, p[j]);
@@ -355,10 +357,12 @@ __device__ __forceinline__ void topk_row(float (&p)[EPL], int E, int topk, int r
   const float inv = 1.f / sum;
 #pragma unroll
   for (int j = 0; j < EPL; ++j) p[j] = j * 32 + lane < E ? p[j] * inv : -1.f;
-  float sel_w[8];
-  int sel_e[8];
+  float sel_w[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int sel_e[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   float wsum = 0.f;
-  for (int k = 0; k < topk; ++k) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // static indices keep sel_* in registers (topk <= 8)
+    if (k >= topk) break;
     float bv = -2.f;
     int be = 1 << 30;
 #pragma unroll
@@ -389,6 +393,10 @@ __device__ __forceinline__ void topk_row(float (&p)[EPL], int E, int topk, int r
     ids[(size_t)tok * topk + lane] = ev;
     weights[(size_t)tok * topk + lane] = bf16r(wv);  // the reference casts weights to bf16
     if (counts != nullptr) atomicAdd(&counts[ev], 1);
+    if (ev_out != nullptr) {  // lane k < topk: the token's k-th expert and its weight
+      *ev_out = ev;
+      *wv_out = bf16r(wv);
+    }
   }
 }
 
@@ -436,7 +444,9 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
                                                            int E, int topk, int renorm, int* __restrict__ ids,
                                                            float* __restrict__ weights, int* __restrict__ counts,
                                                            int* __restrict__ status, float* __restrict__ part,
-                                                           int* __restrict__ tile_cnt) {
+                                                           int* __restrict__ tile_cnt,
+                                                           const __nv_bfloat16* __restrict__ xg, const EpArgs ep,
+                                                           int ep_on) {
   pdl_enter();
   constexpr int XB = kRtTok * 128;  // bytes of one x chunk (the W chunk follows it)
   extern __shared__ __align__(1024) uint8_t rt_raw[];
@@ -545,6 +555,9 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
     }
     if (threadIdx.x == 0) tile_cnt[blockIdx.x] = 0;  // ready for the next launch
   }
+  __shared__ uint32_t ep_epoch_s;
+  __shared__ int ep_last_s;
+  if (ep_on && threadIdx.x == 0) ep_epoch_s = *ep.epoch + 1;
   __syncthreads();
   for (int r = warp; r < kRtTok; r += 8) {
     const int tok = t0 + r;
@@ -555,8 +568,19 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
       const int e = j * 32 + lane;
       p[j] = e < E ? bf16r(logit[r][e]) : -INFINITY;
     }
-    topk_row<4>(p, E, topk, renorm, tok, lane, ids, weights, counts);
+    int ev = 0;
+    float wv = 0.f;
+    topk_row<4>(p, E, topk, renorm, tok, lane, ids, weights, counts, &ev, &wv);
+    if (ep_on) {
+      // expert parallelism: send the token's rows to their experts' owners right here
+      // (the stand-alone ep_dispatch_kernel does the same from ids / weights)
+      for (int k = 0; k < topk; ++k)
+        ep_send_row(ep, xg + (int64_t)tok * H, tok * topk + k, __shfl_sync(0xffffffffu, ev, k),
+                    __shfl_sync(0xffffffffu, wv, k), lane);
+    }
   }
+  // one CTA per token tile gets here (split-K: the tile's last); the grid's last publishes
+  if (ep_on && ep_block_arrive(ep, gridDim.x, &ep_last_s)) ep_publish(ep, ep_epoch_s);
   pdl_trigger();
 }
 
@@ -819,8 +843,13 @@ static CUtensorMap rt_map(const void* base, int rows, int H, int box_rows) {
 
 void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows, int topk, bool renorm, int* ids,
                   float* weights, int* counts, int* status, cudaStream_t s, float* part, int* tile_cnt,
-                  int part_tiles) {
-  if (T == 0) return;
+                  int part_tiles, const EpArgs* ep) {
+  if (T == 0) {
+    // expert parallelism: a rank without tokens still publishes (zero counts) every layer
+    if (ep != nullptr) ep_dispatch(*ep, x, ids, weights, 0, topk, s);
+    return;
+  }
+  if (ep != nullptr && ep->hidden != H) throw std::runtime_error("router_fused: expert-parallel hidden mismatch");
   if (E > kRtE || w_rows < kRtE || topk < 1 || topk > 8 || H % kRtK)
     throw std::runtime_error("router_fused: needs <= 128 experts (weight padded to 128 rows), top-k in [1, 8], "
                              "hidden % 64 == 0");
@@ -838,7 +867,8 @@ void router_fused(const void* x, const void* w, int T, int H, int E, int w_rows,
     while (ks < 8 && tiles * ks * 2 <= sms && (H / kRtK) >= ks * 2 * 2 && tiles * ks * 2 <= part_tiles) ks *= 2;
   }
   pdl_launch(router_fused_kernel, dim3(tiles, ks), 256, kRtSmem, s, xm, wm, T, H, E, topk, renorm ? 1 : 0, ids,
-             weights, counts, status, part, tile_cnt);
+             weights, counts, status, part, tile_cnt, static_cast<const bf16*>(x), ep != nullptr ? *ep : EpArgs{},
+             ep != nullptr ? 1 : 0);
   check_launch("router_fused");
 }
 

@@ -432,10 +432,12 @@ class Qwen3MoeForCausalLM(nn.Module):
             if self.ep is None and not getattr(self, "_counts_clear", False):
                 counts.zero_()  # otherwise the previous layer's combine kernel cleared them
             self._counts_clear = False
-            ids, w = self.route(layer, x, counts[:E] if self.ep is None else None)
+            routed = self.ep.route_dispatch(self, layer, x) if self.ep is not None else None
+            dispatched = routed is not None
+            ids, w = routed if dispatched else self.route(layer, x, counts[:E] if self.ep is None else None)
         if self.ep is not None:
             with self._range("moe.ep"):
-                return self.ep.moe_fused(self, layer, x, ids, w, slots)
+                return self.ep.moe_fused(self, layer, x, ids, w, slots, dispatched)
         rows = T * k
         with self._range("moe.permute"):
             x_perm = self._buf("x_perm", (rows, H), self.dtype)

@@ -115,9 +115,16 @@ class ExpertParallel:
         return self.p2p.combine_wait() if self.backend == "fused" else None
 
     # --------------------------------------------------------------- fused
-    def moe_fused(self, model, layer, x, ids, w, slots):
+    def route_dispatch(self, model, layer, x):
+        """Fused path: router and dispatch in one launch, (ids, weights); None where it
+        does not apply (other backends, or the router shape)."""
+        if self.backend != "fused" or not x.is_cuda:
+            return None
+        return self.p2p.route_dispatch(model, layer, x)
+
+    def moe_fused(self, model, layer, x, ids, w, slots, dispatched: bool = False):
         if self.backend == "fused":
-            return self.p2p.moe(model, layer, x, ids, w, slots)
+            return self.p2p.moe(model, layer, x, ids, w, slots, dispatched)
         if self.backend == "reference":
             out = self.moe_reference(model, layer, x, ids, w)
             slots.zero_()

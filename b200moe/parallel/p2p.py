@@ -18,6 +18,8 @@ ever reads it.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -170,15 +172,38 @@ class P2PMoE:
         """(this rank's done array, epoch, status, wait_ns) for the combine kernel's wait."""
         return self.symm["done"][0], self.epoch, self.status, self.wait_ns
 
-    def moe(self, model, layer, x, ids, w, slots):
+    # The router's top-k warps send the routed rows themselves (one launch instead of
+    # router + ep_dispatch); B200MOE_EP_ROUTER_DISPATCH=0 keeps them separate.
+    ROUTER_DISPATCH = os.environ.get("B200MOE_EP_ROUTER_DISPATCH", "1") != "0"
+
+    def route_dispatch(self, model, layer, x):
+        """Router + dispatch in one launch: (ids, weights) as ``model.route`` returns
+        them, or None where the fused router does not apply (more than 128 experts,
+        a non-bf16 router weight)."""
+        a = model.args
+        if not self.ROUTER_DISPATCH or a.num_experts > 128 or layer.router.dtype != torch.bfloat16:
+            return None
+        T, k = x.shape[0], a.num_experts_per_tok
+        ids = model._buf("ids", (T * k,), torch.int32).view(T, k)
+        w = model._buf("topw", (T * k,), torch.float32).view(T, k)
+        part, cnt = ops.router_scratch(x.device)
+        ops.native().router_dispatch(*self._a(), x, layer.router, a.num_experts, k, a.norm_topk_prob, ids, w, part,
+                                     cnt)
+        ops.count_launches()
+        return ids, w
+
+    def moe(self, model, layer, x, ids, w, slots, dispatched: bool = False):
         """Returns the tensor holding this rank's (token, k) slots; the caller's combine
-        waits on ``combine_wait()`` before reading it."""
+        waits on ``combine_wait()`` before reading it.  ``dispatched``: the router
+        already sent the rows (``route_dispatch``)."""
         C = ops.native()
         a = self._a()
         T = x.shape[0]
         El = model.num_local_experts
         I = layer.w2.shape[-1]
-        C.ep_dispatch(*a, x, ids, w.contiguous())
+        if not dispatched:
+            C.ep_dispatch(*a, x, ids, w.contiguous())
+            ops.count_launches()
         rows = self.W * self.cap
         cnt = model._buf("ep_counts", (El,), torch.int32)
         off = model._buf("ep_offsets", (El + 1,), torch.int32)
@@ -197,5 +222,5 @@ class P2PMoE:
                             ops.pick_bn(expected * model.args.num_experts_per_tok, self.H // 128, El),
                             code, sw, self.symm["slots"][1], self.slot_cap, self.H, self.status,
                             model.weights_tiled, self.epoch, self.cta_done, self.symm["done"][1], self.rank)
-        ops.count_launches(3)
+        ops.count_launches(2)
         return self.symm["slots"][0]

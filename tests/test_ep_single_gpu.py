@@ -1,7 +1,8 @@
 """The fused expert-parallel kernels on ONE GPU: with a world of one rank the rank
 is its own owner, so dispatch (rows and per-expert counts into the owner's
 buffers), the scatter that places rows from the count matrix, the down GEMM's
-done release and the combine's wait all run on local memory.  The result must
+done release and the combine's wait all run on local memory -- with the rows sent by
+the router's top-k warps and by the stand-alone dispatch kernel.  The result must
 equal the single-GPU MoE path bit for bit: the GEMMs see the same rows per
 expert, and the combine sums the same slots in the same order."""
 import random
@@ -64,8 +65,10 @@ def test_fused_ep_world1_matches_local_moe():
         bs = 16
         steps = [([40, 17, 64, 3], [40, 17, 64, 3]), ([41, 18, 65, 4], [1, 1, 1, 1]), ([42, 19, 66, 5], [1, 1, 1, 1])]
         outs = {}
-        for use_ep in (False, True):
+        # local MoE; EP with the router sending the rows; EP with a separate dispatch launch
+        for use_ep, router_dispatch in ((False, False), (True, True), (True, False)):
             model.ep = ep if use_ep else None
+            ep.p2p.ROUTER_DISPATCH = router_dispatch
             pool = KVPool(64, args.num_hidden_layers, args.num_key_value_heads, bs, args.head_dim,
                           torch.bfloat16, "cuda")
             got = []
@@ -74,9 +77,10 @@ def test_fused_ep_world1_matches_local_moe():
                 got.append(model.compute_logits(model(inp, pool)).float().cpu())
             torch.cuda.synchronize()
             ops.check_status(torch.device("cuda", 0))
-            outs[use_ep] = got
-        for a, b in zip(outs[False], outs[True]):
-            assert torch.equal(a, b)
+            outs[(use_ep, router_dispatch)] = got
+        for key in ((True, True), (True, False)):
+            for a, b in zip(outs[(False, False)], outs[key]):
+                assert torch.equal(a, b), key
         waits = ep.p2p.wait_stats()
         assert len(waits["dispatch_ms"]) == 1 and len(waits["combine_ms"]) == 1
         model.ep = None
