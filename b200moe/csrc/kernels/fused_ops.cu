@@ -574,9 +574,7 @@ __global__ void __launch_bounds__(256) router_fused_kernel(const __grid_constant
     if (ep_on) {
       // expert parallelism: send the token's rows to their experts' owners right here
       // (the stand-alone ep_dispatch_kernel does the same from ids / weights)
-      for (int k = 0; k < topk; ++k)
-        ep_send_row(ep, xg + (int64_t)tok * H, tok * topk + k, __shfl_sync(0xffffffffu, ev, k),
-                    __shfl_sync(0xffffffffu, wv, k), lane);
+      ep_send_token(ep, xg + (int64_t)tok * H, tok, topk, ev, wv, lane);
     }
   }
   // one CTA per token tile gets here (split-K: the tile's last); the grid's last publishes
