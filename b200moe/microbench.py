@@ -263,6 +263,49 @@ def case_step(T, ctx, iters, layers=48):
     report("decode_step", ms, wbytes + kvbytes, 0, rows=T, ctx=ctx, layers=layers)
 
 
+def case_ops(T, iters, H=2048, nq=32, nkv=4, D=128, V=151936, topk=8):
+    """The memory-bound hot ops of a decode step at T rows, each timed alone (CUDA
+    events, L2 flushed before every call); bytes are what each op must move:
+    residual add + RMSNorm, q/k RMSNorm + RoPE + paged KV store, the MoE combine
+    (fixed-order top-k sum + residual + next RMSNorm), greedy argmax and the sampler
+    (temperature 0.7, top-k 50, top-p 0.9) over the full 151,936-token vocabulary."""
+    from b200moe.engine.kv_cache import KVPool
+    dev = "cuda"
+    bf = torch.bfloat16
+    x = torch.randn(T, H, device=dev).to(bf)
+    res = torch.randn(T, H, device=dev).to(bf)
+    w = (1 + 0.1 * torch.randn(H, device=dev)).to(bf)
+    out = torch.empty(T, H, device=dev, dtype=bf)
+    ms = timeit(lambda: ops.rmsnorm(x, w, 1e-6, residual=res, out=out), iters)
+    report("rmsnorm_residual", ms, 4 * T * H * 2, 0, rows=T, hidden=H)
+    width = (nq + 2 * nkv) * D
+    qkv = torch.randn(T, width, device=dev).to(bf)
+    bs = 256
+    pool = KVPool(T // 4 + 2, 2, nkv, bs, D, bf, dev)
+    slots = torch.randperm((T // 4 + 1) * bs, device=dev)[:T].to(torch.int32)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32, device=dev)
+    qw = (1 + 0.1 * torch.randn(D, device=dev)).to(bf)
+    kw = (1 + 0.1 * torch.randn(D, device=dev)).to(bf)
+    cs = ops.rope_cos_sin(D, 4096, 1e6, dev)
+    q_out = torch.empty(T, nq, D, device=dev, dtype=bf)
+    ms = timeit(lambda: ops.qknorm_rope_kvstore(qkv, pos, slots, qw, kw, cs, pool.layer(1), nq, nkv, D, 1e-6,
+                                                q_out=q_out), iters)
+    report("qknorm_rope_kvstore", ms, T * width * 2 + T * (nq + 2 * nkv) * D * 2, 0, rows=T)
+    slot_buf = torch.randn(T * topk, H, device=dev).to(bf)
+    ms = timeit(lambda: ops.moe_combine_add_rmsnorm(slot_buf, topk, res, w, 1e-6, out=out), iters)
+    report("moe_combine_add_rmsnorm", ms, (T * topk * H + 3 * T * H) * 2, 0, rows=T, topk=topk)
+    logits = torch.randn(T, V, device=dev)
+    tok = torch.empty(T, dtype=torch.int32, device=dev)
+    ms = timeit(lambda: ops.argmax(logits, tok), iters)
+    report("argmax", ms, T * V * 4, 0, rows=T, vocab=V)
+    temp = torch.full((T,), 0.7, device=dev)
+    top_k = torch.full((T,), 50, dtype=torch.int32, device=dev)
+    top_p = torch.full((T,), 0.9, device=dev)
+    seeds = torch.arange(T, dtype=torch.int64, device=dev)
+    ms = timeit(lambda: ops.sample(logits, temp, top_k, top_p, None, seeds, None, out=tok), iters)
+    report("sample_topk_topp", ms, T * V * 4, 0, rows=T, vocab=V)
+
+
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's NVSwitch systems
 
 
@@ -510,7 +553,7 @@ def case_trace(T):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "ep", "tp", "all"])
+    p.add_argument("case", choices=["moe", "dense", "decode", "prefill", "step", "trace", "ep", "tp", "ops", "all"])
     p.add_argument("--tokens", type=int, default=256)
     p.add_argument("--ctx", type=int, default=1152)
     p.add_argument("--iters", type=int, default=20)
@@ -537,6 +580,8 @@ def main():
         case_trace(a.tokens)
     if a.case == "step":
         case_step(a.tokens, a.ctx, a.iters, a.layers)
+    if a.case in ("ops", "all"):
+        case_ops(a.tokens, a.iters)
     ops.check_status("cuda")
 
 
