@@ -162,3 +162,16 @@ def test_offline_driver_workload_presets():
     assert "kv_offload_enabled" not in kw and kw["kv_cache_dtype"] == "bf16" and kw["attention_parallel"] == "dp"
     c = parse_args([])
     assert c.model == "qwen3-30b-a3b" and c.prompt_len == 128
+
+
+def test_bench_layout_label_follows_the_engine_report():
+    """bench.py names the layout the engine reports (rank 0's parallel_report), not the flags."""
+    import importlib.util
+    import pathlib
+    spec = importlib.util.spec_from_file_location("bench_main", pathlib.Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench._parallelism(8, {"attention_parallel": "dp", "ep_backend": "fused"}) == "ep8+dp8-attn"
+    assert bench._parallelism(2, {"attention_parallel": "tp", "tp_fused": True}) == "tp2-fused-peer-sums"
+    assert bench._parallelism(2, {"attention_parallel": "tp", "tp_fused": False}) == "tp2-nccl"
+    assert bench._parallelism(1, {"attention_parallel": "dp", "ep_backend": None}) == "ep1+dp1-attn"
