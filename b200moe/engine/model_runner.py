@@ -108,6 +108,7 @@ class ModelRunner:
             self.model.tile_weights_()  # e4m3 GEMM weights tile-major: one contiguous HBM block per stage
             trace.mark("tile_weights")
         self.model.profiler = self.profiler if config.enable_profiling else None
+        self.bf16_expert_cache_bytes = self._maybe_cache_bf16_experts()
         self.load_s = time.perf_counter() - t0
         self.max_blocks = -(-config.max_model_len // self.block_size)
         self.max_rows = config.max_num_seqs
@@ -228,6 +229,25 @@ class ModelRunner:
             dist.init_process_group(backend, init_method=method, world_size=self.world_size, rank=self.rank,
                                     timeout=timedelta(seconds=self.config.rank_timeout_s),
                                     device_id=self.device if self.device.type == "cuda" else None)
+
+    # Resident bf16 copy of the expert weights for prefill-size steps (single-GPU expert
+    # path): "auto" keeps it when at least this fraction of the GPU's memory stays free
+    # for the KV cache afterwards; "1" always, "0" never (B200MOE_BF16_EXPERT_CACHE).
+    BF16_CACHE_KEEP_FREE = 0.35
+
+    def _maybe_cache_bf16_experts(self) -> int:
+        mode = os.environ.get("B200MOE_BF16_EXPERT_CACHE", "auto")
+        m = self.model
+        if (mode == "0" or self.device.type != "cuda" or m.ep is not None or m.attn_tp > 1
+                or m.BF16_EXPERT_ROWS <= 0):
+            return 0
+        need = m.bf16_expert_bytes()
+        if need == 0:
+            return 0
+        free, total = torch.cuda.mem_get_info(self.device)
+        if mode != "1" and free - need < self.BF16_CACHE_KEEP_FREE * total:
+            return 0
+        return m.cache_bf16_experts_()
 
     def allocate_kv_cache(self):
         c, a = self.config, self.args

@@ -172,6 +172,33 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.weights_tiled = True
 
     @torch.no_grad()
+    def cache_bf16_experts_(self) -> int:
+        """Keep a bf16 copy of every MoE layer's expert weights, dequantised once
+        (the same kernel and bits as the per-step dequantisation), for the steps
+        large enough to run bf16 expert GEMMs (``_bf16_experts``): those then skip
+        the per-step dequantisation pass.  Decode keeps reading e4m3 (half the
+        bytes).  Returns the bytes held."""
+        held = 0
+        if not (self.cuda and self.quant and self.args.is_moe):
+            return 0
+        for layer in self.layers:
+            if not layer.is_moe or getattr(layer, "w13_bf16", None) is not None:
+                continue
+            w13 = torch.empty(tuple(layer.w13.shape), dtype=torch.bfloat16, device=layer.w13.device)
+            w2 = torch.empty(tuple(layer.w2.shape), dtype=torch.bfloat16, device=layer.w2.device)
+            ops.dequant_weights(layer.w13, layer.s13, w13, self.weights_tiled)
+            ops.dequant_weights(layer.w2, layer.s2, w2, self.weights_tiled)
+            layer.w13_bf16, layer.w2_bf16 = w13, w2
+            held += (w13.numel() + w2.numel()) * 2
+        return held
+
+    def bf16_expert_bytes(self) -> int:
+        """Bytes ``cache_bf16_experts_`` would hold."""
+        if not (self.quant and self.args.is_moe):
+            return 0
+        return sum((l.w13.numel() + l.w2.numel()) * 2 for l in self.layers if l.is_moe)
+
+    @torch.no_grad()
     def untile_weights_(self) -> None:
         if not self.weights_tiled:
             return
@@ -237,7 +264,7 @@ class Qwen3MoeForCausalLM(nn.Module):
             self._buf("ids", (max_tokens * k,), torch.int32)
             self._buf("topw", (max_tokens * k,), torch.float32)
         self._buf("h_perm", (max(rows, max_tokens), I), self.dtype)
-        if self._bf16_experts(rows) and self.layers:
+        if self._bf16_experts(rows) and self.layers and getattr(self.layers[0], "w13_bf16", None) is None:
             l0 = self.layers[0]
             self._buf("w13_bf16", tuple(l0.w13.shape), torch.bfloat16)
             self._buf("w2_bf16", tuple(l0.w2.shape), torch.bfloat16)
@@ -447,12 +474,15 @@ class Qwen3MoeForCausalLM(nn.Module):
         if self.profiler is not None:
             self.profiler.observe("moe.max_expert_rows", counts[:E].max())  # routing imbalance
         if self._bf16_experts(rows):
-            # large prefill batch: dequantise once, then bf16 GEMMs (no per-tile dequantisation)
-            w13 = self._buf("w13_bf16", tuple(layer.w13.shape), torch.bfloat16)
-            w2 = self._buf("w2_bf16", tuple(layer.w2.shape), torch.bfloat16)
-            with self._range("moe.dequant"):
-                ops.dequant_weights(layer.w13, layer.s13, w13, self.weights_tiled)
-                ops.dequant_weights(layer.w2, layer.s2, w2, self.weights_tiled)
+            # large prefill batch: bf16 GEMMs (no per-tile dequantisation) on the resident
+            # bf16 copy (cache_bf16_experts_) or on a copy dequantised for this step
+            w13, w2 = getattr(layer, "w13_bf16", None), getattr(layer, "w2_bf16", None)
+            if w13 is None:
+                w13 = self._buf("w13_bf16", tuple(layer.w13.shape), torch.bfloat16)
+                w2 = self._buf("w2_bf16", tuple(layer.w2.shape), torch.bfloat16)
+                with self._range("moe.dequant"):
+                    ops.dequant_weights(layer.w13, layer.s13, w13, self.weights_tiled)
+                    ops.dequant_weights(layer.w2, layer.s2, w2, self.weights_tiled)
             s13 = s2 = None
             tiled = False
         else:

@@ -124,6 +124,25 @@ def test_qwen3_235b_shapes_generate():
     assert agree > 0.7, agree
 
 
+def test_resident_bf16_experts_same_tokens(monkeypatch):
+    """Prefill-size steps on the resident bf16 expert copy (dequantised once at load)
+    give the same tokens as dequantising the layer's experts in every step: both are
+    the same dequantisation kernel's bits feeding the same bf16 GEMMs."""
+    monkeypatch.setattr(Qwen3MoeForCausalLM, "BF16_EXPERT_ROWS", 1)  # every step takes the bf16 expert path
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    prompts = _prompts(6, seed=9)
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("B200MOE_BF16_EXPERT_CACHE", mode)
+        llm = _engine(enforce_eager=True)
+        held = llm.model_runner.bf16_expert_cache_bytes
+        assert (held > 0) == (mode == "1"), held
+        out[mode] = [o["token_ids"] for o in llm.generate(prompts, sp, use_tqdm=False)]
+        llm.model_runner.check_status()
+        llm.exit()
+    assert out["1"] == out["0"]
+
+
 def test_generate_sampling_and_stall_free():
     prompts = _prompts(6, seed=2)
     llm = _engine(scheduler_policy="stall_free", prefill_chunk_size=32)
