@@ -139,22 +139,27 @@ void gemm(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor gr
 
 // Down GEMM whose epilogue writes each weighted row into its source rank's
 // slot buffer (peer memory): slot_code = rank * slot_cap + slot.
-void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor group_count, Tensor group_offset,
-                       int64_t bn, Tensor slot_code, Tensor slot_w, std::vector<int64_t> peer_ptrs, int64_t slot_cap,
-                       int64_t ld_out, Tensor status, bool a_tiled, c10::optional<Tensor> ep_epoch,
+void gemm_peer_scatter(Tensor weight, c10::optional<Tensor> weight_scale, Tensor x, Tensor group_count,
+                       Tensor group_offset, int64_t bn, Tensor slot_code, Tensor slot_w, std::vector<int64_t> peer_ptrs,
+                       int64_t slot_cap, int64_t ld_out, Tensor status, bool a_tiled, c10::optional<Tensor> ep_epoch,
                        c10::optional<Tensor> ep_cta_done, std::vector<int64_t> done_ptrs, int64_t ep_rank) {
   CHECK_CUDA(weight); CHECK_CUDA(x); CHECK_CONTIG(weight);
-  TORCH_CHECK(weight.dim() == 3 && weight.scalar_type() == torch::kFloat8_e4m3fn, "expert weights must be [E, N, K] e4m3");
+  // e4m3 + 128x128 scales (dequantised per tile), or bf16 (a resident dequantised copy)
+  const bool fp8 = weight.scalar_type() == torch::kFloat8_e4m3fn;
+  TORCH_CHECK(weight.dim() == 3 && (fp8 || weight.scalar_type() == torch::kBFloat16),
+              "expert weights must be [E, N, K] e4m3 or bf16");
+  TORCH_CHECK(fp8 == weight_scale.has_value(), "e4m3 weights need their scales; bf16 weights take none");
+  TORCH_CHECK(fp8 || !a_tiled, "bf16 weights are row-major");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.scalar_type() == torch::kBFloat16, "x must be [rows, K] bf16");
   TORCH_CHECK(peer_ptrs.size() >= 1 && peer_ptrs.size() <= 8, "1..8 peer pointers");
   CHECK_DT(slot_code, torch::kInt32); CHECK_DT(slot_w, torch::kFloat32);
   const int64_t groups = weight.size(0), N = weight.size(1), K = weight.size(2);
   TORCH_CHECK(x.size(1) == K, "K mismatch");
-  TORCH_CHECK(weight_scale.numel() == groups * (N / 128) * (K / 128), "weight_scale shape");
+  if (fp8) TORCH_CHECK(weight_scale->numel() == groups * (N / 128) * (K / 128), "weight_scale shape");
   TORCH_CHECK(x.size(0) > 0, "gemm_peer_scatter: x needs at least one row (the grid releases the done epoch)");
   c10::cuda::CUDAGuard guard(x.device());
   b200::GemmLaunch L{};
-  L.args.a_scale = weight_scale.data_ptr<float>();
+  L.args.a_scale = fp8 ? weight_scale->data_ptr<float>() : nullptr;
   L.args.a_rows_per_group = (int)N;
   L.args.m_tiles = (int)(N / 128);
   L.args.k_stages = (int)(K / 64);
@@ -183,13 +188,13 @@ void gemm_peer_scatter(Tensor weight, Tensor weight_scale, Tensor x, Tensor grou
     L.args.ep_world = (int)done_ptrs.size();
   }
   L.a = weight.data_ptr();
-  L.a_row_stride_bytes = K;
+  L.a_row_stride_bytes = fp8 ? K : K * 2;
   L.b = x.data_ptr();
   L.b_rows = x.size(0);
   L.b_row_stride_bytes = x.stride(0) * 2;
   L.K = (int)K;
   L.bn = (int)bn;
-  L.a_fp8 = true;
+  L.a_fp8 = fp8;
   L.pair = false;
   L.epi = b200::kEpiScatter;
   b200::gemm_tc_launch(L, stream());

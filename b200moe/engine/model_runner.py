@@ -230,16 +230,17 @@ class ModelRunner:
                                     timeout=timedelta(seconds=self.config.rank_timeout_s),
                                     device_id=self.device if self.device.type == "cuda" else None)
 
-    # Resident bf16 copy of the expert weights for prefill-size steps (single-GPU expert
-    # path): "auto" keeps it when at least this fraction of the GPU's memory stays free
-    # for the KV cache afterwards; "1" always, "0" never (B200MOE_BF16_EXPERT_CACHE).
+    # Resident bf16 copy of this rank's expert weights for prefill-size steps (the
+    # single-GPU expert path and the fused expert-parallel path): "auto" keeps it when at
+    # least this fraction of the GPU's memory stays free for the KV cache afterwards;
+    # "1" always, "0" never (B200MOE_BF16_EXPERT_CACHE).
     BF16_CACHE_KEEP_FREE = 0.35
 
     def _maybe_cache_bf16_experts(self) -> int:
         mode = os.environ.get("B200MOE_BF16_EXPERT_CACHE", "auto")
         m = self.model
-        if (mode == "0" or self.device.type != "cuda" or m.ep is not None or m.attn_tp > 1
-                or m.BF16_EXPERT_ROWS <= 0):
+        if (mode == "0" or self.device.type != "cuda" or m.attn_tp > 1 or m.BF16_EXPERT_ROWS <= 0
+                or (m.ep is not None and m.ep.backend != "fused")):
             return 0
         need = m.bf16_expert_bytes()
         if need == 0:

@@ -218,12 +218,18 @@ class P2PMoE:
             model.profiler.observe("moe.local_pairs", cnt.sum())
         h = model._buf("h_perm", (rows, I), model.dtype)
         expected = max(1, T * self.W)  # rows this rank expects on average
-        ops.grouped_gate_up_silu(xp, layer.w13, layer.s13, cnt, off, h, I,
-                                 bn=ops.pick_bn(expected * model.args.num_experts_per_tok, I // 128, El, pair=True),
-                                 tiled=model.weights_tiled)
-        C.gemm_peer_scatter(layer.w2, layer.s2, h, cnt, off,
-                            ops.pick_bn(expected * model.args.num_experts_per_tok, self.H // 128, El),
+        k = model.args.num_experts_per_tok
+        # prefill-size steps: bf16 GEMMs on the resident dequantised copy when the rank keeps
+        # one (the same bits as per-tile dequantisation, without re-converting every tile);
+        # the rows this rank receives are estimated by the rows it sends (balanced routing)
+        if model._bf16_experts(T * k) and getattr(layer, "w13_bf16", None) is not None:
+            w13, s13, w2, s2, tiled = layer.w13_bf16, None, layer.w2_bf16, None, False
+        else:
+            w13, s13, w2, s2, tiled = layer.w13, layer.s13, layer.w2, layer.s2, model.weights_tiled
+        ops.grouped_gate_up_silu(xp, w13, s13, cnt, off, h, I,
+                                 bn=ops.pick_bn(expected * k, I // 128, El, pair=True), tiled=tiled)
+        C.gemm_peer_scatter(w2, s2, h, cnt, off, ops.pick_bn(expected * k, self.H // 128, El),
                             code, sw, self.symm["slots"][1], self.slot_cap, self.H, self.status,
-                            model.weights_tiled, self.epoch, self.cta_done, self.symm["done"][1], self.rank)
+                            tiled, self.epoch, self.cta_done, self.symm["done"][1], self.rank)
         ops.count_launches(2)
         return self.symm["slots"][0]

@@ -46,7 +46,10 @@ def _inputs(seq_lens, q_lens, bs, vocab, seed):
                       t(cu[nd:] - cu[nd])), base
 
 
-def test_fused_ep_world1_matches_local_moe():
+@pytest.mark.parametrize("bf16_experts", [False, True])
+def test_fused_ep_world1_matches_local_moe(monkeypatch, bf16_experts):
+    """``bf16_experts``: every step takes the bf16 expert GEMMs on the resident
+    dequantised copy (local path and expert-parallel path alike)."""
     from b200moe.parallel.ep import ExpertParallel
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{free_port()}", rank=0, world_size=1,
                             device_id=torch.device("cuda", 0))
@@ -57,6 +60,9 @@ def test_fused_ep_world1_matches_local_moe():
         model = Qwen3MoeForCausalLM(args, "cuda")
         random_init_(model, seed=4)
         model.tile_weights_()
+        if bf16_experts:
+            monkeypatch.setattr(Qwen3MoeForCausalLM, "BF16_EXPERT_ROWS", 1)
+            assert model.cache_bf16_experts_() > 0
         model.reserve_workspace(512, 16, 8)
         runner = SimpleNamespace(world_size=1, rank=0, device=torch.device("cuda", 0), args=args, config=cfg,
                                  model=model)
