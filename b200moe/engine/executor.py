@@ -322,6 +322,15 @@ class Executor:
                     c.send(("exit", ()))
             except Exception:
                 pass
+        # this rank's teardown runs alongside the workers': releasing the peer-memory
+        # buffers and destroying the process group are collectives every rank must reach,
+        # so waiting for the workers' replies first would leave them blocked on rank 0
+        if getattr(self, "runner", None) is not None:
+            try:
+                self.runner.exit()
+            except Exception:
+                pass  # the workers are still reaped below
+            self.runner = None
         for r, c in enumerate(self.conns, start=1):
             try:
                 self._recv(r, c, timeout=30.0)
