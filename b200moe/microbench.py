@@ -268,7 +268,8 @@ def case_ops(T, iters, H=2048, nq=32, nkv=4, D=128, V=151936, topk=8):
     events, L2 flushed before every call); bytes are what each op must move:
     residual add + RMSNorm, q/k RMSNorm + RoPE + paged KV store, the MoE combine
     (fixed-order top-k sum + residual + next RMSNorm), greedy argmax and the sampler
-    (temperature 0.7, top-k 50, top-p 0.9) over the full 151,936-token vocabulary."""
+    (temperature 0.7 with top-k 50 + top-p 0.9, and top-p 0.9 alone) over the full
+    151,936-token vocabulary."""
     from b200moe.engine.kv_cache import KVPool
     dev = "cuda"
     bf = torch.bfloat16
@@ -304,6 +305,9 @@ def case_ops(T, iters, H=2048, nq=32, nkv=4, D=128, V=151936, topk=8):
     seeds = torch.arange(T, dtype=torch.int64, device=dev)
     ms = timeit(lambda: ops.sample(logits, temp, top_k, top_p, None, seeds, None, out=tok), iters)
     report("sample_topk_topp", ms, T * V * 4, 0, rows=T, vocab=V)
+    no_k = torch.full((T,), -1, dtype=torch.int32, device=dev)
+    ms = timeit(lambda: ops.sample(logits, temp, no_k, top_p, None, seeds, None, out=tok), iters)
+    report("sample_topp", ms, T * V * 4, 0, rows=T, vocab=V)
 
 
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's NVSwitch systems
