@@ -154,39 +154,14 @@ __device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t 
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += kST) { hist_u[i] = 0; hist_f[i] = 0.f; }
     __syncthreads();
-    // Logits of one row share a few exponents, so the high digits put most values in a
-    // handful of bins: lanes of a warp that hit the same bin are combined first (one
-    // shared-memory atomic per bin and warp instead of one per value).  The loop bound is
-    // warp-uniform so every lane reaches the warp collectives.
-    const int lane = threadIdx.x & 31;
-    for (int base = 0; base < V; base += kST) {
-      const int i = base + threadIdx.x;
-      bool take = i < V && allowed(am, i);
-      const float x = take ? row[i] * inv_t : 0.f;
+    for (int i = threadIdx.x; i < V; i += kST) {
+      if (!allowed(am, i)) continue;
+      const float x = row[i] * inv_t;
       const uint32_t o = f2ord(x);
-      take = take && o >= lo_bound && (o & mask) == prefix;
+      if (o < lo_bound || (o & mask) != prefix) continue;
       const uint32_t bin = (o >> shift) & 0xFFu;
-      const unsigned grp = __match_any_sync(0xffffffffu, take ? bin : 0x100u);
-      const bool lead = take && __ffs(grp) - 1 == lane;
-      if (mode == 0) {
-        if (lead) atomicAdd(&hist_u[bin], (uint32_t)__popc(grp));
-      } else {
-        const float v = take ? __expf(x - M) * invZ : 0.f;
-        unsigned leaders = __ballot_sync(0xffffffffu, lead);
-        if (__popc(leaders) <= 4) {  // few distinct bins: a warp sum per bin
-          while (leaders) {
-            const int src = __ffs(leaders) - 1;
-            const uint32_t b = __shfl_sync(0xffffffffu, bin, src);
-            float sv = (take && bin == b) ? v : 0.f;
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, off);
-            if (lane == src) atomicAdd(&hist_f[b], sv);
-            leaders &= leaders - 1;
-          }
-        } else if (take) {
-          atomicAdd(&hist_f[bin], v);
-        }
-      }
+      if (mode == 0) atomicAdd(&hist_u[bin], 1u);
+      else atomicAdd(&hist_f[bin], __expf(x - M) * invZ);
     }
     __syncthreads();
     if (threadIdx.x < 32) {
