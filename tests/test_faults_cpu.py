@@ -105,11 +105,14 @@ def test_exit_watchdog_bounds_wedged_teardown(tmp_path):
         eng.exit()
         print("unreachable")
     """ % os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-    t0 = time.monotonic()
-    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60)
-    assert time.monotonic() - t0 < 30
-    assert "unreachable" not in r.stdout
-    assert "watchdog" in r.stderr
+    for rc in ("0", "5"):  # the forced exit's status is configurable (tests use a non-zero one)
+        t0 = time.monotonic()
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60,
+                           env={**os.environ, "B200MOE_EXIT_WATCHDOG_RC": rc})
+        assert time.monotonic() - t0 < 30
+        assert "unreachable" not in r.stdout
+        assert "watchdog" in r.stderr
+        assert r.returncode == int(rc), (r.returncode, r.stderr[-300:])
 
 
 def _link_pair(capacity=1 << 16):
@@ -202,3 +205,30 @@ def test_worker_killed_mid_generate_fails_within_bound():
         assert time.monotonic() - t0 < 60
     finally:
         llm.exit()
+
+
+def test_driver_tears_down_alongside_workers():
+    """Rank 0 releases its own collective resources (peer-memory buffers, process
+    group) after telling the workers to exit and before waiting for their replies:
+    a worker's teardown waits in those collectives for rank 0."""
+    from b200moe.engine.executor import Executor
+    order = []
+
+    class Runner:
+        def exit(self):
+            order.append("runner")
+
+    class Conn:
+        def send(self, msg, timeout=None):
+            order.append("send")
+
+    ex = Executor.__new__(Executor)
+    ex.runner, ex.conns, ex.procs = Runner(), [Conn(), Conn()], []
+
+    def recv(r, c, timeout):
+        assert "runner" in order, "a worker's exit reply needs rank 0's collectives first"
+        order.append("recv")
+
+    ex._recv = recv
+    ex.exit()
+    assert order == ["send", "send", "runner", "recv", "recv"]
