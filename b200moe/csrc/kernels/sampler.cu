@@ -222,6 +222,7 @@ __device__ uint32_t radix_select(const float* row, int V, float inv_t, uint32_t 
 }
 
 constexpr int kCand = 64;  // candidates gathered for the top log-probs (ties past it are dropped)
+constexpr int kCompact = 1024;  // top-k survivors kept in shared memory for the rest of a row's sampling
 
 // The k best (value, id) among allowed tokens whose scaled image is >= lo, best
 // first (ties: lower id first), written as log-probabilities x - M - logZ.
@@ -272,6 +273,9 @@ __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ l
   __shared__ float cand_v[kCand];
   __shared__ int cand_i[kCand];
   __shared__ int n_cand;
+  __shared__ float comp_x[kCompact];
+  __shared__ int comp_i[kCompact];
+  __shared__ int n_comp;
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * ld;
   const uint32_t* am = nullptr;
@@ -304,27 +308,47 @@ __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ l
 
   uint32_t lo = 0;  // the distribution: allowed tokens with f2ord(x) >= lo
   int tok;
+  // top-k survivors (scaled logits and ids) compacted into shared memory when they fit:
+  // the nucleus, the min-p bound, the draw and the sampled distribution's normaliser
+  // then walk at most kCompact entries instead of the whole row
+  int nc = -1;  // -1: not compacted
   if (greedy) {
     tok = bi;
   } else {
-    float z = 0.f;
-    for (int i = threadIdx.x; i < V; i += kST)
-      if (allowed(am, i)) z += __expf(row[i] * inv_t - M);
-    const float Z = block_reduce_sum(z, red);
     const int top_k = a.top_k ? a.top_k[r] : -1;
-    if (top_k > 0 && top_k < V)
-      lo = radix_select(row, V, inv_t, 0, 0, top_k, 0.f, M, 1.f / Z, am, hist_u, hist_f);
+    if (top_k > 0 && top_k < V) {
+      lo = radix_select(row, V, inv_t, 0, 0, top_k, 0.f, M, 1.f, am, hist_u, hist_f);
+      if (top_k <= kCompact) {
+        if (threadIdx.x == 0) n_comp = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < V; i += kST) {
+          if (!allowed(am, i)) continue;
+          const float x = row[i] * inv_t;
+          if (f2ord(x) < lo) continue;
+          const int slot = atomicAdd(&n_comp, 1);
+          if (slot < kCompact) { comp_x[slot] = x; comp_i[slot] = i; }
+        }
+        __syncthreads();
+        nc = n_comp <= kCompact ? n_comp : -1;  // ties past the cap: the whole row again
+        __syncthreads();
+      }
+    }
     const float top_p = a.top_p ? a.top_p[r] : 1.f;
     if (top_p < 1.f) {
       // nucleus mass is measured over the top-k survivors
       float zk = 0.f;
-      for (int i = threadIdx.x; i < V; i += kST) {
-        if (!allowed(am, i)) continue;
-        const float x = row[i] * inv_t;
-        if (f2ord(x) >= lo) zk += __expf(x - M);
+      if (nc >= 0) {
+        for (int j = threadIdx.x; j < nc; j += kST) zk += __expf(comp_x[j] - M);
+      } else {
+        for (int i = threadIdx.x; i < V; i += kST) {
+          if (!allowed(am, i)) continue;
+          const float x = row[i] * inv_t;
+          if (f2ord(x) >= lo) zk += __expf(x - M);
+        }
       }
       const float Zk = block_reduce_sum(zk, red);
-      const uint32_t tp = radix_select(row, V, inv_t, lo, 1, 0, top_p, M, 1.f / Zk, am, hist_u, hist_f);
+      const uint32_t tp = nc >= 0 ? radix_select(comp_x, nc, 1.f, lo, 1, 0, top_p, M, 1.f / Zk, nullptr, hist_u, hist_f)
+                                  : radix_select(row, V, inv_t, lo, 1, 0, top_p, M, 1.f / Zk, am, hist_u, hist_f);
       lo = max(lo, tp);
     }
     const float min_p = a.min_p ? a.min_p[r] : 0.f;
@@ -334,14 +358,20 @@ __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ l
     const uint32_t off = a.offsets ? (uint32_t)a.offsets[r] : 0u;
     float sv = -INFINITY;
     int si = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += kST) {
-      if (!allowed(am, i)) continue;
-      const float x = row[i] * inv_t;
-      if (f2ord(x) < lo) continue;
+    // exponential race keyed by the token id: the same draw whether or not the
+    // survivors were compacted
+    auto race = [&](int i, float x) {
+      if (f2ord(x) < lo) return;
       const uint4 rnd = philox4x32(make_uint4((uint32_t)i, off, 0x5A3Cu, 0u), key);
       const float e = -__logf(u01(rnd.x));  // Exp(1)
       const float score = (x - M) - __logf(fmaxf(e, 1e-20f));
-      if (score > sv) { sv = score; si = i; }
+      if (score > sv || (score == sv && i < si)) { sv = score; si = i; }
+    };
+    if (nc >= 0) {
+      for (int j = threadIdx.x; j < nc; j += kST) race(comp_i[j], comp_x[j]);
+    } else {
+      for (int i = threadIdx.x; i < V; i += kST)
+        if (allowed(am, i)) race(i, row[i] * inv_t);
     }
     block_argmax(sv, si, red, redi);
     tok = si == 0x7fffffff ? bi : si;
@@ -351,10 +381,15 @@ __global__ void __launch_bounds__(kST) sample_kernel(const float* __restrict__ l
 
   // log-probabilities of the distribution just sampled from
   float zs = 0.f;
-  for (int i = threadIdx.x; i < V; i += kST) {
-    if (!allowed(am, i)) continue;
-    const float x = row[i] * inv_t;
-    if (f2ord(x) >= lo) zs += expf(x - M);
+  if (nc >= 0) {
+    for (int j = threadIdx.x; j < nc; j += kST)
+      if (f2ord(comp_x[j]) >= lo) zs += expf(comp_x[j] - M);
+  } else {
+    for (int i = threadIdx.x; i < V; i += kST) {
+      if (!allowed(am, i)) continue;
+      const float x = row[i] * inv_t;
+      if (f2ord(x) >= lo) zs += expf(x - M);
+    }
   }
   const float logZ = logf(block_reduce_sum(zs, red));
   if (threadIdx.x == 0) a.lp_chosen[r] = row[tok] * inv_t - M - logZ;
