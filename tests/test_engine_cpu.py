@@ -397,3 +397,32 @@ def test_int8_channel_kv_engine_cpu():
         assert all(len(o["token_ids"]) == 6 for o in out)
     finally:
         llm.exit()
+
+
+def test_resident_bf16_expert_copy_decision(monkeypatch):
+    """The resident bf16 expert copy is kept only on CUDA, for the single-GPU or fused
+    expert-parallel paths, and only when enough memory stays free for the KV cache
+    ("auto"); "1" forces it and "0" turns it off."""
+    from types import SimpleNamespace
+    from b200moe.engine.model_runner import ModelRunner
+    GiB = 1 << 30
+    calls = []
+
+    def model(ep=None, need=60 * GiB):
+        return SimpleNamespace(ep=ep, attn_tp=1, BF16_EXPERT_ROWS=512, bf16_expert_bytes=lambda: need,
+                               cache_bf16_experts_=lambda: calls.append(1) or need)
+
+    def decide(m, free, mode="auto", dev="cuda"):
+        monkeypatch.setenv("B200MOE_BF16_EXPERT_CACHE", mode)
+        monkeypatch.setattr(torch.cuda, "mem_get_info", lambda d=None: (free, 180 * GiB))
+        runner = SimpleNamespace(model=m, device=torch.device(dev), BF16_CACHE_KEEP_FREE=0.35)
+        return ModelRunner._maybe_cache_bf16_experts(runner)
+
+    assert decide(model(), free=150 * GiB) == 60 * GiB                 # 90 GiB stay free: keep it
+    assert decide(model(), free=100 * GiB) == 0                        # 40 GiB would stay: no
+    assert decide(model(), free=100 * GiB, mode="1") == 60 * GiB       # forced
+    assert decide(model(), free=150 * GiB, mode="0") == 0              # off
+    assert decide(model(), free=150 * GiB, dev="cpu") == 0             # CUDA only
+    assert decide(model(ep=SimpleNamespace(backend="nccl_a2a")), free=150 * GiB) == 0
+    assert decide(model(ep=SimpleNamespace(backend="fused")), free=150 * GiB) == 60 * GiB
+    assert len(calls) == 3
